@@ -1,0 +1,422 @@
+"""Benchmark of the speculative-decode verify step (BASELINE.json metric:
+accepted tok/s at batch 1, draft 3; verify-step latency; HBM roofline).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config NAME]
+                    [--impl ours|reference] [--accept-p 0.7]
+
+One "step" is one speculative round through the public C ABI: a verify of
+1 + 3 rows (the target's token + 3 planted drafts) at the configured
+context, greedy acceptance and rollback.  Drafts are planted: each equals the
+target's own greedy token at that position with probability p (seeded),
+otherwise a different uniform token, so acceptance is controlled; the
+target's greedy stream comes from an untimed plain-decode pass of the same
+session.  Weights, the seeded latent KV prefix and every activation are
+resident in HBM before timing starts.
+
+Under torchrun (N > 1) every rank runs an independent replica on its own GPU
+(per-GPU work fixed: weak scaling); value = tokens of all ranks / the slowest
+rank's device time.
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "accepted tok/s (batch 1, draft=3)"
+DEFAULT_CONFIG = "c4_ds4_flash"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default=DEFAULT_CONFIG)
+    ap.add_argument("--accept-p", type=float, default=0.7)
+    ap.add_argument("--draft", type=int, default=3)
+    ap.add_argument("--profile-passes", type=int, default=3)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--out", default=None, help="also write the JSON line here")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# distributed plumbing (one process per GPU)
+# ---------------------------------------------------------------------------
+class Dist:
+    def __init__(self):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pg = None
+        if self.world > 1:
+            import torch
+            import torch.distributed as dist
+            torch.cuda.set_device(self.local)
+            dist.init_process_group("nccl", device_id=torch.device("cuda", self.local))
+            self.dist = dist
+            self.torch = torch
+
+    def barrier(self):
+        if self.world > 1:
+            self.dist.barrier()
+
+    def max(self, v):
+        if self.world == 1:
+            return v
+        t = self.torch.tensor([float(v)], device=f"cuda:{self.local}")
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum(self, v):
+        if self.world == 1:
+            return v
+        t = self.torch.tensor([float(v)], device=f"cuda:{self.local}")
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.SUM)
+        return float(t.item())
+
+    def close(self):
+        if self.world > 1:
+            self.dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------
+class Clocks:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu):
+        self.gpu = gpu
+        self.proc = None
+        self.path = tempfile.mktemp(prefix="fc_clocks_", suffix=".csv")
+
+    def start(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f,
+                stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.f.close()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        os.unlink(self.path)
+        return {"sm_mhz": float(np.median(sm)) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# workload
+# ---------------------------------------------------------------------------
+def planted_rounds(stream, n_rounds, draft, p, vocab, seed=0):
+    """Draft proposals for rounds that start at stream offset o: ids[0] =
+    stream[o], ids[i] = stream[o+i] with probability p, else another token."""
+    rng = np.random.default_rng(seed)
+    plans = []
+    for _ in range(n_rounds):
+        hits = rng.random(draft) < p
+        noise = rng.integers(1, vocab, size=draft)
+        plans.append((hits, noise))
+    return plans
+
+
+def make_ids(stream, o, plan, vocab):
+    hits, noise = plan
+    ids = [stream[o]]
+    for i in range(len(hits)):
+        t = stream[o + i + 1]
+        ids.append(int(t) if hits[i] else int((t + noise[i]) % vocab))
+    return ids
+
+
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        d = json.load(open(path))
+        return d.get("hbm_gbs"), "measured"
+    return 6650.0, "fallback"
+
+
+def kernel_bytes(cfg, name, rows, context, n_active):
+    """Algorithmic bytes of one launch of the named kernel (per MoE layer).
+    Weights at their stored bytes per parameter, activations ignored (they
+    are < 0.1% of the weight bytes)."""
+    from floyd_b200.configs import _BPP
+    D, I = cfg["hidden_size"], cfg["moe_intermediate_size"]
+    ef, df = _BPP[cfg["expert_format"]], _BPP[cfg["dense_format"]]
+    W = I * cfg["shared_expert_count"]
+    if name == "moe_gate_up":
+        return n_active * 2 * I * D * ef + 2 * W * D * df
+    if name == "moe_down":
+        return n_active * I * D * ef + W * D * df
+    if name == "mla_attention":
+        return context * (cfg["kv_lora_rank"] + cfg["qk_rope_dim"]) * 2
+    if name == "gemv_lm_head":
+        return cfg["vocab_size"] * D * df
+    return None
+
+
+def cpu_baseline(cfg, rows, mean_commit, budget_s=20.0):
+    """The oracle port timed on this host on a bounded sample: one MoE layer of
+    the config (experts cut to the ones a 4-row verify can touch; the per-token
+    work is unchanged) plus a vocab slice of the lm-head, extrapolated to the
+    full step."""
+    from oracle import oracle as O
+    from floyd_b200.configs import scaled
+    cores = os.cpu_count() or 1
+    os.environ.setdefault("OMP_NUM_THREADS", str(cores))
+    E = min(cfg["expert_count"], rows * cfg["experts_per_token"])
+    vslice = 8192
+    ctx = cfg["context"]
+    sl = scaled(cfg, layer_count=1, first_dense_layer_count=0, hash_layer_count=0,
+                expert_count=E, vocab_size=vslice)
+    m = O.OracleModel(sl, 0)
+    s = O.OracleSession(m, ctx + rows + 1, kv_fp16=True)
+    s.seed_context(ctx, 7)
+    times = []
+    t_end = time.time() + budget_s
+    while time.time() < t_end and len(times) < 5:
+        s.set_position(ctx)
+        t0 = time.perf_counter()
+        s.forward(list(range(1, rows + 1)))
+        times.append(time.perf_counter() - t0)
+    t_slice = float(np.median(times))
+    # the vocab-slice head on its own
+    rng = np.random.default_rng(0)
+    vals = rng.integers(-127, 128, size=(vslice, cfg["hidden_size"]), dtype=np.int8)
+    sc = np.full((vslice, cfg["hidden_size"] // 32), 1e-3, dtype=np.float32)
+    x = rng.standard_normal((rows, cfg["hidden_size"])).astype(np.float32)
+    t0 = time.perf_counter()
+    O.gemv(1, vals, sc, x)
+    t_head = time.perf_counter() - t0
+    t_layer = max(t_slice - t_head, 1e-9)
+    t_step = cfg["layer_count"] * t_layer + t_head * cfg["vocab_size"] / vslice
+    m.close()
+    return {"value": mean_commit / t_step, "unit": "tok/s", "cores": cores, "kind": "port",
+            "sample": (f"oracle (C, OpenMP {cores} threads) on 1 MoE layer of {cfg['_name']} "
+                       f"({E} experts, ctx {ctx}, {rows} rows) + {vslice}-row lm-head slice, "
+                       f"extrapolated to {cfg['layer_count']} layers / vocab {cfg['vocab_size']}; "
+                       f"step {t_step * 1e3:.1f} ms x measured mean commit {mean_commit:.3f}"),
+            "step_ms": t_step * 1e3}
+
+
+def run_reference(args, d):
+    """--impl reference: the CPU implementation of the path (the oracle port;
+    the reference's verify path exists only in Metal and in the absent ds4
+    engine) timed on this host, one bounded sample per step."""
+    if d.rank != 0:
+        return None
+    from floyd_b200.configs import CONFIGS
+    cfg = dict(CONFIGS[args.config])
+    cfg["_name"] = args.config
+    rows = args.draft + 1
+    p = args.accept_p
+    expected = sum(p ** i for i in range(rows))
+    for _ in range(args.warmup):
+        cpu_baseline(cfg, rows, expected, budget_s=2.0)
+    vals = []
+    t0 = time.time()
+    for _ in range(args.steps):
+        vals.append(cpu_baseline(cfg, rows, expected, budget_s=2.0))
+    wall = time.time() - t0
+    v = float(np.mean([x["value"] for x in vals]))
+    base = vals[-1]
+    base["value"] = v
+    base["sample"] += f"; expected commit 1+p+p^2+p^3 at p={p}"
+    return {"metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": float(np.mean([x["step_ms"] for x in vals])),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8/fp4 x fp32",
+            "data": "synthetic", "impl": "reference",
+            "config": {"workload": args.config, "draft": args.draft, "accept_p": p,
+                       "context": cfg["context"]},
+            "cpu_baseline": base,
+            "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "wall_s": wall}
+
+
+def run_ours(args, d):
+    import floyd_b200
+    from floyd_b200.configs import CONFIGS
+    cfg = dict(CONFIGS[args.config])
+    cfg["_name"] = args.config
+    rows = args.draft + 1
+    ctx0 = cfg["context"]
+    n_rounds = args.warmup + args.steps
+    gen_tokens = rows * n_rounds + 2
+    capacity = ctx0 + gen_tokens + 8
+    V = cfg["vocab_size"]
+
+    t_setup = time.time()
+    model = floyd_b200.Model(cfg, device=d.local, seed=0)
+    sess = floyd_b200.Session(model, capacity, rows)
+    sess.seed_context(ctx0, 7)
+    # untimed: the target's greedy stream from the seeded context
+    stream = [1]
+    logits = sess.decode(stream[0])
+    for _ in range(gen_tokens):
+        t = int(np.argmax(logits))
+        stream.append(t)
+        logits = sess.decode(t)
+    sess.rollback(ctx0)
+    plans = planted_rounds(stream, n_rounds, args.draft, args.accept_p, V, seed=1234)
+    setup_s = time.time() - t_setup
+
+    o = 0
+    emitted_timed = 0
+    wall_timed = 0.0
+    clocks = Clocks(d.local)
+    mismatches = 0
+    for r in range(n_rounds):
+        if r == args.warmup:
+            d.barrier()
+            st0 = sess.stats()
+            clocks.start()
+        ids = make_ids(stream, o, plans[r], V)
+        t0 = time.perf_counter()
+        em, nxt, _ = sess.verify(ids)
+        dt = time.perf_counter() - t0
+        # bit-exact batch == decode makes the commit exactly the planted prefix
+        hits = plans[r][0]
+        expect = 1
+        for h in hits:
+            if not h:
+                break
+            expect += 1
+        if len(em) != expect or nxt != stream[o + len(em)]:
+            mismatches += 1
+        o += len(em)
+        if r >= args.warmup:
+            emitted_timed += len(em)
+            wall_timed += dt
+    clk = clocks.stop()
+    st1 = sess.stats()
+    gpu_ms = st1["gpu_ms"] - st0["gpu_ms"]
+    d.barrier()
+    gpu_ms_max = d.max(gpu_ms)
+    wall_max = d.max(wall_timed)
+    total_emitted = d.sum(emitted_timed)
+    value = total_emitted / (gpu_ms_max / 1e3)
+    e2e = total_emitted / wall_max
+
+    # per-kernel profile (eager passes with CUDA events on the session stream)
+    sess.set_profiling(True)
+    sess.profile_reset()
+    for i in range(args.profile_passes):
+        ids = make_ids(stream, o, plans[-1], V)
+        p0 = sess.position()
+        sess.verify(ids)
+        sess.rollback(p0)
+    prof = sess.profile()
+    sess.set_profiling(False)
+    layers = cfg["layer_count"]
+    moe_layers = [l for l in range(cfg["first_dense_layer_count"], layers)]
+    actives = []
+    for l in moe_layers:
+        rts = sess.routes(l, rows)
+        actives.append(len(np.unique(rts)))
+    n_active = float(np.mean(actives)) if actives else 0.0
+    peak, peak_kind = measured_peaks()
+    dominant = max(prof.items(), key=lambda kv: kv[1][0])[0] if prof else None
+    roof = None
+    if dominant:
+        tot, launches = prof[dominant]
+        per = tot / launches
+        b = kernel_bytes(cfg, dominant, rows, sess.position(), n_active)
+        if b:
+            ach = b / (per / 1e3) / 1e9
+            roof = {"bound": "hbm", "kernel": dominant, "achieved": ach, "peak": peak, "unit": "GB/s",
+                    "frac": ach / peak, "traffic": None, "peak_kind": peak_kind,
+                    "algorithmic_bytes_per_launch": b, "avg_launch_us": per * 1e3,
+                    "measured": "CUDA events between launches on the session stream, eager profiled passes"}
+    step_ms = gpu_ms_max / args.steps
+    step_bytes = floyd_b200.step_bytes(cfg, rows, ctx0, n_active)
+    out = {
+        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": d.world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int8/fp4 x fp32",
+        "data": "synthetic (seeded weights N(0,0.02)-like quantized, latent KV prefix, planted drafts)",
+        "config": {"workload": args.config, "draft": args.draft, "accept_p": args.accept_p,
+                   "context": ctx0, "rows_per_verify": rows,
+                   "l2": "inputs larger than L2 (weights read once per step)",
+                   "parallelism": f"replicas x{d.world}"},
+        "verify_us": step_ms * 1e3,
+        "step_hbm": {"algorithmic_bytes": step_bytes, "achieved_gbs": step_bytes / (step_ms / 1e3) / 1e9,
+                     "frac": step_bytes / (step_ms / 1e3) / 1e9 / peak, "peak": peak},
+        "mean_commit": total_emitted / (args.steps * d.world),
+        "acceptance_mismatches": int(d.sum(mismatches)),
+        "roofline": roof,
+        "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 72, "d2h_bytes_per_step": 40,
+                "note": "fc_session_verify wall time with host id / result buffers"},
+        "gpu_launches": None,
+        "kernels": {k: {"ms": v[0], "launches": v[1]} for k, v in prof.items()},
+        "clocks": clk,
+        "setup_s": setup_s,
+        "device": model.device_name(),
+    }
+    launches = sum(v[1] for v in prof.values()) / max(args.profile_passes, 1)
+    out["gpu_launches"] = int(round(launches * args.steps))
+    if d.rank == 0 and d.world == 1 and not args.no_cpu_baseline:
+        try:
+            out["cpu_baseline"] = cpu_baseline(cfg, rows, out["mean_commit"])
+        except Exception as exc:  # reported, never silently replaced
+            out["cpu_baseline"] = {"error": str(exc)}
+    sess.close()
+    model.close()
+    return out
+
+
+def main():
+    args = parse()
+    d = Dist()
+    if args.impl == "reference":
+        out = run_reference(args, d)
+    else:
+        out = run_ours(args, d)
+    if d.rank == 0 and out is not None:
+        line = json.dumps(out)
+        print(line, flush=True)
+        if args.out:
+            with open(args.out, "w") as f:
+                f.write(line + "\n")
+    d.close()
+
+
+if __name__ == "__main__":
+    main()

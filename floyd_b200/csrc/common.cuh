@@ -1,0 +1,171 @@
+// common.cuh - device helpers shared by the sm_100a kernels of the verify
+// step: tensor-core MMA wrappers, exact int8 / int4 / e2m1 -> fp16 dequant,
+// the hi/lo fp16 activation format, warp reductions and error checks.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/floyd_cuda.h"
+#include "../../include/floyd_synth.h"
+
+namespace fc {
+
+constexpr int kWarp = 32;
+
+// ---------------------------------------------------------------------------
+// Activation operand format ("xq").  A row of K activations is stored as K/4
+// 16-byte records {hi[4], lo[4]} of fp16 with x = hi + lo exactly to about
+// 22 bits (hi = fp16(x), lo = fp16(x - hi)).  Record r holds k = 4r .. 4r+3,
+// which is exactly the B fragment one thread needs for one m16n8k16 MMA.
+// Values must satisfy |x| < 65504; the producers saturate.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void split_hi_lo(float x, __half &hi, __half &lo) {
+    x = fminf(fmaxf(x, -65504.0f), 65504.0f);
+    hi = __float2half_rn(x);
+    lo = __float2half_rn(x - __half2float(hi));
+}
+
+// Writes x at (row s, column k) of an xq buffer with row length kp.
+__device__ __forceinline__ void store_xq(__half *xq, int kp, int s, int k, float x) {
+    __half hi, lo;
+    split_hi_lo(x, hi, lo);
+    __half *rec = xq + ((size_t)s * kp + (k & ~3)) * 2;
+    rec[k & 3] = hi;
+    rec[4 + (k & 3)] = lo;
+}
+
+// ---------------------------------------------------------------------------
+// Tensor-core MMA m16n8k16, fp16 inputs, fp32 accumulate.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void mma_f16(float (&d)[4], const uint32_t (&a)[4],
+                                        uint32_t b0, uint32_t b1, const float (&c)[4]) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%12,%13};\n"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1),
+          "f"(c[0]), "f"(c[1]), "f"(c[2]), "f"(c[3]));
+}
+
+// ---------------------------------------------------------------------------
+// Streaming loads (weights are read once per step: skip L1).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint4 ldg_stream(const void *p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ uint4 ldg_v4(const void *p) {
+    uint4 v;
+    asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;\n" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+    return d;
+}
+
+__device__ __forceinline__ uint32_t hsub2_bits(uint32_t a, uint32_t b) {
+    __half2 r = __hsub2(*reinterpret_cast<__half2 *>(&a), *reinterpret_cast<__half2 *>(&b));
+    return *reinterpret_cast<uint32_t *>(&r);
+}
+
+// int8 x4 (one 32-bit word) -> two fp16x2 registers, exact:
+// fp16(1024 + (v ^ 0x80)) - 1152 = v.  lo = bytes {0,1}, hi = bytes {2,3}.
+__device__ __forceinline__ void dequant_q8_word(uint32_t w, uint32_t &lo, uint32_t &hi) {
+    uint32_t u = w ^ 0x80808080u;
+    lo = hsub2_bits(prmt(u, 0x64646464u, 0x5140u), 0x64806480u);
+    hi = hsub2_bits(prmt(u, 0x64646464u, 0x7362u), 0x64806480u);
+}
+
+// int4 pair at nibble offset `shift` and shift+16 -> fp16x2 (nibble - 8), exact.
+__device__ __forceinline__ uint32_t dequant_q4_pair(uint32_t w, int shift) {
+    uint32_t t = ((w >> shift) & 0x000F000Fu) | 0x64006400u;
+    return hsub2_bits(t, 0x64086408u);
+}
+
+// e2m1 codes: magnitudes {0, .5, 1, 1.5, 2, 3, 4, 6} have fp16 encodings whose
+// low byte is zero; their high bytes form this 8-entry table.
+constexpr uint32_t kE2m1Lo = 0x3E3C3800u;
+constexpr uint32_t kE2m1Hi = 0x46444240u;
+
+// One 32-bit word of 8 e2m1 codes (code p at bits 4p) -> 4 fp16x2 registers;
+// register p holds codes (p, p + 4).
+__device__ __forceinline__ void dequant_e2m1_word(uint32_t w, uint32_t (&out)[4]) {
+    uint32_t ra = prmt(kE2m1Lo, kE2m1Hi, w & 0x7777u);
+    uint32_t rb = prmt(kE2m1Lo, kE2m1Hi, (w >> 16) & 0x7777u);
+    // byte0 / byte2: sign-replicate of a table byte (always < 0x80) -> 0x00.
+    out[0] = prmt(ra, rb, 0x4808u) | ((w << 12) & 0x80008000u);
+    out[1] = prmt(ra, rb, 0x5919u) | ((w << 8) & 0x80008000u);
+    out[2] = prmt(ra, rb, 0x6A2Au) | ((w << 4) & 0x80008000u);
+    out[3] = prmt(ra, rb, 0x7B3Bu) | (w & 0x80008000u);
+}
+
+__device__ __forceinline__ float e8m0_to_float(uint32_t code) {
+    if (code == 255u) return __int_as_float(0x7FC00000);
+    if (code == 0u) return __int_as_float(0x00400000);  // 2^-127, subnormal
+    return __int_as_float((int)(code << 23));
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+__device__ __forceinline__ float silu(float x) { return x / (1.0f + expf(-x)); }
+
+// Chunk geometry of the device weight layout: every row is a sequence of
+// 64-byte chunks; a q8 chunk covers 64 columns (4 MMAs), a q4 / MXFP4 chunk
+// 128 columns (8 MMAs).  Rows are zero-padded to a whole number of chunks.
+__host__ __device__ constexpr int chunk_cols(int fmt) { return fmt == FC_FMT_Q8 ? 64 : 128; }
+__host__ __device__ constexpr int row_bytes(int fmt, int kp) {
+    return fmt == FC_FMT_Q8 ? kp : kp / 2;
+}
+__host__ __device__ inline int pad_cols(int fmt, int k) {
+    int c = fmt == FC_FMT_F32 ? 1 : chunk_cols(fmt);
+    return (k + c - 1) / c * c;
+}
+
+// Byte offset inside a row (values) for logical column k of a quantized row,
+// and for q4 / e2m1 the nibble position (0 = low).  Inverse of the MMA
+// fragment mapping used by the GEMV kernel:
+//   q8:  chunk c = k/64, r = k%64, MMA i = r/16, thread j = (r%16)/4, b = r%4
+//        byte = 64c + 16j + 4i + b
+//   q4 / e2m1: chunk c = k/128, r = k%128, MMA i = r/16, j = (r%16)/4,
+//        b = r%4, h = b/2, e = b%2; register q = 2i + h, word = q/4,
+//        q4:   nibble slot s = q%4 + 4e (bit 4s of the word)
+//        e2m1: nibble slot p = q%4 + 4e (bit 4p of the word)
+//        byte = 64c + 16j + 4*word + slot/2, nibble = slot%2
+__host__ __device__ inline void weight_position(int fmt, int k, int &byte, int &nibble) {
+    if (fmt == FC_FMT_Q8) {
+        int c = k >> 6, r = k & 63;
+        byte = 64 * c + 16 * ((r & 15) >> 2) + 4 * (r >> 4) + (r & 3);
+        nibble = 0;
+        return;
+    }
+    int c = k >> 7, r = k & 127;
+    int i = r >> 4, j = (r & 15) >> 2, b = r & 3;
+    int q = 2 * i + (b >> 1), e = b & 1;
+    int word = q >> 2;
+    int slot = (q & 3) + 4 * e;
+    byte = 64 * c + 16 * j + 4 * word + (slot >> 1);
+    nibble = slot & 1;
+}
+
+}  // namespace fc
+
+#define FC_CUDA_OK(expr) ((expr) == cudaSuccess)

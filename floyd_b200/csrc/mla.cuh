@@ -1,0 +1,453 @@
+// mla.cuh - compressed-latent MLA attention over the resident KV cache for
+// 1 + k verify rows (absorbed W_UK / W_UV, the cache is never decompressed).
+//
+// Replaces, from moonlight_kernels.metal: cache_append (:132-170),
+// rope_query (:172-200), attention_absorb_query (:218-245),
+// attention_scores (:247-282), attention_latent_context (:284-343); the
+// decode_value step (:345-375) is a GEMV family in gemv.cuh.
+//
+// Cache layout: per layer [context][L + R] fp16 (latent row, then the rotated
+// rope part), 1152 bytes per position for L=512, R=64.  The query operand is
+// the same shape: qcat[s * H + h][L + R] = (q_nope . W_UK[h], rope(q_rope)).
+//
+// The attention kernel is flash-decoding on the tensor cores: a CTA owns 32
+// query rows (heads x verify rows share one cache, MQA-like) and a fixed
+// range of 64-key chunks; scores (32 x 64, K = L + R) and P . C (32 x L,
+// K = 64 keys) are m16n8k16 MMAs from shared memory, with an online softmax
+// across the chunks of the range.  Split boundaries are a function of the key
+// index and the session's context size only, and masked keys contribute
+// exact zeros, so a verify row reproduces a single-token decode bit for bit.
+#pragma once
+
+#include "common.cuh"
+
+namespace fc {
+
+// ---------------------------------------------------------------------------
+// Embedding gather (moonlight_kernels.metal:10-21) of a quantized table.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float dequant_element(int fmt, const uint8_t *w, const void *sc,
+                                                 int kp, size_t row, int k) {
+    if (fmt == FC_FMT_F32) return reinterpret_cast<const float *>(w)[row * kp + k];
+    int byte, nib;
+    weight_position(fmt, k, byte, nib);
+    const uint8_t *rowp = w + row * (size_t)row_bytes(fmt, kp);
+    size_t gi = row * (size_t)(kp / 32) + (size_t)(k >> 5);
+    if (fmt == FC_FMT_Q8) {
+        float s = __half2float(reinterpret_cast<const __half *>(sc)[gi]);
+        return (float)(int8_t)rowp[byte] * s;
+    }
+    uint32_t code = (rowp[byte] >> (4 * nib)) & 15u;
+    if (fmt == FC_FMT_Q4) {
+        float s = __half2float(reinterpret_cast<const __half *>(sc)[gi]);
+        return (float)((int)code - 8) * s;
+    }
+    const float table[8] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};
+    float v = table[code & 7];
+    if (code & 8) v = -v;
+    return v * e8m0_to_float(reinterpret_cast<const uint8_t *>(sc)[gi]);
+}
+
+__global__ void embed_kernel(int fmt, const uint8_t *w, const void *sc, int D, int kp,
+                             const int *ids, float *x) {
+    int s = blockIdx.x;
+    size_t row = (size_t)ids[s];
+    for (int k = threadIdx.x; k < D; k += blockDim.x)
+        x[(size_t)s * D + k] = dequant_element(fmt, w, sc, kp, row, k);
+}
+
+// ---------------------------------------------------------------------------
+// RMSNorm (moonlight_kernels.metal:23-41): y = x / sqrt(mean(x^2) + eps) * w.
+// Writes the xq operand of the next GEMV and, optionally, fp32.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float block_sum(float v, float *scratch) {
+    v = warp_sum(v);
+    int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    __syncthreads();
+    if (lane == 0) scratch[warp] = v;
+    __syncthreads();
+    float t = 0.0f;
+    for (int i = 0; i < nw; ++i) t += scratch[i];
+    return t;
+}
+
+__global__ void rmsnorm_kernel(const float *x, int ldx, const float *w, int D, float eps,
+                               __half *yq, int kpy, float *y, int ldy) {
+    __shared__ float scratch[32];
+    int s = blockIdx.x;
+    const float *xs = x + (size_t)s * ldx;
+    float ss = 0.0f;
+    for (int k = threadIdx.x; k < D; k += blockDim.x) ss += xs[k] * xs[k];
+    ss = block_sum(ss, scratch);
+    float scale = 1.0f / sqrtf(ss / (float)D + eps);
+    for (int k = threadIdx.x; k < D; k += blockDim.x) {
+        float v = xs[k] * scale * w[k];
+        if (yq) store_xq(yq, kpy, s, k, v);
+        if (y) y[(size_t)s * ldy + k] = v;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// KV append + query rope (moonlight_kernels.metal:132-200).  One block per
+// verify row: RMSNorm(latent) and RoPE(rope part) into the cache at
+// position pos + s; RoPE of every head's rope slice into qcat.  RoPE takes
+// interleaved pairs and writes the half-split order.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void rope_pair(float first, float second, int p, int R, int position,
+                                          float theta, float &out_a, float &out_b) {
+    float angle = (float)position * powf(theta, -2.0f * (float)p / (float)R);
+    float c = cosf(angle), sn = sinf(angle);
+    out_a = first * c - second * sn;
+    out_b = second * c + first * sn;
+}
+
+__global__ void mla_prep_kernel(const float *ckv, const float *q, const float *norm_w, int L,
+                                int R, int H, int nope, float eps, float theta,
+                                const int *d_pos, __half *cache, __half *qcat) {
+    __shared__ float scratch[32];
+    int s = blockIdx.x;
+    int position = *d_pos + s;
+    const float *src = ckv + (size_t)s * (L + R);
+    float ss = 0.0f;
+    for (int i = threadIdx.x; i < L; i += blockDim.x) ss += src[i] * src[i];
+    ss = block_sum(ss, scratch);
+    float scale = 1.0f / sqrtf(ss / (float)L + eps);
+    __half *dst = cache + (size_t)position * (L + R);
+    for (int i = threadIdx.x; i < L; i += blockDim.x)
+        dst[i] = __float2half_rn(src[i] * scale * norm_w[i]);
+    int half = R / 2;
+    for (int p = threadIdx.x; p < half; p += blockDim.x) {
+        float a, b;
+        rope_pair(src[L + 2 * p], src[L + 2 * p + 1], p, R, position, theta, a, b);
+        dst[L + p] = __float2half_rn(a);
+        dst[L + half + p] = __float2half_rn(b);
+    }
+    int qw = nope + R;
+    for (int t = threadIdx.x; t < H * half; t += blockDim.x) {
+        int h = t / half, p = t % half;
+        const float *qh = q + ((size_t)s * H + h) * qw + nope;
+        float a, b;
+        rope_pair(qh[2 * p], qh[2 * p + 1], p, R, position, theta, a, b);
+        __half *qo = qcat + ((size_t)s * H + h) * (L + R) + L;
+        qo[p] = __float2half_rn(a);
+        qo[half + p] = __float2half_rn(b);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Query absorption (moonlight_kernels.metal:218-245):
+//   qcat[s*H+h][l] = fp16( sum_n q[s][h][n] * W_kvb[h*(nope+v)+n][l] )
+// One thread per (h, l), all rows; sequential sum over n in fp32 without
+// contraction (the oracle's order).
+// ---------------------------------------------------------------------------
+__global__ void mla_absorb_kernel(int fmt, const uint8_t *w, const void *sc, int kp,
+                                  const float *q, int S, int H, int nope, int vdim, int R,
+                                  int L, __half *qcat) {
+    int h = blockIdx.x;
+    int l = blockIdx.y * blockDim.x + threadIdx.x;
+    if (l >= L) return;
+    float acc[8];
+#pragma unroll
+    for (int s = 0; s < 8; ++s) acc[s] = 0.0f;
+    int qw = nope + R;
+    for (int n = 0; n < nope; ++n) {
+        size_t row = (size_t)h * (nope + vdim) + n;
+        float wv = dequant_element(fmt, w, sc, kp, row, l);
+#pragma unroll
+        for (int s = 0; s < 8; ++s)
+            if (s < S) acc[s] = __fadd_rn(acc[s], __fmul_rn(q[((size_t)s * H + h) * qw + n], wv));
+    }
+#pragma unroll
+    for (int s = 0; s < 8; ++s)
+        if (s < S) qcat[((size_t)s * H + h) * (L + R) + l] = __float2half_rn(acc[s]);
+}
+
+// ---------------------------------------------------------------------------
+// Flash-decoding attention on the tensor cores.
+// ---------------------------------------------------------------------------
+constexpr int kAttnQ = 32;       // query rows per CTA
+constexpr int kAttnKeys = 64;    // keys per chunk
+constexpr int kAttnThreads = 256;
+
+__device__ __forceinline__ void ldmatrix_x4(uint32_t (&r)[4], const void *p) {
+    uint32_t a = (uint32_t)__cvta_generic_to_shared(p);
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(a));
+}
+
+__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&r)[4], const void *p) {
+    uint32_t a = (uint32_t)__cvta_generic_to_shared(p);
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(a));
+}
+
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem, bool valid) {
+    uint32_t a = (uint32_t)__cvta_generic_to_shared(smem);
+    int bytes = valid ? 16 : 0;
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(a), "l"(gmem), "r"(bytes));
+}
+
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
+
+__device__ __forceinline__ uint32_t pack_half2(float a, float b) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t *>(&h);
+}
+
+// Shared-memory plan (bytes) for width DW = L + R and L.
+struct AttnSmem {
+    static __host__ __device__ constexpr int stride(int dw) { return dw + 8; }  // halves
+    static __host__ __device__ constexpr size_t q_bytes(int dw) { return (size_t)kAttnQ * stride(dw) * 2; }
+    static __host__ __device__ constexpr size_t k_bytes(int dw) { return (size_t)kAttnKeys * stride(dw) * 2; }
+    static __host__ __device__ constexpr size_t p_bytes() { return (size_t)kAttnQ * (kAttnKeys + 8) * 2; }
+    static __host__ __device__ constexpr size_t total(int dw) {
+        return q_bytes(dw) + 2 * k_bytes(dw) + p_bytes() + (size_t)(4 * kAttnQ * 2 + 3 * kAttnQ) * 4;
+    }
+};
+
+// grid (query tiles, splits).  Each split covers chunks [split*G, split*G+G).
+// Writes unnormalized partial outputs part_o [split][q][L], part_m / part_l
+// [split][q] (m = -inf, l = 0 when no key of the split is visible).
+template <int L, int R>
+__global__ void __launch_bounds__(kAttnThreads, 1)
+mla_attention_kernel(const __half *cache, const __half *qcat, int S, int H, int chunks_per_split,
+                     const int *d_pos, float softmax_scale, float *part_o, float *part_m,
+                     float *part_l) {
+    constexpr int DW = L + R;
+    constexpr int ST = DW + 8;        // smem row stride (halves)
+    constexpr int PST = kAttnKeys + 8;
+    constexpr int NCB = L / 4;        // O columns per warp (4 column blocks)
+    constexpr int NT_O = NCB / 8;     // n8 tiles per warp in P.C
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    __half *Qs = reinterpret_cast<__half *>(smem_raw);
+    __half *Ks = Qs + kAttnQ * ST;                 // 2 buffers
+    __half *Ps = Ks + 2 * kAttnKeys * ST;
+    float *red_max = reinterpret_cast<float *>(Ps + kAttnQ * PST);  // [4][32]
+    float *red_sum = red_max + 4 * kAttnQ;                          // [4][32]
+    float *m_run = red_sum + 4 * kAttnQ;
+    float *l_run = m_run + kAttnQ;
+    float *alpha = l_run + kAttnQ;
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int g = lane >> 2, j = lane & 3;
+    const int nq = S * H;
+    const int q0 = blockIdx.x * kAttnQ;
+    const int pos = *d_pos;
+    const int total_keys = pos + S;  // keys 0 .. pos+S-1 exist
+    const int chunk0 = blockIdx.y * chunks_per_split;
+    int chunk1 = chunk0 + chunks_per_split;
+    const int last_chunk = (total_keys + kAttnKeys - 1) / kAttnKeys;
+    if (chunk1 > last_chunk) chunk1 = last_chunk;
+
+    // Load the query tile (rows beyond nq are zero).
+    for (int i = tid; i < kAttnQ * (DW / 8); i += kAttnThreads) {
+        int r = i / (DW / 8), c8 = i % (DW / 8);
+        bool ok = q0 + r < nq;
+        cp_async16(Qs + r * ST + c8 * 8, qcat + (size_t)(ok ? q0 + r : 0) * DW + c8 * 8, ok);
+    }
+    if (tid < kAttnQ) {
+        m_run[tid] = -INFINITY;
+        l_run[tid] = 0.0f;
+    }
+    auto load_chunk = [&](int chunk, int buf) {
+        __half *dst = Ks + buf * kAttnKeys * ST;
+        int base = chunk * kAttnKeys;
+        for (int i = tid; i < kAttnKeys * (DW / 8); i += kAttnThreads) {
+            int r = i / (DW / 8), c8 = i % (DW / 8);
+            bool ok = base + r < total_keys;
+            cp_async16(dst + r * ST + c8 * 8,
+                       cache + (size_t)(ok ? base + r : 0) * DW + c8 * 8, ok);
+        }
+    };
+    if (chunk0 < chunk1) load_chunk(chunk0, 0);
+    cp_async_commit();
+
+    const int mt = warp >> 2;        // m16 tile of the query rows
+    const int kq = warp & 3;         // key quarter (16 keys) in S, column block in P.C
+    float o_acc[NT_O][4];
+#pragma unroll
+    for (int t = 0; t < NT_O; ++t)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) o_acc[t][e] = 0.0f;
+
+    // The visible-key limit of each of this thread's two query rows.
+    int row_limit[2];
+#pragma unroll
+    for (int h2 = 0; h2 < 2; ++h2) {
+        int q = q0 + 16 * mt + g + 8 * h2;
+        row_limit[h2] = q < nq ? pos + q / H : -1;  // key <= limit is visible
+    }
+
+    for (int chunk = chunk0; chunk < chunk1; ++chunk) {
+        int buf = (chunk - chunk0) & 1;
+        if (chunk + 1 < chunk1) load_chunk(chunk + 1, buf ^ 1);
+        cp_async_commit();
+        cp_async_wait<1>();
+        __syncthreads();
+        const __half *Kb = Ks + buf * kAttnKeys * ST;
+
+        // ---- scores: rows 16*mt.., keys 16*kq .. +16 (two n8 tiles) ----
+        float sacc[2][4];
+#pragma unroll
+        for (int t = 0; t < 2; ++t)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) sacc[t][e] = 0.0f;
+#pragma unroll 4
+        for (int d = 0; d < DW; d += 16) {
+            uint32_t a[4];
+            // A 16x16: matrices (rows 0-7, k 0-7), (rows 8-15, k 0-7), (rows 0-7, k 8-15), (rows 8-15, k 8-15)
+            const __half *ap = Qs + (16 * mt + (lane & 15)) * ST + d + 8 * (lane >> 4);
+            ldmatrix_x4(a, ap);
+            uint32_t b[4];
+            // B: keys n0..n0+7 (two n8 tiles) x k16: matrices (keys 0-7, k0-7), (keys 0-7, k8-15),
+            // (keys 8-15, k0-7), (keys 8-15, k8-15)
+            const __half *bp = Kb + (16 * kq + (lane & 7) + 8 * (lane >> 4)) * ST + d + 8 * ((lane >> 3) & 1);
+            ldmatrix_x4(b, bp);
+            mma_f16(sacc[0], a, b[0], b[1], sacc[0]);
+            mma_f16(sacc[1], a, b[2], b[3], sacc[1]);
+        }
+        // scale + mask; per-row chunk max within the warp
+        float rmax[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+        for (int t = 0; t < 2; ++t)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                int key = chunk * kAttnKeys + 16 * kq + 8 * t + 2 * j + (e & 1);
+                int h2 = e >> 1;
+                float v = key <= row_limit[h2] ? sacc[t][e] * softmax_scale : -INFINITY;
+                sacc[t][e] = v;
+                rmax[h2] = fmaxf(rmax[h2], v);
+            }
+#pragma unroll
+        for (int h2 = 0; h2 < 2; ++h2) {
+            rmax[h2] = fmaxf(rmax[h2], __shfl_xor_sync(0xffffffffu, rmax[h2], 1));
+            rmax[h2] = fmaxf(rmax[h2], __shfl_xor_sync(0xffffffffu, rmax[h2], 2));
+        }
+        if (j == 0) {
+            red_max[kq * kAttnQ + 16 * mt + g] = rmax[0];
+            red_max[kq * kAttnQ + 16 * mt + g + 8] = rmax[1];
+        }
+        __syncthreads();
+        float m_new[2], rsum[2] = {0.0f, 0.0f};
+#pragma unroll
+        for (int h2 = 0; h2 < 2; ++h2) {
+            int r = 16 * mt + g + 8 * h2;
+            float cm = fmaxf(fmaxf(red_max[r], red_max[kAttnQ + r]),
+                             fmaxf(red_max[2 * kAttnQ + r], red_max[3 * kAttnQ + r]));
+            m_new[h2] = fmaxf(m_run[r], cm);
+        }
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+            float p[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                int h2 = e >> 1;
+                p[e] = m_new[h2] == -INFINITY ? 0.0f : expf(sacc[t][e] - m_new[h2]);
+                rsum[h2] += p[e];
+            }
+            int col = 16 * kq + 8 * t + 2 * j;
+            int r0 = 16 * mt + g;
+            *reinterpret_cast<uint32_t *>(Ps + r0 * PST + col) = pack_half2(p[0], p[1]);
+            *reinterpret_cast<uint32_t *>(Ps + (r0 + 8) * PST + col) = pack_half2(p[2], p[3]);
+        }
+#pragma unroll
+        for (int h2 = 0; h2 < 2; ++h2) {
+            rsum[h2] += __shfl_xor_sync(0xffffffffu, rsum[h2], 1);
+            rsum[h2] += __shfl_xor_sync(0xffffffffu, rsum[h2], 2);
+        }
+        if (j == 0) {
+            red_sum[kq * kAttnQ + 16 * mt + g] = rsum[0];
+            red_sum[kq * kAttnQ + 16 * mt + g + 8] = rsum[1];
+        }
+        __syncthreads();
+        if (tid < kAttnQ) {
+            float cm = fmaxf(fmaxf(red_max[tid], red_max[kAttnQ + tid]),
+                             fmaxf(red_max[2 * kAttnQ + tid], red_max[3 * kAttnQ + tid]));
+            float mo = m_run[tid];
+            float mn = fmaxf(mo, cm);
+            float a = (mn == -INFINITY) ? 1.0f : expf(mo - mn);
+            float cs = red_sum[tid] + red_sum[kAttnQ + tid] + red_sum[2 * kAttnQ + tid] +
+                       red_sum[3 * kAttnQ + tid];
+            l_run[tid] = l_run[tid] * a + cs;
+            m_run[tid] = mn;
+            alpha[tid] = a;
+        }
+        __syncthreads();
+
+        // ---- O += P . C over this chunk: rows 16*mt.., columns kq*NCB .. ----
+        {
+            float a0 = alpha[16 * mt + g], a1 = alpha[16 * mt + g + 8];
+#pragma unroll
+            for (int t = 0; t < NT_O; ++t) {
+                o_acc[t][0] *= a0; o_acc[t][1] *= a0;
+                o_acc[t][2] *= a1; o_acc[t][3] *= a1;
+            }
+        }
+#pragma unroll
+        for (int ks = 0; ks < kAttnKeys; ks += 16) {
+            uint32_t a[4];
+            ldmatrix_x4(a, Ps + (16 * mt + (lane & 15)) * PST + ks + 8 * (lane >> 4));
+#pragma unroll
+            for (int t = 0; t < NT_O; t += 2) {
+                // B = C[key][l]: k = keys ks..ks+15, n = columns n0..n0+15 (two n8 tiles)
+                int n0 = kq * NCB + 8 * t;
+                uint32_t b[4];
+                const __half *bp = Kb + (ks + (lane & 7) + 8 * ((lane >> 3) & 1)) * ST + n0 + 8 * (lane >> 4);
+                ldmatrix_x4_trans(b, bp);
+                mma_f16(o_acc[t], a, b[0], b[1], o_acc[t]);
+                mma_f16(o_acc[t + 1], a, b[2], b[3], o_acc[t + 1]);
+            }
+        }
+        __syncthreads();  // Ps / Kb reuse
+    }
+    cp_async_wait<0>();
+
+    // ---- write partials ----
+    const int split = blockIdx.y;
+#pragma unroll
+    for (int t = 0; t < NT_O; ++t) {
+        int col = kq * NCB + 8 * t + 2 * j;
+#pragma unroll
+        for (int h2 = 0; h2 < 2; ++h2) {
+            int q = q0 + 16 * mt + g + 8 * h2;
+            if (q < nq) {
+                float2 v = make_float2(o_acc[t][2 * h2], o_acc[t][2 * h2 + 1]);
+                *reinterpret_cast<float2 *>(part_o + ((size_t)split * nq + q) * L + col) = v;
+            }
+        }
+    }
+    __syncthreads();
+    if (tid < kAttnQ && q0 + tid < nq) {
+        part_m[(size_t)split * nq + q0 + tid] = m_run[tid];
+        part_l[(size_t)split * nq + q0 + tid] = l_run[tid];
+    }
+}
+
+// Combines the split partials in split order and writes the latent context of
+// each (row s, head h) in xq format at ctx_xq + h * head_stride + s * L * 2.
+__global__ void mla_combine_kernel(const float *part_o, const float *part_m, const float *part_l,
+                                   int splits, int S, int H, int L, __half *ctx_xq,
+                                   size_t head_stride) {
+    int q = blockIdx.x;
+    int nq = S * H;
+    float M = -INFINITY;
+    for (int i = 0; i < splits; ++i) M = fmaxf(M, part_m[(size_t)i * nq + q]);
+    float den = 0.0f;
+    for (int i = 0; i < splits; ++i) {
+        float m = part_m[(size_t)i * nq + q];
+        if (m != -INFINITY) den += expf(m - M) * part_l[(size_t)i * nq + q];
+    }
+    int s = q / H, h = q % H;
+    for (int l = threadIdx.x; l < L; l += blockDim.x) {
+        float acc = 0.0f;
+        for (int i = 0; i < splits; ++i) {
+            float m = part_m[(size_t)i * nq + q];
+            if (m != -INFINITY) acc += expf(m - M) * part_o[((size_t)i * nq + q) * L + l];
+        }
+        store_xq(ctx_xq + (size_t)h * head_stride, L, s, l, acc / den);
+    }
+}
+
+}  // namespace fc

@@ -1,0 +1,302 @@
+// moe.cuh - top-k router, device-side expert grouping and the grouped expert
+// GEMVs of the MoE block.
+//
+// Replaces moonlight_route_sigmoid_topk (moonlight_kernels.metal:469-512),
+// the host-side prepare_route_tables (moonlight_metal.m:525-559, a GPU->host
+// round trip per layer in the reference) and the per-expert
+// gather / gate / up / SiLU / down / scatter sequence of
+// encode_moe_residual_buffer (moonlight_metal.m:561-676), under the
+// moe_route.h / moe_exec.h contract:
+//   - scores by MoeScoreFn; the selection bias changes selection only;
+//   - top-k by repeated argmax, lower expert index on ties;
+//   - weights normalized with +1e-20, then times routed_scale;
+//   - routed experts summed in ascending expert id, then the shared experts
+//     with coefficient 1 (moe_exec.h:97-110), no atomics.
+#pragma once
+
+#include "common.cuh"
+#include "gemv.cuh"
+
+namespace fc {
+
+// Router logits, fp32 weights [E][D]: one warp per expert row, float4 loads,
+// S <= 8 accumulators, fixed lane order then a fixed butterfly.
+__global__ void router_logits_kernel(const float *W, const float *x, int E, int D, int S,
+                                     float *logits) {
+    int e = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    int lane = threadIdx.x & 31;
+    if (e >= E) return;
+    float acc[8];
+#pragma unroll
+    for (int s = 0; s < 8; ++s) acc[s] = 0.0f;
+    const float4 *w4 = reinterpret_cast<const float4 *>(W + (size_t)e * D);
+    for (int k4 = lane; k4 < D / 4; k4 += 32) {
+        float4 w = __ldg(w4 + k4);
+#pragma unroll
+        for (int s = 0; s < 8; ++s) {
+            if (s < S) {
+                float4 xv = *reinterpret_cast<const float4 *>(x + (size_t)s * D + 4 * k4);
+                acc[s] = fmaf(w.x, xv.x, acc[s]);
+                acc[s] = fmaf(w.y, xv.y, acc[s]);
+                acc[s] = fmaf(w.z, xv.z, acc[s]);
+                acc[s] = fmaf(w.w, xv.w, acc[s]);
+            }
+        }
+    }
+#pragma unroll
+    for (int s = 0; s < 8; ++s) {
+        float v = warp_sum(acc[s]);
+        if (lane == 0 && s < S) logits[(size_t)s * E + e] = v;
+    }
+}
+
+struct RouteParams {
+    int E, K, S;
+    int score_fn, normalize;
+    float routed_scale;
+    const float *bias;       // nullable
+    const int *hash;         // nullable [vocab][K] (fixed routes)
+    const int *ids;          // token ids [S] (hash routing)
+    int expert_lo, expert_hi;  // experts owned by this rank [lo, hi)
+    int *route_ids;          // [S][K] selection order
+    float *route_w;          // [S][K]
+    int *n_active;           // number of local active experts
+    int *active;             // [max_slots] ascending expert ids (local range)
+    float *coef;             // [max_slots][8] coefficient of slot for row s
+};
+
+__device__ __forceinline__ float route_score(float x, int fn) {
+    if (fn == FC_SCORE_SQRT_SOFTPLUS) {
+        float sp;
+        if (x > 20.0f) sp = x;
+        else if (x < -20.0f) sp = expf(x);
+        else sp = log1pf(expf(x));
+        return sqrtf(sp);
+    }
+    return 1.0f / (1.0f + expf(-x));
+}
+
+// One block of 256 threads; warp s handles row s (S <= 8).
+__global__ void route_select_kernel(const float *logits, RouteParams p) {
+    extern __shared__ float rs_smem[];  // scores [8][E], choice [8][E]
+    __shared__ int used_flag[1024];
+    __shared__ int slot_of[1024];
+    __shared__ int sel[8][64];
+    __shared__ float selw[8][64];
+    const int E = p.E, K = p.K;
+    float *scores = rs_smem;
+    float *choice = rs_smem + 8 * E;
+    int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int e = threadIdx.x; e < E; e += blockDim.x) used_flag[e] = 0;
+    if (warp < p.S) {
+        int s = warp;
+        const float *lg = logits + (size_t)s * E;
+        float *sc = scores + s * E;
+        float *ch = choice + s * E;
+        if (p.score_fn == FC_SCORE_SOFTMAX) {
+            // moe_route.h:26-37, sequential max and sum on lane 0
+            if (lane == 0) {
+                float m = lg[0];
+                for (int e = 1; e < E; ++e) if (lg[e] > m) m = lg[e];
+                float sum = 0.0f;
+                for (int e = 0; e < E; ++e) { sc[e] = expf(lg[e] - m); sum += sc[e]; }
+                for (int e = 0; e < E; ++e) sc[e] = sc[e] / sum;
+            }
+            __syncwarp();
+        } else {
+            for (int e = lane; e < E; e += 32) sc[e] = route_score(lg[e], p.score_fn);
+            __syncwarp();
+        }
+        for (int e = lane; e < E; e += 32) ch[e] = sc[e] + (p.bias ? p.bias[e] : 0.0f);
+        __syncwarp();
+        if (p.hash) {
+            if (lane < K) {
+                int e = p.hash[(size_t)p.ids[s] * K + lane];
+                sel[s][lane] = e;
+                selw[s][lane] = sc[e];
+            }
+        } else {
+            for (int k = 0; k < K; ++k) {
+                float best = -INFINITY;
+                int bi = 0x7fffffff;
+                for (int e = lane; e < E; e += 32) {
+                    bool taken = false;
+                    for (int t = 0; t < k; ++t) taken |= sel[s][t] == e;
+                    float v = ch[e];
+                    if (!taken && v > best) { best = v; bi = e; }
+                }
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    float ov = __shfl_xor_sync(0xffffffffu, best, o);
+                    int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                    if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
+                }
+                if (lane == 0) {
+                    sel[s][k] = bi;
+                    selw[s][k] = sc[bi];
+                }
+                __syncwarp();
+            }
+        }
+        __syncwarp();
+        if (lane == 0) {  // moe_route_finalize, moe_route.h:89-99
+            float w[64];
+            for (int k = 0; k < K; ++k) w[k] = selw[s][k];
+            if (p.normalize) {
+                float sum = 0.0f;
+                for (int k = 0; k < K; ++k) sum += w[k];
+                sum += 1e-20f;
+                for (int k = 0; k < K; ++k) w[k] = w[k] / sum;
+            }
+            for (int k = 0; k < K; ++k) {
+                w[k] = w[k] * p.routed_scale;
+                p.route_ids[s * K + k] = sel[s][k];
+                p.route_w[s * K + k] = w[k];
+                selw[s][k] = w[k];
+            }
+        }
+    }
+    __syncthreads();
+    // Device-side grouping: ascending list of active local experts.
+    if (threadIdx.x < p.S * K) {
+        int s = threadIdx.x / K, k = threadIdx.x % K;
+        int e = sel[s][k];
+        if (e >= p.expert_lo && e < p.expert_hi) used_flag[e] = 1;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int n = 0;
+        for (int e = p.expert_lo; e < p.expert_hi; ++e) {
+            slot_of[e] = n;
+            if (used_flag[e]) p.active[n++] = e;
+        }
+        *p.n_active = n;
+        for (int i = 0; i < n * 8; ++i) p.coef[i] = 0.0f;
+        for (int s = 0; s < p.S; ++s)
+            for (int k = 0; k < K; ++k) {
+                int e = sel[s][k];
+                if (e >= p.expert_lo && e < p.expert_hi) p.coef[slot_of[e] * 8 + s] = selw[s][k];
+            }
+    }
+}
+
+// Grouped expert GEMV.  Blocks [0, max_slots * tiles) serve the routed slots
+// (slot >= *n_active exits), the rest serve the shared expert (`shared`,
+// member 0).  Routed member = active[slot]; inputs / outputs are per slot.
+struct MoeGemv {
+    GemvSeg routed;          // w, sc, (w2, sc2) at expert 0; strides per expert
+    GemvSeg shared;          // static segment (count 1)
+    int max_slots;
+    int routed_tiles;
+    int shared_tiles;
+    const int *n_active;
+    const int *active;
+    int64_t in_slot_stride;  // halves between slots' xq inputs (0 = shared input)
+    int64_t out_slot_stride; // routed outputs: floats (EPI_STORE) or halves (xq)
+    int S;
+    float swiglu_limit;
+};
+
+template <int FE, int FS>
+__global__ void __launch_bounds__(kGemvThreads, 2) moe_gemv_kernel(const __grid_constant__ MoeGemv m) {
+    __shared__ float red[kGemvWarps * 2 * 32 * 4];
+    __shared__ float out[kGemvRows * 8];
+    int block = blockIdx.x;
+    int routed_blocks = m.max_slots * m.routed_tiles;
+    if (block < routed_blocks) {
+        int slot = block / m.routed_tiles, tile = block % m.routed_tiles;
+        if (slot >= *m.n_active) return;
+        int e = m.active[slot];
+        GemvSeg sg = m.routed;
+        const size_t se = FE == FC_FMT_MXFP4 ? 1 : 2;
+        const uint8_t *w = sg.w + e * sg.w_stride;
+        const uint8_t *sc = reinterpret_cast<const uint8_t *>(sg.sc) + e * sg.sc_stride * se;
+        const __half *xq = sg.xq + slot * m.in_slot_stride;
+        const int rb = row_bytes(FE, sg.kp), groups = sg.kp / 32;
+        int row0;
+        if (sg.epi == EPI_SWIGLU_XQ) {
+            row0 = tile * 16;
+            const uint8_t *up = sg.w2 + e * sg.w_stride;
+            const uint8_t *usc = reinterpret_cast<const uint8_t *>(sg.sc2) + e * sg.sc_stride * se;
+            int n = min(16, sg.O - row0);
+            gemv_tile<FE>(w + (size_t)row0 * rb, sc + (size_t)row0 * groups * se, n,
+                          up + (size_t)row0 * rb, usc + (size_t)row0 * groups * se, n,
+                          sg.kp, xq, m.S, red, out);
+            sg.yq = sg.yq + slot * m.out_slot_stride;
+        } else {
+            row0 = tile * 32;
+            gemv_tile<FE>(w + (size_t)row0 * rb, sc + (size_t)row0 * groups * se,
+                          min(16, sg.O - row0), w + (size_t)(row0 + 16) * rb,
+                          sc + (size_t)(row0 + 16) * groups * se, min(16, sg.O - row0 - 16),
+                          sg.kp, xq, m.S, red, out);
+            sg.y = sg.y + slot * m.out_slot_stride;
+        }
+        gemv_epilogue(sg, 0, row0, m.S, m.swiglu_limit, out);
+        return;
+    }
+    block -= routed_blocks;
+    if (block >= m.shared_tiles) return;
+    const GemvSeg &sg = m.shared;
+    const size_t se = FS == FC_FMT_MXFP4 ? 1 : 2;
+    const uint8_t *sc = reinterpret_cast<const uint8_t *>(sg.sc);
+    const int rb = row_bytes(FS, sg.kp), groups = sg.kp / 32;
+    int row0;
+    if (sg.epi == EPI_SWIGLU_XQ) {
+        row0 = block * 16;
+        const uint8_t *usc = reinterpret_cast<const uint8_t *>(sg.sc2);
+        int n = min(16, sg.O - row0);
+        gemv_tile<FS>(sg.w + (size_t)row0 * rb, sc + (size_t)row0 * groups * se, n,
+                      sg.w2 + (size_t)row0 * rb, usc + (size_t)row0 * groups * se, n, sg.kp,
+                      sg.xq, m.S, red, out);
+    } else {
+        row0 = block * 32;
+        gemv_tile<FS>(sg.w + (size_t)row0 * rb, sc + (size_t)row0 * groups * se,
+                      min(16, sg.O - row0), sg.w + (size_t)(row0 + 16) * rb,
+                      sc + (size_t)(row0 + 16) * groups * se, min(16, sg.O - row0 - 16), sg.kp,
+                      sg.xq, m.S, red, out);
+    }
+    gemv_epilogue(sg, 0, row0, m.S, m.swiglu_limit, out);
+}
+
+inline cudaError_t launch_moe_gemv(int fe, int fs, MoeGemv &m, cudaStream_t stream) {
+    m.routed_tiles = gemv_tiles(m.routed);
+    m.shared_tiles = m.shared.w ? gemv_tiles(m.shared) : 0;
+    int blocks = m.max_slots * m.routed_tiles + m.shared_tiles;
+    if (blocks == 0) return cudaSuccess;
+#define FC_MOE_CASE(A, B)                                                              \
+    if (fe == A && fs == B) {                                                          \
+        moe_gemv_kernel<A, B><<<blocks, kGemvThreads, 0, stream>>>(m);                 \
+        return cudaGetLastError();                                                     \
+    }
+    FC_MOE_CASE(FC_FMT_Q8, FC_FMT_Q8)
+    FC_MOE_CASE(FC_FMT_Q4, FC_FMT_Q4)
+    FC_MOE_CASE(FC_FMT_MXFP4, FC_FMT_Q8)
+    FC_MOE_CASE(FC_FMT_Q4, FC_FMT_Q8)
+    FC_MOE_CASE(FC_FMT_MXFP4, FC_FMT_MXFP4)
+    FC_MOE_CASE(FC_FMT_Q8, FC_FMT_Q4)
+#undef FC_MOE_CASE
+    return cudaErrorInvalidValue;
+}
+
+// resid[s][d] += (sum over slots ascending of coef * routed[slot][s][d])
+//                + shared[s][d]                           (moe_exec.h:97-110)
+// Products and sums are rounded separately (no contraction), the order the
+// C reference spells out.
+__global__ void moe_combine_kernel(float *resid, const float *routed, const float *shared,
+                                   const float *coef, const int *n_active, int S, int D,
+                                   int max_batch) {
+    int idx = blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= S * D) return;
+    int s = idx / D, d = idx % D;
+    int n = *n_active;
+    float y = 0.0f;
+    for (int slot = 0; slot < n; ++slot) {
+        float c = coef[slot * 8 + s];
+        if (c != 0.0f)
+            y = __fadd_rn(y, __fmul_rn(c, routed[((size_t)slot * max_batch + s) * D + d]));
+    }
+    if (shared) y = __fadd_rn(y, shared[(size_t)s * D + d]);
+    resid[(size_t)s * D + d] = __fadd_rn(resid[(size_t)s * D + d], y);
+}
+
+}  // namespace fc

@@ -1,0 +1,1414 @@
+// runtime.cu - model, session and C ABI of the B200 verify-step backend
+// (include/floyd_cuda.h).
+//
+// The host side mirrors moonlight_metal.m: weights resident on the device,
+// every session buffer allocated up front (moonlight_metal.m:938-1125), one
+// submission per forward.  Where the Metal runtime records a command buffer
+// per MoE layer and round-trips the route tables through the host
+// (moonlight_metal.m:1892-1986), here the whole forward - embedding, every
+// layer, lm-head, argmax and acceptance - is one CUDA graph per row count,
+// with one H2D copy of the per-call parameters at its head and one D2H copy
+// of the result at its tail.  Everything runs on the GPU; a missing or
+// failing kernel is an error, never a CPU fallback.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <string>
+#include <vector>
+
+#include "../../include/floyd_kernels.h"
+#include "common.cuh"
+#include "gemv.cuh"
+#include "head.cuh"
+#include "mla.cuh"
+#include "moe.cuh"
+#include "synth.cuh"
+
+using namespace fc;
+
+namespace {
+
+int set_error(char *error, size_t error_size, const char *format, ...) {
+    if (error && error_size) {
+        va_list args;
+        va_start(args, format);
+        vsnprintf(error, error_size, format, args);
+        va_end(args);
+    }
+    return 0;
+}
+
+double now_ms() {
+    return std::chrono::duration<double, std::milli>(
+               std::chrono::steady_clock::now().time_since_epoch())
+        .count();
+}
+
+inline int kpad(int k) { return (k + 127) / 128 * 128; }
+
+// A matrix (or a family of `count` equally shaped matrices) in device layout.
+struct DevMat {
+    int fmt = FC_FMT_F32, O = 0, K = 0, kp = 0, count = 0;
+    uint8_t *w = nullptr;   // values (or fp32 data for F32)
+    void *sc = nullptr;     // group scales
+    size_t w_bytes = 0;     // per member
+    size_t sc_bytes = 0;    // per member
+    size_t sc_elems = 0;    // per member
+    uint32_t tid = 0;       // synthetic tensor id (slot 0)
+    int slot0 = 0;          // synthetic slot of member 0
+};
+
+struct DevVec {
+    float *p = nullptr;
+    size_t n = 0;
+    uint32_t tid = 0;
+    int kind = 1;  // 0 f32 matrix, 1 norm, 2 bias
+};
+
+struct DevLayer {
+    DevVec attn_norm, ffn_norm, kv_a_norm, q_a_norm, router, bias;
+    DevMat q_proj, q_a, q_b, kv_a, kv_b, o_proj;
+    DevMat d_gate, d_up, d_down;
+    DevMat e_gate, e_up, e_down;   // routed expert families (local experts)
+    DevMat s_gate, s_up, s_down;   // shared experts (one wide MLP)
+    int *hash = nullptr;           // [vocab][K] or null
+    uint32_t hash_tid = 0;
+    bool dense = false;
+};
+
+struct TensorRef {
+    DevMat *mat = nullptr;
+    int member = 0;
+    DevVec *vec = nullptr;
+    int *ints = nullptr;
+    size_t ints_n = 0;
+};
+
+}  // namespace
+
+struct FcModel {
+    FcModelConfig c{};
+    int device = 0;
+    int expert_lo = 0, expert_hi = 0;  // local routed experts
+    std::string device_name;
+    uint8_t *arena = nullptr;
+    size_t arena_bytes = 0, arena_used = 0;
+    DevMat embed, lm_head;
+    DevVec final_norm;
+    std::vector<DevLayer> layers;
+    std::map<std::string, TensorRef> names;
+    uint64_t resident = 0;
+};
+
+struct FcSession {
+    FcModel *m = nullptr;
+    FcOptions opt{};
+    cudaStream_t stream = nullptr;
+    int rows_max = 0;        // rows per pass (<= kMaxRows)
+    int position = 0;
+    int last_rows = 0;
+    int max_slots = 0;
+    int splits = 0, chunks_per_split = 1;
+    int head_chunks = 0;
+    std::vector<void *> allocs;
+    FcStats stats{};
+    // buffers
+    __half *cache = nullptr;
+    float *resid = nullptr, *xn = nullptr, *q = nullptr, *qa = nullptr, *ckv = nullptr;
+    __half *xq_norm = nullptr, *qa_xq = nullptr, *qcat = nullptr, *ctx_xq = nullptr, *o_xq = nullptr;
+    float *part_o = nullptr, *part_m = nullptr, *part_l = nullptr;
+    float *router_logits = nullptr, *route_w = nullptr, *coef = nullptr;
+    int *route_ids = nullptr, *n_active = nullptr, *active = nullptr;
+    __half *h_xq = nullptr, *hsh_xq = nullptr, *hd_xq = nullptr;
+    float *moe_part = nullptr, *sh_part = nullptr;
+    float *logits = nullptr, *last_logits = nullptr, *layer_out = nullptr;
+    HeadPartials hp{};
+    Staging *d_stage = nullptr, *h_stage = nullptr;
+    Result *d_res = nullptr, *h_res = nullptr;
+    std::map<int, cudaGraphExec_t> graphs;
+    size_t attn_smem = 0;
+    cudaEvent_t ev_begin = nullptr, ev_end = nullptr;   // device time of each pass
+    // per-kernel profiling (eager passes with an event after every launch)
+    bool profiling = false;
+    bool trace = false;      // per-layer hidden-state copies (test hook)
+    std::vector<cudaEvent_t> prof_events;
+    std::vector<std::string> prof_marks;
+    std::vector<std::pair<std::string, std::pair<double, uint64_t>>> prof;
+};
+
+namespace {
+
+// ---------------------------------------------------------------------------
+// model construction
+// ---------------------------------------------------------------------------
+size_t align256(size_t n) { return (n + 255) / 256 * 256; }
+
+void plan_mat(DevMat &m, int fmt, int O, int K, int count, uint32_t tid, int slot0) {
+    m.fmt = fmt; m.O = O; m.K = K; m.count = count; m.tid = tid; m.slot0 = slot0;
+    if (fmt == FC_FMT_F32) {
+        m.kp = K;
+        m.w_bytes = (size_t)O * K * 4;
+        m.sc_bytes = 0;
+        m.sc_elems = 0;
+    } else {
+        m.kp = kpad(K);
+        m.w_bytes = (size_t)O * row_bytes(fmt, m.kp);
+        m.sc_elems = (size_t)O * (m.kp / 32);
+        m.sc_bytes = m.sc_elems * (fmt == FC_FMT_MXFP4 ? 1 : 2);
+    }
+}
+
+size_t mat_bytes(const DevMat &m) {
+    if (!m.count) return 0;
+    return align256(m.w_bytes * m.count) + align256(m.sc_bytes * m.count);
+}
+
+void place_mat(FcModel *model, DevMat &m) {
+    if (!m.count) return;
+    m.w = model->arena + model->arena_used;
+    model->arena_used += align256(m.w_bytes * m.count);
+    if (m.sc_bytes) {
+        m.sc = model->arena + model->arena_used;
+        model->arena_used += align256(m.sc_bytes * m.count);
+    }
+}
+
+void plan_vec(DevVec &v, size_t n, uint32_t tid, int kind) { v.n = n; v.tid = tid; v.kind = kind; }
+
+void place_vec(FcModel *model, DevVec &v) {
+    if (!v.n) return;
+    v.p = reinterpret_cast<float *>(model->arena + model->arena_used);
+    model->arena_used += align256(v.n * 4);
+}
+
+template <typename F>
+void for_each_tensor(FcModel *m, F f) {
+    f(&m->embed, nullptr);
+    f(&m->lm_head, nullptr);
+    f(nullptr, &m->final_norm);
+    for (auto &y : m->layers) {
+        DevVec *vecs[] = {&y.attn_norm, &y.ffn_norm, &y.kv_a_norm, &y.q_a_norm, &y.router, &y.bias};
+        for (DevVec *v : vecs) f(nullptr, v);
+        DevMat *mats[] = {&y.q_proj, &y.q_a, &y.q_b, &y.kv_a, &y.kv_b, &y.o_proj,
+                          &y.d_gate, &y.d_up, &y.d_down, &y.e_gate, &y.e_up, &y.e_down,
+                          &y.s_gate, &y.s_up, &y.s_down};
+        for (DevMat *mm : mats) f(mm, nullptr);
+    }
+}
+
+bool config_ok(const FcModelConfig *c, char *err, size_t n) {
+    if (c->hidden_size <= 0 || c->layer_count <= 0 || c->vocab_size <= 0 || c->head_count <= 0)
+        return set_error(err, n, "invalid model dimensions");
+    if (c->hidden_size % 32 || c->kv_lora_rank % 32 || (c->q_lora_rank % 32) ||
+        c->moe_intermediate_size % 32 || c->dense_intermediate_size % 32 ||
+        (c->head_count * c->value_dim) % 32)
+        return set_error(err, n, "every matrix input width must be a multiple of 32");
+    if (c->hidden_size % 4)
+        return set_error(err, n, "hidden_size must be a multiple of 4");
+    if (!(c->kv_lora_rank == 512 && c->qk_rope_dim == 64) &&
+        !(c->kv_lora_rank == 256 && c->qk_rope_dim == 64))
+        return set_error(err, n, "supported MLA shapes: kv_lora_rank 512 or 256 with rope 64");
+    if (c->qk_rope_dim & 1) return set_error(err, n, "qk_rope_dim must be even");
+    if (c->first_dense_layer_count < c->layer_count &&
+        (c->expert_count <= 0 || c->expert_count > 1024 || c->experts_per_token <= 0 ||
+         c->experts_per_token > c->expert_count || c->experts_per_token > 64))
+        return set_error(err, n, "unsupported expert configuration");
+    auto fmt_ok = [](int f) { return f == FC_FMT_Q8 || f == FC_FMT_Q4 || f == FC_FMT_MXFP4; };
+    if (!fmt_ok(c->dense_format) || !fmt_ok(c->expert_format))
+        return set_error(err, n, "dense and expert formats must be Q8, Q4 or MXFP4");
+    if (c->first_dense_layer_count > 0 && c->dense_intermediate_size <= 0)
+        return set_error(err, n, "dense layers need dense_intermediate_size");
+    return true;
+}
+
+int build_model(FcModel *m, char *err, size_t n) {
+    const FcModelConfig &c = m->c;
+    int D = c.hidden_size, H = c.head_count, L = c.kv_lora_rank, R = c.qk_rope_dim;
+    int df = c.dense_format, ef = c.expert_format;
+    plan_mat(m->embed, df, c.vocab_size, D, 1, fc_tensor_id(-1, FC_T_EMBED, 0), 0);
+    plan_mat(m->lm_head, df, c.vocab_size, D, 1, fc_tensor_id(-1, FC_T_LM_HEAD, 0), 0);
+    plan_vec(m->final_norm, D, fc_tensor_id(-1, FC_T_FINAL_NORM, 0), 1);
+    m->layers.resize(c.layer_count);
+    int nl = m->expert_hi - m->expert_lo;
+    for (int l = 0; l < c.layer_count; ++l) {
+        DevLayer &y = m->layers[l];
+        plan_vec(y.attn_norm, D, fc_tensor_id(l, FC_T_ATTN_NORM, 0), 1);
+        plan_vec(y.ffn_norm, D, fc_tensor_id(l, FC_T_FFN_NORM, 0), 1);
+        plan_vec(y.kv_a_norm, L, fc_tensor_id(l, FC_T_KV_A_NORM, 0), 1);
+        int qw = H * (c.qk_nope_dim + R);
+        if (c.q_lora_rank > 0) {
+            plan_vec(y.q_a_norm, c.q_lora_rank, fc_tensor_id(l, FC_T_Q_A_NORM, 0), 1);
+            plan_mat(y.q_a, df, c.q_lora_rank, D, 1, fc_tensor_id(l, FC_T_Q_A, 0), 0);
+            plan_mat(y.q_b, df, qw, c.q_lora_rank, 1, fc_tensor_id(l, FC_T_Q_B, 0), 0);
+        } else {
+            plan_mat(y.q_proj, df, qw, D, 1, fc_tensor_id(l, FC_T_Q_PROJ, 0), 0);
+        }
+        plan_mat(y.kv_a, df, L + R, D, 1, fc_tensor_id(l, FC_T_KV_A, 0), 0);
+        plan_mat(y.kv_b, df, H * (c.qk_nope_dim + c.value_dim), L, 1, fc_tensor_id(l, FC_T_KV_B, 0), 0);
+        plan_mat(y.o_proj, df, D, H * c.value_dim, 1, fc_tensor_id(l, FC_T_O_PROJ, 0), 0);
+        y.dense = l < c.first_dense_layer_count;
+        if (y.dense) {
+            int I = c.dense_intermediate_size;
+            plan_mat(y.d_gate, df, I, D, 1, fc_tensor_id(l, FC_T_DENSE_GATE, 0), 0);
+            plan_mat(y.d_up, df, I, D, 1, fc_tensor_id(l, FC_T_DENSE_UP, 0), 0);
+            plan_mat(y.d_down, df, D, I, 1, fc_tensor_id(l, FC_T_DENSE_DOWN, 0), 0);
+            continue;
+        }
+        int E = c.expert_count, I = c.moe_intermediate_size;
+        plan_vec(y.router, (size_t)E * D, fc_tensor_id(l, FC_T_ROUTER, 0), 0);
+        if (c.has_selection_bias) plan_vec(y.bias, E, fc_tensor_id(l, FC_T_ROUTER_BIAS, 0), 2);
+        // slot of expert e is e + 1; the local family starts at expert_lo
+        plan_mat(y.e_gate, ef, I, D, nl, fc_tensor_id(l, FC_T_EXP_GATE, 0), m->expert_lo + 1);
+        plan_mat(y.e_up, ef, I, D, nl, fc_tensor_id(l, FC_T_EXP_UP, 0), m->expert_lo + 1);
+        plan_mat(y.e_down, ef, D, I, nl, fc_tensor_id(l, FC_T_EXP_DOWN, 0), m->expert_lo + 1);
+        if (c.shared_expert_count > 0) {
+            int W = I * c.shared_expert_count;
+            plan_mat(y.s_gate, df, W, D, 1, fc_tensor_id(l, FC_T_SH_GATE, 0), 0);
+            plan_mat(y.s_up, df, W, D, 1, fc_tensor_id(l, FC_T_SH_UP, 0), 0);
+            plan_mat(y.s_down, df, D, W, 1, fc_tensor_id(l, FC_T_SH_DOWN, 0), 0);
+        }
+        if (l < c.hash_layer_count) y.hash_tid = fc_tensor_id(l, FC_T_HASH, 0);
+    }
+    // size the arena
+    size_t total = 0;
+    for_each_tensor(m, [&](DevMat *mm, DevVec *v) {
+        if (mm) total += mat_bytes(*mm);
+        if (v) total += align256(v->n * 4);
+    });
+    size_t hash_bytes = 0;
+    for (auto &y : m->layers)
+        if (y.hash_tid) hash_bytes += align256((size_t)c.vocab_size * c.experts_per_token * 4);
+    total += hash_bytes;
+    size_t free_b = 0, total_b = 0;
+    cudaMemGetInfo(&free_b, &total_b);
+    if (total > free_b / 100 * 95)
+        return set_error(err, n, "model requires %.2f GiB, above 95%% of free device memory %.2f GiB",
+                         total / 1073741824.0, free_b / 1073741824.0);
+    if (cudaMalloc(&m->arena, total) != cudaSuccess)
+        return set_error(err, n, "device allocation of %.2f GiB failed", total / 1073741824.0);
+    m->arena_bytes = total;
+    cudaMemset(m->arena, 0, total);
+    for_each_tensor(m, [&](DevMat *mm, DevVec *v) {
+        if (mm) place_mat(m, *mm);
+        if (v) place_vec(m, *v);
+    });
+    for (auto &y : m->layers)
+        if (y.hash_tid) {
+            y.hash = reinterpret_cast<int *>(m->arena + m->arena_used);
+            m->arena_used += align256((size_t)c.vocab_size * c.experts_per_token * 4);
+        }
+    m->resident = total;
+
+    // checkpoint names (moonlight_metal.m:301-321, :450-466, :494-500, :580-612)
+    auto add_mat = [&](const std::string &name, DevMat &mm, int member) {
+        if (mm.count) m->names[name] = TensorRef{&mm, member, nullptr, nullptr, 0};
+    };
+    auto add_vec = [&](const std::string &name, DevVec &v) {
+        if (v.n) m->names[name] = TensorRef{nullptr, 0, &v, nullptr, 0};
+    };
+    add_mat("model.embed_tokens.weight", m->embed, 0);
+    add_mat("lm_head.weight", m->lm_head, 0);
+    add_vec("model.norm.weight", m->final_norm);
+    for (int l = 0; l < c.layer_count; ++l) {
+        DevLayer &y = m->layers[l];
+        std::string p = "model.layers." + std::to_string(l) + ".";
+        add_vec(p + "input_layernorm.weight", y.attn_norm);
+        add_vec(p + "post_attention_layernorm.weight", y.ffn_norm);
+        add_vec(p + "self_attn.kv_a_layernorm.weight", y.kv_a_norm);
+        add_vec(p + "self_attn.q_a_layernorm.weight", y.q_a_norm);
+        add_mat(p + "self_attn.q_proj.weight", y.q_proj, 0);
+        add_mat(p + "self_attn.q_a_proj.weight", y.q_a, 0);
+        add_mat(p + "self_attn.q_b_proj.weight", y.q_b, 0);
+        add_mat(p + "self_attn.kv_a_proj_with_mqa.weight", y.kv_a, 0);
+        add_mat(p + "self_attn.kv_b_proj.weight", y.kv_b, 0);
+        add_mat(p + "self_attn.o_proj.weight", y.o_proj, 0);
+        add_mat(p + "mlp.gate_proj.weight", y.d_gate, 0);
+        add_mat(p + "mlp.up_proj.weight", y.d_up, 0);
+        add_mat(p + "mlp.down_proj.weight", y.d_down, 0);
+        add_vec(p + "mlp.gate.weight", y.router);
+        add_vec(p + "mlp.gate.e_score_correction_bias", y.bias);
+        if (y.hash)
+            m->names[p + "mlp.gate.tid2eid"] =
+                TensorRef{nullptr, 0, nullptr, y.hash, (size_t)c.vocab_size * c.experts_per_token};
+        for (int e = m->expert_lo; e < m->expert_hi && !y.dense; ++e) {
+            std::string q = p + "mlp.experts." + std::to_string(e) + ".";
+            add_mat(q + "gate_proj.weight", y.e_gate, e - m->expert_lo);
+            add_mat(q + "up_proj.weight", y.e_up, e - m->expert_lo);
+            add_mat(q + "down_proj.weight", y.e_down, e - m->expert_lo);
+        }
+        add_mat(p + "mlp.shared_experts.gate_proj.weight", y.s_gate, 0);
+        add_mat(p + "mlp.shared_experts.up_proj.weight", y.s_up, 0);
+        add_mat(p + "mlp.shared_experts.down_proj.weight", y.s_down, 0);
+    }
+    return 1;
+}
+
+int grid_for(size_t n) { return (int)std::min<size_t>((n + 255) / 256, 148 * 16); }
+
+cudaError_t fill_mat(const DevMat &mm, uint64_t seed, cudaStream_t st) {
+    if (!mm.count) return cudaSuccess;
+    if (mm.fmt == FC_FMT_F32) return cudaSuccess;
+    size_t nb = mm.w_bytes * mm.count;
+    synth_values_kernel<<<grid_for(nb), 256, 0, st>>>(mm.fmt, mm.w, mm.O, mm.K, mm.kp, mm.count,
+                                                      seed, mm.tid, mm.slot0);
+    size_t ns = mm.sc_elems * mm.count;
+    synth_scales_kernel<<<grid_for(ns), 256, 0, st>>>(mm.fmt, mm.sc, mm.O, mm.K, mm.kp, mm.count,
+                                                      seed, mm.tid, mm.slot0);
+    return cudaGetLastError();
+}
+
+// logical row-major values (int8 / packed nibbles, even element low) ->
+// device layout of member `member`
+void pack_values(const DevMat &mm, const uint8_t *src, std::vector<uint8_t> &dst) {
+    size_t rb = row_bytes(mm.fmt, mm.kp);
+    dst.assign((size_t)mm.O * rb, mm.fmt == FC_FMT_Q4 ? 0x88 : 0);
+    for (int o = 0; o < mm.O; ++o)
+        for (int k = 0; k < mm.K; ++k) {
+            int byte, nib;
+            weight_position(mm.fmt, k, byte, nib);
+            uint8_t *d = &dst[(size_t)o * rb + byte];
+            if (mm.fmt == FC_FMT_Q8) {
+                *d = src[(size_t)o * mm.K + k];
+            } else {
+                size_t e = (size_t)o * mm.K + k;
+                uint8_t v = (src[e >> 1] >> (4 * (e & 1))) & 15;
+                *d = (uint8_t)((*d & ~(15 << (4 * nib))) | (v << (4 * nib)));
+            }
+        }
+}
+
+void unpack_values(const DevMat &mm, const uint8_t *dev, uint8_t *dst) {
+    size_t rb = row_bytes(mm.fmt, mm.kp);
+    if (mm.fmt != FC_FMT_Q8) memset(dst, 0, (size_t)mm.O * mm.K / 2);
+    for (int o = 0; o < mm.O; ++o)
+        for (int k = 0; k < mm.K; ++k) {
+            int byte, nib;
+            weight_position(mm.fmt, k, byte, nib);
+            uint8_t b = dev[(size_t)o * rb + byte];
+            if (mm.fmt == FC_FMT_Q8) {
+                dst[(size_t)o * mm.K + k] = b;
+            } else {
+                size_t e = (size_t)o * mm.K + k;
+                uint8_t v = (b >> (4 * nib)) & 15;
+                dst[e >> 1] |= (uint8_t)(v << (4 * (e & 1)));
+            }
+        }
+}
+
+// ---------------------------------------------------------------------------
+// session
+// ---------------------------------------------------------------------------
+template <typename T>
+bool salloc(FcSession *s, T *&p, size_t count) {
+    void *raw = nullptr;
+    size_t bytes = align256(std::max<size_t>(count * sizeof(T), 16));
+    if (cudaMalloc(&raw, bytes) != cudaSuccess) return false;
+    cudaMemset(raw, 0, bytes);
+    s->allocs.push_back(raw);
+    s->stats.buffer_allocations++;
+    s->stats.resident_bytes += bytes;
+    p = reinterpret_cast<T *>(raw);
+    return true;
+}
+
+void free_session_buffers(FcSession *s) {
+    for (auto &g : s->graphs) cudaGraphExecDestroy(g.second);
+    s->graphs.clear();
+    for (void *p : s->allocs) cudaFree(p);
+    s->allocs.clear();
+    if (s->h_stage) cudaFreeHost(s->h_stage);
+    if (s->h_res) cudaFreeHost(s->h_res);
+    s->h_stage = nullptr;
+    s->h_res = nullptr;
+    if (s->stream) cudaStreamDestroy(s->stream);
+    s->stream = nullptr;
+    if (s->ev_begin) cudaEventDestroy(s->ev_begin);
+    if (s->ev_end) cudaEventDestroy(s->ev_end);
+    for (cudaEvent_t ev : s->prof_events) cudaEventDestroy(ev);
+    s->prof_events.clear();
+}
+
+GemvSeg seg_of(const DevMat &mm, const __half *xq, int epi) {
+    GemvSeg g{};
+    g.w = mm.w;
+    g.sc = mm.sc;
+    g.xq = xq;
+    g.O = mm.O;
+    g.kp = mm.kp;
+    g.epi = epi;
+    g.count = 1;
+    return g;
+}
+
+#define FC_TRY(expr)                                 \
+    do {                                             \
+        cudaError_t e_ = (expr);                     \
+        if (e_ != cudaSuccess) return e_;            \
+    } while (0)
+
+cudaError_t gemv1(int fmt, GemvSeg a, int S, float limit, cudaStream_t st) {
+    GemvBatch b{};
+    b.seg[0] = a;
+    b.nseg = 1;
+    b.S = S;
+    b.swiglu_limit = limit;
+    return launch_gemv_batch(fmt, b, st);
+}
+
+// Records a profiling event after the launch named `name` (eager passes only).
+void mark(FcSession *s, const char *name) {
+    if (!s->profiling) return;
+    size_t i = s->prof_marks.size();
+    if (i + 1 >= s->prof_events.size()) return;
+    s->prof_marks.push_back(name);
+    cudaEventRecord(s->prof_events[i + 1], s->stream);
+}
+
+// Enqueues one forward of `rows` rows (parameters already in d_stage) on the
+// session stream: embedding, every layer, lm-head, argmax / acceptance.
+cudaError_t record_forward(FcSession *s, int S) {
+    FcModel *m = s->m;
+    const FcModelConfig &c = m->c;
+    cudaStream_t st = s->stream;
+    const int D = c.hidden_size, H = c.head_count, L = c.kv_lora_rank, R = c.qk_rope_dim;
+    const int NP = c.qk_nope_dim, VD = c.value_dim, QW = NP + R;
+    const int kpD = kpad(D), kpL = kpad(L), kpO = kpad(H * VD);
+    const int mb = s->rows_max;
+    const int *d_pos = &s->d_stage->pos;
+    const float scale = 1.0f / sqrtf((float)(NP + R));
+    const int df = c.dense_format, ef = c.expert_format;
+
+    FC_TRY(cudaMemcpyAsync(s->d_stage, s->h_stage, sizeof(Staging), cudaMemcpyHostToDevice, st));
+    embed_kernel<<<S, 256, 0, st>>>(m->embed.fmt, m->embed.w, m->embed.sc, D, m->embed.kp,
+                                    s->d_stage->ids, s->resid);
+    FC_TRY(cudaGetLastError());
+    mark(s, "embed");
+    for (int l = 0; l < c.layer_count; ++l) {
+        DevLayer &y = m->layers[l];
+        __half *cache = s->cache + (size_t)l * s->opt.context_size * (L + R);
+        rmsnorm_kernel<<<S, 256, 0, st>>>(s->resid, D, y.attn_norm.p, D, c.rms_norm_epsilon,
+                                          s->xq_norm, kpD, nullptr, 0);
+        mark(s, "rmsnorm");
+        {
+            GemvBatch b{};
+            b.S = S;
+            if (c.q_lora_rank > 0) {
+                b.seg[0] = seg_of(y.q_a, s->xq_norm, EPI_STORE);
+                b.seg[0].y = s->qa;
+                b.seg[0].ldy = c.q_lora_rank;
+            } else {
+                b.seg[0] = seg_of(y.q_proj, s->xq_norm, EPI_STORE);
+                b.seg[0].y = s->q;
+                b.seg[0].ldy = H * QW;
+            }
+            b.seg[1] = seg_of(y.kv_a, s->xq_norm, EPI_STORE);
+            b.seg[1].y = s->ckv;
+            b.seg[1].ldy = L + R;
+            b.nseg = 2;
+            FC_TRY(launch_gemv_batch(df, b, st));
+            mark(s, "gemv_q_kv_a");
+        }
+        if (c.q_lora_rank > 0) {
+            rmsnorm_kernel<<<S, 256, 0, st>>>(s->qa, c.q_lora_rank, y.q_a_norm.p, c.q_lora_rank,
+                                              c.rms_norm_epsilon, s->qa_xq, kpad(c.q_lora_rank),
+                                              nullptr, 0);
+            mark(s, "rmsnorm");
+            GemvSeg g = seg_of(y.q_b, s->qa_xq, EPI_STORE);
+            g.y = s->q;
+            g.ldy = H * QW;
+            FC_TRY(gemv1(df, g, S, 0.0f, st));
+            mark(s, "gemv_q_b");
+        }
+        mla_prep_kernel<<<S, 256, 0, st>>>(s->ckv, s->q, y.kv_a_norm.p, L, R, H, NP,
+                                           c.rms_norm_epsilon, c.rope_theta, d_pos, cache, s->qcat);
+        mark(s, "mla_prep");
+        {
+            dim3 grid(H, (L + 127) / 128);
+            mla_absorb_kernel<<<grid, 128, 0, st>>>(df, y.kv_b.w, y.kv_b.sc, y.kv_b.kp, s->q, S, H,
+                                                    NP, VD, R, L, s->qcat);
+            mark(s, "mla_absorb");
+        }
+        {
+            dim3 grid((S * H + kAttnQ - 1) / kAttnQ, s->splits);
+            if (L == 512)
+                mla_attention_kernel<512, 64><<<grid, kAttnThreads, s->attn_smem, st>>>(
+                    cache, s->qcat, S, H, s->chunks_per_split, d_pos, scale, s->part_o, s->part_m,
+                    s->part_l);
+            else
+                mla_attention_kernel<256, 64><<<grid, kAttnThreads, s->attn_smem, st>>>(
+                    cache, s->qcat, S, H, s->chunks_per_split, d_pos, scale, s->part_o, s->part_m,
+                    s->part_l);
+            FC_TRY(cudaGetLastError());
+            mark(s, "mla_attention");
+            size_t head_stride = (size_t)mb * kpL * 2;
+            mla_combine_kernel<<<S * H, 128, 0, st>>>(s->part_o, s->part_m, s->part_l, s->splits, S,
+                                                      H, L, s->ctx_xq, head_stride);
+            mark(s, "mla_combine");
+            // W_UV: rows nope .. nope+v of each head's kv_b block (decode_value, :345-375)
+            GemvSeg g = seg_of(y.kv_b, s->ctx_xq, EPI_STORE_XQ);
+            size_t rb = row_bytes(df, y.kv_b.kp);
+            size_t groups = y.kv_b.kp / 32;
+            size_t se = df == FC_FMT_MXFP4 ? 1 : 2;
+            g.w = y.kv_b.w + (size_t)NP * rb;
+            g.sc = reinterpret_cast<const uint8_t *>(y.kv_b.sc) + (size_t)NP * groups * se;
+            g.O = VD;
+            g.count = H;
+            g.w_stride = (int64_t)(NP + VD) * rb;
+            g.sc_stride = (int64_t)(NP + VD) * groups;
+            g.xq_stride = (int64_t)head_stride;
+            g.yq = s->o_xq;
+            g.kpy = kpO;
+            g.out_stride = VD;
+            FC_TRY(gemv1(df, g, S, 0.0f, st));
+            mark(s, "gemv_w_uv");
+        }
+        {
+            GemvSeg g = seg_of(y.o_proj, s->o_xq, EPI_ADD);
+            g.y = s->resid;
+            g.ldy = D;
+            FC_TRY(gemv1(df, g, S, 0.0f, st));
+            mark(s, "gemv_o_proj");
+        }
+        rmsnorm_kernel<<<S, 256, 0, st>>>(s->resid, D, y.ffn_norm.p, D, c.rms_norm_epsilon,
+                                          s->xq_norm, kpD, s->xn, D);
+        mark(s, "rmsnorm");
+        if (y.dense) {
+            int kpI = kpad(c.dense_intermediate_size);
+            GemvSeg g = seg_of(y.d_gate, s->xq_norm, EPI_SWIGLU_XQ);
+            g.w2 = y.d_up.w;
+            g.sc2 = y.d_up.sc;
+            g.yq = s->hd_xq;
+            g.kpy = kpI;
+            FC_TRY(gemv1(df, g, S, 0.0f, st));
+            mark(s, "gemv_dense_gate_up");
+            GemvSeg d = seg_of(y.d_down, s->hd_xq, EPI_ADD);
+            d.y = s->resid;
+            d.ldy = D;
+            FC_TRY(gemv1(df, d, S, 0.0f, st));
+            mark(s, "gemv_dense_down");
+        } else {
+            int E = c.expert_count, K = c.experts_per_token;
+            router_logits_kernel<<<(E + 7) / 8, 256, 0, st>>>(y.router.p, s->xn, E, D, S,
+                                                             s->router_logits);
+            mark(s, "router_logits");
+            RouteParams rp{};
+            rp.E = E; rp.K = K; rp.S = S;
+            rp.score_fn = c.score_fn;
+            rp.normalize = c.normalize_topk;
+            rp.routed_scale = c.routed_scale;
+            rp.bias = y.bias.p;
+            rp.hash = y.hash;
+            rp.ids = s->d_stage->ids;
+            rp.expert_lo = m->expert_lo;
+            rp.expert_hi = m->expert_hi;
+            rp.route_ids = s->route_ids + (size_t)l * mb * K;
+            rp.route_w = s->route_w + (size_t)l * mb * K;
+            rp.n_active = s->n_active;
+            rp.active = s->active;
+            rp.coef = s->coef;
+            route_select_kernel<<<1, 256, 2 * 8 * E * sizeof(float), st>>>(s->router_logits, rp);
+            FC_TRY(cudaGetLastError());
+            mark(s, "route_select");
+            int I = c.moe_intermediate_size, kpI = kpad(I);
+            int W = I * c.shared_expert_count, kpW = kpad(std::max(W, 1));
+            // gate / up + SwiGLU
+            MoeGemv gu{};
+            gu.routed = seg_of(y.e_gate, s->xq_norm, EPI_SWIGLU_XQ);
+            gu.routed.w = y.e_gate.w - (size_t)m->expert_lo * y.e_gate.w_bytes;
+            gu.routed.sc = reinterpret_cast<const uint8_t *>(y.e_gate.sc) -
+                           (size_t)m->expert_lo * y.e_gate.sc_bytes;
+            gu.routed.w2 = y.e_up.w - (size_t)m->expert_lo * y.e_up.w_bytes;
+            gu.routed.sc2 = reinterpret_cast<const uint8_t *>(y.e_up.sc) -
+                            (size_t)m->expert_lo * y.e_up.sc_bytes;
+            gu.routed.w_stride = (int64_t)y.e_gate.w_bytes;
+            gu.routed.sc_stride = (int64_t)y.e_gate.sc_elems;
+            gu.routed.yq = s->h_xq;
+            gu.routed.kpy = kpI;
+            if (y.s_gate.count) {
+                gu.shared = seg_of(y.s_gate, s->xq_norm, EPI_SWIGLU_XQ);
+                gu.shared.w2 = y.s_up.w;
+                gu.shared.sc2 = y.s_up.sc;
+                gu.shared.yq = s->hsh_xq;
+                gu.shared.kpy = kpW;
+            }
+            gu.max_slots = s->max_slots;
+            gu.n_active = s->n_active;
+            gu.active = s->active;
+            gu.in_slot_stride = 0;
+            gu.out_slot_stride = (int64_t)mb * kpI * 2;
+            gu.S = S;
+            gu.swiglu_limit = c.swiglu_limit;
+            FC_TRY(launch_moe_gemv(ef, df, gu, st));
+            mark(s, "moe_gate_up");
+            // down
+            MoeGemv dn{};
+            dn.routed = seg_of(y.e_down, s->h_xq, EPI_STORE);
+            dn.routed.w = y.e_down.w - (size_t)m->expert_lo * y.e_down.w_bytes;
+            dn.routed.sc = reinterpret_cast<const uint8_t *>(y.e_down.sc) -
+                           (size_t)m->expert_lo * y.e_down.sc_bytes;
+            dn.routed.w_stride = (int64_t)y.e_down.w_bytes;
+            dn.routed.sc_stride = (int64_t)y.e_down.sc_elems;
+            dn.routed.y = s->moe_part;
+            dn.routed.ldy = D;
+            if (y.s_down.count) {
+                dn.shared = seg_of(y.s_down, s->hsh_xq, EPI_STORE);
+                dn.shared.y = s->sh_part;
+                dn.shared.ldy = D;
+            }
+            dn.max_slots = s->max_slots;
+            dn.n_active = s->n_active;
+            dn.active = s->active;
+            dn.in_slot_stride = (int64_t)mb * kpI * 2;
+            dn.out_slot_stride = (int64_t)mb * D;
+            dn.S = S;
+            FC_TRY(launch_moe_gemv(ef, df, dn, st));
+            mark(s, "moe_down");
+            moe_combine_kernel<<<(S * D + 255) / 256, 256, 0, st>>>(
+                s->resid, s->moe_part, y.s_down.count ? s->sh_part : nullptr, s->coef, s->n_active,
+                S, D, mb);
+            mark(s, "moe_combine");
+        }
+        if (s->trace) {
+            FC_TRY(cudaMemcpyAsync(s->layer_out + (size_t)l * mb * D, s->resid, (size_t)S * D * 4,
+                                   cudaMemcpyDeviceToDevice, st));
+            mark(s, "layer_trace_copy");
+        }
+    }
+    rmsnorm_kernel<<<S, 256, 0, st>>>(s->resid, D, m->final_norm.p, D, c.rms_norm_epsilon,
+                                      s->xq_norm, kpD, nullptr, 0);
+    mark(s, "rmsnorm");
+    {
+        GemvSeg g = seg_of(m->lm_head, s->xq_norm, EPI_STORE);
+        g.y = s->logits;
+        g.ldy = c.vocab_size;
+        FC_TRY(gemv1(df, g, S, 0.0f, st));
+        mark(s, "gemv_lm_head");
+    }
+    {
+        dim3 grid(s->head_chunks, S);
+        head_partial_kernel<<<grid, 256, 0, st>>>(s->logits, c.vocab_size, s->d_stage, s->hp,
+                                                  s->head_chunks);
+        mark(s, "head_partial");
+        accept_kernel<<<1, 256, 0, st>>>(s->logits, c.vocab_size, s->d_stage, s->hp, s->head_chunks,
+                                         s->d_res, s->last_logits);
+        mark(s, "accept");
+    }
+    FC_TRY(cudaGetLastError());
+    FC_TRY(cudaMemcpyAsync(s->h_res, s->d_res, sizeof(Result), cudaMemcpyDeviceToHost, st));
+    return cudaSuccess;
+}
+
+cudaGraphExec_t get_graph(FcSession *s, int S, char *err, size_t n) {
+    int key = S * 2 + (s->trace ? 1 : 0);
+    auto it = s->graphs.find(key);
+    if (it != s->graphs.end()) return it->second;
+    cudaGraph_t graph = nullptr;
+    if (cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+        set_error(err, n, "cudaStreamBeginCapture failed");
+        return nullptr;
+    }
+    cudaError_t rec = record_forward(s, S);
+    cudaError_t end = cudaStreamEndCapture(s->stream, &graph);
+    if (rec != cudaSuccess || end != cudaSuccess) {
+        if (graph) cudaGraphDestroy(graph);
+        set_error(err, n, "recording the forward graph failed: %s",
+                  cudaGetErrorString(rec != cudaSuccess ? rec : end));
+        return nullptr;
+    }
+    cudaGraphExec_t exec = nullptr;
+    cudaError_t inst = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (inst != cudaSuccess) {
+        set_error(err, n, "cudaGraphInstantiate failed: %s", cudaGetErrorString(inst));
+        return nullptr;
+    }
+    s->graphs[key] = exec;
+    return exec;
+}
+
+// Runs one forward pass of `rows` <= rows_max tokens at the session position.
+int run_pass(FcSession *s, const int *ids, int rows, int k, const FcAcceptConfig *accept,
+             char *err, size_t n) {
+    Staging *st = s->h_stage;
+    memset(st, 0, sizeof(*st));
+    st->pos = s->position;
+    st->rows = rows;
+    st->k = k;
+    st->mode = accept ? accept->mode : FC_ACCEPT_GREEDY;
+    st->temperature = accept ? accept->temperature : 1.0f;
+    st->seed = accept ? accept->seed : 0;
+    st->counter = accept ? accept->counter : 0;
+    for (int i = 0; i < rows; ++i) st->ids[i] = ids[i];
+    cudaSetDevice(s->m->device);
+    cudaError_t e;
+    if (s->profiling) {
+        // eager pass with an event after every kernel (MOONLIGHT_PROFILE-style
+        // per-phase timing, moonlight_metal.m:1899-1979)
+        s->prof_marks.clear();
+        cudaEventRecord(s->prof_events[0], s->stream);
+        e = record_forward(s, rows);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(s->stream);
+        if (e == cudaSuccess) {
+            for (size_t i = 0; i < s->prof_marks.size(); ++i) {
+                float ms = 0.0f;
+                cudaEventElapsedTime(&ms, s->prof_events[i], s->prof_events[i + 1]);
+                bool found = false;
+                for (auto &p : s->prof)
+                    if (p.first == s->prof_marks[i]) {
+                        p.second.first += ms;
+                        p.second.second++;
+                        found = true;
+                        break;
+                    }
+                if (!found) s->prof.push_back({s->prof_marks[i], {ms, 1}});
+            }
+        }
+    } else {
+        cudaGraphExec_t g = get_graph(s, rows, err, n);
+        if (!g) return 0;
+        cudaEventRecord(s->ev_begin, s->stream);
+        e = cudaGraphLaunch(g, s->stream);
+        cudaEventRecord(s->ev_end, s->stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(s->stream);
+        if (e == cudaSuccess) {
+            float ms = 0.0f;
+            cudaEventElapsedTime(&ms, s->ev_begin, s->ev_end);
+            s->stats.gpu_ms += ms;
+        }
+        s->stats.graph_replays++;
+    }
+    if (e != cudaSuccess) return set_error(err, n, "CUDA forward failed: %s", cudaGetErrorString(e));
+    s->stats.command_buffers++;
+    s->last_rows = rows;
+    return 1;
+}
+
+int check_ids(const FcSession *s, const int *ids, int count, char *err, size_t n) {
+    for (int i = 0; i < count; ++i)
+        if (ids[i] < 0 || ids[i] >= s->m->c.vocab_size)
+            return set_error(err, n, "token id %d out of range", ids[i]);
+    return 1;
+}
+
+// prefill / append body: chunks of rows_max, logits of the last row.
+int run_tokens(FcSession *s, const int *ids, int count, float *last_logits, char *err, size_t n) {
+    if (!check_ids(s, ids, count, err, n)) return 0;
+    int done = 0;
+    while (done < count) {
+        int rows = std::min(s->rows_max, count - done);
+        if (!run_pass(s, ids + done, rows, -1, nullptr, err, n)) return 0;
+        s->position += rows;
+        done += rows;
+    }
+    if (last_logits) {
+        int V = s->m->c.vocab_size;
+        cudaError_t e = cudaMemcpy(last_logits, s->logits + (size_t)(s->last_rows - 1) * V,
+                                   (size_t)V * 4, cudaMemcpyDeviceToHost);
+        if (e != cudaSuccess) return set_error(err, n, "logits copy failed: %s", cudaGetErrorString(e));
+    }
+    return 1;
+}
+
+}  // namespace
+
+// ===========================================================================
+// C ABI
+// ===========================================================================
+extern "C" {
+
+int fc_model_create(FcModel **out, const FcModelConfig *config, int device, char *error,
+                    size_t error_size) {
+    if (!out) return set_error(error, error_size, "model output is required");
+    *out = nullptr;
+    if (!config) return set_error(error, error_size, "config is required");
+    if (!config_ok(config, error, error_size)) return 0;
+    int count = 0;
+    if (cudaGetDeviceCount(&count) != cudaSuccess || count <= 0)
+        return set_error(error, error_size, "no CUDA device is available");
+    if (device < 0 || device >= count) return set_error(error, error_size, "invalid device %d", device);
+    if (cudaSetDevice(device) != cudaSuccess)
+        return set_error(error, error_size, "cannot select CUDA device %d", device);
+    cudaDeviceProp prop{};
+    cudaGetDeviceProperties(&prop, device);
+    if (prop.major < 10)
+        return set_error(error, error_size, "device %s is sm_%d%d; this backend is built for sm_100a",
+                         prop.name, prop.major, prop.minor);
+    FcModel *m = new FcModel();
+    m->c = *config;
+    m->device = device;
+    m->device_name = prop.name;
+    m->expert_lo = 0;
+    m->expert_hi = config->expert_count;
+    if (!build_model(m, error, error_size)) {
+        fc_model_close(m);
+        return 0;
+    }
+    *out = m;
+    return 1;
+}
+
+int fc_model_create_ep(FcModel **out, const FcModelConfig *config, int device, int rank,
+                       int world, char *error, size_t error_size) {
+    if (!out) return set_error(error, error_size, "model output is required");
+    *out = nullptr;
+    if (!config || world <= 0 || rank < 0 || rank >= world ||
+        (config->expert_count > 0 && config->expert_count % world))
+        return set_error(error, error_size, "invalid expert-parallel layout");
+    if (!config_ok(config, error, error_size)) return 0;
+    if (cudaSetDevice(device) != cudaSuccess)
+        return set_error(error, error_size, "cannot select CUDA device %d", device);
+    cudaDeviceProp prop{};
+    cudaGetDeviceProperties(&prop, device);
+    FcModel *m = new FcModel();
+    m->c = *config;
+    m->device = device;
+    m->device_name = prop.name;
+    int per = config->expert_count / world;
+    m->expert_lo = rank * per;
+    m->expert_hi = rank * per + per;
+    if (!build_model(m, error, error_size)) {
+        fc_model_close(m);
+        return 0;
+    }
+    *out = m;
+    return 1;
+}
+
+int fc_model_fill_synthetic(FcModel *m, uint64_t seed, char *error, size_t error_size) {
+    if (!m) return set_error(error, error_size, "model is required");
+    cudaSetDevice(m->device);
+    cudaStream_t st = nullptr;
+    cudaError_t e = cudaSuccess;
+    for_each_tensor(m, [&](DevMat *mm, DevVec *v) {
+        if (e != cudaSuccess) return;
+        if (mm) e = fill_mat(*mm, seed, st);
+        if (v && v->n) {
+            synth_f32_kernel<<<grid_for(v->n), 256, 0, st>>>(v->p, v->n, v->kind, seed, v->tid);
+            e = cudaGetLastError();
+        }
+    });
+    for (auto &y : m->layers)
+        if (y.hash && e == cudaSuccess) {
+            size_t cnt = (size_t)m->c.vocab_size * m->c.experts_per_token;
+            synth_hash_kernel<<<grid_for(cnt), 256, 0, st>>>(y.hash, m->c.vocab_size,
+                                                            m->c.experts_per_token,
+                                                            m->c.expert_count, seed, y.hash_tid);
+            e = cudaGetLastError();
+        }
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess)
+        return set_error(error, error_size, "synthetic fill failed: %s", cudaGetErrorString(e));
+    return 1;
+}
+
+static int tensor_io(const FcModel *m, const char *name, void *data, size_t bytes, bool upload,
+                     char *error, size_t error_size) {
+    if (!m || !name || !data) return set_error(error, error_size, "model, name and data are required");
+    std::string key(name);
+    bool scales = false;
+    if (key.size() > 3 && key.compare(key.size() - 3, 3, ".gs") == 0) {
+        scales = true;
+        key.resize(key.size() - 3);
+    }
+    auto it = m->names.find(key);
+    if (it == m->names.end()) return set_error(error, error_size, "unknown tensor %s", name);
+    const TensorRef &r = it->second;
+    cudaSetDevice(m->device);
+    if (r.vec || r.ints) {
+        if (scales) return set_error(error, error_size, "tensor %s has no group scales", key.c_str());
+        size_t need = r.vec ? r.vec->n * 4 : r.ints_n * 4;
+        void *dev = r.vec ? (void *)r.vec->p : (void *)r.ints;
+        if (bytes != need)
+            return set_error(error, error_size, "%s: expected %zu bytes, got %zu", name, need, bytes);
+        cudaError_t e = upload ? cudaMemcpy(dev, data, need, cudaMemcpyHostToDevice)
+                               : cudaMemcpy(data, dev, need, cudaMemcpyDeviceToHost);
+        return e == cudaSuccess ? 1 : set_error(error, error_size, "copy failed: %s", cudaGetErrorString(e));
+    }
+    const DevMat &mm = *r.mat;
+    if (scales) {
+        size_t elem = mm.fmt == FC_FMT_MXFP4 ? 1 : 2;
+        size_t gk = mm.K / 32, gp = mm.kp / 32;
+        size_t need = (size_t)mm.O * gk * elem;
+        if (bytes != need)
+            return set_error(error, error_size, "%s: expected %zu bytes, got %zu", name, need, bytes);
+        std::vector<uint8_t> dev(mm.sc_bytes, 0);
+        uint8_t *base = reinterpret_cast<uint8_t *>(mm.sc) + (size_t)r.member * mm.sc_bytes;
+        if (!upload && cudaMemcpy(dev.data(), base, mm.sc_bytes, cudaMemcpyDeviceToHost) != cudaSuccess)
+            return set_error(error, error_size, "copy failed");
+        for (int o = 0; o < mm.O; ++o) {
+            uint8_t *d = dev.data() + (size_t)o * gp * elem;
+            uint8_t *h = reinterpret_cast<uint8_t *>(data) + (size_t)o * gk * elem;
+            if (upload) memcpy(d, h, gk * elem);
+            else memcpy(h, d, gk * elem);
+        }
+        if (upload && cudaMemcpy(base, dev.data(), mm.sc_bytes, cudaMemcpyHostToDevice) != cudaSuccess)
+            return set_error(error, error_size, "copy failed");
+        return 1;
+    }
+    uint8_t *base = mm.w + (size_t)r.member * mm.w_bytes;
+    size_t need = mm.fmt == FC_FMT_F32 ? (size_t)mm.O * mm.K * 4
+                  : mm.fmt == FC_FMT_Q8 ? (size_t)mm.O * mm.K : (size_t)mm.O * mm.K / 2;
+    if (bytes != need)
+        return set_error(error, error_size, "%s: expected %zu bytes, got %zu", name, need, bytes);
+    if (upload) {
+        std::vector<uint8_t> dev;
+        pack_values(mm, reinterpret_cast<const uint8_t *>(data), dev);
+        if (cudaMemcpy(base, dev.data(), dev.size(), cudaMemcpyHostToDevice) != cudaSuccess)
+            return set_error(error, error_size, "copy failed");
+    } else {
+        std::vector<uint8_t> dev(mm.w_bytes);
+        if (cudaMemcpy(dev.data(), base, mm.w_bytes, cudaMemcpyDeviceToHost) != cudaSuccess)
+            return set_error(error, error_size, "copy failed");
+        unpack_values(mm, dev.data(), reinterpret_cast<uint8_t *>(data));
+    }
+    return 1;
+}
+
+int fc_model_set_tensor(FcModel *m, const char *name, const void *data, size_t bytes, char *error,
+                        size_t error_size) {
+    return tensor_io(m, name, const_cast<void *>(data), bytes, true, error, error_size);
+}
+
+int fc_model_get_tensor(const FcModel *m, const char *name, void *data, size_t bytes, char *error,
+                        size_t error_size) {
+    return tensor_io(m, name, data, bytes, false, error, error_size);
+}
+
+void fc_model_close(FcModel *m) {
+    if (!m) return;
+    cudaSetDevice(m->device);
+    if (m->arena) cudaFree(m->arena);
+    delete m;
+}
+
+const char *fc_device_name(const FcModel *m) { return m ? m->device_name.c_str() : "(none)"; }
+
+FcModelConfig fc_model_info(const FcModel *m) {
+    FcModelConfig c{};
+    if (!m) return c;
+    c = m->c;
+    c.resident_bytes = m->resident;
+    return c;
+}
+
+int fc_session_create(FcSession **out, FcModel *m, const FcOptions *options, char *error,
+                      size_t error_size) {
+    if (!out || !m || !options)
+        return set_error(error, error_size, "model and session options are required");
+    *out = nullptr;
+    if (options->context_size <= 0 || options->max_batch <= 0 ||
+        options->max_batch > options->context_size)
+        return set_error(error, error_size, "invalid context or batch size");
+    cudaSetDevice(m->device);
+    const FcModelConfig &c = m->c;
+    FcSession *s = new FcSession();
+    s->m = m;
+    s->opt = *options;
+    s->rows_max = std::min(options->max_batch, kMaxRows);
+    s->stats.resident_bytes = m->resident;
+    const int mb = s->rows_max;
+    const int D = c.hidden_size, H = c.head_count, L = c.kv_lora_rank, R = c.qk_rope_dim;
+    const int QW = c.qk_nope_dim + R, V = c.vocab_size;
+    const int E = std::max(c.expert_count, 1), K = std::max(c.experts_per_token, 1);
+    const int I = std::max(c.moe_intermediate_size, 32);
+    const int W = std::max(I * c.shared_expert_count, 32);
+    const int nl = std::max(m->expert_hi - m->expert_lo, 1);
+    s->max_slots = std::min(nl, mb * K);
+    // attention split plan: fixed per session (see mla.cuh)
+    int max_chunks = (options->context_size + kAttnKeys - 1) / kAttnKeys;
+    int qtiles = (mb * H + kAttnQ - 1) / kAttnQ;
+    int target = std::max(1, 2 * 148 / qtiles);
+    s->chunks_per_split = (max_chunks + target - 1) / target;
+    s->splits = (max_chunks + s->chunks_per_split - 1) / s->chunks_per_split;
+    s->head_chunks = (V + kHeadChunk - 1) / kHeadChunk;
+    s->attn_smem = AttnSmem::total(L + R);
+    bool ok = cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking) == cudaSuccess;
+    ok = ok && cudaEventCreate(&s->ev_begin) == cudaSuccess && cudaEventCreate(&s->ev_end) == cudaSuccess;
+    ok = ok && salloc(s, s->cache, (size_t)c.layer_count * options->context_size * (L + R));
+    ok = ok && salloc(s, s->resid, (size_t)mb * D) && salloc(s, s->xn, (size_t)mb * D);
+    ok = ok && salloc(s, s->xq_norm, (size_t)mb * kpad(D) * 2);
+    ok = ok && salloc(s, s->q, (size_t)mb * H * QW);
+    ok = ok && salloc(s, s->qa, (size_t)mb * std::max(c.q_lora_rank, 1));
+    ok = ok && salloc(s, s->qa_xq, (size_t)mb * kpad(std::max(c.q_lora_rank, 1)) * 2);
+    ok = ok && salloc(s, s->ckv, (size_t)mb * (L + R));
+    ok = ok && salloc(s, s->qcat, (size_t)mb * H * (L + R));
+    ok = ok && salloc(s, s->part_o, (size_t)s->splits * mb * H * L);
+    ok = ok && salloc(s, s->part_m, (size_t)s->splits * mb * H);
+    ok = ok && salloc(s, s->part_l, (size_t)s->splits * mb * H);
+    ok = ok && salloc(s, s->ctx_xq, (size_t)H * mb * kpad(L) * 2);
+    ok = ok && salloc(s, s->o_xq, (size_t)mb * kpad(H * c.value_dim) * 2);
+    ok = ok && salloc(s, s->router_logits, (size_t)mb * E);
+    ok = ok && salloc(s, s->route_ids, (size_t)c.layer_count * mb * K);
+    ok = ok && salloc(s, s->route_w, (size_t)c.layer_count * mb * K);
+    ok = ok && salloc(s, s->n_active, 1) && salloc(s, s->active, (size_t)s->max_slots + 1);
+    ok = ok && salloc(s, s->coef, (size_t)(s->max_slots + 1) * 8);
+    ok = ok && salloc(s, s->h_xq, (size_t)s->max_slots * mb * kpad(I) * 2);
+    ok = ok && salloc(s, s->hsh_xq, (size_t)mb * kpad(W) * 2);
+    ok = ok && salloc(s, s->hd_xq, (size_t)mb * kpad(std::max(c.dense_intermediate_size, 32)) * 2);
+    ok = ok && salloc(s, s->moe_part, (size_t)s->max_slots * mb * D);
+    ok = ok && salloc(s, s->sh_part, (size_t)mb * D);
+    ok = ok && salloc(s, s->logits, (size_t)mb * V) && salloc(s, s->last_logits, (size_t)V);
+    ok = ok && salloc(s, s->layer_out, (size_t)c.layer_count * mb * D);
+    size_t hc = (size_t)mb * s->head_chunks;
+    ok = ok && salloc(s, s->hp.amax, hc) && salloc(s, s->hp.aidx, hc) && salloc(s, s->hp.zmax, hc) &&
+         salloc(s, s->hp.zsum, hc) && salloc(s, s->hp.gval, hc) && salloc(s, s->hp.gidx, hc);
+    ok = ok && salloc(s, s->d_stage, 1) && salloc(s, s->d_res, 1);
+    ok = ok && cudaMallocHost(&s->h_stage, sizeof(Staging)) == cudaSuccess;
+    ok = ok && cudaMallocHost(&s->h_res, sizeof(Result)) == cudaSuccess;
+    if (ok) {
+        cudaError_t e1 = cudaFuncSetAttribute(mla_attention_kernel<512, 64>,
+                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              (int)AttnSmem::total(576));
+        cudaError_t e2 = cudaFuncSetAttribute(mla_attention_kernel<256, 64>,
+                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              (int)AttnSmem::total(320));
+        cudaError_t e3 = cudaFuncSetAttribute(route_select_kernel,
+                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              2 * 8 * 1024 * 4);
+        ok = e1 == cudaSuccess && e2 == cudaSuccess && e3 == cudaSuccess;
+    }
+    if (!ok) {
+        free_session_buffers(s);
+        delete s;
+        return set_error(error, error_size, "session allocation failed");
+    }
+    *out = s;
+    return 1;
+}
+
+void fc_session_destroy(FcSession *s) {
+    if (!s) return;
+    cudaSetDevice(s->m->device);
+    free_session_buffers(s);
+    delete s;
+}
+
+void fc_session_reset(FcSession *s) {
+    if (!s) return;
+    s->position = 0;
+    s->last_rows = 0;
+    uint64_t allocs = s->stats.buffer_allocations, resident = s->stats.resident_bytes;
+    s->stats = FcStats{};
+    s->stats.buffer_allocations = allocs;
+    s->stats.resident_bytes = resident;
+}
+
+int fc_session_position(const FcSession *s) { return s ? s->position : 0; }
+
+FcStats fc_session_stats(const FcSession *s) {
+    FcStats r{};
+    return s ? s->stats : r;
+}
+
+int fc_session_prefill(FcSession *s, const int *ids, int count, float *last_logits, char *error,
+                       size_t error_size) {
+    if (!s || !ids || !last_logits || count <= 0 || count > s->opt.max_batch ||
+        count > s->opt.context_size)
+        return set_error(error, error_size, "invalid prefill request");
+    if (s->position != 0) return set_error(error, error_size, "prefill requires an empty session");
+    double t0 = now_ms();
+    if (!run_tokens(s, ids, count, last_logits, error, error_size)) return 0;
+    s->stats.prefill_tokens += (uint64_t)count;
+    s->stats.prefill_ms += now_ms() - t0;
+    return 1;
+}
+
+int fc_session_append(FcSession *s, const int *ids, int count, float *last_logits, char *error,
+                      size_t error_size) {
+    if (!s || !ids || !last_logits || count <= 0 || count > s->opt.max_batch || s->position <= 0 ||
+        s->position + count > s->opt.context_size)
+        return set_error(error, error_size, "invalid append request");
+    double t0 = now_ms();
+    if (!run_tokens(s, ids, count, last_logits, error, error_size)) return 0;
+    s->stats.prefill_tokens += (uint64_t)count;
+    s->stats.prefill_ms += now_ms() - t0;
+    return 1;
+}
+
+int fc_session_decode(FcSession *s, int token, float *logits, char *error, size_t error_size) {
+    if (!s || !logits || s->position < 0 || s->position >= s->opt.context_size)
+        return set_error(error, error_size, "invalid decode request");
+    double t0 = now_ms();
+    if (!run_tokens(s, &token, 1, logits, error, error_size)) return 0;
+    s->stats.decode_tokens++;
+    s->stats.decode_ms += now_ms() - t0;
+    return 1;
+}
+
+int fc_session_verify(FcSession *s, const int *ids, int k, const FcAcceptConfig *accept,
+                      int *emitted, int *n_emitted, int *next_token, float *last_logits,
+                      char *error, size_t error_size) {
+    if (!s || !ids || !emitted || !n_emitted || !next_token || k < 0)
+        return set_error(error, error_size, "invalid verify request");
+    int rows = k + 1;
+    if (rows > s->rows_max)
+        return set_error(error, error_size, "verify of %d rows exceeds the %d-row pass", rows,
+                         s->rows_max);
+    if (s->position + rows > s->opt.context_size)
+        return set_error(error, error_size, "verify exceeds the context (%d + %d > %d)", s->position,
+                         rows, s->opt.context_size);
+    if (accept && accept->mode == FC_ACCEPT_SAMPLE && !(accept->temperature > 0.0f))
+        return set_error(error, error_size, "sampling needs a positive temperature");
+    if (!check_ids(s, ids, rows, error, error_size)) return 0;
+    double t0 = now_ms();
+    if (!run_pass(s, ids, rows, k, accept, error, error_size)) return 0;
+    const Result &r = *s->h_res;
+    int commit = r.commit;
+    if (commit < 1 || commit > rows) return set_error(error, error_size, "verify produced commit %d", commit);
+    for (int i = 0; i < commit; ++i) emitted[i] = ids[i];
+    *n_emitted = commit;
+    *next_token = r.next_token;
+    if (last_logits) {
+        cudaError_t e = cudaMemcpy(last_logits, s->last_logits, (size_t)s->m->c.vocab_size * 4,
+                                   cudaMemcpyDeviceToHost);
+        if (e != cudaSuccess) return set_error(error, error_size, "logits copy failed");
+    }
+    s->position += commit;  // rollback of rows >= commit: the cache is append-only
+    s->stats.verify_calls++;
+    s->stats.proposed_tokens += (uint64_t)k;
+    s->stats.accepted_tokens += (uint64_t)commit;
+    s->stats.verify_ms += now_ms() - t0;
+    return 1;
+}
+
+int fc_session_set_profiling(FcSession *s, int enabled) {
+    if (!s) return 0;
+    cudaSetDevice(s->m->device);
+    if (enabled && s->prof_events.empty()) {
+        size_t count = (size_t)s->m->c.layer_count * 24 + 32;
+        s->prof_events.resize(count);
+        for (auto &ev : s->prof_events)
+            if (cudaEventCreate(&ev) != cudaSuccess) return 0;
+    }
+    s->profiling = enabled != 0;
+    return 1;
+}
+
+int fc_session_profile(const FcSession *s, int index, char *name, size_t name_size,
+                       double *total_ms, uint64_t *launches) {
+    if (!s || index < 0 || (size_t)index >= s->prof.size()) return 0;
+    const auto &p = s->prof[(size_t)index];
+    if (name && name_size) snprintf(name, name_size, "%s", p.first.c_str());
+    if (total_ms) *total_ms = p.second.first;
+    if (launches) *launches = p.second.second;
+    return 1;
+}
+
+int fc_session_set_layer_trace(FcSession *s, int enabled) {
+    if (!s) return 0;
+    s->trace = enabled != 0;
+    return 1;
+}
+
+void fc_session_profile_reset(FcSession *s) {
+    if (s) s->prof.clear();
+}
+
+int fc_session_rollback(FcSession *s, int position, char *error, size_t error_size) {
+    if (!s || position < 0) return set_error(error, error_size, "invalid rollback request");
+    if (position < s->position) s->position = position;
+    return 1;
+}
+
+int fc_session_copy_row_logits(const FcSession *s, float *logits, int capacity_rows) {
+    if (!s || !logits || capacity_rows < s->last_rows || s->last_rows <= 0) return 0;
+    return cudaMemcpy(logits, s->logits, (size_t)s->last_rows * s->m->c.vocab_size * 4,
+                      cudaMemcpyDeviceToHost) == cudaSuccess;
+}
+
+int fc_session_seed_context(FcSession *s, int positions, uint64_t seed, char *error,
+                            size_t error_size) {
+    if (!s || positions < 0 || positions > s->opt.context_size)
+        return set_error(error, error_size, "invalid seeded context");
+    const FcModelConfig &c = s->m->c;
+    cudaSetDevice(s->m->device);
+    int L = c.kv_lora_rank, R = c.qk_rope_dim;
+    for (int l = 0; l < c.layer_count && positions > 0; ++l) {
+        __half *cache = s->cache + (size_t)l * s->opt.context_size * (L + R);
+        synth_kv_kernel<<<grid_for((size_t)positions * (L + R)), 256, 0, s->stream>>>(
+            cache, positions, L, R, seed, fc_tensor_id(l, FC_T_KV_LATENT, 0),
+            fc_tensor_id(l, FC_T_KV_ROPE, 0));
+    }
+    cudaError_t e = cudaStreamSynchronize(s->stream);
+    if (e == cudaSuccess) e = cudaGetLastError();
+    if (e != cudaSuccess) return set_error(error, error_size, "seeding failed: %s", cudaGetErrorString(e));
+    s->position = positions;
+    return 1;
+}
+
+int fc_test_kv_length(const FcSession *s, int layer) {
+    if (!s || layer < 0 || layer >= s->m->c.layer_count) return -1;
+    return s->position;
+}
+
+int fc_test_copy_kv(const FcSession *s, int layer, float *latent, float *rope, int capacity) {
+    if (!s || layer < 0 || layer >= s->m->c.layer_count || capacity < s->position) return 0;
+    const FcModelConfig &c = s->m->c;
+    int L = c.kv_lora_rank, R = c.qk_rope_dim, P = s->position;
+    std::vector<__half> h((size_t)P * (L + R));
+    if (P && cudaMemcpy(h.data(), s->cache + (size_t)layer * s->opt.context_size * (L + R),
+                        h.size() * 2, cudaMemcpyDeviceToHost) != cudaSuccess)
+        return 0;
+    for (int p = 0; p < P; ++p) {
+        for (int i = 0; i < L; ++i)
+            if (latent) latent[(size_t)p * L + i] = __half2float(h[(size_t)p * (L + R) + i]);
+        for (int i = 0; i < R; ++i)
+            if (rope) rope[(size_t)p * R + i] = __half2float(h[(size_t)p * (L + R) + L + i]);
+    }
+    return 1;
+}
+
+int fc_test_copy_routes(const FcSession *s, int layer, int *route_ids, int capacity) {
+    if (!s || !route_ids || capacity < s->last_rows) return 0;
+    const FcModelConfig &c = s->m->c;
+    if (layer < c.first_dense_layer_count || layer >= c.layer_count) return 0;
+    int K = c.experts_per_token;
+    return cudaMemcpy(route_ids, s->route_ids + (size_t)layer * s->rows_max * K,
+                      (size_t)s->last_rows * K * 4, cudaMemcpyDeviceToHost) == cudaSuccess;
+}
+
+int fc_test_copy_layer_outputs(const FcSession *s, float *outputs, int capacity_rows) {
+    if (!s || !outputs || capacity_rows < s->last_rows || !s->trace) return 0;
+    const FcModelConfig &c = s->m->c;
+    int D = c.hidden_size;
+    for (int l = 0; l < c.layer_count; ++l)
+        if (cudaMemcpy(outputs + (size_t)l * s->last_rows * D,
+                       s->layer_out + (size_t)l * s->rows_max * D, (size_t)s->last_rows * D * 4,
+                       cudaMemcpyDeviceToHost) != cudaSuccess)
+            return 0;
+    return 1;
+}
+
+// ---- spec-runtime shim (deepseek_v4_runtime.h:72-256) ----
+int fc_runtime_init(FcRuntime *rt, FcModel *m, int max_context, int max_batch) {
+    if (!rt || !m || max_context <= 0) return 0;
+    memset(rt, 0, sizeof(*rt));
+    FcOptions o{max_context, std::max(1, std::min(max_batch, max_context))};
+    char err[256];
+    if (!fc_session_create(&rt->session, m, &o, err, sizeof(err))) return 0;
+    rt->vocab_size = m->c.vocab_size;
+    rt->max_context = max_context;
+    rt->logits = (float *)malloc((size_t)rt->vocab_size * 4);
+    if (!rt->logits) {
+        fc_session_destroy(rt->session);
+        memset(rt, 0, sizeof(*rt));
+        return 0;
+    }
+    return 1;
+}
+
+int fc_runtime_forward(FcRuntime *rt, const int *ids, int n, const float **logits) {
+    if (!rt || !rt->session || !ids || n <= 0 ||
+        fc_session_position(rt->session) + n > rt->max_context)
+        return 0;
+    char err[256];
+    int start = fc_session_position(rt->session);
+    int done = 0;
+    while (done < n) {
+        int chunk = std::min(n - done, rt->session->opt.max_batch);
+        int ok = fc_session_position(rt->session) == 0
+                     ? fc_session_prefill(rt->session, ids + done, chunk, rt->logits, err, sizeof(err))
+                     : fc_session_append(rt->session, ids + done, chunk, rt->logits, err, sizeof(err));
+        if (!ok) return 0;
+        done += chunk;
+    }
+    rt->last_start_position = start;
+    rt->last_count = n;
+    if (logits) *logits = rt->logits;
+    return 1;
+}
+
+int fc_runtime_argmax(const float *logits, int vocab_size) {
+    if (!logits || vocab_size <= 0) return -1;
+    int best = 0;
+    for (int t = 1; t < vocab_size; ++t)
+        if (logits[t] > logits[best]) best = t;
+    return best;
+}
+
+int fc_runtime_verify_token(const float *logits, int vocab_size, int64_t proposal, int *accepted) {
+    int base = fc_runtime_argmax(logits, vocab_size);
+    if (accepted) *accepted = base >= 0 && proposal == base;
+    return base;
+}
+
+void fc_runtime_reset(FcRuntime *rt) {
+    if (!rt || !rt->session) return;
+    fc_session_reset(rt->session);
+    rt->last_count = 0;
+    rt->last_start_position = 0;
+}
+
+void fc_runtime_free(FcRuntime *rt) {
+    if (!rt) return;
+    if (rt->session) fc_session_destroy(rt->session);
+    free(rt->logits);
+    memset(rt, 0, sizeof(*rt));
+}
+
+}  // extern "C"
+
+// ===========================================================================
+// single-kernel entry points (include/floyd_kernels.h)
+// ===========================================================================
+namespace {
+
+__global__ void to_xq_kernel(const float *x, int S, int K, int kp, __half *xq) {
+    int idx = blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= S * K) return;
+    store_xq(xq, kp, idx / K, idx % K, x[idx]);
+}
+
+}  // namespace
+
+extern "C" int fc_matmul(int format, float *y, const float *x, const void *values,
+                         const void *scales, int O, int K, int S, char *error,
+                         size_t error_size) {
+    if (!y || !x || !values || !scales || O <= 0 || K <= 0 || K % 32 || S < 1 || S > kMaxRows)
+        return set_error(error, error_size, "invalid matmul shape");
+    if (format != FC_FMT_Q8 && format != FC_FMT_Q4 && format != FC_FMT_MXFP4)
+        return set_error(error, error_size, "unsupported format %d", format);
+    DevMat mm;
+    plan_mat(mm, format, O, K, 1, 0, 0);
+    std::vector<uint8_t> packed;
+    pack_values(mm, reinterpret_cast<const uint8_t *>(values), packed);
+    size_t elem = format == FC_FMT_MXFP4 ? 1 : 2;
+    std::vector<uint8_t> sc(mm.sc_bytes, 0);
+    for (int o = 0; o < O; ++o)
+        memcpy(&sc[(size_t)o * (mm.kp / 32) * elem],
+               reinterpret_cast<const uint8_t *>(scales) + (size_t)o * (K / 32) * elem,
+               (size_t)(K / 32) * elem);
+    uint8_t *dw = nullptr, *dsc = nullptr;
+    float *dx = nullptr, *dy = nullptr;
+    __half *dxq = nullptr;
+    size_t xq_bytes = (size_t)S * mm.kp * 2 * sizeof(__half);
+    bool ok = cudaMalloc(&dw, packed.size()) == cudaSuccess &&
+              cudaMalloc(&dsc, sc.size()) == cudaSuccess &&
+              cudaMalloc(&dx, (size_t)S * K * 4) == cudaSuccess &&
+              cudaMalloc(&dy, (size_t)S * O * 4) == cudaSuccess &&
+              cudaMalloc(&dxq, xq_bytes) == cudaSuccess;
+    cudaError_t e = cudaErrorMemoryAllocation;
+    if (ok) {
+        cudaMemcpy(dw, packed.data(), packed.size(), cudaMemcpyHostToDevice);
+        cudaMemcpy(dsc, sc.data(), sc.size(), cudaMemcpyHostToDevice);
+        cudaMemcpy(dx, x, (size_t)S * K * 4, cudaMemcpyHostToDevice);
+        cudaMemset(dxq, 0, xq_bytes);
+        to_xq_kernel<<<(S * K + 255) / 256, 256>>>(dx, S, K, mm.kp, dxq);
+        GemvSeg g = seg_of(mm, dxq, EPI_STORE);
+        g.w = dw;
+        g.sc = dsc;
+        g.y = dy;
+        g.ldy = O;
+        e = gemv1(format, g, S, 0.0f, 0);
+        if (e == cudaSuccess) e = cudaDeviceSynchronize();
+        if (e == cudaSuccess) e = cudaMemcpy(y, dy, (size_t)S * O * 4, cudaMemcpyDeviceToHost);
+    }
+    cudaFree(dw); cudaFree(dsc); cudaFree(dx); cudaFree(dy); cudaFree(dxq);
+    if (e != cudaSuccess) return set_error(error, error_size, "matmul failed: %s", cudaGetErrorString(e));
+    return 1;
+}

@@ -1,0 +1,293 @@
+/*
+ * floyd_cuda.h - C ABI of the B200 (sm_100a) backend for floyd's
+ * speculative-decode verify step.
+ *
+ * This header is the drop-in boundary.  It mirrors floyd's Metal session API
+ * (moonlight_metal.h:1-96) function for function, with the prefix `fc_`
+ * instead of `moonlight_`, and adds the verify / rollback calls that the
+ * DS4 speculative loop needs (deepseek_v4_ds4.c:570-691 drives them through
+ * ds4_session_eval_speculative_argmax, patches/ds4/deepseek-v4-dspark-metal.patch
+ * :1727-1906).
+ *
+ * Conventions kept from the reference (moonlight_metal.m:97-105):
+ *   - functions that can fail return int: 1 = ok, 0 = failure;
+ *   - failures fill `error` (size `error_size`) via vsnprintf;
+ *   - `*out` handles are set to NULL on failure;
+ *   - every host array is caller-owned; logits are copied out as float[vocab];
+ *   - a session is used from one host thread; a model may be shared
+ *     read-only by several sessions.
+ *
+ * Everything runs on the GPU.  There is no CPU fallback: FcStats.cpu_fallbacks
+ * exists for parity with MoonlightStats and always reads 0.
+ *
+ * Weights are resident on the device, in the layouts described next to
+ * FcFormat.  Session buffers (latent KV cache, activations, scratch) are all
+ * allocated in fc_session_create; FcStats.buffer_allocations stays flat
+ * afterwards (tests/test_moonlight_metal_runtime.c:106-115).
+ */
+#ifndef FLOYD_CUDA_H
+#define FLOYD_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct FcModel FcModel;     /* replaces MoonlightModel   (moonlight_metal.h:7) */
+typedef struct FcSession FcSession; /* replaces MoonlightSession (moonlight_metal.h:8) */
+
+/* Weight storage formats.  Quantized formats use groups of 32 along the
+ * input (K) dimension; K must be a multiple of 32.
+ *   FC_FMT_F32   fp32 [O][K] (router weights, norms).
+ *   FC_FMT_Q8    symmetric int8, one fp16 scale per group of 32
+ *                (the 34-byte Q8_0-style block of BASELINE config 1/2).
+ *   FC_FMT_Q4    int4 stored with a +8 offset (value = nibble - 8), one fp16
+ *                scale per 32; the even element sits in the low nibble
+ *                (moonlight_kernels.metal:123-127).
+ *   FC_FMT_MXFP4 e2m1 codes (deepseek_v4_quant.h:48-51) with one ue8m0 scale
+ *                per 32 (deepseek_v4_quant.h:63-66).
+ * On the device the values of a row are permuted so that one tensor-core
+ * MMA step always covers a single scale group; fc_model_set_tensor takes the
+ * plain row-major logical layout and performs that permutation. */
+typedef enum {
+    FC_FMT_F32 = 0,
+    FC_FMT_Q8 = 1,
+    FC_FMT_Q4 = 2,
+    FC_FMT_MXFP4 = 3
+} FcFormat;
+
+/* Router score functions, same values and meaning as MoeScoreFn
+ * (moe_route.h:6-10). */
+typedef enum {
+    FC_SCORE_SOFTMAX = 0,
+    FC_SCORE_SIGMOID = 1,
+    FC_SCORE_SQRT_SOFTPLUS = 2
+} FcScoreFn;
+
+/* Model description.  Field names follow MoonlightModelInfo
+ * (moonlight_metal.h:15-33); the extra fields cover the DS4-style stand-in
+ * (q-lora, hash-routed layers, swiglu clamp) and the per-family formats. */
+typedef struct {
+    int hidden_size;
+    int layer_count;
+    int vocab_size;
+    int head_count;
+    int q_lora_rank;             /* 0 = plain q_proj (Moonlight)        */
+    int kv_lora_rank;            /* latent width L                      */
+    int qk_nope_dim;
+    int qk_rope_dim;             /* R, even                             */
+    int value_dim;
+    int expert_count;
+    int experts_per_token;
+    int moe_intermediate_size;
+    int shared_expert_count;     /* shared experts fused into one wide MLP */
+    int first_dense_layer_count;
+    int dense_intermediate_size;
+    int hash_layer_count;        /* layers < this use moe_route_fixed     */
+    int score_fn;                /* FcScoreFn                           */
+    int normalize_topk;
+    int has_selection_bias;      /* e_score_correction_bias present     */
+    float routed_scale;
+    float swiglu_limit;          /* <= 0: no clamp (moe_exec.h:55-60)   */
+    float rms_norm_epsilon;
+    float rope_theta;
+    int dense_format;            /* FcFormat of attention, dense, shared,
+                                    embedding and lm-head matrices       */
+    int expert_format;           /* FcFormat of routed experts           */
+    uint64_t resident_bytes;     /* filled by fc_model_info              */
+} FcModelConfig;
+
+/* Session sizing, same meaning as MoonlightOptions (moonlight_metal.h:10-13):
+ * 0 < max_batch <= context_size. */
+typedef struct {
+    int context_size;
+    int max_batch;
+} FcOptions;
+
+/* MoonlightStats (moonlight_metal.h:35-44) plus verify counters. */
+typedef struct {
+    uint64_t command_buffers;     /* graph / stream submissions          */
+    uint64_t prefill_tokens;
+    uint64_t decode_tokens;
+    uint64_t cpu_fallbacks;       /* always 0: there is no CPU path      */
+    uint64_t buffer_allocations;
+    uint64_t resident_bytes;
+    double prefill_ms;
+    double decode_ms;
+    uint64_t verify_calls;
+    uint64_t proposed_tokens;     /* drafts offered to verify            */
+    uint64_t accepted_tokens;     /* tokens committed by verify          */
+    uint64_t graph_replays;       /* CUDA-graph launches                 */
+    double verify_ms;             /* host wall time inside fc_session_verify */
+    double gpu_ms;                /* device time of all graph replays
+                                     (CUDA events on the session stream)  */
+} FcStats;
+
+/* Acceptance rule of fc_session_verify. */
+typedef enum {
+    FC_ACCEPT_GREEDY = 0,  /* dspark-metal.patch:1793-1797                */
+    FC_ACCEPT_SAMPLE = 1   /* speculative rejection sampling, Philox RNG  */
+} FcAcceptMode;
+
+typedef struct {
+    int mode;              /* FcAcceptMode                                */
+    float temperature;     /* > 0 for FC_ACCEPT_SAMPLE                    */
+    uint64_t seed;         /* Philox4x32-10 key                           */
+    uint64_t counter;      /* Philox counter base; callers advance it     */
+} FcAcceptConfig;
+
+/* ---- model -------------------------------------------------------------- */
+
+/* Creates a model on CUDA device `device` with every weight allocated and
+ * resident but not yet filled.  Rejects configurations whose weights exceed
+ * 95% of free device memory (moonlight_metal.m:834-843 does the same against
+ * the Metal working-set budget). */
+int fc_model_create(FcModel **out, const FcModelConfig *config, int device,
+                    char *error, size_t error_size);
+
+/* Expert-parallel variant: rank `rank` of `world` holds routed experts
+ * [rank * E / world, (rank + 1) * E / world); attention, dense, shared,
+ * router and lm-head weights are replicated.  E must divide by world. */
+int fc_model_create_ep(FcModel **out, const FcModelConfig *config, int device,
+                       int rank, int world, char *error, size_t error_size);
+
+/* Fills every weight with the seeded synthetic generator of floyd_synth.h
+ * (integer-only Philox mapping, identical to the CPU oracle's). */
+int fc_model_fill_synthetic(FcModel *model, uint64_t seed,
+                            char *error, size_t error_size);
+
+/* Uploads one tensor by its checkpoint name
+ * ("model.layers.3.self_attn.kv_b_proj.weight", moonlight_metal.m:301-321).
+ * Quantized matrices take two calls: `name` with the values in logical
+ * row-major layout (int8 [O][K], packed nibbles [O][K/2] with the even
+ * element low, or e2m1 codes packed the same way) and `name` + ".gs" with the
+ * group scales (fp16 [O][K/32], or ue8m0 bytes for MXFP4).  F32 tensors take
+ * float data.  `bytes` must match exactly. */
+int fc_model_set_tensor(FcModel *model, const char *name, const void *data,
+                        size_t bytes, char *error, size_t error_size);
+
+/* Downloads a tensor in the same logical layout fc_model_set_tensor takes. */
+int fc_model_get_tensor(const FcModel *model, const char *name, void *data,
+                        size_t bytes, char *error, size_t error_size);
+
+void fc_model_close(FcModel *model);                      /* moonlight_metal.h:50 */
+const char *fc_device_name(const FcModel *model);         /* moonlight_metal.h:51 */
+FcModelConfig fc_model_info(const FcModel *model);        /* moonlight_metal.h:52 */
+
+/* ---- session ------------------------------------------------------------ */
+
+int fc_session_create(FcSession **out, FcModel *model, const FcOptions *options,
+                      char *error, size_t error_size);   /* moonlight_metal.h:54-56 */
+void fc_session_destroy(FcSession *session);               /* moonlight_metal.h:57 */
+void fc_session_reset(FcSession *session);                 /* moonlight_metal.h:58 */
+int fc_session_position(const FcSession *session);         /* moonlight_metal.h:59 */
+FcStats fc_session_stats(const FcSession *session);        /* moonlight_metal.h:60 */
+
+/* Runs `count` tokens at position 0 (requires an empty session) and copies
+ * the logits of the last row.  moonlight_metal.h:61-63, moonlight_metal.m:1988-2005. */
+int fc_session_prefill(FcSession *session, const int *ids, int count,
+                       float *last_logits, char *error, size_t error_size);
+
+/* Runs `count` tokens at the current position (> 0).  moonlight_metal.h:64-66. */
+int fc_session_append(FcSession *session, const int *ids, int count,
+                      float *last_logits, char *error, size_t error_size);
+
+/* One token.  moonlight_metal.h:67-68, moonlight_metal.m:2024-2037. */
+int fc_session_decode(FcSession *session, int token, float *logits,
+                      char *error, size_t error_size);
+
+/* Speculative verify of 1 + k rows at the current position.
+ *   ids[0]      the token the target already chose (the previous round's
+ *               next_token, i.e. proposals[0] in the DS4 loop);
+ *   ids[1..k]   the k draft tokens.
+ * Greedy: row_tops[i] = argmax(logits of row i) (strict >, lowest index on
+ * ties, NaN ignored); commit = 1 + the number of leading i >= 1 with
+ * row_tops[i-1] == ids[i] (dspark-metal.patch:1793-1797).
+ * Sample: draft ids[i] is accepted when u_i < p_{i-1}(ids[i]) with
+ * p = softmax(logits / temperature); the first rejected draft is replaced
+ * by a sample of p_{i-1} with ids[i] removed, and a fully accepted round
+ * samples a bonus token from p_k.  Uniforms and Gumbel noise come from
+ * Philox4x32-10 keyed by `seed` at counter (`counter`, row, index).
+ * On return emitted[0..commit-1] = ids[0..commit-1], *n_emitted = commit,
+ * *next_token = the target's token after them, the latent KV cache is
+ * rolled back to position + commit and the position advances by commit.
+ * `last_logits` (nullable) receives the logits row commit-1. */
+int fc_session_verify(FcSession *session, const int *ids, int k,
+                      const FcAcceptConfig *accept, int *emitted,
+                      int *n_emitted, int *next_token, float *last_logits,
+                      char *error, size_t error_size);
+
+/* Truncates the session to `position` (clamped to <= the current one), as
+ * ds4_session_rewind (dspark-metal.patch:1973).  MLA keeps no compressor
+ * state, so rollback is a KV-length change. */
+int fc_session_rollback(FcSession *session, int position,
+                        char *error, size_t error_size);
+
+/* Copies the logits of every row of the last forward ([rows][vocab]); the
+ * Metal backend keeps only the last row (moonlight_metal.m:708-725). */
+int fc_session_copy_row_logits(const FcSession *session, float *logits,
+                               int capacity_rows);
+
+/* Fills latent KV positions [0, positions) of every layer with the seeded
+ * synthetic generator and sets the position, so a long context exists without
+ * a prefill (benchmark and test hook, like moonlight_test_* in
+ * moonlight_metal.h:69-96). */
+int fc_session_seed_context(FcSession *session, int positions, uint64_t seed,
+                            char *error, size_t error_size);
+
+/* Per-kernel profiling, the CUDA counterpart of MOONLIGHT_PROFILE
+ * (moonlight_metal.m:1899-1979) and ds4's kernel counters.  While enabled,
+ * forwards run eagerly (no graph) with a CUDA event after every kernel, and
+ * the time between events accumulates per kernel name.  fc_session_profile
+ * returns entry `index` (0 past the end). */
+int fc_session_set_profiling(FcSession *session, int enabled);
+int fc_session_profile(const FcSession *session, int index, char *name,
+                       size_t name_size, double *total_ms, uint64_t *launches);
+void fc_session_profile_reset(FcSession *session);
+
+/* ---- test hooks (moonlight_metal.h:69-96) -------------------------------- */
+
+int fc_test_kv_length(const FcSession *session, int layer);      /* :85 */
+/* latent [capacity][kv_lora_rank], rope [capacity][qk_rope_dim] as fp32. */
+int fc_test_copy_kv(const FcSession *session, int layer, float *latent,
+                    float *rope, int capacity);                   /* :86-87 */
+/* route ids [rows][experts_per_token] of the last forward (selection order). */
+int fc_test_copy_routes(const FcSession *session, int layer, int *route_ids,
+                        int capacity);                            /* :95-96 */
+/* Enables the per-layer hidden-state copies that fc_test_copy_layer_outputs
+ * reads (off by default: they add a copy per layer to every forward). */
+int fc_session_set_layer_trace(FcSession *session, int enabled);
+/* hidden state after each layer of the last forward: [layers][rows][hidden];
+ * needs fc_session_set_layer_trace(session, 1) before that forward. */
+int fc_test_copy_layer_outputs(const FcSession *session, float *outputs,
+                               int capacity_rows);
+
+/* ---- spec-runtime contract (deepseek_v4_runtime.h:72-256) --------------- */
+
+/* A thin owner of one session with the deepseek_v4_runtime_* call shapes. */
+typedef struct {
+    FcSession *session;
+    float *logits;       /* last forward's last row, [vocab]           */
+    int vocab_size;
+    int max_context;
+    int last_count;
+    int last_start_position;
+} FcRuntime;
+
+int fc_runtime_init(FcRuntime *runtime, FcModel *model, int max_context,
+                    int max_batch);                                /* :72-97   */
+int fc_runtime_forward(FcRuntime *runtime, const int *token_ids, int n_tokens,
+                       const float **logits);                      /* :148-178 */
+int fc_runtime_argmax(const float *logits, int vocab_size);        /* :231-237 */
+int fc_runtime_verify_token(const float *logits, int vocab_size,
+                            int64_t proposal, int *accepted);      /* :239-244 */
+void fc_runtime_reset(FcRuntime *runtime);                         /* :99-128  */
+void fc_runtime_free(FcRuntime *runtime);                          /* :246-256 */
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FLOYD_CUDA_H */

@@ -1,0 +1,32 @@
+/*
+ * floyd_kernels.h - single-kernel entry points of the B200 backend, for
+ * callers that offload one operation at a time (floyd's backend_metal.h
+ * surface) and for per-kernel parity tests.
+ *
+ * These take HOST arrays, copy them to the device, run the same sm_100a
+ * kernel the session path uses, and copy the result back.
+ */
+#ifndef FLOYD_KERNELS_H
+#define FLOYD_KERNELS_H
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* y[s][o] = sum_k x[s][k] * dequant(w[o][k]) for s < S, fp32 accumulation.
+ * `format` is an FcFormat (Q8, Q4 or MXFP4); `values` / `scales` are in the
+ * logical layout of fc_model_set_tensor (int8 [O][K] or packed nibbles
+ * [O][K/2], fp16 / ue8m0 group scales [O][K/32]).  K % 32 == 0, 1 <= S <= 8.
+ * Replaces fm_matmul_q8 / fm_matmul_q4 (backend_metal.h:18-33) and the Metal
+ * offload of deepseek_v4_fp4_matmul_f32 (deepseek_v4_quant.h:103-139). */
+int fc_matmul(int format, float *y, const float *x, const void *values,
+              const void *scales, int O, int K, int S, char *error,
+              size_t error_size);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

@@ -1,0 +1,854 @@
+/*
+ * floyd_oracle.c - CPU restatement of floyd's verify step (TEST
+ * INFRASTRUCTURE ONLY; see floyd_oracle.h for who may use it and how its
+ * parity is pinned).
+ *
+ * The model is the compressed-latent MLA + MoE transformer that floyd's
+ * Moonlight Metal runtime executes (moonlight_metal.m:287-725), with the
+ * MoE contract of moe_route.h / moe_exec.h and the acceptance rule of the
+ * DS4 speculative verifier (patches/ds4/deepseek-v4-dspark-metal.patch
+ * :1727-1906).  Weights come from the integer synthetic generator of
+ * include/floyd_synth.h, so the CUDA backend and this file hold identical
+ * weights for the same seed.
+ */
+#include "floyd_oracle.h"
+
+#include <math.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include "../include/floyd_synth.h"
+
+/* ---- primitives ---------------------------------------------------------- */
+
+void orc_philox4x32_10(const uint32_t counter[4], const uint32_t key[2],
+                       uint32_t out[4]) {
+    fc_philox4x32_10(counter, key, out);
+}
+
+float orc_fp16_to_f32(uint16_t bits) {
+    uint32_t sign = (uint32_t)(bits >> 15) << 31;
+    int exponent = (bits >> 10) & 31;
+    uint32_t mantissa = bits & 1023u;
+    float value;
+    if (exponent == 0) value = ldexpf((float)mantissa, -24);
+    else if (exponent == 31) value = mantissa ? NAN : INFINITY;
+    else value = ldexpf((float)(mantissa | 1024u), exponent - 25);
+    uint32_t out;
+    memcpy(&out, &value, 4);
+    out |= sign;
+    memcpy(&value, &out, 4);
+    return value;
+}
+
+uint16_t orc_f32_to_fp16(float value) {
+    /* IEEE round-to-nearest-even conversion, the same as __float2half_rn. */
+    uint32_t x;
+    memcpy(&x, &value, 4);
+    uint32_t sign = (x >> 16) & 0x8000u;
+    uint32_t absx = x & 0x7FFFFFFFu;
+    if (absx >= 0x7F800000u) /* inf or nan */
+        return (uint16_t)(sign | 0x7C00u | (absx > 0x7F800000u ? 0x200u : 0u));
+    if (absx >= 0x477FF000u) return (uint16_t)(sign | 0x7C00u); /* overflow */
+    if (absx < 0x33000001u) return (uint16_t)sign;               /* < half min subnormal */
+    int exponent = (int)(absx >> 23) - 127;
+    uint32_t mantissa = (absx & 0x7FFFFFu) | 0x800000u;
+    int shift;
+    uint32_t base;
+    if (exponent < -14) { /* subnormal half */
+        shift = -exponent - 14 + 13;
+        base = 0;
+    } else {
+        shift = 13;
+        base = (uint32_t)(exponent + 15) << 10;
+        mantissa &= 0x7FFFFFu;
+    }
+    uint32_t kept = mantissa >> shift;
+    uint32_t rest = mantissa & ((1u << shift) - 1u);
+    uint32_t half = 1u << (shift - 1);
+    uint32_t result = base + kept;
+    if (rest > half || (rest == half && (kept & 1u))) result += 1u;
+    return (uint16_t)(sign | result);
+}
+
+float orc_e8m0_to_f32(uint8_t code) {
+    if (code == 255) return NAN;
+    return ldexpf(1.0f, (int)code - 127);
+}
+
+static const float orc_e2m1_table[16] = {
+    0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f,
+    -0.0f, -0.5f, -1.0f, -1.5f, -2.0f, -3.0f, -4.0f, -6.0f
+};
+
+float orc_e2m1_to_f32(uint8_t code) { return orc_e2m1_table[code & 15]; }
+
+static inline float value_of(int fmt, int8_t v) {
+    return fmt == FC_FMT_MXFP4 ? orc_e2m1_table[(uint8_t)v & 15] : (float)v;
+}
+
+void orc_gemv(int fmt, const int8_t *values, const float *scales,
+              const float *f32, int O, int K, const float *x, int S, float *y) {
+    int groups = K / 32;
+#pragma omp parallel for schedule(static)
+    for (int o = 0; o < O; ++o) {
+        for (int s = 0; s < S; ++s) {
+            const float *xs = x + (int64_t)s * K;
+            float sum = 0.0f;
+            if (fmt == FC_FMT_F32) {
+                const float *w = f32 + (int64_t)o * K;
+                for (int k = 0; k < K; ++k) sum += w[k] * xs[k];
+            } else {
+                const int8_t *w = values + (int64_t)o * K;
+                for (int g = 0; g < groups; ++g) {
+                    float partial = 0.0f;
+                    for (int k = 32 * g; k < 32 * g + 32; ++k)
+                        partial += value_of(fmt, w[k]) * xs[k];
+                    sum += partial * scales[(int64_t)o * groups + g];
+                }
+            }
+            y[(int64_t)s * O + o] = sum;
+        }
+    }
+}
+
+void orc_rmsnorm(const float *x, const float *w, int rows, int width, float eps,
+                 float *out) {
+    for (int r = 0; r < rows; ++r) {
+        const float *src = x + (int64_t)r * width;
+        float sum = 0.0f;
+        for (int c = 0; c < width; ++c) sum += src[c] * src[c];
+        float scale = 1.0f / sqrtf(sum / (float)width + eps);
+        for (int c = 0; c < width; ++c)
+            out[(int64_t)r * width + c] = src[c] * scale * w[c];
+    }
+}
+
+void orc_rope(const float *in, float *out, int width, int position, float theta) {
+    int half = width / 2;
+    float tmp[512];
+    for (int c = 0; c < width; ++c) tmp[c] = in[c];
+    for (int p = 0; p < half; ++p) {
+        float angle = (float)position * powf(theta, -2.0f * (float)p / (float)width);
+        float cosine = cosf(angle), sine = sinf(angle);
+        float first = tmp[2 * p], second = tmp[2 * p + 1];
+        out[p] = first * cosine - second * sine;
+        out[half + p] = second * cosine + first * sine;
+    }
+}
+
+static void route_scores(const float *logits, int n, int score_fn, float *scores) {
+    if (score_fn == FC_SCORE_SOFTMAX) {
+        float m = logits[0];
+        for (int e = 1; e < n; ++e) if (logits[e] > m) m = logits[e];
+        float sum = 0.0f;
+        for (int e = 0; e < n; ++e) { scores[e] = expf(logits[e] - m); sum += scores[e]; }
+        for (int e = 0; e < n; ++e) scores[e] /= sum;
+        return;
+    }
+    for (int e = 0; e < n; ++e) {
+        float x = logits[e];
+        if (score_fn == FC_SCORE_SQRT_SOFTPLUS) {
+            float sp;
+            if (x > 20.0f) sp = x;
+            else if (x < -20.0f) sp = expf(x);
+            else sp = log1pf(expf(x));
+            scores[e] = sqrtf(sp);
+        } else {
+            scores[e] = 1.0f / (1.0f + expf(-x));
+        }
+    }
+}
+
+int orc_route(const float *logits, const float *bias, int n_experts, int top_k,
+              int score_fn, int normalize, float routed_scale,
+              const int *fixed, int *indices, float *weights) {
+    float scores[1024], choice[1024];
+    if (n_experts <= 0 || n_experts > 1024 || top_k <= 0) return 0;
+    if (top_k > n_experts) top_k = n_experts;
+    route_scores(logits, n_experts, score_fn, scores);
+    if (fixed) { /* moe_route_fixed, moe_route.h:76-87 */
+        for (int k = 0; k < top_k; ++k) {
+            if (fixed[k] < 0 || fixed[k] >= n_experts) return 0;
+            indices[k] = fixed[k];
+            weights[k] = scores[fixed[k]];
+        }
+    } else { /* moe_route_select, moe_route.h:47-74 */
+        for (int e = 0; e < n_experts; ++e) choice[e] = scores[e] + (bias ? bias[e] : 0.0f);
+        for (int k = 0; k < top_k; ++k) {
+            int best = -1;
+            float best_value = -INFINITY;
+            for (int e = 0; e < n_experts; ++e) {
+                int taken = 0;
+                for (int j = 0; j < k; ++j) if (indices[j] == e) { taken = 1; break; }
+                if (!taken && choice[e] > best_value) { best = e; best_value = choice[e]; }
+            }
+            indices[k] = best;
+            weights[k] = scores[best];
+        }
+    }
+    /* moe_route_finalize, moe_route.h:89-99 */
+    if (normalize) {
+        float sum = 0.0f;
+        for (int k = 0; k < top_k; ++k) sum += weights[k];
+        sum += 1e-20f;
+        for (int k = 0; k < top_k; ++k) weights[k] /= sum;
+    }
+    for (int k = 0; k < top_k; ++k) weights[k] *= routed_scale;
+    return top_k;
+}
+
+int orc_argmax(const float *logits, int n) {
+    int best = -1;
+    for (int i = 0; i < n; ++i) {
+        float v = logits[i];
+        if (v != v) continue;
+        if (best < 0 || v > logits[best]) best = i;
+    }
+    return best;
+}
+
+int orc_accept_greedy(const int *row_tops, const int *ids, int k) {
+    int commit = 1;
+    for (int i = 1; i <= k; ++i) {
+        if (row_tops[i - 1] != ids[i]) break;
+        commit++;
+    }
+    return commit;
+}
+
+float orc_accept_uniform(uint64_t seed, uint64_t counter, int row) {
+    uint32_t c[4] = {(uint32_t)row, 0xACCE97EDu, (uint32_t)counter, (uint32_t)(counter >> 32)};
+    uint32_t key[2] = {(uint32_t)seed, (uint32_t)(seed >> 32)};
+    uint32_t out[4];
+    fc_philox4x32_10(c, key, out);
+    return (float)(out[0] >> 8) * (1.0f / 16777216.0f);
+}
+
+float orc_gumbel(uint64_t seed, uint64_t counter, int row, int v) {
+    uint32_t c[4] = {(uint32_t)v >> 2, (uint32_t)row, (uint32_t)counter,
+                     (uint32_t)(counter >> 32) ^ 0x9E3779B9u};
+    uint32_t key[2] = {(uint32_t)seed, (uint32_t)(seed >> 32)};
+    uint32_t out[4];
+    fc_philox4x32_10(c, key, out);
+    float u = ((float)(out[v & 3] >> 8) + 0.5f) * (1.0f / 16777216.0f);
+    return -logf(-logf(u));
+}
+
+static int sample_excluding(const float *logits, int V, float temperature,
+                            uint64_t seed, uint64_t counter, int row, int excluded) {
+    int best = -1;
+    float best_value = -INFINITY;
+    for (int v = 0; v < V; ++v) {
+        if (v == excluded || logits[v] != logits[v]) continue;
+        float z = logits[v] / temperature + orc_gumbel(seed, counter, row, v);
+        if (best < 0 || z > best_value) { best = v; best_value = z; }
+    }
+    return best;
+}
+
+static float softmax_prob(const float *logits, int V, float temperature, int x) {
+    float m = -INFINITY;
+    for (int v = 0; v < V; ++v) {
+        float z = logits[v] / temperature;
+        if (z > m) m = z;
+    }
+    float sum = 0.0f;
+    for (int v = 0; v < V; ++v) sum += expf(logits[v] / temperature - m);
+    return expf(logits[x] / temperature - m) / sum;
+}
+
+int orc_accept_sample(const float *logits, int V, const int *ids, int k,
+                      float temperature, uint64_t seed, uint64_t counter,
+                      int *next_token) {
+    for (int i = 1; i <= k; ++i) {
+        const float *row = logits + (int64_t)(i - 1) * V;
+        float p = softmax_prob(row, V, temperature, ids[i]);
+        float u = orc_accept_uniform(seed, counter, i - 1);
+        if (!(u < p)) {
+            *next_token = sample_excluding(row, V, temperature, seed, counter, i - 1, ids[i]);
+            return i;
+        }
+    }
+    *next_token = sample_excluding(logits + (int64_t)k * V, V, temperature, seed, counter, k, -1);
+    return k + 1;
+}
+
+/* ---- model ---------------------------------------------------------------- */
+
+typedef struct {
+    int fmt, O, K;
+    int8_t *values;   /* [O][K] logical (int8, int4 value, or e2m1 code)   */
+    float *scales;    /* [O][K/32]                                         */
+    uint16_t *scale_bits; /* fp16 bits or e8m0 byte per group              */
+    float *f32;       /* [O][K] for F32                                    */
+} Mat;
+
+typedef struct {
+    float *attn_norm, *ffn_norm, *kv_a_norm, *q_a_norm;
+    Mat q_proj, q_a, q_b, kv_a, kv_b, o_proj;
+    Mat router;       /* F32 [E][D] */
+    float *bias;      /* [E] or NULL */
+    int *hash;        /* [V][top_k] or NULL */
+    Mat *gate, *up, *down;   /* [E] */
+    Mat sh_gate, sh_up, sh_down;
+    Mat d_gate, d_up, d_down;
+    int dense;
+} Layer;
+
+struct OrcModel {
+    FcModelConfig c;
+    uint64_t seed;
+    Mat embed, lm_head;
+    float *final_norm;
+    Layer *layers;
+};
+
+struct OrcSession {
+    OrcModel *m;
+    int ctx, kv_fp16, position;
+    float *latent; /* [layers][ctx][L] */
+    float *rope;   /* [layers][ctx][R] */
+};
+
+static float *alloc_f(size_t n) { return (float *)calloc(n ? n : 1, sizeof(float)); }
+
+static void mat_gen(Mat *m, int fmt, int O, int K, uint64_t seed, uint32_t tid) {
+    m->fmt = fmt; m->O = O; m->K = K;
+    size_t n = (size_t)O * K;
+    if (fmt == FC_FMT_F32) {
+        m->f32 = alloc_f(n);
+#pragma omp parallel for schedule(static)
+        for (size_t e = 0; e < n; ++e) m->f32[e] = fc_synth_f32(seed, tid, e);
+        return;
+    }
+    int groups = K / 32;
+    m->values = (int8_t *)malloc(n);
+    m->scales = alloc_f((size_t)O * groups);
+    m->scale_bits = (uint16_t *)malloc((size_t)O * groups * sizeof(uint16_t));
+    /* One Philox block yields 8 int8 values or 32 nibbles (floyd_synth.h). */
+    if (fmt == FC_FMT_Q8) {
+        size_t blocks = (n + 7) / 8;
+#pragma omp parallel for schedule(static)
+        for (size_t b = 0; b < blocks; ++b) {
+            uint32_t w[4];
+            fc_synth_block(seed, tid, FC_STREAM_VALUES, b, w);
+            for (int i = 0; i < 8 && b * 8 + i < n; ++i) {
+                int v = (int)fc_synth_byte(w, 2 * i) + (int)fc_synth_byte(w, 2 * i + 1) - 255;
+                m->values[b * 8 + i] = (int8_t)(v / 2);
+            }
+        }
+    } else {
+        size_t blocks = (n + 31) / 32;
+#pragma omp parallel for schedule(static)
+        for (size_t b = 0; b < blocks; ++b) {
+            uint32_t w[4];
+            fc_synth_block(seed, tid, FC_STREAM_VALUES, b, w);
+            for (int i = 0; i < 32 && b * 32 + i < n; ++i) {
+                int nib = (int)((w[i >> 3] >> (4 * (i & 7))) & 0xFu);
+                m->values[b * 32 + i] = (int8_t)(fmt == FC_FMT_Q4 ? nib - 8 : nib);
+            }
+        }
+    }
+#pragma omp parallel for schedule(static)
+    for (size_t g = 0; g < (size_t)O * groups; ++g) {
+        if (fmt == FC_FMT_Q8) {
+            m->scale_bits[g] = fc_synth_scale_q8(seed, tid, g);
+            m->scales[g] = orc_fp16_to_f32(m->scale_bits[g]);
+        } else if (fmt == FC_FMT_Q4) {
+            m->scale_bits[g] = fc_synth_scale_q4(seed, tid, g);
+            m->scales[g] = orc_fp16_to_f32(m->scale_bits[g]);
+        } else {
+            m->scale_bits[g] = fc_synth_scale_e8m0(seed, tid, g);
+            m->scales[g] = orc_e8m0_to_f32((uint8_t)m->scale_bits[g]);
+        }
+    }
+}
+
+static void mat_free(Mat *m) {
+    free(m->values); free(m->scales); free(m->scale_bits); free(m->f32);
+    memset(m, 0, sizeof(*m));
+}
+
+static float *norm_gen(int n, uint64_t seed, uint32_t tid) {
+    float *w = alloc_f((size_t)n);
+    for (int i = 0; i < n; ++i) w[i] = fc_synth_norm(seed, tid, (uint64_t)i);
+    return w;
+}
+
+static void mat_apply(const Mat *m, const float *x, int S, float *y) {
+    orc_gemv(m->fmt, m->values, m->scales, m->f32, m->O, m->K, x, S, y);
+}
+
+OrcModel *orc_model_create(const FcModelConfig *config, uint64_t seed) {
+    if (!config || config->hidden_size % 32 || config->kv_lora_rank % 32) return NULL;
+    OrcModel *m = (OrcModel *)calloc(1, sizeof(*m));
+    const FcModelConfig *c = config;
+    m->c = *config;
+    m->seed = seed;
+    int D = c->hidden_size, H = c->head_count, L = c->kv_lora_rank, R = c->qk_rope_dim;
+    int qw = H * (c->qk_nope_dim + R);
+    int df = c->dense_format, ef = c->expert_format;
+    mat_gen(&m->embed, df, c->vocab_size, D, seed, fc_tensor_id(-1, FC_T_EMBED, 0));
+    mat_gen(&m->lm_head, df, c->vocab_size, D, seed, fc_tensor_id(-1, FC_T_LM_HEAD, 0));
+    m->final_norm = norm_gen(D, seed, fc_tensor_id(-1, FC_T_FINAL_NORM, 0));
+    m->layers = (Layer *)calloc((size_t)c->layer_count, sizeof(Layer));
+    for (int l = 0; l < c->layer_count; ++l) {
+        Layer *y = &m->layers[l];
+        y->attn_norm = norm_gen(D, seed, fc_tensor_id(l, FC_T_ATTN_NORM, 0));
+        y->ffn_norm = norm_gen(D, seed, fc_tensor_id(l, FC_T_FFN_NORM, 0));
+        y->kv_a_norm = norm_gen(L, seed, fc_tensor_id(l, FC_T_KV_A_NORM, 0));
+        if (c->q_lora_rank > 0) {
+            y->q_a_norm = norm_gen(c->q_lora_rank, seed, fc_tensor_id(l, FC_T_Q_A_NORM, 0));
+            mat_gen(&y->q_a, df, c->q_lora_rank, D, seed, fc_tensor_id(l, FC_T_Q_A, 0));
+            mat_gen(&y->q_b, df, qw, c->q_lora_rank, seed, fc_tensor_id(l, FC_T_Q_B, 0));
+        } else {
+            mat_gen(&y->q_proj, df, qw, D, seed, fc_tensor_id(l, FC_T_Q_PROJ, 0));
+        }
+        mat_gen(&y->kv_a, df, L + R, D, seed, fc_tensor_id(l, FC_T_KV_A, 0));
+        mat_gen(&y->kv_b, df, H * (c->qk_nope_dim + c->value_dim), L, seed,
+                fc_tensor_id(l, FC_T_KV_B, 0));
+        mat_gen(&y->o_proj, df, D, H * c->value_dim, seed, fc_tensor_id(l, FC_T_O_PROJ, 0));
+        y->dense = l < c->first_dense_layer_count;
+        if (y->dense) {
+            int I = c->dense_intermediate_size;
+            mat_gen(&y->d_gate, df, I, D, seed, fc_tensor_id(l, FC_T_DENSE_GATE, 0));
+            mat_gen(&y->d_up, df, I, D, seed, fc_tensor_id(l, FC_T_DENSE_UP, 0));
+            mat_gen(&y->d_down, df, D, I, seed, fc_tensor_id(l, FC_T_DENSE_DOWN, 0));
+            continue;
+        }
+        int E = c->expert_count, I = c->moe_intermediate_size;
+        mat_gen(&y->router, FC_FMT_F32, E, D, seed, fc_tensor_id(l, FC_T_ROUTER, 0));
+        if (c->has_selection_bias) {
+            y->bias = alloc_f((size_t)E);
+            for (int e = 0; e < E; ++e)
+                y->bias[e] = fc_synth_bias(seed, fc_tensor_id(l, FC_T_ROUTER_BIAS, 0), (uint64_t)e);
+        }
+        if (l < c->hash_layer_count) {
+            y->hash = (int *)malloc((size_t)c->vocab_size * c->experts_per_token * sizeof(int));
+            for (int t = 0; t < c->vocab_size; ++t)
+                for (int k = 0; k < c->experts_per_token; ++k)
+                    y->hash[(int64_t)t * c->experts_per_token + k] = fc_synth_hash_expert(
+                        seed, fc_tensor_id(l, FC_T_HASH, 0), t, k, E, c->experts_per_token);
+        }
+        y->gate = (Mat *)calloc((size_t)E, sizeof(Mat));
+        y->up = (Mat *)calloc((size_t)E, sizeof(Mat));
+        y->down = (Mat *)calloc((size_t)E, sizeof(Mat));
+        for (int e = 0; e < E; ++e) {
+            mat_gen(&y->gate[e], ef, I, D, seed, fc_tensor_id(l, FC_T_EXP_GATE, e + 1));
+            mat_gen(&y->up[e], ef, I, D, seed, fc_tensor_id(l, FC_T_EXP_UP, e + 1));
+            mat_gen(&y->down[e], ef, D, I, seed, fc_tensor_id(l, FC_T_EXP_DOWN, e + 1));
+        }
+        if (c->shared_expert_count > 0) {
+            int W = I * c->shared_expert_count;
+            mat_gen(&y->sh_gate, df, W, D, seed, fc_tensor_id(l, FC_T_SH_GATE, 0));
+            mat_gen(&y->sh_up, df, W, D, seed, fc_tensor_id(l, FC_T_SH_UP, 0));
+            mat_gen(&y->sh_down, df, D, W, seed, fc_tensor_id(l, FC_T_SH_DOWN, 0));
+        }
+    }
+    return m;
+}
+
+void orc_model_free(OrcModel *m) {
+    if (!m) return;
+    mat_free(&m->embed); mat_free(&m->lm_head); free(m->final_norm);
+    for (int l = 0; l < m->c.layer_count; ++l) {
+        Layer *y = &m->layers[l];
+        free(y->attn_norm); free(y->ffn_norm); free(y->kv_a_norm); free(y->q_a_norm);
+        mat_free(&y->q_proj); mat_free(&y->q_a); mat_free(&y->q_b);
+        mat_free(&y->kv_a); mat_free(&y->kv_b); mat_free(&y->o_proj);
+        mat_free(&y->router); free(y->bias); free(y->hash);
+        if (y->gate) {
+            for (int e = 0; e < m->c.expert_count; ++e) {
+                mat_free(&y->gate[e]); mat_free(&y->up[e]); mat_free(&y->down[e]);
+            }
+        }
+        free(y->gate); free(y->up); free(y->down);
+        mat_free(&y->sh_gate); mat_free(&y->sh_up); mat_free(&y->sh_down);
+        mat_free(&y->d_gate); mat_free(&y->d_up); mat_free(&y->d_down);
+    }
+    free(m->layers);
+    free(m);
+}
+
+/* Name lookup for the checkpoint tensor names the reference uses
+ * (moonlight_metal.m:301-321, :450-466, :494-500, :580-612). */
+static int lookup(OrcModel *m, const char *name, Mat **mat, float **vec, size_t *count) {
+    int l = -1, e = -1;
+    char rest[256];
+    *mat = NULL; *vec = NULL; *count = 0;
+    const FcModelConfig *c = &m->c;
+    if (!strcmp(name, "model.embed_tokens.weight")) { *mat = &m->embed; return 1; }
+    if (!strcmp(name, "lm_head.weight")) { *mat = &m->lm_head; return 1; }
+    if (!strcmp(name, "model.norm.weight")) { *vec = m->final_norm; *count = (size_t)c->hidden_size; return 1; }
+    if (sscanf(name, "model.layers.%d.%255s", &l, rest) != 2 || l < 0 || l >= c->layer_count) return 0;
+    Layer *y = &m->layers[l];
+    if (!strcmp(rest, "input_layernorm.weight")) { *vec = y->attn_norm; *count = (size_t)c->hidden_size; return 1; }
+    if (!strcmp(rest, "post_attention_layernorm.weight")) { *vec = y->ffn_norm; *count = (size_t)c->hidden_size; return 1; }
+    if (!strcmp(rest, "self_attn.kv_a_layernorm.weight")) { *vec = y->kv_a_norm; *count = (size_t)c->kv_lora_rank; return 1; }
+    if (!strcmp(rest, "self_attn.q_a_layernorm.weight") && y->q_a_norm) { *vec = y->q_a_norm; *count = (size_t)c->q_lora_rank; return 1; }
+    if (!strcmp(rest, "self_attn.q_proj.weight") && !c->q_lora_rank) { *mat = &y->q_proj; return 1; }
+    if (!strcmp(rest, "self_attn.q_a_proj.weight") && c->q_lora_rank) { *mat = &y->q_a; return 1; }
+    if (!strcmp(rest, "self_attn.q_b_proj.weight") && c->q_lora_rank) { *mat = &y->q_b; return 1; }
+    if (!strcmp(rest, "self_attn.kv_a_proj_with_mqa.weight")) { *mat = &y->kv_a; return 1; }
+    if (!strcmp(rest, "self_attn.kv_b_proj.weight")) { *mat = &y->kv_b; return 1; }
+    if (!strcmp(rest, "self_attn.o_proj.weight")) { *mat = &y->o_proj; return 1; }
+    if (y->dense) {
+        if (!strcmp(rest, "mlp.gate_proj.weight")) { *mat = &y->d_gate; return 1; }
+        if (!strcmp(rest, "mlp.up_proj.weight")) { *mat = &y->d_up; return 1; }
+        if (!strcmp(rest, "mlp.down_proj.weight")) { *mat = &y->d_down; return 1; }
+        return 0;
+    }
+    if (!strcmp(rest, "mlp.gate.weight")) { *mat = &y->router; return 1; }
+    if (!strcmp(rest, "mlp.gate.e_score_correction_bias") && y->bias) { *vec = y->bias; *count = (size_t)c->expert_count; return 1; }
+    if (!strcmp(rest, "mlp.shared_experts.gate_proj.weight")) { *mat = &y->sh_gate; return 1; }
+    if (!strcmp(rest, "mlp.shared_experts.up_proj.weight")) { *mat = &y->sh_up; return 1; }
+    if (!strcmp(rest, "mlp.shared_experts.down_proj.weight")) { *mat = &y->sh_down; return 1; }
+    char proj[64];
+    if (sscanf(rest, "mlp.experts.%d.%63s", &e, proj) == 2 && e >= 0 && e < c->expert_count) {
+        if (!strcmp(proj, "gate_proj.weight")) { *mat = &y->gate[e]; return 1; }
+        if (!strcmp(proj, "up_proj.weight")) { *mat = &y->up[e]; return 1; }
+        if (!strcmp(proj, "down_proj.weight")) { *mat = &y->down[e]; return 1; }
+    }
+    return 0;
+}
+
+int orc_model_set_f32(OrcModel *m, const char *name, const float *data, size_t count) {
+    Mat *mat; float *vec; size_t n;
+    if (!m || !lookup(m, name, &mat, &vec, &n)) return 0;
+    if (vec) {
+        if (count != n) return 0;
+        memcpy(vec, data, n * sizeof(float));
+        return 1;
+    }
+    if (count != (size_t)mat->O * mat->K) return 0;
+    int O = mat->O, K = mat->K;
+    mat_free(mat);
+    mat->fmt = FC_FMT_F32; mat->O = O; mat->K = K;
+    mat->f32 = alloc_f(count);
+    memcpy(mat->f32, data, count * sizeof(float));
+    return 1;
+}
+
+size_t orc_model_get_tensor(const OrcModel *m, const char *name, int scales_part,
+                            void *data, size_t bytes) {
+    Mat *mat; float *vec; size_t n;
+    if (!m || !lookup((OrcModel *)m, name, &mat, &vec, &n)) return 0;
+    if (vec) {
+        if (bytes < n * 4) return 0;
+        memcpy(data, vec, n * 4);
+        return n * 4;
+    }
+    size_t elems = (size_t)mat->O * mat->K;
+    if (mat->fmt == FC_FMT_F32) {
+        if (bytes < elems * 4) return 0;
+        memcpy(data, mat->f32, elems * 4);
+        return elems * 4;
+    }
+    size_t groups = (size_t)mat->O * (mat->K / 32);
+    if (scales_part) {
+        if (mat->fmt == FC_FMT_MXFP4) {
+            if (bytes < groups) return 0;
+            for (size_t g = 0; g < groups; ++g) ((uint8_t *)data)[g] = (uint8_t)mat->scale_bits[g];
+            return groups;
+        }
+        if (bytes < groups * 2) return 0;
+        memcpy(data, mat->scale_bits, groups * 2);
+        return groups * 2;
+    }
+    if (mat->fmt == FC_FMT_Q8) {
+        if (bytes < elems) return 0;
+        memcpy(data, mat->values, elems);
+        return elems;
+    }
+    /* packed nibbles, even element low (moonlight_kernels.metal:123-127) */
+    if (bytes < elems / 2) return 0;
+    uint8_t *out = (uint8_t *)data;
+    for (size_t i = 0; i < elems / 2; ++i) {
+        int lo = mat->values[2 * i], hi = mat->values[2 * i + 1];
+        if (mat->fmt == FC_FMT_Q4) { lo += 8; hi += 8; }
+        out[i] = (uint8_t)((lo & 15) | ((hi & 15) << 4));
+    }
+    return elems / 2;
+}
+
+OrcSession *orc_session_create(OrcModel *m, int context_size, int kv_fp16) {
+    if (!m || context_size <= 0) return NULL;
+    OrcSession *s = (OrcSession *)calloc(1, sizeof(*s));
+    s->m = m; s->ctx = context_size; s->kv_fp16 = kv_fp16;
+    size_t rows = (size_t)m->c.layer_count * context_size;
+    s->latent = alloc_f(rows * m->c.kv_lora_rank);
+    s->rope = alloc_f(rows * m->c.qk_rope_dim);
+    if (!s->latent || !s->rope) { orc_session_free(s); return NULL; }
+    return s;
+}
+
+void orc_session_free(OrcSession *s) {
+    if (!s) return;
+    free(s->latent); free(s->rope); free(s);
+}
+
+int orc_session_position(const OrcSession *s) { return s ? s->position : 0; }
+
+void orc_session_set_position(OrcSession *s, int position) {
+    if (s && position >= 0 && position <= s->position) s->position = position;
+}
+
+int orc_session_seed_context(OrcSession *s, int positions, uint64_t seed) {
+    const FcModelConfig *c = &s->m->c;
+    if (positions < 0 || positions > s->ctx) return 0;
+    int L = c->kv_lora_rank, R = c->qk_rope_dim;
+    for (int l = 0; l < c->layer_count; ++l) {
+        uint32_t tl = fc_tensor_id(l, FC_T_KV_LATENT, 0), tr = fc_tensor_id(l, FC_T_KV_ROPE, 0);
+        float *lat = s->latent + (size_t)l * s->ctx * L;
+        float *rop = s->rope + (size_t)l * s->ctx * R;
+        for (size_t e = 0; e < (size_t)positions * L; ++e) lat[e] = fc_synth_kv(seed, tl, e);
+        for (size_t e = 0; e < (size_t)positions * R; ++e) rop[e] = fc_synth_kv(seed, tr, e);
+    }
+    s->position = positions;
+    return 1;
+}
+
+static float round_kv(const OrcSession *s, float v) {
+    return s->kv_fp16 ? orc_fp16_to_f32(orc_f32_to_fp16(v)) : v;
+}
+
+static float silu(float x) { return x / (1.0f + expf(-x)); }
+
+/* moe_f32_add_expert (moe_exec.h:47-63) on a quantized expert, accumulating
+ * coefficient * down(swiglu(gate x, up x)) into out. */
+static void add_expert(const Mat *gate, const Mat *up, const Mat *down, const float *x,
+                       float coefficient, float limit, float *out, float *tmp) {
+    int I = gate->O, D = down->O;
+    float *g = tmp, *u = tmp + I, *h = tmp + 2 * I, *p = tmp + 3 * I;
+    mat_apply(gate, x, 1, g);
+    mat_apply(up, x, 1, u);
+    for (int i = 0; i < I; ++i) {
+        float gv = g[i], uv = u[i];
+        if (limit > 0.0f) {
+            if (gv > limit) gv = limit;
+            if (uv > limit) uv = limit;
+            if (uv < -limit) uv = -limit;
+        }
+        h[i] = silu(gv) * uv;
+    }
+    mat_apply(down, h, 1, p);
+    for (int d = 0; d < D; ++d) out[d] += coefficient * p[d];
+}
+
+int orc_session_forward(OrcSession *s, const int *ids, int rows, float *logits,
+                        float *layer_out, int *routes) {
+    OrcModel *m = s->m;
+    const FcModelConfig *c = &m->c;
+    int D = c->hidden_size, H = c->head_count, L = c->kv_lora_rank, R = c->qk_rope_dim;
+    int NP = c->qk_nope_dim, VD = c->value_dim, QW = NP + R, V = c->vocab_size;
+    int pos = s->position;
+    if (rows <= 0 || pos + rows > s->ctx) return 0;
+    for (int r = 0; r < rows; ++r) if (ids[r] < 0 || ids[r] >= V) return 0;
+
+    int maxI = c->moe_intermediate_size * (c->shared_expert_count > 1 ? c->shared_expert_count : 1);
+    if (c->dense_intermediate_size > maxI) maxI = c->dense_intermediate_size;
+    if (c->moe_intermediate_size > maxI) maxI = c->moe_intermediate_size;
+    int maxO = D;
+    if (H * QW > maxO) maxO = H * QW;
+    if (H * (NP + VD) > maxO) maxO = H * (NP + VD);
+    if (c->q_lora_rank > maxO) maxO = c->q_lora_rank;
+    float *x = alloc_f((size_t)rows * D);
+    float *xn = alloc_f((size_t)rows * D);
+    float *q = alloc_f((size_t)rows * H * QW);
+    float *qa = alloc_f((size_t)rows * (c->q_lora_rank > 0 ? c->q_lora_rank : 1));
+    float *ckv = alloc_f((size_t)rows * (L + R));
+    float *attn = alloc_f((size_t)rows * H * VD);
+    float *tmp = alloc_f((size_t)4 * maxI + (size_t)4 * maxO + (size_t)s->ctx + (size_t)8 * L + D);
+    float *y = alloc_f((size_t)D);
+    float *ao = alloc_f((size_t)rows * D);
+    float scale = 1.0f / sqrtf((float)(NP + R));
+
+    /* embedding: dequantized row (moonlight_kernels.metal:10-21) */
+    for (int r = 0; r < rows; ++r) {
+        const Mat *e = &m->embed;
+        for (int k = 0; k < D; ++k) {
+            float v = e->fmt == FC_FMT_F32 ? e->f32[(int64_t)ids[r] * D + k]
+                : value_of(e->fmt, e->values[(int64_t)ids[r] * D + k]) *
+                  e->scales[(int64_t)ids[r] * (D / 32) + k / 32];
+            x[(int64_t)r * D + k] = v;
+        }
+    }
+
+    for (int l = 0; l < c->layer_count; ++l) {
+        Layer *ly = &m->layers[l];
+        float *lat = s->latent + (size_t)l * s->ctx * L;
+        float *rop = s->rope + (size_t)l * s->ctx * R;
+        /* attention block, moonlight_metal.m:287-440 */
+        orc_rmsnorm(x, ly->attn_norm, rows, D, c->rms_norm_epsilon, xn);
+        if (c->q_lora_rank > 0) {
+            mat_apply(&ly->q_a, xn, rows, qa);
+            orc_rmsnorm(qa, ly->q_a_norm, rows, c->q_lora_rank, c->rms_norm_epsilon, qa);
+            mat_apply(&ly->q_b, qa, rows, q);
+        } else {
+            mat_apply(&ly->q_proj, xn, rows, q);
+        }
+        mat_apply(&ly->kv_a, xn, rows, ckv);
+        for (int r = 0; r < rows; ++r) {
+            /* cache_append: RMSNorm latent, RoPE rope part (:132-170) */
+            float *src = ckv + (int64_t)r * (L + R);
+            float *dl = lat + (int64_t)(pos + r) * L;
+            orc_rmsnorm(src, ly->kv_a_norm, 1, L, c->rms_norm_epsilon, dl);
+            orc_rope(src + L, rop + (int64_t)(pos + r) * R, R, pos + r, c->rope_theta);
+            for (int i = 0; i < L; ++i) dl[i] = round_kv(s, dl[i]);
+            for (int i = 0; i < R; ++i) rop[(int64_t)(pos + r) * R + i] = round_kv(s, rop[(int64_t)(pos + r) * R + i]);
+            /* rope_query (:172-200) */
+            for (int h = 0; h < H; ++h) {
+                float *qh = q + ((int64_t)r * H + h) * QW;
+                orc_rope(qh + NP, qh + NP, R, pos + r, c->rope_theta);
+            }
+        }
+        for (int r = 0; r < rows; ++r) {
+            int keys = pos + r + 1;
+#pragma omp parallel for schedule(dynamic)
+            for (int h = 0; h < H; ++h) {
+                const float *qh = q + ((int64_t)r * H + h) * QW;
+                float *work = alloc_f((size_t)3 * L + 2 * R + (size_t)keys);
+                float *qabs = work, *qr = work + L, *ctxl = work + L + R, *sc = work + 2 * L + R;
+                /* absorb_query (:218-245): q_abs = q_nope . W_UK[h] */
+                for (int i = 0; i < L; ++i) qabs[i] = 0.0f;
+                const Mat *kb = &ly->kv_b;
+                for (int n = 0; n < NP; ++n) {
+                    int row = h * (NP + VD) + n;
+                    for (int i = 0; i < L; ++i) {
+                        float w = kb->fmt == FC_FMT_F32 ? kb->f32[(int64_t)row * L + i]
+                            : value_of(kb->fmt, kb->values[(int64_t)row * L + i]) *
+                              kb->scales[(int64_t)row * (L / 32) + i / 32];
+                        qabs[i] += qh[n] * w;
+                    }
+                }
+                for (int i = 0; i < L; ++i) qabs[i] = round_kv(s, qabs[i]);
+                for (int i = 0; i < R; ++i) qr[i] = round_kv(s, qh[NP + i]);
+                /* scores + softmax + latent context (:247-343) */
+                float mx = -INFINITY;
+                for (int key = 0; key < keys; ++key) {
+                    const float *cl = lat + (int64_t)key * L, *cr = rop + (int64_t)key * R;
+                    float a = 0.0f;
+                    for (int i = 0; i < L; ++i) a += qabs[i] * cl[i];
+                    for (int i = 0; i < R; ++i) a += qr[i] * cr[i];
+                    sc[key] = a * scale;
+                    if (sc[key] > mx) mx = sc[key];
+                }
+                float den = 0.0f;
+                for (int key = 0; key < keys; ++key) den += expf(sc[key] - mx);
+                for (int i = 0; i < L; ++i) ctxl[i] = 0.0f;
+                for (int key = 0; key < keys; ++key) {
+                    float p = expf(sc[key] - mx) / den;
+                    const float *cl = lat + (int64_t)key * L;
+                    for (int i = 0; i < L; ++i) ctxl[i] += p * cl[i];
+                }
+                /* decode_value (:345-375): o = ctx_L . W_UV[h] */
+                for (int v = 0; v < VD; ++v) {
+                    int row = h * (NP + VD) + NP + v;
+                    float a = 0.0f;
+                    for (int i = 0; i < L; ++i) {
+                        float w = kb->fmt == FC_FMT_F32 ? kb->f32[(int64_t)row * L + i]
+                            : value_of(kb->fmt, kb->values[(int64_t)row * L + i]) *
+                              kb->scales[(int64_t)row * (L / 32) + i / 32];
+                        a += ctxl[i] * w;
+                    }
+                    attn[((int64_t)r * H + h) * VD + v] = a;
+                }
+                free(work);
+            }
+        }
+        mat_apply(&ly->o_proj, attn, rows, ao);
+        for (size_t i = 0; i < (size_t)rows * D; ++i) x[i] += ao[i];
+
+        /* FFN block */
+        orc_rmsnorm(x, ly->ffn_norm, rows, D, c->rms_norm_epsilon, xn);
+        for (int r = 0; r < rows; ++r) {
+            const float *xr = xn + (int64_t)r * D;
+            for (int d = 0; d < D; ++d) y[d] = 0.0f;
+            if (ly->dense) { /* encode_dense_residual_buffer, moonlight_metal.m:442-483 */
+                add_expert(&ly->d_gate, &ly->d_up, &ly->d_down, xr, 1.0f, 0.0f, y, tmp);
+                if (routes)
+                    for (int k = 0; k < c->experts_per_token; ++k)
+                        routes[((int64_t)l * rows + r) * c->experts_per_token + k] = -1;
+            } else { /* moe_f32_forward, moe_exec.h:65-114 */
+                int E = c->expert_count, K = c->experts_per_token;
+                float *lg = tmp + 4 * maxI;
+                int idx[64], order[64];
+                float wt[64];
+                mat_apply(&ly->router, xr, 1, lg);
+                const int *fixed = ly->hash ? ly->hash + (int64_t)ids[r] * K : NULL;
+                if (orc_route(lg, ly->bias, E, K, c->score_fn, c->normalize_topk,
+                              c->routed_scale, fixed, idx, wt) != K) goto fail;
+                if (routes)
+                    for (int k = 0; k < K; ++k)
+                        routes[((int64_t)l * rows + r) * K + k] = idx[k];
+                for (int k = 0; k < K; ++k) order[k] = k;
+                for (int a = 1; a < K; ++a) {
+                    int v = order[a], b = a - 1;
+                    while (b >= 0 && idx[order[b]] > idx[v]) { order[b + 1] = order[b]; b--; }
+                    order[b + 1] = v;
+                }
+                for (int k = 0; k < K; ++k) {
+                    int e = idx[order[k]];
+                    add_expert(&ly->gate[e], &ly->up[e], &ly->down[e], xr, wt[order[k]],
+                               c->swiglu_limit, y, tmp);
+                }
+                if (c->shared_expert_count > 0)
+                    add_expert(&ly->sh_gate, &ly->sh_up, &ly->sh_down, xr, 1.0f,
+                               c->swiglu_limit, y, tmp);
+            }
+            for (int d = 0; d < D; ++d) x[(int64_t)r * D + d] += y[d];
+        }
+        if (layer_out) memcpy(layer_out + (size_t)l * rows * D, x, (size_t)rows * D * sizeof(float));
+    }
+    if (logits) {
+        orc_rmsnorm(x, m->final_norm, rows, D, c->rms_norm_epsilon, xn);
+        mat_apply(&m->lm_head, xn, rows, logits);
+    }
+    s->position = pos + rows;
+    free(x); free(xn); free(q); free(qa); free(ckv); free(attn); free(tmp); free(y); free(ao);
+    return 1;
+fail:
+    free(x); free(xn); free(q); free(qa); free(ckv); free(attn); free(tmp); free(y); free(ao);
+    return 0;
+}
+
+int orc_session_copy_kv(const OrcSession *s, int layer, float *latent, float *rope,
+                        int capacity) {
+    const FcModelConfig *c = &s->m->c;
+    if (layer < 0 || layer >= c->layer_count || capacity < s->position) return 0;
+    int L = c->kv_lora_rank, R = c->qk_rope_dim;
+    if (latent) memcpy(latent, s->latent + (size_t)layer * s->ctx * L, (size_t)s->position * L * 4);
+    if (rope) memcpy(rope, s->rope + (size_t)layer * s->ctx * R, (size_t)s->position * R * 4);
+    return 1;
+}
+
+int orc_session_verify(OrcSession *s, const int *ids, int k, const FcAcceptConfig *accept,
+                       int *emitted, int *n_emitted, int *next_token, float *row_logits,
+                       int *row_tops) {
+    int V = s->m->c.vocab_size, rows = k + 1, start = s->position;
+    float *logits = row_logits ? row_logits : alloc_f((size_t)rows * V);
+    int tops[64];
+    if (k < 0 || rows > 64) return 0;
+    if (!orc_session_forward(s, ids, rows, logits, NULL, NULL)) {
+        if (!row_logits) free(logits);
+        return 0;
+    }
+    for (int r = 0; r < rows; ++r) tops[r] = orc_argmax(logits + (int64_t)r * V, V);
+    if (row_tops) memcpy(row_tops, tops, (size_t)rows * sizeof(int));
+    int commit, next;
+    if (accept && accept->mode == FC_ACCEPT_SAMPLE) {
+        commit = orc_accept_sample(logits, V, ids, k, accept->temperature, accept->seed,
+                                   accept->counter, &next);
+    } else {
+        commit = orc_accept_greedy(tops, ids, k);
+        next = tops[commit - 1];
+    }
+    for (int i = 0; i < commit; ++i) emitted[i] = ids[i];
+    *n_emitted = commit;
+    *next_token = next;
+    s->position = start + commit; /* rollback: the MLA cache is append-only */
+    if (!row_logits) free(logits);
+    return 1;
+}

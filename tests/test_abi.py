@@ -1,0 +1,81 @@
+"""The C-ABI library loads and exports every function include/*.h declares;
+without a GPU every entry point fails cleanly with an error message (no CPU
+fallback, no crash)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_functions():
+    names = set()
+    for h in os.listdir(os.path.join(ROOT, "include")):
+        if not h.endswith(".h"):
+            continue
+        text = open(os.path.join(ROOT, "include", h)).read()
+        text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+        text = re.sub(r"//[^\n]*", "", text)
+        for m in re.finditer(r"\b(fc_[a-z0-9_]+)\s*\(", text):
+            names.add(m.group(1))
+    # static inline helpers of floyd_synth.h are not exported
+    return {n for n in names if not n.startswith("fc_synth") and n not in
+            ("fc_tensor_id", "fc_mulhilo32", "fc_philox4x32_10")}
+
+
+def test_library_exports_every_declared_symbol():
+    import floyd_b200
+    lib = floyd_b200.lib()
+    missing = [n for n in sorted(declared_functions()) if not hasattr(lib, n)]
+    assert not missing, missing
+    assert set(floyd_b200._lib.SIGNATURES) == declared_functions()
+
+
+def test_library_is_built_for_sm100a_only():
+    import floyd_b200
+    from floyd_b200 import build
+    text = open(build.__file__).read()
+    assert "arch=compute_100a,code=sm_100a" in text
+    assert os.path.exists(floyd_b200._lib.LIB_PATH)
+
+
+@pytest.mark.skipif(os.environ.get("CUDA_VISIBLE_DEVICES", None) is None and
+                    os.path.exists("/dev/nvidia0"), reason="a GPU is present")
+def test_without_gpu_model_creation_fails_cleanly():
+    import floyd_b200
+    from floyd_b200 import CONFIGS
+    try:
+        import torch
+        if torch.cuda.is_available():
+            pytest.skip("a GPU is present")
+    except ImportError:
+        pass
+    with pytest.raises(floyd_b200.FloydError) as exc:
+        floyd_b200.Model(CONFIGS["c1_tiny"])
+    assert "CUDA" in str(exc.value) or "device" in str(exc.value)
+
+
+def test_invalid_configs_are_rejected_before_allocation():
+    import floyd_b200
+    from floyd_b200 import CONFIGS, scaled
+    bad = scaled(CONFIGS["c1_tiny"], hidden_size=1000)
+    with pytest.raises(floyd_b200.FloydError) as exc:
+        floyd_b200.Model(bad)
+    assert "multiple of 32" in str(exc.value)
+    bad = scaled(CONFIGS["c1_tiny"], kv_lora_rank=384)
+    with pytest.raises(floyd_b200.FloydError):
+        floyd_b200.Model(bad)
+
+
+def test_host_entry_points_reject_null_arguments():
+    import floyd_b200
+    lib = floyd_b200.lib()
+    err = ctypes.create_string_buffer(128)
+    assert lib.fc_model_create(None, None, 0, err, len(err)) == 0
+    assert lib.fc_session_create(None, None, None, err, len(err)) == 0
+    assert lib.fc_session_position(None) == 0
+    assert lib.fc_runtime_argmax(None, 10) == -1
+    lib.fc_model_close(None)
+    lib.fc_session_destroy(None)
