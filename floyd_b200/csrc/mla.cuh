@@ -137,29 +137,36 @@ __global__ void mla_prep_kernel(const float *ckv, const float *q, const float *n
 // ---------------------------------------------------------------------------
 // Query absorption (moonlight_kernels.metal:218-245):
 //   qcat[s*H+h][l] = fp16( sum_n q[s][h][n] * W_kvb[h*(nope+v)+n][l] )
-// One thread per (h, l), all rows; sequential sum over n in fp32 without
-// contraction (the oracle's order).
+// grid (H, L/64), 256 threads: the W_UK block [nope][64] is dequantized into
+// shared memory with all loads in flight, then each output sums over n in
+// fp32 sequentially without contraction (the oracle's order).
 // ---------------------------------------------------------------------------
-__global__ void mla_absorb_kernel(int fmt, const uint8_t *w, const void *sc, int kp,
-                                  const float *q, int S, int H, int nope, int vdim, int R,
-                                  int L, __half *qcat) {
-    int h = blockIdx.x;
-    int l = blockIdx.y * blockDim.x + threadIdx.x;
-    if (l >= L) return;
-    float acc[8];
-#pragma unroll
-    for (int s = 0; s < 8; ++s) acc[s] = 0.0f;
-    int qw = nope + R;
-    for (int n = 0; n < nope; ++n) {
-        size_t row = (size_t)h * (nope + vdim) + n;
-        float wv = dequant_element(fmt, w, sc, kp, row, l);
-#pragma unroll
-        for (int s = 0; s < 8; ++s)
-            if (s < S) acc[s] = __fadd_rn(acc[s], __fmul_rn(q[((size_t)s * H + h) * qw + n], wv));
+constexpr int kAbsorbCols = 64;
+constexpr int kAbsorbMaxNope = 128;
+
+__global__ void __launch_bounds__(256) mla_absorb_kernel(int fmt, const uint8_t *w, const void *sc,
+                                                         int kp, const float *q, int S, int H,
+                                                         int nope, int vdim, int R, int L,
+                                                         __half *qcat) {
+    __shared__ float wsm[kAbsorbMaxNope][kAbsorbCols + 1];
+    __shared__ float qs[8][kAbsorbMaxNope];
+    const int h = blockIdx.x, l0 = blockIdx.y * kAbsorbCols;
+    const int qw = nope + R;
+    for (int i = threadIdx.x; i < S * nope; i += blockDim.x) {
+        int s = i / nope, n = i % nope;
+        qs[s][n] = q[((size_t)s * H + h) * qw + n];
     }
-#pragma unroll
-    for (int s = 0; s < 8; ++s)
-        if (s < S) qcat[((size_t)s * H + h) * (L + R) + l] = __float2half_rn(acc[s]);
+    for (int i = threadIdx.x; i < nope * kAbsorbCols; i += blockDim.x) {
+        int n = i / kAbsorbCols, c = i % kAbsorbCols;
+        wsm[n][c] = dequant_element(fmt, w, sc, kp, (size_t)h * (nope + vdim) + n, l0 + c);
+    }
+    __syncthreads();
+    for (int o = threadIdx.x; o < S * kAbsorbCols; o += blockDim.x) {
+        int s = o / kAbsorbCols, c = o % kAbsorbCols;
+        float acc = 0.0f;
+        for (int n = 0; n < nope; ++n) acc = __fadd_rn(acc, __fmul_rn(qs[s][n], wsm[n][c]));
+        qcat[((size_t)s * H + h) * (L + R) + l0 + c] = __float2half_rn(acc);
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -427,27 +434,49 @@ mla_attention_kernel(const __half *cache, const __half *qcat, int S, int H, int 
 
 // Combines the split partials in split order and writes the latent context of
 // each (row s, head h) in xq format at ctx_xq + h * head_stride + s * L * 2.
-__global__ void mla_combine_kernel(const float *part_o, const float *part_m, const float *part_l,
-                                   int splits, int S, int H, int L, __half *ctx_xq,
-                                   size_t head_stride) {
-    int q = blockIdx.x;
-    int nq = S * H;
-    float M = -INFINITY;
-    for (int i = 0; i < splits; ++i) M = fmaxf(M, part_m[(size_t)i * nq + q]);
+// grid (S*H, L/128), 128 threads.  Splits with no visible key (m = -inf)
+// contribute nothing, so a verify row and a decode of the same token see the
+// same sequence of terms.
+constexpr int kCombineThreads = 128;
+constexpr int kMaxSplits = 1024;
+
+__global__ void __launch_bounds__(kCombineThreads)
+mla_combine_kernel(const float *part_o, const float *part_m, const float *part_l, int splits, int S,
+                   int H, int L, __half *ctx_xq, size_t head_stride) {
+    __shared__ float wts[kMaxSplits];
+    __shared__ float red[kCombineThreads / 32];
+    const int q = blockIdx.x, nq = S * H;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    float m = -INFINITY;
+    for (int i = threadIdx.x; i < splits; i += kCombineThreads) m = fmaxf(m, part_m[(size_t)i * nq + q]);
+    m = warp_max(m);
+    if (lane == 0) red[warp] = m;
+    __syncthreads();
+    float M = red[0];
+    for (int w = 1; w < kCombineThreads / 32; ++w) M = fmaxf(M, red[w]);
+    __syncthreads();
     float den = 0.0f;
+    for (int i = threadIdx.x; i < splits; i += kCombineThreads) {
+        float mi = part_m[(size_t)i * nq + q];
+        float wi = mi == -INFINITY ? 0.0f : expf(mi - M);
+        wts[i] = wi;
+        if (wi != 0.0f) den += wi * part_l[(size_t)i * nq + q];
+    }
+    den = warp_sum(den);
+    if (lane == 0) red[warp] = den;
+    __syncthreads();
+    den = 0.0f;
+    for (int w = 0; w < kCombineThreads / 32; ++w) den += red[w];
+    const int l = blockIdx.y * kCombineThreads + threadIdx.x;
+    if (l >= L) return;
+    float acc = 0.0f;
+#pragma unroll 4
     for (int i = 0; i < splits; ++i) {
-        float m = part_m[(size_t)i * nq + q];
-        if (m != -INFINITY) den += expf(m - M) * part_l[(size_t)i * nq + q];
+        float wi = wts[i];
+        if (wi != 0.0f) acc += wi * part_o[((size_t)i * nq + q) * L + l];
     }
-    int s = q / H, h = q % H;
-    for (int l = threadIdx.x; l < L; l += blockDim.x) {
-        float acc = 0.0f;
-        for (int i = 0; i < splits; ++i) {
-            float m = part_m[(size_t)i * nq + q];
-            if (m != -INFINITY) acc += expf(m - M) * part_o[((size_t)i * nq + q) * L + l];
-        }
-        store_xq(ctx_xq + (size_t)h * head_stride, L, s, l, acc / den);
-    }
+    const int s = q / H, h = q % H;
+    store_xq(ctx_xq + (size_t)h * head_stride, L, s, l, acc / den);
 }
 
 }  // namespace fc

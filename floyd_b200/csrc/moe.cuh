@@ -19,18 +19,19 @@
 
 namespace fc {
 
-// Router logits, fp32 weights [E][D]: one warp per expert row, float4 loads,
-// S <= 8 accumulators, fixed lane order then a fixed butterfly.
-__global__ void router_logits_kernel(const float *W, const float *x, int E, int D, int S,
-                                     float *logits) {
-    int e = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    int lane = threadIdx.x & 31;
-    if (e >= E) return;
+// Router logits, fp32 weights [E][D]: one block per expert row, the 256
+// threads split D (float4 loads), per-row partial sums reduced in a fixed
+// order (warp butterfly, then warps in index order).
+__global__ void __launch_bounds__(256) router_logits_kernel(const float *W, const float *x, int E,
+                                                            int D, int S, float *logits) {
+    __shared__ float red[8][8];
+    const int e = blockIdx.x;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     float acc[8];
 #pragma unroll
     for (int s = 0; s < 8; ++s) acc[s] = 0.0f;
     const float4 *w4 = reinterpret_cast<const float4 *>(W + (size_t)e * D);
-    for (int k4 = lane; k4 < D / 4; k4 += 32) {
+    for (int k4 = threadIdx.x; k4 < D / 4; k4 += blockDim.x) {
         float4 w = __ldg(w4 + k4);
 #pragma unroll
         for (int s = 0; s < 8; ++s) {
@@ -46,7 +47,13 @@ __global__ void router_logits_kernel(const float *W, const float *x, int E, int 
 #pragma unroll
     for (int s = 0; s < 8; ++s) {
         float v = warp_sum(acc[s]);
-        if (lane == 0 && s < S) logits[(size_t)s * E + e] = v;
+        if (lane == 0) red[warp][s] = v;
+    }
+    __syncthreads();
+    if (threadIdx.x < S) {
+        float t = 0.0f;
+        for (int w = 0; w < 8; ++w) t += red[w][threadIdx.x];
+        logits[(size_t)threadIdx.x * E + e] = t;
     }
 }
 
@@ -88,9 +95,12 @@ __global__ void route_select_kernel(const float *logits, RouteParams p) {
     float *choice = rs_smem + 8 * E;
     int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int e = threadIdx.x; e < E; e += blockDim.x) used_flag[e] = 0;
+    // stage the logits in shared memory (choice[] doubles as the staging area)
+    for (int i = threadIdx.x; i < p.S * E; i += blockDim.x) choice[i] = logits[i];
+    __syncthreads();
     if (warp < p.S) {
         int s = warp;
-        const float *lg = logits + (size_t)s * E;
+        float *lg = choice + s * E;
         float *sc = scores + s * E;
         float *ch = choice + s * E;
         if (p.score_fn == FC_SCORE_SOFTMAX) {
@@ -107,6 +117,7 @@ __global__ void route_select_kernel(const float *logits, RouteParams p) {
             for (int e = lane; e < E; e += 32) sc[e] = route_score(lg[e], p.score_fn);
             __syncwarp();
         }
+        __syncwarp();
         for (int e = lane; e < E; e += 32) ch[e] = sc[e] + (p.bias ? p.bias[e] : 0.0f);
         __syncwarp();
         if (p.hash) {

@@ -528,8 +528,8 @@ cudaError_t record_forward(FcSession *s, int S) {
                                            c.rms_norm_epsilon, c.rope_theta, d_pos, cache, s->qcat);
         mark(s, "mla_prep");
         {
-            dim3 grid(H, (L + 127) / 128);
-            mla_absorb_kernel<<<grid, 128, 0, st>>>(df, y.kv_b.w, y.kv_b.sc, y.kv_b.kp, s->q, S, H,
+            dim3 grid(H, L / kAbsorbCols);
+            mla_absorb_kernel<<<grid, 256, 0, st>>>(df, y.kv_b.w, y.kv_b.sc, y.kv_b.kp, s->q, S, H,
                                                     NP, VD, R, L, s->qcat);
             mark(s, "mla_absorb");
         }
@@ -546,8 +546,9 @@ cudaError_t record_forward(FcSession *s, int S) {
             FC_TRY(cudaGetLastError());
             mark(s, "mla_attention");
             size_t head_stride = (size_t)mb * kpL * 2;
-            mla_combine_kernel<<<S * H, 128, 0, st>>>(s->part_o, s->part_m, s->part_l, s->splits, S,
-                                                      H, L, s->ctx_xq, head_stride);
+            mla_combine_kernel<<<dim3(S * H, (L + kCombineThreads - 1) / kCombineThreads),
+                                 kCombineThreads, 0, st>>>(s->part_o, s->part_m, s->part_l,
+                                                           s->splits, S, H, L, s->ctx_xq, head_stride);
             mark(s, "mla_combine");
             // W_UV: rows nope .. nope+v of each head's kv_b block (decode_value, :345-375)
             GemvSeg g = seg_of(y.kv_b, s->ctx_xq, EPI_STORE_XQ);
@@ -593,8 +594,7 @@ cudaError_t record_forward(FcSession *s, int S) {
             mark(s, "gemv_dense_down");
         } else {
             int E = c.expert_count, K = c.experts_per_token;
-            router_logits_kernel<<<(E + 7) / 8, 256, 0, st>>>(y.router.p, s->xn, E, D, S,
-                                                             s->router_logits);
+            router_logits_kernel<<<E, 256, 0, st>>>(y.router.p, s->xn, E, D, S, s->router_logits);
             mark(s, "router_logits");
             RouteParams rp{};
             rp.E = E; rp.K = K; rp.S = S;

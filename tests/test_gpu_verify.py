@@ -221,17 +221,18 @@ def test_sampling_decisions_match_oracle(oracle_lib):
     assert agree == 24
 
 
-def test_sampled_drafts_that_match_are_often_accepted():
-    """Drafts equal to the target's greedy token have p(x) near the top of the
-    distribution; at temperature 0.7 most are accepted."""
+def test_low_temperature_sampling_accepts_greedy_drafts():
+    """As the temperature goes to 0 the target distribution collapses onto the
+    greedy token, so drafts equal to the greedy stream are accepted and the
+    bonus token is the next greedy token.  (With random weights the logits
+    are nearly flat, so at temperature 0.7 a planted greedy draft is accepted
+    with probability p(x) of a few 1e-3.)"""
     cfg, name = C1, "c1"
     stream = greedy_stream(cfg, name, 42, 4)
-    accepted = 0
-    for counter in range(16):
+    for counter in range(4):
         s, _ = sessions(cfg, name)
-        em, nxt, _ = s.verify(stream[0:4], mode=ACCEPT_SAMPLE, temperature=0.7, seed=1, counter=counter)
-        accepted += len(em) - 1
-    assert accepted > 0
+        em, nxt, _ = s.verify(stream[0:4], mode=ACCEPT_SAMPLE, temperature=1e-3, seed=1, counter=counter)
+        assert em == stream[0:4] and nxt == stream[4]
 
 
 def test_zero_draft_verify_equals_decode():
