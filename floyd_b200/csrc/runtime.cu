@@ -353,10 +353,10 @@ int grid_for(size_t n) { return (int)std::min<size_t>((n + 255) / 256, 148 * 16)
 cudaError_t fill_mat(const DevMat &mm, uint64_t seed, cudaStream_t st) {
     if (!mm.count) return cudaSuccess;
     if (mm.fmt == FC_FMT_F32) return cudaSuccess;
-    size_t nb = mm.w_bytes * mm.count;
+    size_t nb = (size_t)mm.O * mm.K / (mm.fmt == FC_FMT_Q8 ? 8 : 32) * mm.count;
     synth_values_kernel<<<grid_for(nb), 256, 0, st>>>(mm.fmt, mm.w, mm.O, mm.K, mm.kp, mm.count,
                                                       seed, mm.tid, mm.slot0);
-    size_t ns = mm.sc_elems * mm.count;
+    size_t ns = ((size_t)mm.O * (mm.K / 32) + 3) / 4 * mm.count;
     synth_scales_kernel<<<grid_for(ns), 256, 0, st>>>(mm.fmt, mm.sc, mm.O, mm.K, mm.kp, mm.count,
                                                       seed, mm.tid, mm.slot0);
     return cudaGetLastError();

@@ -21,57 +21,90 @@ __host__ __device__ inline int logical_column(int fmt, int c, int b, int nib) {
 }
 
 // Fills `count` matrices (rows O, logical K, padded kp) of a family with the
-// synthetic values of tensors tid0 + slot (slot = member + slot0).
+// synthetic values of tensors tid_base | (member + slot0).  One thread per
+// Philox block: 8 int8 values or 32 nibbles of consecutive logical elements
+// (a block never crosses a row since K % 32 == 0), scattered to their
+// permuted device positions.  Both nibbles of a device byte come from the
+// same block, so no two threads write one byte.  Padded columns are not
+// written (the activations there are zero).
 __global__ void synth_values_kernel(int fmt, uint8_t *w, int O, int K, int kp, int count,
                                     uint64_t seed, uint32_t tid_base, int slot0) {
-    size_t rb = (size_t)row_bytes(fmt, kp);
-    size_t per = (size_t)O * rb;
-    size_t total = per * count;
+    const int per_block = fmt == FC_FMT_Q8 ? 8 : 32;
+    const size_t rb = (size_t)row_bytes(fmt, kp);
+    const size_t blocks_per_member = (size_t)O * K / per_block;
+    const size_t total = blocks_per_member * count;
     for (size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
          idx += (size_t)gridDim.x * blockDim.x) {
-        int member = (int)(idx / per);
-        size_t in = idx % per;
-        int o = (int)(in / rb);
-        int byte = (int)(in % rb);
-        int c = byte >> 6, b = byte & 63;
+        int member = (int)(idx / blocks_per_member);
+        size_t blk = idx % blocks_per_member;
         uint32_t tid = tid_base | (uint32_t)(member + slot0);
-        uint8_t out;
+        uint32_t words[4];
+        fc_synth_block(seed, tid, FC_STREAM_VALUES, blk, words);
+        size_t e0 = blk * per_block;
+        int o = (int)(e0 / K), k0 = (int)(e0 % K);
+        uint8_t *row = w + (size_t)member * O * rb + (size_t)o * rb;
         if (fmt == FC_FMT_Q8) {
-            int k = logical_column(fmt, c, b, 0);
-            int v = k < K ? fc_synth_q8(seed, tid, (uint64_t)o * K + k) : 0;
-            out = (uint8_t)(int8_t)v;
-        } else {
-            uint32_t nib[2];
-            for (int n = 0; n < 2; ++n) {
-                int k = logical_column(fmt, c, b, n);
-                if (k < K) nib[n] = (uint32_t)fc_synth_nibble(seed, tid, (uint64_t)o * K + k);
-                else nib[n] = fmt == FC_FMT_Q4 ? 8u : 0u;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                int v = ((int)fc_synth_byte(words, 2 * i) + (int)fc_synth_byte(words, 2 * i + 1) - 255) / 2;
+                int byte, nib;
+                weight_position(fmt, k0 + i, byte, nib);
+                row[byte] = (uint8_t)(int8_t)v;
             }
-            out = (uint8_t)(nib[0] | (nib[1] << 4));
+        } else {
+            // gather the 16 device bytes this block covers: byte -> two nibbles
+#pragma unroll 4
+            for (int i = 0; i < 32; i += 2) {
+                int byte, nib0, byte1, nib1;
+                weight_position(fmt, k0 + i, byte, nib0);
+                weight_position(fmt, k0 + i + 1, byte1, nib1);
+                uint32_t c0 = (words[i >> 3] >> (4 * (i & 7))) & 0xFu;
+                uint32_t c1 = (words[(i + 1) >> 3] >> (4 * ((i + 1) & 7))) & 0xFu;
+                if (byte == byte1) {
+                    row[byte] = (uint8_t)((c0 << (4 * nib0)) | (c1 << (4 * nib1)));
+                } else {
+                    // elements k, k+1 live in different bytes; their partner
+                    // nibbles are elements k+2 / k+3 (same block)
+                    int byte2, nib2, byte3, nib3;
+                    weight_position(fmt, k0 + i + 2, byte2, nib2);
+                    weight_position(fmt, k0 + i + 3, byte3, nib3);
+                    uint32_t c2 = (words[(i + 2) >> 3] >> (4 * ((i + 2) & 7))) & 0xFu;
+                    uint32_t c3 = (words[(i + 3) >> 3] >> (4 * ((i + 3) & 7))) & 0xFu;
+                    row[byte] = (uint8_t)((c0 << (4 * nib0)) | (c2 << (4 * nib2)));
+                    row[byte1] = (uint8_t)((c1 << (4 * nib1)) | (c3 << (4 * nib3)));
+                    i += 2;
+                }
+            }
         }
-        w[idx] = out;
     }
 }
 
+// Group scales: one thread per Philox block of 4 scales.
 __global__ void synth_scales_kernel(int fmt, void *sc, int O, int K, int kp, int count,
                                     uint64_t seed, uint32_t tid_base, int slot0) {
-    int gk = K / 32, gp = kp / 32;
-    size_t per = (size_t)O * gp;
-    size_t total = per * count;
+    const int gk = K / 32, gp = kp / 32;
+    const size_t groups = (size_t)O * gk;
+    const size_t blocks_per_member = (groups + 3) / 4;
+    const size_t total = blocks_per_member * count;
     for (size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
          idx += (size_t)gridDim.x * blockDim.x) {
-        int member = (int)(idx / per);
-        size_t in = idx % per;
-        int o = (int)(in / gp), g = (int)(in % gp);
+        int member = (int)(idx / blocks_per_member);
+        size_t blk = idx % blocks_per_member;
         uint32_t tid = tid_base | (uint32_t)(member + slot0);
-        uint64_t lg = (uint64_t)o * gk + g;
-        if (fmt == FC_FMT_MXFP4) {
-            reinterpret_cast<uint8_t *>(sc)[idx] = g < gk ? fc_synth_scale_e8m0(seed, tid, lg) : 0;
-        } else {
-            uint16_t bits = 0;
-            if (g < gk) bits = fmt == FC_FMT_Q8 ? fc_synth_scale_q8(seed, tid, lg)
-                                                : fc_synth_scale_q4(seed, tid, lg);
-            reinterpret_cast<uint16_t *>(sc)[idx] = bits;
+        uint32_t words[4];
+        fc_synth_block(seed, tid, FC_STREAM_SCALES, blk, words);
+        for (int i = 0; i < 4; ++i) {
+            size_t lg = blk * 4 + i;
+            if (lg >= groups) break;
+            size_t o = lg / gk, g = lg % gk;
+            size_t dst = (size_t)member * O * gp + o * gp + g;
+            uint32_t wd = words[i];
+            if (fmt == FC_FMT_MXFP4)
+                reinterpret_cast<uint8_t *>(sc)[dst] = (uint8_t)(119u + (wd & 1u));
+            else if (fmt == FC_FMT_Q8)
+                reinterpret_cast<uint16_t *>(sc)[dst] = (uint16_t)((3u << 10) | (wd & 0x3FFu));
+            else
+                reinterpret_cast<uint16_t *>(sc)[dst] = (uint16_t)((7u << 10) | (wd & 0x3FFu));
         }
     }
 }
