@@ -382,7 +382,7 @@ def run_ours(args, d):
         "mean_commit": total_emitted / (args.steps * d.world),
         "acceptance_mismatches": int(d.sum(mismatches)),
         "roofline": roof,
-        "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 72, "d2h_bytes_per_step": 40,
+        "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 72, "d2h_bytes_per_step": 48,
                 "note": "fc_session_verify wall time with host id / result buffers"},
         "gpu_launches": None,
         "kernels": {k: {"ms": v[0], "launches": v[1]} for k, v in prof.items()},

@@ -128,42 +128,132 @@ __device__ __forceinline__ float warp_max(float v) {
 
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + expf(-x)); }
 
-// Chunk geometry of the device weight layout: every row is a sequence of
-// 64-byte chunks; a q8 chunk covers 64 columns (4 MMAs), a q4 / MXFP4 chunk
-// 128 columns (8 MMAs).  Rows are zero-padded to a whole number of chunks.
+// ---------------------------------------------------------------------------
+// Device weight layout of a quantized matrix [O][K] ("tile-major"):
+//   - rows are grouped in 16-row tiles (O padded up to a multiple of 16);
+//   - K is cut in chunks of chunk_cols columns (64 for Q8, 128 for Q4 /
+//     MXFP4), i.e. 64 bytes of values per row and chunk (K padded up to a
+//     whole number of 128 columns);
+//   - a tile is a sequence of chunk blocks, and a chunk block is
+//       [16 rows x 64 value bytes][16 rows x scale_row_bytes group scales]
+//     so one tile is contiguous and one block is what a warp consumes for
+//     one chunk (1088 / 1152 bytes, a multiple of 16 for bulk copies);
+//   - inside a row's 64 value bytes the columns are permuted so that the
+//     16 bytes thread j of a warp loads feed whole m16n8k16 MMAs and every
+//     MMA covers a single 32-column scale group:
+//       q8:   column r (0..63): MMA i = r/16, thread j = (r%16)/4, b = r%4
+//             byte = 16j + 4i + b
+//       q4 / e2m1: column r (0..127): MMA i = r/16, j = (r%16)/4, b = r%4,
+//             h = b/2, e = b%2; register q = 2i + h; word = q/4;
+//             nibble slot = q%4 + 4e; byte = 16j + 4*word + slot/2,
+//             nibble = slot%2
+// ---------------------------------------------------------------------------
+constexpr int kTileRows = 16;
+constexpr int kBlockValueBytes = kTileRows * 64;
+
 __host__ __device__ constexpr int chunk_cols(int fmt) { return fmt == FC_FMT_Q8 ? 64 : 128; }
-__host__ __device__ constexpr int row_bytes(int fmt, int kp) {
-    return fmt == FC_FMT_Q8 ? kp : kp / 2;
+__host__ __device__ constexpr int groups_per_chunk(int fmt) { return fmt == FC_FMT_Q8 ? 2 : 4; }
+__host__ __device__ constexpr int scale_elem_bytes(int fmt) { return fmt == FC_FMT_MXFP4 ? 1 : 2; }
+__host__ __device__ constexpr int scale_row_bytes(int fmt) {
+    return groups_per_chunk(fmt) * scale_elem_bytes(fmt);
 }
-__host__ __device__ inline int pad_cols(int fmt, int k) {
-    int c = fmt == FC_FMT_F32 ? 1 : chunk_cols(fmt);
-    return (k + c - 1) / c * c;
+__host__ __device__ constexpr int block_bytes(int fmt) {
+    return kBlockValueBytes + kTileRows * scale_row_bytes(fmt);
+}
+__host__ __device__ inline int pad_cols(int k) { return (k + 127) / 128 * 128; }
+__host__ __device__ inline int chunk_count(int fmt, int kp) { return kp / chunk_cols(fmt); }
+__host__ __device__ inline size_t tile_bytes(int fmt, int kp) {
+    return (size_t)chunk_count(fmt, kp) * block_bytes(fmt);
+}
+__host__ __device__ inline size_t matrix_bytes(int fmt, int O, int kp) {
+    return (size_t)((O + kTileRows - 1) / kTileRows) * tile_bytes(fmt, kp);
 }
 
-// Byte offset inside a row (values) for logical column k of a quantized row,
-// and for q4 / e2m1 the nibble position (0 = low).  Inverse of the MMA
-// fragment mapping used by the GEMV kernel:
-//   q8:  chunk c = k/64, r = k%64, MMA i = r/16, thread j = (r%16)/4, b = r%4
-//        byte = 64c + 16j + 4i + b
-//   q4 / e2m1: chunk c = k/128, r = k%128, MMA i = r/16, j = (r%16)/4,
-//        b = r%4, h = b/2, e = b%2; register q = 2i + h, word = q/4,
-//        q4:   nibble slot s = q%4 + 4e (bit 4s of the word)
-//        e2m1: nibble slot p = q%4 + 4e (bit 4p of the word)
-//        byte = 64c + 16j + 4*word + slot/2, nibble = slot%2
-__host__ __device__ inline void weight_position(int fmt, int k, int &byte, int &nibble) {
+// Byte (and nibble) of column r (0 <= r < chunk_cols) inside a row's 64
+// value bytes of a chunk.
+__host__ __device__ inline void inner_position(int fmt, int r, int &byte, int &nibble) {
     if (fmt == FC_FMT_Q8) {
-        int c = k >> 6, r = k & 63;
-        byte = 64 * c + 16 * ((r & 15) >> 2) + 4 * (r >> 4) + (r & 3);
+        byte = 16 * ((r & 15) >> 2) + 4 * (r >> 4) + (r & 3);
         nibble = 0;
         return;
     }
-    int c = k >> 7, r = k & 127;
     int i = r >> 4, j = (r & 15) >> 2, b = r & 3;
     int q = 2 * i + (b >> 1), e = b & 1;
     int word = q >> 2;
     int slot = (q & 3) + 4 * e;
-    byte = 64 * c + 16 * j + 4 * word + (slot >> 1);
+    byte = 16 * j + 4 * word + (slot >> 1);
     nibble = slot & 1;
+}
+
+// Offset of the value byte holding element (o, k) of a matrix with padded
+// width kp; *nibble selects the half-byte for Q4 / MXFP4.
+__host__ __device__ inline size_t value_offset(int fmt, int kp, int o, int k, int *nibble) {
+    int cc = chunk_cols(fmt);
+    int byte, nib;
+    inner_position(fmt, k % cc, byte, nib);
+    if (nibble) *nibble = nib;
+    size_t blk = (size_t)(o / kTileRows) * chunk_count(fmt, kp) + (size_t)(k / cc);
+    return blk * block_bytes(fmt) + (size_t)(o % kTileRows) * 64 + byte;
+}
+
+// Offset of the scale of group `grp` (32 columns) of row o.
+__host__ __device__ inline size_t scale_offset(int fmt, int kp, int o, int grp) {
+    int gpc = groups_per_chunk(fmt);
+    size_t blk = (size_t)(o / kTileRows) * chunk_count(fmt, kp) + (size_t)(grp / gpc);
+    return blk * block_bytes(fmt) + kBlockValueBytes + (size_t)(o % kTileRows) * scale_row_bytes(fmt) +
+           (size_t)(grp % gpc) * scale_elem_bytes(fmt);
+}
+
+// ---------------------------------------------------------------------------
+// mbarrier + bulk async copy (TMA 1-D) helpers.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_fence_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Waits for phase `parity` of `bar` with an iteration limit; on timeout
+// records error bit 1 in *err and returns false (the caller carries on; the
+// host reports the error after the pass).
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, int *err) {
+    for (uint32_t it = 0; it < (1u << 20); ++it)
+        if (mbar_try_wait(bar, parity)) return true;
+    if (err) atomicOr(err, 1);
+    return false;
+}
+
+// Global -> shared bulk copy completing on `bar` (16-byte aligned, size a
+// multiple of 16).  A plain (non-multicast) copy of this GPU's own memory.
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
 }
 
 }  // namespace fc

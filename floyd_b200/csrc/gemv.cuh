@@ -6,20 +6,21 @@
 //     y[s][o] = sum_k x[s][k] * dequant(w[o][k])
 // with fp32 accumulation.
 //
-// B200 design.  The step is HBM-bound: every weight byte is read once, so
-// the kernel's only job is to keep enough bytes in flight and to spend few
-// issue slots per byte.  Weights are dequantized exactly into fp16 registers
-// (int8, int4 and e2m1 values are all exact in fp16) and multiplied on the
-// tensor cores with mma.m16n8k16 against activations split into hi + lo fp16
-// halves (about 22 significant bits), so one warp instruction covers 256
-// weights.  The device weight layout is permuted (common.cuh,
-// weight_position) so that each thread's 16-byte load feeds whole MMAs and
-// each MMA covers one scale group; the per-group scale is applied in fp32 to
-// the MMA result.  A CTA of 8 warps owns 32 output rows; warps take
-// interleaved 64-byte column chunks and are reduced in a fixed order through
-// shared memory, so every output row's summation order depends only on K,
-// never on the number of rows S: a verify row is bit-identical to the same
-// token decoded alone.
+// B200 design.  The step is HBM-bound: every weight byte is read once, so the
+// kernel's job is to keep HBM busy and to spend few issue slots per byte.
+//   - A CTA owns two 16-row tiles (two tiles of one matrix, or the gate and
+//     up tiles of a SwiGLU pair).  A tile is contiguous in the tile-major
+//     layout (common.cuh), so one thread streams it through shared memory
+//     with cp.async.bulk (TMA 1-D bulk copies) in 8-chunk stages, kStages
+//     stages in flight, completion tracked by mbarriers.
+//   - Each of the 8 warps takes one chunk of every stage, dequantizes it
+//     exactly into fp16 registers (int8, int4 and e2m1 values are all exact
+//     in fp16) and runs m16n8k16 tensor-core MMAs against the activations
+//     split into hi + lo fp16 halves (about 22 significant bits), one scale
+//     group per MMA pair, the group scale applied in fp32 to the MMA result.
+//   - Warps are reduced in a fixed order through shared memory, so every
+//     output's summation order depends only on K, never on the number of
+//     rows S: a verify row is bit-identical to the same token decoded alone.
 #pragma once
 
 #include "common.cuh"
@@ -28,7 +29,15 @@ namespace fc {
 
 constexpr int kGemvWarps = 8;
 constexpr int kGemvThreads = kGemvWarps * kWarp;
-constexpr int kGemvRows = 32;  // two m16 tiles per CTA
+constexpr int kGemvRows = 32;  // two 16-row tiles per CTA
+constexpr int kStages = 4;     // bulk-copy stages in flight per CTA
+
+__host__ __device__ constexpr size_t gemv_stage_bytes(int fmt) {
+    return (size_t)kGemvWarps * block_bytes(fmt);
+}
+__host__ __device__ constexpr size_t gemv_smem_bytes(int fmt) {
+    return (size_t)kStages * 2 * gemv_stage_bytes(fmt) + kStages * 8;
+}
 
 enum GemvEpilogue {
     EPI_STORE = 0,      // y[s*ldy + o] = v
@@ -37,28 +46,25 @@ enum GemvEpilogue {
     EPI_SWIGLU_XQ = 3   // tile 0 = gate rows, tile 1 = up rows -> silu(g)*u as xq
 };
 
-// One matrix (or a family of `count` equally shaped matrices laid out with
-// fixed strides, e.g. the per-head W_UV blocks of kv_b) applied to one xq
+// One matrix (or a family of `count` equally shaped matrices laid out with a
+// fixed stride, e.g. the per-head W_UV blocks of kv_b) applied to one xq
 // input and written through one epilogue.
 struct GemvSeg {
-    const uint8_t *w;       // device values, row stride row_bytes(fmt, kp)
-    const void *sc;         // group scales [O][kp/32]
-    const uint8_t *w2;      // SWIGLU: up-projection values
-    const void *sc2;        // SWIGLU: up-projection scales
+    const uint8_t *w;       // tile-major values + scales
+    const uint8_t *w2;      // SWIGLU: up-projection (same shape as w)
     const __half *xq;       // input rows [S][kp] in xq format
     float *y;               // EPI_STORE / EPI_ADD output
     __half *yq;             // xq outputs
-    int O, kp;              // rows (per matrix), padded K
+    int O, kp;              // rows (per member), padded K
     int ldy;                // fp32 output row stride
     int kpy;                // xq output row length
     int col_off;            // xq output column offset
     int epi;
-    int count;              // matrices in the family
-    int64_t w_stride;       // bytes between family members
-    int64_t sc_stride;      // scale elements between family members
-    int64_t xq_stride;      // halves between family members' inputs
-    int out_stride;         // output columns between family members
-    int tiles;              // CTAs per member (filled by the launcher)
+    int count;              // members in the family
+    int64_t w_stride;       // bytes between members
+    int64_t xq_stride;      // halves between members' inputs
+    int out_stride;         // output columns between members
+    int tiles;              // CTAs per member (set by the launcher)
 };
 
 constexpr int kMaxSegs = 6;
@@ -68,133 +74,144 @@ struct GemvBatch {
     int nseg;
     int S;
     float swiglu_limit;
+    int *err;
 };
 
-// Accumulates the 32 x 8 output tile (two m16 tiles x one n8 tile) of rows
-// [row0, row0 + 32) (tile t uses w_t, sc_t; rows >= nrows_t give zero) into
-// shared memory `out` [32][8] after a fixed-order reduction over the warps.
+// Streams tiles t0 / t1 (nullptr = absent) of padded width kp through shared
+// memory and leaves the reduced 32 x 8 tile (rows 0-15 from t0, 16-31 from
+// t1, columns = activation rows) in `out`.
 template <int FMT>
-__device__ __forceinline__ void gemv_tile(const uint8_t *w0, const void *sc0, int nrows0,
-                                          const uint8_t *w1, const void *sc1, int nrows1,
-                                          int kp, const __half *xq, int S, float *red,
-                                          float *out) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int g = lane >> 2, j = lane & 3;
-    const int rb = row_bytes(FMT, kp);
-    const int groups = kp / 32;
-    const int nchunks = rb / 64;
+__device__ __forceinline__ void gemv_tile(const uint8_t *t0, const uint8_t *t1, int kp,
+                                          const __half *xq, int S, uint8_t *smem, float *red,
+                                          float *out, int *err) {
+    constexpr int kBlock = block_bytes(FMT);
+    constexpr size_t kStageBytes = gemv_stage_bytes(FMT);
     constexpr int kMmas = FMT == FC_FMT_Q8 ? 4 : 8;  // MMAs per chunk
     constexpr int kGroups = kMmas / 2;               // scale groups per chunk
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int g = lane >> 2, j = lane & 3;
+    const int nchunks = chunk_count(FMT, kp);
+    const int nstages = (nchunks + kGemvWarps - 1) / kGemvWarps;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kStages * 2 * kStageBytes);
+    const uint8_t *src[2] = {t0, t1};
 
-    const uint8_t *wp[2] = {w0, w1};
-    const void *sp[2] = {sc0, sc1};
-    const int nr[2] = {nrows0, nrows1};
+    if (tid == 0) {
+        for (int i = 0; i < kStages; ++i) mbar_init(&bars[i], 1);
+        mbar_fence_init();
+    }
+    __syncthreads();
+    auto issue = [&](int s) {
+        int slot = s % kStages;
+        int c0 = s * kGemvWarps;
+        int nc = min(kGemvWarps, nchunks - c0);
+        uint32_t bytes = (uint32_t)(nc * kBlock);
+        uint32_t total = bytes * ((t0 ? 1u : 0u) + (t1 ? 1u : 0u));
+        mbar_expect_tx(&bars[slot], total);
+        for (int t = 0; t < 2; ++t)
+            if (src[t])
+                bulk_g2s(smem + (slot * 2 + t) * kStageBytes, src[t] + (size_t)c0 * kBlock, bytes,
+                         &bars[slot]);
+    };
+    if (tid == 0)
+        for (int s = 0; s < min(kStages, nstages); ++s) issue(s);
+
     const bool has_b = g < S;
-
     float acc[2][4];
 #pragma unroll
     for (int t = 0; t < 2; ++t)
 #pragma unroll
         for (int e = 0; e < 4; ++e) acc[t][e] = 0.0f;
 
-    for (int c = warp; c < nchunks; c += kGemvWarps) {
-        // ---- loads: A (2 tiles x 2 rows x 16 bytes), scales, B (xq) ----
-        uint4 a_raw[2][2];
-        float scale[2][2][kGroups];
-#pragma unroll
-        for (int t = 0; t < 2; ++t) {
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                int r = g + 8 * h;
-                if (r < nr[t]) {
-                    a_raw[t][h] = ldg_stream(wp[t] + (size_t)r * rb + 64 * c + 16 * j);
-                    if (FMT == FC_FMT_Q8) {
-                        uint32_t s2 = __ldg(reinterpret_cast<const uint32_t *>(
-                            reinterpret_cast<const __half *>(sp[t]) + (size_t)r * groups + 2 * c));
-                        __half2 hs = *reinterpret_cast<__half2 *>(&s2);
-                        scale[t][h][0] = __low2float(hs);
-                        scale[t][h][1] = __high2float(hs);
-                    } else if (FMT == FC_FMT_Q4) {
-                        uint2 s4 = __ldg(reinterpret_cast<const uint2 *>(
-                            reinterpret_cast<const __half *>(sp[t]) + (size_t)r * groups + 4 * c));
-                        __half2 h0 = *reinterpret_cast<__half2 *>(&s4.x);
-                        __half2 h1 = *reinterpret_cast<__half2 *>(&s4.y);
-                        scale[t][h][0] = __low2float(h0);
-                        scale[t][h][1] = __high2float(h0);
-                        scale[t][h][kGroups > 2 ? 2 : 0] = __low2float(h1);
-                        scale[t][h][kGroups > 3 ? 3 : 0] = __high2float(h1);
-                    } else {
-                        uint32_t s4 = __ldg(reinterpret_cast<const uint32_t *>(
-                            reinterpret_cast<const uint8_t *>(sp[t]) + (size_t)r * groups + 4 * c));
-#pragma unroll
-                        for (int q = 0; q < kGroups; ++q)
-                            scale[t][h][q] = e8m0_to_float((s4 >> (8 * q)) & 0xFFu);
-                    }
-                } else {
-                    a_raw[t][h] = make_uint4(0, 0, 0, 0);
-#pragma unroll
-                    for (int q = 0; q < kGroups; ++q) scale[t][h][q] = 0.0f;
-                }
-            }
-        }
+    for (int s = 0; s < nstages; ++s) {
+        const int slot = s % kStages;
+        const int c = s * kGemvWarps + warp;
+        // B fragments (activations, L2-resident) are fetched before the wait
         uint4 b_raw[kMmas];
 #pragma unroll
         for (int i = 0; i < kMmas; ++i) {
-            if (has_b) {
-                int m = kMmas * c + i;  // global k16 step
-                b_raw[i] = ldg_v4(xq + ((size_t)g * kp + 16 * m + 4 * j) * 2);
-            } else {
+            if (has_b && c < nchunks)
+                b_raw[i] = ldg_v4(xq + ((size_t)g * kp + 16 * (kMmas * c + i) + 4 * j) * 2);
+            else
                 b_raw[i] = make_uint4(0, 0, 0, 0);
-            }
         }
-
-        // ---- dequant + MMA, one scale group (2 MMAs) at a time ----
+        mbar_wait_bounded(&bars[slot], (uint32_t)((s / kStages) & 1), err);
+        if (c < nchunks) {
 #pragma unroll
-        for (int t = 0; t < 2; ++t) {
-            uint32_t regs[2][16];  // per row h: fp16x2 registers (q index)
+            for (int t = 0; t < 2; ++t) {
+                if (!src[t]) continue;
+                const uint8_t *blk = smem + (slot * 2 + t) * kStageBytes + (size_t)warp * kBlock;
+                uint4 a_raw[2];
+                float scale[2][kGroups];
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                const uint32_t words[4] = {a_raw[t][h].x, a_raw[t][h].y, a_raw[t][h].z,
-                                           a_raw[t][h].w};
-                if (FMT == FC_FMT_Q8) {
+                for (int h = 0; h < 2; ++h) {
+                    int r = g + 8 * h;
+                    a_raw[h] = *reinterpret_cast<const uint4 *>(blk + r * 64 + 16 * j);
+                    const uint8_t *sp = blk + kBlockValueBytes + r * scale_row_bytes(FMT);
+                    if (FMT == FC_FMT_Q8) {
+                        __half2 hs = *reinterpret_cast<const __half2 *>(sp);
+                        scale[h][0] = __low2float(hs);
+                        scale[h][kGroups > 1 ? 1 : 0] = __high2float(hs);
+                    } else if (FMT == FC_FMT_Q4) {
+                        uint2 s4 = *reinterpret_cast<const uint2 *>(sp);
+                        __half2 h0 = *reinterpret_cast<__half2 *>(&s4.x);
+                        __half2 h1 = *reinterpret_cast<__half2 *>(&s4.y);
+                        scale[h][0] = __low2float(h0);
+                        scale[h][1] = __high2float(h0);
+                        scale[h][kGroups > 2 ? 2 : 0] = __low2float(h1);
+                        scale[h][kGroups > 3 ? 3 : 0] = __high2float(h1);
+                    } else {
+                        uint32_t s4 = *reinterpret_cast<const uint32_t *>(sp);
 #pragma unroll
-                    for (int wi = 0; wi < 4; ++wi)
-                        dequant_q8_word(words[wi], regs[h][2 * wi], regs[h][2 * wi + 1]);
-                } else if (FMT == FC_FMT_Q4) {
-#pragma unroll
-                    for (int wi = 0; wi < 4; ++wi)
-#pragma unroll
-                        for (int s = 0; s < 4; ++s)
-                            regs[h][4 * wi + s] = dequant_q4_pair(words[wi], 4 * s);
-                } else {
-#pragma unroll
-                    for (int wi = 0; wi < 4; ++wi) {
-                        uint32_t o4[4];
-                        dequant_e2m1_word(words[wi], o4);
-#pragma unroll
-                        for (int p = 0; p < 4; ++p) regs[h][4 * wi + p] = o4[p];
+                        for (int q = 0; q < kGroups; ++q)
+                            scale[h][q] = e8m0_to_float((s4 >> (8 * q)) & 0xFFu);
                     }
                 }
-            }
+                uint32_t regs[2][16];  // per row h: fp16x2 registers (index q)
 #pragma unroll
-            for (int q = 0; q < kGroups; ++q) {
-                float tmp[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                for (int h = 0; h < 2; ++h) {
+                    const uint32_t words[4] = {a_raw[h].x, a_raw[h].y, a_raw[h].z, a_raw[h].w};
+                    if (FMT == FC_FMT_Q8) {
 #pragma unroll
-                for (int ii = 0; ii < 2; ++ii) {
-                    int i = 2 * q + ii;
-                    // A fragment: a0 = row g (k slots 2j,2j+1), a1 = row g+8,
-                    // a2 = row g (slots 2j+8, 2j+9), a3 = row g+8.
-                    uint32_t a[4] = {regs[0][2 * i], regs[1][2 * i], regs[0][2 * i + 1],
-                                     regs[1][2 * i + 1]};
-                    mma_f16(tmp, a, b_raw[i].x, b_raw[i].y, tmp);
-                    mma_f16(tmp, a, b_raw[i].z, b_raw[i].w, tmp);
+                        for (int wi = 0; wi < 4; ++wi)
+                            dequant_q8_word(words[wi], regs[h][2 * wi], regs[h][2 * wi + 1]);
+                    } else if (FMT == FC_FMT_Q4) {
+#pragma unroll
+                        for (int wi = 0; wi < 4; ++wi)
+#pragma unroll
+                            for (int sh = 0; sh < 4; ++sh)
+                                regs[h][4 * wi + sh] = dequant_q4_pair(words[wi], 4 * sh);
+                    } else {
+#pragma unroll
+                        for (int wi = 0; wi < 4; ++wi) {
+                            uint32_t o4[4];
+                            dequant_e2m1_word(words[wi], o4);
+#pragma unroll
+                            for (int p = 0; p < 4; ++p) regs[h][4 * wi + p] = o4[p];
+                        }
+                    }
                 }
-                acc[t][0] = fmaf(scale[t][0][q], tmp[0], acc[t][0]);
-                acc[t][1] = fmaf(scale[t][0][q], tmp[1], acc[t][1]);
-                acc[t][2] = fmaf(scale[t][1][q], tmp[2], acc[t][2]);
-                acc[t][3] = fmaf(scale[t][1][q], tmp[3], acc[t][3]);
+#pragma unroll
+                for (int q = 0; q < kGroups; ++q) {
+                    float tmp[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+                    for (int ii = 0; ii < 2; ++ii) {
+                        int i = 2 * q + ii;
+                        // a0 = row g (k slots 2j,2j+1), a1 = row g+8,
+                        // a2 = row g (slots 2j+8, 2j+9), a3 = row g+8.
+                        uint32_t a[4] = {regs[0][2 * i], regs[1][2 * i], regs[0][2 * i + 1],
+                                         regs[1][2 * i + 1]};
+                        mma_f16(tmp, a, b_raw[i].x, b_raw[i].y, tmp);
+                        mma_f16(tmp, a, b_raw[i].z, b_raw[i].w, tmp);
+                    }
+                    acc[t][0] = fmaf(scale[0][q], tmp[0], acc[t][0]);
+                    acc[t][1] = fmaf(scale[0][q], tmp[1], acc[t][1]);
+                    acc[t][2] = fmaf(scale[1][q], tmp[2], acc[t][2]);
+                    acc[t][3] = fmaf(scale[1][q], tmp[3], acc[t][3]);
+                }
             }
         }
+        __syncthreads();  // every warp is done with this slot
+        if (tid == 0 && s + kStages < nstages) issue(s + kStages);
     }
 
     // ---- fixed-order reduction over warps ----
@@ -204,8 +221,7 @@ __device__ __forceinline__ void gemv_tile(const uint8_t *w0, const void *sc0, in
         for (int e = 0; e < 4; ++e) red[((warp * 2 + t) * 32 + lane) * 4 + e] = acc[t][e];
     __syncthreads();
     {
-        // 256 threads -> 256 outputs (2 tiles x 32 lanes x 4)
-        int idx = threadIdx.x;
+        int idx = threadIdx.x;  // 256 threads -> 2 tiles x 32 lanes x 4
         int t = idx >> 7, l = (idx >> 2) & 31, e = idx & 3;
         float sum = 0.0f;
 #pragma unroll
@@ -219,8 +235,8 @@ __device__ __forceinline__ void gemv_tile(const uint8_t *w0, const void *sc0, in
 
 // Applies the epilogue of `sg` to the finished tile `out` [32][8] whose first
 // row is `row0` of member matrix `member`.
-__device__ __forceinline__ void gemv_epilogue(const GemvSeg &sg, int member, int row0,
-                                              int S, float limit, const float *out) {
+__device__ __forceinline__ void gemv_epilogue(const GemvSeg &sg, int member, int row0, int S,
+                                              float limit, const float *out) {
     int idx = threadIdx.x;
     if (sg.epi == EPI_SWIGLU_XQ) {
         if (idx >= 128) return;
@@ -249,8 +265,27 @@ __device__ __forceinline__ void gemv_epilogue(const GemvSeg &sg, int member, int
     }
 }
 
+// CTA `tile` of a member matrix: the two tile streams and the first row.
+template <int FMT>
+__device__ __forceinline__ void seg_tiles(const GemvSeg &sg, const uint8_t *w, const uint8_t *w2,
+                                          int tile, const uint8_t *&t0, const uint8_t *&t1,
+                                          int &row0) {
+    const size_t tb = tile_bytes(FMT, sg.kp);
+    const int ntiles = (sg.O + kTileRows - 1) / kTileRows;
+    if (sg.epi == EPI_SWIGLU_XQ) {
+        row0 = tile * kTileRows;
+        t0 = w + (size_t)tile * tb;
+        t1 = w2 + (size_t)tile * tb;
+    } else {
+        row0 = tile * 2 * kTileRows;
+        t0 = w + (size_t)(2 * tile) * tb;
+        t1 = 2 * tile + 1 < ntiles ? w + (size_t)(2 * tile + 1) * tb : nullptr;
+    }
+}
+
 template <int FMT>
 __global__ void __launch_bounds__(kGemvThreads, 2) gemv_batch_kernel(const __grid_constant__ GemvBatch b) {
+    extern __shared__ __align__(128) uint8_t gemv_smem[];
     __shared__ float red[kGemvWarps * 2 * 32 * 4];
     __shared__ float out[kGemvRows * 8];
     int block = blockIdx.x;
@@ -262,55 +297,58 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_batch_kernel(const __gri
     const GemvSeg &sg = b.seg[si];
     int member = block / sg.tiles, tile = block % sg.tiles;
     const uint8_t *w = sg.w + member * sg.w_stride;
-    const int rb = row_bytes(FMT, sg.kp);
-    const size_t scale_elem = FMT == FC_FMT_MXFP4 ? 1 : 2;
-    const uint8_t *sc = reinterpret_cast<const uint8_t *>(sg.sc) + member * sg.sc_stride * scale_elem;
+    const uint8_t *w2 = sg.w2 ? sg.w2 + member * sg.w_stride : nullptr;
     const __half *xq = sg.xq + member * sg.xq_stride;
+    const uint8_t *t0, *t1;
     int row0;
-    const uint8_t *w0, *w1;
-    const void *s0, *s1;
-    int n0, n1;
-    int groups = sg.kp / 32;
-    if (sg.epi == EPI_SWIGLU_XQ) {
-        row0 = tile * 16;
-        const uint8_t *up = sg.w2 + member * sg.w_stride;
-        const uint8_t *usc = reinterpret_cast<const uint8_t *>(sg.sc2) + member * sg.sc_stride * scale_elem;
-        w0 = w + (size_t)row0 * rb;
-        w1 = up + (size_t)row0 * rb;
-        s0 = sc + (size_t)row0 * groups * scale_elem;
-        s1 = usc + (size_t)row0 * groups * scale_elem;
-        n0 = n1 = min(16, sg.O - row0);
-    } else {
-        row0 = tile * 32;
-        w0 = w + (size_t)row0 * rb;
-        w1 = w + (size_t)(row0 + 16) * rb;
-        s0 = sc + (size_t)row0 * groups * scale_elem;
-        s1 = sc + (size_t)(row0 + 16) * groups * scale_elem;
-        n0 = min(16, sg.O - row0);
-        n1 = min(16, sg.O - row0 - 16);
-    }
-    gemv_tile<FMT>(w0, s0, n0, w1, s1, n1, sg.kp, xq, b.S, red, out);
+    seg_tiles<FMT>(sg, w, w2, tile, t0, t1, row0);
+    gemv_tile<FMT>(t0, t1, sg.kp, xq, b.S, gemv_smem, red, out, b.err);
     gemv_epilogue(sg, member, row0, b.S, b.swiglu_limit, out);
 }
 
 inline int gemv_tiles(const GemvSeg &s) {
-    return s.epi == EPI_SWIGLU_XQ ? (s.O + 15) / 16 : (s.O + 31) / 32;
+    int ntiles = (s.O + kTileRows - 1) / kTileRows;
+    return s.epi == EPI_SWIGLU_XQ ? ntiles : (ntiles + 1) / 2;
+}
+
+// Opts the GEMV kernels into their dynamic shared memory (call once per
+// device before launching or capturing).
+inline cudaError_t gemv_prepare_all() {
+    cudaError_t e = cudaFuncSetAttribute(gemv_batch_kernel<FC_FMT_Q8>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)gemv_smem_bytes(FC_FMT_Q8));
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(gemv_batch_kernel<FC_FMT_Q4>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)gemv_smem_bytes(FC_FMT_Q4));
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(gemv_batch_kernel<FC_FMT_MXFP4>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)gemv_smem_bytes(FC_FMT_MXFP4));
+    return e;
 }
 
 // Launches one batch of segments that share a weight format.
 inline cudaError_t launch_gemv_batch(int fmt, GemvBatch &b, cudaStream_t stream) {
     int blocks = 0;
     for (int i = 0; i < b.nseg; ++i) {
-        b.seg[i].tiles = gemv_tiles(b.seg[i]);
         if (b.seg[i].count <= 0) b.seg[i].count = 1;
+        b.seg[i].tiles = gemv_tiles(b.seg[i]);
         blocks += b.seg[i].tiles * b.seg[i].count;
     }
     if (blocks == 0) return cudaSuccess;
     switch (fmt) {
-        case FC_FMT_Q8: gemv_batch_kernel<FC_FMT_Q8><<<blocks, kGemvThreads, 0, stream>>>(b); break;
-        case FC_FMT_Q4: gemv_batch_kernel<FC_FMT_Q4><<<blocks, kGemvThreads, 0, stream>>>(b); break;
-        case FC_FMT_MXFP4: gemv_batch_kernel<FC_FMT_MXFP4><<<blocks, kGemvThreads, 0, stream>>>(b); break;
-        default: return cudaErrorInvalidValue;
+        case FC_FMT_Q8:
+            gemv_batch_kernel<FC_FMT_Q8><<<blocks, kGemvThreads, gemv_smem_bytes(FC_FMT_Q8), stream>>>(b);
+            break;
+        case FC_FMT_Q4:
+            gemv_batch_kernel<FC_FMT_Q4><<<blocks, kGemvThreads, gemv_smem_bytes(FC_FMT_Q4), stream>>>(b);
+            break;
+        case FC_FMT_MXFP4:
+            gemv_batch_kernel<FC_FMT_MXFP4><<<blocks, kGemvThreads, gemv_smem_bytes(FC_FMT_MXFP4), stream>>>(b);
+            break;
+        default:
+            return cudaErrorInvalidValue;
     }
     return cudaGetLastError();
 }

@@ -36,6 +36,8 @@ struct Staging {
 struct Result {
     int commit;
     int next_token;
+    int error;      // error bits raised by kernels of this pass
+    int pad;
     int row_tops[kMaxRows];
 };
 
@@ -144,7 +146,7 @@ __global__ void head_partial_kernel(const float *logits, int V, const Staging *s
 // One block.  Final argmax per row (chunk order), acceptance, result record
 // and, when `last_logits` is set, the logits row commit-1.
 __global__ void accept_kernel(const float *logits, int V, const Staging *st, HeadPartials hp,
-                              int chunks, Result *res, float *last_logits) {
+                              int chunks, Result *res, float *last_logits, int *err) {
     __shared__ int commit_s;
     int rows = st->rows;
     if (threadIdx.x == 0) {
@@ -205,6 +207,8 @@ __global__ void accept_kernel(const float *logits, int V, const Staging *st, Hea
         }
         res->commit = commit;
         res->next_token = next;
+        res->error = *err;
+        *err = 0;
         commit_s = commit;
     }
     __syncthreads();

@@ -26,34 +26,25 @@ namespace fc {
 // ---------------------------------------------------------------------------
 // Embedding gather (moonlight_kernels.metal:10-21) of a quantized table.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ float dequant_element(int fmt, const uint8_t *w, const void *sc,
-                                                 int kp, size_t row, int k) {
-    if (fmt == FC_FMT_F32) return reinterpret_cast<const float *>(w)[row * kp + k];
-    int byte, nib;
-    weight_position(fmt, k, byte, nib);
-    const uint8_t *rowp = w + row * (size_t)row_bytes(fmt, kp);
-    size_t gi = row * (size_t)(kp / 32) + (size_t)(k >> 5);
-    if (fmt == FC_FMT_Q8) {
-        float s = __half2float(reinterpret_cast<const __half *>(sc)[gi]);
-        return (float)(int8_t)rowp[byte] * s;
-    }
-    uint32_t code = (rowp[byte] >> (4 * nib)) & 15u;
-    if (fmt == FC_FMT_Q4) {
-        float s = __half2float(reinterpret_cast<const __half *>(sc)[gi]);
-        return (float)((int)code - 8) * s;
-    }
+__device__ __forceinline__ float dequant_element(int fmt, const uint8_t *w, int kp, int row, int k) {
+    int nib;
+    uint8_t byte = w[value_offset(fmt, kp, row, k, &nib)];
+    const uint8_t *sp = w + scale_offset(fmt, kp, row, k >> 5);
+    if (fmt == FC_FMT_Q8) return (float)(int8_t)byte * __half2float(*reinterpret_cast<const __half *>(sp));
+    uint32_t code = (byte >> (4 * nib)) & 15u;
+    if (fmt == FC_FMT_Q4)
+        return (float)((int)code - 8) * __half2float(*reinterpret_cast<const __half *>(sp));
     const float table[8] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};
     float v = table[code & 7];
     if (code & 8) v = -v;
-    return v * e8m0_to_float(reinterpret_cast<const uint8_t *>(sc)[gi]);
+    return v * e8m0_to_float(*sp);
 }
 
-__global__ void embed_kernel(int fmt, const uint8_t *w, const void *sc, int D, int kp,
-                             const int *ids, float *x) {
+__global__ void embed_kernel(int fmt, const uint8_t *w, int D, int kp, const int *ids, float *x) {
     int s = blockIdx.x;
-    size_t row = (size_t)ids[s];
+    int row = ids[s];
     for (int k = threadIdx.x; k < D; k += blockDim.x)
-        x[(size_t)s * D + k] = dequant_element(fmt, w, sc, kp, row, k);
+        x[(size_t)s * D + k] = dequant_element(fmt, w, kp, row, k);
 }
 
 // ---------------------------------------------------------------------------
@@ -144,7 +135,7 @@ __global__ void mla_prep_kernel(const float *ckv, const float *q, const float *n
 constexpr int kAbsorbCols = 64;
 constexpr int kAbsorbMaxNope = 128;
 
-__global__ void __launch_bounds__(256) mla_absorb_kernel(int fmt, const uint8_t *w, const void *sc,
+__global__ void __launch_bounds__(256) mla_absorb_kernel(int fmt, const uint8_t *w,
                                                          int kp, const float *q, int S, int H,
                                                          int nope, int vdim, int R, int L,
                                                          __half *qcat) {
@@ -158,7 +149,7 @@ __global__ void __launch_bounds__(256) mla_absorb_kernel(int fmt, const uint8_t 
     }
     for (int i = threadIdx.x; i < nope * kAbsorbCols; i += blockDim.x) {
         int n = i / kAbsorbCols, c = i % kAbsorbCols;
-        wsm[n][c] = dequant_element(fmt, w, sc, kp, (size_t)h * (nope + vdim) + n, l0 + c);
+        wsm[n][c] = dequant_element(fmt, w, kp, h * (nope + vdim) + n, l0 + c);
     }
     __syncthreads();
     for (int o = threadIdx.x; o < S * kAbsorbCols; o += blockDim.x) {

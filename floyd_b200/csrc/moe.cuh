@@ -191,100 +191,91 @@ __global__ void route_select_kernel(const float *logits, RouteParams p) {
     }
 }
 
-// Grouped expert GEMV.  Blocks [0, max_slots * tiles) serve the routed slots
-// (slot >= *n_active exits), the rest serve the shared expert (`shared`,
-// member 0).  Routed member = active[slot]; inputs / outputs are per slot.
+// Grouped expert GEMV.  Blocks [0, max_slots * routed_tiles) serve the
+// routed slots (slot >= *n_active exits), the rest serve the shared expert.
+// Routed member = active[slot] - expert_base; inputs / outputs are per slot.
 struct MoeGemv {
-    GemvSeg routed;          // w, sc, (w2, sc2) at expert 0; strides per expert
-    GemvSeg shared;          // static segment (count 1)
+    GemvSeg routed;          // w / w2 at local expert 0; w_stride per expert
+    GemvSeg shared;          // static segment (w == nullptr: none)
     int max_slots;
     int routed_tiles;
     int shared_tiles;
+    int expert_base;         // first local expert id
     const int *n_active;
     const int *active;
     int64_t in_slot_stride;  // halves between slots' xq inputs (0 = shared input)
     int64_t out_slot_stride; // routed outputs: floats (EPI_STORE) or halves (xq)
     int S;
     float swiglu_limit;
+    int *err;
 };
 
 template <int FE, int FS>
 __global__ void __launch_bounds__(kGemvThreads, 2) moe_gemv_kernel(const __grid_constant__ MoeGemv m) {
+    extern __shared__ __align__(128) uint8_t gemv_smem[];
     __shared__ float red[kGemvWarps * 2 * 32 * 4];
     __shared__ float out[kGemvRows * 8];
     int block = blockIdx.x;
     int routed_blocks = m.max_slots * m.routed_tiles;
+    const uint8_t *t0, *t1;
+    int row0;
     if (block < routed_blocks) {
         int slot = block / m.routed_tiles, tile = block % m.routed_tiles;
         if (slot >= *m.n_active) return;
-        int e = m.active[slot];
+        int e = m.active[slot] - m.expert_base;
         GemvSeg sg = m.routed;
-        const size_t se = FE == FC_FMT_MXFP4 ? 1 : 2;
         const uint8_t *w = sg.w + e * sg.w_stride;
-        const uint8_t *sc = reinterpret_cast<const uint8_t *>(sg.sc) + e * sg.sc_stride * se;
-        const __half *xq = sg.xq + slot * m.in_slot_stride;
-        const int rb = row_bytes(FE, sg.kp), groups = sg.kp / 32;
-        int row0;
-        if (sg.epi == EPI_SWIGLU_XQ) {
-            row0 = tile * 16;
-            const uint8_t *up = sg.w2 + e * sg.w_stride;
-            const uint8_t *usc = reinterpret_cast<const uint8_t *>(sg.sc2) + e * sg.sc_stride * se;
-            int n = min(16, sg.O - row0);
-            gemv_tile<FE>(w + (size_t)row0 * rb, sc + (size_t)row0 * groups * se, n,
-                          up + (size_t)row0 * rb, usc + (size_t)row0 * groups * se, n,
-                          sg.kp, xq, m.S, red, out);
-            sg.yq = sg.yq + slot * m.out_slot_stride;
-        } else {
-            row0 = tile * 32;
-            gemv_tile<FE>(w + (size_t)row0 * rb, sc + (size_t)row0 * groups * se,
-                          min(16, sg.O - row0), w + (size_t)(row0 + 16) * rb,
-                          sc + (size_t)(row0 + 16) * groups * se, min(16, sg.O - row0 - 16),
-                          sg.kp, xq, m.S, red, out);
-            sg.y = sg.y + slot * m.out_slot_stride;
-        }
+        const uint8_t *w2 = sg.w2 ? sg.w2 + e * sg.w_stride : nullptr;
+        seg_tiles<FE>(sg, w, w2, tile, t0, t1, row0);
+        gemv_tile<FE>(t0, t1, sg.kp, sg.xq + slot * m.in_slot_stride, m.S, gemv_smem, red, out, m.err);
+        if (sg.epi == EPI_SWIGLU_XQ) sg.yq = sg.yq + slot * m.out_slot_stride;
+        else sg.y = sg.y + slot * m.out_slot_stride;
         gemv_epilogue(sg, 0, row0, m.S, m.swiglu_limit, out);
         return;
     }
     block -= routed_blocks;
     if (block >= m.shared_tiles) return;
     const GemvSeg &sg = m.shared;
-    const size_t se = FS == FC_FMT_MXFP4 ? 1 : 2;
-    const uint8_t *sc = reinterpret_cast<const uint8_t *>(sg.sc);
-    const int rb = row_bytes(FS, sg.kp), groups = sg.kp / 32;
-    int row0;
-    if (sg.epi == EPI_SWIGLU_XQ) {
-        row0 = block * 16;
-        const uint8_t *usc = reinterpret_cast<const uint8_t *>(sg.sc2);
-        int n = min(16, sg.O - row0);
-        gemv_tile<FS>(sg.w + (size_t)row0 * rb, sc + (size_t)row0 * groups * se, n,
-                      sg.w2 + (size_t)row0 * rb, usc + (size_t)row0 * groups * se, n, sg.kp,
-                      sg.xq, m.S, red, out);
-    } else {
-        row0 = block * 32;
-        gemv_tile<FS>(sg.w + (size_t)row0 * rb, sc + (size_t)row0 * groups * se,
-                      min(16, sg.O - row0), sg.w + (size_t)(row0 + 16) * rb,
-                      sc + (size_t)(row0 + 16) * groups * se, min(16, sg.O - row0 - 16), sg.kp,
-                      sg.xq, m.S, red, out);
-    }
+    seg_tiles<FS>(sg, sg.w, sg.w2, block, t0, t1, row0);
+    gemv_tile<FS>(t0, t1, sg.kp, sg.xq, m.S, gemv_smem, red, out, m.err);
     gemv_epilogue(sg, 0, row0, m.S, m.swiglu_limit, out);
 }
 
+constexpr size_t moe_smem_bytes(int fe, int fs) {
+    return gemv_smem_bytes(fe) > gemv_smem_bytes(fs) ? gemv_smem_bytes(fe) : gemv_smem_bytes(fs);
+}
+
+#define FC_MOE_FORMATS(X)                 \
+    X(FC_FMT_Q8, FC_FMT_Q8)               \
+    X(FC_FMT_Q4, FC_FMT_Q4)               \
+    X(FC_FMT_MXFP4, FC_FMT_Q8)            \
+    X(FC_FMT_Q4, FC_FMT_Q8)               \
+    X(FC_FMT_MXFP4, FC_FMT_MXFP4)         \
+    X(FC_FMT_Q8, FC_FMT_Q4)
+
+inline cudaError_t moe_prepare_all() {
+    cudaError_t e = cudaSuccess;
+#define FC_MOE_ATTR(A, B)                                                                         \
+    if (e == cudaSuccess)                                                                         \
+        e = cudaFuncSetAttribute(moe_gemv_kernel<A, B>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                 (int)moe_smem_bytes(A, B));
+    FC_MOE_FORMATS(FC_MOE_ATTR)
+#undef FC_MOE_ATTR
+    return e;
+}
+
 inline cudaError_t launch_moe_gemv(int fe, int fs, MoeGemv &m, cudaStream_t stream) {
+    if (m.routed.count <= 0) m.routed.count = 1;
     m.routed_tiles = gemv_tiles(m.routed);
     m.shared_tiles = m.shared.w ? gemv_tiles(m.shared) : 0;
     int blocks = m.max_slots * m.routed_tiles + m.shared_tiles;
     if (blocks == 0) return cudaSuccess;
-#define FC_MOE_CASE(A, B)                                                              \
-    if (fe == A && fs == B) {                                                          \
-        moe_gemv_kernel<A, B><<<blocks, kGemvThreads, 0, stream>>>(m);                 \
-        return cudaGetLastError();                                                     \
+#define FC_MOE_CASE(A, B)                                                                \
+    if (fe == A && fs == B) {                                                            \
+        moe_gemv_kernel<A, B><<<blocks, kGemvThreads, moe_smem_bytes(A, B), stream>>>(m); \
+        return cudaGetLastError();                                                       \
     }
-    FC_MOE_CASE(FC_FMT_Q8, FC_FMT_Q8)
-    FC_MOE_CASE(FC_FMT_Q4, FC_FMT_Q4)
-    FC_MOE_CASE(FC_FMT_MXFP4, FC_FMT_Q8)
-    FC_MOE_CASE(FC_FMT_Q4, FC_FMT_Q8)
-    FC_MOE_CASE(FC_FMT_MXFP4, FC_FMT_MXFP4)
-    FC_MOE_CASE(FC_FMT_Q8, FC_FMT_Q4)
+    FC_MOE_FORMATS(FC_MOE_CASE)
 #undef FC_MOE_CASE
     return cudaErrorInvalidValue;
 }

@@ -54,11 +54,8 @@ inline int kpad(int k) { return (k + 127) / 128 * 128; }
 // A matrix (or a family of `count` equally shaped matrices) in device layout.
 struct DevMat {
     int fmt = FC_FMT_F32, O = 0, K = 0, kp = 0, count = 0;
-    uint8_t *w = nullptr;   // values (or fp32 data for F32)
-    void *sc = nullptr;     // group scales
+    uint8_t *w = nullptr;   // tile-major values + scales (common.cuh), or fp32 data
     size_t w_bytes = 0;     // per member
-    size_t sc_bytes = 0;    // per member
-    size_t sc_elems = 0;    // per member
     uint32_t tid = 0;       // synthetic tensor id (slot 0)
     int slot0 = 0;          // synthetic slot of member 0
 };
@@ -128,6 +125,7 @@ struct FcSession {
     float *moe_part = nullptr, *sh_part = nullptr;
     float *logits = nullptr, *last_logits = nullptr, *layer_out = nullptr;
     HeadPartials hp{};
+    int *d_err = nullptr;    // bit 1: a bounded wait in a kernel gave up
     Staging *d_stage = nullptr, *h_stage = nullptr;
     Result *d_res = nullptr, *h_res = nullptr;
     std::map<int, cudaGraphExec_t> graphs;
@@ -153,29 +151,21 @@ void plan_mat(DevMat &m, int fmt, int O, int K, int count, uint32_t tid, int slo
     if (fmt == FC_FMT_F32) {
         m.kp = K;
         m.w_bytes = (size_t)O * K * 4;
-        m.sc_bytes = 0;
-        m.sc_elems = 0;
     } else {
         m.kp = kpad(K);
-        m.w_bytes = (size_t)O * row_bytes(fmt, m.kp);
-        m.sc_elems = (size_t)O * (m.kp / 32);
-        m.sc_bytes = m.sc_elems * (fmt == FC_FMT_MXFP4 ? 1 : 2);
+        m.w_bytes = matrix_bytes(fmt, O, m.kp);
     }
 }
 
 size_t mat_bytes(const DevMat &m) {
     if (!m.count) return 0;
-    return align256(m.w_bytes * m.count) + align256(m.sc_bytes * m.count);
+    return align256(m.w_bytes * m.count);
 }
 
 void place_mat(FcModel *model, DevMat &m) {
     if (!m.count) return;
     m.w = model->arena + model->arena_used;
     model->arena_used += align256(m.w_bytes * m.count);
-    if (m.sc_bytes) {
-        m.sc = model->arena + model->arena_used;
-        model->arena_used += align256(m.sc_bytes * m.count);
-    }
 }
 
 void plan_vec(DevVec &v, size_t n, uint32_t tid, int kind) { v.n = n; v.tid = tid; v.kind = kind; }
@@ -357,39 +347,34 @@ cudaError_t fill_mat(const DevMat &mm, uint64_t seed, cudaStream_t st) {
     synth_values_kernel<<<grid_for(nb), 256, 0, st>>>(mm.fmt, mm.w, mm.O, mm.K, mm.kp, mm.count,
                                                       seed, mm.tid, mm.slot0);
     size_t ns = ((size_t)mm.O * (mm.K / 32) + 3) / 4 * mm.count;
-    synth_scales_kernel<<<grid_for(ns), 256, 0, st>>>(mm.fmt, mm.sc, mm.O, mm.K, mm.kp, mm.count,
+    synth_scales_kernel<<<grid_for(ns), 256, 0, st>>>(mm.fmt, mm.w, mm.O, mm.K, mm.kp, mm.count,
                                                       seed, mm.tid, mm.slot0);
     return cudaGetLastError();
 }
 
-// logical row-major values (int8 / packed nibbles, even element low) ->
-// device layout of member `member`
-void pack_values(const DevMat &mm, const uint8_t *src, std::vector<uint8_t> &dst) {
-    size_t rb = row_bytes(mm.fmt, mm.kp);
-    dst.assign((size_t)mm.O * rb, mm.fmt == FC_FMT_Q4 ? 0x88 : 0);
+// Logical row-major values (int8 / packed nibbles, even element low) into
+// the tile-major device image `dev` of one member (values only).
+void pack_values(const DevMat &mm, const uint8_t *src, uint8_t *dev) {
     for (int o = 0; o < mm.O; ++o)
         for (int k = 0; k < mm.K; ++k) {
-            int byte, nib;
-            weight_position(mm.fmt, k, byte, nib);
-            uint8_t *d = &dst[(size_t)o * rb + byte];
+            int nib;
+            size_t off = value_offset(mm.fmt, mm.kp, o, k, &nib);
             if (mm.fmt == FC_FMT_Q8) {
-                *d = src[(size_t)o * mm.K + k];
+                dev[off] = src[(size_t)o * mm.K + k];
             } else {
                 size_t e = (size_t)o * mm.K + k;
                 uint8_t v = (src[e >> 1] >> (4 * (e & 1))) & 15;
-                *d = (uint8_t)((*d & ~(15 << (4 * nib))) | (v << (4 * nib)));
+                dev[off] = (uint8_t)((dev[off] & ~(15 << (4 * nib))) | (v << (4 * nib)));
             }
         }
 }
 
 void unpack_values(const DevMat &mm, const uint8_t *dev, uint8_t *dst) {
-    size_t rb = row_bytes(mm.fmt, mm.kp);
     if (mm.fmt != FC_FMT_Q8) memset(dst, 0, (size_t)mm.O * mm.K / 2);
     for (int o = 0; o < mm.O; ++o)
         for (int k = 0; k < mm.K; ++k) {
-            int byte, nib;
-            weight_position(mm.fmt, k, byte, nib);
-            uint8_t b = dev[(size_t)o * rb + byte];
+            int nib;
+            uint8_t b = dev[value_offset(mm.fmt, mm.kp, o, k, &nib)];
             if (mm.fmt == FC_FMT_Q8) {
                 dst[(size_t)o * mm.K + k] = b;
             } else {
@@ -398,6 +383,21 @@ void unpack_values(const DevMat &mm, const uint8_t *dev, uint8_t *dst) {
                 dst[e >> 1] |= (uint8_t)(v << (4 * (e & 1)));
             }
         }
+}
+
+// Group scales [O][K/32] (fp16 bits or ue8m0 bytes) <-> the device image.
+void pack_scales(const DevMat &mm, const uint8_t *src, uint8_t *dev) {
+    int gk = mm.K / 32, el = scale_elem_bytes(mm.fmt);
+    for (int o = 0; o < mm.O; ++o)
+        for (int g = 0; g < gk; ++g)
+            memcpy(dev + scale_offset(mm.fmt, mm.kp, o, g), src + ((size_t)o * gk + g) * el, el);
+}
+
+void unpack_scales(const DevMat &mm, const uint8_t *dev, uint8_t *dst) {
+    int gk = mm.K / 32, el = scale_elem_bytes(mm.fmt);
+    for (int o = 0; o < mm.O; ++o)
+        for (int g = 0; g < gk; ++g)
+            memcpy(dst + ((size_t)o * gk + g) * el, dev + scale_offset(mm.fmt, mm.kp, o, g), el);
 }
 
 // ---------------------------------------------------------------------------
@@ -436,7 +436,6 @@ void free_session_buffers(FcSession *s) {
 GemvSeg seg_of(const DevMat &mm, const __half *xq, int epi) {
     GemvSeg g{};
     g.w = mm.w;
-    g.sc = mm.sc;
     g.xq = xq;
     g.O = mm.O;
     g.kp = mm.kp;
@@ -451,12 +450,13 @@ GemvSeg seg_of(const DevMat &mm, const __half *xq, int epi) {
         if (e_ != cudaSuccess) return e_;            \
     } while (0)
 
-cudaError_t gemv1(int fmt, GemvSeg a, int S, float limit, cudaStream_t st) {
+cudaError_t gemv1(int fmt, GemvSeg a, int S, float limit, int *err, cudaStream_t st) {
     GemvBatch b{};
     b.seg[0] = a;
     b.nseg = 1;
     b.S = S;
     b.swiglu_limit = limit;
+    b.err = err;
     return launch_gemv_batch(fmt, b, st);
 }
 
@@ -484,8 +484,8 @@ cudaError_t record_forward(FcSession *s, int S) {
     const int df = c.dense_format, ef = c.expert_format;
 
     FC_TRY(cudaMemcpyAsync(s->d_stage, s->h_stage, sizeof(Staging), cudaMemcpyHostToDevice, st));
-    embed_kernel<<<S, 256, 0, st>>>(m->embed.fmt, m->embed.w, m->embed.sc, D, m->embed.kp,
-                                    s->d_stage->ids, s->resid);
+    embed_kernel<<<S, 256, 0, st>>>(m->embed.fmt, m->embed.w, D, m->embed.kp, s->d_stage->ids,
+                                    s->resid);
     FC_TRY(cudaGetLastError());
     mark(s, "embed");
     for (int l = 0; l < c.layer_count; ++l) {
@@ -497,6 +497,7 @@ cudaError_t record_forward(FcSession *s, int S) {
         {
             GemvBatch b{};
             b.S = S;
+            b.err = s->d_err;
             if (c.q_lora_rank > 0) {
                 b.seg[0] = seg_of(y.q_a, s->xq_norm, EPI_STORE);
                 b.seg[0].y = s->qa;
@@ -521,7 +522,7 @@ cudaError_t record_forward(FcSession *s, int S) {
             GemvSeg g = seg_of(y.q_b, s->qa_xq, EPI_STORE);
             g.y = s->q;
             g.ldy = H * QW;
-            FC_TRY(gemv1(df, g, S, 0.0f, st));
+            FC_TRY(gemv1(df, g, S, 0.0f, s->d_err, st));
             mark(s, "gemv_q_b");
         }
         mla_prep_kernel<<<S, 256, 0, st>>>(s->ckv, s->q, y.kv_a_norm.p, L, R, H, NP,
@@ -529,7 +530,7 @@ cudaError_t record_forward(FcSession *s, int S) {
         mark(s, "mla_prep");
         {
             dim3 grid(H, L / kAbsorbCols);
-            mla_absorb_kernel<<<grid, 256, 0, st>>>(df, y.kv_b.w, y.kv_b.sc, y.kv_b.kp, s->q, S, H,
+            mla_absorb_kernel<<<grid, 256, 0, st>>>(df, y.kv_b.w, y.kv_b.kp, s->q, S, H,
                                                     NP, VD, R, L, s->qcat);
             mark(s, "mla_absorb");
         }
@@ -551,28 +552,26 @@ cudaError_t record_forward(FcSession *s, int S) {
                                                            s->splits, S, H, L, s->ctx_xq, head_stride);
             mark(s, "mla_combine");
             // W_UV: rows nope .. nope+v of each head's kv_b block (decode_value, :345-375)
+            // nope and value_dim are multiples of 16, so each head's W_UV
+            // block starts on a tile boundary of kv_b
             GemvSeg g = seg_of(y.kv_b, s->ctx_xq, EPI_STORE_XQ);
-            size_t rb = row_bytes(df, y.kv_b.kp);
-            size_t groups = y.kv_b.kp / 32;
-            size_t se = df == FC_FMT_MXFP4 ? 1 : 2;
-            g.w = y.kv_b.w + (size_t)NP * rb;
-            g.sc = reinterpret_cast<const uint8_t *>(y.kv_b.sc) + (size_t)NP * groups * se;
+            size_t tb = tile_bytes(df, y.kv_b.kp);
+            g.w = y.kv_b.w + (size_t)(NP / kTileRows) * tb;
             g.O = VD;
             g.count = H;
-            g.w_stride = (int64_t)(NP + VD) * rb;
-            g.sc_stride = (int64_t)(NP + VD) * groups;
+            g.w_stride = (int64_t)((NP + VD) / kTileRows) * (int64_t)tb;
             g.xq_stride = (int64_t)head_stride;
             g.yq = s->o_xq;
             g.kpy = kpO;
             g.out_stride = VD;
-            FC_TRY(gemv1(df, g, S, 0.0f, st));
+            FC_TRY(gemv1(df, g, S, 0.0f, s->d_err, st));
             mark(s, "gemv_w_uv");
         }
         {
             GemvSeg g = seg_of(y.o_proj, s->o_xq, EPI_ADD);
             g.y = s->resid;
             g.ldy = D;
-            FC_TRY(gemv1(df, g, S, 0.0f, st));
+            FC_TRY(gemv1(df, g, S, 0.0f, s->d_err, st));
             mark(s, "gemv_o_proj");
         }
         rmsnorm_kernel<<<S, 256, 0, st>>>(s->resid, D, y.ffn_norm.p, D, c.rms_norm_epsilon,
@@ -582,15 +581,14 @@ cudaError_t record_forward(FcSession *s, int S) {
             int kpI = kpad(c.dense_intermediate_size);
             GemvSeg g = seg_of(y.d_gate, s->xq_norm, EPI_SWIGLU_XQ);
             g.w2 = y.d_up.w;
-            g.sc2 = y.d_up.sc;
             g.yq = s->hd_xq;
             g.kpy = kpI;
-            FC_TRY(gemv1(df, g, S, 0.0f, st));
+            FC_TRY(gemv1(df, g, S, 0.0f, s->d_err, st));
             mark(s, "gemv_dense_gate_up");
             GemvSeg d = seg_of(y.d_down, s->hd_xq, EPI_ADD);
             d.y = s->resid;
             d.ldy = D;
-            FC_TRY(gemv1(df, d, S, 0.0f, st));
+            FC_TRY(gemv1(df, d, S, 0.0f, s->d_err, st));
             mark(s, "gemv_dense_down");
         } else {
             int E = c.expert_count, K = c.experts_per_token;
@@ -619,20 +617,15 @@ cudaError_t record_forward(FcSession *s, int S) {
             // gate / up + SwiGLU
             MoeGemv gu{};
             gu.routed = seg_of(y.e_gate, s->xq_norm, EPI_SWIGLU_XQ);
-            gu.routed.w = y.e_gate.w - (size_t)m->expert_lo * y.e_gate.w_bytes;
-            gu.routed.sc = reinterpret_cast<const uint8_t *>(y.e_gate.sc) -
-                           (size_t)m->expert_lo * y.e_gate.sc_bytes;
-            gu.routed.w2 = y.e_up.w - (size_t)m->expert_lo * y.e_up.w_bytes;
-            gu.routed.sc2 = reinterpret_cast<const uint8_t *>(y.e_up.sc) -
-                            (size_t)m->expert_lo * y.e_up.sc_bytes;
+            gu.routed.w2 = y.e_up.w;
             gu.routed.w_stride = (int64_t)y.e_gate.w_bytes;
-            gu.routed.sc_stride = (int64_t)y.e_gate.sc_elems;
+            gu.expert_base = m->expert_lo;
+            gu.err = s->d_err;
             gu.routed.yq = s->h_xq;
             gu.routed.kpy = kpI;
             if (y.s_gate.count) {
                 gu.shared = seg_of(y.s_gate, s->xq_norm, EPI_SWIGLU_XQ);
                 gu.shared.w2 = y.s_up.w;
-                gu.shared.sc2 = y.s_up.sc;
                 gu.shared.yq = s->hsh_xq;
                 gu.shared.kpy = kpW;
             }
@@ -648,11 +641,9 @@ cudaError_t record_forward(FcSession *s, int S) {
             // down
             MoeGemv dn{};
             dn.routed = seg_of(y.e_down, s->h_xq, EPI_STORE);
-            dn.routed.w = y.e_down.w - (size_t)m->expert_lo * y.e_down.w_bytes;
-            dn.routed.sc = reinterpret_cast<const uint8_t *>(y.e_down.sc) -
-                           (size_t)m->expert_lo * y.e_down.sc_bytes;
             dn.routed.w_stride = (int64_t)y.e_down.w_bytes;
-            dn.routed.sc_stride = (int64_t)y.e_down.sc_elems;
+            dn.expert_base = m->expert_lo;
+            dn.err = s->d_err;
             dn.routed.y = s->moe_part;
             dn.routed.ldy = D;
             if (y.s_down.count) {
@@ -686,7 +677,7 @@ cudaError_t record_forward(FcSession *s, int S) {
         GemvSeg g = seg_of(m->lm_head, s->xq_norm, EPI_STORE);
         g.y = s->logits;
         g.ldy = c.vocab_size;
-        FC_TRY(gemv1(df, g, S, 0.0f, st));
+        FC_TRY(gemv1(df, g, S, 0.0f, s->d_err, st));
         mark(s, "gemv_lm_head");
     }
     {
@@ -695,7 +686,7 @@ cudaError_t record_forward(FcSession *s, int S) {
                                                   s->head_chunks);
         mark(s, "head_partial");
         accept_kernel<<<1, 256, 0, st>>>(s->logits, c.vocab_size, s->d_stage, s->hp, s->head_chunks,
-                                         s->d_res, s->last_logits);
+                                         s->d_res, s->last_logits, s->d_err);
         mark(s, "accept");
     }
     FC_TRY(cudaGetLastError());
@@ -783,6 +774,9 @@ int run_pass(FcSession *s, const int *ids, int rows, int k, const FcAcceptConfig
         s->stats.graph_replays++;
     }
     if (e != cudaSuccess) return set_error(err, n, "CUDA forward failed: %s", cudaGetErrorString(e));
+    if (!s->profiling && s->h_res->error)
+        return set_error(err, n, "a kernel wait gave up (error bits 0x%x); results are invalid",
+                         s->h_res->error);
     s->stats.command_buffers++;
     s->last_rows = rows;
     return 1;
@@ -930,42 +924,32 @@ static int tensor_io(const FcModel *m, const char *name, void *data, size_t byte
         return e == cudaSuccess ? 1 : set_error(error, error_size, "copy failed: %s", cudaGetErrorString(e));
     }
     const DevMat &mm = *r.mat;
-    if (scales) {
-        size_t elem = mm.fmt == FC_FMT_MXFP4 ? 1 : 2;
-        size_t gk = mm.K / 32, gp = mm.kp / 32;
-        size_t need = (size_t)mm.O * gk * elem;
+    uint8_t *base = mm.w + (size_t)r.member * mm.w_bytes;
+    if (mm.fmt == FC_FMT_F32) {
+        if (scales) return set_error(error, error_size, "tensor %s has no group scales", key.c_str());
+        size_t need = (size_t)mm.O * mm.K * 4;
         if (bytes != need)
             return set_error(error, error_size, "%s: expected %zu bytes, got %zu", name, need, bytes);
-        std::vector<uint8_t> dev(mm.sc_bytes, 0);
-        uint8_t *base = reinterpret_cast<uint8_t *>(mm.sc) + (size_t)r.member * mm.sc_bytes;
-        if (!upload && cudaMemcpy(dev.data(), base, mm.sc_bytes, cudaMemcpyDeviceToHost) != cudaSuccess)
-            return set_error(error, error_size, "copy failed");
-        for (int o = 0; o < mm.O; ++o) {
-            uint8_t *d = dev.data() + (size_t)o * gp * elem;
-            uint8_t *h = reinterpret_cast<uint8_t *>(data) + (size_t)o * gk * elem;
-            if (upload) memcpy(d, h, gk * elem);
-            else memcpy(h, d, gk * elem);
-        }
-        if (upload && cudaMemcpy(base, dev.data(), mm.sc_bytes, cudaMemcpyHostToDevice) != cudaSuccess)
-            return set_error(error, error_size, "copy failed");
-        return 1;
+        cudaError_t e = upload ? cudaMemcpy(base, data, need, cudaMemcpyHostToDevice)
+                               : cudaMemcpy(data, base, need, cudaMemcpyDeviceToHost);
+        return e == cudaSuccess ? 1 : set_error(error, error_size, "copy failed");
     }
-    uint8_t *base = mm.w + (size_t)r.member * mm.w_bytes;
-    size_t need = mm.fmt == FC_FMT_F32 ? (size_t)mm.O * mm.K * 4
+    size_t need = scales ? (size_t)mm.O * (mm.K / 32) * scale_elem_bytes(mm.fmt)
                   : mm.fmt == FC_FMT_Q8 ? (size_t)mm.O * mm.K : (size_t)mm.O * mm.K / 2;
     if (bytes != need)
         return set_error(error, error_size, "%s: expected %zu bytes, got %zu", name, need, bytes);
-    if (upload) {
-        std::vector<uint8_t> dev;
-        pack_values(mm, reinterpret_cast<const uint8_t *>(data), dev);
-        if (cudaMemcpy(base, dev.data(), dev.size(), cudaMemcpyHostToDevice) != cudaSuccess)
-            return set_error(error, error_size, "copy failed");
-    } else {
-        std::vector<uint8_t> dev(mm.w_bytes);
-        if (cudaMemcpy(dev.data(), base, mm.w_bytes, cudaMemcpyDeviceToHost) != cudaSuccess)
-            return set_error(error, error_size, "copy failed");
-        unpack_values(mm, dev.data(), reinterpret_cast<uint8_t *>(data));
+    std::vector<uint8_t> dev(mm.w_bytes);
+    if (cudaMemcpy(dev.data(), base, mm.w_bytes, cudaMemcpyDeviceToHost) != cudaSuccess)
+        return set_error(error, error_size, "copy failed");
+    if (!upload) {
+        if (scales) unpack_scales(mm, dev.data(), reinterpret_cast<uint8_t *>(data));
+        else unpack_values(mm, dev.data(), reinterpret_cast<uint8_t *>(data));
+        return 1;
     }
+    if (scales) pack_scales(mm, reinterpret_cast<const uint8_t *>(data), dev.data());
+    else pack_values(mm, reinterpret_cast<const uint8_t *>(data), dev.data());
+    if (cudaMemcpy(base, dev.data(), mm.w_bytes, cudaMemcpyHostToDevice) != cudaSuccess)
+        return set_error(error, error_size, "copy failed");
     return 1;
 }
 
@@ -1057,7 +1041,7 @@ int fc_session_create(FcSession **out, FcModel *m, const FcOptions *options, cha
     size_t hc = (size_t)mb * s->head_chunks;
     ok = ok && salloc(s, s->hp.amax, hc) && salloc(s, s->hp.aidx, hc) && salloc(s, s->hp.zmax, hc) &&
          salloc(s, s->hp.zsum, hc) && salloc(s, s->hp.gval, hc) && salloc(s, s->hp.gidx, hc);
-    ok = ok && salloc(s, s->d_stage, 1) && salloc(s, s->d_res, 1);
+    ok = ok && salloc(s, s->d_stage, 1) && salloc(s, s->d_res, 1) && salloc(s, s->d_err, 1);
     ok = ok && cudaMallocHost(&s->h_stage, sizeof(Staging)) == cudaSuccess;
     ok = ok && cudaMallocHost(&s->h_res, sizeof(Result)) == cudaSuccess;
     if (ok) {
@@ -1070,7 +1054,8 @@ int fc_session_create(FcSession **out, FcModel *m, const FcOptions *options, cha
         cudaError_t e3 = cudaFuncSetAttribute(route_select_kernel,
                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
                                               2 * 8 * 1024 * 4);
-        ok = e1 == cudaSuccess && e2 == cudaSuccess && e3 == cudaSuccess;
+        ok = e1 == cudaSuccess && e2 == cudaSuccess && e3 == cudaSuccess &&
+             gemv_prepare_all() == cudaSuccess && moe_prepare_all() == cudaSuccess;
     }
     if (!ok) {
         free_session_buffers(s);
@@ -1375,40 +1360,38 @@ extern "C" int fc_matmul(int format, float *y, const float *x, const void *value
         return set_error(error, error_size, "unsupported format %d", format);
     DevMat mm;
     plan_mat(mm, format, O, K, 1, 0, 0);
-    std::vector<uint8_t> packed;
-    pack_values(mm, reinterpret_cast<const uint8_t *>(values), packed);
-    size_t elem = format == FC_FMT_MXFP4 ? 1 : 2;
-    std::vector<uint8_t> sc(mm.sc_bytes, 0);
-    for (int o = 0; o < O; ++o)
-        memcpy(&sc[(size_t)o * (mm.kp / 32) * elem],
-               reinterpret_cast<const uint8_t *>(scales) + (size_t)o * (K / 32) * elem,
-               (size_t)(K / 32) * elem);
-    uint8_t *dw = nullptr, *dsc = nullptr;
+    std::vector<uint8_t> image(mm.w_bytes, 0);
+    pack_values(mm, reinterpret_cast<const uint8_t *>(values), image.data());
+    pack_scales(mm, reinterpret_cast<const uint8_t *>(scales), image.data());
+    uint8_t *dw = nullptr;
     float *dx = nullptr, *dy = nullptr;
     __half *dxq = nullptr;
+    int *derr = nullptr;
     size_t xq_bytes = (size_t)S * mm.kp * 2 * sizeof(__half);
-    bool ok = cudaMalloc(&dw, packed.size()) == cudaSuccess &&
-              cudaMalloc(&dsc, sc.size()) == cudaSuccess &&
+    bool ok = cudaMalloc(&dw, image.size()) == cudaSuccess &&
               cudaMalloc(&dx, (size_t)S * K * 4) == cudaSuccess &&
               cudaMalloc(&dy, (size_t)S * O * 4) == cudaSuccess &&
-              cudaMalloc(&dxq, xq_bytes) == cudaSuccess;
+              cudaMalloc(&dxq, xq_bytes) == cudaSuccess && cudaMalloc(&derr, 4) == cudaSuccess;
     cudaError_t e = cudaErrorMemoryAllocation;
-    if (ok) {
-        cudaMemcpy(dw, packed.data(), packed.size(), cudaMemcpyHostToDevice);
-        cudaMemcpy(dsc, sc.data(), sc.size(), cudaMemcpyHostToDevice);
+    int herr = 0;
+    if (ok) e = gemv_prepare_all();
+    if (ok && e == cudaSuccess) {
+        cudaMemcpy(dw, image.data(), image.size(), cudaMemcpyHostToDevice);
         cudaMemcpy(dx, x, (size_t)S * K * 4, cudaMemcpyHostToDevice);
         cudaMemset(dxq, 0, xq_bytes);
+        cudaMemset(derr, 0, 4);
         to_xq_kernel<<<(S * K + 255) / 256, 256>>>(dx, S, K, mm.kp, dxq);
         GemvSeg g = seg_of(mm, dxq, EPI_STORE);
         g.w = dw;
-        g.sc = dsc;
         g.y = dy;
         g.ldy = O;
-        e = gemv1(format, g, S, 0.0f, 0);
+        e = gemv1(format, g, S, 0.0f, derr, 0);
         if (e == cudaSuccess) e = cudaDeviceSynchronize();
         if (e == cudaSuccess) e = cudaMemcpy(y, dy, (size_t)S * O * 4, cudaMemcpyDeviceToHost);
+        if (e == cudaSuccess) e = cudaMemcpy(&herr, derr, 4, cudaMemcpyDeviceToHost);
     }
-    cudaFree(dw); cudaFree(dsc); cudaFree(dx); cudaFree(dy); cudaFree(dxq);
+    cudaFree(dw); cudaFree(dx); cudaFree(dy); cudaFree(dxq); cudaFree(derr);
+    if (e == cudaSuccess && herr) return set_error(error, error_size, "a kernel wait gave up");
     if (e != cudaSuccess) return set_error(error, error_size, "matmul failed: %s", cudaGetErrorString(e));
     return 1;
 }

@@ -6,20 +6,6 @@
 
 namespace fc {
 
-// Logical column of byte `b` (and nibble `nib`) of a 64-byte row chunk `c`;
-// the inverse of weight_position (common.cuh).
-__host__ __device__ inline int logical_column(int fmt, int c, int b, int nib) {
-    if (fmt == FC_FMT_Q8) {
-        int j = b >> 4, i = (b & 15) >> 2, bb = b & 3;
-        return 64 * c + 16 * i + 4 * j + bb;
-    }
-    int j = b >> 4, word = (b & 15) >> 2, bw = b & 3;
-    int slot = 2 * bw + nib;
-    int q = 4 * word + (slot & 3), e = slot >> 2;
-    int i = q >> 1, h = q & 1;
-    return 128 * c + 16 * i + 4 * j + 2 * h + e;
-}
-
 // Fills `count` matrices (rows O, logical K, padded kp) of a family with the
 // synthetic values of tensors tid_base | (member + slot0).  One thread per
 // Philox block: 8 int8 values or 32 nibbles of consecutive logical elements
@@ -30,7 +16,7 @@ __host__ __device__ inline int logical_column(int fmt, int c, int b, int nib) {
 __global__ void synth_values_kernel(int fmt, uint8_t *w, int O, int K, int kp, int count,
                                     uint64_t seed, uint32_t tid_base, int slot0) {
     const int per_block = fmt == FC_FMT_Q8 ? 8 : 32;
-    const size_t rb = (size_t)row_bytes(fmt, kp);
+    const size_t mb = matrix_bytes(fmt, O, kp);
     const size_t blocks_per_member = (size_t)O * K / per_block;
     const size_t total = blocks_per_member * count;
     for (size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
@@ -42,22 +28,20 @@ __global__ void synth_values_kernel(int fmt, uint8_t *w, int O, int K, int kp, i
         fc_synth_block(seed, tid, FC_STREAM_VALUES, blk, words);
         size_t e0 = blk * per_block;
         int o = (int)(e0 / K), k0 = (int)(e0 % K);
-        uint8_t *row = w + (size_t)member * O * rb + (size_t)o * rb;
+        uint8_t *row = w + (size_t)member * mb;
         if (fmt == FC_FMT_Q8) {
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
                 int v = ((int)fc_synth_byte(words, 2 * i) + (int)fc_synth_byte(words, 2 * i + 1) - 255) / 2;
-                int byte, nib;
-                weight_position(fmt, k0 + i, byte, nib);
-                row[byte] = (uint8_t)(int8_t)v;
+                row[value_offset(fmt, kp, o, k0 + i, nullptr)] = (uint8_t)(int8_t)v;
             }
         } else {
             // gather the 16 device bytes this block covers: byte -> two nibbles
 #pragma unroll 4
             for (int i = 0; i < 32; i += 2) {
-                int byte, nib0, byte1, nib1;
-                weight_position(fmt, k0 + i, byte, nib0);
-                weight_position(fmt, k0 + i + 1, byte1, nib1);
+                int nib0, nib1;
+                size_t byte = value_offset(fmt, kp, o, k0 + i, &nib0);
+                size_t byte1 = value_offset(fmt, kp, o, k0 + i + 1, &nib1);
                 uint32_t c0 = (words[i >> 3] >> (4 * (i & 7))) & 0xFu;
                 uint32_t c1 = (words[(i + 1) >> 3] >> (4 * ((i + 1) & 7))) & 0xFu;
                 if (byte == byte1) {
@@ -65,9 +49,9 @@ __global__ void synth_values_kernel(int fmt, uint8_t *w, int O, int K, int kp, i
                 } else {
                     // elements k, k+1 live in different bytes; their partner
                     // nibbles are elements k+2 / k+3 (same block)
-                    int byte2, nib2, byte3, nib3;
-                    weight_position(fmt, k0 + i + 2, byte2, nib2);
-                    weight_position(fmt, k0 + i + 3, byte3, nib3);
+                    int nib2, nib3;
+                    value_offset(fmt, kp, o, k0 + i + 2, &nib2);
+                    value_offset(fmt, kp, o, k0 + i + 3, &nib3);
                     uint32_t c2 = (words[(i + 2) >> 3] >> (4 * ((i + 2) & 7))) & 0xFu;
                     uint32_t c3 = (words[(i + 3) >> 3] >> (4 * ((i + 3) & 7))) & 0xFu;
                     row[byte] = (uint8_t)((c0 << (4 * nib0)) | (c2 << (4 * nib2)));
@@ -80,9 +64,10 @@ __global__ void synth_values_kernel(int fmt, uint8_t *w, int O, int K, int kp, i
 }
 
 // Group scales: one thread per Philox block of 4 scales.
-__global__ void synth_scales_kernel(int fmt, void *sc, int O, int K, int kp, int count,
+__global__ void synth_scales_kernel(int fmt, uint8_t *w, int O, int K, int kp, int count,
                                     uint64_t seed, uint32_t tid_base, int slot0) {
-    const int gk = K / 32, gp = kp / 32;
+    const int gk = K / 32;
+    const size_t mb = matrix_bytes(fmt, O, kp);
     const size_t groups = (size_t)O * gk;
     const size_t blocks_per_member = (groups + 3) / 4;
     const size_t total = blocks_per_member * count;
@@ -96,15 +81,15 @@ __global__ void synth_scales_kernel(int fmt, void *sc, int O, int K, int kp, int
         for (int i = 0; i < 4; ++i) {
             size_t lg = blk * 4 + i;
             if (lg >= groups) break;
-            size_t o = lg / gk, g = lg % gk;
-            size_t dst = (size_t)member * O * gp + o * gp + g;
+            int o = (int)(lg / gk), g = (int)(lg % gk);
+            uint8_t *dst = w + (size_t)member * mb + scale_offset(fmt, kp, o, g);
             uint32_t wd = words[i];
             if (fmt == FC_FMT_MXFP4)
-                reinterpret_cast<uint8_t *>(sc)[dst] = (uint8_t)(119u + (wd & 1u));
+                *dst = (uint8_t)(119u + (wd & 1u));
             else if (fmt == FC_FMT_Q8)
-                reinterpret_cast<uint16_t *>(sc)[dst] = (uint16_t)((3u << 10) | (wd & 0x3FFu));
+                *reinterpret_cast<uint16_t *>(dst) = (uint16_t)((3u << 10) | (wd & 0x3FFu));
             else
-                reinterpret_cast<uint16_t *>(sc)[dst] = (uint16_t)((7u << 10) | (wd & 0x3FFu));
+                *reinterpret_cast<uint16_t *>(dst) = (uint16_t)((7u << 10) | (wd & 0x3FFu));
         }
     }
 }

@@ -221,18 +221,29 @@ def test_sampling_decisions_match_oracle(oracle_lib):
     assert agree == 24
 
 
-def test_low_temperature_sampling_accepts_greedy_drafts():
-    """As the temperature goes to 0 the target distribution collapses onto the
-    greedy token, so drafts equal to the greedy stream are accepted and the
-    bonus token is the next greedy token.  (With random weights the logits
-    are nearly flat, so at temperature 0.7 a planted greedy draft is accepted
-    with probability p(x) of a few 1e-3.)"""
+@pytest.mark.parametrize("temperature", [1e-3, 0.02])
+def test_low_temperature_sampling_matches_oracle(oracle_lib, temperature):
+    """At low temperature drafts equal to the greedy stream are mostly
+    accepted: the accept branch, the residual resample and the bonus sample
+    all run, and every decision equals the oracle's on the same logits."""
     cfg, name = C1, "c1"
+    V = cfg["vocab_size"]
     stream = greedy_stream(cfg, name, 42, 4)
-    for counter in range(4):
+    accepted = 0
+    for counter in range(12):
         s, _ = sessions(cfg, name)
-        em, nxt, _ = s.verify(stream[0:4], mode=ACCEPT_SAMPLE, temperature=1e-3, seed=1, counter=counter)
-        assert em == stream[0:4] and nxt == stream[4]
+        em, nxt, _ = s.verify(stream[0:4], mode=ACCEPT_SAMPLE, temperature=temperature, seed=1,
+                              counter=counter)
+        logits = s.row_logits(4)
+        nxt_o = ctypes.c_int()
+        idp = np.array(stream[0:4], dtype=np.int32)
+        commit_o = oracle_lib.lib().orc_accept_sample(
+            logits.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), V,
+            idp.ctypes.data_as(ctypes.POINTER(ctypes.c_int)), 3, temperature, 1, counter,
+            ctypes.byref(nxt_o))
+        assert len(em) == commit_o and nxt == nxt_o.value
+        accepted += len(em) - 1
+    assert accepted >= 12
 
 
 def test_zero_draft_verify_equals_decode():
