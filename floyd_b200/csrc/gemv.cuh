@@ -4,39 +4,49 @@
 // :62-130), fm_matmul_q8 / q4 (backend_metal.m:124-130) and
 // deepseek_v4_fp4_matmul_f32 (deepseek_v4_quant.h:103-139):
 //     y[s][o] = sum_k x[s][k] * dequant(w[o][k])
-// with fp32 accumulation.
+// with fp32 accumulation, plus the grouped expert form of
+// encode_moe_residual_buffer (moonlight_metal.m:561-676).
 //
 // B200 design.  The step is HBM-bound: every weight byte is read once, so the
 // kernel's job is to keep HBM busy and to spend few issue slots per byte.
-//   - A CTA owns two 16-row tiles (two tiles of one matrix, or the gate and
-//     up tiles of a SwiGLU pair).  A tile is contiguous in the tile-major
-//     layout (common.cuh), so one thread streams it through shared memory
-//     with cp.async.bulk (TMA 1-D bulk copies) in 8-chunk stages, kStages
-//     stages in flight, completion tracked by mbarriers.
-//   - Each of the 8 warps takes one chunk of every stage, dequantizes it
-//     exactly into fp16 registers (int8, int4 and e2m1 values are all exact
-//     in fp16) and runs m16n8k16 tensor-core MMAs against the activations
-//     split into hi + lo fp16 halves (about 22 significant bits), one scale
-//     group per MMA pair, the group scale applied in fp32 to the MMA result.
+//   - Work items are pairs of 16-row tiles (two tiles of one matrix, or the
+//     gate and up tiles of a SwiGLU pair).  A tile is contiguous in the
+//     tile-major layout (common.cuh).
+//   - The kernel is persistent and warp-specialized: CTAs loop over work
+//     items; one producer warp streams every item's tiles through a ring of
+//     kStages shared-memory stages with cp.async.bulk (TMA 1-D bulk copies),
+//     full / empty mbarriers between it and the consumers, so copies for the
+//     next item are in flight while the current one is reduced.
+//   - Each of the 8 consumer warps takes one 64-byte-per-row chunk of every
+//     stage, dequantizes it exactly into fp16 registers (int8, int4 and e2m1
+//     values are all exact in fp16) and runs m16n8k16 tensor-core MMAs
+//     against the activations split into hi + lo fp16 halves (about 22
+//     significant bits); each MMA pair covers one 32-column scale group and
+//     the group scale is applied in fp32 to the MMA result.
 //   - Warps are reduced in a fixed order through shared memory, so every
 //     output's summation order depends only on K, never on the number of
-//     rows S: a verify row is bit-identical to the same token decoded alone.
+//     rows S or on the work distribution: a verify row is bit-identical to
+//     the same token decoded alone.
 #pragma once
 
 #include "common.cuh"
 
 namespace fc {
 
-constexpr int kGemvWarps = 8;
-constexpr int kGemvThreads = kGemvWarps * kWarp;
-constexpr int kGemvRows = 32;  // two 16-row tiles per CTA
-constexpr int kStages = 4;     // bulk-copy stages in flight per CTA
+constexpr int kGemvWarps = 8;                      // consumer warps
+constexpr int kGemvThreads = (kGemvWarps + 1) * kWarp;  // + producer warp
+constexpr int kGemvConsumers = kGemvWarps * kWarp;
+constexpr int kGemvRows = 32;  // two 16-row tiles per work item
+constexpr int kStages = 4;     // bulk-copy stages in the ring
 
 __host__ __device__ constexpr size_t gemv_stage_bytes(int fmt) {
     return (size_t)kGemvWarps * block_bytes(fmt);
 }
-__host__ __device__ constexpr size_t gemv_smem_bytes(int fmt) {
-    return (size_t)kStages * 2 * gemv_stage_bytes(fmt) + kStages * 8;
+__host__ __device__ constexpr size_t gemv_smem_bytes(int fa, int fb) {
+    return (size_t)kStages * 2 *
+               (gemv_stage_bytes(fa) > gemv_stage_bytes(fb) ? gemv_stage_bytes(fa)
+                                                             : gemv_stage_bytes(fb)) +
+           2 * kStages * 8;
 }
 
 enum GemvEpilogue {
@@ -64,11 +74,377 @@ struct GemvSeg {
     int64_t w_stride;       // bytes between members
     int64_t xq_stride;      // halves between members' inputs
     int out_stride;         // output columns between members
-    int tiles;              // CTAs per member (set by the launcher)
+    int tiles;              // work items per member (set by the launcher)
 };
 
 constexpr int kMaxSegs = 6;
 
+// A launch: either a batch of static segments sharing format FA, or (moe = 1)
+// the grouped routed experts (seg[0], format FA, member = active[slot] -
+// expert_base, per-slot inputs / outputs) followed by the shared expert
+// (seg[1], format FB).
+struct GemvWork {
+    GemvSeg seg[kMaxSegs];
+    int nseg;
+    int moe;
+    int max_slots;
+    int expert_base;
+    const int *n_active;
+    const int *active;
+    int64_t in_slot_stride;   // halves between slots' xq inputs
+    int64_t out_slot_stride;  // floats (EPI_STORE) or halves (xq) between slots
+    int total_items;
+    int S;
+    float swiglu_limit;
+    int *err;
+};
+
+// A resolved work item.
+struct GemvItem {
+    const uint8_t *t0, *t1;
+    const __half *xq;
+    int kp, fmt, seg, member, row0;
+    int64_t out_shift;  // slot offset of the outputs
+};
+
+__device__ __forceinline__ int seg_items(const GemvSeg &s) {
+    int ntiles = (s.O + kTileRows - 1) / kTileRows;
+    return s.epi == EPI_SWIGLU_XQ ? ntiles : (ntiles + 1) / 2;
+}
+
+template <int FA, int FB>
+__device__ __forceinline__ bool resolve_item(const GemvWork &wk, int item, GemvItem &it) {
+    int si, member, tile;
+    it.out_shift = 0;
+    if (wk.moe) {
+        const GemvSeg &r = wk.seg[0];
+        int rt = r.tiles;
+        int routed_items = wk.max_slots * rt;
+        if (item < routed_items) {
+            int slot = item / rt;
+            if (slot >= *wk.n_active) return false;
+            si = 0;
+            tile = item % rt;
+            member = wk.active[slot] - wk.expert_base;
+            it.xq = r.xq + slot * wk.in_slot_stride;
+            it.out_shift = slot * wk.out_slot_stride;
+            it.fmt = FA;
+        } else {
+            si = 1;
+            tile = item - routed_items;
+            member = 0;
+            it.xq = wk.seg[1].xq;
+            it.fmt = FB;
+        }
+    } else {
+        si = 0;
+        while (si < wk.nseg - 1 && item >= wk.seg[si].tiles * wk.seg[si].count) {
+            item -= wk.seg[si].tiles * wk.seg[si].count;
+            ++si;
+        }
+        member = item / wk.seg[si].tiles;
+        tile = item % wk.seg[si].tiles;
+        it.xq = wk.seg[si].xq + member * wk.seg[si].xq_stride;
+        it.fmt = FA;
+    }
+    const GemvSeg &sg = wk.seg[si];
+    it.seg = si;
+    it.member = wk.moe ? 0 : member;
+    it.kp = sg.kp;
+    const uint8_t *w = sg.w + member * sg.w_stride;
+    const size_t tb = tile_bytes(it.fmt, sg.kp);
+    const int ntiles = (sg.O + kTileRows - 1) / kTileRows;
+    if (sg.epi == EPI_SWIGLU_XQ) {
+        it.row0 = tile * kTileRows;
+        it.t0 = w + (size_t)tile * tb;
+        it.t1 = sg.w2 + member * sg.w_stride + (size_t)tile * tb;
+    } else {
+        it.row0 = tile * 2 * kTileRows;
+        it.t0 = w + (size_t)(2 * tile) * tb;
+        it.t1 = 2 * tile + 1 < ntiles ? w + (size_t)(2 * tile + 1) * tb : nullptr;
+    }
+    return true;
+}
+
+// Consumes one chunk block per tile from shared memory and accumulates
+// the 2 x (16 x 8) partial tile of this warp.
+template <int FMT>
+__device__ __forceinline__ void gemv_chunk(const uint8_t *blk0, const uint8_t *blk1,
+                                           const uint4 (&b_raw)[8], float (&acc)[2][4]) {
+    constexpr int kMmas = FMT == FC_FMT_Q8 ? 4 : 8;
+    constexpr int kGroups = kMmas / 2;
+    const int lane = threadIdx.x & 31;
+    const int g = lane >> 2, j = lane & 3;
+    const uint8_t *blks[2] = {blk0, blk1};
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+        const uint8_t *blk = blks[t];
+        if (!blk) continue;
+        uint4 a_raw[2];
+        float scale[2][kGroups];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            int r = g + 8 * h;
+            a_raw[h] = *reinterpret_cast<const uint4 *>(blk + r * 64 + 16 * j);
+            const uint8_t *sp = blk + kBlockValueBytes + r * scale_row_bytes(FMT);
+            if (FMT == FC_FMT_Q8) {
+                __half2 hs = *reinterpret_cast<const __half2 *>(sp);
+                scale[h][0] = __low2float(hs);
+                scale[h][kGroups > 1 ? 1 : 0] = __high2float(hs);
+            } else if (FMT == FC_FMT_Q4) {
+                uint2 s4 = *reinterpret_cast<const uint2 *>(sp);
+                __half2 h0 = *reinterpret_cast<__half2 *>(&s4.x);
+                __half2 h1 = *reinterpret_cast<__half2 *>(&s4.y);
+                scale[h][0] = __low2float(h0);
+                scale[h][1] = __high2float(h0);
+                scale[h][kGroups > 2 ? 2 : 0] = __low2float(h1);
+                scale[h][kGroups > 3 ? 3 : 0] = __high2float(h1);
+            } else {
+                uint32_t s4 = *reinterpret_cast<const uint32_t *>(sp);
+#pragma unroll
+                for (int q = 0; q < kGroups; ++q) scale[h][q] = e8m0_to_float((s4 >> (8 * q)) & 0xFFu);
+            }
+        }
+        uint32_t regs[2][16];  // per row h: fp16x2 registers (index q)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const uint32_t words[4] = {a_raw[h].x, a_raw[h].y, a_raw[h].z, a_raw[h].w};
+            if (FMT == FC_FMT_Q8) {
+#pragma unroll
+                for (int wi = 0; wi < 4; ++wi) dequant_q8_word(words[wi], regs[h][2 * wi], regs[h][2 * wi + 1]);
+            } else if (FMT == FC_FMT_Q4) {
+#pragma unroll
+                for (int wi = 0; wi < 4; ++wi)
+#pragma unroll
+                    for (int sh = 0; sh < 4; ++sh) regs[h][4 * wi + sh] = dequant_q4_pair(words[wi], 4 * sh);
+            } else {
+#pragma unroll
+                for (int wi = 0; wi < 4; ++wi) {
+                    uint32_t o4[4];
+                    dequant_e2m1_word(words[wi], o4);
+#pragma unroll
+                    for (int p = 0; p < 4; ++p) regs[h][4 * wi + p] = o4[p];
+                }
+            }
+        }
+#pragma unroll
+        for (int q = 0; q < kGroups; ++q) {
+            float tmp[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+            for (int ii = 0; ii < 2; ++ii) {
+                int i = 2 * q + ii;
+                // a0 = row g (k slots 2j,2j+1), a1 = row g+8,
+                // a2 = row g (slots 2j+8, 2j+9), a3 = row g+8.
+                uint32_t a[4] = {regs[0][2 * i], regs[1][2 * i], regs[0][2 * i + 1], regs[1][2 * i + 1]};
+                mma_f16(tmp, a, b_raw[i].x, b_raw[i].y, tmp);
+                mma_f16(tmp, a, b_raw[i].z, b_raw[i].w, tmp);
+            }
+            acc[t][0] = fmaf(scale[0][q], tmp[0], acc[t][0]);
+            acc[t][1] = fmaf(scale[0][q], tmp[1], acc[t][1]);
+            acc[t][2] = fmaf(scale[1][q], tmp[2], acc[t][2]);
+            acc[t][3] = fmaf(scale[1][q], tmp[3], acc[t][3]);
+        }
+    }
+}
+
+__device__ __forceinline__ void consumer_sync() {
+    asm volatile("bar.sync 1, %0;\n" ::"n"(kGemvConsumers) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Applies the epilogue of segment `sg` to the finished tile `out` [32][8].
+__device__ __forceinline__ void gemv_epilogue(const GemvSeg &sg, const GemvItem &it, int S,
+                                              float limit, const float *out) {
+    int idx = threadIdx.x;  // consumer threads 0 .. 255
+    if (sg.epi == EPI_SWIGLU_XQ) {
+        if (idx >= 128) return;
+        int r = idx >> 3, s = idx & 7;
+        int o = it.row0 + r;
+        if (s >= S || o >= sg.O) return;
+        float gv = out[r * 8 + s], uv = out[(16 + r) * 8 + s];
+        if (limit > 0.0f) {  // moe_exec.h:55-60
+            gv = fminf(gv, limit);
+            uv = fminf(fmaxf(uv, -limit), limit);
+        }
+        store_xq(sg.yq + it.out_shift, sg.kpy, s, sg.col_off + it.member * sg.out_stride + o,
+                 silu(gv) * uv);
+        return;
+    }
+    int r = idx >> 3, s = idx & 7;
+    int o = it.row0 + r;
+    if (s >= S || o >= sg.O) return;
+    float v = out[r * 8 + s];
+    int col = it.member * sg.out_stride + o;
+    if (sg.epi == EPI_STORE) {
+        sg.y[it.out_shift + (size_t)s * sg.ldy + col] = v;
+    } else if (sg.epi == EPI_ADD) {
+        sg.y[it.out_shift + (size_t)s * sg.ldy + col] += v;
+    } else {
+        store_xq(sg.yq + it.out_shift, sg.kpy, s, sg.col_off + col, v);
+    }
+}
+
+template <int FA, int FB>
+__global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_constant__ GemvWork wk) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ float red[kGemvWarps * 2 * 32 * 4];
+    __shared__ float out[kGemvRows * 8];
+    constexpr size_t kSlotBytes = gemv_stage_bytes(FA) > gemv_stage_bytes(FB) ? gemv_stage_bytes(FA)
+                                                                              : gemv_stage_bytes(FB);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + kStages * 2 * kSlotBytes);
+    uint64_t *empty = full + kStages;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+    if (tid == 0) {
+        for (int i = 0; i < kStages; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], kGemvWarps);
+        }
+        mbar_fence_init();
+    }
+    __syncthreads();
+
+    if (warp == kGemvWarps) {
+        // ---------------- producer ----------------
+        if (lane != 0) return;
+        int idx = 0;
+        for (int item = blockIdx.x; item < wk.total_items; item += gridDim.x) {
+            GemvItem it;
+            if (!resolve_item<FA, FB>(wk, item, it)) continue;
+            const int blk = it.fmt == FA ? block_bytes(FA) : block_bytes(FB);
+            const int nchunks = chunk_count(it.fmt, it.kp);
+            const int nst = (nchunks + kGemvWarps - 1) / kGemvWarps;
+            for (int s = 0; s < nst; ++s, ++idx) {
+                const int slot = idx % kStages, round = idx / kStages;
+                if (round > 0) mbar_wait_bounded(&empty[slot], (uint32_t)((round - 1) & 1), wk.err);
+                const int c0 = s * kGemvWarps;
+                const uint32_t bytes = (uint32_t)(min(kGemvWarps, nchunks - c0) * blk);
+                mbar_expect_tx(&full[slot], bytes * (it.t1 ? 2u : 1u));
+                bulk_g2s(smem + (slot * 2) * kSlotBytes, it.t0 + (size_t)c0 * blk, bytes, &full[slot]);
+                if (it.t1)
+                    bulk_g2s(smem + (slot * 2 + 1) * kSlotBytes, it.t1 + (size_t)c0 * blk, bytes,
+                             &full[slot]);
+            }
+        }
+        return;
+    }
+
+    // ---------------- consumers ----------------
+    const int g = lane >> 2, j = lane & 3;
+    const bool has_b = g < wk.S;
+    int idx = 0;
+    for (int item = blockIdx.x; item < wk.total_items; item += gridDim.x) {
+        GemvItem it;
+        if (!resolve_item<FA, FB>(wk, item, it)) continue;
+        const bool fa = it.fmt == FA;
+        const int blk = fa ? block_bytes(FA) : block_bytes(FB);
+        const int kmmas = it.fmt == FC_FMT_Q8 ? 4 : 8;
+        const int nchunks = chunk_count(it.fmt, it.kp);
+        const int nst = (nchunks + kGemvWarps - 1) / kGemvWarps;
+        float acc[2][4];
+#pragma unroll
+        for (int t = 0; t < 2; ++t)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc[t][e] = 0.0f;
+        for (int s = 0; s < nst; ++s, ++idx) {
+            const int slot = idx % kStages, round = idx / kStages;
+            const int c = s * kGemvWarps + warp;
+            uint4 b_raw[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                if (has_b && c < nchunks && i < kmmas)
+                    b_raw[i] = ldg_v4(it.xq + ((size_t)g * it.kp + 16 * (kmmas * c + i) + 4 * j) * 2);
+                else
+                    b_raw[i] = make_uint4(0, 0, 0, 0);
+            }
+            mbar_wait_bounded(&full[slot], (uint32_t)(round & 1), wk.err);
+            if (c < nchunks) {
+                const uint8_t *b0 = smem + (slot * 2) * kSlotBytes + (size_t)warp * blk;
+                const uint8_t *b1 = it.t1 ? smem + (slot * 2 + 1) * kSlotBytes + (size_t)warp * blk : nullptr;
+                if (fa) gemv_chunk<FA>(b0, b1, b_raw, acc);
+                else gemv_chunk<FB>(b0, b1, b_raw, acc);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+        }
+        // fixed-order reduction over the consumer warps
+#pragma unroll
+        for (int t = 0; t < 2; ++t)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) red[((warp * 2 + t) * 32 + lane) * 4 + e] = acc[t][e];
+        consumer_sync();
+        {
+            int t = tid >> 7, l = (tid >> 2) & 31, e = tid & 3;
+            float sum = 0.0f;
+#pragma unroll
+            for (int w = 0; w < kGemvWarps; ++w) sum += red[((w * 2 + t) * 32 + l) * 4 + e];
+            int row = 16 * t + (l >> 2) + 8 * (e >> 1);
+            int col = 2 * (l & 3) + (e & 1);
+            out[row * 8 + col] = sum;
+        }
+        consumer_sync();
+        gemv_epilogue(wk.seg[it.seg], it, wk.S, wk.swiglu_limit, out);
+    }
+}
+
+inline int gemv_tiles(const GemvSeg &s) {
+    int ntiles = (s.O + kTileRows - 1) / kTileRows;
+    return s.epi == EPI_SWIGLU_XQ ? ntiles : (ntiles + 1) / 2;
+}
+
+#define FC_GEMV_FORMATS(X)         \
+    X(FC_FMT_Q8, FC_FMT_Q8)        \
+    X(FC_FMT_Q4, FC_FMT_Q4)        \
+    X(FC_FMT_MXFP4, FC_FMT_MXFP4)  \
+    X(FC_FMT_MXFP4, FC_FMT_Q8)     \
+    X(FC_FMT_Q4, FC_FMT_Q8)        \
+    X(FC_FMT_Q8, FC_FMT_Q4)
+
+// Opts the GEMV kernels into their dynamic shared memory (once per device,
+// before launching or capturing).
+inline cudaError_t gemv_prepare_all() {
+    cudaError_t e = cudaSuccess;
+#define FC_GEMV_ATTR(A, B)                                                                    \
+    if (e == cudaSuccess)                                                                     \
+        e = cudaFuncSetAttribute(gemv_kernel<A, B>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                 (int)gemv_smem_bytes(A, B));
+    FC_GEMV_FORMATS(FC_GEMV_ATTR)
+#undef FC_GEMV_ATTR
+    return e;
+}
+
+constexpr int kGemvCtasPerSm = 2;
+
+inline cudaError_t launch_gemv_work(int fa, int fb, GemvWork &wk, int sms, cudaStream_t stream) {
+    int items = 0;
+    if (wk.moe) {
+        wk.seg[0].tiles = gemv_tiles(wk.seg[0]);
+        wk.seg[1].tiles = wk.seg[1].w ? gemv_tiles(wk.seg[1]) : 0;
+        items = wk.max_slots * wk.seg[0].tiles + wk.seg[1].tiles;
+    } else {
+        for (int i = 0; i < wk.nseg; ++i) {
+            if (wk.seg[i].count <= 0) wk.seg[i].count = 1;
+            wk.seg[i].tiles = gemv_tiles(wk.seg[i]);
+            items += wk.seg[i].tiles * wk.seg[i].count;
+        }
+    }
+    wk.total_items = items;
+    if (items == 0) return cudaSuccess;
+    int grid = std::min(items, sms * kGemvCtasPerSm);
+#define FC_GEMV_CASE(A, B)                                                               \
+    if (fa == A && fb == B) {                                                            \
+        gemv_kernel<A, B><<<grid, kGemvThreads, gemv_smem_bytes(A, B), stream>>>(wk);    \
+        return cudaGetLastError();                                                       \
+    }
+    FC_GEMV_FORMATS(FC_GEMV_CASE)
+#undef FC_GEMV_CASE
+    return cudaErrorInvalidValue;
+}
+
+// Batch of static segments sharing one format.
 struct GemvBatch {
     GemvSeg seg[kMaxSegs];
     int nseg;
@@ -77,280 +453,14 @@ struct GemvBatch {
     int *err;
 };
 
-// Streams tiles t0 / t1 (nullptr = absent) of padded width kp through shared
-// memory and leaves the reduced 32 x 8 tile (rows 0-15 from t0, 16-31 from
-// t1, columns = activation rows) in `out`.
-template <int FMT>
-__device__ __forceinline__ void gemv_tile(const uint8_t *t0, const uint8_t *t1, int kp,
-                                          const __half *xq, int S, uint8_t *smem, float *red,
-                                          float *out, int *err) {
-    constexpr int kBlock = block_bytes(FMT);
-    constexpr size_t kStageBytes = gemv_stage_bytes(FMT);
-    constexpr int kMmas = FMT == FC_FMT_Q8 ? 4 : 8;  // MMAs per chunk
-    constexpr int kGroups = kMmas / 2;               // scale groups per chunk
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int g = lane >> 2, j = lane & 3;
-    const int nchunks = chunk_count(FMT, kp);
-    const int nstages = (nchunks + kGemvWarps - 1) / kGemvWarps;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kStages * 2 * kStageBytes);
-    const uint8_t *src[2] = {t0, t1};
-
-    if (tid == 0) {
-        for (int i = 0; i < kStages; ++i) mbar_init(&bars[i], 1);
-        mbar_fence_init();
-    }
-    __syncthreads();
-    auto issue = [&](int s) {
-        int slot = s % kStages;
-        int c0 = s * kGemvWarps;
-        int nc = min(kGemvWarps, nchunks - c0);
-        uint32_t bytes = (uint32_t)(nc * kBlock);
-        uint32_t total = bytes * ((t0 ? 1u : 0u) + (t1 ? 1u : 0u));
-        mbar_expect_tx(&bars[slot], total);
-        for (int t = 0; t < 2; ++t)
-            if (src[t])
-                bulk_g2s(smem + (slot * 2 + t) * kStageBytes, src[t] + (size_t)c0 * kBlock, bytes,
-                         &bars[slot]);
-    };
-    if (tid == 0)
-        for (int s = 0; s < min(kStages, nstages); ++s) issue(s);
-
-    const bool has_b = g < S;
-    float acc[2][4];
-#pragma unroll
-    for (int t = 0; t < 2; ++t)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) acc[t][e] = 0.0f;
-
-    for (int s = 0; s < nstages; ++s) {
-        const int slot = s % kStages;
-        const int c = s * kGemvWarps + warp;
-        // B fragments (activations, L2-resident) are fetched before the wait
-        uint4 b_raw[kMmas];
-#pragma unroll
-        for (int i = 0; i < kMmas; ++i) {
-            if (has_b && c < nchunks)
-                b_raw[i] = ldg_v4(xq + ((size_t)g * kp + 16 * (kMmas * c + i) + 4 * j) * 2);
-            else
-                b_raw[i] = make_uint4(0, 0, 0, 0);
-        }
-        mbar_wait_bounded(&bars[slot], (uint32_t)((s / kStages) & 1), err);
-        if (c < nchunks) {
-#pragma unroll
-            for (int t = 0; t < 2; ++t) {
-                if (!src[t]) continue;
-                const uint8_t *blk = smem + (slot * 2 + t) * kStageBytes + (size_t)warp * kBlock;
-                uint4 a_raw[2];
-                float scale[2][kGroups];
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    int r = g + 8 * h;
-                    a_raw[h] = *reinterpret_cast<const uint4 *>(blk + r * 64 + 16 * j);
-                    const uint8_t *sp = blk + kBlockValueBytes + r * scale_row_bytes(FMT);
-                    if (FMT == FC_FMT_Q8) {
-                        __half2 hs = *reinterpret_cast<const __half2 *>(sp);
-                        scale[h][0] = __low2float(hs);
-                        scale[h][kGroups > 1 ? 1 : 0] = __high2float(hs);
-                    } else if (FMT == FC_FMT_Q4) {
-                        uint2 s4 = *reinterpret_cast<const uint2 *>(sp);
-                        __half2 h0 = *reinterpret_cast<__half2 *>(&s4.x);
-                        __half2 h1 = *reinterpret_cast<__half2 *>(&s4.y);
-                        scale[h][0] = __low2float(h0);
-                        scale[h][1] = __high2float(h0);
-                        scale[h][kGroups > 2 ? 2 : 0] = __low2float(h1);
-                        scale[h][kGroups > 3 ? 3 : 0] = __high2float(h1);
-                    } else {
-                        uint32_t s4 = *reinterpret_cast<const uint32_t *>(sp);
-#pragma unroll
-                        for (int q = 0; q < kGroups; ++q)
-                            scale[h][q] = e8m0_to_float((s4 >> (8 * q)) & 0xFFu);
-                    }
-                }
-                uint32_t regs[2][16];  // per row h: fp16x2 registers (index q)
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const uint32_t words[4] = {a_raw[h].x, a_raw[h].y, a_raw[h].z, a_raw[h].w};
-                    if (FMT == FC_FMT_Q8) {
-#pragma unroll
-                        for (int wi = 0; wi < 4; ++wi)
-                            dequant_q8_word(words[wi], regs[h][2 * wi], regs[h][2 * wi + 1]);
-                    } else if (FMT == FC_FMT_Q4) {
-#pragma unroll
-                        for (int wi = 0; wi < 4; ++wi)
-#pragma unroll
-                            for (int sh = 0; sh < 4; ++sh)
-                                regs[h][4 * wi + sh] = dequant_q4_pair(words[wi], 4 * sh);
-                    } else {
-#pragma unroll
-                        for (int wi = 0; wi < 4; ++wi) {
-                            uint32_t o4[4];
-                            dequant_e2m1_word(words[wi], o4);
-#pragma unroll
-                            for (int p = 0; p < 4; ++p) regs[h][4 * wi + p] = o4[p];
-                        }
-                    }
-                }
-#pragma unroll
-                for (int q = 0; q < kGroups; ++q) {
-                    float tmp[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll
-                    for (int ii = 0; ii < 2; ++ii) {
-                        int i = 2 * q + ii;
-                        // a0 = row g (k slots 2j,2j+1), a1 = row g+8,
-                        // a2 = row g (slots 2j+8, 2j+9), a3 = row g+8.
-                        uint32_t a[4] = {regs[0][2 * i], regs[1][2 * i], regs[0][2 * i + 1],
-                                         regs[1][2 * i + 1]};
-                        mma_f16(tmp, a, b_raw[i].x, b_raw[i].y, tmp);
-                        mma_f16(tmp, a, b_raw[i].z, b_raw[i].w, tmp);
-                    }
-                    acc[t][0] = fmaf(scale[0][q], tmp[0], acc[t][0]);
-                    acc[t][1] = fmaf(scale[0][q], tmp[1], acc[t][1]);
-                    acc[t][2] = fmaf(scale[1][q], tmp[2], acc[t][2]);
-                    acc[t][3] = fmaf(scale[1][q], tmp[3], acc[t][3]);
-                }
-            }
-        }
-        __syncthreads();  // every warp is done with this slot
-        if (tid == 0 && s + kStages < nstages) issue(s + kStages);
-    }
-
-    // ---- fixed-order reduction over warps ----
-#pragma unroll
-    for (int t = 0; t < 2; ++t)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) red[((warp * 2 + t) * 32 + lane) * 4 + e] = acc[t][e];
-    __syncthreads();
-    {
-        int idx = threadIdx.x;  // 256 threads -> 2 tiles x 32 lanes x 4
-        int t = idx >> 7, l = (idx >> 2) & 31, e = idx & 3;
-        float sum = 0.0f;
-#pragma unroll
-        for (int w = 0; w < kGemvWarps; ++w) sum += red[((w * 2 + t) * 32 + l) * 4 + e];
-        int row = 16 * t + (l >> 2) + 8 * (e >> 1);
-        int col = 2 * (l & 3) + (e & 1);
-        out[row * 8 + col] = sum;
-    }
-    __syncthreads();
-}
-
-// Applies the epilogue of `sg` to the finished tile `out` [32][8] whose first
-// row is `row0` of member matrix `member`.
-__device__ __forceinline__ void gemv_epilogue(const GemvSeg &sg, int member, int row0, int S,
-                                              float limit, const float *out) {
-    int idx = threadIdx.x;
-    if (sg.epi == EPI_SWIGLU_XQ) {
-        if (idx >= 128) return;
-        int r = idx >> 3, s = idx & 7;
-        int o = row0 + r;
-        if (s >= S || o >= sg.O) return;
-        float gv = out[r * 8 + s], uv = out[(16 + r) * 8 + s];
-        if (limit > 0.0f) {  // moe_exec.h:55-60
-            gv = fminf(gv, limit);
-            uv = fminf(fmaxf(uv, -limit), limit);
-        }
-        store_xq(sg.yq, sg.kpy, s, sg.col_off + member * sg.out_stride + o, silu(gv) * uv);
-        return;
-    }
-    int r = idx >> 3, s = idx & 7;
-    int o = row0 + r;
-    if (s >= S || o >= sg.O) return;
-    float v = out[r * 8 + s];
-    int col = member * sg.out_stride + o;
-    if (sg.epi == EPI_STORE) {
-        sg.y[(size_t)s * sg.ldy + col] = v;
-    } else if (sg.epi == EPI_ADD) {
-        sg.y[(size_t)s * sg.ldy + col] += v;
-    } else {
-        store_xq(sg.yq, sg.kpy, s, sg.col_off + col, v);
-    }
-}
-
-// CTA `tile` of a member matrix: the two tile streams and the first row.
-template <int FMT>
-__device__ __forceinline__ void seg_tiles(const GemvSeg &sg, const uint8_t *w, const uint8_t *w2,
-                                          int tile, const uint8_t *&t0, const uint8_t *&t1,
-                                          int &row0) {
-    const size_t tb = tile_bytes(FMT, sg.kp);
-    const int ntiles = (sg.O + kTileRows - 1) / kTileRows;
-    if (sg.epi == EPI_SWIGLU_XQ) {
-        row0 = tile * kTileRows;
-        t0 = w + (size_t)tile * tb;
-        t1 = w2 + (size_t)tile * tb;
-    } else {
-        row0 = tile * 2 * kTileRows;
-        t0 = w + (size_t)(2 * tile) * tb;
-        t1 = 2 * tile + 1 < ntiles ? w + (size_t)(2 * tile + 1) * tb : nullptr;
-    }
-}
-
-template <int FMT>
-__global__ void __launch_bounds__(kGemvThreads, 2) gemv_batch_kernel(const __grid_constant__ GemvBatch b) {
-    extern __shared__ __align__(128) uint8_t gemv_smem[];
-    __shared__ float red[kGemvWarps * 2 * 32 * 4];
-    __shared__ float out[kGemvRows * 8];
-    int block = blockIdx.x;
-    int si = 0;
-    while (si < b.nseg - 1 && block >= b.seg[si].tiles * b.seg[si].count) {
-        block -= b.seg[si].tiles * b.seg[si].count;
-        ++si;
-    }
-    const GemvSeg &sg = b.seg[si];
-    int member = block / sg.tiles, tile = block % sg.tiles;
-    const uint8_t *w = sg.w + member * sg.w_stride;
-    const uint8_t *w2 = sg.w2 ? sg.w2 + member * sg.w_stride : nullptr;
-    const __half *xq = sg.xq + member * sg.xq_stride;
-    const uint8_t *t0, *t1;
-    int row0;
-    seg_tiles<FMT>(sg, w, w2, tile, t0, t1, row0);
-    gemv_tile<FMT>(t0, t1, sg.kp, xq, b.S, gemv_smem, red, out, b.err);
-    gemv_epilogue(sg, member, row0, b.S, b.swiglu_limit, out);
-}
-
-inline int gemv_tiles(const GemvSeg &s) {
-    int ntiles = (s.O + kTileRows - 1) / kTileRows;
-    return s.epi == EPI_SWIGLU_XQ ? ntiles : (ntiles + 1) / 2;
-}
-
-// Opts the GEMV kernels into their dynamic shared memory (call once per
-// device before launching or capturing).
-inline cudaError_t gemv_prepare_all() {
-    cudaError_t e = cudaFuncSetAttribute(gemv_batch_kernel<FC_FMT_Q8>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)gemv_smem_bytes(FC_FMT_Q8));
-    if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(gemv_batch_kernel<FC_FMT_Q4>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)gemv_smem_bytes(FC_FMT_Q4));
-    if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(gemv_batch_kernel<FC_FMT_MXFP4>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)gemv_smem_bytes(FC_FMT_MXFP4));
-    return e;
-}
-
-// Launches one batch of segments that share a weight format.
-inline cudaError_t launch_gemv_batch(int fmt, GemvBatch &b, cudaStream_t stream) {
-    int blocks = 0;
-    for (int i = 0; i < b.nseg; ++i) {
-        if (b.seg[i].count <= 0) b.seg[i].count = 1;
-        b.seg[i].tiles = gemv_tiles(b.seg[i]);
-        blocks += b.seg[i].tiles * b.seg[i].count;
-    }
-    if (blocks == 0) return cudaSuccess;
-    switch (fmt) {
-        case FC_FMT_Q8:
-            gemv_batch_kernel<FC_FMT_Q8><<<blocks, kGemvThreads, gemv_smem_bytes(FC_FMT_Q8), stream>>>(b);
-            break;
-        case FC_FMT_Q4:
-            gemv_batch_kernel<FC_FMT_Q4><<<blocks, kGemvThreads, gemv_smem_bytes(FC_FMT_Q4), stream>>>(b);
-            break;
-        case FC_FMT_MXFP4:
-            gemv_batch_kernel<FC_FMT_MXFP4><<<blocks, kGemvThreads, gemv_smem_bytes(FC_FMT_MXFP4), stream>>>(b);
-            break;
-        default:
-            return cudaErrorInvalidValue;
-    }
-    return cudaGetLastError();
+inline cudaError_t launch_gemv_batch(int fmt, GemvBatch &b, int sms, cudaStream_t stream) {
+    GemvWork wk{};
+    for (int i = 0; i < b.nseg; ++i) wk.seg[i] = b.seg[i];
+    wk.nseg = b.nseg;
+    wk.S = b.S;
+    wk.swiglu_limit = b.swiglu_limit;
+    wk.err = b.err;
+    return launch_gemv_work(fmt, fmt, wk, sms, stream);
 }
 
 }  // namespace fc

@@ -191,95 +191,6 @@ __global__ void route_select_kernel(const float *logits, RouteParams p) {
     }
 }
 
-// Grouped expert GEMV.  Blocks [0, max_slots * routed_tiles) serve the
-// routed slots (slot >= *n_active exits), the rest serve the shared expert.
-// Routed member = active[slot] - expert_base; inputs / outputs are per slot.
-struct MoeGemv {
-    GemvSeg routed;          // w / w2 at local expert 0; w_stride per expert
-    GemvSeg shared;          // static segment (w == nullptr: none)
-    int max_slots;
-    int routed_tiles;
-    int shared_tiles;
-    int expert_base;         // first local expert id
-    const int *n_active;
-    const int *active;
-    int64_t in_slot_stride;  // halves between slots' xq inputs (0 = shared input)
-    int64_t out_slot_stride; // routed outputs: floats (EPI_STORE) or halves (xq)
-    int S;
-    float swiglu_limit;
-    int *err;
-};
-
-template <int FE, int FS>
-__global__ void __launch_bounds__(kGemvThreads, 2) moe_gemv_kernel(const __grid_constant__ MoeGemv m) {
-    extern __shared__ __align__(128) uint8_t gemv_smem[];
-    __shared__ float red[kGemvWarps * 2 * 32 * 4];
-    __shared__ float out[kGemvRows * 8];
-    int block = blockIdx.x;
-    int routed_blocks = m.max_slots * m.routed_tiles;
-    const uint8_t *t0, *t1;
-    int row0;
-    if (block < routed_blocks) {
-        int slot = block / m.routed_tiles, tile = block % m.routed_tiles;
-        if (slot >= *m.n_active) return;
-        int e = m.active[slot] - m.expert_base;
-        GemvSeg sg = m.routed;
-        const uint8_t *w = sg.w + e * sg.w_stride;
-        const uint8_t *w2 = sg.w2 ? sg.w2 + e * sg.w_stride : nullptr;
-        seg_tiles<FE>(sg, w, w2, tile, t0, t1, row0);
-        gemv_tile<FE>(t0, t1, sg.kp, sg.xq + slot * m.in_slot_stride, m.S, gemv_smem, red, out, m.err);
-        if (sg.epi == EPI_SWIGLU_XQ) sg.yq = sg.yq + slot * m.out_slot_stride;
-        else sg.y = sg.y + slot * m.out_slot_stride;
-        gemv_epilogue(sg, 0, row0, m.S, m.swiglu_limit, out);
-        return;
-    }
-    block -= routed_blocks;
-    if (block >= m.shared_tiles) return;
-    const GemvSeg &sg = m.shared;
-    seg_tiles<FS>(sg, sg.w, sg.w2, block, t0, t1, row0);
-    gemv_tile<FS>(t0, t1, sg.kp, sg.xq, m.S, gemv_smem, red, out, m.err);
-    gemv_epilogue(sg, 0, row0, m.S, m.swiglu_limit, out);
-}
-
-constexpr size_t moe_smem_bytes(int fe, int fs) {
-    return gemv_smem_bytes(fe) > gemv_smem_bytes(fs) ? gemv_smem_bytes(fe) : gemv_smem_bytes(fs);
-}
-
-#define FC_MOE_FORMATS(X)                 \
-    X(FC_FMT_Q8, FC_FMT_Q8)               \
-    X(FC_FMT_Q4, FC_FMT_Q4)               \
-    X(FC_FMT_MXFP4, FC_FMT_Q8)            \
-    X(FC_FMT_Q4, FC_FMT_Q8)               \
-    X(FC_FMT_MXFP4, FC_FMT_MXFP4)         \
-    X(FC_FMT_Q8, FC_FMT_Q4)
-
-inline cudaError_t moe_prepare_all() {
-    cudaError_t e = cudaSuccess;
-#define FC_MOE_ATTR(A, B)                                                                         \
-    if (e == cudaSuccess)                                                                         \
-        e = cudaFuncSetAttribute(moe_gemv_kernel<A, B>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                                 (int)moe_smem_bytes(A, B));
-    FC_MOE_FORMATS(FC_MOE_ATTR)
-#undef FC_MOE_ATTR
-    return e;
-}
-
-inline cudaError_t launch_moe_gemv(int fe, int fs, MoeGemv &m, cudaStream_t stream) {
-    if (m.routed.count <= 0) m.routed.count = 1;
-    m.routed_tiles = gemv_tiles(m.routed);
-    m.shared_tiles = m.shared.w ? gemv_tiles(m.shared) : 0;
-    int blocks = m.max_slots * m.routed_tiles + m.shared_tiles;
-    if (blocks == 0) return cudaSuccess;
-#define FC_MOE_CASE(A, B)                                                                \
-    if (fe == A && fs == B) {                                                            \
-        moe_gemv_kernel<A, B><<<blocks, kGemvThreads, moe_smem_bytes(A, B), stream>>>(m); \
-        return cudaGetLastError();                                                       \
-    }
-    FC_MOE_FORMATS(FC_MOE_CASE)
-#undef FC_MOE_CASE
-    return cudaErrorInvalidValue;
-}
-
 // resid[s][d] += (sum over slots ascending of coef * routed[slot][s][d])
 //                + shared[s][d]                           (moe_exec.h:97-110)
 // Products and sums are rounded separately (no contraction), the order the

@@ -91,6 +91,7 @@ struct TensorRef {
 struct FcModel {
     FcModelConfig c{};
     int device = 0;
+    int sms = 148;                     // multiprocessors of the device
     int expert_lo = 0, expert_hi = 0;  // local routed experts
     std::string device_name;
     uint8_t *arena = nullptr;
@@ -450,14 +451,14 @@ GemvSeg seg_of(const DevMat &mm, const __half *xq, int epi) {
         if (e_ != cudaSuccess) return e_;            \
     } while (0)
 
-cudaError_t gemv1(int fmt, GemvSeg a, int S, float limit, int *err, cudaStream_t st) {
+cudaError_t gemv1(int fmt, GemvSeg a, int S, float limit, int *err, int sms, cudaStream_t st) {
     GemvBatch b{};
     b.seg[0] = a;
     b.nseg = 1;
     b.S = S;
     b.swiglu_limit = limit;
     b.err = err;
-    return launch_gemv_batch(fmt, b, st);
+    return launch_gemv_batch(fmt, b, sms, st);
 }
 
 // Records a profiling event after the launch named `name` (eager passes only).
@@ -511,7 +512,7 @@ cudaError_t record_forward(FcSession *s, int S) {
             b.seg[1].y = s->ckv;
             b.seg[1].ldy = L + R;
             b.nseg = 2;
-            FC_TRY(launch_gemv_batch(df, b, st));
+            FC_TRY(launch_gemv_batch(df, b, m->sms, st));
             mark(s, "gemv_q_kv_a");
         }
         if (c.q_lora_rank > 0) {
@@ -522,7 +523,7 @@ cudaError_t record_forward(FcSession *s, int S) {
             GemvSeg g = seg_of(y.q_b, s->qa_xq, EPI_STORE);
             g.y = s->q;
             g.ldy = H * QW;
-            FC_TRY(gemv1(df, g, S, 0.0f, s->d_err, st));
+            FC_TRY(gemv1(df, g, S, 0.0f, s->d_err, m->sms, st));
             mark(s, "gemv_q_b");
         }
         mla_prep_kernel<<<S, 256, 0, st>>>(s->ckv, s->q, y.kv_a_norm.p, L, R, H, NP,
@@ -564,14 +565,14 @@ cudaError_t record_forward(FcSession *s, int S) {
             g.yq = s->o_xq;
             g.kpy = kpO;
             g.out_stride = VD;
-            FC_TRY(gemv1(df, g, S, 0.0f, s->d_err, st));
+            FC_TRY(gemv1(df, g, S, 0.0f, s->d_err, m->sms, st));
             mark(s, "gemv_w_uv");
         }
         {
             GemvSeg g = seg_of(y.o_proj, s->o_xq, EPI_ADD);
             g.y = s->resid;
             g.ldy = D;
-            FC_TRY(gemv1(df, g, S, 0.0f, s->d_err, st));
+            FC_TRY(gemv1(df, g, S, 0.0f, s->d_err, m->sms, st));
             mark(s, "gemv_o_proj");
         }
         rmsnorm_kernel<<<S, 256, 0, st>>>(s->resid, D, y.ffn_norm.p, D, c.rms_norm_epsilon,
@@ -583,12 +584,12 @@ cudaError_t record_forward(FcSession *s, int S) {
             g.w2 = y.d_up.w;
             g.yq = s->hd_xq;
             g.kpy = kpI;
-            FC_TRY(gemv1(df, g, S, 0.0f, s->d_err, st));
+            FC_TRY(gemv1(df, g, S, 0.0f, s->d_err, m->sms, st));
             mark(s, "gemv_dense_gate_up");
             GemvSeg d = seg_of(y.d_down, s->hd_xq, EPI_ADD);
             d.y = s->resid;
             d.ldy = D;
-            FC_TRY(gemv1(df, d, S, 0.0f, s->d_err, st));
+            FC_TRY(gemv1(df, d, S, 0.0f, s->d_err, m->sms, st));
             mark(s, "gemv_dense_down");
         } else {
             int E = c.expert_count, K = c.experts_per_token;
@@ -614,50 +615,54 @@ cudaError_t record_forward(FcSession *s, int S) {
             mark(s, "route_select");
             int I = c.moe_intermediate_size, kpI = kpad(I);
             int W = I * c.shared_expert_count, kpW = kpad(std::max(W, 1));
-            // gate / up + SwiGLU
-            MoeGemv gu{};
-            gu.routed = seg_of(y.e_gate, s->xq_norm, EPI_SWIGLU_XQ);
-            gu.routed.w2 = y.e_up.w;
-            gu.routed.w_stride = (int64_t)y.e_gate.w_bytes;
-            gu.expert_base = m->expert_lo;
-            gu.err = s->d_err;
-            gu.routed.yq = s->h_xq;
-            gu.routed.kpy = kpI;
+            // gate / up + SwiGLU of the active routed experts and the shared expert
+            GemvWork gu{};
+            gu.moe = 1;
+            gu.seg[0] = seg_of(y.e_gate, s->xq_norm, EPI_SWIGLU_XQ);
+            gu.seg[0].w2 = y.e_up.w;
+            gu.seg[0].w_stride = (int64_t)y.e_gate.w_bytes;
+            gu.seg[0].yq = s->h_xq;
+            gu.seg[0].kpy = kpI;
             if (y.s_gate.count) {
-                gu.shared = seg_of(y.s_gate, s->xq_norm, EPI_SWIGLU_XQ);
-                gu.shared.w2 = y.s_up.w;
-                gu.shared.yq = s->hsh_xq;
-                gu.shared.kpy = kpW;
+                gu.seg[1] = seg_of(y.s_gate, s->xq_norm, EPI_SWIGLU_XQ);
+                gu.seg[1].w2 = y.s_up.w;
+                gu.seg[1].yq = s->hsh_xq;
+                gu.seg[1].kpy = kpW;
             }
+            gu.nseg = 2;
             gu.max_slots = s->max_slots;
+            gu.expert_base = m->expert_lo;
             gu.n_active = s->n_active;
             gu.active = s->active;
             gu.in_slot_stride = 0;
             gu.out_slot_stride = (int64_t)mb * kpI * 2;
             gu.S = S;
             gu.swiglu_limit = c.swiglu_limit;
-            FC_TRY(launch_moe_gemv(ef, df, gu, st));
+            gu.err = s->d_err;
+            FC_TRY(launch_gemv_work(ef, df, gu, m->sms, st));
             mark(s, "moe_gate_up");
-            // down
-            MoeGemv dn{};
-            dn.routed = seg_of(y.e_down, s->h_xq, EPI_STORE);
-            dn.routed.w_stride = (int64_t)y.e_down.w_bytes;
-            dn.expert_base = m->expert_lo;
-            dn.err = s->d_err;
-            dn.routed.y = s->moe_part;
-            dn.routed.ldy = D;
+            // down projections
+            GemvWork dn{};
+            dn.moe = 1;
+            dn.seg[0] = seg_of(y.e_down, s->h_xq, EPI_STORE);
+            dn.seg[0].w_stride = (int64_t)y.e_down.w_bytes;
+            dn.seg[0].y = s->moe_part;
+            dn.seg[0].ldy = D;
             if (y.s_down.count) {
-                dn.shared = seg_of(y.s_down, s->hsh_xq, EPI_STORE);
-                dn.shared.y = s->sh_part;
-                dn.shared.ldy = D;
+                dn.seg[1] = seg_of(y.s_down, s->hsh_xq, EPI_STORE);
+                dn.seg[1].y = s->sh_part;
+                dn.seg[1].ldy = D;
             }
+            dn.nseg = 2;
             dn.max_slots = s->max_slots;
+            dn.expert_base = m->expert_lo;
             dn.n_active = s->n_active;
             dn.active = s->active;
             dn.in_slot_stride = (int64_t)mb * kpI * 2;
             dn.out_slot_stride = (int64_t)mb * D;
             dn.S = S;
-            FC_TRY(launch_moe_gemv(ef, df, dn, st));
+            dn.err = s->d_err;
+            FC_TRY(launch_gemv_work(ef, df, dn, m->sms, st));
             mark(s, "moe_down");
             moe_combine_kernel<<<(S * D + 255) / 256, 256, 0, st>>>(
                 s->resid, s->moe_part, y.s_down.count ? s->sh_part : nullptr, s->coef, s->n_active,
@@ -677,7 +682,7 @@ cudaError_t record_forward(FcSession *s, int S) {
         GemvSeg g = seg_of(m->lm_head, s->xq_norm, EPI_STORE);
         g.y = s->logits;
         g.ldy = c.vocab_size;
-        FC_TRY(gemv1(df, g, S, 0.0f, s->d_err, st));
+        FC_TRY(gemv1(df, g, S, 0.0f, s->d_err, m->sms, st));
         mark(s, "gemv_lm_head");
     }
     {
@@ -836,6 +841,7 @@ int fc_model_create(FcModel **out, const FcModelConfig *config, int device, char
     m->c = *config;
     m->device = device;
     m->device_name = prop.name;
+    m->sms = prop.multiProcessorCount;
     m->expert_lo = 0;
     m->expert_hi = config->expert_count;
     if (!build_model(m, error, error_size)) {
@@ -862,6 +868,7 @@ int fc_model_create_ep(FcModel **out, const FcModelConfig *config, int device, i
     m->c = *config;
     m->device = device;
     m->device_name = prop.name;
+    m->sms = prop.multiProcessorCount;
     int per = config->expert_count / world;
     m->expert_lo = rank * per;
     m->expert_hi = rank * per + per;
@@ -1055,7 +1062,7 @@ int fc_session_create(FcSession **out, FcModel *m, const FcOptions *options, cha
                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
                                               2 * 8 * 1024 * 4);
         ok = e1 == cudaSuccess && e2 == cudaSuccess && e3 == cudaSuccess &&
-             gemv_prepare_all() == cudaSuccess && moe_prepare_all() == cudaSuccess;
+             gemv_prepare_all() == cudaSuccess;
     }
     if (!ok) {
         free_session_buffers(s);
@@ -1385,7 +1392,10 @@ extern "C" int fc_matmul(int format, float *y, const float *x, const void *value
         g.w = dw;
         g.y = dy;
         g.ldy = O;
-        e = gemv1(format, g, S, 0.0f, derr, 0);
+        int dev = 0, sms = 148;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        e = gemv1(format, g, S, 0.0f, derr, sms, 0);
         if (e == cudaSuccess) e = cudaDeviceSynchronize();
         if (e == cudaSuccess) e = cudaMemcpy(y, dy, (size_t)S * O * 4, cudaMemcpyDeviceToHost);
         if (e == cudaSuccess) e = cudaMemcpy(&herr, derr, 4, cudaMemcpyDeviceToHost);
