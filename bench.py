@@ -46,6 +46,8 @@ def parse():
     ap.add_argument("--draft", type=int, default=3)
     ap.add_argument("--profile-passes", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=None,
+                    help="override layer_count (small profiling cases only)")
     ap.add_argument("--out", default=None, help="also write the JSON line here")
     return ap.parse_args()
 
@@ -275,6 +277,8 @@ def run_ours(args, d):
     import floyd_b200
     from floyd_b200.configs import CONFIGS
     cfg = dict(CONFIGS[args.config])
+    if args.layers:
+        cfg["layer_count"] = args.layers
     cfg["_name"] = args.config
     rows = args.draft + 1
     ctx0 = cfg["context"]
@@ -336,7 +340,8 @@ def run_ours(args, d):
     e2e = total_emitted / wall_max
 
     # per-kernel profile (eager passes with CUDA events on the session stream)
-    sess.set_profiling(True)
+    if args.profile_passes > 0:
+        sess.set_profiling(True)
     sess.profile_reset()
     for i in range(args.profile_passes):
         ids = make_ids(stream, o, plans[-1], V)
@@ -344,7 +349,8 @@ def run_ours(args, d):
         sess.verify(ids)
         sess.rollback(p0)
     prof = sess.profile()
-    sess.set_profiling(False)
+    if args.profile_passes > 0:
+        sess.set_profiling(False)
     layers = cfg["layer_count"]
     moe_layers = [l for l in range(cfg["first_dense_layer_count"], layers)]
     actives = []
