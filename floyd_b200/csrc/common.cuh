@@ -91,21 +91,15 @@ __device__ __forceinline__ uint32_t dequant_q4_pair(uint32_t w, int shift) {
     return hsub2_bits(t, 0x64086408u);
 }
 
-// e2m1 codes: magnitudes {0, .5, 1, 1.5, 2, 3, 4, 6} have fp16 encodings whose
-// low byte is zero; their high bytes form this 8-entry table.
-constexpr uint32_t kE2m1Lo = 0x3E3C3800u;
-constexpr uint32_t kE2m1Hi = 0x46444240u;
-
-// One 32-bit word of 8 e2m1 codes (code p at bits 4p) -> 4 fp16x2 registers;
-// register p holds codes (p, p + 4).
+// One 32-bit word of 4 bytes of e2m1 code pairs -> 4 fp16x2 registers with
+// Blackwell's hardware conversion (exact: every e2m1 value is an fp16);
+// register b holds (low nibble, high nibble) of byte b.
 __device__ __forceinline__ void dequant_e2m1_word(uint32_t w, uint32_t (&out)[4]) {
-    uint32_t ra = prmt(kE2m1Lo, kE2m1Hi, w & 0x7777u);
-    uint32_t rb = prmt(kE2m1Lo, kE2m1Hi, (w >> 16) & 0x7777u);
-    // byte0 / byte2: sign-replicate of a table byte (always < 0x80) -> 0x00.
-    out[0] = prmt(ra, rb, 0x4808u) | ((w << 12) & 0x80008000u);
-    out[1] = prmt(ra, rb, 0x5919u) | ((w << 8) & 0x80008000u);
-    out[2] = prmt(ra, rb, 0x6A2Au) | ((w << 4) & 0x80008000u);
-    out[3] = prmt(ra, rb, 0x7B3Bu) | (w & 0x80008000u);
+    asm("{\n .reg .b8 b0, b1, b2, b3;\n mov.b32 {b0, b1, b2, b3}, %4;\n"
+        " cvt.rn.f16x2.e2m1x2 %0, b0;\n cvt.rn.f16x2.e2m1x2 %1, b1;\n"
+        " cvt.rn.f16x2.e2m1x2 %2, b2;\n cvt.rn.f16x2.e2m1x2 %3, b3;\n}\n"
+        : "=r"(out[0]), "=r"(out[1]), "=r"(out[2]), "=r"(out[3])
+        : "r"(w));
 }
 
 __device__ __forceinline__ float e8m0_to_float(uint32_t code) {
@@ -143,10 +137,13 @@ __device__ __forceinline__ float silu(float x) { return x / (1.0f + expf(-x)); }
 //     MMA covers a single 32-column scale group:
 //       q8:   column r (0..63): MMA i = r/16, thread j = (r%16)/4, b = r%4
 //             byte = 16j + 4i + b
-//       q4 / e2m1: column r (0..127): MMA i = r/16, j = (r%16)/4, b = r%4,
+//       q4:   column r (0..127): MMA i = r/16, j = (r%16)/4, b = r%4,
 //             h = b/2, e = b%2; register q = 2i + h; word = q/4;
 //             nibble slot = q%4 + 4e; byte = 16j + 4*word + slot/2,
-//             nibble = slot%2
+//             nibble = slot%2   (shift-and-mask decode, two values a word
+//             apart land in one fp16x2 register)
+//       e2m1: same i, j, h, e; byte = 16j + q, nibble = e, so each byte is
+//             exactly one fp16x2 A register for cvt.rn.f16x2.e2m1x2
 // ---------------------------------------------------------------------------
 constexpr int kTileRows = 16;
 constexpr int kBlockValueBytes = kTileRows * 64;
@@ -179,6 +176,11 @@ __host__ __device__ inline void inner_position(int fmt, int r, int &byte, int &n
     }
     int i = r >> 4, j = (r & 15) >> 2, b = r & 3;
     int q = 2 * i + (b >> 1), e = b & 1;
+    if (fmt == FC_FMT_MXFP4) {
+        byte = 16 * j + q;
+        nibble = e;
+        return;
+    }
     int word = q >> 2;
     int slot = (q & 3) + 4 * e;
     byte = 16 * j + 4 * word + (slot >> 1);
