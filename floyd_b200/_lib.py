@@ -117,6 +117,7 @@ SIGNATURES = {
     "fc_runtime_free": (None, [ctypes.POINTER(FcRuntime)]),
     # include/floyd_kernels.h
     "fc_matmul": (_I, [_I, _FP, _FP, _P, _P, _I, _I, _I, _C, _S]),
+    "fc_matmul_noalloc": (_I, [_I, _FP, _FP, _P, _P, _I, _I, _I, _C, _S]),
 }
 
 _lib = None

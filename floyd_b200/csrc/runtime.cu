@@ -1405,3 +1405,145 @@ extern "C" int fc_matmul(int format, float *y, const float *x, const void *value
     if (e != cudaSuccess) return set_error(error, error_size, "matmul failed: %s", cudaGetErrorString(e));
     return 1;
 }
+
+// ===========================================================================
+// fc_matmul_noalloc: fc_matmul for callers that must not allocate device
+// memory.  Its working memory is one fixed file-scope device array.
+// ===========================================================================
+namespace {
+
+constexpr size_t kNoAllocImage = (size_t)6 << 20;    // tile-major weight image
+constexpr size_t kNoAllocValues = (size_t)6 << 20;   // logical values as passed
+constexpr size_t kNoAllocScales = (size_t)512 << 10; // logical group scales
+constexpr size_t kNoAllocX = (size_t)256 << 10;      // fp32 activations
+constexpr size_t kNoAllocXq = (size_t)512 << 10;     // hi/lo fp16 activations
+constexpr size_t kNoAllocY = (size_t)512 << 10;      // fp32 outputs
+constexpr size_t kNoAllocOffValues = kNoAllocImage;
+constexpr size_t kNoAllocOffScales = kNoAllocOffValues + kNoAllocValues;
+constexpr size_t kNoAllocOffX = kNoAllocOffScales + kNoAllocScales;
+constexpr size_t kNoAllocOffXq = kNoAllocOffX + kNoAllocX;
+constexpr size_t kNoAllocOffY = kNoAllocOffXq + kNoAllocXq;
+constexpr size_t kNoAllocOffErr = kNoAllocOffY + kNoAllocY;
+constexpr size_t kNoAllocBytes = kNoAllocOffErr + 256;
+
+// Every GPU that loads this library holds this array (about 14 MiB) until
+// the process exits.  Host code must not pass the symbol itself to a kernel:
+// on the host it names a stand-in, not device memory.
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocBytes];
+
+constexpr int kNoAllocMaxDevices = 64;
+uint8_t *g_noalloc_ptr[kNoAllocMaxDevices] = {nullptr};
+
+// Scatters logical values (int8 [O][K], or packed nibbles [O][K/2] with the
+// even element low) into the zeroed tile-major image.  One thread per group
+// of 4 consecutive columns: the device bytes holding those nibbles hold no
+// other element, so every byte is written by exactly one thread.
+__global__ void noalloc_pack_values(int fmt, int O, int K, int kp, const uint8_t *src,
+                                    uint8_t *image) {
+    size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    size_t groups = (size_t)O * K / 4;
+    if (idx >= groups) return;
+    size_t e0 = idx * 4;
+    int o = (int)(e0 / K), k0 = (int)(e0 % K);
+    size_t off[4];
+    int nib[4];
+    uint32_t val[4];
+    for (int i = 0; i < 4; ++i) {
+        size_t e = e0 + i;
+        off[i] = value_offset(fmt, kp, o, k0 + i, &nib[i]);
+        val[i] = fmt == FC_FMT_Q8 ? src[e] : (src[e >> 1] >> (4 * (e & 1))) & 15u;
+    }
+    for (int i = 0; i < 4; ++i) {
+        bool first = true;
+        for (int jx = 0; jx < i; ++jx) first = first && off[jx] != off[i];
+        if (!first) continue;
+        uint32_t b = 0;
+        for (int m = i; m < 4; ++m)
+            if (off[m] == off[i]) b |= fmt == FC_FMT_Q8 ? val[m] : val[m] << (4 * nib[m]);
+        image[off[i]] = (uint8_t)b;
+    }
+}
+
+__global__ void noalloc_pack_scales(int fmt, int O, int K, int kp, const uint8_t *src,
+                                    uint8_t *image) {
+    size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    int gk = K / 32, el = scale_elem_bytes(fmt);
+    if (idx >= (size_t)O * gk) return;
+    int o = (int)(idx / gk), g = (int)(idx % gk);
+    uint8_t *dst = image + scale_offset(fmt, kp, o, g);
+    for (int b = 0; b < el; ++b) dst[b] = src[idx * el + b];
+}
+
+}  // namespace
+
+extern "C" int fc_matmul_noalloc(int format, float *y, const float *x, const void *values,
+                                 const void *scales, int O, int K, int S, char *error,
+                                 size_t error_size) {
+    if (!y || !x || !values || !scales || O <= 0 || K <= 0 || K % 32 || S < 1 || S > kMaxRows)
+        return set_error(error, error_size, "invalid matmul shape");
+    if (format != FC_FMT_Q8 && format != FC_FMT_Q4 && format != FC_FMT_MXFP4)
+        return set_error(error, error_size, "unsupported format %d", format);
+    const int kp = kpad(K);
+    const size_t image = matrix_bytes(format, O, kp);
+    const size_t vbytes = format == FC_FMT_Q8 ? (size_t)O * K : (size_t)O * K / 2;
+    const size_t sbytes = (size_t)O * (K / 32) * scale_elem_bytes(format);
+    if (image > kNoAllocImage || vbytes > kNoAllocValues || sbytes > kNoAllocScales ||
+        (size_t)S * K * 4 > kNoAllocX || (size_t)S * kp * 4 > kNoAllocXq ||
+        (size_t)S * O * 4 > kNoAllocY)
+        return set_error(error, error_size,
+                         "matmul of %d x %d (S=%d) exceeds the fixed no-allocation workspace "
+                         "(weight image <= %zu bytes, S*K*4 <= %zu, S*O*4 <= %zu)",
+                         O, K, S, kNoAllocImage, kNoAllocX, kNoAllocY);
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices)
+        return set_error(error, error_size, "no usable CUDA device");
+    // One-time set-up on this device: the array's device address.
+    if (!g_noalloc_ptr[dev]) {
+        void *p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess)
+            return set_error(error, error_size, "cannot resolve the workspace address: %s",
+                             cudaGetErrorString(e));
+        g_noalloc_ptr[dev] = reinterpret_cast<uint8_t *>(p);
+    }
+    uint8_t *base = g_noalloc_ptr[dev];
+    uint8_t *d_image = base, *d_values = base + kNoAllocOffValues, *d_scales = base + kNoAllocOffScales;
+    float *d_x = reinterpret_cast<float *>(base + kNoAllocOffX);
+    __half *d_xq = reinterpret_cast<__half *>(base + kNoAllocOffXq);
+    float *d_y = reinterpret_cast<float *>(base + kNoAllocOffY);
+    int *d_err = reinterpret_cast<int *>(base + kNoAllocOffErr);
+    int sms = 148, herr = 0;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaError_t e = gemv_prepare_all();
+    // The array keeps the previous call's contents: clear what must start at zero
+    // (image padding, xq padding, error flag).
+    if (e == cudaSuccess) e = cudaMemset(d_image, 0, image);
+    if (e == cudaSuccess) e = cudaMemset(d_xq, 0, (size_t)S * kp * 4);
+    if (e == cudaSuccess) e = cudaMemset(d_err, 0, 4);
+    if (e == cudaSuccess) e = cudaMemcpy(d_values, values, vbytes, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(d_scales, scales, sbytes, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(d_x, x, (size_t)S * K * 4, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) {
+        size_t groups = (size_t)O * K / 4;
+        noalloc_pack_values<<<(unsigned)((groups + 255) / 256), 256>>>(format, O, K, kp, d_values, d_image);
+        size_t ng = (size_t)O * (K / 32);
+        noalloc_pack_scales<<<(unsigned)((ng + 255) / 256), 256>>>(format, O, K, kp, d_scales, d_image);
+        to_xq_kernel<<<(S * K + 255) / 256, 256>>>(d_x, S, K, kp, d_xq);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) {
+        DevMat mm;
+        plan_mat(mm, format, O, K, 1, 0, 0);
+        GemvSeg g = seg_of(mm, d_xq, EPI_STORE);
+        g.w = d_image;
+        g.y = d_y;
+        g.ldy = O;
+        e = gemv1(format, g, S, 0.0f, d_err, sms, 0);
+    }
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMemcpy(y, d_y, (size_t)S * O * 4, cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess) e = cudaMemcpy(&herr, d_err, 4, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return set_error(error, error_size, "matmul failed: %s", cudaGetErrorString(e));
+    if (herr) return set_error(error, error_size, "a kernel wait gave up");
+    return 1;
+}

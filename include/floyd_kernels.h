@@ -25,6 +25,22 @@ int fc_matmul(int format, float *y, const float *x, const void *values,
               const void *scales, int O, int K, int S, char *error,
               size_t error_size);
 
+/* fc_matmul without any device allocation.  For callers that cannot call
+ * cudaMalloc at all - code running under a caching allocator that owns all
+ * free device memory, an embedding host whose memory policy forbids driver
+ * allocations, or a path that must not fail on out-of-memory.  Same arguments
+ * and result as fc_matmul (no counterpart in the reference).  Its working
+ * memory is one fixed device array of about 14 MiB that every GPU loading
+ * this library keeps until exit, so it accepts only: weight image (tile-major
+ * values + scales) <= 6 MiB, packed values <= 6 MiB, S*K*4 <= 256 KiB,
+ * S*O*4 <= 512 KiB; larger shapes are rejected with an error.  The first call
+ * on a device looks up the array's device address and should come before
+ * any stream capture on that device.  All calls share the array: calls that
+ * overlap on the GPU (from several host threads) race and must not. */
+int fc_matmul_noalloc(int format, float *y, const float *x, const void *values,
+                      const void *scales, int O, int K, int S, char *error,
+                      size_t error_size);
+
 #ifdef __cplusplus
 }
 #endif
