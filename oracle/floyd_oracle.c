@@ -637,6 +637,79 @@ static void add_expert(const Mat *gate, const Mat *up, const Mat *down, const fl
     for (int d = 0; d < D; ++d) out[d] += coefficient * p[d];
 }
 
+/* moe_f32_forward for one token (moe_exec.h:65-114): router matvec, select or
+ * fixed routes, finalize, routed experts accumulated in ascending expert id,
+ * then the shared expert with coefficient 1.  y must start at zero. */
+static int moe_row(const FcModelConfig *c, const Mat *router, const float *bias,
+                   const int *fixed, const Mat *gate, const Mat *up, const Mat *down,
+                   const Mat *sh_gate, const Mat *sh_up, const Mat *sh_down, const float *xr,
+                   float *y, int *routes, float *lg, float *tmp) {
+    int E = c->expert_count, K = c->experts_per_token;
+    int idx[64], order[64];
+    float wt[64];
+    mat_apply(router, xr, 1, lg);
+    if (orc_route(lg, bias, E, K, c->score_fn, c->normalize_topk, c->routed_scale, fixed, idx,
+                  wt) != K)
+        return 0;
+    if (routes)
+        for (int k = 0; k < K; ++k) routes[k] = idx[k];
+    for (int k = 0; k < K; ++k) order[k] = k;
+    for (int a = 1; a < K; ++a) { /* insertion sort, moe_exec.h:97-105 */
+        int v = order[a], b = a - 1;
+        while (b >= 0 && idx[order[b]] > idx[v]) { order[b + 1] = order[b]; b--; }
+        order[b + 1] = v;
+    }
+    for (int k = 0; k < K; ++k) {
+        int e = idx[order[k]];
+        add_expert(&gate[e], &up[e], &down[e], xr, wt[order[k]], c->swiglu_limit, y, tmp);
+    }
+    if (sh_gate) add_expert(sh_gate, sh_up, sh_down, xr, 1.0f, c->swiglu_limit, y, tmp);
+    return 1;
+}
+
+static Mat f32_mat(int O, int K, const float *p) {
+    Mat m;
+    memset(&m, 0, sizeof(m));
+    m.fmt = FC_FMT_F32; m.O = O; m.K = K; m.f32 = (float *)p;
+    return m;
+}
+
+int orc_moe_forward_f32(int hidden, int intermediate, int n_experts, int top_k, int score_fn,
+                        int normalize, float routed_scale, float swiglu_limit,
+                        const float *router, const float *bias, const float *expert_weights,
+                        int n_shared, const float *shared_weights, const float *input,
+                        int n_tokens, float *output) {
+    if (n_experts > 1024 || top_k > 64 || n_shared > 1) return 0;
+    FcModelConfig c;
+    memset(&c, 0, sizeof(c));
+    c.expert_count = n_experts; c.experts_per_token = top_k; c.score_fn = score_fn;
+    c.normalize_topk = normalize; c.routed_scale = routed_scale; c.swiglu_limit = swiglu_limit;
+    size_t block = (size_t)hidden * intermediate;
+    Mat r = f32_mat(n_experts, hidden, router);
+    Mat *g = (Mat *)calloc((size_t)n_experts, sizeof(Mat));
+    Mat *u = (Mat *)calloc((size_t)n_experts, sizeof(Mat));
+    Mat *d = (Mat *)calloc((size_t)n_experts, sizeof(Mat));
+    for (int e = 0; e < n_experts; ++e) { /* w1 = gate, w2 = down, w3 = up */
+        g[e] = f32_mat(intermediate, hidden, expert_weights + (3 * (size_t)e) * block);
+        d[e] = f32_mat(hidden, intermediate, expert_weights + (3 * (size_t)e + 1) * block);
+        u[e] = f32_mat(intermediate, hidden, expert_weights + (3 * (size_t)e + 2) * block);
+    }
+    Mat sg = f32_mat(intermediate, hidden, shared_weights);
+    Mat sd = f32_mat(hidden, intermediate, n_shared ? shared_weights + block : NULL);
+    Mat su = f32_mat(intermediate, hidden, n_shared ? shared_weights + 2 * block : NULL);
+    float *lg = alloc_f((size_t)n_experts);
+    float *tmp = alloc_f((size_t)4 * intermediate + hidden);
+    int ok = 1;
+    for (int t = 0; t < n_tokens && ok; ++t) {
+        float *y = output + (size_t)t * hidden;
+        for (int i = 0; i < hidden; ++i) y[i] = 0.0f;
+        ok = moe_row(&c, &r, bias, NULL, g, u, d, n_shared ? &sg : NULL, &su, &sd,
+                     input + (size_t)t * hidden, y, NULL, lg, tmp);
+    }
+    free(g); free(u); free(d); free(lg); free(tmp);
+    return ok;
+}
+
 int orc_session_forward(OrcSession *s, const int *ids, int rows, float *logits,
                         float *layer_out, int *routes) {
     OrcModel *m = s->m;
@@ -771,32 +844,12 @@ int orc_session_forward(OrcSession *s, const int *ids, int rows, float *logits,
                 if (routes)
                     for (int k = 0; k < c->experts_per_token; ++k)
                         routes[((int64_t)l * rows + r) * c->experts_per_token + k] = -1;
-            } else { /* moe_f32_forward, moe_exec.h:65-114 */
-                int E = c->expert_count, K = c->experts_per_token;
-                float *lg = tmp + 4 * maxI;
-                int idx[64], order[64];
-                float wt[64];
-                mat_apply(&ly->router, xr, 1, lg);
-                const int *fixed = ly->hash ? ly->hash + (int64_t)ids[r] * K : NULL;
-                if (orc_route(lg, ly->bias, E, K, c->score_fn, c->normalize_topk,
-                              c->routed_scale, fixed, idx, wt) != K) goto fail;
-                if (routes)
-                    for (int k = 0; k < K; ++k)
-                        routes[((int64_t)l * rows + r) * K + k] = idx[k];
-                for (int k = 0; k < K; ++k) order[k] = k;
-                for (int a = 1; a < K; ++a) {
-                    int v = order[a], b = a - 1;
-                    while (b >= 0 && idx[order[b]] > idx[v]) { order[b + 1] = order[b]; b--; }
-                    order[b + 1] = v;
-                }
-                for (int k = 0; k < K; ++k) {
-                    int e = idx[order[k]];
-                    add_expert(&ly->gate[e], &ly->up[e], &ly->down[e], xr, wt[order[k]],
-                               c->swiglu_limit, y, tmp);
-                }
-                if (c->shared_expert_count > 0)
-                    add_expert(&ly->sh_gate, &ly->sh_up, &ly->sh_down, xr, 1.0f,
-                               c->swiglu_limit, y, tmp);
+            } else {
+                const int *fixed = ly->hash ? ly->hash + (int64_t)ids[r] * c->experts_per_token : NULL;
+                int *rt = routes ? routes + ((int64_t)l * rows + r) * c->experts_per_token : NULL;
+                if (!moe_row(c, &ly->router, ly->bias, fixed, ly->gate, ly->up, ly->down,
+                             c->shared_expert_count > 0 ? &ly->sh_gate : NULL, &ly->sh_up,
+                             &ly->sh_down, xr, y, rt, tmp + 4 * maxI, tmp)) goto fail;
             }
             for (int d = 0; d < D; ++d) x[(int64_t)r * D + d] += y[d];
         }

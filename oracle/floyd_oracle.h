@@ -79,6 +79,14 @@ int orc_accept_sample(const float *logits, int V, const int *ids, int k,
 float orc_accept_uniform(uint64_t seed, uint64_t counter, int row);
 float orc_gumbel(uint64_t seed, uint64_t counter, int row, int v);
 
+/* moe_f32_forward (moe_exec.h:65-114) on fp32 experts laid out like the
+ * reference harness: per expert [w1 gate I x D][w2 down D x I][w3 up I x D]. */
+int orc_moe_forward_f32(int hidden, int intermediate, int n_experts, int top_k, int score_fn,
+                        int normalize, float routed_scale, float swiglu_limit,
+                        const float *router, const float *bias, const float *expert_weights,
+                        int n_shared, const float *shared_weights, const float *input,
+                        int n_tokens, float *output);
+
 /* ---- model ---------------------------------------------------------------- */
 
 typedef struct OrcModel OrcModel;
