@@ -143,79 +143,83 @@ __global__ void head_partial_kernel(const float *logits, int V, const Staging *s
     }
 }
 
-// One block.  Final argmax per row (chunk order), acceptance, result record
-// and, when `last_logits` is set, the logits row commit-1.
-__global__ void accept_kernel(const float *logits, int V, const Staging *st, HeadPartials hp,
-                              int chunks, Result *res, float *last_logits, int *err) {
-    __shared__ int commit_s;
-    int rows = st->rows;
-    if (threadIdx.x == 0) {
-        int tops[kMaxRows];
-        for (int r = 0; r < rows; ++r) {
-            float bv = -INFINITY; int bi = -1;
-            for (int c = 0; c < chunks; ++c) {
-                size_t o = (size_t)r * chunks + c;
-                int idx = hp.aidx[o];
-                if (idx == 0x7fffffff) continue;
-                if (bi < 0 || better(hp.amax[o], idx, bv, bi)) { bv = hp.amax[o]; bi = idx; }
+// One block of 256 threads.  Warp r reduces row r's per-chunk partials in
+// parallel (the (value, index) order is total, so the result does not depend
+// on the reduction shape); thread 0 then applies the acceptance rule and
+// writes the result record.
+__global__ void __launch_bounds__(256) accept_kernel(const float *logits, int V, const Staging *st,
+                                                     HeadPartials hp, int chunks, Result *res,
+                                                     int *err) {
+    __shared__ int tops[kMaxRows], picks[kMaxRows];
+    __shared__ float zmax_row[kMaxRows], den_row[kMaxRows];
+    const int rows = st->rows, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const bool sample = st->k >= 0 && st->mode == FC_ACCEPT_SAMPLE;
+    if (warp < rows) {
+        const int r = warp;
+        float bv = -INFINITY, gv = -INFINITY, M = -INFINITY;
+        int bi = 0x7fffffff, gi = 0x7fffffff;
+        for (int c = lane; c < chunks; c += 32) {
+            size_t o = (size_t)r * chunks + c;
+            if (better(hp.amax[o], hp.aidx[o], bv, bi)) { bv = hp.amax[o]; bi = hp.aidx[o]; }
+            if (sample) {
+                if (better(hp.gval[o], hp.gidx[o], gv, gi)) { gv = hp.gval[o]; gi = hp.gidx[o]; }
+                M = fmaxf(M, hp.zmax[o]);
             }
-            tops[r] = bi;
-            res->row_tops[r] = bi;
         }
-        int k = st->k;
-        int commit = rows, next = tops[rows - 1];
-        if (k >= 0 && st->mode == FC_ACCEPT_SAMPLE) {
-            float temp = st->temperature;
-            auto gumbel_pick = [&](int r) {
-                float bv = -INFINITY; int bi = -1;
-                for (int c = 0; c < chunks; ++c) {
-                    size_t o = (size_t)r * chunks + c;
-                    int idx = hp.gidx[o];
-                    if (idx == 0x7fffffff) continue;
-                    if (bi < 0 || better(hp.gval[o], idx, bv, bi)) { bv = hp.gval[o]; bi = idx; }
-                }
-                return bi;
-            };
-            commit = k + 1;
-            next = -1;
-            for (int i = 1; i <= k; ++i) {
-                int r = i - 1;
-                float M = -INFINITY;
-                for (int c = 0; c < chunks; ++c) M = fmaxf(M, hp.zmax[(size_t)r * chunks + c]);
-                float den = 0.0f;
-                for (int c = 0; c < chunks; ++c) {
-                    float zm = hp.zmax[(size_t)r * chunks + c];
-                    if (zm != -INFINITY) den += expf(zm - M) * hp.zsum[(size_t)r * chunks + c];
-                }
-                int x = st->ids[i];
-                float p = expf(logits[(size_t)r * V + x] / temp - M) / den;
-                float u = accept_uniform(st->seed, st->counter, r);
-                if (!(u < p)) {
-                    commit = i;
-                    next = gumbel_pick(r);
-                    break;
-                }
-            }
-            if (next < 0) next = gumbel_pick(k);
-        } else if (k >= 0) {
-            commit = 1;
-            for (int i = 1; i <= k; ++i) {
-                if (tops[i - 1] != st->ids[i]) break;
-                commit++;
-            }
-            next = tops[commit - 1];
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+            int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+            if (better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
+            float og = __shfl_xor_sync(0xffffffffu, gv, off);
+            int ogi = __shfl_xor_sync(0xffffffffu, gi, off);
+            if (better(og, ogi, gv, gi)) { gv = og; gi = ogi; }
+            M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
         }
-        res->commit = commit;
-        res->next_token = next;
-        res->error = *err;
-        *err = 0;
-        commit_s = commit;
+        float den = 0.0f;
+        if (sample)
+            for (int c = lane; c < chunks; c += 32) {
+                float zm = hp.zmax[(size_t)r * chunks + c];
+                if (zm != -INFINITY) den += expf(zm - M) * hp.zsum[(size_t)r * chunks + c];
+            }
+        den = warp_sum(den);
+        if (lane == 0) {
+            tops[r] = bi == 0x7fffffff ? -1 : bi;
+            picks[r] = gi == 0x7fffffff ? -1 : gi;
+            zmax_row[r] = M;
+            den_row[r] = den;
+        }
     }
     __syncthreads();
-    if (last_logits) {
-        const float *src = logits + (size_t)(commit_s - 1) * V;
-        for (int v = threadIdx.x; v < V; v += blockDim.x) last_logits[v] = src[v];
+    if (threadIdx.x != 0) return;
+    for (int r = 0; r < rows; ++r) res->row_tops[r] = tops[r];
+    const int k = st->k;
+    int commit = rows, next = tops[rows - 1];
+    if (sample) {
+        commit = k + 1;
+        next = picks[k];
+        for (int i = 1; i <= k; ++i) {
+            const int r = i - 1, x = st->ids[i];
+            float p = expf(logits[(size_t)r * V + x] / st->temperature - zmax_row[r]) / den_row[r];
+            float u = accept_uniform(st->seed, st->counter, r);
+            if (!(u < p)) {
+                commit = i;
+                next = picks[r];
+                break;
+            }
+        }
+    } else if (k >= 0) {
+        commit = 1;
+        for (int i = 1; i <= k; ++i) {
+            if (tops[i - 1] != st->ids[i]) break;
+            commit++;
+        }
+        next = tops[commit - 1];
     }
+    res->commit = commit;
+    res->next_token = next;
+    res->error = *err;
+    *err = 0;
 }
 
 }  // namespace fc

@@ -62,20 +62,55 @@ __device__ __forceinline__ float block_sum(float v, float *scratch) {
     return t;
 }
 
-__global__ void rmsnorm_kernel(const float *x, int ldx, const float *w, int D, float eps,
-                               __half *yq, int kpy, float *y, int ldy) {
+// One block per row, one float4 per thread per pass (D / 4 <= 4 * blockDim):
+// a single read of the row, the sum of squares reduced in a fixed order,
+// then 16-byte xq records (and optionally fp32) written back.
+constexpr int kNormThreads = 1024;
+
+__global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const float *x, int ldx, const float *w,
+                                                               int D, float eps, __half *yq, int kpy,
+                                                               float *y, int ldy) {
     __shared__ float scratch[32];
-    int s = blockIdx.x;
-    const float *xs = x + (size_t)s * ldx;
+    const int s = blockIdx.x, n4 = D / 4;
+    const float4 *xs = reinterpret_cast<const float4 *>(x + (size_t)s * ldx);
+    float4 v[4];
     float ss = 0.0f;
-    for (int k = threadIdx.x; k < D; k += blockDim.x) ss += xs[k] * xs[k];
-    ss = block_sum(ss, scratch);
-    float scale = 1.0f / sqrtf(ss / (float)D + eps);
-    for (int k = threadIdx.x; k < D; k += blockDim.x) {
-        float v = xs[k] * scale * w[k];
-        if (yq) store_xq(yq, kpy, s, k, v);
-        if (y) y[(size_t)s * ldy + k] = v;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        int k4 = threadIdx.x + i * blockDim.x;
+        if (k4 < n4) {
+            v[i] = xs[k4];
+            ss += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
+        }
     }
+    ss = block_sum(ss, scratch);
+    const float scale = 1.0f / sqrtf(ss / (float)D + eps);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        int k4 = threadIdx.x + i * blockDim.x;
+        if (k4 >= n4) continue;
+        float4 wv = reinterpret_cast<const float4 *>(w)[k4];
+        float o[4] = {v[i].x * scale * wv.x, v[i].y * scale * wv.y, v[i].z * scale * wv.z,
+                      v[i].w * scale * wv.w};
+        if (yq) {
+            __half hi[4], lo[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) split_hi_lo(o[e], hi[e], lo[e]);
+            uint4 rec;
+            rec.x = (uint32_t)__half_as_ushort(hi[0]) | ((uint32_t)__half_as_ushort(hi[1]) << 16);
+            rec.y = (uint32_t)__half_as_ushort(hi[2]) | ((uint32_t)__half_as_ushort(hi[3]) << 16);
+            rec.z = (uint32_t)__half_as_ushort(lo[0]) | ((uint32_t)__half_as_ushort(lo[1]) << 16);
+            rec.w = (uint32_t)__half_as_ushort(lo[2]) | ((uint32_t)__half_as_ushort(lo[3]) << 16);
+            *reinterpret_cast<uint4 *>(yq + ((size_t)s * kpy + 4 * k4) * 2) = rec;
+        }
+        if (y) *reinterpret_cast<float4 *>(y + (size_t)s * ldy + 4 * k4) = make_float4(o[0], o[1], o[2], o[3]);
+    }
+}
+
+inline int norm_threads(int D) {
+    int t = (D / 4 + 3) / 4;  // at most 4 float4 per thread
+    t = (t + 31) / 32 * 32;
+    return t < 32 ? 32 : (t > kNormThreads ? kNormThreads : t);
 }
 
 // ---------------------------------------------------------------------------
@@ -92,37 +127,42 @@ __device__ __forceinline__ void rope_pair(float first, float second, int p, int 
     out_b = second * c + first * sn;
 }
 
+// grid (S, 1 + ceil(H * R/2 / blockDim)): block y == 0 appends the KV row,
+// blocks y >= 1 rotate a slice of the heads' query rope pairs.
 __global__ void mla_prep_kernel(const float *ckv, const float *q, const float *norm_w, int L,
                                 int R, int H, int nope, float eps, float theta,
                                 const int *d_pos, __half *cache, __half *qcat) {
     __shared__ float scratch[32];
-    int s = blockIdx.x;
-    int position = *d_pos + s;
-    const float *src = ckv + (size_t)s * (L + R);
-    float ss = 0.0f;
-    for (int i = threadIdx.x; i < L; i += blockDim.x) ss += src[i] * src[i];
-    ss = block_sum(ss, scratch);
-    float scale = 1.0f / sqrtf(ss / (float)L + eps);
-    __half *dst = cache + (size_t)position * (L + R);
-    for (int i = threadIdx.x; i < L; i += blockDim.x)
-        dst[i] = __float2half_rn(src[i] * scale * norm_w[i]);
-    int half = R / 2;
-    for (int p = threadIdx.x; p < half; p += blockDim.x) {
-        float a, b;
-        rope_pair(src[L + 2 * p], src[L + 2 * p + 1], p, R, position, theta, a, b);
-        dst[L + p] = __float2half_rn(a);
-        dst[L + half + p] = __float2half_rn(b);
+    const int s = blockIdx.x;
+    const int position = *d_pos + s;
+    const int half = R / 2;
+    if (blockIdx.y == 0) {
+        const float *src = ckv + (size_t)s * (L + R);
+        float ss = 0.0f;
+        for (int i = threadIdx.x; i < L; i += blockDim.x) ss += src[i] * src[i];
+        ss = block_sum(ss, scratch);
+        float scale = 1.0f / sqrtf(ss / (float)L + eps);
+        __half *dst = cache + (size_t)position * (L + R);
+        for (int i = threadIdx.x; i < L; i += blockDim.x)
+            dst[i] = __float2half_rn(src[i] * scale * norm_w[i]);
+        for (int p = threadIdx.x; p < half; p += blockDim.x) {
+            float a, b;
+            rope_pair(src[L + 2 * p], src[L + 2 * p + 1], p, R, position, theta, a, b);
+            dst[L + p] = __float2half_rn(a);
+            dst[L + half + p] = __float2half_rn(b);
+        }
+        return;
     }
-    int qw = nope + R;
-    for (int t = threadIdx.x; t < H * half; t += blockDim.x) {
-        int h = t / half, p = t % half;
-        const float *qh = q + ((size_t)s * H + h) * qw + nope;
-        float a, b;
-        rope_pair(qh[2 * p], qh[2 * p + 1], p, R, position, theta, a, b);
-        __half *qo = qcat + ((size_t)s * H + h) * (L + R) + L;
-        qo[p] = __float2half_rn(a);
-        qo[half + p] = __float2half_rn(b);
-    }
+    const int qw = nope + R;
+    const int t = (blockIdx.y - 1) * blockDim.x + threadIdx.x;
+    if (t >= H * half) return;
+    const int h = t / half, p = t % half;
+    const float *qh = q + ((size_t)s * H + h) * qw + nope;
+    float a, b;
+    rope_pair(qh[2 * p], qh[2 * p + 1], p, R, position, theta, a, b);
+    __half *qo = qcat + ((size_t)s * H + h) * (L + R) + L;
+    qo[p] = __float2half_rn(a);
+    qo[half + p] = __float2half_rn(b);
 }
 
 // ---------------------------------------------------------------------------
@@ -141,22 +181,56 @@ __global__ void __launch_bounds__(256) mla_absorb_kernel(int fmt, const uint8_t 
                                                          __half *qcat) {
     __shared__ float wsm[kAbsorbMaxNope][kAbsorbCols + 1];
     __shared__ float qs[8][kAbsorbMaxNope];
+    __shared__ __align__(16) uint8_t raw[kAbsorbMaxNope / kTileRows][1152];
     const int h = blockIdx.x, l0 = blockIdx.y * kAbsorbCols;
     const int qw = nope + R;
+    const int cc = chunk_cols(fmt), blk = block_bytes(fmt);
+    const int c = l0 / cc, col0 = l0 % cc;
+    const int tile0 = h * (nope + vdim) / kTileRows, ntiles = nope / kTileRows;
+    const int nchunks = chunk_count(fmt, kp);
+    // the W_UK rows of this head and this column chunk: ntiles contiguous blocks
+    for (int i = threadIdx.x; i < ntiles * (blk / 16); i += blockDim.x) {
+        int t = i / (blk / 16), v = i % (blk / 16);
+        const uint4 *src = reinterpret_cast<const uint4 *>(
+            w + ((size_t)(tile0 + t) * nchunks + c) * blk);
+        reinterpret_cast<uint4 *>(raw[t])[v] = src[v];
+    }
     for (int i = threadIdx.x; i < S * nope; i += blockDim.x) {
         int s = i / nope, n = i % nope;
         qs[s][n] = q[((size_t)s * H + h) * qw + n];
     }
+    __syncthreads();
+    const int srb = scale_row_bytes(fmt), el = scale_elem_bytes(fmt);
     for (int i = threadIdx.x; i < nope * kAbsorbCols; i += blockDim.x) {
-        int n = i / kAbsorbCols, c = i % kAbsorbCols;
-        wsm[n][c] = dequant_element(fmt, w, kp, h * (nope + vdim) + n, l0 + c);
+        int n = i / kAbsorbCols, col = i % kAbsorbCols;
+        int r = col0 + col, byte, nib;
+        inner_position(fmt, r, byte, nib);
+        const uint8_t *b = raw[n / kTileRows];
+        int g = n % kTileRows;
+        uint8_t v = b[g * 64 + byte];
+        const uint8_t *sp = b + kBlockValueBytes + g * srb + (r / 32) * el;
+        float wv;
+        if (fmt == FC_FMT_Q8) {
+            wv = (float)(int8_t)v * __half2float(*reinterpret_cast<const __half *>(sp));
+        } else {
+            uint32_t code = (v >> (4 * nib)) & 15u;
+            if (fmt == FC_FMT_Q4) {
+                wv = (float)((int)code - 8) * __half2float(*reinterpret_cast<const __half *>(sp));
+            } else {
+                const float table[8] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};
+                float m = table[code & 7];
+                if (code & 8) m = -m;
+                wv = m * e8m0_to_float(*sp);
+            }
+        }
+        wsm[n][col] = wv;
     }
     __syncthreads();
     for (int o = threadIdx.x; o < S * kAbsorbCols; o += blockDim.x) {
-        int s = o / kAbsorbCols, c = o % kAbsorbCols;
+        int s = o / kAbsorbCols, col = o % kAbsorbCols;
         float acc = 0.0f;
-        for (int n = 0; n < nope; ++n) acc = __fadd_rn(acc, __fmul_rn(qs[s][n], wsm[n][c]));
-        qcat[((size_t)s * H + h) * (L + R) + l0 + c] = __float2half_rn(acc);
+        for (int n = 0; n < nope; ++n) acc = __fadd_rn(acc, __fmul_rn(qs[s][n], wsm[n][col]));
+        qcat[((size_t)s * H + h) * (L + R) + l0 + col] = __float2half_rn(acc);
     }
 }
 

@@ -83,39 +83,47 @@ __device__ __forceinline__ float route_score(float x, int fn) {
     return 1.0f / (1.0f + expf(-x));
 }
 
-// One block of 256 threads; warp s handles row s (S <= 8).
-__global__ void route_select_kernel(const float *logits, RouteParams p) {
+// One block of 256 threads; warp s handles row s (S <= 8).  Scores are
+// computed lane-parallel with fixed-order warp reductions, top-k by repeated
+// warp argmax (lower index on ties), finalize in slot order on lane 0; then
+// the ascending list of active local experts and their per-row coefficients
+// come from a block-wide scan.
+constexpr int kRouteThreads = 256;
+
+__global__ void __launch_bounds__(kRouteThreads) route_select_kernel(const float *logits, RouteParams p) {
     extern __shared__ float rs_smem[];  // scores [8][E], choice [8][E]
     __shared__ int used_flag[1024];
     __shared__ int slot_of[1024];
+    __shared__ int warp_total[kRouteThreads / 32];
     __shared__ int sel[8][64];
     __shared__ float selw[8][64];
     const int E = p.E, K = p.K;
     float *scores = rs_smem;
     float *choice = rs_smem + 8 * E;
-    int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int e = threadIdx.x; e < E; e += blockDim.x) used_flag[e] = 0;
-    // stage the logits in shared memory (choice[] doubles as the staging area)
     for (int i = threadIdx.x; i < p.S * E; i += blockDim.x) choice[i] = logits[i];
     __syncthreads();
     if (warp < p.S) {
-        int s = warp;
+        const int s = warp;
         float *lg = choice + s * E;
         float *sc = scores + s * E;
         float *ch = choice + s * E;
-        if (p.score_fn == FC_SCORE_SOFTMAX) {
-            // moe_route.h:26-37, sequential max and sum on lane 0
-            if (lane == 0) {
-                float m = lg[0];
-                for (int e = 1; e < E; ++e) if (lg[e] > m) m = lg[e];
-                float sum = 0.0f;
-                for (int e = 0; e < E; ++e) { sc[e] = expf(lg[e] - m); sum += sc[e]; }
-                for (int e = 0; e < E; ++e) sc[e] = sc[e] / sum;
+        if (p.score_fn == FC_SCORE_SOFTMAX) {  // moe_route.h:26-37
+            float m = -INFINITY;
+            for (int e = lane; e < E; e += 32) m = fmaxf(m, lg[e]);
+            m = warp_max(m);
+            float sum = 0.0f;
+            for (int e = lane; e < E; e += 32) {
+                float v = expf(lg[e] - m);
+                sc[e] = v;
+                sum += v;
             }
+            sum = warp_sum(sum);
             __syncwarp();
+            for (int e = lane; e < E; e += 32) sc[e] = sc[e] / sum;
         } else {
             for (int e = lane; e < E; e += 32) sc[e] = route_score(lg[e], p.score_fn);
-            __syncwarp();
         }
         __syncwarp();
         for (int e = lane; e < E; e += 32) ch[e] = sc[e] + (p.bias ? p.bias[e] : 0.0f);
@@ -151,43 +159,62 @@ __global__ void route_select_kernel(const float *logits, RouteParams p) {
         }
         __syncwarp();
         if (lane == 0) {  // moe_route_finalize, moe_route.h:89-99
-            float w[64];
-            for (int k = 0; k < K; ++k) w[k] = selw[s][k];
+            float sum = 0.0f;
             if (p.normalize) {
-                float sum = 0.0f;
-                for (int k = 0; k < K; ++k) sum += w[k];
+                for (int k = 0; k < K; ++k) sum += selw[s][k];
                 sum += 1e-20f;
-                for (int k = 0; k < K; ++k) w[k] = w[k] / sum;
             }
             for (int k = 0; k < K; ++k) {
-                w[k] = w[k] * p.routed_scale;
+                float w = p.normalize ? selw[s][k] / sum : selw[s][k];
+                w = w * p.routed_scale;
                 p.route_ids[s * K + k] = sel[s][k];
-                p.route_w[s * K + k] = w[k];
-                selw[s][k] = w[k];
+                p.route_w[s * K + k] = w;
+                selw[s][k] = w;
             }
         }
     }
     __syncthreads();
-    // Device-side grouping: ascending list of active local experts.
     if (threadIdx.x < p.S * K) {
         int s = threadIdx.x / K, k = threadIdx.x % K;
         int e = sel[s][k];
-        if (e >= p.expert_lo && e < p.expert_hi) used_flag[e] = 1;
+        if (e >= p.expert_lo && e < p.expert_hi) used_flag[e - p.expert_lo] = 1;
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-        int n = 0;
-        for (int e = p.expert_lo; e < p.expert_hi; ++e) {
-            slot_of[e] = n;
-            if (used_flag[e]) p.active[n++] = e;
+    // block scan over the local experts, 4 per thread, ascending
+    const int nl = p.expert_hi - p.expert_lo;
+    int cnt = 0;
+    for (int i = 0; i < 4; ++i) {
+        int e = 4 * threadIdx.x + i;
+        if (e < nl) cnt += used_flag[e];
+    }
+    int incl = cnt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        int v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
+    }
+    if (lane == 31) warp_total[warp] = incl;
+    __syncthreads();
+    int base = 0;
+    for (int w = 0; w < warp; ++w) base += warp_total[w];
+    int slot = base + incl - cnt;
+    for (int i = 0; i < 4; ++i) {
+        int e = 4 * threadIdx.x + i;
+        if (e < nl && used_flag[e]) {
+            slot_of[e] = slot;
+            p.active[slot] = p.expert_lo + e;
+            ++slot;
         }
-        *p.n_active = n;
-        for (int i = 0; i < n * 8; ++i) p.coef[i] = 0.0f;
-        for (int s = 0; s < p.S; ++s)
-            for (int k = 0; k < K; ++k) {
-                int e = sel[s][k];
-                if (e >= p.expert_lo && e < p.expert_hi) p.coef[slot_of[e] * 8 + s] = selw[s][k];
-            }
+    }
+    int total = 0;
+    for (int w = 0; w < kRouteThreads / 32; ++w) total += warp_total[w];
+    if (threadIdx.x == 0) *p.n_active = total;
+    for (int i = threadIdx.x; i < total * 8; i += blockDim.x) p.coef[i] = 0.0f;
+    __syncthreads();
+    if (threadIdx.x < p.S * K) {
+        int s = threadIdx.x / K, k = threadIdx.x % K;
+        int e = sel[s][k];
+        if (e >= p.expert_lo && e < p.expert_hi) p.coef[slot_of[e - p.expert_lo] * 8 + s] = selw[s][k];
     }
 }
 

@@ -124,7 +124,7 @@ struct FcSession {
     int *route_ids = nullptr, *n_active = nullptr, *active = nullptr;
     __half *h_xq = nullptr, *hsh_xq = nullptr, *hd_xq = nullptr;
     float *moe_part = nullptr, *sh_part = nullptr;
-    float *logits = nullptr, *last_logits = nullptr, *layer_out = nullptr;
+    float *logits = nullptr, *layer_out = nullptr;
     HeadPartials hp{};
     int *d_err = nullptr;    // bit 1: a bounded wait in a kernel gave up
     Staging *d_stage = nullptr, *h_stage = nullptr;
@@ -492,7 +492,7 @@ cudaError_t record_forward(FcSession *s, int S) {
     for (int l = 0; l < c.layer_count; ++l) {
         DevLayer &y = m->layers[l];
         __half *cache = s->cache + (size_t)l * s->opt.context_size * (L + R);
-        rmsnorm_kernel<<<S, 256, 0, st>>>(s->resid, D, y.attn_norm.p, D, c.rms_norm_epsilon,
+        rmsnorm_kernel<<<S, norm_threads(D), 0, st>>>(s->resid, D, y.attn_norm.p, D, c.rms_norm_epsilon,
                                           s->xq_norm, kpD, nullptr, 0);
         mark(s, "rmsnorm");
         {
@@ -516,7 +516,7 @@ cudaError_t record_forward(FcSession *s, int S) {
             mark(s, "gemv_q_kv_a");
         }
         if (c.q_lora_rank > 0) {
-            rmsnorm_kernel<<<S, 256, 0, st>>>(s->qa, c.q_lora_rank, y.q_a_norm.p, c.q_lora_rank,
+            rmsnorm_kernel<<<S, norm_threads(c.q_lora_rank), 0, st>>>(s->qa, c.q_lora_rank, y.q_a_norm.p, c.q_lora_rank,
                                               c.rms_norm_epsilon, s->qa_xq, kpad(c.q_lora_rank),
                                               nullptr, 0);
             mark(s, "rmsnorm");
@@ -526,7 +526,7 @@ cudaError_t record_forward(FcSession *s, int S) {
             FC_TRY(gemv1(df, g, S, 0.0f, s->d_err, m->sms, st));
             mark(s, "gemv_q_b");
         }
-        mla_prep_kernel<<<S, 256, 0, st>>>(s->ckv, s->q, y.kv_a_norm.p, L, R, H, NP,
+        mla_prep_kernel<<<dim3(S, 1 + (H * (R / 2) + 255) / 256), 256, 0, st>>>(s->ckv, s->q, y.kv_a_norm.p, L, R, H, NP,
                                            c.rms_norm_epsilon, c.rope_theta, d_pos, cache, s->qcat);
         mark(s, "mla_prep");
         {
@@ -575,7 +575,7 @@ cudaError_t record_forward(FcSession *s, int S) {
             FC_TRY(gemv1(df, g, S, 0.0f, s->d_err, m->sms, st));
             mark(s, "gemv_o_proj");
         }
-        rmsnorm_kernel<<<S, 256, 0, st>>>(s->resid, D, y.ffn_norm.p, D, c.rms_norm_epsilon,
+        rmsnorm_kernel<<<S, norm_threads(D), 0, st>>>(s->resid, D, y.ffn_norm.p, D, c.rms_norm_epsilon,
                                           s->xq_norm, kpD, s->xn, D);
         mark(s, "rmsnorm");
         if (y.dense) {
@@ -675,7 +675,7 @@ cudaError_t record_forward(FcSession *s, int S) {
             mark(s, "layer_trace_copy");
         }
     }
-    rmsnorm_kernel<<<S, 256, 0, st>>>(s->resid, D, m->final_norm.p, D, c.rms_norm_epsilon,
+    rmsnorm_kernel<<<S, norm_threads(D), 0, st>>>(s->resid, D, m->final_norm.p, D, c.rms_norm_epsilon,
                                       s->xq_norm, kpD, nullptr, 0);
     mark(s, "rmsnorm");
     {
@@ -691,7 +691,7 @@ cudaError_t record_forward(FcSession *s, int S) {
                                                   s->head_chunks);
         mark(s, "head_partial");
         accept_kernel<<<1, 256, 0, st>>>(s->logits, c.vocab_size, s->d_stage, s->hp, s->head_chunks,
-                                         s->d_res, s->last_logits, s->d_err);
+                                         s->d_res, s->d_err);
         mark(s, "accept");
     }
     FC_TRY(cudaGetLastError());
@@ -1043,7 +1043,7 @@ int fc_session_create(FcSession **out, FcModel *m, const FcOptions *options, cha
     ok = ok && salloc(s, s->hd_xq, (size_t)mb * kpad(std::max(c.dense_intermediate_size, 32)) * 2);
     ok = ok && salloc(s, s->moe_part, (size_t)s->max_slots * mb * D);
     ok = ok && salloc(s, s->sh_part, (size_t)mb * D);
-    ok = ok && salloc(s, s->logits, (size_t)mb * V) && salloc(s, s->last_logits, (size_t)V);
+    ok = ok && salloc(s, s->logits, (size_t)mb * V);
     ok = ok && salloc(s, s->layer_out, (size_t)c.layer_count * mb * D);
     size_t hc = (size_t)mb * s->head_chunks;
     ok = ok && salloc(s, s->hp.amax, hc) && salloc(s, s->hp.aidx, hc) && salloc(s, s->hp.zmax, hc) &&
@@ -1155,9 +1155,9 @@ int fc_session_verify(FcSession *s, const int *ids, int k, const FcAcceptConfig 
     for (int i = 0; i < commit; ++i) emitted[i] = ids[i];
     *n_emitted = commit;
     *next_token = r.next_token;
-    if (last_logits) {
-        cudaError_t e = cudaMemcpy(last_logits, s->last_logits, (size_t)s->m->c.vocab_size * 4,
-                                   cudaMemcpyDeviceToHost);
+    if (last_logits) {  // the logits row of the last committed token
+        cudaError_t e = cudaMemcpy(last_logits, s->logits + (size_t)(commit - 1) * s->m->c.vocab_size,
+                                   (size_t)s->m->c.vocab_size * 4, cudaMemcpyDeviceToHost);
         if (e != cudaSuccess) return set_error(error, error_size, "logits copy failed");
     }
     s->position += commit;  // rollback of rows >= commit: the cache is append-only
