@@ -297,6 +297,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + kStages * 2 * kSlotBytes);
     uint64_t *empty = full + kStages;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    pdl_release();
 
     if (tid == 0) {
         for (int i = 0; i < kStages; ++i) {
@@ -310,6 +311,10 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
     if (warp == kGemvWarps) {
         // ---------------- producer ----------------
         if (lane != 0) return;
+        // Weights are constant during a forward, so the producer streams them
+        // before the predecessor finishes; only the MoE work list (written by
+        // the router kernel) needs the wait.
+        if (wk.moe) pdl_wait();
         int idx = 0;
         for (int item = blockIdx.x; item < wk.total_items; item += gridDim.x) {
             GemvItem it;
@@ -333,6 +338,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
     }
 
     // ---------------- consumers ----------------
+    pdl_wait();
     const int g = lane >> 2, j = lane & 3;
     const bool has_b = g < wk.S;
     int idx = 0;
@@ -436,8 +442,8 @@ inline cudaError_t launch_gemv_work(int fa, int fb, GemvWork &wk, int sms, cudaS
     int grid = std::min(items, sms * kGemvCtasPerSm);
 #define FC_GEMV_CASE(A, B)                                                               \
     if (fa == A && fb == B) {                                                            \
-        gemv_kernel<A, B><<<grid, kGemvThreads, gemv_smem_bytes(A, B), stream>>>(wk);    \
-        return cudaGetLastError();                                                       \
+        return launch_pdl(gemv_kernel<A, B>, dim3(grid), dim3(kGemvThreads),               \
+                          gemv_smem_bytes(A, B), stream, wk);                              \
     }
     FC_GEMV_FORMATS(FC_GEMV_CASE)
 #undef FC_GEMV_CASE

@@ -75,6 +75,8 @@ struct HeadPartials {
 // grid (chunks, rows), 256 threads.
 __global__ void head_partial_kernel(const float *logits, int V, const Staging *st, HeadPartials hp,
                                     int chunks) {
+    pdl_wait();
+    pdl_release();
     __shared__ float sv[3][8];
     __shared__ int si[2][8];
     int chunk = blockIdx.x, row = blockIdx.y;
@@ -150,6 +152,8 @@ __global__ void head_partial_kernel(const float *logits, int V, const Staging *s
 __global__ void __launch_bounds__(256) accept_kernel(const float *logits, int V, const Staging *st,
                                                      HeadPartials hp, int chunks, Result *res,
                                                      int *err) {
+    pdl_wait();
+    pdl_release();
     __shared__ int tops[kMaxRows], picks[kMaxRows];
     __shared__ float zmax_row[kMaxRows], den_row[kMaxRows];
     const int rows = st->rows, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;

@@ -41,6 +41,8 @@ __device__ __forceinline__ float dequant_element(int fmt, const uint8_t *w, int 
 }
 
 __global__ void embed_kernel(int fmt, const uint8_t *w, int D, int kp, const int *ids, float *x) {
+    pdl_wait();
+    pdl_release();
     int s = blockIdx.x;
     int row = ids[s];
     for (int k = threadIdx.x; k < D; k += blockDim.x)
@@ -70,6 +72,8 @@ constexpr int kNormThreads = 1024;
 __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const float *x, int ldx, const float *w,
                                                                int D, float eps, __half *yq, int kpy,
                                                                float *y, int ldy) {
+    pdl_wait();
+    pdl_release();
     __shared__ float scratch[32];
     const int s = blockIdx.x, n4 = D / 4;
     const float4 *xs = reinterpret_cast<const float4 *>(x + (size_t)s * ldx);
@@ -132,6 +136,8 @@ __device__ __forceinline__ void rope_pair(float first, float second, int p, int 
 __global__ void mla_prep_kernel(const float *ckv, const float *q, const float *norm_w, int L,
                                 int R, int H, int nope, float eps, float theta,
                                 const int *d_pos, __half *cache, __half *qcat) {
+    pdl_wait();
+    pdl_release();
     __shared__ float scratch[32];
     const int s = blockIdx.x;
     const int position = *d_pos + s;
@@ -179,6 +185,8 @@ __global__ void __launch_bounds__(256) mla_absorb_kernel(int fmt, const uint8_t 
                                                          int kp, const float *q, int S, int H,
                                                          int nope, int vdim, int R, int L,
                                                          __half *qcat) {
+    pdl_wait();
+    pdl_release();
     __shared__ float wsm[kAbsorbMaxNope][kAbsorbCols + 1];
     __shared__ float qs[8][kAbsorbMaxNope];
     __shared__ __align__(16) uint8_t raw[kAbsorbMaxNope / kTileRows][1152];
@@ -287,6 +295,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 mla_attention_kernel(const __half *cache, const __half *qcat, int S, int H, int chunks_per_split,
                      const int *d_pos, float softmax_scale, float *part_o, float *part_m,
                      float *part_l) {
+    pdl_wait();
+    pdl_release();
     constexpr int DW = L + R;
     constexpr int ST = DW + 8;        // smem row stride (halves)
     constexpr int PST = kAttnKeys + 8;
@@ -508,6 +518,8 @@ constexpr int kMaxSplits = 1024;
 __global__ void __launch_bounds__(kCombineThreads)
 mla_combine_kernel(const float *part_o, const float *part_m, const float *part_l, int splits, int S,
                    int H, int L, __half *ctx_xq, size_t head_stride) {
+    pdl_wait();
+    pdl_release();
     __shared__ float wts[kMaxSplits];
     __shared__ float red[kCombineThreads / 32];
     const int q = blockIdx.x, nq = S * H;

@@ -24,6 +24,8 @@ namespace fc {
 // order (warp butterfly, then warps in index order).
 __global__ void __launch_bounds__(256) router_logits_kernel(const float *W, const float *x, int E,
                                                             int D, int S, float *logits) {
+    pdl_wait();
+    pdl_release();
     __shared__ float red[8][8];
     const int e = blockIdx.x;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -91,6 +93,8 @@ __device__ __forceinline__ float route_score(float x, int fn) {
 constexpr int kRouteThreads = 256;
 
 __global__ void __launch_bounds__(kRouteThreads) route_select_kernel(const float *logits, RouteParams p) {
+    pdl_wait();
+    pdl_release();
     extern __shared__ float rs_smem[];  // scores [8][E], choice [8][E]
     __shared__ int used_flag[1024];
     __shared__ int slot_of[1024];
@@ -225,6 +229,8 @@ __global__ void __launch_bounds__(kRouteThreads) route_select_kernel(const float
 __global__ void moe_combine_kernel(float *resid, const float *routed, const float *shared,
                                    const float *coef, const int *n_active, int S, int D,
                                    int max_batch) {
+    pdl_wait();
+    pdl_release();
     int idx = blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= S * D) return;
     int s = idx / D, d = idx % D;

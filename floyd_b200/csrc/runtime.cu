@@ -485,15 +485,15 @@ cudaError_t record_forward(FcSession *s, int S) {
     const int df = c.dense_format, ef = c.expert_format;
 
     FC_TRY(cudaMemcpyAsync(s->d_stage, s->h_stage, sizeof(Staging), cudaMemcpyHostToDevice, st));
-    embed_kernel<<<S, 256, 0, st>>>(m->embed.fmt, m->embed.w, D, m->embed.kp, s->d_stage->ids,
-                                    s->resid);
+    FC_TRY(launch_pdl(embed_kernel, dim3(S), dim3(256), 0, st, m->embed.fmt, m->embed.w, D, m->embed.kp, s->d_stage->ids,
+                                    s->resid));
     FC_TRY(cudaGetLastError());
     mark(s, "embed");
     for (int l = 0; l < c.layer_count; ++l) {
         DevLayer &y = m->layers[l];
         __half *cache = s->cache + (size_t)l * s->opt.context_size * (L + R);
-        rmsnorm_kernel<<<S, norm_threads(D), 0, st>>>(s->resid, D, y.attn_norm.p, D, c.rms_norm_epsilon,
-                                          s->xq_norm, kpD, nullptr, 0);
+        FC_TRY(launch_pdl(rmsnorm_kernel, dim3(S), dim3(norm_threads(D)), 0, st, s->resid, D, y.attn_norm.p, D, c.rms_norm_epsilon,
+                                          s->xq_norm, kpD, nullptr, 0));
         mark(s, "rmsnorm");
         {
             GemvBatch b{};
@@ -516,9 +516,9 @@ cudaError_t record_forward(FcSession *s, int S) {
             mark(s, "gemv_q_kv_a");
         }
         if (c.q_lora_rank > 0) {
-            rmsnorm_kernel<<<S, norm_threads(c.q_lora_rank), 0, st>>>(s->qa, c.q_lora_rank, y.q_a_norm.p, c.q_lora_rank,
+            FC_TRY(launch_pdl(rmsnorm_kernel, dim3(S), dim3(norm_threads(c.q_lora_rank)), 0, st, s->qa, c.q_lora_rank, y.q_a_norm.p, c.q_lora_rank,
                                               c.rms_norm_epsilon, s->qa_xq, kpad(c.q_lora_rank),
-                                              nullptr, 0);
+                                              nullptr, 0));
             mark(s, "rmsnorm");
             GemvSeg g = seg_of(y.q_b, s->qa_xq, EPI_STORE);
             g.y = s->q;
@@ -526,31 +526,31 @@ cudaError_t record_forward(FcSession *s, int S) {
             FC_TRY(gemv1(df, g, S, 0.0f, s->d_err, m->sms, st));
             mark(s, "gemv_q_b");
         }
-        mla_prep_kernel<<<dim3(S, 1 + (H * (R / 2) + 255) / 256), 256, 0, st>>>(s->ckv, s->q, y.kv_a_norm.p, L, R, H, NP,
-                                           c.rms_norm_epsilon, c.rope_theta, d_pos, cache, s->qcat);
+        FC_TRY(launch_pdl(mla_prep_kernel, dim3(dim3(S, 1 + (H * (R / 2) + 255) / 256)), dim3(256), 0, st, s->ckv, s->q, y.kv_a_norm.p, L, R, H, NP,
+                                           c.rms_norm_epsilon, c.rope_theta, d_pos, cache, s->qcat));
         mark(s, "mla_prep");
         {
             dim3 grid(H, L / kAbsorbCols);
-            mla_absorb_kernel<<<grid, 256, 0, st>>>(df, y.kv_b.w, y.kv_b.kp, s->q, S, H,
-                                                    NP, VD, R, L, s->qcat);
+            FC_TRY(launch_pdl(mla_absorb_kernel, dim3(grid), dim3(256), 0, st, df, y.kv_b.w, y.kv_b.kp, s->q, S, H,
+                                                    NP, VD, R, L, s->qcat));
             mark(s, "mla_absorb");
         }
         {
             dim3 grid((S * H + kAttnQ - 1) / kAttnQ, s->splits);
             if (L == 512)
-                mla_attention_kernel<512, 64><<<grid, kAttnThreads, s->attn_smem, st>>>(
-                    cache, s->qcat, S, H, s->chunks_per_split, d_pos, scale, s->part_o, s->part_m,
-                    s->part_l);
+                FC_TRY(launch_pdl(mla_attention_kernel<512, 64>, grid, dim3(kAttnThreads), s->attn_smem,
+                                  st, (const __half *)cache, (const __half *)s->qcat, S, H,
+                                  s->chunks_per_split, d_pos, scale, s->part_o, s->part_m, s->part_l));
             else
-                mla_attention_kernel<256, 64><<<grid, kAttnThreads, s->attn_smem, st>>>(
-                    cache, s->qcat, S, H, s->chunks_per_split, d_pos, scale, s->part_o, s->part_m,
-                    s->part_l);
-            FC_TRY(cudaGetLastError());
+                FC_TRY(launch_pdl(mla_attention_kernel<256, 64>, grid, dim3(kAttnThreads), s->attn_smem,
+                                  st, (const __half *)cache, (const __half *)s->qcat, S, H,
+                                  s->chunks_per_split, d_pos, scale, s->part_o, s->part_m, s->part_l));
             mark(s, "mla_attention");
             size_t head_stride = (size_t)mb * kpL * 2;
-            mla_combine_kernel<<<dim3(S * H, (L + kCombineThreads - 1) / kCombineThreads),
-                                 kCombineThreads, 0, st>>>(s->part_o, s->part_m, s->part_l,
-                                                           s->splits, S, H, L, s->ctx_xq, head_stride);
+            FC_TRY(launch_pdl(mla_combine_kernel, dim3(S * H, (L + kCombineThreads - 1) / kCombineThreads),
+                              dim3(kCombineThreads), 0, st, (const float *)s->part_o,
+                              (const float *)s->part_m, (const float *)s->part_l, s->splits, S, H, L,
+                              s->ctx_xq, head_stride));
             mark(s, "mla_combine");
             // W_UV: rows nope .. nope+v of each head's kv_b block (decode_value, :345-375)
             // nope and value_dim are multiples of 16, so each head's W_UV
@@ -575,8 +575,8 @@ cudaError_t record_forward(FcSession *s, int S) {
             FC_TRY(gemv1(df, g, S, 0.0f, s->d_err, m->sms, st));
             mark(s, "gemv_o_proj");
         }
-        rmsnorm_kernel<<<S, norm_threads(D), 0, st>>>(s->resid, D, y.ffn_norm.p, D, c.rms_norm_epsilon,
-                                          s->xq_norm, kpD, s->xn, D);
+        FC_TRY(launch_pdl(rmsnorm_kernel, dim3(S), dim3(norm_threads(D)), 0, st, s->resid, D, y.ffn_norm.p, D, c.rms_norm_epsilon,
+                                          s->xq_norm, kpD, s->xn, D));
         mark(s, "rmsnorm");
         if (y.dense) {
             int kpI = kpad(c.dense_intermediate_size);
@@ -593,7 +593,7 @@ cudaError_t record_forward(FcSession *s, int S) {
             mark(s, "gemv_dense_down");
         } else {
             int E = c.expert_count, K = c.experts_per_token;
-            router_logits_kernel<<<E, 256, 0, st>>>(y.router.p, s->xn, E, D, S, s->router_logits);
+            FC_TRY(launch_pdl(router_logits_kernel, dim3(E), dim3(256), 0, st, y.router.p, s->xn, E, D, S, s->router_logits));
             mark(s, "router_logits");
             RouteParams rp{};
             rp.E = E; rp.K = K; rp.S = S;
@@ -610,7 +610,7 @@ cudaError_t record_forward(FcSession *s, int S) {
             rp.n_active = s->n_active;
             rp.active = s->active;
             rp.coef = s->coef;
-            route_select_kernel<<<1, 256, 2 * 8 * E * sizeof(float), st>>>(s->router_logits, rp);
+            FC_TRY(launch_pdl(route_select_kernel, dim3(1), dim3(256), 2 * 8 * E * sizeof(float), st, s->router_logits, rp));
             FC_TRY(cudaGetLastError());
             mark(s, "route_select");
             int I = c.moe_intermediate_size, kpI = kpad(I);
@@ -664,9 +664,9 @@ cudaError_t record_forward(FcSession *s, int S) {
             dn.err = s->d_err;
             FC_TRY(launch_gemv_work(ef, df, dn, m->sms, st));
             mark(s, "moe_down");
-            moe_combine_kernel<<<(S * D + 255) / 256, 256, 0, st>>>(
+            FC_TRY(launch_pdl(moe_combine_kernel, dim3((S * D + 255) / 256), dim3(256), 0, st, 
                 s->resid, s->moe_part, y.s_down.count ? s->sh_part : nullptr, s->coef, s->n_active,
-                S, D, mb);
+                S, D, mb));
             mark(s, "moe_combine");
         }
         if (s->trace) {
@@ -675,8 +675,8 @@ cudaError_t record_forward(FcSession *s, int S) {
             mark(s, "layer_trace_copy");
         }
     }
-    rmsnorm_kernel<<<S, norm_threads(D), 0, st>>>(s->resid, D, m->final_norm.p, D, c.rms_norm_epsilon,
-                                      s->xq_norm, kpD, nullptr, 0);
+    FC_TRY(launch_pdl(rmsnorm_kernel, dim3(S), dim3(norm_threads(D)), 0, st, s->resid, D, m->final_norm.p, D, c.rms_norm_epsilon,
+                                      s->xq_norm, kpD, nullptr, 0));
     mark(s, "rmsnorm");
     {
         GemvSeg g = seg_of(m->lm_head, s->xq_norm, EPI_STORE);
@@ -687,15 +687,37 @@ cudaError_t record_forward(FcSession *s, int S) {
     }
     {
         dim3 grid(s->head_chunks, S);
-        head_partial_kernel<<<grid, 256, 0, st>>>(s->logits, c.vocab_size, s->d_stage, s->hp,
-                                                  s->head_chunks);
+        FC_TRY(launch_pdl(head_partial_kernel, dim3(grid), dim3(256), 0, st, s->logits, c.vocab_size, s->d_stage, s->hp,
+                                                  s->head_chunks));
         mark(s, "head_partial");
-        accept_kernel<<<1, 256, 0, st>>>(s->logits, c.vocab_size, s->d_stage, s->hp, s->head_chunks,
-                                         s->d_res, s->d_err);
+        FC_TRY(launch_pdl(accept_kernel, dim3(1), dim3(256), 0, st, s->logits, c.vocab_size, s->d_stage, s->hp, s->head_chunks,
+                                         s->d_res, s->d_err));
         mark(s, "accept");
     }
     FC_TRY(cudaGetLastError());
     FC_TRY(cudaMemcpyAsync(s->h_res, s->d_res, sizeof(Result), cudaMemcpyDeviceToHost, st));
+    return cudaSuccess;
+}
+
+// Every kernel of the forward asks for the same (maximum) shared-memory
+// carveout, so consecutive kernels never make an SM reconfigure its L1 split.
+cudaError_t prefer_shared_carveout() {
+    const void *kernels[] = {
+        (const void *)embed_kernel, (const void *)rmsnorm_kernel, (const void *)mla_prep_kernel,
+        (const void *)mla_absorb_kernel, (const void *)mla_attention_kernel<512, 64>,
+        (const void *)mla_attention_kernel<256, 64>, (const void *)mla_combine_kernel,
+        (const void *)router_logits_kernel, (const void *)route_select_kernel,
+        (const void *)moe_combine_kernel, (const void *)head_partial_kernel,
+        (const void *)accept_kernel,
+#define FC_GEMV_PTR(A, B) (const void *)gemv_kernel<A, B>,
+        FC_GEMV_FORMATS(FC_GEMV_PTR)
+#undef FC_GEMV_PTR
+    };
+    for (const void *k : kernels) {
+        cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                             (int)cudaSharedmemCarveoutMaxShared);
+        if (e != cudaSuccess) return e;
+    }
     return cudaSuccess;
 }
 
@@ -1062,7 +1084,7 @@ int fc_session_create(FcSession **out, FcModel *m, const FcOptions *options, cha
                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
                                               2 * 8 * 1024 * 4);
         ok = e1 == cudaSuccess && e2 == cudaSuccess && e3 == cudaSuccess &&
-             gemv_prepare_all() == cudaSuccess;
+             gemv_prepare_all() == cudaSuccess && prefer_shared_carveout() == cudaSuccess;
     }
     if (!ok) {
         free_session_buffers(s);
