@@ -108,6 +108,19 @@ __device__ __forceinline__ float e8m0_to_float(uint32_t code) {
     return __int_as_float((int)(code << 23));
 }
 
+// Four ue8m0 scale bytes -> fp32 powers of two without branches: code << 23
+// (an integer multiply, issued on the FMA pipe) is the fp32 pattern of
+// 2^(code - 127) for 1 <= code <= 254; an integer max maps code 0 to the
+// subnormal 2^-127 exactly.  Code 255 (NaN in the format) becomes +inf, which
+// is equally non-finite in every product.
+__device__ __forceinline__ void e8m0x4_to_float(uint32_t s4, float (&out)[4]) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        uint32_t bits = ((s4 >> (8 * q)) & 0xFFu) * 8388608u;
+        out[q] = __uint_as_float(max(bits, 0x00400000u));
+    }
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

@@ -200,9 +200,10 @@ __device__ __forceinline__ void gemv_chunk(const uint8_t *blk0, const uint8_t *b
                 scale[h][kGroups > 2 ? 2 : 0] = __low2float(h1);
                 scale[h][kGroups > 3 ? 3 : 0] = __high2float(h1);
             } else {
-                uint32_t s4 = *reinterpret_cast<const uint32_t *>(sp);
+                float f4[4];
+                e8m0x4_to_float(*reinterpret_cast<const uint32_t *>(sp), f4);
 #pragma unroll
-                for (int q = 0; q < kGroups; ++q) scale[h][q] = e8m0_to_float((s4 >> (8 * q)) & 0xFFu);
+                for (int q = 0; q < kGroups; ++q) scale[h][q] = f4[q];
             }
         }
         uint32_t regs[2][16];  // per row h: fp16x2 registers (index q)
