@@ -91,20 +91,16 @@ __device__ __forceinline__ uint32_t dequant_q4_pair(uint32_t w, int shift) {
     return hsub2_bits(t, 0x64086408u);
 }
 
-// e2m1 pair at nibble offsets `4*shift` and `4*shift + 16` of w -> fp16x2
-// holding e2m1 * 2^-14 exactly: the code's magnitude bits land in fp16
-// bits 9..11 (exponent low bits + mantissa msb, subnormal for the 0.5 code)
-// and its sign in bit 15.  Two ALU masks; the shifts are integer multiplies
-// (FMA pipe).  Callers scale the accumulated result by 2^14.
-template <int SHIFT>
-__device__ __forceinline__ uint32_t dequant_e2m1_pair(uint32_t w) {
-    const uint32_t mag = w & (0x00070007u << (4 * SHIFT));
-    const uint32_t sgn = w & (0x00080008u << (4 * SHIFT));
-    if (SHIFT == 3) return __umulhi(mag, 1u << 29) + sgn;
-    return mag * (512u >> (4 * SHIFT)) + sgn * (4096u >> (4 * SHIFT));
+// One 32-bit word of 4 bytes of e2m1 code pairs -> 4 fp16x2 registers with
+// Blackwell's hardware conversion (exact: every e2m1 value is an fp16);
+// register b holds (low nibble, high nibble) of byte b.
+__device__ __forceinline__ void dequant_e2m1_word(uint32_t w, uint32_t (&out)[4]) {
+    asm("{\n .reg .b8 b0, b1, b2, b3;\n mov.b32 {b0, b1, b2, b3}, %4;\n"
+        " cvt.rn.f16x2.e2m1x2 %0, b0;\n cvt.rn.f16x2.e2m1x2 %1, b1;\n"
+        " cvt.rn.f16x2.e2m1x2 %2, b2;\n cvt.rn.f16x2.e2m1x2 %3, b3;\n}\n"
+        : "=r"(out[0]), "=r"(out[1]), "=r"(out[2]), "=r"(out[3])
+        : "r"(w));
 }
-
-constexpr float kE2m1Fp16Scale = 16384.0f;  // undoes the 2^-14 of dequant_e2m1_pair
 
 __device__ __forceinline__ float e8m0_to_float(uint32_t code) {
     if (code == 255u) return __int_as_float(0x7FC00000);
@@ -159,7 +155,8 @@ __device__ __forceinline__ float silu(float x) { return x / (1.0f + expf(-x)); }
 //             nibble slot = q%4 + 4e; byte = 16j + 4*word + slot/2,
 //             nibble = slot%2   (shift-and-mask decode, two values a word
 //             apart land in one fp16x2 register)
-//       e2m1: the q4 placement (decoded by dequant_e2m1_pair)
+//       e2m1: same i, j, h, e; byte = 16j + q, nibble = e, so each byte is
+//             exactly one fp16x2 A register for cvt.rn.f16x2.e2m1x2
 // ---------------------------------------------------------------------------
 constexpr int kTileRows = 16;
 constexpr int kBlockValueBytes = kTileRows * 64;
@@ -192,6 +189,11 @@ __host__ __device__ inline void inner_position(int fmt, int r, int &byte, int &n
     }
     int i = r >> 4, j = (r & 15) >> 2, b = r & 3;
     int q = 2 * i + (b >> 1), e = b & 1;
+    if (fmt == FC_FMT_MXFP4) {
+        byte = 16 * j + q;
+        nibble = e;
+        return;
+    }
     int word = q >> 2;
     int slot = (q & 3) + 4 * e;
     byte = 16 * j + 4 * word + (slot >> 1);

@@ -18,8 +18,8 @@
 //     full / empty mbarriers between it and the consumers, so copies for the
 //     next item are in flight while the current one is reduced.
 //   - Each of the 8 consumer warps takes one 64-byte-per-row chunk of every
-//     stage, dequantizes it exactly into fp16 registers (int8 and int4 values
-//     are exact in fp16, e2m1 values exactly scaled by 2^-14) and runs m16n8k16 tensor-core MMAs
+//     stage, dequantizes it exactly into fp16 registers (int8, int4 and e2m1
+//     values are all exact in fp16) and runs m16n8k16 tensor-core MMAs
 //     against the activations split into hi + lo fp16 halves (about 22
 //     significant bits); each MMA pair covers one 32-column scale group and
 //     the group scale is applied in fp32 to the MMA result.
@@ -221,10 +221,10 @@ __device__ __forceinline__ void gemv_chunk(const uint8_t *blk0, const uint8_t *b
             } else {
 #pragma unroll
                 for (int wi = 0; wi < 4; ++wi) {
-                    regs[h][4 * wi + 0] = dequant_e2m1_pair<0>(words[wi]);
-                    regs[h][4 * wi + 1] = dequant_e2m1_pair<1>(words[wi]);
-                    regs[h][4 * wi + 2] = dequant_e2m1_pair<2>(words[wi]);
-                    regs[h][4 * wi + 3] = dequant_e2m1_pair<3>(words[wi]);
+                    uint32_t o4[4];
+                    dequant_e2m1_word(words[wi], o4);
+#pragma unroll
+                    for (int p = 0; p < 4; ++p) regs[h][4 * wi + p] = o4[p];
                 }
             }
         }
@@ -390,7 +390,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
             for (int w = 0; w < kGemvWarps; ++w) sum += red[((w * 2 + t) * 32 + l) * 4 + e];
             int row = 16 * t + (l >> 2) + 8 * (e >> 1);
             int col = 2 * (l & 3) + (e & 1);
-            out[row * 8 + col] = it.fmt == FC_FMT_MXFP4 ? sum * kE2m1Fp16Scale : sum;
+            out[row * 8 + col] = sum;
         }
         consumer_sync();
         gemv_epilogue(wk.seg[it.seg], it, wk.S, wk.swiglu_limit, out);
