@@ -371,25 +371,40 @@ mla_attention_kernel(const __half *cache, const __half *qcat, int S, int H, int 
         const __half *Kb = Ks + buf * kAttnKeys * ST;
 
         // ---- scores: rows 16*mt.., keys 16*kq .. +16 (two n8 tiles) ----
+        // Four independent accumulator sets over interleaved k-steps (short
+        // MMA dependency chains), fragments for 4 k-steps loaded up front;
+        // summed in a fixed order, so each row's result is unchanged by the
+        // number of rows in the batch.
+        static_assert(DW % 64 == 0, "score width must be a multiple of 64");
+        float part[4][2][4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+#pragma unroll
+            for (int t = 0; t < 2; ++t)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) part[u][t][e] = 0.0f;
+        const __half *ap0 = Qs + (16 * mt + (lane & 15)) * ST + 8 * (lane >> 4);
+        const __half *bp0 = Kb + (16 * kq + (lane & 7) + 8 * (lane >> 4)) * ST + 8 * ((lane >> 3) & 1);
+#pragma unroll 1
+        for (int d = 0; d < DW; d += 64) {
+            uint32_t a[4][4], b[4][4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                ldmatrix_x4(a[u], ap0 + d + 16 * u);
+                ldmatrix_x4(b[u], bp0 + d + 16 * u);
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                mma_f16(part[u][0], a[u], b[u][0], b[u][1], part[u][0]);
+                mma_f16(part[u][1], a[u], b[u][2], b[u][3], part[u][1]);
+            }
+        }
         float sacc[2][4];
 #pragma unroll
         for (int t = 0; t < 2; ++t)
 #pragma unroll
-            for (int e = 0; e < 4; ++e) sacc[t][e] = 0.0f;
-#pragma unroll 4
-        for (int d = 0; d < DW; d += 16) {
-            uint32_t a[4];
-            // A 16x16: matrices (rows 0-7, k 0-7), (rows 8-15, k 0-7), (rows 0-7, k 8-15), (rows 8-15, k 8-15)
-            const __half *ap = Qs + (16 * mt + (lane & 15)) * ST + d + 8 * (lane >> 4);
-            ldmatrix_x4(a, ap);
-            uint32_t b[4];
-            // B: keys n0..n0+7 (two n8 tiles) x k16: matrices (keys 0-7, k0-7), (keys 0-7, k8-15),
-            // (keys 8-15, k0-7), (keys 8-15, k8-15)
-            const __half *bp = Kb + (16 * kq + (lane & 7) + 8 * (lane >> 4)) * ST + d + 8 * ((lane >> 3) & 1);
-            ldmatrix_x4(b, bp);
-            mma_f16(sacc[0], a, b[0], b[1], sacc[0]);
-            mma_f16(sacc[1], a, b[2], b[3], sacc[1]);
-        }
+            for (int e = 0; e < 4; ++e)
+                sacc[t][e] = (part[0][t][e] + part[1][t][e]) + (part[2][t][e] + part[3][t][e]);
         // scale + mask; per-row chunk max within the warp
         float rmax[2] = {-INFINITY, -INFINITY};
 #pragma unroll
