@@ -336,11 +336,19 @@ mla_attention_kernel(const __half *cache, const __half *qcat, int S, int H, int 
     auto load_chunk = [&](int chunk, int buf) {
         __half *dst = Ks + buf * kAttnKeys * ST;
         int base = chunk * kAttnKeys;
-        for (int i = tid; i < kAttnKeys * (DW / 8); i += kAttnThreads) {
-            int r = i / (DW / 8), c8 = i % (DW / 8);
+        // 16-byte pieces i = tid + n * threads of the [keys][DW/8] tile;
+        // (row, column) advance incrementally instead of by division
+        constexpr int kCols = DW / 8;
+        constexpr int kStepR = kAttnThreads / kCols, kStepC = kAttnThreads % kCols;
+        int r = tid / kCols, c8 = tid % kCols;
+#pragma unroll 4
+        for (int i = tid; i < kAttnKeys * kCols; i += kAttnThreads) {
             bool ok = base + r < total_keys;
             cp_async16(dst + r * ST + c8 * 8,
                        cache + (size_t)(ok ? base + r : 0) * DW + c8 * 8, ok);
+            r += kStepR;
+            c8 += kStepC;
+            if (c8 >= kCols) { c8 -= kCols; ++r; }
         }
     };
     if (chunk0 < chunk1) load_chunk(chunk0, 0);
