@@ -59,6 +59,12 @@ __device__ __forceinline__ uint4 ldg_stream(const void *p) {
     return v;
 }
 
+__device__ __forceinline__ uint2 ldg_v2(const void *p) {
+    uint2 v;
+    asm volatile("ld.global.nc.v2.u32 {%0,%1}, [%2];\n" : "=r"(v.x), "=r"(v.y) : "l"(p));
+    return v;
+}
+
 __device__ __forceinline__ uint4 ldg_v4(const void *p) {
     uint4 v;
     asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];\n"

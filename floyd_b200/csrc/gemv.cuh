@@ -167,10 +167,16 @@ __device__ __forceinline__ bool resolve_item(const GemvWork &wk, int item, GemvI
 }
 
 // Consumes one chunk block per tile from shared memory and accumulates
-// the 2 x (16 x 8) partial tile of this warp.
-template <int FMT>
+// the 2 x (16 x 8) partial tile of this warp.  The activation fragments
+// carry fp16 hi / lo halves.  PACK (at most 4 activation rows): one MMA per
+// fragment, B columns 0-3 the hi halves of rows 0-3 and columns 4-7 their lo
+// halves (b_raw[i].x/.y).  Otherwise hi (.x/.y) and lo (.z/.w) go to two MMAs
+// with separate accumulators (acc, accl).  Each output column of an MMA is
+// its own dot product, so both forms give the same bits for a row.
+template <int FMT, bool PACK>
 __device__ __forceinline__ void gemv_chunk(const uint8_t *blk0, const uint8_t *blk1,
-                                           const uint4 (&b_raw)[8], float (&acc)[2][4]) {
+                                           const uint4 (&b_raw)[8], float (&acc)[2][4],
+                                           float (&accl)[2][4]) {
     constexpr int kMmas = FMT == FC_FMT_Q8 ? 4 : 8;
     constexpr int kGroups = kMmas / 2;
     const int lane = threadIdx.x & 31;
@@ -231,6 +237,7 @@ __device__ __forceinline__ void gemv_chunk(const uint8_t *blk0, const uint8_t *b
 #pragma unroll
         for (int q = 0; q < kGroups; ++q) {
             float tmp[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            float tml[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
             for (int ii = 0; ii < 2; ++ii) {
                 int i = 2 * q + ii;
@@ -238,12 +245,18 @@ __device__ __forceinline__ void gemv_chunk(const uint8_t *blk0, const uint8_t *b
                 // a2 = row g (slots 2j+8, 2j+9), a3 = row g+8.
                 uint32_t a[4] = {regs[0][2 * i], regs[1][2 * i], regs[0][2 * i + 1], regs[1][2 * i + 1]};
                 mma_f16(tmp, a, b_raw[i].x, b_raw[i].y, tmp);
-                mma_f16(tmp, a, b_raw[i].z, b_raw[i].w, tmp);
+                if (!PACK) mma_f16(tml, a, b_raw[i].z, b_raw[i].w, tml);
             }
             acc[t][0] = fmaf(scale[0][q], tmp[0], acc[t][0]);
             acc[t][1] = fmaf(scale[0][q], tmp[1], acc[t][1]);
             acc[t][2] = fmaf(scale[1][q], tmp[2], acc[t][2]);
             acc[t][3] = fmaf(scale[1][q], tmp[3], acc[t][3]);
+            if (!PACK) {
+                accl[t][0] = fmaf(scale[0][q], tml[0], accl[t][0]);
+                accl[t][1] = fmaf(scale[0][q], tml[1], accl[t][1]);
+                accl[t][2] = fmaf(scale[1][q], tml[2], accl[t][2]);
+                accl[t][3] = fmaf(scale[1][q], tml[3], accl[t][3]);
+            }
         }
     }
 }
@@ -285,6 +298,103 @@ __device__ __forceinline__ void gemv_epilogue(const GemvSeg &sg, const GemvItem 
         sg.y[it.out_shift + (size_t)s * sg.ldy + col] += v;
     } else {
         store_xq(sg.yq + it.out_shift, sg.kpy, s, sg.col_off + col, v);
+    }
+}
+
+// Sums the consumer warps' fragments (fixed warp order) into out8 [32][8].
+__device__ __forceinline__ void reduce_warps(float *red, const float (&acc)[2][4], float *out8) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+#pragma unroll
+    for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) red[((warp * 2 + t) * 32 + lane) * 4 + e] = acc[t][e];
+    consumer_sync();
+    int t = tid >> 7, l = (tid >> 2) & 31, e = tid & 3;
+    float sum = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kGemvWarps; ++w) sum += red[((w * 2 + t) * 32 + l) * 4 + e];
+    int row = 16 * t + (l >> 2) + 8 * (e >> 1);
+    int col = 2 * (l & 3) + (e & 1);
+    out8[row * 8 + col] = sum;
+    consumer_sync();
+}
+
+// The consumer warps of gemv_kernel: per work item, wait for each stage,
+// multiply its chunk blocks, reduce, and run the epilogue.
+template <int FA, int FB, bool PACK>
+__device__ __forceinline__ void gemv_consume(const GemvWork &wk, const uint8_t *smem, size_t kSlotBytes,
+                                             uint64_t *full, uint64_t *empty, float *red, float *out) {
+    __shared__ float out_hi[kGemvRows * 8];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int g = lane >> 2, j = lane & 3;
+    // PACK: lane group g reads activation row g & 3, hi half (g < 4) or lo half
+    const int brow = PACK ? (g & 3) : g;
+    const int bhalf = PACK ? (g >> 2) * 8 : 0;
+    const bool has_b = brow < wk.S;
+    int idx = 0;
+    for (int item = blockIdx.x; item < wk.total_items; item += gridDim.x) {
+        GemvItem it;
+        if (!resolve_item<FA, FB>(wk, item, it)) continue;
+        const bool fa = it.fmt == FA;
+        const int blk = fa ? block_bytes(FA) : block_bytes(FB);
+        const int kmmas = it.fmt == FC_FMT_Q8 ? 4 : 8;
+        const int nchunks = chunk_count(it.fmt, it.kp);
+        const int nst = (nchunks + kGemvWarps - 1) / kGemvWarps;
+        float acc[2][4], accl[2][4];
+#pragma unroll
+        for (int t = 0; t < 2; ++t)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc[t][e] = accl[t][e] = 0.0f;
+        // activation fragments of chunk c (zeros past the end / unused rows)
+        auto load_b = [&](int c, uint4 (&b)[8]) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const bool live = has_b && c < nchunks && i < kmmas;
+                const __half *src = it.xq + ((size_t)brow * it.kp + 16 * (kmmas * c + i) + 4 * j) * 2;
+                if (PACK) {
+                    uint2 v = live ? ldg_v2(reinterpret_cast<const uint8_t *>(src) + bhalf) : make_uint2(0, 0);
+                    b[i] = make_uint4(v.x, v.y, 0, 0);
+                } else {
+                    b[i] = live ? ldg_v4(src) : make_uint4(0, 0, 0, 0);
+                }
+            }
+        };
+        // PACK: the next stage's fragments load while this stage computes
+        uint4 b_next[8];
+        if (PACK) load_b(warp, b_next);
+        for (int s = 0; s < nst; ++s, ++idx) {
+            const int slot = idx % kStages, round = idx / kStages;
+            const int c = s * kGemvWarps + warp;
+            uint4 b_raw[8];
+            if (PACK) {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) b_raw[i] = b_next[i];
+                if (s + 1 < nst) load_b(c + kGemvWarps, b_next);
+            } else {
+                load_b(c, b_raw);
+            }
+            mbar_wait_bounded(&full[slot], (uint32_t)(round & 1), wk.err);
+            if (c < nchunks) {
+                const uint8_t *b0 = smem + (slot * 2) * kSlotBytes + (size_t)warp * blk;
+                const uint8_t *b1 = it.t1 ? smem + (slot * 2 + 1) * kSlotBytes + (size_t)warp * blk : nullptr;
+                if (fa) gemv_chunk<FA, PACK>(b0, b1, b_raw, acc, accl);
+                else gemv_chunk<FB, PACK>(b0, b1, b_raw, acc, accl);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+        }
+        // out[row][s] = (hi sum over warps) + (lo sum over warps), the same
+        // arithmetic for both forms
+        if (PACK) {
+            reduce_warps(red, acc, out_hi);
+            out[tid] = (tid & 7) < 4 ? out_hi[tid] + out_hi[tid + 4] : 0.0f;
+        } else {
+            reduce_warps(red, acc, out_hi);
+            reduce_warps(red, accl, out);
+            out[tid] = out_hi[tid] + out[tid];
+        }
+        consumer_sync();
+        gemv_epilogue(wk.seg[it.seg], it, wk.S, wk.swiglu_limit, out);
     }
 }
 
@@ -340,61 +450,10 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
 
     // ---------------- consumers ----------------
     pdl_wait();
-    const int g = lane >> 2, j = lane & 3;
-    const bool has_b = g < wk.S;
-    int idx = 0;
-    for (int item = blockIdx.x; item < wk.total_items; item += gridDim.x) {
-        GemvItem it;
-        if (!resolve_item<FA, FB>(wk, item, it)) continue;
-        const bool fa = it.fmt == FA;
-        const int blk = fa ? block_bytes(FA) : block_bytes(FB);
-        const int kmmas = it.fmt == FC_FMT_Q8 ? 4 : 8;
-        const int nchunks = chunk_count(it.fmt, it.kp);
-        const int nst = (nchunks + kGemvWarps - 1) / kGemvWarps;
-        float acc[2][4];
-#pragma unroll
-        for (int t = 0; t < 2; ++t)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) acc[t][e] = 0.0f;
-        for (int s = 0; s < nst; ++s, ++idx) {
-            const int slot = idx % kStages, round = idx / kStages;
-            const int c = s * kGemvWarps + warp;
-            uint4 b_raw[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                if (has_b && c < nchunks && i < kmmas)
-                    b_raw[i] = ldg_v4(it.xq + ((size_t)g * it.kp + 16 * (kmmas * c + i) + 4 * j) * 2);
-                else
-                    b_raw[i] = make_uint4(0, 0, 0, 0);
-            }
-            mbar_wait_bounded(&full[slot], (uint32_t)(round & 1), wk.err);
-            if (c < nchunks) {
-                const uint8_t *b0 = smem + (slot * 2) * kSlotBytes + (size_t)warp * blk;
-                const uint8_t *b1 = it.t1 ? smem + (slot * 2 + 1) * kSlotBytes + (size_t)warp * blk : nullptr;
-                if (fa) gemv_chunk<FA>(b0, b1, b_raw, acc);
-                else gemv_chunk<FB>(b0, b1, b_raw, acc);
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[slot]);
-        }
-        // fixed-order reduction over the consumer warps
-#pragma unroll
-        for (int t = 0; t < 2; ++t)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) red[((warp * 2 + t) * 32 + lane) * 4 + e] = acc[t][e];
-        consumer_sync();
-        {
-            int t = tid >> 7, l = (tid >> 2) & 31, e = tid & 3;
-            float sum = 0.0f;
-#pragma unroll
-            for (int w = 0; w < kGemvWarps; ++w) sum += red[((w * 2 + t) * 32 + l) * 4 + e];
-            int row = 16 * t + (l >> 2) + 8 * (e >> 1);
-            int col = 2 * (l & 3) + (e & 1);
-            out[row * 8 + col] = sum;
-        }
-        consumer_sync();
-        gemv_epilogue(wk.seg[it.seg], it, wk.S, wk.swiglu_limit, out);
-    }
+    if (wk.S <= 4)
+        gemv_consume<FA, FB, true>(wk, smem, kSlotBytes, full, empty, red, out);
+    else
+        gemv_consume<FA, FB, false>(wk, smem, kSlotBytes, full, empty, red, out);
 }
 
 inline int gemv_tiles(const GemvSeg &s) {

@@ -19,46 +19,6 @@
 
 namespace fc {
 
-// Router logits, fp32 weights [E][D]: one block per expert row, the 256
-// threads split D (float4 loads), per-row partial sums reduced in a fixed
-// order (warp butterfly, then warps in index order).
-__global__ void __launch_bounds__(256) router_logits_kernel(const float *W, const float *x, int E,
-                                                            int D, int S, float *logits) {
-    pdl_wait();
-    pdl_release();
-    __shared__ float red[8][8];
-    const int e = blockIdx.x;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    float acc[8];
-#pragma unroll
-    for (int s = 0; s < 8; ++s) acc[s] = 0.0f;
-    const float4 *w4 = reinterpret_cast<const float4 *>(W + (size_t)e * D);
-    for (int k4 = threadIdx.x; k4 < D / 4; k4 += blockDim.x) {
-        float4 w = __ldg(w4 + k4);
-#pragma unroll
-        for (int s = 0; s < 8; ++s) {
-            if (s < S) {
-                float4 xv = *reinterpret_cast<const float4 *>(x + (size_t)s * D + 4 * k4);
-                acc[s] = fmaf(w.x, xv.x, acc[s]);
-                acc[s] = fmaf(w.y, xv.y, acc[s]);
-                acc[s] = fmaf(w.z, xv.z, acc[s]);
-                acc[s] = fmaf(w.w, xv.w, acc[s]);
-            }
-        }
-    }
-#pragma unroll
-    for (int s = 0; s < 8; ++s) {
-        float v = warp_sum(acc[s]);
-        if (lane == 0) red[warp][s] = v;
-    }
-    __syncthreads();
-    if (threadIdx.x < S) {
-        float t = 0.0f;
-        for (int w = 0; w < 8; ++w) t += red[w][threadIdx.x];
-        logits[(size_t)threadIdx.x * E + e] = t;
-    }
-}
-
 struct RouteParams {
     int E, K, S;
     int score_fn, normalize;
@@ -72,6 +32,7 @@ struct RouteParams {
     int *n_active;           // number of local active experts
     int *active;             // [max_slots] ascending expert ids (local range)
     float *coef;             // [max_slots][8] coefficient of slot for row s
+    int *arrivals;           // block arrival counter (zero between launches)
 };
 
 __device__ __forceinline__ float route_score(float x, int fn) {
@@ -85,97 +46,132 @@ __device__ __forceinline__ float route_score(float x, int fn) {
     return 1.0f / (1.0f + expf(-x));
 }
 
-// One block of 256 threads; warp s handles row s (S <= 8).  Scores are
-// computed lane-parallel with fixed-order warp reductions, top-k by repeated
-// warp argmax (lower index on ties), finalize in slot order on lane 0; then
-// the ascending list of active local experts and their per-row coefficients
-// come from a block-wide scan.
 constexpr int kRouteThreads = 256;
 
-__global__ void __launch_bounds__(kRouteThreads) route_select_kernel(const float *logits, RouteParams p) {
-    pdl_wait();
-    pdl_release();
-    extern __shared__ float rs_smem[];  // scores [8][E], choice [8][E]
+// Scores and top-k of row s by one warp; lane l holds experts l + 32 i
+// (i < PER) in registers.  Scores by MoeScoreFn (softmax: lane sums in
+// ascending expert order, then a butterfly), top-k by repeated warp argmax
+// over score + bias (lower index on ties), finalize in slot order on lane 0
+// (moe_route.h:26-99).
+template <int PER>
+__device__ __forceinline__ void route_row(const float *logits, const RouteParams &p, int s,
+                                          int (&sel)[64], float (&selw)[64]) {
+    const int lane = threadIdx.x & 31;
+    const int E = p.E, K = p.K;
+    float sc[PER], ch[PER];
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+        int e = lane + 32 * i;
+        sc[i] = e < E ? __ldcg(logits + (size_t)s * E + e) : -INFINITY;
+    }
+    if (p.score_fn == FC_SCORE_SOFTMAX) {
+        float m = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < PER; ++i) m = fmaxf(m, sc[i]);
+        m = warp_max(m);
+        float sum = 0.0f;
+#pragma unroll
+        for (int i = 0; i < PER; ++i) {
+            float v = lane + 32 * i < E ? expf(sc[i] - m) : 0.0f;
+            sc[i] = v;
+            sum += v;
+        }
+        sum = warp_sum(sum);
+#pragma unroll
+        for (int i = 0; i < PER; ++i) sc[i] = sc[i] / sum;
+    } else {
+#pragma unroll
+        for (int i = 0; i < PER; ++i) sc[i] = route_score(sc[i], p.score_fn);
+    }
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+        int e = lane + 32 * i;
+        ch[i] = e < E ? sc[i] + (p.bias ? p.bias[e] : 0.0f) : -INFINITY;
+    }
+    // score of expert e (same value on every lane)
+    auto score_of = [&](int e) {
+        float v = 0.0f;
+#pragma unroll
+        for (int i = 0; i < PER; ++i)
+            if (i == (e >> 5)) v = sc[i];
+        return __shfl_sync(0xffffffffu, v, e & 31);
+    };
+    if (p.hash) {
+        int mine = lane < K ? p.hash[(size_t)p.ids[s] * K + lane] : 0;
+        for (int k = 0; k < K; ++k) {
+            int e = __shfl_sync(0xffffffffu, mine, k & 31);
+            if (k >= 32) e = p.hash[(size_t)p.ids[s] * K + k];
+            float w = score_of(e);
+            if (lane == 0) {
+                sel[k] = e;
+                selw[k] = w;
+            }
+        }
+    } else {
+        uint32_t taken = 0;
+        for (int k = 0; k < K; ++k) {
+            float best = -INFINITY;
+            int bi = 0x7fffffff;
+#pragma unroll
+            for (int i = 0; i < PER; ++i) {
+                int e = lane + 32 * i;
+                if (e < E && !((taken >> i) & 1u) && ch[i] > best) {
+                    best = ch[i];
+                    bi = e;
+                }
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                float ov = __shfl_xor_sync(0xffffffffu, best, o);
+                int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
+            }
+            if (bi == 0x7fffffff) bi = 0;  // no finite candidate left
+            if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+            float w = score_of(bi);
+            if (lane == 0) {
+                sel[k] = bi;
+                selw[k] = w;
+            }
+        }
+    }
+    __syncwarp();
+    if (lane == 0) {  // moe_route_finalize, moe_route.h:89-99
+        float sum = 0.0f;
+        if (p.normalize) {
+            for (int k = 0; k < K; ++k) sum += selw[k];
+            sum += 1e-20f;
+        }
+        for (int k = 0; k < K; ++k) {
+            float w = p.normalize ? selw[k] / sum : selw[k];
+            w = w * p.routed_scale;
+            p.route_ids[s * K + k] = sel[k];
+            p.route_w[s * K + k] = w;
+            selw[k] = w;
+        }
+    }
+    __syncwarp();
+}
+
+// Selection for all rows by one block (warp s = row s), then the ascending
+// list of active local experts and their per-row coefficients from a
+// block-wide scan (the device-side replacement of prepare_route_tables).
+__device__ __forceinline__ void route_select_block(const float *logits, const RouteParams &p) {
     __shared__ int used_flag[1024];
     __shared__ int slot_of[1024];
     __shared__ int warp_total[kRouteThreads / 32];
     __shared__ int sel[8][64];
     __shared__ float selw[8][64];
-    const int E = p.E, K = p.K;
-    float *scores = rs_smem;
-    float *choice = rs_smem + 8 * E;
+    const int K = p.K;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int e = threadIdx.x; e < E; e += blockDim.x) used_flag[e] = 0;
-    for (int i = threadIdx.x; i < p.S * E; i += blockDim.x) choice[i] = logits[i];
-    __syncthreads();
+    for (int e = threadIdx.x; e < 1024; e += blockDim.x) used_flag[e] = 0;
     if (warp < p.S) {
-        const int s = warp;
-        float *lg = choice + s * E;
-        float *sc = scores + s * E;
-        float *ch = choice + s * E;
-        if (p.score_fn == FC_SCORE_SOFTMAX) {  // moe_route.h:26-37
-            float m = -INFINITY;
-            for (int e = lane; e < E; e += 32) m = fmaxf(m, lg[e]);
-            m = warp_max(m);
-            float sum = 0.0f;
-            for (int e = lane; e < E; e += 32) {
-                float v = expf(lg[e] - m);
-                sc[e] = v;
-                sum += v;
-            }
-            sum = warp_sum(sum);
-            __syncwarp();
-            for (int e = lane; e < E; e += 32) sc[e] = sc[e] / sum;
-        } else {
-            for (int e = lane; e < E; e += 32) sc[e] = route_score(lg[e], p.score_fn);
-        }
-        __syncwarp();
-        for (int e = lane; e < E; e += 32) ch[e] = sc[e] + (p.bias ? p.bias[e] : 0.0f);
-        __syncwarp();
-        if (p.hash) {
-            if (lane < K) {
-                int e = p.hash[(size_t)p.ids[s] * K + lane];
-                sel[s][lane] = e;
-                selw[s][lane] = sc[e];
-            }
-        } else {
-            for (int k = 0; k < K; ++k) {
-                float best = -INFINITY;
-                int bi = 0x7fffffff;
-                for (int e = lane; e < E; e += 32) {
-                    bool taken = false;
-                    for (int t = 0; t < k; ++t) taken |= sel[s][t] == e;
-                    float v = ch[e];
-                    if (!taken && v > best) { best = v; bi = e; }
-                }
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) {
-                    float ov = __shfl_xor_sync(0xffffffffu, best, o);
-                    int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-                    if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
-                }
-                if (lane == 0) {
-                    sel[s][k] = bi;
-                    selw[s][k] = sc[bi];
-                }
-                __syncwarp();
-            }
-        }
-        __syncwarp();
-        if (lane == 0) {  // moe_route_finalize, moe_route.h:89-99
-            float sum = 0.0f;
-            if (p.normalize) {
-                for (int k = 0; k < K; ++k) sum += selw[s][k];
-                sum += 1e-20f;
-            }
-            for (int k = 0; k < K; ++k) {
-                float w = p.normalize ? selw[s][k] / sum : selw[s][k];
-                w = w * p.routed_scale;
-                p.route_ids[s * K + k] = sel[s][k];
-                p.route_w[s * K + k] = w;
-                selw[s][k] = w;
-            }
-        }
+        const int per = (p.E + 31) / 32;
+        if (per <= 2) route_row<2>(logits, p, warp, sel[warp], selw[warp]);
+        else if (per <= 4) route_row<4>(logits, p, warp, sel[warp], selw[warp]);
+        else if (per <= 8) route_row<8>(logits, p, warp, sel[warp], selw[warp]);
+        else if (per <= 16) route_row<16>(logits, p, warp, sel[warp], selw[warp]);
+        else route_row<32>(logits, p, warp, sel[warp], selw[warp]);
     }
     __syncthreads();
     if (threadIdx.x < p.S * K) {
@@ -220,6 +216,59 @@ __global__ void __launch_bounds__(kRouteThreads) route_select_kernel(const float
         int e = sel[s][k];
         if (e >= p.expert_lo && e < p.expert_hi) p.coef[slot_of[e - p.expert_lo] * 8 + s] = selw[s][k];
     }
+}
+
+// Router: one block per expert computes its logits for every row (fp32
+// weights [E][D], float4 loads, fixed-order reduction: warp butterfly, then
+// warps in index order); the last block to finish runs the selection and
+// the expert grouping.
+__global__ void __launch_bounds__(kRouteThreads) router_kernel(const float *W, const float *x, int D,
+                                                               float *logits, RouteParams p) {
+    pdl_wait();
+    pdl_release();
+    __shared__ float red[8][8];
+    __shared__ int is_last;
+    const int e = blockIdx.x, E = p.E, S = p.S;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    float acc[8];
+#pragma unroll
+    for (int s = 0; s < 8; ++s) acc[s] = 0.0f;
+    const float4 *w4 = reinterpret_cast<const float4 *>(W + (size_t)e * D);
+    for (int k4 = threadIdx.x; k4 < D / 4; k4 += blockDim.x) {
+        float4 w = __ldg(w4 + k4);
+#pragma unroll
+        for (int s = 0; s < 8; ++s) {
+            if (s < S) {
+                float4 xv = *reinterpret_cast<const float4 *>(x + (size_t)s * D + 4 * k4);
+                acc[s] = fmaf(w.x, xv.x, acc[s]);
+                acc[s] = fmaf(w.y, xv.y, acc[s]);
+                acc[s] = fmaf(w.z, xv.z, acc[s]);
+                acc[s] = fmaf(w.w, xv.w, acc[s]);
+            }
+        }
+    }
+#pragma unroll
+    for (int s = 0; s < 8; ++s) {
+        float v = warp_sum(acc[s]);
+        if (lane == 0) red[warp][s] = v;
+    }
+    __syncthreads();
+    if (threadIdx.x < S) {
+        float t = 0.0f;
+        for (int w = 0; w < 8; ++w) t += red[w][threadIdx.x];
+        logits[(size_t)threadIdx.x * E + e] = t;
+        __threadfence();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int prev = atomicAdd(p.arrivals, 1);
+        is_last = prev == E - 1;
+        if (is_last) *p.arrivals = 0;
+    }
+    __syncthreads();
+    if (!is_last) return;
+    __threadfence();
+    route_select_block(logits, p);
 }
 
 // resid[s][d] += (sum over slots ascending of coef * routed[slot][s][d])

@@ -127,6 +127,7 @@ struct FcSession {
     float *logits = nullptr, *layer_out = nullptr;
     HeadPartials hp{};
     int *d_err = nullptr;    // bit 1: a bounded wait in a kernel gave up
+    int *route_arrivals = nullptr;   // router block counter (zero between launches)
     Staging *d_stage = nullptr, *h_stage = nullptr;
     Result *d_res = nullptr, *h_res = nullptr;
     std::map<int, cudaGraphExec_t> graphs;
@@ -593,8 +594,6 @@ cudaError_t record_forward(FcSession *s, int S) {
             mark(s, "gemv_dense_down");
         } else {
             int E = c.expert_count, K = c.experts_per_token;
-            FC_TRY(launch_pdl(router_logits_kernel, dim3(E), dim3(256), 0, st, y.router.p, s->xn, E, D, S, s->router_logits));
-            mark(s, "router_logits");
             RouteParams rp{};
             rp.E = E; rp.K = K; rp.S = S;
             rp.score_fn = c.score_fn;
@@ -610,9 +609,10 @@ cudaError_t record_forward(FcSession *s, int S) {
             rp.n_active = s->n_active;
             rp.active = s->active;
             rp.coef = s->coef;
-            FC_TRY(launch_pdl(route_select_kernel, dim3(1), dim3(256), 2 * 8 * E * sizeof(float), st, s->router_logits, rp));
-            FC_TRY(cudaGetLastError());
-            mark(s, "route_select");
+            rp.arrivals = s->route_arrivals;
+            FC_TRY(launch_pdl(router_kernel, dim3(E), dim3(kRouteThreads), 0, st, y.router.p, s->xn, D,
+                              s->router_logits, rp));
+            mark(s, "router");
             int I = c.moe_intermediate_size, kpI = kpad(I);
             int W = I * c.shared_expert_count, kpW = kpad(std::max(W, 1));
             // gate / up + SwiGLU of the active routed experts and the shared expert
@@ -706,7 +706,7 @@ cudaError_t prefer_shared_carveout() {
         (const void *)embed_kernel, (const void *)rmsnorm_kernel, (const void *)mla_prep_kernel,
         (const void *)mla_absorb_kernel, (const void *)mla_attention_kernel<512, 64>,
         (const void *)mla_attention_kernel<256, 64>, (const void *)mla_combine_kernel,
-        (const void *)router_logits_kernel, (const void *)route_select_kernel,
+        (const void *)router_kernel,
         (const void *)moe_combine_kernel, (const void *)head_partial_kernel,
         (const void *)accept_kernel,
 #define FC_GEMV_PTR(A, B) (const void *)gemv_kernel<A, B>,
@@ -801,9 +801,13 @@ int run_pass(FcSession *s, const int *ids, int rows, int k, const FcAcceptConfig
         s->stats.graph_replays++;
     }
     if (e != cudaSuccess) return set_error(err, n, "CUDA forward failed: %s", cudaGetErrorString(e));
-    if (!s->profiling && s->h_res->error)
+    if (!s->profiling && s->h_res->error) {
+        // a kernel that gave up may have left the router counter mid-count
+        cudaMemsetAsync(s->route_arrivals, 0, sizeof(int), s->stream);
+        cudaStreamSynchronize(s->stream);
         return set_error(err, n, "a kernel wait gave up (error bits 0x%x); results are invalid",
                          s->h_res->error);
+    }
     s->stats.command_buffers++;
     s->last_rows = rows;
     return 1;
@@ -1071,6 +1075,7 @@ int fc_session_create(FcSession **out, FcModel *m, const FcOptions *options, cha
     ok = ok && salloc(s, s->hp.amax, hc) && salloc(s, s->hp.aidx, hc) && salloc(s, s->hp.zmax, hc) &&
          salloc(s, s->hp.zsum, hc) && salloc(s, s->hp.gval, hc) && salloc(s, s->hp.gidx, hc);
     ok = ok && salloc(s, s->d_stage, 1) && salloc(s, s->d_res, 1) && salloc(s, s->d_err, 1);
+    ok = ok && salloc(s, s->route_arrivals, 1);
     ok = ok && cudaMallocHost(&s->h_stage, sizeof(Staging)) == cudaSuccess;
     ok = ok && cudaMallocHost(&s->h_res, sizeof(Result)) == cudaSuccess;
     if (ok) {
@@ -1080,10 +1085,7 @@ int fc_session_create(FcSession **out, FcModel *m, const FcOptions *options, cha
         cudaError_t e2 = cudaFuncSetAttribute(mla_attention_kernel<256, 64>,
                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
                                               (int)AttnSmem::total(320));
-        cudaError_t e3 = cudaFuncSetAttribute(route_select_kernel,
-                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                              2 * 8 * 1024 * 4);
-        ok = e1 == cudaSuccess && e2 == cudaSuccess && e3 == cudaSuccess &&
+        ok = e1 == cudaSuccess && e2 == cudaSuccess &&
              gemv_prepare_all() == cudaSuccess && prefer_shared_carveout() == cudaSuccess;
     }
     if (!ok) {
