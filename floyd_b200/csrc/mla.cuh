@@ -72,10 +72,17 @@ constexpr int kNormThreads = 1024;
 __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const float *x, int ldx, const float *w,
                                                                int D, float eps, __half *yq, int kpy,
                                                                float *y, int ldy) {
-    pdl_wait();
-    pdl_release();
     __shared__ float scratch[32];
     const int s = blockIdx.x, n4 = D / 4;
+    // the norm weights are constant: fetch them before waiting for x
+    float4 wv[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        int k4 = threadIdx.x + i * blockDim.x;
+        if (k4 < n4) wv[i] = __ldg(reinterpret_cast<const float4 *>(w) + k4);
+    }
+    pdl_wait();
+    pdl_release();
     const float4 *xs = reinterpret_cast<const float4 *>(x + (size_t)s * ldx);
     float4 v[4];
     float ss = 0.0f;
@@ -93,9 +100,8 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const float *x, i
     for (int i = 0; i < 4; ++i) {
         int k4 = threadIdx.x + i * blockDim.x;
         if (k4 >= n4) continue;
-        float4 wv = reinterpret_cast<const float4 *>(w)[k4];
-        float o[4] = {v[i].x * scale * wv.x, v[i].y * scale * wv.y, v[i].z * scale * wv.z,
-                      v[i].w * scale * wv.w};
+        float o[4] = {v[i].x * scale * wv[i].x, v[i].y * scale * wv[i].y, v[i].z * scale * wv[i].z,
+                      v[i].w * scale * wv[i].w};
         if (yq) {
             __half hi[4], lo[4];
 #pragma unroll
@@ -175,8 +181,9 @@ __global__ void mla_prep_kernel(const float *ckv, const float *q, const float *n
 // Query absorption (moonlight_kernels.metal:218-245):
 //   qcat[s*H+h][l] = fp16( sum_n q[s][h][n] * W_kvb[h*(nope+v)+n][l] )
 // grid (H, L/64), 256 threads: the W_UK block [nope][64] is dequantized into
-// shared memory with all loads in flight, then each output sums over n in
-// fp32 sequentially without contraction (the oracle's order).
+// shared memory before waiting for the queries (weights are constant), then
+// each output sums over n in fp32 sequentially without contraction (the
+// oracle's order).
 // ---------------------------------------------------------------------------
 constexpr int kAbsorbCols = 64;
 constexpr int kAbsorbMaxNope = 128;
@@ -185,8 +192,6 @@ __global__ void __launch_bounds__(256) mla_absorb_kernel(int fmt, const uint8_t 
                                                          int kp, const float *q, int S, int H,
                                                          int nope, int vdim, int R, int L,
                                                          __half *qcat) {
-    pdl_wait();
-    pdl_release();
     __shared__ float wsm[kAbsorbMaxNope][kAbsorbCols + 1];
     __shared__ float qs[8][kAbsorbMaxNope];
     __shared__ __align__(16) uint8_t raw[kAbsorbMaxNope / kTileRows][1152];
@@ -201,11 +206,7 @@ __global__ void __launch_bounds__(256) mla_absorb_kernel(int fmt, const uint8_t 
         int t = i / (blk / 16), v = i % (blk / 16);
         const uint4 *src = reinterpret_cast<const uint4 *>(
             w + ((size_t)(tile0 + t) * nchunks + c) * blk);
-        reinterpret_cast<uint4 *>(raw[t])[v] = src[v];
-    }
-    for (int i = threadIdx.x; i < S * nope; i += blockDim.x) {
-        int s = i / nope, n = i % nope;
-        qs[s][n] = q[((size_t)s * H + h) * qw + n];
+        reinterpret_cast<uint4 *>(raw[t])[v] = __ldg(src + v);
     }
     __syncthreads();
     const int srb = scale_row_bytes(fmt), el = scale_elem_bytes(fmt);
@@ -225,13 +226,20 @@ __global__ void __launch_bounds__(256) mla_absorb_kernel(int fmt, const uint8_t 
             if (fmt == FC_FMT_Q4) {
                 wv = (float)((int)code - 8) * __half2float(*reinterpret_cast<const __half *>(sp));
             } else {
-                const float table[8] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};
-                float m = table[code & 7];
+                // e2m1 magnitude: 0, 0.5, 1, 1.5, 2, 3, 4, 6
+                uint32_t e = (code >> 1) & 3u, mb = code & 1u;
+                float m = e == 0 ? 0.5f * (float)mb : (float)(2u + mb) * (float)(1u << e) * 0.25f;
                 if (code & 8) m = -m;
                 wv = m * e8m0_to_float(*sp);
             }
         }
         wsm[n][col] = wv;
+    }
+    pdl_wait();
+    pdl_release();
+    for (int i = threadIdx.x; i < S * nope; i += blockDim.x) {
+        int s = i / nope, n = i % nope;
+        qs[s][n] = q[((size_t)s * H + h) * qw + n];
     }
     __syncthreads();
     for (int o = threadIdx.x; o < S * kAbsorbCols; o += blockDim.x) {
@@ -538,6 +546,64 @@ mla_attention_kernel(const __half *cache, const __half *qcat, int S, int H, int 
 constexpr int kCombineThreads = 128;
 constexpr int kMaxSplits = 1024;
 
+template <int NS>
+__device__ __forceinline__ void combine_row(const float *part_o, const float *part_m, const float *part_l,
+                                            int splits, int nq, int q, int L, int l, float *wts, float *red,
+                                            float &out) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    // the partial outputs of every split, loaded together
+    float o[NS > 0 ? NS : 1];
+#pragma unroll
+    for (int i = 0; i < NS; ++i)
+        o[i] = (i < splits && l < L) ? __ldcg(part_o + ((size_t)i * nq + q) * L + l) : 0.0f;
+    float m = -INFINITY, mi = -INFINITY, li = 0.0f;
+    for (int i = threadIdx.x; i < splits; i += kCombineThreads) {
+        mi = __ldcg(part_m + (size_t)i * nq + q);
+        li = __ldcg(part_l + (size_t)i * nq + q);
+        m = fmaxf(m, mi);
+    }
+    m = warp_max(m);
+    if (lane == 0) red[warp] = m;
+    __syncthreads();
+    float M = red[0];
+    for (int w = 1; w < kCombineThreads / 32; ++w) M = fmaxf(M, red[w]);
+    __syncthreads();
+    float den = 0.0f;
+    if (splits <= kCombineThreads) {
+        if (threadIdx.x < splits) {
+            float wi = mi == -INFINITY ? 0.0f : expf(mi - M);
+            wts[threadIdx.x] = wi;
+            if (wi != 0.0f) den = wi * li;
+        }
+    } else {
+        for (int i = threadIdx.x; i < splits; i += kCombineThreads) {
+            float mj = __ldcg(part_m + (size_t)i * nq + q);
+            float wi = mj == -INFINITY ? 0.0f : expf(mj - M);
+            wts[i] = wi;
+            if (wi != 0.0f) den += wi * __ldcg(part_l + (size_t)i * nq + q);
+        }
+    }
+    den = warp_sum(den);
+    if (lane == 0) red[warp] = den;
+    __syncthreads();
+    den = 0.0f;
+    for (int w = 0; w < kCombineThreads / 32; ++w) den += red[w];
+    float acc = 0.0f;
+    if (NS > 0) {
+#pragma unroll
+        for (int i = 0; i < NS; ++i) {
+            float wi = i < splits ? wts[i] : 0.0f;
+            if (wi != 0.0f) acc += wi * o[i];
+        }
+    } else {
+        for (int i = 0; i < splits; ++i) {
+            float wi = wts[i];
+            if (wi != 0.0f) acc += wi * __ldcg(part_o + ((size_t)i * nq + q) * L + l);
+        }
+    }
+    out = acc / den;
+}
+
 __global__ void __launch_bounds__(kCombineThreads)
 mla_combine_kernel(const float *part_o, const float *part_m, const float *part_l, int splits, int S,
                    int H, int L, __half *ctx_xq, size_t head_stride) {
@@ -546,37 +612,15 @@ mla_combine_kernel(const float *part_o, const float *part_m, const float *part_l
     __shared__ float wts[kMaxSplits];
     __shared__ float red[kCombineThreads / 32];
     const int q = blockIdx.x, nq = S * H;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    float m = -INFINITY;
-    for (int i = threadIdx.x; i < splits; i += kCombineThreads) m = fmaxf(m, part_m[(size_t)i * nq + q]);
-    m = warp_max(m);
-    if (lane == 0) red[warp] = m;
-    __syncthreads();
-    float M = red[0];
-    for (int w = 1; w < kCombineThreads / 32; ++w) M = fmaxf(M, red[w]);
-    __syncthreads();
-    float den = 0.0f;
-    for (int i = threadIdx.x; i < splits; i += kCombineThreads) {
-        float mi = part_m[(size_t)i * nq + q];
-        float wi = mi == -INFINITY ? 0.0f : expf(mi - M);
-        wts[i] = wi;
-        if (wi != 0.0f) den += wi * part_l[(size_t)i * nq + q];
-    }
-    den = warp_sum(den);
-    if (lane == 0) red[warp] = den;
-    __syncthreads();
-    den = 0.0f;
-    for (int w = 0; w < kCombineThreads / 32; ++w) den += red[w];
     const int l = blockIdx.y * kCombineThreads + threadIdx.x;
+    float v;
+    if (splits <= 16) combine_row<16>(part_o, part_m, part_l, splits, nq, q, L, l, wts, red, v);
+    else if (splits <= 32) combine_row<32>(part_o, part_m, part_l, splits, nq, q, L, l, wts, red, v);
+    else if (splits <= 64) combine_row<64>(part_o, part_m, part_l, splits, nq, q, L, l, wts, red, v);
+    else combine_row<0>(part_o, part_m, part_l, splits, nq, q, L, l, wts, red, v);
     if (l >= L) return;
-    float acc = 0.0f;
-#pragma unroll 4
-    for (int i = 0; i < splits; ++i) {
-        float wi = wts[i];
-        if (wi != 0.0f) acc += wi * part_o[((size_t)i * nq + q) * L + l];
-    }
     const int s = q / H, h = q % H;
-    store_xq(ctx_xq + (size_t)h * head_stride, L, s, l, acc / den);
+    store_xq(ctx_xq + (size_t)h * head_stride, L, s, l, v);
 }
 
 }  // namespace fc

@@ -224,8 +224,6 @@ __device__ __forceinline__ void route_select_block(const float *logits, const Ro
 // the expert grouping.
 __global__ void __launch_bounds__(kRouteThreads) router_kernel(const float *W, const float *x, int D,
                                                                float *logits, RouteParams p) {
-    pdl_wait();
-    pdl_release();
     __shared__ float red[8][8];
     __shared__ int is_last;
     const int e = blockIdx.x, E = p.E, S = p.S;
@@ -234,8 +232,27 @@ __global__ void __launch_bounds__(kRouteThreads) router_kernel(const float *W, c
 #pragma unroll
     for (int s = 0; s < 8; ++s) acc[s] = 0.0f;
     const float4 *w4 = reinterpret_cast<const float4 *>(W + (size_t)e * D);
-    for (int k4 = threadIdx.x; k4 < D / 4; k4 += blockDim.x) {
-        float4 w = __ldg(w4 + k4);
+    // the weight row is constant: up to 4 float4 per thread fetched before
+    // waiting for the activations
+    constexpr int kPre = 4;
+    float4 wpre[kPre];
+#pragma unroll
+    for (int i = 0; i < kPre; ++i) {
+        int k4 = threadIdx.x + i * kRouteThreads;
+        if (k4 < D / 4) wpre[i] = __ldg(w4 + k4);
+    }
+    pdl_wait();
+    pdl_release();
+    for (int k4 = threadIdx.x, i = 0; k4 < D / 4; k4 += blockDim.x, ++i) {
+        float4 w;
+        if (i < kPre) {
+            w = wpre[0];
+#pragma unroll
+            for (int t = 1; t < kPre; ++t)
+                if (i == t) w = wpre[t];
+        } else {
+            w = __ldg(w4 + k4);
+        }
 #pragma unroll
         for (int s = 0; s < 8; ++s) {
             if (s < S) {
@@ -275,21 +292,51 @@ __global__ void __launch_bounds__(kRouteThreads) router_kernel(const float *W, c
 //                + shared[s][d]                           (moe_exec.h:97-110)
 // Products and sums are rounded separately (no contraction), the order the
 // C reference spells out.
-__global__ void moe_combine_kernel(float *resid, const float *routed, const float *shared,
-                                   const float *coef, const int *n_active, int S, int D,
-                                   int max_batch) {
+constexpr int kMoeCombineThreads = 256;
+
+__global__ void __launch_bounds__(kMoeCombineThreads)
+moe_combine_kernel(float *resid, const float *routed, const float *shared, const float *coef,
+                   const int *n_active, int S, int D, int max_batch) {
     pdl_wait();
     pdl_release();
-    int idx = blockIdx.x * blockDim.x + threadIdx.x;
-    if (idx >= S * D) return;
-    int s = idx / D, d = idx % D;
-    int n = *n_active;
-    float y = 0.0f;
-    for (int slot = 0; slot < n; ++slot) {
-        float c = coef[slot * 8 + s];
-        if (c != 0.0f)
-            y = __fadd_rn(y, __fmul_rn(c, routed[((size_t)slot * max_batch + s) * D + d]));
+    __shared__ int list[1024];
+    __shared__ float lc[1024];
+    __shared__ int count;
+    // blocks of one row: blockIdx.x = s * (D / 256) + column block
+    const int per_row = (D + kMoeCombineThreads - 1) / kMoeCombineThreads;
+    const int s = blockIdx.x / per_row;
+    const int d = (blockIdx.x % per_row) * kMoeCombineThreads + threadIdx.x;
+    const int n = *n_active;
+    if (threadIdx.x < 32) {  // ascending list of the slots that feed row s
+        int base = 0;
+        for (int i0 = 0; i0 < n; i0 += 32) {
+            int slot = i0 + threadIdx.x;
+            float c = slot < n ? coef[slot * 8 + s] : 0.0f;
+            unsigned m = __ballot_sync(0xffffffffu, c != 0.0f);
+            if (c != 0.0f) {
+                int at = base + __popc(m & ((1u << threadIdx.x) - 1u));
+                if (at < 1024) {
+                    list[at] = slot;
+                    lc[at] = c;
+                }
+            }
+            base += __popc(m);
+        }
+        if (threadIdx.x == 0) count = base < 1024 ? base : 1024;
     }
+    __syncthreads();
+    if (d >= D) return;
+    const int cnt = count;
+    float y = 0.0f;
+    int i = 0;
+    for (; i + 8 <= cnt; i += 8) {
+        float v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) v[u] = __ldcg(routed + ((size_t)list[i + u] * max_batch + s) * D + d);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) y = __fadd_rn(y, __fmul_rn(lc[i + u], v[u]));
+    }
+    for (; i < cnt; ++i) y = __fadd_rn(y, __fmul_rn(lc[i], __ldcg(routed + ((size_t)list[i] * max_batch + s) * D + d)));
     if (shared) y = __fadd_rn(y, shared[(size_t)s * D + d]);
     resid[(size_t)s * D + d] = __fadd_rn(resid[(size_t)s * D + d], y);
 }

@@ -664,7 +664,8 @@ cudaError_t record_forward(FcSession *s, int S) {
             dn.err = s->d_err;
             FC_TRY(launch_gemv_work(ef, df, dn, m->sms, st));
             mark(s, "moe_down");
-            FC_TRY(launch_pdl(moe_combine_kernel, dim3((S * D + 255) / 256), dim3(256), 0, st, 
+            FC_TRY(launch_pdl(moe_combine_kernel, dim3(S * ((D + kMoeCombineThreads - 1) / kMoeCombineThreads)),
+                              dim3(kMoeCombineThreads), 0, st, 
                 s->resid, s->moe_part, y.s_down.count ? s->sh_part : nullptr, s->coef, s->n_active,
                 S, D, mb));
             mark(s, "moe_combine");
