@@ -10,6 +10,8 @@
 // with one H2D copy of the per-call parameters at its head and one D2H copy
 // of the result at its tail.  Everything runs on the GPU; a missing or
 // failing kernel is an error, never a CPU fallback.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -26,6 +28,7 @@
 #include "gemv.cuh"
 #include "head.cuh"
 #include "mla.cuh"
+#include "mla_tc.cuh"
 #include "moe.cuh"
 #include "synth.cuh"
 
@@ -112,6 +115,8 @@ struct FcSession {
     int last_rows = 0;
     int max_slots = 0;
     int splits = 0, chunks_per_split = 1;
+    bool attn_tc = true;     // tcgen05 attention (else the mma.sync kernel)
+    CUtensorMap qmap{}, kvmap{};  // TMA maps of qcat and of the latent cache
     int head_chunks = 0;
     std::vector<void *> allocs;
     FcStats stats{};
@@ -462,6 +467,27 @@ cudaError_t gemv1(int fmt, GemvSeg a, int S, float limit, int *err, int sms, cud
     return launch_gemv_batch(fmt, b, sms, st);
 }
 
+// 2-D fp16 tensor map [rows][inner] with a {64, box_rows} box and the
+// 128-byte swizzle the tcgen05 descriptors expect.
+bool make_map_f16(CUtensorMap *map, void *base, uint64_t inner, uint64_t rows, uint32_t box_rows) {
+    static PFN_cuTensorMapEncodeTiled_v12000 encode = [] {
+        void *fn = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            fn = nullptr;
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }();
+    if (!encode) return false;
+    cuuint64_t dims[2] = {inner, rows};
+    cuuint64_t strides[1] = {inner * 2};
+    cuuint32_t box[2] = {64, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    return encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, base, dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // Records a profiling event after the launch named `name` (eager passes only).
 void mark(FcSession *s, const char *name) {
     if (!s->profiling) return;
@@ -536,7 +562,19 @@ cudaError_t record_forward(FcSession *s, int S) {
                                                     NP, VD, R, L, s->qcat));
             mark(s, "mla_absorb");
         }
-        {
+        if (s->attn_tc) {
+            dim3 grid((S * H + kTcRows - 1) / kTcRows, 2, s->splits);
+            const int kv_row0 = l * s->opt.context_size, kps = s->chunks_per_split * kAttnKeys;
+            if (L == 512)
+                FC_TRY(launch_pdl(mla_attention_tc_kernel<512>, grid, dim3(kTcThreads), TcAttnPlan<512>::SMEM, st,
+                                  s->qmap, s->kvmap, kv_row0, S, H, kps, d_pos, scale, s->part_o, s->part_m,
+                                  s->part_l, s->d_err));
+            else
+                FC_TRY(launch_pdl(mla_attention_tc_kernel<256>, grid, dim3(kTcThreads), TcAttnPlan<256>::SMEM, st,
+                                  s->qmap, s->kvmap, kv_row0, S, H, kps, d_pos, scale, s->part_o, s->part_m,
+                                  s->part_l, s->d_err));
+            mark(s, "mla_attention");
+        } else {
             dim3 grid((S * H + kAttnQ - 1) / kAttnQ, s->splits);
             if (L == 512)
                 FC_TRY(launch_pdl(mla_attention_kernel<512, 64>, grid, dim3(kAttnThreads), s->attn_smem,
@@ -547,6 +585,8 @@ cudaError_t record_forward(FcSession *s, int S) {
                                   st, (const __half *)cache, (const __half *)s->qcat, S, H,
                                   s->chunks_per_split, d_pos, scale, s->part_o, s->part_m, s->part_l));
             mark(s, "mla_attention");
+        }
+        {
             size_t head_stride = (size_t)mb * kpL * 2;
             FC_TRY(launch_pdl(mla_combine_kernel, dim3(S * H, (L + kCombineThreads - 1) / kCombineThreads),
                               dim3(kCombineThreads), 0, st, (const float *)s->part_o,
@@ -707,6 +747,7 @@ cudaError_t prefer_shared_carveout() {
         (const void *)embed_kernel, (const void *)rmsnorm_kernel, (const void *)mla_prep_kernel,
         (const void *)mla_absorb_kernel, (const void *)mla_attention_kernel<512, 64>,
         (const void *)mla_attention_kernel<256, 64>, (const void *)mla_combine_kernel,
+        (const void *)mla_attention_tc_kernel<512>, (const void *)mla_attention_tc_kernel<256>,
         (const void *)router_kernel,
         (const void *)moe_combine_kernel, (const void *)head_partial_kernel,
         (const void *)accept_kernel,
@@ -1039,8 +1080,24 @@ int fc_session_create(FcSession **out, FcModel *m, const FcOptions *options, cha
     s->max_slots = std::min(nl, mb * K);
     // attention split plan: fixed per session (see mla.cuh)
     int max_chunks = (options->context_size + kAttnKeys - 1) / kAttnKeys;
-    int qtiles = (mb * H + kAttnQ - 1) / kAttnQ;
-    int target = std::max(1, 2 * 148 / qtiles);
+    // tcgen05 attention when a verify batch fills at least one 128-query
+    // tile; the choice depends only on the session shape, so decode and
+    // verify rows always take the same kernel (FLOYD_ATTENTION=mma / tc
+    // overrides it for measurements)
+    const char *attn_env = getenv("FLOYD_ATTENTION");
+    s->attn_tc = std::min(mb, 4) * H >= kTcRows;
+    if (attn_env && strcmp(attn_env, "mma") == 0) s->attn_tc = false;
+    if (attn_env && strcmp(attn_env, "tc") == 0) s->attn_tc = true;
+    int target;
+    if (s->attn_tc) {
+        // one wave of (128-query tile, half) CTAs at up to 4 rows; at most
+        // 64 splits (the combine's register budget)
+        int qt = (std::min(mb, 4) * H + kTcRows - 1) / kTcRows;
+        target = std::max(1, std::min(64, 148 / (2 * qt)));
+    } else {
+        int qtiles = (mb * H + kAttnQ - 1) / kAttnQ;
+        target = std::max(1, 2 * 148 / qtiles);
+    }
     s->chunks_per_split = (max_chunks + target - 1) / target;
     s->splits = (max_chunks + s->chunks_per_split - 1) / s->chunks_per_split;
     s->head_chunks = (V + kHeadChunk - 1) / kHeadChunk;
@@ -1054,7 +1111,9 @@ int fc_session_create(FcSession **out, FcModel *m, const FcOptions *options, cha
     ok = ok && salloc(s, s->qa, (size_t)mb * std::max(c.q_lora_rank, 1));
     ok = ok && salloc(s, s->qa_xq, (size_t)mb * kpad(std::max(c.q_lora_rank, 1)) * 2);
     ok = ok && salloc(s, s->ckv, (size_t)mb * (L + R));
-    ok = ok && salloc(s, s->qcat, (size_t)mb * H * (L + R));
+    // rows padded to whole 128-query tiles (the TMA box of the query tile)
+    const int q_rows = (mb * H + kTcRows - 1) / kTcRows * kTcRows;
+    ok = ok && salloc(s, s->qcat, (size_t)q_rows * (L + R));
     ok = ok && salloc(s, s->part_o, (size_t)s->splits * mb * H * L);
     ok = ok && salloc(s, s->part_m, (size_t)s->splits * mb * H);
     ok = ok && salloc(s, s->part_l, (size_t)s->splits * mb * H);
@@ -1079,6 +1138,10 @@ int fc_session_create(FcSession **out, FcModel *m, const FcOptions *options, cha
     ok = ok && salloc(s, s->route_arrivals, 1);
     ok = ok && cudaMallocHost(&s->h_stage, sizeof(Staging)) == cudaSuccess;
     ok = ok && cudaMallocHost(&s->h_res, sizeof(Result)) == cudaSuccess;
+    if (ok && s->attn_tc)
+        ok = make_map_f16(&s->qmap, s->qcat, (uint64_t)(L + R), (uint64_t)q_rows, kTcRows) &&
+             make_map_f16(&s->kvmap, s->cache, (uint64_t)(L + R), (uint64_t)c.layer_count * options->context_size,
+                          kTcKeys);
     if (ok) {
         cudaError_t e1 = cudaFuncSetAttribute(mla_attention_kernel<512, 64>,
                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1086,7 +1149,13 @@ int fc_session_create(FcSession **out, FcModel *m, const FcOptions *options, cha
         cudaError_t e2 = cudaFuncSetAttribute(mla_attention_kernel<256, 64>,
                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
                                               (int)AttnSmem::total(320));
-        ok = e1 == cudaSuccess && e2 == cudaSuccess &&
+        cudaError_t e3 = cudaFuncSetAttribute(mla_attention_tc_kernel<512>,
+                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              (int)TcAttnPlan<512>::SMEM);
+        cudaError_t e4 = cudaFuncSetAttribute(mla_attention_tc_kernel<256>,
+                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              (int)TcAttnPlan<256>::SMEM);
+        ok = e1 == cudaSuccess && e2 == cudaSuccess && e3 == cudaSuccess && e4 == cudaSuccess &&
              gemv_prepare_all() == cudaSuccess && prefer_shared_carveout() == cudaSuccess;
     }
     if (!ok) {
@@ -1572,3 +1641,9 @@ extern "C" int fc_matmul_noalloc(int format, float *y, const float *x, const voi
     if (herr) return set_error(error, error_size, "a kernel wait gave up");
     return 1;
 }
+
+#ifdef FC_TC_TRACE
+extern "C" int fc_debug_tc_trace(unsigned long long *out, int n) {
+    return cudaMemcpyFromSymbol(out, g_tc_trace, sizeof(unsigned long long) * (n < 256 ? n : 256)) == cudaSuccess;
+}
+#endif
