@@ -37,16 +37,40 @@ constexpr int kGemvWarps = 8;                      // consumer warps
 constexpr int kGemvThreads = (kGemvWarps + 1) * kWarp;  // + producer warp
 constexpr int kGemvConsumers = kGemvWarps * kWarp;
 constexpr int kGemvRows = 32;  // two 16-row tiles per work item
-constexpr int kStages = 4;     // bulk-copy stages in the ring
+constexpr int kStages = 4;     // most bulk-copy stages in the ring
 
 __host__ __device__ constexpr size_t gemv_stage_bytes(int fmt) {
     return (size_t)kGemvWarps * block_bytes(fmt);
 }
-__host__ __device__ constexpr size_t gemv_smem_bytes(int fa, int fb) {
-    return (size_t)kStages * 2 *
-               (gemv_stage_bytes(fa) > gemv_stage_bytes(fb) ? gemv_stage_bytes(fa)
-                                                             : gemv_stage_bytes(fb)) +
-           2 * kStages * 8;
+__host__ __device__ constexpr size_t gemv_slot_w(int fa, int fb) {
+    return gemv_stage_bytes(fa) > gemv_stage_bytes(fb) ? gemv_stage_bytes(fa) : gemv_stage_bytes(fb);
+}
+// Launches of the q8 / q4 formats also stage the stage's activation rows in
+// shared memory (the producer copies them next to the weights), so the
+// consumers never wait on L2 for B fragments; the MXFP4 launches, whose
+// wider chunks would leave too few stages, load B fragments from global.
+__host__ __device__ constexpr bool gemv_smem_b(int fa, int fb) {
+#ifdef FC_GEMV_NO_SMEM_B
+    return false;
+#else
+    return fa != FC_FMT_MXFP4 && fb != FC_FMT_MXFP4;
+#endif
+}
+// Bytes of one activation row of one stage (kGemvWarps chunks, hi + lo fp16,
+// 4 B per column), padded so the rows start in different banks.
+__host__ __device__ constexpr int gemv_b_row_bytes(int fa, int fb) {
+    return kGemvWarps * (chunk_cols(fa) > chunk_cols(fb) ? chunk_cols(fa) : chunk_cols(fb)) * 4 + 64;
+}
+constexpr size_t kGemvDynSmemBudget = 100 * 1024;  // two CTAs per SM with the static arrays
+__host__ __device__ constexpr size_t gemv_slot_bytes(int fa, int fb, int S) {
+    return 2 * gemv_slot_w(fa, fb) + (gemv_smem_b(fa, fb) ? (size_t)S * gemv_b_row_bytes(fa, fb) : 0);
+}
+inline int gemv_stages(int fa, int fb, int S) {
+    int n = (int)((kGemvDynSmemBudget - 2 * kStages * 8) / gemv_slot_bytes(fa, fb, S));
+    return n > kStages ? kStages : (n < 2 ? 2 : n);
+}
+inline size_t gemv_smem_bytes(int fa, int fb, int S) {
+    return (size_t)gemv_stages(fa, fb, S) * gemv_slot_bytes(fa, fb, S) + 2 * kStages * 8;
 }
 
 enum GemvEpilogue {
@@ -97,6 +121,10 @@ struct GemvWork {
     int S;
     float swiglu_limit;
     int *err;
+    int stages;               // ring depth (set by the launcher)
+#ifdef FC_GEMV_TRACE
+    int trace;
+#endif
 };
 
 // A resolved work item.
@@ -261,6 +289,20 @@ __device__ __forceinline__ void gemv_chunk(const uint8_t *blk0, const uint8_t *b
     }
 }
 
+#ifdef FC_GEMV_TRACE
+__device__ unsigned long long g_gemv_trace[512];
+__device__ int g_gemv_trace_items;
+static int g_host_trace_items = -1;
+#define GEMV_MARK(i)                                                                                  \
+    do {                                                                                              \
+        if (wk.trace && blockIdx.x == 0 && (i) < 512) g_gemv_trace[(i)] = clock64(); \
+    } while (0)
+#else
+#define GEMV_MARK(i) \
+    do {             \
+    } while (0)
+#endif
+
 __device__ __forceinline__ void consumer_sync() {
     asm volatile("bar.sync 1, %0;\n" ::"n"(kGemvConsumers) : "memory");
 }
@@ -322,8 +364,12 @@ __device__ __forceinline__ void reduce_warps(float *red, const float (&acc)[2][4
 // The consumer warps of gemv_kernel: per work item, wait for each stage,
 // multiply its chunk blocks, reduce, and run the epilogue.
 template <int FA, int FB, bool PACK>
-__device__ __forceinline__ void gemv_consume(const GemvWork &wk, const uint8_t *smem, size_t kSlotBytes,
-                                             uint64_t *full, uint64_t *empty, float *red, float *out) {
+__device__ __forceinline__ void gemv_consume(const GemvWork &wk, const uint8_t *smem, size_t kSlotW,
+                                             size_t kSlotBytes, uint64_t *full, uint64_t *empty, float *red,
+                                             float *out) {
+    constexpr bool kSmemB = gemv_smem_b(FA, FB);
+    constexpr int kBRow = gemv_b_row_bytes(FA, FB);
+    const int stages = kSmemB ? wk.stages : kStages;  // compile-time ring for the global-B kernels
     __shared__ float out_hi[kGemvRows * 8];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, j = lane & 3;
@@ -331,7 +377,8 @@ __device__ __forceinline__ void gemv_consume(const GemvWork &wk, const uint8_t *
     const int brow = PACK ? (g & 3) : g;
     const int bhalf = PACK ? (g >> 2) * 8 : 0;
     const bool has_b = brow < wk.S;
-    int idx = 0;
+    int idx = 0, slot = 0;
+    uint32_t phase = 0;  // parity of the ring pass `slot` is in
     for (int item = blockIdx.x; item < wk.total_items; item += gridDim.x) {
         GemvItem it;
         if (!resolve_item<FA, FB>(wk, item, it)) continue;
@@ -359,29 +406,52 @@ __device__ __forceinline__ void gemv_consume(const GemvWork &wk, const uint8_t *
                 }
             }
         };
-        // PACK: the next stage's fragments load while this stage computes
+        // (global B) PACK: the next stage's fragments load while this stage computes
         uint4 b_next[8];
-        if (PACK) load_b(warp, b_next);
+        if (!kSmemB && PACK) load_b(warp, b_next);
         for (int s = 0; s < nst; ++s, ++idx) {
-            const int slot = idx % kStages, round = idx / kStages;
             const int c = s * kGemvWarps + warp;
+            const uint8_t *sb = smem + (size_t)slot * kSlotBytes;
             uint4 b_raw[8];
-            if (PACK) {
+            if (!kSmemB) {
+                if (PACK) {
 #pragma unroll
-                for (int i = 0; i < 8; ++i) b_raw[i] = b_next[i];
-                if (s + 1 < nst) load_b(c + kGemvWarps, b_next);
-            } else {
-                load_b(c, b_raw);
+                    for (int i = 0; i < 8; ++i) b_raw[i] = b_next[i];
+                    if (s + 1 < nst) load_b(c + kGemvWarps, b_next);
+                } else {
+                    load_b(c, b_raw);
+                }
             }
-            mbar_wait_bounded(&full[slot], (uint32_t)(round & 1), wk.err);
+            if (warp == 0 && lane == 0) GEMV_MARK(128 + idx);
+            mbar_wait_bounded(&full[slot], phase, wk.err);
+            if (warp == 0 && lane == 0) GEMV_MARK(256 + idx);
+            if (kSmemB) {
+                // this stage's activation rows, copied by the producer
+                const uint8_t *brow_p = sb + 2 * kSlotW + (size_t)brow * kBRow + warp * kmmas * 64 + 16 * j;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const bool live = has_b && c < nchunks && i < kmmas;
+                    if (PACK) {
+                        uint2 v = live ? *reinterpret_cast<const uint2 *>(brow_p + i * 64 + bhalf) : make_uint2(0, 0);
+                        b_raw[i] = make_uint4(v.x, v.y, 0, 0);
+                    } else {
+                        b_raw[i] = live ? *reinterpret_cast<const uint4 *>(brow_p + i * 64) : make_uint4(0, 0, 0, 0);
+                    }
+                }
+            }
             if (c < nchunks) {
-                const uint8_t *b0 = smem + (slot * 2) * kSlotBytes + (size_t)warp * blk;
-                const uint8_t *b1 = it.t1 ? smem + (slot * 2 + 1) * kSlotBytes + (size_t)warp * blk : nullptr;
+                const uint8_t *b0 = sb + (size_t)warp * blk;
+                const uint8_t *b1 = it.t1 ? sb + kSlotW + (size_t)warp * blk : nullptr;
                 if (fa) gemv_chunk<FA, PACK>(b0, b1, b_raw, acc, accl);
                 else gemv_chunk<FB, PACK>(b0, b1, b_raw, acc, accl);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
+            if (warp == 0 && lane == 0) GEMV_MARK(384 + idx);
+            if (++slot == stages) {
+                slot = 0;
+                phase ^= 1u;
+            }
         }
         // out[row][s] = (hi sum over warps) + (lo sum over warps), the same
         // arithmetic for both forms
@@ -395,6 +465,7 @@ __device__ __forceinline__ void gemv_consume(const GemvWork &wk, const uint8_t *
         }
         consumer_sync();
         gemv_epilogue(wk.seg[it.seg], it, wk.S, wk.swiglu_limit, out);
+        if (tid == 0) GEMV_MARK(127);
     }
 }
 
@@ -403,15 +474,18 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ float red[kGemvWarps * 2 * 32 * 4];
     __shared__ float out[kGemvRows * 8];
-    constexpr size_t kSlotBytes = gemv_stage_bytes(FA) > gemv_stage_bytes(FB) ? gemv_stage_bytes(FA)
-                                                                              : gemv_stage_bytes(FB);
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + kStages * 2 * kSlotBytes);
+    constexpr size_t kSlotW = gemv_slot_w(FA, FB);
+    constexpr bool kSmemB = gemv_smem_b(FA, FB);
+    constexpr int kBRow = gemv_b_row_bytes(FA, FB);
+    const int stages = kSmemB ? wk.stages : kStages;  // compile-time ring for the global-B kernels
+    const size_t kSlotBytes = 2 * kSlotW + (kSmemB ? (size_t)wk.S * kBRow : 0);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + stages * kSlotBytes);
     uint64_t *empty = full + kStages;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     pdl_release();
 
     if (tid == 0) {
-        for (int i = 0; i < kStages; ++i) {
+        for (int i = 0; i < stages; ++i) {
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], kGemvWarps);
         }
@@ -422,38 +496,90 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
     if (warp == kGemvWarps) {
         // ---------------- producer ----------------
         if (lane != 0) return;
-        // Weights are constant during a forward, so the producer streams them
-        // before the predecessor finishes; only the MoE work list (written by
-        // the router kernel) needs the wait.
-        if (wk.moe) pdl_wait();
-        int idx = 0;
+        // Weights are constant during a forward, so the producer streams the
+        // first ring of weights before the predecessor finishes; the
+        // activation rows (kSmemB) and the MoE work list (written by the
+        // router kernel) need the wait.
+        bool waited = false;
+        if (wk.moe) {
+            pdl_wait();
+            waited = true;
+        }
+        // activation copies of stages issued before the wait
+        struct BJob {
+            int slot;
+            const __half *xq;
+            int kp, col0, cols;
+        } pend[kStages];
+        int npend = 0;
+        int idx = 0, slot = 0;
+        uint32_t phase = 0;    // parity of the ring pass `slot` is in
+        bool reuse = false;    // slot already used once (wait for its release)
         for (int item = blockIdx.x; item < wk.total_items; item += gridDim.x) {
             GemvItem it;
             if (!resolve_item<FA, FB>(wk, item, it)) continue;
             const int blk = it.fmt == FA ? block_bytes(FA) : block_bytes(FB);
+            const int ccols = chunk_cols(it.fmt);
             const int nchunks = chunk_count(it.fmt, it.kp);
             const int nst = (nchunks + kGemvWarps - 1) / kGemvWarps;
             for (int s = 0; s < nst; ++s, ++idx) {
-                const int slot = idx % kStages, round = idx / kStages;
-                if (round > 0) mbar_wait_bounded(&empty[slot], (uint32_t)((round - 1) & 1), wk.err);
+                if (kSmemB && !waited && reuse) {
+                    // the ring is full: wait for the predecessor, then send
+                    // the activation rows of the stages already in flight
+                    pdl_wait();
+                    waited = true;
+                    for (int p = 0; p < npend; ++p)
+                        for (int r = 0; r < wk.S; ++r)
+                            bulk_g2s(smem + (size_t)pend[p].slot * kSlotBytes + 2 * kSlotW + (size_t)r * kBRow,
+                                     pend[p].xq + ((size_t)r * pend[p].kp + pend[p].col0) * 2,
+                                     (uint32_t)(pend[p].cols * 4), &full[pend[p].slot]);
+                    npend = 0;
+                }
+                if (reuse) mbar_wait_bounded(&empty[slot], phase ^ 1u, wk.err);
+                GEMV_MARK(idx);
                 const int c0 = s * kGemvWarps;
-                const uint32_t bytes = (uint32_t)(min(kGemvWarps, nchunks - c0) * blk);
-                mbar_expect_tx(&full[slot], bytes * (it.t1 ? 2u : 1u));
-                bulk_g2s(smem + (slot * 2) * kSlotBytes, it.t0 + (size_t)c0 * blk, bytes, &full[slot]);
-                if (it.t1)
-                    bulk_g2s(smem + (slot * 2 + 1) * kSlotBytes, it.t1 + (size_t)c0 * blk, bytes,
-                             &full[slot]);
+                const int nch = min(kGemvWarps, nchunks - c0);
+                const uint32_t bytes = (uint32_t)(nch * blk);
+                const uint32_t bbytes = kSmemB ? (uint32_t)(wk.S * nch * ccols * 4) : 0u;
+                mbar_expect_tx(&full[slot], bytes * (it.t1 ? 2u : 1u) + bbytes);
+                uint8_t *sb = smem + (size_t)slot * kSlotBytes;
+                bulk_g2s(sb, it.t0 + (size_t)c0 * blk, bytes, &full[slot]);
+                if (it.t1) bulk_g2s(sb + kSlotW, it.t1 + (size_t)c0 * blk, bytes, &full[slot]);
+                if (kSmemB) {
+                    if (waited) {
+                        for (int r = 0; r < wk.S; ++r)
+                            bulk_g2s(sb + 2 * kSlotW + (size_t)r * kBRow, it.xq + ((size_t)r * it.kp + c0 * ccols) * 2,
+                                     (uint32_t)(nch * ccols * 4), &full[slot]);
+                    } else {
+                        pend[npend++] = BJob{slot, it.xq, it.kp, c0 * ccols, nch * ccols};
+                    }
+                }
+                if (++slot == stages) {
+                    slot = 0;
+                    phase ^= 1u;
+                    reuse = true;
+                }
             }
+        }
+        if (kSmemB && !waited) {
+            pdl_wait();
+            for (int p = 0; p < npend; ++p)
+                for (int r = 0; r < wk.S; ++r)
+                    bulk_g2s(smem + (size_t)pend[p].slot * kSlotBytes + 2 * kSlotW + (size_t)r * kBRow,
+                             pend[p].xq + ((size_t)r * pend[p].kp + pend[p].col0) * 2,
+                             (uint32_t)(pend[p].cols * 4), &full[pend[p].slot]);
         }
         return;
     }
 
     // ---------------- consumers ----------------
+    if (tid == 0) GEMV_MARK(125);
     pdl_wait();
+    if (tid == 0) GEMV_MARK(126);
     if (wk.S <= 4)
-        gemv_consume<FA, FB, true>(wk, smem, kSlotBytes, full, empty, red, out);
+        gemv_consume<FA, FB, true>(wk, smem, kSlotW, kSlotBytes, full, empty, red, out);
     else
-        gemv_consume<FA, FB, false>(wk, smem, kSlotBytes, full, empty, red, out);
+        gemv_consume<FA, FB, false>(wk, smem, kSlotW, kSlotBytes, full, empty, red, out);
 }
 
 inline int gemv_tiles(const GemvSeg &s) {
@@ -476,7 +602,7 @@ inline cudaError_t gemv_prepare_all() {
 #define FC_GEMV_ATTR(A, B)                                                                    \
     if (e == cudaSuccess)                                                                     \
         e = cudaFuncSetAttribute(gemv_kernel<A, B>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                                 (int)gemv_smem_bytes(A, B));
+                                 (int)kGemvDynSmemBudget);
     FC_GEMV_FORMATS(FC_GEMV_ATTR)
 #undef FC_GEMV_ATTR
     return e;
@@ -498,12 +624,16 @@ inline cudaError_t launch_gemv_work(int fa, int fb, GemvWork &wk, int sms, cudaS
         }
     }
     wk.total_items = items;
+    wk.stages = gemv_stages(fa, fb, wk.S);
+#ifdef FC_GEMV_TRACE
+    wk.trace = g_host_trace_items == items;
+#endif
     if (items == 0) return cudaSuccess;
     int grid = std::min(items, sms * kGemvCtasPerSm);
 #define FC_GEMV_CASE(A, B)                                                               \
     if (fa == A && fb == B) {                                                            \
         return launch_pdl(gemv_kernel<A, B>, dim3(grid), dim3(kGemvThreads),               \
-                          gemv_smem_bytes(A, B), stream, wk);                              \
+                          gemv_smem_bytes(A, B, wk.S), stream, wk);                        \
     }
     FC_GEMV_FORMATS(FC_GEMV_CASE)
 #undef FC_GEMV_CASE

@@ -1647,3 +1647,13 @@ extern "C" int fc_debug_tc_trace(unsigned long long *out, int n) {
     return cudaMemcpyFromSymbol(out, g_tc_trace, sizeof(unsigned long long) * (n < 256 ? n : 256)) == cudaSuccess;
 }
 #endif
+
+#ifdef FC_GEMV_TRACE
+extern "C" int fc_debug_gemv_trace(int items, unsigned long long *out, int n) {
+    if (!out) {
+        g_host_trace_items = items;
+        return 1;
+    }
+    return cudaMemcpyFromSymbol(out, g_gemv_trace, sizeof(unsigned long long) * (n < 512 ? n : 512)) == cudaSuccess;
+}
+#endif
