@@ -65,12 +65,20 @@ constexpr size_t kGemvDynSmemBudget = 100 * 1024;  // two CTAs per SM with the s
 __host__ __device__ constexpr size_t gemv_slot_bytes(int fa, int fb, int S) {
     return 2 * gemv_slot_w(fa, fb) + (gemv_smem_b(fa, fb) ? (size_t)S * gemv_b_row_bytes(fa, fb) : 0);
 }
+// Ring depth: as many stages as the budget holds, at least two (wide
+// formats with 8 activation rows then exceed the budget and run one CTA per
+// SM).
 inline int gemv_stages(int fa, int fb, int S) {
     int n = (int)((kGemvDynSmemBudget - 2 * kStages * 8) / gemv_slot_bytes(fa, fb, S));
     return n > kStages ? kStages : (n < 2 ? 2 : n);
 }
 inline size_t gemv_smem_bytes(int fa, int fb, int S) {
     return (size_t)gemv_stages(fa, fb, S) * gemv_slot_bytes(fa, fb, S) + 2 * kStages * 8;
+}
+inline size_t gemv_smem_max(int fa, int fb) {  // over 1 .. 8 activation rows
+    size_t m = 0;
+    for (int S = 1; S <= 8; ++S) m = gemv_smem_bytes(fa, fb, S) > m ? gemv_smem_bytes(fa, fb, S) : m;
+    return m;
 }
 
 enum GemvEpilogue {
@@ -602,7 +610,7 @@ inline cudaError_t gemv_prepare_all() {
 #define FC_GEMV_ATTR(A, B)                                                                    \
     if (e == cudaSuccess)                                                                     \
         e = cudaFuncSetAttribute(gemv_kernel<A, B>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                                 (int)kGemvDynSmemBudget);
+                                 (int)gemv_smem_max(A, B));
     FC_GEMV_FORMATS(FC_GEMV_ATTR)
 #undef FC_GEMV_ATTR
     return e;
