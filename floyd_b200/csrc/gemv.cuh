@@ -45,15 +45,15 @@ __host__ __device__ constexpr size_t gemv_stage_bytes(int fmt) {
 __host__ __device__ constexpr size_t gemv_slot_w(int fa, int fb) {
     return gemv_stage_bytes(fa) > gemv_stage_bytes(fb) ? gemv_stage_bytes(fa) : gemv_stage_bytes(fb);
 }
-// Launches of the q8 / q4 formats also stage the stage's activation rows in
-// shared memory (the producer copies them next to the weights), so the
-// consumers never wait on L2 for B fragments; the MXFP4 launches, whose
-// wider chunks would leave too few stages, load B fragments from global.
+// Every launch stages each stage's activation rows in shared memory next to
+// the weights (the producer copies them), so the consumers never wait on L2
+// for B fragments (FC_GEMV_NO_SMEM_B builds the global-load variant for
+// measurements).
 __host__ __device__ constexpr bool gemv_smem_b(int fa, int fb) {
-#ifdef FC_GEMV_NO_SMEM_B
+#if defined(FC_GEMV_NO_SMEM_B)
     return false;
 #else
-    return fa != FC_FMT_MXFP4 && fb != FC_FMT_MXFP4;
+    return true;
 #endif
 }
 // Bytes of one activation row of one stage (kGemvWarps chunks, hi + lo fp16,
