@@ -45,6 +45,8 @@ def parse():
     ap.add_argument("--accept-p", type=float, default=0.7)
     ap.add_argument("--draft", type=int, default=3)
     ap.add_argument("--profile-passes", type=int, default=3)
+    ap.add_argument("--sample-steps", type=int, default=30,
+                    help="verify steps with rejection-sampling acceptance (T=0.7, seed 1)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=None,
                     help="override layer_count (small profiling cases only)")
@@ -61,11 +63,18 @@ class Dist:
         self.rank = int(os.environ.get("RANK", "0"))
         self.local = int(os.environ.get("LOCAL_RANK", "0"))
         self.pg = None
+        # nccl on the GPU box; FC_DIST_BACKEND=gloo runs the host plumbing on CPU (tests)
+        self.backend = os.environ.get("FC_DIST_BACKEND", "nccl")
         if self.world > 1:
             import torch
             import torch.distributed as dist
-            torch.cuda.set_device(self.local)
-            dist.init_process_group("nccl", device_id=torch.device("cuda", self.local))
+            if self.backend == "nccl":
+                torch.cuda.set_device(self.local)
+                dist.init_process_group("nccl", device_id=torch.device("cuda", self.local))
+                self.dev = f"cuda:{self.local}"
+            else:
+                dist.init_process_group(self.backend)
+                self.dev = "cpu"
             self.dist = dist
             self.torch = torch
 
@@ -76,16 +85,24 @@ class Dist:
     def max(self, v):
         if self.world == 1:
             return v
-        t = self.torch.tensor([float(v)], device=f"cuda:{self.local}")
+        t = self.torch.tensor([float(v)], device=self.dev)
         self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
         return float(t.item())
 
     def sum(self, v):
         if self.world == 1:
             return v
-        t = self.torch.tensor([float(v)], device=f"cuda:{self.local}")
+        t = self.torch.tensor([float(v)], device=self.dev)
         self.dist.all_reduce(t, op=self.dist.ReduceOp.SUM)
         return float(t.item())
+
+    def all_gather_bytes(self, b):
+        """Every rank's `b` (same length), in rank order."""
+        if self.world == 1:
+            return [b]
+        out = [None] * self.world
+        self.dist.all_gather_object(out, b)
+        return out
 
     def close(self):
         if self.world > 1:
@@ -295,8 +312,19 @@ def run_ours(args, d):
     V = cfg["vocab_size"]
 
     t_setup = time.time()
-    model = floyd_b200.Model(cfg, device=d.local, seed=0)
+    # N > 1: the routed experts are split across the N GPUs (contiguous id
+    # ranges), attention / dense / shared / router / lm-head replicated, one
+    # NVLink exchange per MoE layer; all ranks run the same single stream in
+    # lockstep (strong scaling of one sequence)
+    ep = d.world > 1
+    if ep and cfg["expert_count"] % d.world:
+        raise SystemExit(f"{args.config}: {cfg['expert_count']} experts do not split {d.world} ways")
+    model = floyd_b200.Model(cfg, device=d.local, seed=0, rank=d.rank if ep else 0,
+                             world=d.world if ep else 1)
     sess = floyd_b200.Session(model, capacity, rows)
+    if ep:
+        sess.ep_connect(d.all_gather_bytes(sess.ep_handle()))
+        d.barrier()
     sess.seed_context(ctx0, 7)
     # untimed: the target's greedy stream from the seeded context
     stream = [1]
@@ -342,9 +370,30 @@ def run_ours(args, d):
     d.barrier()
     gpu_ms_max = d.max(gpu_ms)
     wall_max = d.max(wall_timed)
-    total_emitted = d.sum(emitted_timed)
+    total_emitted = emitted_timed  # one stream (identical on every rank)
     value = total_emitted / (gpu_ms_max / 1e3)
     e2e = total_emitted / wall_max
+
+    # the same workload with rejection-sampling acceptance (temperature 0.7,
+    # Philox seed 1, counter = round), reported beside the greedy headline
+    samp = None
+    if args.sample_steps > 0:
+        sess.rollback(ctx0)
+        s0 = sess.stats()
+        em_s, j = 0, 0
+        for r in range(args.sample_steps):
+            j = min(j, len(stream) - rows)
+            ids = stream[j:j + rows]
+            em, nxt, _ = sess.verify(ids, mode=floyd_b200.ACCEPT_SAMPLE, temperature=0.7, seed=1,
+                                     counter=r)
+            em_s += len(em)
+            j += len(em)
+        s1 = sess.stats()
+        g = d.max(s1["gpu_ms"] - s0["gpu_ms"])
+        samp = {"temperature": 0.7, "philox_seed": 1, "steps": args.sample_steps,
+                "value": em_s / (g / 1e3), "unit": "tok/s",
+                "ms_per_step": g / args.sample_steps, "mean_commit": em_s / args.sample_steps,
+                "drafts": "the target's greedy continuation (argmax drafts)"}
 
     # per-kernel profile (eager passes with CUDA events on the session stream)
     if args.profile_passes > 0:
@@ -365,6 +414,8 @@ def run_ours(args, d):
         rts = sess.routes(l, rows)
         actives.append(len(np.unique(rts)))
     n_active = float(np.mean(actives)) if actives else 0.0
+    if ep:
+        n_active /= d.world  # routed experts per rank (contiguous split, on average)
     peak, peak_kind = measured_peaks()
     dominant = max(prof.items(), key=lambda kv: kv[1][0])[0] if prof else None
     roof = None
@@ -388,17 +439,19 @@ def run_ours(args, d):
     out = {
         "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": d.world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "int8/fp4 x fp32",
+        "scaling": "strong" if ep else "weak", "vs_baseline": None, "dtype": "int8/fp4 x fp32",
         "data": "synthetic (seeded weights N(0,0.02)-like quantized, latent KV prefix, planted drafts)",
         "config": {"workload": args.config, "draft": args.draft, "accept_p": args.accept_p,
                    "context": ctx0, "rows_per_verify": rows,
                    "l2": "inputs larger than L2 (weights read once per step)",
-                   "parallelism": f"replicas x{d.world}"},
+                   "parallelism": (f"ep{d.world}: routed experts split {d.world} ways, the rest "
+                                   f"replicated, one NVLink exchange per MoE layer") if ep else "single GPU"},
         "verify_us": step_ms * 1e3,
         "step_hbm": {"algorithmic_bytes": step_bytes, "achieved_gbs": step_bytes / (step_ms / 1e3) / 1e9,
                      "frac": step_bytes / (step_ms / 1e3) / 1e9 / peak, "peak": peak},
-        "mean_commit": total_emitted / (args.steps * d.world),
+        "mean_commit": total_emitted / args.steps,
         "acceptance_mismatches": int(d.sum(mismatches)),
+        "sampling": samp,
         "roofline": roof,
         "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 72, "d2h_bytes_per_step": 48,
                 "note": "fc_session_verify wall time with host id / result buffers"},

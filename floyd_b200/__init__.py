@@ -164,6 +164,19 @@ class Session:
         err = _err()
         self._check(self._lib.fc_session_rollback(self.handle, int(position), err, len(err)), err)
 
+    def ep_handle(self):
+        """This rank's expert-parallel receive-region handle (bytes)."""
+        buf = ctypes.create_string_buffer(64)
+        err = _err()
+        self._check(self._lib.fc_session_ep_handle(self.handle, buf, 64, err, len(err)), err)
+        return buf.raw
+
+    def ep_connect(self, handles):
+        """Connects to every rank's region; `handles` in rank order."""
+        blob = b"".join(handles)
+        err = _err()
+        self._check(self._lib.fc_session_ep_connect(self.handle, blob, len(handles), err, len(err)), err)
+
     def seed_context(self, positions, seed):
         err = _err()
         self._check(self._lib.fc_session_seed_context(self.handle, int(positions),

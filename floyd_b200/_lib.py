@@ -12,6 +12,7 @@ LIB_PATH = os.path.join(HERE, "libfloyd_cuda.so")
 
 FMT_F32, FMT_Q8, FMT_Q4, FMT_MXFP4 = 0, 1, 2, 3
 SCORE_SOFTMAX, SCORE_SIGMOID, SCORE_SQRT_SOFTPLUS = 0, 1, 2
+EP_HANDLE_BYTES = 64    # FC_EP_HANDLE_BYTES
 ACCEPT_GREEDY, ACCEPT_SAMPLE = 0, 1
 
 
@@ -100,6 +101,8 @@ SIGNATURES = {
     "fc_session_rollback": (_I, [_P, _I, _C, _S]),
     "fc_session_copy_row_logits": (_I, [_P, _FP, _I]),
     "fc_session_seed_context": (_I, [_P, _I, ctypes.c_uint64, _C, _S]),
+    "fc_session_ep_handle": (_I, [_P, ctypes.c_void_p, _S, _C, _S]),
+    "fc_session_ep_connect": (_I, [_P, ctypes.c_char_p, _I, _C, _S]),
     "fc_session_set_profiling": (_I, [_P, _I]),
     "fc_session_profile": (_I, [_P, _I, _C, _S, ctypes.POINTER(ctypes.c_double),
                                 ctypes.POINTER(ctypes.c_uint64)]),

@@ -107,6 +107,8 @@ struct GemvSeg {
     int64_t xq_stride;      // halves between members' inputs
     int out_stride;         // output columns between members
     int tiles;              // work items per member (set by the launcher)
+    int npeer;              // EPI_STORE copies into peer GPUs' buffers (expert parallel)
+    float *peer_y[7];       // same offsets as y, in each peer's receive buffer
 };
 
 constexpr int kMaxSegs = 6;
@@ -125,6 +127,9 @@ struct GemvWork {
     const int *active;
     int64_t in_slot_stride;   // halves between slots' xq inputs
     int64_t out_slot_stride;  // floats (EPI_STORE) or halves (xq) between slots
+    const int *slot_base;     // nullable: global slot of local slot 0 (expert parallel)
+    const int *ep_epoch;      // nullable: receive buffer = (epoch + 1) & 1
+    int64_t parity_stride;    // floats between the two receive buffers
     int total_items;
     int S;
     float swiglu_limit;
@@ -163,7 +168,8 @@ __device__ __forceinline__ bool resolve_item(const GemvWork &wk, int item, GemvI
             tile = item % rt;
             member = wk.active[slot] - wk.expert_base;
             it.xq = r.xq + slot * wk.in_slot_stride;
-            it.out_shift = slot * wk.out_slot_stride;
+            it.out_shift = (slot + (wk.slot_base ? *wk.slot_base : 0)) * wk.out_slot_stride;
+            if (wk.ep_epoch) it.out_shift += ((*wk.ep_epoch + 1) & 1) * wk.parity_stride;
             it.fmt = FA;
         } else {
             si = 1;
@@ -337,13 +343,18 @@ __device__ __forceinline__ void gemv_epilogue(const GemvSeg &sg, const GemvItem 
                  silu(gv) * uv);
         return;
     }
-    int r = idx >> 3, s = idx & 7;
+    // plain outputs: consecutive threads take consecutive rows of one
+    // activation row (coalesced, also for the stores into peer GPUs)
+    const bool plain = sg.epi == EPI_STORE || sg.epi == EPI_ADD;
+    int r = plain ? (idx & 31) : (idx >> 3), s = plain ? (idx >> 5) : (idx & 7);
     int o = it.row0 + r;
     if (s >= S || o >= sg.O) return;
     float v = out[r * 8 + s];
     int col = it.member * sg.out_stride + o;
     if (sg.epi == EPI_STORE) {
-        sg.y[it.out_shift + (size_t)s * sg.ldy + col] = v;
+        const size_t at = it.out_shift + (size_t)s * sg.ldy + col;
+        sg.y[at] = v;
+        for (int p = 0; p < sg.npeer; ++p) sg.peer_y[p][at] = v;  // NVLink stores
     } else if (sg.epi == EPI_ADD) {
         sg.y[it.out_shift + (size_t)s * sg.ldy + col] += v;
     } else {
@@ -474,6 +485,12 @@ __device__ __forceinline__ void gemv_consume(const GemvWork &wk, const uint8_t *
         consumer_sync();
         gemv_epilogue(wk.seg[it.seg], it, wk.S, wk.swiglu_limit, out);
         if (tid == 0) GEMV_MARK(127);
+    }
+    if (wk.seg[0].npeer) {
+        // all of this CTA's peer stores before the epoch flag (one
+        // cumulative system fence after a CTA barrier)
+        consumer_sync();
+        if (tid == 0) __threadfence_system();
     }
 }
 

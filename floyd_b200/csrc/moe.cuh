@@ -31,7 +31,9 @@ struct RouteParams {
     float *route_w;          // [S][K]
     int *n_active;           // number of local active experts
     int *active;             // [max_slots] ascending expert ids (local range)
-    float *coef;             // [max_slots][8] coefficient of slot for row s
+    float *coef;             // [global slots][8] coefficient of global slot g for row s
+    int *n_global;           // active experts of all ranks (global slots)
+    int *n_before;           // active experts below expert_lo (first global slot of this rank)
     int *arrivals;           // block arrival counter (zero between launches)
 };
 
@@ -176,16 +178,17 @@ __device__ __forceinline__ void route_select_block(const float *logits, const Ro
     __syncthreads();
     if (threadIdx.x < p.S * K) {
         int s = threadIdx.x / K, k = threadIdx.x % K;
-        int e = sel[s][k];
-        if (e >= p.expert_lo && e < p.expert_hi) used_flag[e - p.expert_lo] = 1;
+        used_flag[sel[s][k]] = 1;
     }
     __syncthreads();
-    // block scan over the local experts, 4 per thread, ascending
-    const int nl = p.expert_hi - p.expert_lo;
+    // Global slots: every selected expert of every rank in ascending id
+    // (block scan, 4 experts per thread).  This rank's local slots are the
+    // window [n_before, n_before + local count) of that order, so the
+    // expert-parallel combine sums exactly the single-GPU sequence.
     int cnt = 0;
     for (int i = 0; i < 4; ++i) {
         int e = 4 * threadIdx.x + i;
-        if (e < nl) cnt += used_flag[e];
+        if (e < p.E) cnt += used_flag[e];
     }
     int incl = cnt;
 #pragma unroll
@@ -197,25 +200,36 @@ __device__ __forceinline__ void route_select_block(const float *logits, const Ro
     __syncthreads();
     int base = 0;
     for (int w = 0; w < warp; ++w) base += warp_total[w];
+    int total = 0;
+    for (int w = 0; w < kRouteThreads / 32; ++w) total += warp_total[w];
+    // slots below expert_lo and below expert_hi (exclusive prefixes)
+    __shared__ int pre_lo, pre_hi;
+    if (threadIdx.x == 0) pre_hi = total;
+    __syncthreads();
     int slot = base + incl - cnt;
     for (int i = 0; i < 4; ++i) {
         int e = 4 * threadIdx.x + i;
-        if (e < nl && used_flag[e]) {
-            slot_of[e] = slot;
-            p.active[slot] = p.expert_lo + e;
-            ++slot;
-        }
+        if (e == p.expert_lo) pre_lo = slot;
+        if (e == p.expert_hi) pre_hi = slot;
+        if (e < p.E && used_flag[e]) slot_of[e] = slot++;
     }
-    int total = 0;
-    for (int w = 0; w < kRouteThreads / 32; ++w) total += warp_total[w];
-    if (threadIdx.x == 0) *p.n_active = total;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        *p.n_before = pre_lo;
+        *p.n_active = pre_hi - pre_lo;
+        *p.n_global = total;
+    }
     for (int i = threadIdx.x; i < total * 8; i += blockDim.x) p.coef[i] = 0.0f;
     __syncthreads();
     if (threadIdx.x < p.S * K) {
         int s = threadIdx.x / K, k = threadIdx.x % K;
         int e = sel[s][k];
-        if (e >= p.expert_lo && e < p.expert_hi) p.coef[slot_of[e - p.expert_lo] * 8 + s] = selw[s][k];
+        p.coef[slot_of[e] * 8 + s] = selw[s][k];
     }
+    // local active list (ascending): global slots of this rank's experts
+    // minus the slots below them
+    for (int e = p.expert_lo + threadIdx.x; e < p.expert_hi; e += blockDim.x)
+        if (used_flag[e]) p.active[slot_of[e] - pre_lo] = e;
 }
 
 // Router: one block per expert computes its logits for every row (fp32
@@ -293,15 +307,78 @@ __global__ void __launch_bounds__(kRouteThreads) router_kernel(const float *W, c
 // Products and sums are rounded separately (no contraction), the order the
 // C reference spells out.
 constexpr int kMoeCombineThreads = 256;
+constexpr int kMaxRanks = 8;
 
+// Expert-parallel exchange state of one session (pointers into the peers'
+// receive regions; absent on a single GPU).
+struct EpLink {
+    int world, rank;
+    int *epoch;                      // local counter, +1 per MoE layer (both sides in lockstep)
+    int *flags;                      // [world] epochs published by the peers into this GPU
+    int *peer_flags[kMaxRanks];      // the peers' flag arrays (index rank = this rank)
+};
+
+__device__ __forceinline__ int ld_acquire_sys(const int *p) {
+    int v;
+    asm volatile("ld.acquire.sys.global.s32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_sys(int *p, int v) {
+    asm volatile("st.release.sys.global.s32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
+}
+
+// After this rank's routed down projections (which stored their outputs
+// into every peer's receive buffer): publish the next epoch to every peer.
+__global__ void ep_signal_kernel(EpLink link) {
+    pdl_wait();
+    pdl_release();
+    __threadfence_system();
+    const int e = *link.epoch + 1;
+    *link.epoch = e;
+    for (int r = 0; r < link.world; ++r)
+        if (r != link.rank) st_release_sys(link.peer_flags[r] + link.rank, e);
+}
+
+// resid[s][d] += (sum over global slots ascending of coef * routed[slot][s][d])
+//                + shared[s][d]                           (moe_exec.h:97-110)
+// Products and sums are rounded separately (no contraction), the order the
+// C reference spells out.  With expert parallelism the routed outputs of
+// every rank sit in this GPU's receive buffer (buffer = epoch parity) once
+// every peer has published the current epoch; the wait is bounded (error
+// bit 2 on timeout).
 __global__ void __launch_bounds__(kMoeCombineThreads)
 moe_combine_kernel(float *resid, const float *routed, const float *shared, const float *coef,
-                   const int *n_active, int S, int D, int max_batch) {
+                   const int *n_active, int S, int D, int max_batch, EpLink link, int64_t parity_stride,
+                   int *err) {
     pdl_wait();
     pdl_release();
     __shared__ int list[1024];
     __shared__ float lc[1024];
     __shared__ int count;
+    if (link.world > 1) {
+        if (threadIdx.x == 0) {
+            const int e = *link.epoch;
+            uint64_t t0 = 0;
+            for (int r = 0; r < link.world; ++r) {
+                if (r == link.rank) continue;
+                for (uint32_t it = 0; ld_acquire_sys(link.flags + r) < e; ++it) {
+                    if ((it & 255u) == 0) {
+                        uint64_t t;
+                        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+                        if (t0 == 0) t0 = t;
+                        else if (t - t0 > 1000000000ull) {
+                            atomicOr(err, 2);
+                            break;
+                        }
+                    }
+                }
+            }
+            count = e;  // reused below for the parity
+        }
+        __syncthreads();
+        routed += (count & 1) * parity_stride;
+        __syncthreads();
+    }
     // blocks of one row: blockIdx.x = s * (D / 256) + column block
     const int per_row = (D + kMoeCombineThreads - 1) / kMoeCombineThreads;
     const int s = blockIdx.x / per_row;

@@ -96,6 +96,7 @@ struct FcModel {
     int device = 0;
     int sms = 148;                     // multiprocessors of the device
     int expert_lo = 0, expert_hi = 0;  // local routed experts
+    int rank = 0, world = 1;           // expert-parallel position
     std::string device_name;
     uint8_t *arena = nullptr;
     size_t arena_bytes = 0, arena_used = 0;
@@ -133,6 +134,16 @@ struct FcSession {
     HeadPartials hp{};
     int *d_err = nullptr;    // bit 1: a bounded wait in a kernel gave up
     int *route_arrivals = nullptr;   // router block counter (zero between launches)
+    int *n_global = nullptr, *n_before = nullptr;  // global active experts / first global slot here
+    int g_slots = 0;                 // global slots (active experts of all ranks) at most
+    // expert parallel (model world > 1): receive region = two buffers of the
+    // routed outputs of every rank [2][g_slots][rows][D] + kMaxRanks epoch
+    // flags, exported by IPC; the peers' regions opened here
+    void *ep_region = nullptr;
+    float *ep_xbuf = nullptr;
+    int *ep_flags = nullptr, *ep_epoch = nullptr;
+    void *ep_peer_region[kMaxRanks] = {};
+    bool ep_connected = false;
     Staging *d_stage = nullptr, *h_stage = nullptr;
     Result *d_res = nullptr, *h_res = nullptr;
     std::map<int, cudaGraphExec_t> graphs;
@@ -426,6 +437,13 @@ bool salloc(FcSession *s, T *&p, size_t count) {
 void free_session_buffers(FcSession *s) {
     for (auto &g : s->graphs) cudaGraphExecDestroy(g.second);
     s->graphs.clear();
+    for (void *&p : s->ep_peer_region)
+        if (p) {
+            cudaIpcCloseMemHandle(p);
+            p = nullptr;
+        }
+    if (s->ep_region) cudaFree(s->ep_region);
+    s->ep_region = nullptr;
     for (void *p : s->allocs) cudaFree(p);
     s->allocs.clear();
     if (s->h_stage) cudaFreeHost(s->h_stage);
@@ -649,6 +667,8 @@ cudaError_t record_forward(FcSession *s, int S) {
             rp.n_active = s->n_active;
             rp.active = s->active;
             rp.coef = s->coef;
+            rp.n_global = s->n_global;
+            rp.n_before = s->n_before;
             rp.arrivals = s->route_arrivals;
             FC_TRY(launch_pdl(router_kernel, dim3(E), dim3(kRouteThreads), 0, st, y.router.p, s->xn, D,
                               s->router_logits, rp));
@@ -688,6 +708,19 @@ cudaError_t record_forward(FcSession *s, int S) {
             dn.seg[0].w_stride = (int64_t)y.e_down.w_bytes;
             dn.seg[0].y = s->moe_part;
             dn.seg[0].ldy = D;
+            const bool ep = m->world > 1;
+            const int64_t parity_stride = (int64_t)s->g_slots * mb * D;
+            if (ep) {
+                // routed outputs go to global slot n_before + local slot of
+                // the receive buffer of every rank (this one and the peers)
+                dn.seg[0].y = s->ep_xbuf;
+                for (int r = 0, k = 0; r < m->world; ++r)
+                    if (r != m->rank) dn.seg[0].peer_y[k++] = reinterpret_cast<float *>(s->ep_peer_region[r]);
+                dn.seg[0].npeer = m->world - 1;
+                dn.slot_base = s->n_before;
+                dn.ep_epoch = s->ep_epoch;
+                dn.parity_stride = parity_stride;
+            }
             if (y.s_down.count) {
                 dn.seg[1] = seg_of(y.s_down, s->hsh_xq, EPI_STORE);
                 dn.seg[1].y = s->sh_part;
@@ -704,10 +737,23 @@ cudaError_t record_forward(FcSession *s, int S) {
             dn.err = s->d_err;
             FC_TRY(launch_gemv_work(ef, df, dn, m->sms, st));
             mark(s, "moe_down");
+            EpLink link{};
+            link.world = m->world;
+            link.rank = m->rank;
+            if (ep) {
+                link.epoch = s->ep_epoch;
+                link.flags = s->ep_flags;
+                for (int r = 0; r < m->world; ++r)
+                    if (r != m->rank)
+                        link.peer_flags[r] = reinterpret_cast<int *>(
+                            reinterpret_cast<uint8_t *>(s->ep_peer_region[r]) + 2 * parity_stride * sizeof(float));
+                FC_TRY(launch_pdl(ep_signal_kernel, dim3(1), dim3(1), 0, st, link));
+                mark(s, "ep_signal");
+            }
             FC_TRY(launch_pdl(moe_combine_kernel, dim3(S * ((D + kMoeCombineThreads - 1) / kMoeCombineThreads)),
-                              dim3(kMoeCombineThreads), 0, st, 
-                s->resid, s->moe_part, y.s_down.count ? s->sh_part : nullptr, s->coef, s->n_active,
-                S, D, mb));
+                              dim3(kMoeCombineThreads), 0, st, s->resid, ep ? (const float *)s->ep_xbuf : s->moe_part,
+                              y.s_down.count ? (const float *)s->sh_part : nullptr, (const float *)s->coef,
+                              (const int *)s->n_global, S, D, mb, link, parity_stride, s->d_err));
             mark(s, "moe_combine");
         }
         if (s->trace) {
@@ -794,6 +840,8 @@ cudaGraphExec_t get_graph(FcSession *s, int S, char *err, size_t n) {
 // Runs one forward pass of `rows` <= rows_max tokens at the session position.
 int run_pass(FcSession *s, const int *ids, int rows, int k, const FcAcceptConfig *accept,
              char *err, size_t n) {
+    if (s->m->world > 1 && !s->ep_connected)
+        return set_error(err, n, "expert-parallel session is not connected (fc_session_ep_connect)");
     Staging *st = s->h_stage;
     memset(st, 0, sizeof(*st));
     st->pos = s->position;
@@ -924,7 +972,7 @@ int fc_model_create_ep(FcModel **out, const FcModelConfig *config, int device, i
                        int world, char *error, size_t error_size) {
     if (!out) return set_error(error, error_size, "model output is required");
     *out = nullptr;
-    if (!config || world <= 0 || rank < 0 || rank >= world ||
+    if (!config || world <= 0 || world > kMaxRanks || rank < 0 || rank >= world ||
         (config->expert_count > 0 && config->expert_count % world))
         return set_error(error, error_size, "invalid expert-parallel layout");
     if (!config_ok(config, error, error_size)) return 0;
@@ -940,6 +988,8 @@ int fc_model_create_ep(FcModel **out, const FcModelConfig *config, int device, i
     int per = config->expert_count / world;
     m->expert_lo = rank * per;
     m->expert_hi = rank * per + per;
+    m->rank = rank;
+    m->world = world;
     if (!build_model(m, error, error_size)) {
         fc_model_close(m);
         return 0;
@@ -1123,11 +1173,23 @@ int fc_session_create(FcSession **out, FcModel *m, const FcOptions *options, cha
     ok = ok && salloc(s, s->route_ids, (size_t)c.layer_count * mb * K);
     ok = ok && salloc(s, s->route_w, (size_t)c.layer_count * mb * K);
     ok = ok && salloc(s, s->n_active, 1) && salloc(s, s->active, (size_t)s->max_slots + 1);
-    ok = ok && salloc(s, s->coef, (size_t)(s->max_slots + 1) * 8);
+    s->g_slots = std::min(E, mb * K);
+    ok = ok && salloc(s, s->coef, (size_t)(s->g_slots + 1) * 8);
+    ok = ok && salloc(s, s->n_global, 1) && salloc(s, s->n_before, 1);
     ok = ok && salloc(s, s->h_xq, (size_t)s->max_slots * mb * kpad(I) * 2);
     ok = ok && salloc(s, s->hsh_xq, (size_t)mb * kpad(W) * 2);
     ok = ok && salloc(s, s->hd_xq, (size_t)mb * kpad(std::max(c.dense_intermediate_size, 32)) * 2);
-    ok = ok && salloc(s, s->moe_part, (size_t)s->max_slots * mb * D);
+    ok = ok && salloc(s, s->moe_part, (size_t)s->g_slots * mb * D);
+    if (ok && m->world > 1) {
+        const size_t xb = (size_t)2 * s->g_slots * mb * D * sizeof(float);
+        ok = cudaMalloc(&s->ep_region, xb + kMaxRanks * sizeof(int)) == cudaSuccess;
+        if (ok) {
+            cudaMemset(s->ep_region, 0, xb + kMaxRanks * sizeof(int));
+            s->ep_xbuf = reinterpret_cast<float *>(s->ep_region);
+            s->ep_flags = reinterpret_cast<int *>(reinterpret_cast<uint8_t *>(s->ep_region) + xb);
+        }
+        ok = ok && salloc(s, s->ep_epoch, 1);
+    }
     ok = ok && salloc(s, s->sh_part, (size_t)mb * D);
     ok = ok && salloc(s, s->logits, (size_t)mb * V);
     ok = ok && salloc(s, s->layer_out, (size_t)c.layer_count * mb * D);
@@ -1305,6 +1367,41 @@ int fc_session_copy_row_logits(const FcSession *s, float *logits, int capacity_r
     if (!s || !logits || capacity_rows < s->last_rows || s->last_rows <= 0) return 0;
     return cudaMemcpy(logits, s->logits, (size_t)s->last_rows * s->m->c.vocab_size * 4,
                       cudaMemcpyDeviceToHost) == cudaSuccess;
+}
+
+int fc_session_ep_handle(FcSession *s, void *handle, size_t handle_size, char *error,
+                         size_t error_size) {
+    if (!s || !handle || handle_size < sizeof(cudaIpcMemHandle_t))
+        return set_error(error, error_size, "session and a %zu-byte handle buffer are required",
+                         sizeof(cudaIpcMemHandle_t));
+    if (!s->ep_region) return set_error(error, error_size, "session is not expert-parallel");
+    cudaSetDevice(s->m->device);
+    cudaIpcMemHandle_t h;
+    cudaError_t e = cudaIpcGetMemHandle(&h, s->ep_region);
+    if (e != cudaSuccess) return set_error(error, error_size, "cudaIpcGetMemHandle: %s", cudaGetErrorString(e));
+    memcpy(handle, &h, sizeof(h));
+    return 1;
+}
+
+int fc_session_ep_connect(FcSession *s, const void *handles, int world, char *error, size_t error_size) {
+    if (!s || !handles) return set_error(error, error_size, "session and handles are required");
+    FcModel *m = s->m;
+    if (world != m->world || !s->ep_region)
+        return set_error(error, error_size, "world %d does not match the model's expert-parallel world %d",
+                         world, m->world);
+    cudaSetDevice(m->device);
+    for (int r = 0; r < world; ++r) {
+        if (r == m->rank || s->ep_peer_region[r]) continue;
+        cudaIpcMemHandle_t h;
+        memcpy(&h, reinterpret_cast<const uint8_t *>(handles) + (size_t)r * FC_EP_HANDLE_BYTES, sizeof(h));
+        cudaError_t e = cudaIpcOpenMemHandle(&s->ep_peer_region[r], h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess)
+            return set_error(error, error_size, "cudaIpcOpenMemHandle(rank %d): %s", r, cudaGetErrorString(e));
+    }
+    for (auto &g : s->graphs) cudaGraphExecDestroy(g.second);
+    s->graphs.clear();
+    s->ep_connected = true;
+    return 1;
 }
 
 int fc_session_seed_context(FcSession *s, int positions, uint64_t seed, char *error,

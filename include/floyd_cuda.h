@@ -237,6 +237,27 @@ int fc_session_copy_row_logits(const FcSession *session, float *logits,
 int fc_session_seed_context(FcSession *session, int positions, uint64_t seed,
                             char *error, size_t error_size);
 
+/* Expert parallelism across the GPUs of one box (no reference counterpart:
+ * floyd has no communication backend; the contract follows the expert
+ * partitioning of moe_exec.h:97-110 with one exchange per MoE layer).
+ * A session of a model made by fc_model_create_ep with world > 1 owns a
+ * receive region (two buffers of every rank's routed expert outputs plus
+ * epoch flags).  fc_session_ep_handle writes its CUDA IPC handle
+ * (FC_EP_HANDLE_BYTES bytes); the caller gathers the handles of all ranks
+ * (rank order) and passes them to fc_session_ep_connect on every rank.
+ * Afterwards every rank must make the same sequence of forward calls
+ * (prefill / append / decode / verify) with the same ids: each MoE layer
+ * stores this rank's expert outputs into every peer's region over
+ * NVLink, publishes an epoch flag, and waits (bounded, about 1 s) for the
+ * peers' flags before the combine, which sums all experts in ascending id
+ * exactly as on one GPU.  Forward calls fail until the session is
+ * connected. */
+#define FC_EP_HANDLE_BYTES 64
+int fc_session_ep_handle(FcSession *session, void *handle, size_t handle_size,
+                         char *error, size_t error_size);
+int fc_session_ep_connect(FcSession *session, const void *handles, int world,
+                          char *error, size_t error_size);
+
 /* Per-kernel profiling, the CUDA counterpart of MOONLIGHT_PROFILE
  * (moonlight_metal.m:1899-1979) and ds4's kernel counters.  While enabled,
  * forwards run eagerly (no graph) with a CUDA event after every kernel, and
