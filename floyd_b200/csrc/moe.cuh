@@ -19,6 +19,15 @@
 
 namespace fc {
 
+#ifdef FC_TC_TRACE
+#define RT_MARK(i) g_tc_trace[(i)] = clock64()
+#else
+#define RT_MARK(i) \
+    do {           \
+    } while (0)
+#endif
+
+
 struct RouteParams {
     int E, K, S;
     int score_fn, normalize;
@@ -32,6 +41,7 @@ struct RouteParams {
     int *n_active;           // number of local active experts
     int *active;             // [max_slots] ascending expert ids (local range)
     float *coef;             // [global slots][8] coefficient of global slot g for row s
+    float *choice;           // [S][E] score + selection bias (non-softmax score functions)
     int *n_global;           // active experts of all ranks (global slots)
     int *n_before;           // active experts below expert_lo (first global slot of this rank)
     int *arrivals;           // block arrival counter (zero between launches)
@@ -61,12 +71,15 @@ __device__ __forceinline__ void route_row(const float *logits, const RouteParams
     const int lane = threadIdx.x & 31;
     const int E = p.E, K = p.K;
     float sc[PER], ch[PER];
+    const bool pre = p.score_fn != FC_SCORE_SOFTMAX;  // scores / choices came from the router blocks
 #pragma unroll
     for (int i = 0; i < PER; ++i) {
         int e = lane + 32 * i;
         sc[i] = e < E ? __ldcg(logits + (size_t)s * E + e) : -INFINITY;
+        ch[i] = (pre && e < E) ? __ldcg(p.choice + (size_t)s * E + e) : -INFINITY;
     }
-    if (p.score_fn == FC_SCORE_SOFTMAX) {
+    if (threadIdx.x == 0) RT_MARK(220);
+    if (!pre) {
         float m = -INFINITY;
 #pragma unroll
         for (int i = 0; i < PER; ++i) m = fmaxf(m, sc[i]);
@@ -81,14 +94,11 @@ __device__ __forceinline__ void route_row(const float *logits, const RouteParams
         sum = warp_sum(sum);
 #pragma unroll
         for (int i = 0; i < PER; ++i) sc[i] = sc[i] / sum;
-    } else {
 #pragma unroll
-        for (int i = 0; i < PER; ++i) sc[i] = route_score(sc[i], p.score_fn);
-    }
-#pragma unroll
-    for (int i = 0; i < PER; ++i) {
-        int e = lane + 32 * i;
-        ch[i] = e < E ? sc[i] + (p.bias ? p.bias[e] : 0.0f) : -INFINITY;
+        for (int i = 0; i < PER; ++i) {
+            int e = lane + 32 * i;
+            ch[i] = e < E ? sc[i] + (p.bias ? p.bias[e] : 0.0f) : -INFINITY;
+        }
     }
     // score of expert e (same value on every lane)
     auto score_of = [&](int e) {
@@ -98,6 +108,7 @@ __device__ __forceinline__ void route_row(const float *logits, const RouteParams
             if (i == (e >> 5)) v = sc[i];
         return __shfl_sync(0xffffffffu, v, e & 31);
     };
+    if (threadIdx.x == 0) RT_MARK(221);
     if (p.hash) {
         int mine = lane < K ? p.hash[(size_t)p.ids[s] * K + lane] : 0;
         for (int k = 0; k < K; ++k) {
@@ -122,12 +133,15 @@ __device__ __forceinline__ void route_row(const float *logits, const RouteParams
                     bi = e;
                 }
             }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                float ov = __shfl_xor_sync(0xffffffffu, best, o);
-                int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-                if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
-            }
+            // warp argmax: the largest value (order-preserving unsigned key,
+            // -0 taken as +0 so equal values compare equal), then the lowest
+            // expert id among the lanes holding it (NaN never became a
+            // lane's best, so it never wins)
+            const float bz = best == 0.0f ? 0.0f : best;
+            const uint32_t bits = __float_as_uint(bz);
+            const uint32_t key = (bits & 0x80000000u) ? ~bits : (bits | 0x80000000u);
+            const uint32_t kmax = __reduce_max_sync(0xffffffffu, key);
+            bi = (int)__reduce_min_sync(0xffffffffu, (uint32_t)(key == kmax ? bi : 0x7fffffff));
             if (bi == 0x7fffffff) bi = 0;  // no finite candidate left
             if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
             float w = score_of(bi);
@@ -137,20 +151,22 @@ __device__ __forceinline__ void route_row(const float *logits, const RouteParams
             }
         }
     }
+    if (threadIdx.x == 0) RT_MARK(222);
     __syncwarp();
-    if (lane == 0) {  // moe_route_finalize, moe_route.h:89-99
-        float sum = 0.0f;
-        if (p.normalize) {
-            for (int k = 0; k < K; ++k) sum += selw[k];
-            sum += 1e-20f;
-        }
-        for (int k = 0; k < K; ++k) {
-            float w = p.normalize ? selw[k] / sum : selw[k];
-            w = w * p.routed_scale;
-            p.route_ids[s * K + k] = sel[k];
-            p.route_w[s * K + k] = w;
-            selw[k] = w;
-        }
+    // moe_route_finalize (moe_route.h:89-99): every lane forms the same
+    // ascending-slot sum, then lane k finishes slot k
+    float sum = 0.0f;
+    if (p.normalize) {
+        for (int k = 0; k < K; ++k) sum += selw[k];
+        sum += 1e-20f;
+    }
+    __syncwarp();
+    for (int k = lane; k < K; k += 32) {
+        float w = p.normalize ? selw[k] / sum : selw[k];
+        w = w * p.routed_scale;
+        p.route_ids[s * K + k] = sel[k];
+        p.route_w[s * K + k] = w;
+        selw[k] = w;
     }
     __syncwarp();
 }
@@ -176,6 +192,7 @@ __device__ __forceinline__ void route_select_block(const float *logits, const Ro
         else route_row<32>(logits, p, warp, sel[warp], selw[warp]);
     }
     __syncthreads();
+    if (threadIdx.x == 0) RT_MARK(213);
     if (threadIdx.x < p.S * K) {
         int s = threadIdx.x / K, k = threadIdx.x % K;
         used_flag[sel[s][k]] = 1;
@@ -214,6 +231,7 @@ __device__ __forceinline__ void route_select_block(const float *logits, const Ro
         if (e < p.E && used_flag[e]) slot_of[e] = slot++;
     }
     __syncthreads();
+    if (threadIdx.x == 0) RT_MARK(214);
     if (threadIdx.x == 0) {
         *p.n_before = pre_lo;
         *p.n_active = pre_hi - pre_lo;
@@ -255,8 +273,10 @@ __global__ void __launch_bounds__(kRouteThreads) router_kernel(const float *W, c
         int k4 = threadIdx.x + i * kRouteThreads;
         if (k4 < D / 4) wpre[i] = __ldg(w4 + k4);
     }
+    if (threadIdx.x == 0 && blockIdx.x == 0) RT_MARK(210);
     pdl_wait();
     pdl_release();
+    if (threadIdx.x == 0 && blockIdx.x == 0) RT_MARK(211);
     for (int k4 = threadIdx.x, i = 0; k4 < D / 4; k4 += blockDim.x, ++i) {
         float4 w;
         if (i < kPre) {
@@ -287,7 +307,14 @@ __global__ void __launch_bounds__(kRouteThreads) router_kernel(const float *W, c
     if (threadIdx.x < S) {
         float t = 0.0f;
         for (int w = 0; w < 8; ++w) t += red[w][threadIdx.x];
-        logits[(size_t)threadIdx.x * E + e] = t;
+        if (p.score_fn == FC_SCORE_SOFTMAX) {
+            logits[(size_t)threadIdx.x * E + e] = t;  // normalized over the row by the selection
+        } else {
+            // per-expert score functions: score and selection value here
+            const float sc = route_score(t, p.score_fn);
+            logits[(size_t)threadIdx.x * E + e] = sc;
+            p.choice[(size_t)threadIdx.x * E + e] = sc + (p.bias ? __ldg(p.bias + e) : 0.0f);
+        }
         __threadfence();
     }
     __syncthreads();
@@ -298,8 +325,10 @@ __global__ void __launch_bounds__(kRouteThreads) router_kernel(const float *W, c
     }
     __syncthreads();
     if (!is_last) return;
+    if (threadIdx.x == 0) RT_MARK(212);
     __threadfence();
     route_select_block(logits, p);
+    if (threadIdx.x == 0) RT_MARK(215);
 }
 
 // resid[s][d] += (sum over slots ascending of coef * routed[slot][s][d])

@@ -668,6 +668,7 @@ cudaError_t record_forward(FcSession *s, int S) {
             rp.active = s->active;
             rp.coef = s->coef;
             rp.n_global = s->n_global;
+            rp.choice = s->router_logits + (size_t)mb * E;
             rp.n_before = s->n_before;
             rp.arrivals = s->route_arrivals;
             FC_TRY(launch_pdl(router_kernel, dim3(E), dim3(kRouteThreads), 0, st, y.router.p, s->xn, D,
@@ -1169,7 +1170,7 @@ int fc_session_create(FcSession **out, FcModel *m, const FcOptions *options, cha
     ok = ok && salloc(s, s->part_l, (size_t)s->splits * mb * H);
     ok = ok && salloc(s, s->ctx_xq, (size_t)H * mb * kpad(L) * 2);
     ok = ok && salloc(s, s->o_xq, (size_t)mb * kpad(H * c.value_dim) * 2);
-    ok = ok && salloc(s, s->router_logits, (size_t)mb * E);
+    ok = ok && salloc(s, s->router_logits, (size_t)2 * mb * E);  // scores, then choices
     ok = ok && salloc(s, s->route_ids, (size_t)c.layer_count * mb * K);
     ok = ok && salloc(s, s->route_w, (size_t)c.layer_count * mb * K);
     ok = ok && salloc(s, s->n_active, 1) && salloc(s, s->active, (size_t)s->max_slots + 1);
