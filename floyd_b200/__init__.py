@@ -164,6 +164,12 @@ class Session:
         err = _err()
         self._check(self._lib.fc_session_rollback(self.handle, int(position), err, len(err)), err)
 
+    def drafts(self):
+        """The on-device drafter's proposals from the last verify."""
+        out = np.zeros(8, dtype=np.int32)
+        n = self._lib.fc_session_drafts(self.handle, out.ctypes.data_as(ctypes.POINTER(ctypes.c_int)), 8)
+        return out[:max(n, 0)].tolist()
+
     def ep_handle(self):
         """This rank's expert-parallel receive-region handle (bytes)."""
         buf = ctypes.create_string_buffer(64)

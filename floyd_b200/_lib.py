@@ -30,7 +30,8 @@ class FcModelConfig(ctypes.Structure):
         ("has_selection_bias", ctypes.c_int), ("routed_scale", ctypes.c_float),
         ("swiglu_limit", ctypes.c_float), ("rms_norm_epsilon", ctypes.c_float),
         ("rope_theta", ctypes.c_float), ("dense_format", ctypes.c_int),
-        ("expert_format", ctypes.c_int), ("resident_bytes", ctypes.c_uint64),
+        ("expert_format", ctypes.c_int), ("mtp_layers", ctypes.c_int),
+        ("resident_bytes", ctypes.c_uint64),
     ]
 
     @classmethod
@@ -102,6 +103,7 @@ SIGNATURES = {
     "fc_session_copy_row_logits": (_I, [_P, _FP, _I]),
     "fc_session_seed_context": (_I, [_P, _I, ctypes.c_uint64, _C, _S]),
     "fc_session_ep_handle": (_I, [_P, ctypes.c_void_p, _S, _C, _S]),
+    "fc_session_drafts": (_I, [_P, _IP, _I]),
     "fc_session_ep_connect": (_I, [_P, ctypes.c_char_p, _I, _C, _S]),
     "fc_session_set_profiling": (_I, [_P, _I]),
     "fc_session_profile": (_I, [_P, _I, _C, _S, ctypes.POINTER(ctypes.c_double),

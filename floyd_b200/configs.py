@@ -49,7 +49,7 @@ CONFIGS = {
         hash_layer_count=3, score_fn=SCORE_SQRT_SOFTPLUS, normalize_topk=1,
         has_selection_bias=1, routed_scale=1.5, swiglu_limit=10.0,
         rms_norm_epsilon=1e-6, rope_theta=10000.0,
-        dense_format=FMT_Q8, expert_format=FMT_MXFP4,
+        dense_format=FMT_Q8, expert_format=FMT_MXFP4, mtp_layers=1,
         context=16384, rows=4),
 }
 

@@ -39,6 +39,7 @@ struct Result {
     int error;      // error bits raised by kernels of this pass
     int pad;
     int row_tops[kMaxRows];
+    int drafts[kMaxRows];   // MTP drafter proposals (verify with k > 0)
 };
 
 __device__ __forceinline__ float accept_uniform(unsigned long long seed, unsigned long long counter,
@@ -224,6 +225,52 @@ __global__ void __launch_bounds__(256) accept_kernel(const float *logits, int V,
     res->next_token = next;
     res->error = *err;
     *err = 0;
+}
+
+// ---- MTP drafter glue --------------------------------------------------
+// Step i of the drafter: position pos + commit + i, input token = the
+// target's next token (i = 0) or the previous proposal; step 0 also takes
+// the hidden state (pre-norm residual) of the last committed row.
+__global__ void mtp_prep_kernel(int i, const Staging *main_st, const Result *res, Staging *mst,
+                                const float *resid, float *mtp_h, int D) {
+    pdl_wait();
+    pdl_release();
+    const int commit = res->commit;
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        mst->pos = main_st->pos + commit + i;
+        mst->rows = 1;
+        mst->k = -1;
+        mst->mode = FC_ACCEPT_GREEDY;
+        int t = i == 0 ? res->next_token : res->drafts[i - 1];
+        mst->ids[0] = t < 0 ? 0 : t;
+    }
+    if (i == 0)
+        for (int d = blockIdx.x * blockDim.x + threadIdx.x; d < D; d += gridDim.x * blockDim.x)
+            mtp_h[d] = resid[(size_t)(commit - 1) * D + d];
+}
+
+// Greedy pick of the drafter's row (same order as the target's argmax:
+// NaN never wins, lower index on ties); writes proposal i.
+__global__ void __launch_bounds__(32) mtp_pick_kernel(HeadPartials hp, int chunks, Result *res,
+                                                      Staging *mst, int i) {
+    pdl_wait();
+    pdl_release();
+    const int lane = threadIdx.x;
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int c = lane; c < chunks; c += 32)
+        if (better(hp.amax[c], hp.aidx[c], bv, bi)) { bv = hp.amax[c]; bi = hp.aidx[c]; }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+        int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+        if (better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
+    }
+    if (lane == 0) {
+        const int t = bi == 0x7fffffff ? 0 : bi;
+        res->drafts[i] = t;
+        mst->ids[0] = t;
+    }
 }
 
 }  // namespace fc

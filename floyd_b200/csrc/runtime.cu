@@ -79,6 +79,8 @@ struct DevLayer {
     int *hash = nullptr;           // [vocab][K] or null
     uint32_t hash_tid = 0;
     bool dense = false;
+    DevVec enorm, hnorm, head_norm;  // MTP drafter layer only
+    DevMat eh_proj;                  // MTP: [D][2D]
 };
 
 struct TensorRef {
@@ -134,6 +136,11 @@ struct FcSession {
     HeadPartials hp{};
     int *d_err = nullptr;    // bit 1: a bounded wait in a kernel gave up
     int *route_arrivals = nullptr;   // router block counter (zero between launches)
+    Staging *d_mtp = nullptr;        // MTP drafter step parameters (device)
+    float *mtp_h = nullptr;          // drafter hidden state [D]
+    float *mtp_logits = nullptr;     // drafter logits [V] (the target's stay readable)
+    __half *mtp_xq = nullptr;        // [enorm(embed) | hnorm(h)] as xq, kpad(2D)
+    int last_drafts = 0;             // proposals made by the last pass
     int *n_global = nullptr, *n_before = nullptr;  // global active experts / first global slot here
     int g_slots = 0;                 // global slots (active experts of all ranks) at most
     // expert parallel (model world > 1): receive region = two buffers of the
@@ -200,11 +207,12 @@ void for_each_tensor(FcModel *m, F f) {
     f(&m->lm_head, nullptr);
     f(nullptr, &m->final_norm);
     for (auto &y : m->layers) {
-        DevVec *vecs[] = {&y.attn_norm, &y.ffn_norm, &y.kv_a_norm, &y.q_a_norm, &y.router, &y.bias};
+        DevVec *vecs[] = {&y.attn_norm, &y.ffn_norm, &y.kv_a_norm, &y.q_a_norm, &y.router, &y.bias,
+                          &y.enorm, &y.hnorm, &y.head_norm};
         for (DevVec *v : vecs) f(nullptr, v);
         DevMat *mats[] = {&y.q_proj, &y.q_a, &y.q_b, &y.kv_a, &y.kv_b, &y.o_proj,
                           &y.d_gate, &y.d_up, &y.d_down, &y.e_gate, &y.e_up, &y.e_down,
-                          &y.s_gate, &y.s_up, &y.s_down};
+                          &y.s_gate, &y.s_up, &y.s_down, &y.eh_proj};
         for (DevMat *mm : mats) f(mm, nullptr);
     }
 }
@@ -231,6 +239,9 @@ bool config_ok(const FcModelConfig *c, char *err, size_t n) {
         return set_error(err, n, "dense and expert formats must be Q8, Q4 or MXFP4");
     if (c->first_dense_layer_count > 0 && c->dense_intermediate_size <= 0)
         return set_error(err, n, "dense layers need dense_intermediate_size");
+    if (c->mtp_layers < 0 || c->mtp_layers > 1 ||
+        (c->mtp_layers && c->first_dense_layer_count > c->layer_count))
+        return set_error(err, n, "mtp_layers must be 0 or 1");
     return true;
 }
 
@@ -241,10 +252,16 @@ int build_model(FcModel *m, char *err, size_t n) {
     plan_mat(m->embed, df, c.vocab_size, D, 1, fc_tensor_id(-1, FC_T_EMBED, 0), 0);
     plan_mat(m->lm_head, df, c.vocab_size, D, 1, fc_tensor_id(-1, FC_T_LM_HEAD, 0), 0);
     plan_vec(m->final_norm, D, fc_tensor_id(-1, FC_T_FINAL_NORM, 0), 1);
-    m->layers.resize(c.layer_count);
+    m->layers.resize(c.layer_count + c.mtp_layers);
     int nl = m->expert_hi - m->expert_lo;
-    for (int l = 0; l < c.layer_count; ++l) {
+    for (int l = 0; l < c.layer_count + c.mtp_layers; ++l) {
         DevLayer &y = m->layers[l];
+        if (l >= c.layer_count) {  // MTP drafter extras
+            plan_vec(y.enorm, D, fc_tensor_id(l, FC_T_MTP_ENORM, 0), 1);
+            plan_vec(y.hnorm, D, fc_tensor_id(l, FC_T_MTP_HNORM, 0), 1);
+            plan_vec(y.head_norm, D, fc_tensor_id(l, FC_T_MTP_HEAD_NORM, 0), 1);
+            plan_mat(y.eh_proj, df, D, 2 * D, 1, fc_tensor_id(l, FC_T_MTP_EH_PROJ, 0), 0);
+        }
         plan_vec(y.attn_norm, D, fc_tensor_id(l, FC_T_ATTN_NORM, 0), 1);
         plan_vec(y.ffn_norm, D, fc_tensor_id(l, FC_T_FFN_NORM, 0), 1);
         plan_vec(y.kv_a_norm, L, fc_tensor_id(l, FC_T_KV_A_NORM, 0), 1);
@@ -322,9 +339,13 @@ int build_model(FcModel *m, char *err, size_t n) {
     add_mat("model.embed_tokens.weight", m->embed, 0);
     add_mat("lm_head.weight", m->lm_head, 0);
     add_vec("model.norm.weight", m->final_norm);
-    for (int l = 0; l < c.layer_count; ++l) {
+    for (int l = 0; l < c.layer_count + c.mtp_layers; ++l) {
         DevLayer &y = m->layers[l];
         std::string p = "model.layers." + std::to_string(l) + ".";
+        add_vec(p + "enorm.weight", y.enorm);
+        add_vec(p + "hnorm.weight", y.hnorm);
+        add_vec(p + "shared_head.norm.weight", y.head_norm);
+        add_mat(p + "eh_proj.weight", y.eh_proj, 0);
         add_vec(p + "input_layernorm.weight", y.attn_norm);
         add_vec(p + "post_attention_layernorm.weight", y.ffn_norm);
         add_vec(p + "self_attn.kv_a_layernorm.weight", y.kv_a_norm);
@@ -517,7 +538,10 @@ void mark(FcSession *s, const char *name) {
 
 // Enqueues one forward of `rows` rows (parameters already in d_stage) on the
 // session stream: embedding, every layer, lm-head, argmax / acceptance.
-cudaError_t record_forward(FcSession *s, int S) {
+// Enqueues layer l (target layers 0 .. layer_count - 1, the MTP layer at
+// layer_count) for S rows at positions *d_pos + s, updating s->resid.
+// `ids` are the rows' token ids (hash routing).
+cudaError_t record_layer(FcSession *s, int S, int l, const int *d_pos, const int *ids) {
     FcModel *m = s->m;
     const FcModelConfig &c = m->c;
     cudaStream_t st = s->stream;
@@ -525,244 +549,258 @@ cudaError_t record_forward(FcSession *s, int S) {
     const int NP = c.qk_nope_dim, VD = c.value_dim, QW = NP + R;
     const int kpD = kpad(D), kpL = kpad(L), kpO = kpad(H * VD);
     const int mb = s->rows_max;
-    const int *d_pos = &s->d_stage->pos;
     const float scale = 1.0f / sqrtf((float)(NP + R));
     const int df = c.dense_format, ef = c.expert_format;
+    (void)kpL;
+    (void)kpO;
+    (void)ef;
+    DevLayer &y = m->layers[l];
+    __half *cache = s->cache + (size_t)l * s->opt.context_size * (L + R);
+    FC_TRY(launch_pdl(rmsnorm_kernel, dim3(S), dim3(norm_threads(D)), 0, st, s->resid, D, y.attn_norm.p, D, c.rms_norm_epsilon,
+                                      s->xq_norm, kpD, nullptr, 0));
+    mark(s, "rmsnorm");
+    {
+        GemvBatch b{};
+        b.S = S;
+        b.err = s->d_err;
+        if (c.q_lora_rank > 0) {
+            b.seg[0] = seg_of(y.q_a, s->xq_norm, EPI_STORE);
+            b.seg[0].y = s->qa;
+            b.seg[0].ldy = c.q_lora_rank;
+        } else {
+            b.seg[0] = seg_of(y.q_proj, s->xq_norm, EPI_STORE);
+            b.seg[0].y = s->q;
+            b.seg[0].ldy = H * QW;
+        }
+        b.seg[1] = seg_of(y.kv_a, s->xq_norm, EPI_STORE);
+        b.seg[1].y = s->ckv;
+        b.seg[1].ldy = L + R;
+        b.nseg = 2;
+        FC_TRY(launch_gemv_batch(df, b, m->sms, st));
+        mark(s, "gemv_q_kv_a");
+    }
+    if (c.q_lora_rank > 0) {
+        FC_TRY(launch_pdl(rmsnorm_kernel, dim3(S), dim3(norm_threads(c.q_lora_rank)), 0, st, s->qa, c.q_lora_rank, y.q_a_norm.p, c.q_lora_rank,
+                                          c.rms_norm_epsilon, s->qa_xq, kpad(c.q_lora_rank),
+                                          nullptr, 0));
+        mark(s, "rmsnorm");
+        GemvSeg g = seg_of(y.q_b, s->qa_xq, EPI_STORE);
+        g.y = s->q;
+        g.ldy = H * QW;
+        FC_TRY(gemv1(df, g, S, 0.0f, s->d_err, m->sms, st));
+        mark(s, "gemv_q_b");
+    }
+    FC_TRY(launch_pdl(mla_prep_kernel, dim3(dim3(S, 1 + (H * (R / 2) + 255) / 256)), dim3(256), 0, st, s->ckv, s->q, y.kv_a_norm.p, L, R, H, NP,
+                                       c.rms_norm_epsilon, c.rope_theta, d_pos, cache, s->qcat));
+    mark(s, "mla_prep");
+    {
+        dim3 grid(H, L / kAbsorbCols);
+        FC_TRY(launch_pdl(mla_absorb_kernel, dim3(grid), dim3(256), 0, st, df, y.kv_b.w, y.kv_b.kp, s->q, S, H,
+                                                NP, VD, R, L, s->qcat));
+        mark(s, "mla_absorb");
+    }
+    if (s->attn_tc) {
+        dim3 grid((S * H + kTcRows - 1) / kTcRows, 2, s->splits);
+        const int kv_row0 = l * s->opt.context_size, kps = s->chunks_per_split * kAttnKeys;
+        if (L == 512)
+            FC_TRY(launch_pdl(mla_attention_tc_kernel<512>, grid, dim3(kTcThreads), TcAttnPlan<512>::SMEM, st,
+                              s->qmap, s->kvmap, kv_row0, S, H, kps, d_pos, scale, s->part_o, s->part_m,
+                              s->part_l, s->d_err));
+        else
+            FC_TRY(launch_pdl(mla_attention_tc_kernel<256>, grid, dim3(kTcThreads), TcAttnPlan<256>::SMEM, st,
+                              s->qmap, s->kvmap, kv_row0, S, H, kps, d_pos, scale, s->part_o, s->part_m,
+                              s->part_l, s->d_err));
+        mark(s, "mla_attention");
+    } else {
+        dim3 grid((S * H + kAttnQ - 1) / kAttnQ, s->splits);
+        if (L == 512)
+            FC_TRY(launch_pdl(mla_attention_kernel<512, 64>, grid, dim3(kAttnThreads), s->attn_smem,
+                              st, (const __half *)cache, (const __half *)s->qcat, S, H,
+                              s->chunks_per_split, d_pos, scale, s->part_o, s->part_m, s->part_l));
+        else
+            FC_TRY(launch_pdl(mla_attention_kernel<256, 64>, grid, dim3(kAttnThreads), s->attn_smem,
+                              st, (const __half *)cache, (const __half *)s->qcat, S, H,
+                              s->chunks_per_split, d_pos, scale, s->part_o, s->part_m, s->part_l));
+        mark(s, "mla_attention");
+    }
+    {
+        size_t head_stride = (size_t)mb * kpL * 2;
+        FC_TRY(launch_pdl(mla_combine_kernel, dim3(S * H, (L + kCombineThreads - 1) / kCombineThreads),
+                          dim3(kCombineThreads), 0, st, (const float *)s->part_o,
+                          (const float *)s->part_m, (const float *)s->part_l, s->splits, S, H, L,
+                          s->ctx_xq, head_stride));
+        mark(s, "mla_combine");
+        // W_UV: rows nope .. nope+v of each head's kv_b block (decode_value, :345-375)
+        // nope and value_dim are multiples of 16, so each head's W_UV
+        // block starts on a tile boundary of kv_b
+        GemvSeg g = seg_of(y.kv_b, s->ctx_xq, EPI_STORE_XQ);
+        size_t tb = tile_bytes(df, y.kv_b.kp);
+        g.w = y.kv_b.w + (size_t)(NP / kTileRows) * tb;
+        g.O = VD;
+        g.count = H;
+        g.w_stride = (int64_t)((NP + VD) / kTileRows) * (int64_t)tb;
+        g.xq_stride = (int64_t)head_stride;
+        g.yq = s->o_xq;
+        g.kpy = kpO;
+        g.out_stride = VD;
+        FC_TRY(gemv1(df, g, S, 0.0f, s->d_err, m->sms, st));
+        mark(s, "gemv_w_uv");
+    }
+    {
+        GemvSeg g = seg_of(y.o_proj, s->o_xq, EPI_ADD);
+        g.y = s->resid;
+        g.ldy = D;
+        FC_TRY(gemv1(df, g, S, 0.0f, s->d_err, m->sms, st));
+        mark(s, "gemv_o_proj");
+    }
+    FC_TRY(launch_pdl(rmsnorm_kernel, dim3(S), dim3(norm_threads(D)), 0, st, s->resid, D, y.ffn_norm.p, D, c.rms_norm_epsilon,
+                                      s->xq_norm, kpD, s->xn, D));
+    mark(s, "rmsnorm");
+    if (y.dense) {
+        int kpI = kpad(c.dense_intermediate_size);
+        GemvSeg g = seg_of(y.d_gate, s->xq_norm, EPI_SWIGLU_XQ);
+        g.w2 = y.d_up.w;
+        g.yq = s->hd_xq;
+        g.kpy = kpI;
+        FC_TRY(gemv1(df, g, S, 0.0f, s->d_err, m->sms, st));
+        mark(s, "gemv_dense_gate_up");
+        GemvSeg d = seg_of(y.d_down, s->hd_xq, EPI_ADD);
+        d.y = s->resid;
+        d.ldy = D;
+        FC_TRY(gemv1(df, d, S, 0.0f, s->d_err, m->sms, st));
+        mark(s, "gemv_dense_down");
+    } else {
+        int E = c.expert_count, K = c.experts_per_token;
+        RouteParams rp{};
+        rp.E = E; rp.K = K; rp.S = S;
+        rp.score_fn = c.score_fn;
+        rp.normalize = c.normalize_topk;
+        rp.routed_scale = c.routed_scale;
+        rp.bias = y.bias.p;
+        rp.hash = y.hash;
+        rp.ids = ids;
+        rp.expert_lo = m->expert_lo;
+        rp.expert_hi = m->expert_hi;
+        rp.route_ids = s->route_ids + (size_t)l * mb * K;
+        rp.route_w = s->route_w + (size_t)l * mb * K;
+        rp.n_active = s->n_active;
+        rp.active = s->active;
+        rp.coef = s->coef;
+        rp.n_global = s->n_global;
+        rp.choice = s->router_logits + (size_t)mb * E;
+        rp.n_before = s->n_before;
+        rp.arrivals = s->route_arrivals;
+        FC_TRY(launch_pdl(router_kernel, dim3(E), dim3(kRouteThreads), 0, st, y.router.p, s->xn, D,
+                          s->router_logits, rp));
+        mark(s, "router");
+        int I = c.moe_intermediate_size, kpI = kpad(I);
+        int W = I * c.shared_expert_count, kpW = kpad(std::max(W, 1));
+        // gate / up + SwiGLU of the active routed experts and the shared expert
+        GemvWork gu{};
+        gu.moe = 1;
+        gu.seg[0] = seg_of(y.e_gate, s->xq_norm, EPI_SWIGLU_XQ);
+        gu.seg[0].w2 = y.e_up.w;
+        gu.seg[0].w_stride = (int64_t)y.e_gate.w_bytes;
+        gu.seg[0].yq = s->h_xq;
+        gu.seg[0].kpy = kpI;
+        if (y.s_gate.count) {
+            gu.seg[1] = seg_of(y.s_gate, s->xq_norm, EPI_SWIGLU_XQ);
+            gu.seg[1].w2 = y.s_up.w;
+            gu.seg[1].yq = s->hsh_xq;
+            gu.seg[1].kpy = kpW;
+        }
+        gu.nseg = 2;
+        gu.max_slots = s->max_slots;
+        gu.expert_base = m->expert_lo;
+        gu.n_active = s->n_active;
+        gu.active = s->active;
+        gu.in_slot_stride = 0;
+        gu.out_slot_stride = (int64_t)mb * kpI * 2;
+        gu.S = S;
+        gu.swiglu_limit = c.swiglu_limit;
+        gu.err = s->d_err;
+        FC_TRY(launch_gemv_work(ef, df, gu, m->sms, st));
+        mark(s, "moe_gate_up");
+        // down projections
+        GemvWork dn{};
+        dn.moe = 1;
+        dn.seg[0] = seg_of(y.e_down, s->h_xq, EPI_STORE);
+        dn.seg[0].w_stride = (int64_t)y.e_down.w_bytes;
+        dn.seg[0].y = s->moe_part;
+        dn.seg[0].ldy = D;
+        const bool ep = m->world > 1;
+        const int64_t parity_stride = (int64_t)s->g_slots * mb * D;
+        if (ep) {
+            // routed outputs go to global slot n_before + local slot of
+            // the receive buffer of every rank (this one and the peers)
+            dn.seg[0].y = s->ep_xbuf;
+            for (int r = 0, k = 0; r < m->world; ++r)
+                if (r != m->rank) dn.seg[0].peer_y[k++] = reinterpret_cast<float *>(s->ep_peer_region[r]);
+            dn.seg[0].npeer = m->world - 1;
+            dn.slot_base = s->n_before;
+            dn.ep_epoch = s->ep_epoch;
+            dn.parity_stride = parity_stride;
+        }
+        if (y.s_down.count) {
+            dn.seg[1] = seg_of(y.s_down, s->hsh_xq, EPI_STORE);
+            dn.seg[1].y = s->sh_part;
+            dn.seg[1].ldy = D;
+        }
+        dn.nseg = 2;
+        dn.max_slots = s->max_slots;
+        dn.expert_base = m->expert_lo;
+        dn.n_active = s->n_active;
+        dn.active = s->active;
+        dn.in_slot_stride = (int64_t)mb * kpI * 2;
+        dn.out_slot_stride = (int64_t)mb * D;
+        dn.S = S;
+        dn.err = s->d_err;
+        FC_TRY(launch_gemv_work(ef, df, dn, m->sms, st));
+        mark(s, "moe_down");
+        EpLink link{};
+        link.world = m->world;
+        link.rank = m->rank;
+        if (ep) {
+            link.epoch = s->ep_epoch;
+            link.flags = s->ep_flags;
+            for (int r = 0; r < m->world; ++r)
+                if (r != m->rank)
+                    link.peer_flags[r] = reinterpret_cast<int *>(
+                        reinterpret_cast<uint8_t *>(s->ep_peer_region[r]) + 2 * parity_stride * sizeof(float));
+            FC_TRY(launch_pdl(ep_signal_kernel, dim3(1), dim3(1), 0, st, link));
+            mark(s, "ep_signal");
+        }
+        FC_TRY(launch_pdl(moe_combine_kernel, dim3(S * ((D + kMoeCombineThreads - 1) / kMoeCombineThreads)),
+                          dim3(kMoeCombineThreads), 0, st, s->resid, ep ? (const float *)s->ep_xbuf : s->moe_part,
+                          y.s_down.count ? (const float *)s->sh_part : nullptr, (const float *)s->coef,
+                          (const int *)s->n_global, S, D, mb, link, parity_stride, s->d_err));
+        mark(s, "moe_combine");
+    }
+    if (s->trace && l < c.layer_count) {
+        FC_TRY(cudaMemcpyAsync(s->layer_out + (size_t)l * mb * D, s->resid, (size_t)S * D * 4,
+                               cudaMemcpyDeviceToDevice, st));
+        mark(s, "layer_trace_copy");
+    }
+
+    return cudaSuccess;
+}
+
+cudaError_t record_mtp_step(FcSession *s, int i);
+
+cudaError_t record_forward(FcSession *s, int S, int drafts) {
+    FcModel *m = s->m;
+    const FcModelConfig &c = m->c;
+    cudaStream_t st = s->stream;
+    const int D = c.hidden_size, kpD = kpad(D);
+    const int *d_pos = &s->d_stage->pos;
+    const int df = c.dense_format;
 
     FC_TRY(cudaMemcpyAsync(s->d_stage, s->h_stage, sizeof(Staging), cudaMemcpyHostToDevice, st));
     FC_TRY(launch_pdl(embed_kernel, dim3(S), dim3(256), 0, st, m->embed.fmt, m->embed.w, D, m->embed.kp, s->d_stage->ids,
                                     s->resid));
     FC_TRY(cudaGetLastError());
     mark(s, "embed");
-    for (int l = 0; l < c.layer_count; ++l) {
-        DevLayer &y = m->layers[l];
-        __half *cache = s->cache + (size_t)l * s->opt.context_size * (L + R);
-        FC_TRY(launch_pdl(rmsnorm_kernel, dim3(S), dim3(norm_threads(D)), 0, st, s->resid, D, y.attn_norm.p, D, c.rms_norm_epsilon,
-                                          s->xq_norm, kpD, nullptr, 0));
-        mark(s, "rmsnorm");
-        {
-            GemvBatch b{};
-            b.S = S;
-            b.err = s->d_err;
-            if (c.q_lora_rank > 0) {
-                b.seg[0] = seg_of(y.q_a, s->xq_norm, EPI_STORE);
-                b.seg[0].y = s->qa;
-                b.seg[0].ldy = c.q_lora_rank;
-            } else {
-                b.seg[0] = seg_of(y.q_proj, s->xq_norm, EPI_STORE);
-                b.seg[0].y = s->q;
-                b.seg[0].ldy = H * QW;
-            }
-            b.seg[1] = seg_of(y.kv_a, s->xq_norm, EPI_STORE);
-            b.seg[1].y = s->ckv;
-            b.seg[1].ldy = L + R;
-            b.nseg = 2;
-            FC_TRY(launch_gemv_batch(df, b, m->sms, st));
-            mark(s, "gemv_q_kv_a");
-        }
-        if (c.q_lora_rank > 0) {
-            FC_TRY(launch_pdl(rmsnorm_kernel, dim3(S), dim3(norm_threads(c.q_lora_rank)), 0, st, s->qa, c.q_lora_rank, y.q_a_norm.p, c.q_lora_rank,
-                                              c.rms_norm_epsilon, s->qa_xq, kpad(c.q_lora_rank),
-                                              nullptr, 0));
-            mark(s, "rmsnorm");
-            GemvSeg g = seg_of(y.q_b, s->qa_xq, EPI_STORE);
-            g.y = s->q;
-            g.ldy = H * QW;
-            FC_TRY(gemv1(df, g, S, 0.0f, s->d_err, m->sms, st));
-            mark(s, "gemv_q_b");
-        }
-        FC_TRY(launch_pdl(mla_prep_kernel, dim3(dim3(S, 1 + (H * (R / 2) + 255) / 256)), dim3(256), 0, st, s->ckv, s->q, y.kv_a_norm.p, L, R, H, NP,
-                                           c.rms_norm_epsilon, c.rope_theta, d_pos, cache, s->qcat));
-        mark(s, "mla_prep");
-        {
-            dim3 grid(H, L / kAbsorbCols);
-            FC_TRY(launch_pdl(mla_absorb_kernel, dim3(grid), dim3(256), 0, st, df, y.kv_b.w, y.kv_b.kp, s->q, S, H,
-                                                    NP, VD, R, L, s->qcat));
-            mark(s, "mla_absorb");
-        }
-        if (s->attn_tc) {
-            dim3 grid((S * H + kTcRows - 1) / kTcRows, 2, s->splits);
-            const int kv_row0 = l * s->opt.context_size, kps = s->chunks_per_split * kAttnKeys;
-            if (L == 512)
-                FC_TRY(launch_pdl(mla_attention_tc_kernel<512>, grid, dim3(kTcThreads), TcAttnPlan<512>::SMEM, st,
-                                  s->qmap, s->kvmap, kv_row0, S, H, kps, d_pos, scale, s->part_o, s->part_m,
-                                  s->part_l, s->d_err));
-            else
-                FC_TRY(launch_pdl(mla_attention_tc_kernel<256>, grid, dim3(kTcThreads), TcAttnPlan<256>::SMEM, st,
-                                  s->qmap, s->kvmap, kv_row0, S, H, kps, d_pos, scale, s->part_o, s->part_m,
-                                  s->part_l, s->d_err));
-            mark(s, "mla_attention");
-        } else {
-            dim3 grid((S * H + kAttnQ - 1) / kAttnQ, s->splits);
-            if (L == 512)
-                FC_TRY(launch_pdl(mla_attention_kernel<512, 64>, grid, dim3(kAttnThreads), s->attn_smem,
-                                  st, (const __half *)cache, (const __half *)s->qcat, S, H,
-                                  s->chunks_per_split, d_pos, scale, s->part_o, s->part_m, s->part_l));
-            else
-                FC_TRY(launch_pdl(mla_attention_kernel<256, 64>, grid, dim3(kAttnThreads), s->attn_smem,
-                                  st, (const __half *)cache, (const __half *)s->qcat, S, H,
-                                  s->chunks_per_split, d_pos, scale, s->part_o, s->part_m, s->part_l));
-            mark(s, "mla_attention");
-        }
-        {
-            size_t head_stride = (size_t)mb * kpL * 2;
-            FC_TRY(launch_pdl(mla_combine_kernel, dim3(S * H, (L + kCombineThreads - 1) / kCombineThreads),
-                              dim3(kCombineThreads), 0, st, (const float *)s->part_o,
-                              (const float *)s->part_m, (const float *)s->part_l, s->splits, S, H, L,
-                              s->ctx_xq, head_stride));
-            mark(s, "mla_combine");
-            // W_UV: rows nope .. nope+v of each head's kv_b block (decode_value, :345-375)
-            // nope and value_dim are multiples of 16, so each head's W_UV
-            // block starts on a tile boundary of kv_b
-            GemvSeg g = seg_of(y.kv_b, s->ctx_xq, EPI_STORE_XQ);
-            size_t tb = tile_bytes(df, y.kv_b.kp);
-            g.w = y.kv_b.w + (size_t)(NP / kTileRows) * tb;
-            g.O = VD;
-            g.count = H;
-            g.w_stride = (int64_t)((NP + VD) / kTileRows) * (int64_t)tb;
-            g.xq_stride = (int64_t)head_stride;
-            g.yq = s->o_xq;
-            g.kpy = kpO;
-            g.out_stride = VD;
-            FC_TRY(gemv1(df, g, S, 0.0f, s->d_err, m->sms, st));
-            mark(s, "gemv_w_uv");
-        }
-        {
-            GemvSeg g = seg_of(y.o_proj, s->o_xq, EPI_ADD);
-            g.y = s->resid;
-            g.ldy = D;
-            FC_TRY(gemv1(df, g, S, 0.0f, s->d_err, m->sms, st));
-            mark(s, "gemv_o_proj");
-        }
-        FC_TRY(launch_pdl(rmsnorm_kernel, dim3(S), dim3(norm_threads(D)), 0, st, s->resid, D, y.ffn_norm.p, D, c.rms_norm_epsilon,
-                                          s->xq_norm, kpD, s->xn, D));
-        mark(s, "rmsnorm");
-        if (y.dense) {
-            int kpI = kpad(c.dense_intermediate_size);
-            GemvSeg g = seg_of(y.d_gate, s->xq_norm, EPI_SWIGLU_XQ);
-            g.w2 = y.d_up.w;
-            g.yq = s->hd_xq;
-            g.kpy = kpI;
-            FC_TRY(gemv1(df, g, S, 0.0f, s->d_err, m->sms, st));
-            mark(s, "gemv_dense_gate_up");
-            GemvSeg d = seg_of(y.d_down, s->hd_xq, EPI_ADD);
-            d.y = s->resid;
-            d.ldy = D;
-            FC_TRY(gemv1(df, d, S, 0.0f, s->d_err, m->sms, st));
-            mark(s, "gemv_dense_down");
-        } else {
-            int E = c.expert_count, K = c.experts_per_token;
-            RouteParams rp{};
-            rp.E = E; rp.K = K; rp.S = S;
-            rp.score_fn = c.score_fn;
-            rp.normalize = c.normalize_topk;
-            rp.routed_scale = c.routed_scale;
-            rp.bias = y.bias.p;
-            rp.hash = y.hash;
-            rp.ids = s->d_stage->ids;
-            rp.expert_lo = m->expert_lo;
-            rp.expert_hi = m->expert_hi;
-            rp.route_ids = s->route_ids + (size_t)l * mb * K;
-            rp.route_w = s->route_w + (size_t)l * mb * K;
-            rp.n_active = s->n_active;
-            rp.active = s->active;
-            rp.coef = s->coef;
-            rp.n_global = s->n_global;
-            rp.choice = s->router_logits + (size_t)mb * E;
-            rp.n_before = s->n_before;
-            rp.arrivals = s->route_arrivals;
-            FC_TRY(launch_pdl(router_kernel, dim3(E), dim3(kRouteThreads), 0, st, y.router.p, s->xn, D,
-                              s->router_logits, rp));
-            mark(s, "router");
-            int I = c.moe_intermediate_size, kpI = kpad(I);
-            int W = I * c.shared_expert_count, kpW = kpad(std::max(W, 1));
-            // gate / up + SwiGLU of the active routed experts and the shared expert
-            GemvWork gu{};
-            gu.moe = 1;
-            gu.seg[0] = seg_of(y.e_gate, s->xq_norm, EPI_SWIGLU_XQ);
-            gu.seg[0].w2 = y.e_up.w;
-            gu.seg[0].w_stride = (int64_t)y.e_gate.w_bytes;
-            gu.seg[0].yq = s->h_xq;
-            gu.seg[0].kpy = kpI;
-            if (y.s_gate.count) {
-                gu.seg[1] = seg_of(y.s_gate, s->xq_norm, EPI_SWIGLU_XQ);
-                gu.seg[1].w2 = y.s_up.w;
-                gu.seg[1].yq = s->hsh_xq;
-                gu.seg[1].kpy = kpW;
-            }
-            gu.nseg = 2;
-            gu.max_slots = s->max_slots;
-            gu.expert_base = m->expert_lo;
-            gu.n_active = s->n_active;
-            gu.active = s->active;
-            gu.in_slot_stride = 0;
-            gu.out_slot_stride = (int64_t)mb * kpI * 2;
-            gu.S = S;
-            gu.swiglu_limit = c.swiglu_limit;
-            gu.err = s->d_err;
-            FC_TRY(launch_gemv_work(ef, df, gu, m->sms, st));
-            mark(s, "moe_gate_up");
-            // down projections
-            GemvWork dn{};
-            dn.moe = 1;
-            dn.seg[0] = seg_of(y.e_down, s->h_xq, EPI_STORE);
-            dn.seg[0].w_stride = (int64_t)y.e_down.w_bytes;
-            dn.seg[0].y = s->moe_part;
-            dn.seg[0].ldy = D;
-            const bool ep = m->world > 1;
-            const int64_t parity_stride = (int64_t)s->g_slots * mb * D;
-            if (ep) {
-                // routed outputs go to global slot n_before + local slot of
-                // the receive buffer of every rank (this one and the peers)
-                dn.seg[0].y = s->ep_xbuf;
-                for (int r = 0, k = 0; r < m->world; ++r)
-                    if (r != m->rank) dn.seg[0].peer_y[k++] = reinterpret_cast<float *>(s->ep_peer_region[r]);
-                dn.seg[0].npeer = m->world - 1;
-                dn.slot_base = s->n_before;
-                dn.ep_epoch = s->ep_epoch;
-                dn.parity_stride = parity_stride;
-            }
-            if (y.s_down.count) {
-                dn.seg[1] = seg_of(y.s_down, s->hsh_xq, EPI_STORE);
-                dn.seg[1].y = s->sh_part;
-                dn.seg[1].ldy = D;
-            }
-            dn.nseg = 2;
-            dn.max_slots = s->max_slots;
-            dn.expert_base = m->expert_lo;
-            dn.n_active = s->n_active;
-            dn.active = s->active;
-            dn.in_slot_stride = (int64_t)mb * kpI * 2;
-            dn.out_slot_stride = (int64_t)mb * D;
-            dn.S = S;
-            dn.err = s->d_err;
-            FC_TRY(launch_gemv_work(ef, df, dn, m->sms, st));
-            mark(s, "moe_down");
-            EpLink link{};
-            link.world = m->world;
-            link.rank = m->rank;
-            if (ep) {
-                link.epoch = s->ep_epoch;
-                link.flags = s->ep_flags;
-                for (int r = 0; r < m->world; ++r)
-                    if (r != m->rank)
-                        link.peer_flags[r] = reinterpret_cast<int *>(
-                            reinterpret_cast<uint8_t *>(s->ep_peer_region[r]) + 2 * parity_stride * sizeof(float));
-                FC_TRY(launch_pdl(ep_signal_kernel, dim3(1), dim3(1), 0, st, link));
-                mark(s, "ep_signal");
-            }
-            FC_TRY(launch_pdl(moe_combine_kernel, dim3(S * ((D + kMoeCombineThreads - 1) / kMoeCombineThreads)),
-                              dim3(kMoeCombineThreads), 0, st, s->resid, ep ? (const float *)s->ep_xbuf : s->moe_part,
-                              y.s_down.count ? (const float *)s->sh_part : nullptr, (const float *)s->coef,
-                              (const int *)s->n_global, S, D, mb, link, parity_stride, s->d_err));
-            mark(s, "moe_combine");
-        }
-        if (s->trace) {
-            FC_TRY(cudaMemcpyAsync(s->layer_out + (size_t)l * mb * D, s->resid, (size_t)S * D * 4,
-                                   cudaMemcpyDeviceToDevice, st));
-            mark(s, "layer_trace_copy");
-        }
-    }
+    for (int l = 0; l < c.layer_count; ++l) FC_TRY(record_layer(s, S, l, d_pos, s->d_stage->ids));
     FC_TRY(launch_pdl(rmsnorm_kernel, dim3(S), dim3(norm_threads(D)), 0, st, s->resid, D, m->final_norm.p, D, c.rms_norm_epsilon,
                                       s->xq_norm, kpD, nullptr, 0));
     mark(s, "rmsnorm");
@@ -782,9 +820,54 @@ cudaError_t record_forward(FcSession *s, int S) {
                                          s->d_res, s->d_err));
         mark(s, "accept");
     }
+    for (int i = 0; i < drafts; ++i) FC_TRY(record_mtp_step(s, i));
     FC_TRY(cudaGetLastError());
     FC_TRY(cudaMemcpyAsync(s->h_res, s->d_res, sizeof(Result), cudaMemcpyDeviceToHost, st));
     return cudaSuccess;
+}
+
+// One greedy step of the MTP drafter (S = 1): embed the input token,
+// h_in = eh_proj([enorm(embed) | hnorm(h)]), the MTP layer over its own latent
+// cache, shared_head.norm, the shared lm-head, argmax -> proposal i.
+cudaError_t record_mtp_step(FcSession *s, int i) {
+    FcModel *m = s->m;
+    const FcModelConfig &c = m->c;
+    cudaStream_t st = s->stream;
+    const int D = c.hidden_size, kpD = kpad(D), kp2 = kpad(2 * D), df = c.dense_format;
+    const int lm = c.layer_count;  // the MTP layer
+    DevLayer &y = m->layers[lm];
+    FC_TRY(launch_pdl(mtp_prep_kernel, dim3((D + 255) / 256), dim3(256), 0, st, i, (const Staging *)s->d_stage,
+                      (const Result *)s->d_res, s->d_mtp, (const float *)s->resid, s->mtp_h, D));
+    mark(s, "mtp_prep");
+    FC_TRY(launch_pdl(embed_kernel, dim3(1), dim3(256), 0, st, m->embed.fmt, m->embed.w, D, m->embed.kp,
+                      (const int *)s->d_mtp->ids, s->resid));
+    FC_TRY(launch_pdl(rmsnorm_kernel, dim3(1), dim3(norm_threads(D)), 0, st, (const float *)s->resid, D,
+                      (const float *)y.enorm.p, D, c.rms_norm_epsilon, s->mtp_xq, kp2, (float *)nullptr, 0));
+    FC_TRY(launch_pdl(rmsnorm_kernel, dim3(1), dim3(norm_threads(D)), 0, st, (const float *)s->mtp_h, D,
+                      (const float *)y.hnorm.p, D, c.rms_norm_epsilon, s->mtp_xq + (size_t)D * 2, kp2,
+                      (float *)nullptr, 0));
+    {
+        GemvSeg g = seg_of(y.eh_proj, s->mtp_xq, EPI_STORE);
+        g.y = s->resid;
+        g.ldy = D;
+        FC_TRY(gemv1(df, g, 1, 0.0f, s->d_err, m->sms, st));
+    }
+    mark(s, "mtp_input");
+    FC_TRY(record_layer(s, 1, lm, &s->d_mtp->pos, s->d_mtp->ids));
+    FC_TRY(cudaMemcpyAsync(s->mtp_h, s->resid, (size_t)D * 4, cudaMemcpyDeviceToDevice, st));
+    FC_TRY(launch_pdl(rmsnorm_kernel, dim3(1), dim3(norm_threads(D)), 0, st, (const float *)s->resid, D,
+                      (const float *)y.head_norm.p, D, c.rms_norm_epsilon, s->xq_norm, kpD, (float *)nullptr, 0));
+    {
+        GemvSeg g = seg_of(m->lm_head, s->xq_norm, EPI_STORE);
+        g.y = s->mtp_logits;
+        g.ldy = c.vocab_size;
+        FC_TRY(gemv1(df, g, 1, 0.0f, s->d_err, m->sms, st));
+    }
+    FC_TRY(launch_pdl(head_partial_kernel, dim3(s->head_chunks, 1), dim3(256), 0, st, (const float *)s->mtp_logits,
+                      c.vocab_size, (const Staging *)s->d_mtp, s->hp, s->head_chunks));
+    FC_TRY(launch_pdl(mtp_pick_kernel, dim3(1), dim3(32), 0, st, s->hp, s->head_chunks, s->d_res, s->d_mtp, i));
+    mark(s, "mtp_head");
+    return cudaGetLastError();
 }
 
 // Every kernel of the forward asks for the same (maximum) shared-memory
@@ -797,7 +880,7 @@ cudaError_t prefer_shared_carveout() {
         (const void *)mla_attention_tc_kernel<512>, (const void *)mla_attention_tc_kernel<256>,
         (const void *)router_kernel,
         (const void *)moe_combine_kernel, (const void *)head_partial_kernel,
-        (const void *)accept_kernel,
+        (const void *)accept_kernel, (const void *)mtp_prep_kernel, (const void *)mtp_pick_kernel,
 #define FC_GEMV_PTR(A, B) (const void *)gemv_kernel<A, B>,
         FC_GEMV_FORMATS(FC_GEMV_PTR)
 #undef FC_GEMV_PTR
@@ -810,8 +893,8 @@ cudaError_t prefer_shared_carveout() {
     return cudaSuccess;
 }
 
-cudaGraphExec_t get_graph(FcSession *s, int S, char *err, size_t n) {
-    int key = S * 2 + (s->trace ? 1 : 0);
+cudaGraphExec_t get_graph(FcSession *s, int S, int drafts, char *err, size_t n) {
+    int key = (S * 2 + (s->trace ? 1 : 0)) * 16 + drafts;
     auto it = s->graphs.find(key);
     if (it != s->graphs.end()) return it->second;
     cudaGraph_t graph = nullptr;
@@ -819,7 +902,7 @@ cudaGraphExec_t get_graph(FcSession *s, int S, char *err, size_t n) {
         set_error(err, n, "cudaStreamBeginCapture failed");
         return nullptr;
     }
-    cudaError_t rec = record_forward(s, S);
+    cudaError_t rec = record_forward(s, S, drafts);
     cudaError_t end = cudaStreamEndCapture(s->stream, &graph);
     if (rec != cudaSuccess || end != cudaSuccess) {
         if (graph) cudaGraphDestroy(graph);
@@ -853,6 +936,8 @@ int run_pass(FcSession *s, const int *ids, int rows, int k, const FcAcceptConfig
     st->seed = accept ? accept->seed : 0;
     st->counter = accept ? accept->counter : 0;
     for (int i = 0; i < rows; ++i) st->ids[i] = ids[i];
+    // the drafter runs after a verify (k > 0) of a model with an MTP layer
+    const int drafts = (s->m->c.mtp_layers > 0 && k > 0) ? k : 0;
     cudaSetDevice(s->m->device);
     cudaError_t e;
     if (s->profiling) {
@@ -860,7 +945,7 @@ int run_pass(FcSession *s, const int *ids, int rows, int k, const FcAcceptConfig
         // per-phase timing, moonlight_metal.m:1899-1979)
         s->prof_marks.clear();
         cudaEventRecord(s->prof_events[0], s->stream);
-        e = record_forward(s, rows);
+        e = record_forward(s, rows, drafts);
         if (e == cudaSuccess) e = cudaStreamSynchronize(s->stream);
         if (e == cudaSuccess) {
             for (size_t i = 0; i < s->prof_marks.size(); ++i) {
@@ -878,7 +963,7 @@ int run_pass(FcSession *s, const int *ids, int rows, int k, const FcAcceptConfig
             }
         }
     } else {
-        cudaGraphExec_t g = get_graph(s, rows, err, n);
+        cudaGraphExec_t g = get_graph(s, rows, drafts, err, n);
         if (!g) return 0;
         cudaEventRecord(s->ev_begin, s->stream);
         e = cudaGraphLaunch(g, s->stream);
@@ -901,6 +986,7 @@ int run_pass(FcSession *s, const int *ids, int rows, int k, const FcAcceptConfig
     }
     s->stats.command_buffers++;
     s->last_rows = rows;
+    s->last_drafts = drafts;
     return 1;
 }
 
@@ -1155,7 +1241,8 @@ int fc_session_create(FcSession **out, FcModel *m, const FcOptions *options, cha
     s->attn_smem = AttnSmem::total(L + R);
     bool ok = cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking) == cudaSuccess;
     ok = ok && cudaEventCreate(&s->ev_begin) == cudaSuccess && cudaEventCreate(&s->ev_end) == cudaSuccess;
-    ok = ok && salloc(s, s->cache, (size_t)c.layer_count * options->context_size * (L + R));
+    const int NLc = c.layer_count + c.mtp_layers;  // cache layers (target + drafter)
+    ok = ok && salloc(s, s->cache, (size_t)NLc * options->context_size * (L + R));
     ok = ok && salloc(s, s->resid, (size_t)mb * D) && salloc(s, s->xn, (size_t)mb * D);
     ok = ok && salloc(s, s->xq_norm, (size_t)mb * kpad(D) * 2);
     ok = ok && salloc(s, s->q, (size_t)mb * H * QW);
@@ -1171,8 +1258,13 @@ int fc_session_create(FcSession **out, FcModel *m, const FcOptions *options, cha
     ok = ok && salloc(s, s->ctx_xq, (size_t)H * mb * kpad(L) * 2);
     ok = ok && salloc(s, s->o_xq, (size_t)mb * kpad(H * c.value_dim) * 2);
     ok = ok && salloc(s, s->router_logits, (size_t)2 * mb * E);  // scores, then choices
-    ok = ok && salloc(s, s->route_ids, (size_t)c.layer_count * mb * K);
-    ok = ok && salloc(s, s->route_w, (size_t)c.layer_count * mb * K);
+    ok = ok && salloc(s, s->route_ids, (size_t)NLc * mb * K);
+    ok = ok && salloc(s, s->route_w, (size_t)NLc * mb * K);
+    if (c.mtp_layers) {
+        ok = ok && salloc(s, s->d_mtp, 1) && salloc(s, s->mtp_h, (size_t)D);
+        ok = ok && salloc(s, s->mtp_logits, (size_t)V);
+        ok = ok && salloc(s, s->mtp_xq, (size_t)kpad(2 * D) * 2);
+    }
     ok = ok && salloc(s, s->n_active, 1) && salloc(s, s->active, (size_t)s->max_slots + 1);
     s->g_slots = std::min(E, mb * K);
     ok = ok && salloc(s, s->coef, (size_t)(s->g_slots + 1) * 8);
@@ -1203,7 +1295,7 @@ int fc_session_create(FcSession **out, FcModel *m, const FcOptions *options, cha
     ok = ok && cudaMallocHost(&s->h_res, sizeof(Result)) == cudaSuccess;
     if (ok && s->attn_tc)
         ok = make_map_f16(&s->qmap, s->qcat, (uint64_t)(L + R), (uint64_t)q_rows, kTcRows) &&
-             make_map_f16(&s->kvmap, s->cache, (uint64_t)(L + R), (uint64_t)c.layer_count * options->context_size,
+             make_map_f16(&s->kvmap, s->cache, (uint64_t)(L + R), (uint64_t)NLc * options->context_size,
                           kTcKeys);
     if (ok) {
         cudaError_t e1 = cudaFuncSetAttribute(mla_attention_kernel<512, 64>,
@@ -1329,7 +1421,7 @@ int fc_session_set_profiling(FcSession *s, int enabled) {
     if (!s) return 0;
     cudaSetDevice(s->m->device);
     if (enabled && s->prof_events.empty()) {
-        size_t count = (size_t)s->m->c.layer_count * 24 + 32;
+        size_t count = (size_t)(s->m->c.layer_count + 4 * s->m->c.mtp_layers) * 24 + 64;
         s->prof_events.resize(count);
         for (auto &ev : s->prof_events)
             if (cudaEventCreate(&ev) != cudaSuccess) return 0;
@@ -1368,6 +1460,13 @@ int fc_session_copy_row_logits(const FcSession *s, float *logits, int capacity_r
     if (!s || !logits || capacity_rows < s->last_rows || s->last_rows <= 0) return 0;
     return cudaMemcpy(logits, s->logits, (size_t)s->last_rows * s->m->c.vocab_size * 4,
                       cudaMemcpyDeviceToHost) == cudaSuccess;
+}
+
+int fc_session_drafts(const FcSession *s, int *drafts, int capacity) {
+    if (!s || !drafts) return 0;
+    int n = std::min(s->last_drafts, capacity);
+    for (int i = 0; i < n; ++i) drafts[i] = s->h_res->drafts[i];
+    return n;
 }
 
 int fc_session_ep_handle(FcSession *s, void *handle, size_t handle_size, char *error,

@@ -96,6 +96,9 @@ typedef struct {
     int dense_format;            /* FcFormat of attention, dense, shared,
                                     embedding and lm-head matrices       */
     int expert_format;           /* FcFormat of routed experts           */
+    int mtp_layers;              /* 0, or 1: a DeepSeek-V3-style MTP drafter
+                                    layer (enorm / hnorm / eh_proj, one MoE
+                                    layer, shared_head.norm, shared lm-head) */
     uint64_t resident_bytes;     /* filled by fc_model_info              */
 } FcModelConfig;
 
@@ -236,6 +239,15 @@ int fc_session_copy_row_logits(const FcSession *session, float *logits,
  * moonlight_metal.h:69-96). */
 int fc_session_seed_context(FcSession *session, int positions, uint64_t seed,
                             char *error, size_t error_size);
+
+/* Draft proposals of the on-device MTP drafter (models with mtp_layers = 1).
+ * Every fc_session_verify with k > 0 runs the drafter in the same device
+ * graph after acceptance: k sequential greedy steps from the last committed
+ * row's hidden state and the next token (the role of
+ * deepseek_v4_forward_dspark_propose, deepseek_v4_forward.h:1873-1949, for
+ * the 1-layer MTP stand-in).  Copies the k proposals of the last verify into
+ * `drafts` and returns k (0 when none were made). */
+int fc_session_drafts(const FcSession *session, int *drafts, int capacity);
 
 /* Expert parallelism across the GPUs of one box (no reference counterpart:
  * floyd has no communication backend; the contract follows the expert

@@ -45,7 +45,8 @@ enum {
     FC_T_EXP_GATE, FC_T_EXP_UP, FC_T_EXP_DOWN,
     FC_T_SH_GATE, FC_T_SH_UP, FC_T_SH_DOWN,
     FC_T_DENSE_GATE, FC_T_DENSE_UP, FC_T_DENSE_DOWN,
-    FC_T_KV_LATENT, FC_T_KV_ROPE
+    FC_T_KV_LATENT, FC_T_KV_ROPE,
+    FC_T_MTP_ENORM, FC_T_MTP_HNORM, FC_T_MTP_EH_PROJ, FC_T_MTP_HEAD_NORM
 };
 
 /* Streams inside one tensor's counter space. */

@@ -295,6 +295,8 @@ typedef struct {
     Mat sh_gate, sh_up, sh_down;
     Mat d_gate, d_up, d_down;
     int dense;
+    float *enorm, *hnorm, *head_norm;  /* MTP drafter layer only */
+    Mat eh_proj;                       /* MTP: [D][2D] */
 } Layer;
 
 struct OrcModel {
@@ -308,8 +310,11 @@ struct OrcModel {
 struct OrcSession {
     OrcModel *m;
     int ctx, kv_fp16, position;
-    float *latent; /* [layers][ctx][L] */
-    float *rope;   /* [layers][ctx][R] */
+    float *latent; /* [layers (+ MTP)][ctx][L] */
+    float *rope;   /* [layers (+ MTP)][ctx][R] */
+    float *last_x; /* final pre-norm hidden rows of the last forward */
+    int last_rows;
+    int drafts[64], n_drafts;  /* MTP proposals of the last verify */
 };
 
 static float *alloc_f(size_t n) { return (float *)calloc(n ? n : 1, sizeof(float)); }
@@ -393,9 +398,15 @@ OrcModel *orc_model_create(const FcModelConfig *config, uint64_t seed) {
     mat_gen(&m->embed, df, c->vocab_size, D, seed, fc_tensor_id(-1, FC_T_EMBED, 0));
     mat_gen(&m->lm_head, df, c->vocab_size, D, seed, fc_tensor_id(-1, FC_T_LM_HEAD, 0));
     m->final_norm = norm_gen(D, seed, fc_tensor_id(-1, FC_T_FINAL_NORM, 0));
-    m->layers = (Layer *)calloc((size_t)c->layer_count, sizeof(Layer));
-    for (int l = 0; l < c->layer_count; ++l) {
+    m->layers = (Layer *)calloc((size_t)(c->layer_count + c->mtp_layers), sizeof(Layer));
+    for (int l = 0; l < c->layer_count + c->mtp_layers; ++l) {
         Layer *y = &m->layers[l];
+        if (l >= c->layer_count) { /* MTP drafter extras (DeepSeek-V3 MTP module) */
+            y->enorm = norm_gen(D, seed, fc_tensor_id(l, FC_T_MTP_ENORM, 0));
+            y->hnorm = norm_gen(D, seed, fc_tensor_id(l, FC_T_MTP_HNORM, 0));
+            y->head_norm = norm_gen(D, seed, fc_tensor_id(l, FC_T_MTP_HEAD_NORM, 0));
+            mat_gen(&y->eh_proj, df, D, 2 * D, seed, fc_tensor_id(l, FC_T_MTP_EH_PROJ, 0));
+        }
         y->attn_norm = norm_gen(D, seed, fc_tensor_id(l, FC_T_ATTN_NORM, 0));
         y->ffn_norm = norm_gen(D, seed, fc_tensor_id(l, FC_T_FFN_NORM, 0));
         y->kv_a_norm = norm_gen(L, seed, fc_tensor_id(l, FC_T_KV_A_NORM, 0));
@@ -453,8 +464,9 @@ OrcModel *orc_model_create(const FcModelConfig *config, uint64_t seed) {
 void orc_model_free(OrcModel *m) {
     if (!m) return;
     mat_free(&m->embed); mat_free(&m->lm_head); free(m->final_norm);
-    for (int l = 0; l < m->c.layer_count; ++l) {
+    for (int l = 0; l < m->c.layer_count + m->c.mtp_layers; ++l) {
         Layer *y = &m->layers[l];
+        free(y->enorm); free(y->hnorm); free(y->head_norm); mat_free(&y->eh_proj);
         free(y->attn_norm); free(y->ffn_norm); free(y->kv_a_norm); free(y->q_a_norm);
         mat_free(&y->q_proj); mat_free(&y->q_a); mat_free(&y->q_b);
         mat_free(&y->kv_a); mat_free(&y->kv_b); mat_free(&y->o_proj);
@@ -577,7 +589,7 @@ OrcSession *orc_session_create(OrcModel *m, int context_size, int kv_fp16) {
     if (!m || context_size <= 0) return NULL;
     OrcSession *s = (OrcSession *)calloc(1, sizeof(*s));
     s->m = m; s->ctx = context_size; s->kv_fp16 = kv_fp16;
-    size_t rows = (size_t)m->c.layer_count * context_size;
+    size_t rows = (size_t)(m->c.layer_count + m->c.mtp_layers) * context_size;
     s->latent = alloc_f(rows * m->c.kv_lora_rank);
     s->rope = alloc_f(rows * m->c.qk_rope_dim);
     if (!s->latent || !s->rope) { orc_session_free(s); return NULL; }
@@ -586,7 +598,7 @@ OrcSession *orc_session_create(OrcModel *m, int context_size, int kv_fp16) {
 
 void orc_session_free(OrcSession *s) {
     if (!s) return;
-    free(s->latent); free(s->rope); free(s);
+    free(s->latent); free(s->rope); free(s->last_x); free(s);
 }
 
 int orc_session_position(const OrcSession *s) { return s ? s->position : 0; }
@@ -710,15 +722,14 @@ int orc_moe_forward_f32(int hidden, int intermediate, int n_experts, int top_k, 
     return ok;
 }
 
-int orc_session_forward(OrcSession *s, const int *ids, int rows, float *logits,
-                        float *layer_out, int *routes) {
+/* Layers [l0, l1) over the residual rows x at positions pos .. pos+rows-1
+ * (the MTP layer is layer_count; its cache follows the target's). */
+static int run_layers(OrcSession *s, float *x, int rows, int pos, const int *ids, int l0, int l1,
+                      float *layer_out, int *routes) {
     OrcModel *m = s->m;
     const FcModelConfig *c = &m->c;
     int D = c->hidden_size, H = c->head_count, L = c->kv_lora_rank, R = c->qk_rope_dim;
-    int NP = c->qk_nope_dim, VD = c->value_dim, QW = NP + R, V = c->vocab_size;
-    int pos = s->position;
-    if (rows <= 0 || pos + rows > s->ctx) return 0;
-    for (int r = 0; r < rows; ++r) if (ids[r] < 0 || ids[r] >= V) return 0;
+    int NP = c->qk_nope_dim, VD = c->value_dim, QW = NP + R;
 
     int maxI = c->moe_intermediate_size * (c->shared_expert_count > 1 ? c->shared_expert_count : 1);
     if (c->dense_intermediate_size > maxI) maxI = c->dense_intermediate_size;
@@ -727,7 +738,6 @@ int orc_session_forward(OrcSession *s, const int *ids, int rows, float *logits,
     if (H * QW > maxO) maxO = H * QW;
     if (H * (NP + VD) > maxO) maxO = H * (NP + VD);
     if (c->q_lora_rank > maxO) maxO = c->q_lora_rank;
-    float *x = alloc_f((size_t)rows * D);
     float *xn = alloc_f((size_t)rows * D);
     float *q = alloc_f((size_t)rows * H * QW);
     float *qa = alloc_f((size_t)rows * (c->q_lora_rank > 0 ? c->q_lora_rank : 1));
@@ -738,18 +748,7 @@ int orc_session_forward(OrcSession *s, const int *ids, int rows, float *logits,
     float *ao = alloc_f((size_t)rows * D);
     float scale = 1.0f / sqrtf((float)(NP + R));
 
-    /* embedding: dequantized row (moonlight_kernels.metal:10-21) */
-    for (int r = 0; r < rows; ++r) {
-        const Mat *e = &m->embed;
-        for (int k = 0; k < D; ++k) {
-            float v = e->fmt == FC_FMT_F32 ? e->f32[(int64_t)ids[r] * D + k]
-                : value_of(e->fmt, e->values[(int64_t)ids[r] * D + k]) *
-                  e->scales[(int64_t)ids[r] * (D / 32) + k / 32];
-            x[(int64_t)r * D + k] = v;
-        }
-    }
-
-    for (int l = 0; l < c->layer_count; ++l) {
+    for (int l = l0; l < l1; ++l) {
         Layer *ly = &m->layers[l];
         float *lat = s->latent + (size_t)l * s->ctx * L;
         float *rop = s->rope + (size_t)l * s->ctx * R;
@@ -855,16 +854,94 @@ int orc_session_forward(OrcSession *s, const int *ids, int rows, float *logits,
         }
         if (layer_out) memcpy(layer_out + (size_t)l * rows * D, x, (size_t)rows * D * sizeof(float));
     }
+    free(xn); free(q); free(qa); free(ckv); free(attn); free(tmp); free(y); free(ao);
+    return 1;
+fail:
+    free(xn); free(q); free(qa); free(ckv); free(attn); free(tmp); free(y); free(ao);
+    return 0;
+}
+
+static void embed_rows(const OrcModel *m, const int *ids, int rows, float *x) {
+    const FcModelConfig *c = &m->c;
+    int D = c->hidden_size;
+    /* embedding: dequantized row (moonlight_kernels.metal:10-21) */
+    for (int r = 0; r < rows; ++r) {
+        const Mat *e = &m->embed;
+        for (int k = 0; k < D; ++k) {
+            float v = e->fmt == FC_FMT_F32 ? e->f32[(int64_t)ids[r] * D + k]
+                : value_of(e->fmt, e->values[(int64_t)ids[r] * D + k]) *
+                  e->scales[(int64_t)ids[r] * (D / 32) + k / 32];
+            x[(int64_t)r * D + k] = v;
+        }
+    }
+
+}
+
+int orc_session_forward(OrcSession *s, const int *ids, int rows, float *logits,
+                        float *layer_out, int *routes) {
+    OrcModel *m = s->m;
+    const FcModelConfig *c = &m->c;
+    int D = c->hidden_size, V = c->vocab_size;
+    int pos = s->position;
+    if (rows <= 0 || pos + rows > s->ctx) return 0;
+    for (int r = 0; r < rows; ++r) if (ids[r] < 0 || ids[r] >= V) return 0;
+    float *x = alloc_f((size_t)rows * D);
+    float *xn = alloc_f((size_t)rows * D);
+    embed_rows(m, ids, rows, x);
+    if (!run_layers(s, x, rows, pos, ids, 0, c->layer_count, layer_out, routes)) {
+        free(x); free(xn);
+        return 0;
+    }
+    free(s->last_x);
+    s->last_x = alloc_f((size_t)rows * D);
+    memcpy(s->last_x, x, (size_t)rows * D * sizeof(float));
+    s->last_rows = rows;
     if (logits) {
         orc_rmsnorm(x, m->final_norm, rows, D, c->rms_norm_epsilon, xn);
         mat_apply(&m->lm_head, xn, rows, logits);
     }
     s->position = pos + rows;
-    free(x); free(xn); free(q); free(qa); free(ckv); free(attn); free(tmp); free(y); free(ao);
+    free(x); free(xn);
     return 1;
-fail:
-    free(x); free(xn); free(q); free(qa); free(ckv); free(attn); free(tmp); free(y); free(ao);
-    return 0;
+}
+
+/* The MTP drafter (DeepSeek-V3 MTP module; the role of
+ * deepseek_v4_forward_dspark_propose, deepseek_v4_forward.h:1873-1949):
+ * step i at position start + i takes token t_i (t_0 = the target's next
+ * token, then the previous proposal) and hidden h (h_0 = the target's last
+ * committed row): x = eh_proj([enorm(embed(t_i)) | hnorm(h)]), the MTP
+ * layer, h = x, proposal = argmax(lm_head(shared_head.norm(x))). */
+static int mtp_drafts(OrcSession *s, const float *h0, int start, int first_token, int k, int *out) {
+    OrcModel *m = s->m;
+    const FcModelConfig *c = &m->c;
+    int D = c->hidden_size, V = c->vocab_size, lm = c->layer_count;
+    const Layer *y = &m->layers[lm];
+    float *h = alloc_f((size_t)D), *e = alloc_f((size_t)D), *cat = alloc_f((size_t)2 * D);
+    float *x = alloc_f((size_t)D), *xn = alloc_f((size_t)D), *lg = alloc_f((size_t)V);
+    memcpy(h, h0, (size_t)D * sizeof(float));
+    int token = first_token, ok = 1;
+    for (int i = 0; i < k && ok; ++i) {
+        if (start + i >= s->ctx) { ok = 0; break; }
+        embed_rows(m, &token, 1, e);
+        orc_rmsnorm(e, y->enorm, 1, D, c->rms_norm_epsilon, cat);
+        orc_rmsnorm(h, y->hnorm, 1, D, c->rms_norm_epsilon, cat + D);
+        mat_apply(&y->eh_proj, cat, 1, x);
+        ok = run_layers(s, x, 1, start + i, &token, lm, lm + 1, NULL, NULL);
+        memcpy(h, x, (size_t)D * sizeof(float));
+        orc_rmsnorm(x, y->head_norm, 1, D, c->rms_norm_epsilon, xn);
+        mat_apply(&m->lm_head, xn, 1, lg);
+        token = orc_argmax(lg, V);
+        out[i] = token;
+    }
+    free(h); free(e); free(cat); free(x); free(xn); free(lg);
+    return ok;
+}
+
+int orc_session_drafts(const OrcSession *s, int *out, int capacity) {
+    if (!s || !out) return 0;
+    int n = s->n_drafts < capacity ? s->n_drafts : capacity;
+    memcpy(out, s->drafts, (size_t)n * sizeof(int));
+    return n;
 }
 
 int orc_session_copy_kv(const OrcSession *s, int layer, float *latent, float *rope,
@@ -902,6 +979,13 @@ int orc_session_verify(OrcSession *s, const int *ids, int k, const FcAcceptConfi
     *n_emitted = commit;
     *next_token = next;
     s->position = start + commit; /* rollback: the MLA cache is append-only */
+    s->n_drafts = 0;
+    if (s->m->c.mtp_layers > 0 && k > 0) {
+        int D = s->m->c.hidden_size;
+        if (mtp_drafts(s, s->last_x + (size_t)(commit - 1) * D, start + commit, next < 0 ? 0 : next, k,
+                       s->drafts))
+            s->n_drafts = k;
+    }
     if (!row_logits) free(logits);
     return 1;
 }

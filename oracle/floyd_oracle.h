@@ -127,6 +127,9 @@ int orc_session_copy_kv(const OrcSession *session, int layer, float *latent,
 
 /* Full verify (forward + acceptance + rollback), the CPU counterpart of
  * fc_session_verify. */
+/* Proposals of the MTP drafter made by the last orc_session_verify (models
+ * with mtp_layers = 1); returns their count. */
+int orc_session_drafts(const OrcSession *s, int *out, int capacity);
 int orc_session_verify(OrcSession *session, const int *ids, int k,
                        const FcAcceptConfig *accept, int *emitted,
                        int *n_emitted, int *next_token, float *row_logits,

@@ -59,6 +59,7 @@ def lib():
             "orc_session_forward": (I, [P, IP, I, FP, FP, IP]),
             "orc_session_copy_kv": (I, [P, I, FP, FP, I]),
             "orc_session_verify": (I, [P, IP, I, ctypes.POINTER(FcAcceptConfig), IP, IP, IP, FP, IP]),
+            "orc_session_drafts": (I, [P, IP, I]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -175,6 +176,12 @@ class OracleSession:
         if not ok:
             raise RuntimeError("oracle forward failed")
         return logits, layers, routes
+
+    def drafts(self):
+        """MTP drafter proposals of the last verify."""
+        out = np.zeros(64, dtype=np.int32)
+        n = lib().orc_session_drafts(self.handle, _ip(out), 64)
+        return out[:n].tolist()
 
     def verify(self, ids, mode=0, temperature=1.0, seed=0, counter=0):
         from floyd_b200._lib import FcAcceptConfig

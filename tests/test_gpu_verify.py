@@ -336,3 +336,24 @@ def test_spec_runtime_shim(fc):
     assert rt.last_count == 5 and rt.last_start_position == 0
     lib.fc_runtime_reset(ctypes.byref(rt))
     lib.fc_runtime_free(ctypes.byref(rt))
+
+
+@pytest.mark.parametrize("seed", [11, 12])
+def test_mtp_drafts_match_oracle(seed):
+    """The on-device MTP drafter (run in the verify graph after acceptance)
+    proposes the same k tokens as the oracle's restatement."""
+    cfg, name = C4_SMALL, "c4s"
+    assert cfg["mtp_layers"] == 1
+    gs, os_ = sessions(cfg, name)
+    rng = np.random.default_rng(seed)
+    ids = rng.integers(0, cfg["vocab_size"], size=4).tolist()
+    em, nxt, _ = gs.verify(ids)
+    oem, onxt, _, _ = os_.verify(ids)
+    assert em == oem and nxt == onxt
+    assert gs.drafts() == os_.drafts()
+    assert len(gs.drafts()) == 3
+    # the drafter leaves the target's state alone: a decode afterwards still
+    # matches the oracle
+    g = gs.decode(nxt)
+    o, _, _ = os_.forward([nxt])
+    check_rows(g[None, :], o)
