@@ -164,6 +164,10 @@ class Session:
         err = _err()
         self._check(self._lib.fc_session_rollback(self.handle, int(position), err, len(err)), err)
 
+    def last_kernel_count(self):
+        """Kernels launched by the last forward pass (graph kernel nodes)."""
+        return int(self._lib.fc_session_last_kernel_count(self.handle))
+
     def drafts(self):
         """The on-device drafter's proposals from the last verify."""
         out = np.zeros(8, dtype=np.int32)

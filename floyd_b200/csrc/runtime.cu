@@ -154,6 +154,8 @@ struct FcSession {
     Staging *d_stage = nullptr, *h_stage = nullptr;
     Result *d_res = nullptr, *h_res = nullptr;
     std::map<int, cudaGraphExec_t> graphs;
+    std::map<int, int> graph_kernels;  // kernel nodes of each captured graph
+    int last_kernels = 0;              // kernels launched by the last pass
     size_t attn_smem = 0;
     cudaEvent_t ev_begin = nullptr, ev_end = nullptr;   // device time of each pass
     // per-kernel profiling (eager passes with an event after every launch)
@@ -910,6 +912,17 @@ cudaGraphExec_t get_graph(FcSession *s, int S, int drafts, char *err, size_t n) 
                   cudaGetErrorString(rec != cudaSuccess ? rec : end));
         return nullptr;
     }
+    size_t nodes = 0;
+    int kernels = 0;
+    if (cudaGraphGetNodes(graph, nullptr, &nodes) == cudaSuccess && nodes) {
+        std::vector<cudaGraphNode_t> list(nodes);
+        if (cudaGraphGetNodes(graph, list.data(), &nodes) == cudaSuccess)
+            for (auto nd : list) {
+                cudaGraphNodeType t;
+                if (cudaGraphNodeGetType(nd, &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) ++kernels;
+            }
+    }
+    s->graph_kernels[key] = kernels;
     cudaGraphExec_t exec = nullptr;
     cudaError_t inst = cudaGraphInstantiate(&exec, graph, 0);
     cudaGraphDestroy(graph);
@@ -965,6 +978,7 @@ int run_pass(FcSession *s, const int *ids, int rows, int k, const FcAcceptConfig
     } else {
         cudaGraphExec_t g = get_graph(s, rows, drafts, err, n);
         if (!g) return 0;
+        s->last_kernels = s->graph_kernels[(rows * 2 + (s->trace ? 1 : 0)) * 16 + drafts];
         cudaEventRecord(s->ev_begin, s->stream);
         e = cudaGraphLaunch(g, s->stream);
         cudaEventRecord(s->ev_end, s->stream);
@@ -1461,6 +1475,8 @@ int fc_session_copy_row_logits(const FcSession *s, float *logits, int capacity_r
     return cudaMemcpy(logits, s->logits, (size_t)s->last_rows * s->m->c.vocab_size * 4,
                       cudaMemcpyDeviceToHost) == cudaSuccess;
 }
+
+int fc_session_last_kernel_count(const FcSession *s) { return s ? s->last_kernels : 0; }
 
 int fc_session_drafts(const FcSession *s, int *drafts, int capacity) {
     if (!s || !drafts) return 0;

@@ -249,6 +249,10 @@ int fc_session_seed_context(FcSession *session, int positions, uint64_t seed,
  * `drafts` and returns k (0 when none were made). */
 int fc_session_drafts(const FcSession *session, int *drafts, int capacity);
 
+/* Kernels launched by the last forward pass (kernel nodes of its CUDA
+ * graph; 0 for eager profiled passes).  No reference counterpart. */
+int fc_session_last_kernel_count(const FcSession *session);
+
 /* Expert parallelism across the GPUs of one box (no reference counterpart:
  * floyd has no communication backend; the contract follows the expert
  * partitioning of moe_exec.h:97-110 with one exchange per MoE layer).
