@@ -19,13 +19,34 @@ from ._lib import (ACCEPT_GREEDY, ACCEPT_SAMPLE, FMT_F32, FMT_MXFP4, FMT_Q4, FMT
                    FcModelConfig, FcOptions)
 from .configs import CONFIGS, model_fields, scaled, step_bytes
 
-__all__ = ["Model", "Session", "FloydError", "CONFIGS", "model_fields", "scaled", "step_bytes",
+__all__ = ["Model", "Session", "FloydError", "CONFIGS", "blocks_to_logical", "BLOCKS_Q8_0", "BLOCKS_MXFP4", "model_fields", "scaled", "step_bytes",
            "FMT_F32", "FMT_Q8", "FMT_Q4", "FMT_MXFP4", "ACCEPT_GREEDY", "ACCEPT_SAMPLE",
            "SCORE_SOFTMAX", "SCORE_SIGMOID", "SCORE_SQRT_SOFTPLUS", "lib"]
 
 
 class FloydError(RuntimeError):
     pass
+
+
+BLOCKS_Q8_0, BLOCKS_MXFP4 = 8, 39  # FcBlockType (ggml type ids)
+
+
+def blocks_to_logical(block_type, blocks, rows, cols):
+    """Host conversion of GGUF blocks to (values, group scales) in the logical
+    layout of Model.set_tensor (fc_blocks_to_logical; no GPU needed)."""
+    blocks = np.ascontiguousarray(blocks, dtype=np.uint8)
+    if block_type == BLOCKS_Q8_0:
+        values = np.zeros((rows, cols), dtype=np.int8)
+        scales = np.zeros((rows, cols // 32), dtype=np.uint16)
+    else:
+        values = np.zeros((rows, cols // 2), dtype=np.uint8)
+        scales = np.zeros((rows, cols // 32), dtype=np.uint8)
+    err = _err()
+    if not lib().fc_blocks_to_logical(int(block_type), blocks.ctypes.data_as(ctypes.c_void_p), blocks.nbytes,
+                                      rows, cols, values.ctypes.data_as(ctypes.c_void_p),
+                                      scales.ctypes.data_as(ctypes.c_void_p), err, len(err)):
+        raise FloydError(err.value.decode())
+    return values, scales
 
 
 def lib():
@@ -77,6 +98,25 @@ class Model:
         err = _err()
         if not self._lib.fc_model_set_tensor(self.handle, name.encode(), data.ctypes.data_as(ctypes.c_void_p),
                                              data.nbytes, err, len(err)):
+            raise FloydError(err.value.decode())
+
+    def set_tensor_blocks(self, name, block_type, blocks):
+        """One q8 / MXFP4 matrix from GGUF Q8_0 / MXFP4 blocks (exact)."""
+        blocks = np.ascontiguousarray(blocks, dtype=np.uint8)
+        err = _err()
+        if not self._lib.fc_model_set_tensor_blocks(self.handle, name.encode(), int(block_type),
+                                                    blocks.ctypes.data_as(ctypes.c_void_p), blocks.nbytes,
+                                                    err, len(err)):
+            raise FloydError(err.value.decode())
+
+    def set_tensor_rowscale(self, name, values, row_scales):
+        """One int8 / int4 matrix of the Moonlight container (per-row fp32 scales)."""
+        values = np.ascontiguousarray(values, dtype=np.uint8)
+        row_scales = np.ascontiguousarray(row_scales, dtype=np.float32)
+        err = _err()
+        if not self._lib.fc_model_set_tensor_rowscale(
+                self.handle, name.encode(), values.ctypes.data_as(ctypes.c_void_p), values.nbytes,
+                row_scales.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), len(row_scales), err, len(err)):
             raise FloydError(err.value.decode())
 
     def get_tensor(self, name, nbytes, dtype=np.uint8):

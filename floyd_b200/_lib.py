@@ -104,6 +104,10 @@ SIGNATURES = {
     "fc_session_seed_context": (_I, [_P, _I, ctypes.c_uint64, _C, _S]),
     "fc_session_ep_handle": (_I, [_P, ctypes.c_void_p, _S, _C, _S]),
     "fc_session_drafts": (_I, [_P, _IP, _I]),
+    "fc_blocks_to_logical": (_I, [_I, ctypes.c_void_p, _S, _I, _I, ctypes.c_void_p, ctypes.c_void_p, _C, _S]),
+    "fc_model_set_tensor_blocks": (_I, [_P, ctypes.c_char_p, _I, ctypes.c_void_p, _S, _C, _S]),
+    "fc_model_set_tensor_rowscale": (_I, [_P, ctypes.c_char_p, ctypes.c_void_p, _S,
+                                          ctypes.POINTER(ctypes.c_float), _I, _C, _S]),
     "fc_session_last_kernel_count": (_I, [_P]),
     "fc_session_ep_connect": (_I, [_P, ctypes.c_char_p, _I, _C, _S]),
     "fc_session_set_profiling": (_I, [_P, _I]),

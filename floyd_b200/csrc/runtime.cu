@@ -1184,6 +1184,90 @@ int fc_model_set_tensor(FcModel *m, const char *name, const void *data, size_t b
     return tensor_io(m, name, const_cast<void *>(data), bytes, true, error, error_size);
 }
 
+int fc_blocks_to_logical(int type, const void *blocks, size_t bytes, int rows, int cols, void *values,
+                         void *scales, char *error, size_t error_size) {
+    if (!blocks || !values || !scales || rows <= 0 || cols <= 0 || cols % 32)
+        return set_error(error, error_size, "blocks need rows > 0 and cols a multiple of 32");
+    const size_t nb = (size_t)rows * (cols / 32);
+    const uint8_t *b = static_cast<const uint8_t *>(blocks);
+    if (type == FC_BLOCKS_Q8_0) {
+        if (bytes != nb * 34) return set_error(error, error_size, "Q8_0 data must be %zu bytes", nb * 34);
+        int8_t *v = static_cast<int8_t *>(values);
+        uint16_t *sc = static_cast<uint16_t *>(scales);
+        for (size_t i = 0; i < nb; ++i, b += 34) {
+            memcpy(&sc[i], b, 2);
+            memcpy(v + i * 32, b + 2, 32);
+        }
+        return 1;
+    }
+    if (type == FC_BLOCKS_MXFP4) {
+        if (bytes != nb * 17) return set_error(error, error_size, "MXFP4 data must be %zu bytes", nb * 17);
+        uint8_t *v = static_cast<uint8_t *>(values);
+        uint8_t *sc = static_cast<uint8_t *>(scales);
+        for (size_t i = 0; i < nb; ++i, b += 17) {
+            sc[i] = b[0];
+            uint8_t code[32];
+            for (int j = 0; j < 16; ++j) {
+                code[j] = b[1 + j] & 15;
+                code[j + 16] = b[1 + j] >> 4;
+            }
+            for (int m = 0; m < 16; ++m) v[i * 16 + m] = (uint8_t)(code[2 * m] | (code[2 * m + 1] << 4));
+        }
+        return 1;
+    }
+    return set_error(error, error_size, "unknown block type %d", type);
+}
+
+namespace {
+const DevMat *find_mat(const FcModel *m, const std::string &name, int *member) {
+    auto it = m->names.find(name);
+    if (it == m->names.end() || !it->second.mat) return nullptr;
+    *member = it->second.member;
+    return it->second.mat;
+}
+}  // namespace
+
+int fc_model_set_tensor_blocks(FcModel *m, const char *name, int type, const void *blocks, size_t bytes,
+                               char *error, size_t error_size) {
+    if (!m || !name) return set_error(error, error_size, "model and name are required");
+    int member = 0;
+    const DevMat *mm = find_mat(m, name, &member);
+    if (!mm) return set_error(error, error_size, "unknown matrix %s", name);
+    const int want = type == FC_BLOCKS_Q8_0 ? FC_FMT_Q8 : type == FC_BLOCKS_MXFP4 ? FC_FMT_MXFP4 : -1;
+    if (mm->fmt != want)
+        return set_error(error, error_size, "%s is stored as format %d; block type %d does not match", name,
+                         mm->fmt, type);
+    const size_t vbytes = (size_t)mm->O * mm->K / (want == FC_FMT_Q8 ? 1 : 2);
+    const size_t sbytes = (size_t)mm->O * (mm->K / 32) * (want == FC_FMT_Q8 ? 2 : 1);
+    std::vector<uint8_t> v(vbytes), sc(sbytes);
+    if (!fc_blocks_to_logical(type, blocks, bytes, mm->O, mm->K, v.data(), sc.data(), error, error_size))
+        return 0;
+    return fc_model_set_tensor(m, name, v.data(), vbytes, error, error_size) &&
+           fc_model_set_tensor(m, (std::string(name) + ".gs").c_str(), sc.data(), sbytes, error, error_size);
+}
+
+int fc_model_set_tensor_rowscale(FcModel *m, const char *name, const void *values, size_t value_bytes,
+                                 const float *row_scales, int rows, char *error, size_t error_size) {
+    if (!m || !name || !values || !row_scales) return set_error(error, error_size, "arguments are required");
+    int member = 0;
+    const DevMat *mm = find_mat(m, name, &member);
+    if (!mm) return set_error(error, error_size, "unknown matrix %s", name);
+    if (mm->fmt != FC_FMT_Q8 && mm->fmt != FC_FMT_Q4)
+        return set_error(error, error_size, "%s is not an int8 / int4 matrix", name);
+    if (rows != mm->O) return set_error(error, error_size, "%s has %d rows, not %d", name, mm->O, rows);
+    const int G = mm->K / 32;
+    std::vector<uint16_t> sc((size_t)mm->O * G);
+    for (int r = 0; r < mm->O; ++r) {
+        __half h = __float2half_rn(row_scales[r]);
+        uint16_t bits;
+        memcpy(&bits, &h, 2);
+        for (int g = 0; g < G; ++g) sc[(size_t)r * G + g] = bits;
+    }
+    return fc_model_set_tensor(m, name, values, value_bytes, error, error_size) &&
+           fc_model_set_tensor(m, (std::string(name) + ".gs").c_str(), sc.data(), sc.size() * 2, error,
+                               error_size);
+}
+
 int fc_model_get_tensor(const FcModel *m, const char *name, void *data, size_t bytes, char *error,
                         size_t error_size) {
     return tensor_io(m, name, data, bytes, false, error, error_size);

@@ -171,6 +171,38 @@ int fc_model_fill_synthetic(FcModel *model, uint64_t seed,
 int fc_model_set_tensor(FcModel *model, const char *name, const void *data,
                         size_t bytes, char *error, size_t error_size);
 
+/* Weight ingest from checkpoint block formats (no counterpart in the Metal
+ * session: floyd's host code reads these formats itself).
+ *
+ * GGUF blocks (ggml type ids): Q8_0 = {fp16 d; int8 q[32]} per 32 values,
+ * MXFP4 = {ue8m0 e; uint8 q[16]} per 32 values with element j in the low
+ * nibble and element j + 16 in the high nibble of q[j]
+ * (patches/ds4/deepseek-v4-mxfp4-runtime.patch, block_mxfp4; the reader in
+ * deepseek-v4-dspark-metal.patch:4430-4460).  Both map exactly onto the
+ * q8 / MXFP4 group-32 formats. */
+typedef enum { FC_BLOCKS_Q8_0 = 8, FC_BLOCKS_MXFP4 = 39 } FcBlockType;
+
+/* Host-only conversion of rows x cols values stored as blocks (cols / 32
+ * blocks per row) into the logical layout of fc_model_set_tensor: values
+ * (int8 [rows][cols], or e2m1 codes packed two per byte with the even element
+ * low) and group scales (fp16 bits, or ue8m0 bytes) [rows][cols / 32]. */
+int fc_blocks_to_logical(int block_type, const void *blocks, size_t bytes, int rows, int cols,
+                         void *values, void *scales, char *error, size_t error_size);
+
+/* Uploads one q8 (Q8_0 blocks) or MXFP4 (MXFP4 blocks) matrix; exact. */
+int fc_model_set_tensor_blocks(FcModel *model, const char *name, int block_type,
+                               const void *blocks, size_t bytes, char *error,
+                               size_t error_size);
+
+/* Uploads one matrix of floyd's Moonlight container
+ * (tools/convert_moonlight.py:50-75): U8 values (int8, or int4 stored as
+ * q + 8 with the even element in the low nibble) and one fp32 scale per row
+ * (`name` + ".qs").  Every 32-column group takes the row's scale rounded to
+ * fp16 (the group-32 fp16 format of this backend; the only change). */
+int fc_model_set_tensor_rowscale(FcModel *model, const char *name, const void *values,
+                                 size_t value_bytes, const float *row_scales, int rows,
+                                 char *error, size_t error_size);
+
 /* Downloads a tensor in the same logical layout fc_model_set_tensor takes. */
 int fc_model_get_tensor(const FcModel *model, const char *name, void *data,
                         size_t bytes, char *error, size_t error_size);
