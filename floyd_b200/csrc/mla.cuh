@@ -139,16 +139,16 @@ __device__ __forceinline__ void rope_pair(float first, float second, int p, int 
 
 // grid (S, 1 + ceil(H * R/2 / blockDim)): block y == 0 appends the KV row,
 // blocks y >= 1 rotate a slice of the heads' query rope pairs.
-__global__ void mla_prep_kernel(const float *ckv, const float *q, const float *norm_w, int L,
-                                int R, int H, int nope, float eps, float theta,
-                                const int *d_pos, __half *cache, __half *qcat) {
+__device__ __forceinline__ void mla_prep_block(int bx, int by, const float *ckv, const float *q,
+                                               const float *norm_w, int L, int R, int H, int nope, float eps,
+                                               float theta, const int *d_pos, __half *cache, __half *qcat) {
     pdl_wait();
     pdl_release();
     __shared__ float scratch[32];
-    const int s = blockIdx.x;
+    const int s = bx;
     const int position = *d_pos + s;
     const int half = R / 2;
-    if (blockIdx.y == 0) {
+    if (by == 0) {
         const float *src = ckv + (size_t)s * (L + R);
         float ss = 0.0f;
         for (int i = threadIdx.x; i < L; i += blockDim.x) ss += src[i] * src[i];
@@ -166,7 +166,7 @@ __global__ void mla_prep_kernel(const float *ckv, const float *q, const float *n
         return;
     }
     const int qw = nope + R;
-    const int t = (blockIdx.y - 1) * blockDim.x + threadIdx.x;
+    const int t = (by - 1) * blockDim.x + threadIdx.x;
     if (t >= H * half) return;
     const int h = t / half, p = t % half;
     const float *qh = q + ((size_t)s * H + h) * qw + nope;
@@ -188,14 +188,13 @@ __global__ void mla_prep_kernel(const float *ckv, const float *q, const float *n
 constexpr int kAbsorbCols = 64;
 constexpr int kAbsorbMaxNope = 128;
 
-__global__ void __launch_bounds__(256) mla_absorb_kernel(int fmt, const uint8_t *w,
-                                                         int kp, const float *q, int S, int H,
-                                                         int nope, int vdim, int R, int L,
-                                                         __half *qcat) {
+__device__ __forceinline__ void mla_absorb_block(int bx, int by, int fmt, const uint8_t *w, int kp,
+                                                 const float *q, int S, int H, int nope, int vdim, int R,
+                                                 int L, __half *qcat) {
     __shared__ float wsm[kAbsorbMaxNope][kAbsorbCols + 1];
     __shared__ float qs[8][kAbsorbMaxNope];
     __shared__ __align__(16) uint8_t raw[kAbsorbMaxNope / kTileRows][1152];
-    const int h = blockIdx.x, l0 = blockIdx.y * kAbsorbCols;
+    const int h = bx, l0 = by * kAbsorbCols;
     const int qw = nope + R;
     const int cc = chunk_cols(fmt), blk = block_bytes(fmt);
     const int c = l0 / cc, col0 = l0 % cc;
@@ -247,6 +246,22 @@ __global__ void __launch_bounds__(256) mla_absorb_kernel(int fmt, const uint8_t 
         float acc = 0.0f;
         for (int n = 0; n < nope; ++n) acc = __fadd_rn(acc, __fmul_rn(qs[s][n], wsm[n][col]));
         qcat[((size_t)s * H + h) * (L + R) + l0 + col] = __float2half_rn(acc);
+    }
+}
+
+// KV append + query rope (blocks 0 .. S * prep_y - 1) and query absorption
+// (the remaining H * L / 64 blocks) in one launch: both read only the q_b and
+// kv_a outputs, so neither waits for the other.
+__global__ void __launch_bounds__(256)
+mla_prep_absorb_kernel(const float *ckv, const float *q, const float *norm_w, int L, int R, int H, int nope,
+                       float eps, float theta, const int *d_pos, __half *cache, __half *qcat, int S, int prep_y,
+                       int fmt, const uint8_t *w, int kp, int vdim) {
+    const int b = blockIdx.x, n_prep = S * prep_y;
+    if (b < n_prep) {
+        mla_prep_block(b / prep_y, b % prep_y, ckv, q, norm_w, L, R, H, nope, eps, theta, d_pos, cache, qcat);
+    } else {
+        const int a = b - n_prep, cols = L / kAbsorbCols;
+        mla_absorb_block(a / cols, a % cols, fmt, w, kp, q, S, H, nope, vdim, R, L, qcat);
     }
 }
 

@@ -592,14 +592,14 @@ cudaError_t record_layer(FcSession *s, int S, int l, const int *d_pos, const int
         FC_TRY(gemv1(df, g, S, 0.0f, s->d_err, m->sms, st));
         mark(s, "gemv_q_b");
     }
-    FC_TRY(launch_pdl(mla_prep_kernel, dim3(dim3(S, 1 + (H * (R / 2) + 255) / 256)), dim3(256), 0, st, s->ckv, s->q, y.kv_a_norm.p, L, R, H, NP,
-                                       c.rms_norm_epsilon, c.rope_theta, d_pos, cache, s->qcat));
-    mark(s, "mla_prep");
     {
-        dim3 grid(H, L / kAbsorbCols);
-        FC_TRY(launch_pdl(mla_absorb_kernel, dim3(grid), dim3(256), 0, st, df, y.kv_b.w, y.kv_b.kp, s->q, S, H,
-                                                NP, VD, R, L, s->qcat));
-        mark(s, "mla_absorb");
+        const int prep_y = 1 + (H * (R / 2) + 255) / 256;
+        const int blocks = S * prep_y + H * (L / kAbsorbCols);
+        FC_TRY(launch_pdl(mla_prep_absorb_kernel, dim3(blocks), dim3(256), 0, st, (const float *)s->ckv,
+                          (const float *)s->q, (const float *)y.kv_a_norm.p, L, R, H, NP, c.rms_norm_epsilon,
+                          c.rope_theta, d_pos, cache, s->qcat, S, prep_y, df, (const uint8_t *)y.kv_b.w,
+                          y.kv_b.kp, VD));
+        mark(s, "mla_prep_absorb");
     }
     if (s->attn_tc) {
         dim3 grid((S * H + kTcRows - 1) / kTcRows, 2, s->splits);
@@ -876,8 +876,8 @@ cudaError_t record_mtp_step(FcSession *s, int i) {
 // carveout, so consecutive kernels never make an SM reconfigure its L1 split.
 cudaError_t prefer_shared_carveout() {
     const void *kernels[] = {
-        (const void *)embed_kernel, (const void *)rmsnorm_kernel, (const void *)mla_prep_kernel,
-        (const void *)mla_absorb_kernel, (const void *)mla_attention_kernel<512, 64>,
+        (const void *)embed_kernel, (const void *)rmsnorm_kernel, (const void *)mla_prep_absorb_kernel,
+        (const void *)mla_attention_kernel<512, 64>,
         (const void *)mla_attention_kernel<256, 64>, (const void *)mla_combine_kernel,
         (const void *)mla_attention_tc_kernel<512>, (const void *)mla_attention_tc_kernel<256>,
         (const void *)router_kernel,
