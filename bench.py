@@ -48,6 +48,10 @@ def parse():
     ap.add_argument("--sample-steps", type=int, default=30,
                     help="verify steps with rejection-sampling acceptance (T=0.7, seed 1)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--prefill-tokens", type=int, default=2048,
+                    help="configs[2] leg: prompt length of the prefill (0 = skip the leg)")
+    ap.add_argument("--prefill-decode", type=int, default=512, help="configs[2] leg: greedy decodes after it")
+    ap.add_argument("--prefill-reps", type=int, default=5, help="configs[2] leg: timed prefills")
     ap.add_argument("--layers", type=int, default=None,
                     help="override layer_count (small profiling cases only)")
     ap.add_argument("--out", default=None, help="also write the JSON line here")
@@ -297,6 +301,108 @@ def run_reference(args, d):
             "wall_s": wall}
 
 
+def measured_tflops():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        d = json.load(open(path))
+        if d.get("bf16_tflops"):
+            return d["bf16_tflops"], "measured"
+    return 1590.0, "fallback"
+
+
+def prefill_kernel_flops(cfg, name, T, start):
+    """Algorithmic FLOPs of one launch of a named prefill kernel (one layer)."""
+    D, H, L, R = cfg["hidden_size"], cfg["head_count"], cfg["kv_lora_rank"], cfg["qk_rope_dim"]
+    NP, VD, I, K = cfg["qk_nope_dim"], cfg["value_dim"], cfg["moe_intermediate_size"], cfg["experts_per_token"]
+    if name == "pf_gemm_moe_gate_up":
+        return 2.0 * T * K * 2 * D * I
+    if name == "pf_gemm_moe_down":
+        return 2.0 * T * K * D * I
+    if name == "pf_gemm_shared":
+        return 2.0 * T * 3 * D * I * cfg["shared_expert_count"]
+    if name == "pf_gemm_q" and not cfg["q_lora_rank"]:
+        return 2.0 * T * D * H * (NP + R)
+    if name == "pf_gemm_o_proj":
+        return 2.0 * T * H * VD * D
+    if name == "pf_gemm_kv_b":
+        return 2.0 * (start + T) * L * H * (NP + VD)
+    if name == "pf_attention":
+        return 2.0 * H * (NP + R + VD) * (T * start + T * (T + 1) / 2)
+    return None
+
+
+def prefill_leg(args, d):
+    """the Moonlight-shaped q4 model, a prompt of
+    --prefill-tokens random ids through the tcgen05 prefill path (every
+    linear layer a tensor-core GEMM), then --prefill-decode greedy decodes."""
+    import floyd_b200
+    from floyd_b200.configs import CONFIGS, prefill_flops
+    name = "c3_moonlight_q4"
+    cfg = dict(CONFIGS[name])
+    T, ndec = args.prefill_tokens, args.prefill_decode
+    model = floyd_b200.Model(cfg, device=d.local, seed=0)
+    sess = floyd_b200.Session(model, T + ndec + 8, T)
+    ids = np.random.default_rng(0).integers(0, cfg["vocab_size"], size=T).tolist()
+    for _ in range(max(args.warmup, 3)):
+        sess.prefill(ids)
+        sess.reset()
+    gpu, wall = [], []
+    for i in range(args.prefill_reps):
+        if i:
+            sess.reset()
+        s0 = sess.stats()["gpu_ms"]
+        t0 = time.perf_counter()
+        last = sess.prefill(ids)
+        wall.append(time.perf_counter() - t0)
+        gpu.append(sess.stats()["gpu_ms"] - s0)
+    # greedy decode on top of the last prefill
+    s0 = sess.stats()["gpu_ms"]
+    t0 = time.perf_counter()
+    tok = int(np.argmax(last))
+    for _ in range(ndec):
+        tok = int(np.argmax(sess.decode(tok)))
+    dec_wall = time.perf_counter() - t0
+    dec_gpu = sess.stats()["gpu_ms"] - s0
+    # per-kernel device times of one eager profiled prefill
+    sess.reset()
+    sess.set_profiling(True)
+    sess.profile_reset()
+    sess.prefill(ids)
+    prof = sess.profile()
+    sess.set_profiling(False)
+    fl = prefill_flops(cfg, T)
+    ms = float(np.median(gpu))
+    peak, peak_kind = measured_tflops()
+    roof = None
+    cands = {k: v for k, v in prof.items() if prefill_kernel_flops(cfg, k, T, 0)}
+    if cands:
+        dom = max(cands.items(), key=lambda kv: kv[1][0])[0]
+        tot, launches = prof[dom]
+        per_ms = tot / launches
+        f = prefill_kernel_flops(cfg, dom, T, 0)
+        ach = f / (per_ms / 1e3) / 1e12
+        roof = {"bound": "tensor", "kernel": dom, "achieved": ach, "peak": peak, "unit": "TFLOP/s",
+                "frac": ach / peak, "peak_kind": peak_kind, "algorithmic_flops_per_launch": f,
+                "avg_launch_us": per_ms * 1e3,
+                "measured": "CUDA events between launches on the session stream, one eager profiled prefill"}
+    out = {
+        "workload": name, "tokens": T, "reps": args.prefill_reps,
+        "prefill_ms": ms, "prefill_tok_s": T / (ms / 1e3),
+        "prefill_e2e_tok_s": T / float(np.median(wall)),
+        "prefill_tflops": (fl["linear"] + fl["attention"]) / (ms / 1e3) / 1e12,
+        "flops": fl,
+        "decode_steps": ndec, "decode_tok_s": ndec / (dec_gpu / 1e3), "decode_e2e_tok_s": ndec / dec_wall,
+        "roofline": roof,
+        "kernels": {k: {"ms": v[0], "launches": v[1]} for k, v in prof.items()},
+        "data": "synthetic (seeded q4 weights, uniform random prompt ids)",
+        "timing": "device time of each fc_session_prefill (CUDA events around the enqueued chunk), median "
+                  "of the timed reps; decode = graph replays of fc_session_decode",
+    }
+    sess.close()
+    model.close()
+    return out
+
+
 def run_ours(args, d):
     import floyd_b200
     from floyd_b200.configs import CONFIGS
@@ -310,6 +416,10 @@ def run_ours(args, d):
     gen_tokens = rows * n_rounds + 2
     capacity = ctx0 + gen_tokens + 8
     V = cfg["vocab_size"]
+
+    prefill = None
+    if args.prefill_tokens > 0 and d.world == 1:
+        prefill = prefill_leg(args, d)
 
     t_setup = time.time()
     # N > 1: the routed experts are split across the N GPUs (contiguous id
@@ -461,6 +571,7 @@ def run_ours(args, d):
         "gpu_launches": None,
         "kernels": {k: {"ms": v[0], "launches": v[1]} for k, v in prof.items()},
         "clocks": clk,
+        "prefill": prefill,
         "setup_s": setup_s,
         "device": model.device_name(),
     }

@@ -96,3 +96,31 @@ def step_bytes(cfg, rows, context, active_experts_per_layer):
         total += context * (L + R) * 2
     total += c["vocab_size"] * D * df  # lm-head
     return total
+
+
+def prefill_flops(cfg, tokens, start=0):
+    """Algorithmic FLOPs of one prefill chunk of `tokens` rows at positions
+    start .. start + tokens - 1, in the form the prefill path computes:
+    every linear layer 2 x params per row (q, kv_a, o; routed experts at
+    experts_per_token per row, shared / dense MLPs, the router), keys and
+    values decompressed from the latent cache for all start + tokens
+    positions (kv_b: H x (nope + v) x L per position), and attention
+    2 x H x (nope + rope + v) per visible (query, key) pair.
+    Returns {"linear": F, "attention": F}."""
+    c = cfg
+    D, H, L, R = c["hidden_size"], c["head_count"], c["kv_lora_rank"], c["qk_rope_dim"]
+    NP, VD = c["qk_nope_dim"], c["value_dim"]
+    q = (D * c["q_lora_rank"] + c["q_lora_rank"] * H * (NP + R)) if c["q_lora_rank"] else D * H * (NP + R)
+    per_row = q + D * (L + R) + H * VD * D
+    linear = 0.0
+    for layer in range(c["layer_count"]):
+        linear += per_row * tokens + H * (NP + VD) * L * (start + tokens)
+        if layer < c["first_dense_layer_count"]:
+            linear += 3 * D * c["dense_intermediate_size"] * tokens
+        else:
+            I = c["moe_intermediate_size"]
+            linear += (c["experts_per_token"] * 3 * D * I + 3 * D * I * c["shared_expert_count"]
+                       + D * c["expert_count"]) * tokens
+    pairs = tokens * start + tokens * (tokens + 1) / 2
+    attention = 2.0 * c["layer_count"] * H * (NP + R + VD) * pairs
+    return {"linear": 2.0 * linear, "attention": attention}

@@ -222,7 +222,8 @@ mla_attention_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_c
     pdl_release();
     if (tid == 0) TC_MARK(1);
 
-    const int pos = *d_pos, nq = S * H, total = pos + S;
+    // keys up to the last query row of this tile (causal: key <= pos + row)
+    const int pos = *d_pos, nq = S * H, total = pos + min(q0 + kTcRows, nq) / H + ((min(q0 + kTcRows, nq) % H) != 0);
     const int k0 = split * keys_per_split;
     const int k1 = min(k0 + keys_per_split, total);
     const int nblk = k1 > k0 ? (k1 - k0 + kTcKeys - 1) / kTcKeys : 0;

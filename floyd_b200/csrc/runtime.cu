@@ -30,6 +30,7 @@
 #include "mla.cuh"
 #include "mla_tc.cuh"
 #include "moe.cuh"
+#include "prefill.cuh"
 #include "synth.cuh"
 
 using namespace fc;
@@ -162,6 +163,20 @@ struct FcSession {
     bool profiling = false;
     bool trace = false;      // per-layer hidden-state copies (test hook)
     std::vector<cudaEvent_t> prof_events;
+    // prefill chunks of more than rows_max tokens (max_batch > 8): tcgen05
+    // GEMMs over up to pf_rows tokens, buffers rows padded to pf_pad (x128)
+    int pf_rows = 0, pf_pad = 0, pf_slots = 0;
+    int *pf_ids = nullptr, *pf_h_ids = nullptr;   // [position, ids...] device / pinned host
+    float *pf_resid = nullptr, *pf_xn = nullptr, *pf_ckv = nullptr, *pf_qa = nullptr;
+    float *pf_logits = nullptr, *pf_choice = nullptr, *pf_route_w = nullptr, *pf_yd = nullptr, *pf_sh = nullptr;
+    float *pf_rpart = nullptr;   // router k-split partials [splits][rows][E]
+    __half *pf_x16 = nullptr, *pf_q16 = nullptr, *pf_qa16 = nullptr, *pf_kvd = nullptr;
+    __half *pf_o16 = nullptr, *pf_h16 = nullptr, *pf_xg = nullptr, *pf_hg = nullptr;
+    int *pf_route_ids = nullptr, *pf_counts = nullptr, *pf_offsets = nullptr, *pf_cursor = nullptr;
+    int *pf_slot_of = nullptr, *pf_mt_count = nullptr;
+    int4 *pf_mt_table = nullptr;
+    CUtensorMap pf_map_x{}, pf_map_q{}, pf_map_qa{}, pf_map_o{}, pf_map_hd{}, pf_map_hs{}, pf_map_xg{},
+        pf_map_hg{}, pf_map_kvd{}, pf_cmap{}, pf_cmap64{};
     std::vector<std::string> prof_marks;
     std::vector<std::pair<std::string, std::pair<double, uint64_t>>> prof;
 };
@@ -471,6 +486,8 @@ void free_session_buffers(FcSession *s) {
     s->allocs.clear();
     if (s->h_stage) cudaFreeHost(s->h_stage);
     if (s->h_res) cudaFreeHost(s->h_res);
+    if (s->pf_h_ids) cudaFreeHost(s->pf_h_ids);
+    s->pf_h_ids = nullptr;
     s->h_stage = nullptr;
     s->h_res = nullptr;
     if (s->stream) cudaStreamDestroy(s->stream);
@@ -934,6 +951,23 @@ cudaGraphExec_t get_graph(FcSession *s, int S, int drafts, char *err, size_t n) 
     return exec;
 }
 
+// Adds the event intervals of the last eager pass to the per-name profile.
+void collect_profile(FcSession *s) {
+    for (size_t i = 0; i < s->prof_marks.size(); ++i) {
+        float ms = 0.0f;
+        cudaEventElapsedTime(&ms, s->prof_events[i], s->prof_events[i + 1]);
+        bool found = false;
+        for (auto &p : s->prof)
+            if (p.first == s->prof_marks[i]) {
+                p.second.first += ms;
+                p.second.second++;
+                found = true;
+                break;
+            }
+        if (!found) s->prof.push_back({s->prof_marks[i], {ms, 1}});
+    }
+}
+
 // Runs one forward pass of `rows` <= rows_max tokens at the session position.
 int run_pass(FcSession *s, const int *ids, int rows, int k, const FcAcceptConfig *accept,
              char *err, size_t n) {
@@ -960,21 +994,7 @@ int run_pass(FcSession *s, const int *ids, int rows, int k, const FcAcceptConfig
         cudaEventRecord(s->prof_events[0], s->stream);
         e = record_forward(s, rows, drafts);
         if (e == cudaSuccess) e = cudaStreamSynchronize(s->stream);
-        if (e == cudaSuccess) {
-            for (size_t i = 0; i < s->prof_marks.size(); ++i) {
-                float ms = 0.0f;
-                cudaEventElapsedTime(&ms, s->prof_events[i], s->prof_events[i + 1]);
-                bool found = false;
-                for (auto &p : s->prof)
-                    if (p.first == s->prof_marks[i]) {
-                        p.second.first += ms;
-                        p.second.second++;
-                        found = true;
-                        break;
-                    }
-                if (!found) s->prof.push_back({s->prof_marks[i], {ms, 1}});
-            }
-        }
+        if (e == cudaSuccess) collect_profile(s);
     } else {
         cudaGraphExec_t g = get_graph(s, rows, drafts, err, n);
         if (!g) return 0;
@@ -1004,6 +1024,244 @@ int run_pass(FcSession *s, const int *ids, int rows, int k, const FcAcceptConfig
     return 1;
 }
 
+// ---------------------------------------------------------------------------
+// prefill chunks on the tensor cores
+// ---------------------------------------------------------------------------
+#define FC_PF_VARIANTS(X, F) \
+    X(F, 256, PF_STORE_F32) X(F, 256, PF_STORE_F16) X(F, 256, PF_ADD_F32) X(F, 256, PF_SWIGLU_F16)
+#define FC_PF_ALL(X) FC_PF_VARIANTS(X, FC_FMT_Q8) FC_PF_VARIANTS(X, FC_FMT_Q4) FC_PF_VARIANTS(X, FC_FMT_MXFP4)
+
+cudaError_t pf_prepare_all() {
+#define FC_PF_ATTR(F, BN, EPI)                                                                       \
+    {                                                                                                \
+        cudaError_t e_ = cudaFuncSetAttribute(pf_gemm_kernel<F, BN, EPI>,                            \
+                                              cudaFuncAttributeMaxDynamicSharedMemorySize,           \
+                                              (int)PfPlan<BN>::SMEM);                                \
+        if (e_ != cudaSuccess) return e_;                                                            \
+    }
+    FC_PF_ALL(FC_PF_ATTR)
+#undef FC_PF_ATTR
+#define FC_FA_ATTR(A, B)                                                                              \
+    {                                                                                                \
+        cudaError_t e_ = cudaFuncSetAttribute(pf_attention_kernel<A, B>,                              \
+                                              cudaFuncAttributeMaxDynamicSharedMemorySize,           \
+                                              (int)FaPlan<A, B>::SMEM);                              \
+        if (e_ != cudaSuccess) return e_;                                                            \
+    }
+    FC_FA_ATTR(2, 1) FC_FA_ATTR(2, 2) FC_FA_ATTR(3, 1) FC_FA_ATTR(3, 2)
+#undef FC_FA_ATTR
+    return cudaSuccess;
+}
+
+// One tcgen05 GEMM launch (one CTA per SM) of weight format `fmt`.
+cudaError_t pf_gemm(int fmt, int epi, const CUtensorMap &map, const PfGemm &p, int sms, cudaStream_t st) {
+    constexpr int bn = 256;
+#define FC_PF_CASE(F, BN, EPI)                                                                       \
+    if (fmt == F && bn == BN && epi == EPI)                                                          \
+        return launch_pdl(pf_gemm_kernel<F, BN, EPI>, dim3(sms), dim3(kPfThreads), PfPlan<BN>::SMEM, st, map, p);
+    FC_PF_ALL(FC_PF_CASE)
+#undef FC_PF_CASE
+    return cudaErrorInvalidValue;
+}
+
+// A GEMM of matrix `mm` (group stride w_gstride) over `rows` rows of the A map.
+PfGemm pf_plain(FcSession *s, const DevMat &mm, int rows, void *out, int64_t out_ld) {
+    PfGemm p{};
+    p.w = mm.w;
+    p.kp = mm.kp;
+    p.N = mm.O;
+    p.K = mm.kp;
+    p.groups = 1;
+    p.rows = rows;
+    p.out = out;
+    p.out_ld = out_ld;
+    p.err = s->d_err;
+    return p;
+}
+
+// Enqueues the forward of T (<= pf_rows) tokens at position pf_ids[0]:
+// every layer over the whole chunk, then the final norm and lm-head of the
+// last row into logits row 0.
+cudaError_t record_prefill(FcSession *s, int T) {
+    FcModel *m = s->m;
+    const FcModelConfig &c = m->c;
+    cudaStream_t st = s->stream;
+    const int D = c.hidden_size, H = c.head_count, L = c.kv_lora_rank, R = c.qk_rope_dim;
+    const int NP = c.qk_nope_dim, VD = c.value_dim, QW = NP + R;
+    const int df = c.dense_format, ef = c.expert_format, sms = m->sms;
+    const float scale = 1.0f / sqrtf((float)(NP + R));
+    const int *d_pos = s->pf_ids, *ids = s->pf_ids + 1;
+    FC_TRY(launch_pdl(embed_kernel, dim3(T), dim3(256), 0, st, m->embed.fmt, (const uint8_t *)m->embed.w, D,
+                      m->embed.kp, ids, s->pf_resid));
+    mark(s, "pf_embed");
+    for (int l = 0; l < c.layer_count; ++l) {
+        DevLayer &y = m->layers[l];
+        __half *cache = s->cache + (size_t)l * s->opt.context_size * (L + R);
+        FC_TRY(launch_pdl(pf_rmsnorm_kernel, dim3(T), dim3(256), 0, st, (const float *)s->pf_resid, D,
+                          (const float *)y.attn_norm.p, c.rms_norm_epsilon, s->pf_x16, D, (float *)nullptr));
+        mark(s, "pf_rmsnorm");
+        if (c.q_lora_rank > 0) {
+            PfGemm a = pf_plain(s, y.q_a, T, s->pf_qa, c.q_lora_rank);
+            FC_TRY(pf_gemm(df, PF_STORE_F32, s->pf_map_x, a, sms, st));
+            FC_TRY(launch_pdl(pf_rmsnorm_kernel, dim3(T), dim3(256), 0, st, (const float *)s->pf_qa, c.q_lora_rank,
+                              (const float *)y.q_a_norm.p, c.rms_norm_epsilon, s->pf_qa16, c.q_lora_rank,
+                              (float *)nullptr));
+            PfGemm b = pf_plain(s, y.q_b, T, s->pf_q16, H * QW);
+            FC_TRY(pf_gemm(df, PF_STORE_F16, s->pf_map_qa, b, sms, st));
+        } else {
+            PfGemm a = pf_plain(s, y.q_proj, T, s->pf_q16, H * QW);
+            FC_TRY(pf_gemm(df, PF_STORE_F16, s->pf_map_x, a, sms, st));
+        }
+        mark(s, "pf_gemm_q");
+        {
+            PfGemm a = pf_plain(s, y.kv_a, T, s->pf_ckv, L + R);
+            FC_TRY(pf_gemm(df, PF_STORE_F32, s->pf_map_x, a, sms, st));
+            mark(s, "pf_gemm_kv_a");
+        }
+        FC_TRY(launch_pdl(pf_prep_kernel, dim3(T, 1 + (H * (R / 2) + 255) / 256), dim3(256), 0, st,
+                          (const float *)s->pf_ckv, s->pf_q16, (const float *)y.kv_a_norm.p, L, R, H, NP,
+                          c.rms_norm_epsilon, c.rope_theta, d_pos, cache));
+        mark(s, "pf_prep");
+        {
+            // keys and values of every visible position: kvd[k][h*(nope+v) + j]
+            // = cache_latent[k] . kv_b[h*(nope+v) + j]  (W_UK rows, then W_UV)
+            PfGemm a = pf_plain(s, y.kv_b, s->position + T, s->pf_kvd, (int64_t)H * (NP + VD));
+            a.a_y0 = l * s->opt.context_size;
+            FC_TRY(pf_gemm(df, PF_STORE_F16, s->pf_cmap, a, sms, st));
+            mark(s, "pf_gemm_kv_b");
+        }
+        {
+            dim3 grid((T + kFaRows - 1) / kFaRows, H);
+            const int nqs = NP / 64 + 1, nvs = VD / 64;
+#define FC_FA_LAUNCH(A, B)                                                                                        \
+    if (nqs == A && nvs == B)                                                                                     \
+        FC_TRY(launch_pdl(pf_attention_kernel<A, B>, grid, dim3(kFaThreads), FaPlan<A, B>::SMEM, st, s->pf_map_q, \
+                          s->pf_map_kvd, s->pf_cmap64, l * s->opt.context_size, L, T, H, d_pos, scale, s->pf_o16, \
+                          s->d_err));
+            FC_FA_LAUNCH(2, 1) FC_FA_LAUNCH(2, 2) FC_FA_LAUNCH(3, 1) FC_FA_LAUNCH(3, 2)
+#undef FC_FA_LAUNCH
+            mark(s, "pf_attention");
+        }
+        {
+            PfGemm a = pf_plain(s, y.o_proj, T, s->pf_resid, D);
+            FC_TRY(pf_gemm(df, PF_ADD_F32, s->pf_map_o, a, sms, st));
+            mark(s, "pf_gemm_o_proj");
+        }
+        FC_TRY(launch_pdl(pf_rmsnorm_kernel, dim3(T), dim3(256), 0, st, (const float *)s->pf_resid, D,
+                          (const float *)y.ffn_norm.p, c.rms_norm_epsilon, s->pf_x16, D, s->pf_xn));
+        mark(s, "pf_rmsnorm");
+        if (y.dense) {
+            const int I = c.dense_intermediate_size;
+            PfGemm a = pf_plain(s, y.d_gate, T, s->pf_h16, I);
+            a.w2 = y.d_up.w;
+            FC_TRY(pf_gemm(df, PF_SWIGLU_F16, s->pf_map_x, a, sms, st));
+            mark(s, "pf_gemm_dense_gate_up");
+            PfGemm b = pf_plain(s, y.d_down, T, s->pf_resid, D);
+            FC_TRY(pf_gemm(df, PF_ADD_F32, s->pf_map_hd, b, sms, st));
+            mark(s, "pf_gemm_dense_down");
+            continue;
+        }
+        const int E = c.expert_count, K = c.experts_per_token, I = c.moe_intermediate_size;
+        // k splits: at least ~2 tiles per SM, 32-column multiples
+        const int tiles = ((T + kPfRtTile - 1) / kPfRtTile) * ((E + kPfRtTile - 1) / kPfRtTile);
+        int nsplit = std::min(kPfRtMaxSplits, std::max(1, (2 * sms + tiles - 1) / tiles));
+        const int ksplit = ((D + nsplit - 1) / nsplit + kPfRtK - 1) / kPfRtK * kPfRtK;
+        nsplit = (D + ksplit - 1) / ksplit;
+        FC_TRY(launch_pdl(pf_router_logits_kernel,
+                          dim3((T + kPfRtTile - 1) / kPfRtTile, (E + kPfRtTile - 1) / kPfRtTile, nsplit), dim3(256),
+                          0, st, (const float *)y.router.p, (const float *)s->pf_xn, T, D, E, ksplit, s->pf_rpart));
+        mark(s, "pf_router");
+        RouteParams rp{};
+        rp.E = E; rp.K = K; rp.S = T;
+        rp.score_fn = c.score_fn;
+        rp.normalize = c.normalize_topk;
+        rp.routed_scale = c.routed_scale;
+        rp.bias = y.bias.p;
+        rp.hash = y.hash;
+        rp.ids = ids;
+        rp.route_ids = s->pf_route_ids;
+        rp.route_w = s->pf_route_w;
+        rp.choice = s->pf_choice;
+        FC_TRY(launch_pdl(pf_route_kernel, dim3((T + kPfRouteWarps - 1) / kPfRouteWarps), dim3(32 * kPfRouteWarps), 0,
+                          st, (const float *)s->pf_rpart, nsplit, s->pf_logits, rp, s->pf_counts));
+        FC_TRY(launch_pdl(pf_group_kernel, dim3(1), dim3(1024), 0, st, s->pf_counts, E, s->pf_offsets, s->pf_cursor,
+                          s->pf_mt_table, s->pf_mt_count));
+        FC_TRY(launch_pdl(pf_gather_kernel, dim3((T * K + 7) / 8), dim3(256), 0, st, (const int *)s->pf_route_ids, T, K,
+                          s->pf_cursor, s->pf_slot_of, (const __half *)s->pf_x16, D, s->pf_xg));
+        mark(s, "pf_route_group");
+        {
+            PfGemm a = pf_plain(s, y.e_gate, 0, s->pf_hg, I);
+            a.w2 = y.e_up.w;
+            a.w_gstride = (int64_t)y.e_gate.w_bytes;
+            a.mt_count = s->pf_mt_count;
+            a.mt_table = s->pf_mt_table;
+            a.limit = c.swiglu_limit;
+            FC_TRY(pf_gemm(ef, PF_SWIGLU_F16, s->pf_map_xg, a, sms, st));
+            mark(s, "pf_gemm_moe_gate_up");
+            PfGemm b = pf_plain(s, y.e_down, 0, s->pf_yd, D);
+            b.w_gstride = (int64_t)y.e_down.w_bytes;
+            b.mt_count = s->pf_mt_count;
+            b.mt_table = s->pf_mt_table;
+            FC_TRY(pf_gemm(ef, PF_STORE_F32, s->pf_map_hg, b, sms, st));
+            mark(s, "pf_gemm_moe_down");
+        }
+        if (y.s_gate.count) {
+            const int W = I * c.shared_expert_count;
+            PfGemm a = pf_plain(s, y.s_gate, T, s->pf_h16, W);
+            a.w2 = y.s_up.w;
+            a.limit = c.swiglu_limit;
+            FC_TRY(pf_gemm(df, PF_SWIGLU_F16, s->pf_map_x, a, sms, st));
+            PfGemm b = pf_plain(s, y.s_down, T, s->pf_sh, D);
+            FC_TRY(pf_gemm(df, PF_STORE_F32, s->pf_map_hs, b, sms, st));
+            mark(s, "pf_gemm_shared");
+        }
+        FC_TRY(launch_pdl(pf_combine_kernel, dim3(T), dim3(256), 0, st, s->pf_resid, (const float *)s->pf_yd,
+                          y.s_gate.count ? (const float *)s->pf_sh : (const float *)nullptr,
+                          (const int *)s->pf_route_ids, (const float *)s->pf_route_w, (const int *)s->pf_slot_of, K, D));
+        mark(s, "pf_moe_combine");
+    }
+    // final norm + lm-head of the last row (a one-row GEMV)
+    const int kpD = kpad(D);
+    FC_TRY(launch_pdl(rmsnorm_kernel, dim3(1), dim3(norm_threads(D)), 0, st, (const float *)(s->pf_resid + (size_t)(T - 1) * D),
+                      D, (const float *)m->final_norm.p, D, c.rms_norm_epsilon, s->xq_norm, kpD, (float *)nullptr, 0));
+    GemvSeg g = seg_of(m->lm_head, s->xq_norm, EPI_STORE);
+    g.y = s->logits;
+    g.ldy = c.vocab_size;
+    FC_TRY(gemv1(df, g, 1, 0.0f, s->d_err, m->sms, st));
+    mark(s, "pf_lm_head");
+    return cudaGetLastError();
+}
+
+// Runs T tokens (rows_max < T <= pf_rows) through the prefill path.
+int run_prefill_chunk(FcSession *s, const int *ids, int T, char *err, size_t n) {
+    cudaSetDevice(s->m->device);
+    s->pf_h_ids[0] = s->position;
+    memcpy(s->pf_h_ids + 1, ids, (size_t)T * sizeof(int));
+    cudaError_t e = cudaMemcpyAsync(s->pf_ids, s->pf_h_ids, (size_t)(T + 1) * sizeof(int), cudaMemcpyHostToDevice,
+                                    s->stream);
+    if (e == cudaSuccess) e = cudaMemsetAsync(s->d_err, 0, sizeof(int), s->stream);
+    if (e == cudaSuccess) e = cudaEventRecord(s->ev_begin, s->stream);
+    if (s->profiling) {
+        s->prof_marks.clear();
+        cudaEventRecord(s->prof_events[0], s->stream);
+    }
+    if (e == cudaSuccess) e = record_prefill(s, T);
+    if (e == cudaSuccess) e = cudaEventRecord(s->ev_end, s->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s->stream);
+    if (e != cudaSuccess) return set_error(err, n, "CUDA prefill failed: %s", cudaGetErrorString(e));
+    if (s->profiling) collect_profile(s);
+    float ms = 0.0f;
+    cudaEventElapsedTime(&ms, s->ev_begin, s->ev_end);
+    s->stats.gpu_ms += ms;
+    s->stats.command_buffers++;
+    int herr = 0;
+    cudaMemcpy(&herr, s->d_err, sizeof(int), cudaMemcpyDeviceToHost);
+    if (herr) return set_error(err, n, "a kernel wait gave up (error bits 0x%x); results are invalid", herr);
+    s->last_rows = 1;
+    s->last_drafts = 0;
+    return 1;
+}
+
 int check_ids(const FcSession *s, const int *ids, int count, char *err, size_t n) {
     for (int i = 0; i < count; ++i)
         if (ids[i] < 0 || ids[i] >= s->m->c.vocab_size)
@@ -1016,6 +1274,13 @@ int run_tokens(FcSession *s, const int *ids, int count, float *last_logits, char
     if (!check_ids(s, ids, count, err, n)) return 0;
     int done = 0;
     while (done < count) {
+        if (s->pf_rows && count - done > s->rows_max) {
+            const int rows = std::min(s->pf_rows, count - done);
+            if (!run_prefill_chunk(s, ids + done, rows, err, n)) return 0;
+            s->position += rows;
+            done += rows;
+            continue;
+        }
         int rows = std::min(s->rows_max, count - done);
         if (!run_pass(s, ids + done, rows, -1, nullptr, err, n)) return 0;
         s->position += rows;
@@ -1392,9 +1657,55 @@ int fc_session_create(FcSession **out, FcModel *m, const FcOptions *options, cha
     ok = ok && cudaMallocHost(&s->h_stage, sizeof(Staging)) == cudaSuccess;
     ok = ok && cudaMallocHost(&s->h_res, sizeof(Result)) == cudaSuccess;
     if (ok && s->attn_tc)
-        ok = make_map_f16(&s->qmap, s->qcat, (uint64_t)(L + R), (uint64_t)q_rows, kTcRows) &&
-             make_map_f16(&s->kvmap, s->cache, (uint64_t)(L + R), (uint64_t)NLc * options->context_size,
-                          kTcKeys);
+        ok = make_map_f16(&s->qmap, s->qcat, (uint64_t)(L + R), (uint64_t)q_rows, kTcRows);
+    // prefill chunks on the tensor cores when the caller asks for more rows
+    // per pass than a verify holds (single-GPU models with quantized weights)
+    auto quant = [](int f) { return f == FC_FMT_Q8 || f == FC_FMT_Q4 || f == FC_FMT_MXFP4; };
+    const int NP = c.qk_nope_dim, VD = c.value_dim, DI = c.dense_intermediate_size;
+    const bool pf_ok = options->max_batch > s->rows_max && m->world == 1 && quant(c.dense_format) &&
+                       (c.expert_count == 0 || quant(c.expert_format)) && L % 64 == 0 && R == 64 &&
+                       (NP == 64 || NP == 128) && (VD == 64 || VD == 128) && (size_t)NLc * options->context_size >= (size_t)kPfM && D % 32 == 0 && (H * QW) % 32 == 0 && I % 32 == 0 &&
+                       W % 32 == 0 && DI % 32 == 0 && c.q_lora_rank % 32 == 0 && K <= 64 && E <= 1024;
+    if (ok && pf_ok) {
+        const int P = options->max_batch, Pp = (P + kPfM - 1) / kPfM * kPfM;
+        const int Sp = (Pp * K + kPfM - 1) / kPfM * kPfM;
+        const int QL = std::max(c.q_lora_rank, 32), HW = std::max(std::max(DI, W), 32);
+        s->pf_rows = P;
+        s->pf_pad = Pp;
+        s->pf_slots = Sp;
+        ok = ok && salloc(s, s->pf_ids, (size_t)P + 1) &&
+             cudaMallocHost(&s->pf_h_ids, ((size_t)P + 1) * sizeof(int)) == cudaSuccess;
+        ok = ok && salloc(s, s->pf_resid, (size_t)Pp * D) && salloc(s, s->pf_xn, (size_t)Pp * D);
+        ok = ok && salloc(s, s->pf_x16, (size_t)Pp * D) && salloc(s, s->pf_q16, (size_t)Pp * H * QW);
+        ok = ok && salloc(s, s->pf_qa, (size_t)Pp * QL) && salloc(s, s->pf_qa16, (size_t)Pp * QL);
+        const int Kr = (options->context_size + kFaKeys - 1) / kFaKeys * kFaKeys;  // kvd rows
+        ok = ok && salloc(s, s->pf_ckv, (size_t)Pp * (L + R)) && salloc(s, s->pf_kvd, (size_t)Kr * H * (NP + VD));
+        ok = ok && salloc(s, s->pf_o16, (size_t)Pp * H * VD);
+        ok = ok && salloc(s, s->pf_h16, (size_t)Pp * HW);
+        ok = ok && salloc(s, s->pf_logits, (size_t)Pp * E) && salloc(s, s->pf_choice, (size_t)Pp * E);
+        ok = ok && salloc(s, s->pf_rpart, (size_t)kPfRtMaxSplits * Pp * E);
+        ok = ok && salloc(s, s->pf_route_ids, (size_t)Pp * K) && salloc(s, s->pf_route_w, (size_t)Pp * K);
+        ok = ok && salloc(s, s->pf_slot_of, (size_t)Pp * K) && salloc(s, s->pf_counts, (size_t)E);
+        ok = ok && salloc(s, s->pf_offsets, (size_t)E) && salloc(s, s->pf_cursor, (size_t)E);
+        ok = ok && salloc(s, s->pf_mt_count, 1) && salloc(s, s->pf_mt_table, (size_t)Sp / kPfM + E + 1);
+        ok = ok && salloc(s, s->pf_xg, (size_t)Sp * D) && salloc(s, s->pf_hg, (size_t)Sp * I);
+        ok = ok && salloc(s, s->pf_yd, (size_t)Sp * D) && salloc(s, s->pf_sh, (size_t)Pp * D);
+        ok = ok && make_map_f16(&s->pf_map_x, s->pf_x16, D, Pp, kPfM) &&
+             make_map_f16(&s->pf_map_q, s->pf_q16, (uint64_t)H * QW, Pp, kPfM) &&
+             make_map_f16(&s->pf_map_qa, s->pf_qa16, QL, Pp, kPfM) &&
+             make_map_f16(&s->pf_map_o, s->pf_o16, (uint64_t)H * VD, Pp, kPfM) &&
+             make_map_f16(&s->pf_map_hd, s->pf_h16, std::max(DI, 32), Pp, kPfM) &&
+             make_map_f16(&s->pf_map_hs, s->pf_h16, W, Pp, kPfM) &&
+             make_map_f16(&s->pf_map_xg, s->pf_xg, D, Sp, kPfM) &&
+             make_map_f16(&s->pf_map_hg, s->pf_hg, I, Sp, kPfM) &&
+             make_map_f16(&s->pf_map_kvd, s->pf_kvd, (uint64_t)H * (NP + VD), Kr, kFaKeys) &&
+             make_map_f16(&s->pf_cmap, s->cache, (uint64_t)(L + R), (uint64_t)NLc * options->context_size, kPfM) &&
+             make_map_f16(&s->pf_cmap64, s->cache, (uint64_t)(L + R), (uint64_t)NLc * options->context_size,
+                          kFaKeys);
+        ok = ok && pf_prepare_all() == cudaSuccess;
+    }
+    if (ok && (s->attn_tc || s->pf_rows))
+        ok = make_map_f16(&s->kvmap, s->cache, (uint64_t)(L + R), (uint64_t)NLc * options->context_size, kTcKeys);
     if (ok) {
         cudaError_t e1 = cudaFuncSetAttribute(mla_attention_kernel<512, 64>,
                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1747,12 +2058,64 @@ __global__ void to_xq_kernel(const float *x, int S, int K, int kp, __half *xq) {
     store_xq(xq, kp, idx / K, idx % K, x[idx]);
 }
 
+__global__ void to_f16_kernel(const float *x, size_t n, __half *y) {
+    size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) y[i] = __float2half_rn(fminf(fmaxf(x[i], -65504.0f), 65504.0f));
+}
+
+// fc_matmul for S > 8 rows: the prefill GEMM on the tensor cores.
+int matmul_gemm(int format, float *y, const float *x, const DevMat &mm, const std::vector<uint8_t> &image, int O,
+                int K, int S, char *error, size_t error_size) {
+    const int Sp = (S + kPfM - 1) / kPfM * kPfM;
+    uint8_t *dw = nullptr;
+    float *dx = nullptr, *dy = nullptr;
+    __half *dx16 = nullptr;
+    int *derr = nullptr;
+    bool ok = cudaMalloc(&dw, image.size()) == cudaSuccess && cudaMalloc(&dx, (size_t)S * K * 4) == cudaSuccess &&
+              cudaMalloc(&dy, (size_t)S * O * 4) == cudaSuccess &&
+              cudaMalloc(&dx16, (size_t)Sp * K * 2) == cudaSuccess && cudaMalloc(&derr, 4) == cudaSuccess;
+    cudaError_t e = cudaErrorMemoryAllocation;
+    int herr = 0;
+    CUtensorMap map{};
+    if (ok) e = pf_prepare_all();
+    if (ok && e == cudaSuccess && !make_map_f16(&map, dx16, (uint64_t)K, (uint64_t)Sp, kPfM)) e = cudaErrorInvalidValue;
+    if (ok && e == cudaSuccess) {
+        cudaMemcpy(dw, image.data(), image.size(), cudaMemcpyHostToDevice);
+        cudaMemcpy(dx, x, (size_t)S * K * 4, cudaMemcpyHostToDevice);
+        cudaMemset(dx16, 0, (size_t)Sp * K * 2);
+        cudaMemset(derr, 0, 4);
+        const size_t n = (size_t)S * K;
+        to_f16_kernel<<<(unsigned)((n + 255) / 256), 256>>>(dx, n, dx16);
+        PfGemm p{};
+        p.w = dw;
+        p.kp = mm.kp;
+        p.N = O;
+        p.K = mm.kp;
+        p.groups = 1;
+        p.rows = S;
+        p.out = dy;
+        p.out_ld = O;
+        p.err = derr;
+        int dev = 0, sms = 148;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        e = pf_gemm(format, PF_STORE_F32, map, p, sms, 0);
+        if (e == cudaSuccess) e = cudaDeviceSynchronize();
+        if (e == cudaSuccess) e = cudaMemcpy(y, dy, (size_t)S * O * 4, cudaMemcpyDeviceToHost);
+        if (e == cudaSuccess) e = cudaMemcpy(&herr, derr, 4, cudaMemcpyDeviceToHost);
+    }
+    cudaFree(dw); cudaFree(dx); cudaFree(dy); cudaFree(dx16); cudaFree(derr);
+    if (e == cudaSuccess && herr) return set_error(error, error_size, "a kernel wait gave up (0x%x)", herr);
+    if (e != cudaSuccess) return set_error(error, error_size, "matmul failed: %s", cudaGetErrorString(e));
+    return 1;
+}
+
 }  // namespace
 
 extern "C" int fc_matmul(int format, float *y, const float *x, const void *values,
                          const void *scales, int O, int K, int S, char *error,
                          size_t error_size) {
-    if (!y || !x || !values || !scales || O <= 0 || K <= 0 || K % 32 || S < 1 || S > kMaxRows)
+    if (!y || !x || !values || !scales || O <= 0 || K <= 0 || K % 32 || S < 1 || (S > kMaxRows && O % 32))
         return set_error(error, error_size, "invalid matmul shape");
     if (format != FC_FMT_Q8 && format != FC_FMT_Q4 && format != FC_FMT_MXFP4)
         return set_error(error, error_size, "unsupported format %d", format);
@@ -1761,6 +2124,7 @@ extern "C" int fc_matmul(int format, float *y, const float *x, const void *value
     std::vector<uint8_t> image(mm.w_bytes, 0);
     pack_values(mm, reinterpret_cast<const uint8_t *>(values), image.data());
     pack_scales(mm, reinterpret_cast<const uint8_t *>(scales), image.data());
+    if (S > kMaxRows) return matmul_gemm(format, y, x, mm, image, O, K, S, error, error_size);
     uint8_t *dw = nullptr;
     float *dx = nullptr, *dy = nullptr;
     __half *dxq = nullptr;

@@ -18,7 +18,11 @@ extern "C" {
 /* y[s][o] = sum_k x[s][k] * dequant(w[o][k]) for s < S, fp32 accumulation.
  * `format` is an FcFormat (Q8, Q4 or MXFP4); `values` / `scales` are in the
  * logical layout of fc_model_set_tensor (int8 [O][K] or packed nibbles
- * [O][K/2], fp16 / ue8m0 group scales [O][K/32]).  K % 32 == 0, 1 <= S <= 8.
+ * [O][K/2], fp16 / ue8m0 group scales [O][K/32]).  K % 32 == 0, S >= 1.
+ * S <= 8 runs the GEMV (fp32-exact activations as hi/lo fp16 pairs);
+ * S > 8 runs the prefill GEMM on the tcgen05 tensor cores (activations and
+ * dequantized weights rounded to fp16 once, fp32 accumulation) and needs
+ * O % 32 == 0.
  * Replaces fm_matmul_q8 / fm_matmul_q4 (backend_metal.h:18-33) and the Metal
  * offload of deepseek_v4_fp4_matmul_f32 (deepseek_v4_quant.h:103-139). */
 int fc_matmul(int format, float *y, const float *x, const void *values,
