@@ -52,6 +52,8 @@ def parse():
                     help="configs[2] leg: prompt length of the prefill (0 = skip the leg)")
     ap.add_argument("--prefill-decode", type=int, default=512, help="configs[2] leg: greedy decodes after it")
     ap.add_argument("--prefill-reps", type=int, default=5, help="configs[2] leg: timed prefills")
+    ap.add_argument("--prefill-only", action="store_true",
+                    help="run only the configs[2] prefill / decode leg and print its JSON")
     ap.add_argument("--layers", type=int, default=None,
                     help="override layer_count (small profiling cases only)")
     ap.add_argument("--out", default=None, help="also write the JSON line here")
@@ -391,7 +393,8 @@ def prefill_leg(args, d):
         "prefill_e2e_tok_s": T / float(np.median(wall)),
         "prefill_tflops": (fl["linear"] + fl["attention"]) / (ms / 1e3) / 1e12,
         "flops": fl,
-        "decode_steps": ndec, "decode_tok_s": ndec / (dec_gpu / 1e3), "decode_e2e_tok_s": ndec / dec_wall,
+        "decode_steps": ndec, "decode_tok_s": ndec / (dec_gpu / 1e3) if ndec else None,
+        "decode_e2e_tok_s": ndec / dec_wall if ndec else None,
         "roofline": roof,
         "kernels": {k: {"ms": v[0], "launches": v[1]} for k, v in prof.items()},
         "data": "synthetic (seeded q4 weights, uniform random prompt ids)",
@@ -591,6 +594,8 @@ def main():
     d = Dist()
     if args.impl == "reference":
         out = run_reference(args, d)
+    elif args.prefill_only:
+        out = prefill_leg(args, d) if d.rank == 0 else None
     else:
         out = run_ours(args, d)
     if d.rank == 0 and out is not None:

@@ -90,6 +90,20 @@ __device__ __forceinline__ PfTile pf_tile(const PfGemm &p, int mi, int mpg) {
     return t;
 }
 
+// Bounded wait (~20 ms) used on the way out: the copies and MMAs a CTA
+// issued must finish before it exits, even after an abort.
+__device__ __forceinline__ void pf_drain(uint64_t *bar, uint32_t parity) {
+    uint64_t t0 = 0;
+    for (uint32_t it = 0;; ++it) {
+        if (mbar_try_wait(bar, parity)) return;
+        if ((it & 255u) == 0) {
+            const uint64_t t = global_ns();
+            if (t0 == 0) t0 = t;
+            else if (t - t0 > 20000000ull) return;
+        }
+    }
+}
+
 __device__ __forceinline__ bool pf_wait(uint64_t *bar, uint32_t parity, int *err, volatile int *abort, int site) {
     if (*abort) return false;
     if (mbar_wait_timed(bar, parity, err, site)) return true;
@@ -200,8 +214,8 @@ pf_gemm_kernel(const __grid_constant__ CUtensorMap amap, const PfGemm p) {
     uint64_t *bars = reinterpret_cast<uint64_t *>(sm + P::OFF_BAR);
     uint64_t *a_full = bars, *a_empty = bars + kPfSA, *d_full = bars + 2 * kPfSA,
              *d_empty = d_full + kPfSD, *q_full = d_empty + kPfSD, *q_empty = q_full + kPfSQ,
-             *acc_full = q_empty + kPfSQ, *acc_empty = acc_full + 2;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
+             *acc_full = q_empty + kPfSQ, *acc_empty = acc_full + 2, *mma_done = acc_empty + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mma_done + 1);
     volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -222,6 +236,7 @@ pf_gemm_kernel(const __grid_constant__ CUtensorMap amap, const PfGemm p) {
             mbar_init(&acc_full[i], 1);
             mbar_init(&acc_empty[i], 4);
         }
+        mbar_init(mma_done, 1);
         *abort = 0;
         mbar_fence_init();
         asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(&amap)) : "memory");
@@ -254,9 +269,9 @@ pf_gemm_kernel(const __grid_constant__ CUtensorMap amap, const PfGemm p) {
                 const PfTile t = pf_tile(p, mi, mpg);
                 const uint8_t *wg = p.w + (int64_t)t.g * p.w_gstride;
                 const uint8_t *wg2 = p.w2 ? p.w2 + (int64_t)t.g * p.w_gstride : nullptr;
-                for (int ks = 0; ks < nk; ++ks) {
+                for (int ks = 0; ks < nk && !*abort; ++ks) {
                     if (ks % KPR == 0) {
-                        if (q_fill >= kPfSQ) pf_wait(&q_empty[q_slot], q_ph ^ 1, p.err, abort, 0);
+                        if (q_fill >= kPfSQ && !pf_wait(&q_empty[q_slot], q_ph ^ 1, p.err, abort, 0)) break;
                         uint8_t *dst = sQ + q_slot * kPfRawBytes;
                         uint32_t bytes = 0;
                         // BN stored rows (BN / 16 tiles) x one chunk
@@ -283,12 +298,22 @@ pf_gemm_kernel(const __grid_constant__ CUtensorMap amap, const PfGemm p) {
                         ++q_fill;
                         if (++q_slot == kPfSQ) { q_slot = 0; q_ph ^= 1; }
                     }
-                    if (a_fill >= kPfSA) pf_wait(&a_empty[a_slot], a_ph ^ 1, p.err, abort, 1);
+                    if (a_fill >= kPfSA && !pf_wait(&a_empty[a_slot], a_ph ^ 1, p.err, abort, 1)) break;
                     mbar_expect_tx(&a_full[a_slot], P::A_BYTES);
                     tma_load_2d(sA + a_slot * P::A_BYTES, &amap, t.a_x + ks * kPfK, t.a_y, &a_full[a_slot]);
                     ++a_fill;
                     if (++a_slot == kPfSA) { a_slot = 0; a_ph ^= 1; }
                 }
+            }
+            // before the CTA can exit, every copy this thread issued has
+            // landed: wait (bounded) for the last fill of each ring slot
+            for (int i = 0; i < kPfSA && i < a_fill; ++i) {
+                const int f = a_fill - 1 - ((a_fill - 1 - i) % kPfSA);  // last fill of slot i
+                pf_drain(&a_full[f % kPfSA], (uint32_t)((f / kPfSA) & 1));
+            }
+            for (int i = 0; i < kPfSQ && i < q_fill; ++i) {
+                const int f = q_fill - 1 - ((q_fill - 1 - i) % kPfSQ);
+                pf_drain(&q_full[f % kPfSQ], (uint32_t)((f / kPfSQ) & 1));
             }
         }
     } else if (warp == kPfWarpMma) {
@@ -319,6 +344,9 @@ pf_gemm_kernel(const __grid_constant__ CUtensorMap amap, const PfGemm p) {
                 }
                 tc_commit(&acc_full[b]);
             }
+            // every MMA this thread issued completes before TMEM is freed
+            tc_commit(mma_done);
+            pf_drain(mma_done, 0);
         }
     } else if (warp >= kPfWarpDq0) {
         constexpr int UPT = BN * 4 / kPfDqThreads;  // dequant units per thread
@@ -592,6 +620,10 @@ pf_attention_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_const
                     tma_load_2d(dst + P::K_BYTES + s * kFaKeys * 128, &kvmap, h * (NP + DV) + NP + s * 64, key0,
                                 &kv_full[st]);
             }
+            // every copy issued has landed before the CTA may exit
+            pf_drain(q_full, 0);
+            for (int j = max(nblk - kFaStages, 0); j < nblk; ++j)
+                pf_drain(&kv_full[j % kFaStages], (uint32_t)((j / kFaStages) & 1));
         }
     } else if (warp == 1) {
         if (lane == 0) {
