@@ -39,8 +39,8 @@ constexpr int kPfRawBytes = 16 * 1152;
 enum PfEpi : int { PF_STORE_F32 = 0, PF_STORE_F16 = 1, PF_ADD_F32 = 2, PF_SWIGLU_F16 = 3 };
 
 struct PfGemm {
-    const uint8_t *w, *w2;   // B: tile-major weights; w2 = the up rows (SwiGLU)
-    int64_t w_gstride;       // bytes from one group's weights to the next
+    int tiles_per_group;     // 16-row weight tiles from one group's matrix to the next
+    int box_tiles;           // tiles per weight-map box (BN / 16, BN / 32 for SwiGLU, fewer for tiny matrices)
     int kp;                  // padded width of the stored matrix
     int N, K;                // outputs per group (multiple of 32); reduction length (multiple of 64)
     int groups, rows;        // arithmetic m-tiles: groups x ceil(rows / 128)
@@ -200,9 +200,14 @@ __device__ __forceinline__ float pf_swiglu(float g, float u, float limit) {
 }
 
 // grid = SM count, kPfThreads threads, PfPlan<BN>::SMEM bytes.
+// wmap / wmap2: 4-D tensor maps of the weights (and, for SwiGLU, of the up
+// rows) viewed as [16-row tiles][chunks][block_bytes / 64][64 bytes], box
+// {64, block_bytes / 64, 1, BN / 16} (BN / 32 tiles each for SwiGLU): one
+// request brings a stage's blocks in the raw ring's layout.
 template <int FMT, int BN, int EPI>
 __global__ void __launch_bounds__(kPfThreads, 1)
-pf_gemm_kernel(const __grid_constant__ CUtensorMap amap, const PfGemm p) {
+pf_gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap wmap,
+               const __grid_constant__ CUtensorMap wmap2, const PfGemm p) {
     using P = PfPlan<BN>;
     constexpr int KC = FMT == FC_FMT_Q8 ? 64 : 128;  // columns per stored chunk
     constexpr int KPR = KC / 64;                     // k-steps per raw stage
@@ -240,6 +245,9 @@ pf_gemm_kernel(const __grid_constant__ CUtensorMap amap, const PfGemm p) {
         *abort = 0;
         mbar_fence_init();
         asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(&amap)) : "memory");
+        asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(&wmap)) : "memory");
+        if (EPI == PF_SWIGLU_F16)
+            asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(&wmap2)) : "memory");
     }
     if (warp == kPfWarpMma) {
         __syncwarp();
@@ -258,7 +266,6 @@ pf_gemm_kernel(const __grid_constant__ CUtensorMap amap, const PfGemm p) {
     const int n_nt = (p.N + BNO - 1) / BNO;
     const int items = n_mt * n_nt;
     const int nk = p.K / kPfK;
-    const size_t tbytes = tile_bytes(FMT, p.kp);
 
     if (warp == kPfWarpProducer) {
         if (lane == 0) {
@@ -267,33 +274,20 @@ pf_gemm_kernel(const __grid_constant__ CUtensorMap amap, const PfGemm p) {
             for (int it = blockIdx.x; it < items && !*abort; it += gridDim.x) {
                 const int mi = it / n_nt, nt = it % n_nt;
                 const PfTile t = pf_tile(p, mi, mpg);
-                const uint8_t *wg = p.w + (int64_t)t.g * p.w_gstride;
-                const uint8_t *wg2 = p.w2 ? p.w2 + (int64_t)t.g * p.w_gstride : nullptr;
                 for (int ks = 0; ks < nk && !*abort; ++ks) {
                     if (ks % KPR == 0) {
                         if (q_fill >= kPfSQ && !pf_wait(&q_empty[q_slot], q_ph ^ 1, p.err, abort, 0)) break;
                         uint8_t *dst = sQ + q_slot * kPfRawBytes;
-                        uint32_t bytes = 0;
-                        // BN stored rows (BN / 16 tiles) x one chunk
+                        // BN stored rows (BN / 16 tiles) x one chunk; rows past the
+                        // matrix arrive as zeros and are never stored
                         const int c = ks * kPfK / KC;
-                        for (int tt = 0; tt < BN / 16; ++tt) {
-                            const int o0 = EPI == PF_SWIGLU_F16 ? nt * BNO + (tt % (BN / 32)) * 16 : nt * BN + tt * 16;
-                            if (o0 < p.N) bytes += BB;
-                        }
-                        mbar_expect_tx(&q_full[q_slot], bytes);
-                        for (int tt = 0; tt < BN / 16; ++tt) {
-                            const uint8_t *src;
-                            int o0;
-                            if (EPI == PF_SWIGLU_F16) {
-                                o0 = nt * BNO + (tt % (BN / 32)) * 16;
-                                src = tt < BN / 32 ? wg : wg2;
-                            } else {
-                                o0 = nt * BN + tt * 16;
-                                src = wg;
-                            }
-                            if (o0 < p.N)
-                                bulk_g2s(dst + tt * BB, src + (size_t)(o0 / 16) * tbytes + (size_t)c * BB, BB,
-                                         &q_full[q_slot]);
+                        const int tile0 = t.g * p.tiles_per_group + nt * BNO / 16;
+                        mbar_expect_tx(&q_full[q_slot], (EPI == PF_SWIGLU_F16 ? 2 : 1) * p.box_tiles * BB);
+                        if (EPI == PF_SWIGLU_F16) {
+                            tma_load_4d(dst, &wmap, 0, 0, c, tile0, &q_full[q_slot]);
+                            tma_load_4d(dst + (BN / 32) * BB, &wmap2, 0, 0, c, tile0, &q_full[q_slot]);
+                        } else {
+                            tma_load_4d(dst, &wmap, 0, 0, c, tile0, &q_full[q_slot]);
                         }
                         ++q_fill;
                         if (++q_slot == kPfSQ) { q_slot = 0; q_ph ^= 1; }

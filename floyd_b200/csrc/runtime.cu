@@ -175,6 +175,7 @@ struct FcSession {
     int *pf_route_ids = nullptr, *pf_counts = nullptr, *pf_offsets = nullptr, *pf_cursor = nullptr;
     int *pf_slot_of = nullptr, *pf_mt_count = nullptr;
     int4 *pf_mt_table = nullptr;
+    std::map<std::pair<const void *, int>, CUtensorMap> pf_wmaps;  // weight maps by (base, box tiles)
     CUtensorMap pf_map_x{}, pf_map_q{}, pf_map_qa{}, pf_map_o{}, pf_map_hd{}, pf_map_hs{}, pf_map_xg{},
         pf_map_hg{}, pf_map_kvd{}, pf_cmap{}, pf_cmap64{};
     std::vector<std::string> prof_marks;
@@ -527,7 +528,7 @@ cudaError_t gemv1(int fmt, GemvSeg a, int S, float limit, int *err, int sms, cud
 
 // 2-D fp16 tensor map [rows][inner] with a {64, box_rows} box and the
 // 128-byte swizzle the tcgen05 descriptors expect.
-bool make_map_f16(CUtensorMap *map, void *base, uint64_t inner, uint64_t rows, uint32_t box_rows) {
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     static PFN_cuTensorMapEncodeTiled_v12000 encode = [] {
         void *fn = nullptr;
         cudaDriverEntryPointQueryResult q{};
@@ -536,6 +537,11 @@ bool make_map_f16(CUtensorMap *map, void *base, uint64_t inner, uint64_t rows, u
             fn = nullptr;
         return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
     }();
+    return encode;
+}
+
+bool make_map_f16(CUtensorMap *map, void *base, uint64_t inner, uint64_t rows, uint32_t box_rows) {
+    PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
     if (!encode) return false;
     cuuint64_t dims[2] = {inner, rows};
     cuuint64_t strides[1] = {inner * 2};
@@ -543,6 +549,23 @@ bool make_map_f16(CUtensorMap *map, void *base, uint64_t inner, uint64_t rows, u
     cuuint32_t estr[2] = {1, 1};
     return encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, base, dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// 4-D byte tensor map of a tile-major quantized matrix family (`tiles`
+// 16-row tiles of padded width kp): [tiles][chunks][block_bytes / 64][64],
+// box {64, block_bytes / 64, 1, box_tiles} - one chunk block of box_tiles
+// consecutive tiles, landing in shared memory as consecutive blocks.
+bool make_map_weights(CUtensorMap *map, const uint8_t *w, int fmt, uint64_t tiles, int kp, uint32_t box_tiles) {
+    PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
+    if (!encode) return false;
+    const uint64_t bb = (uint64_t)block_bytes(fmt);
+    cuuint64_t dims[4] = {64, bb / 64, (cuuint64_t)chunk_count(fmt, kp), tiles};
+    cuuint64_t strides[3] = {64, bb, (cuuint64_t)tile_bytes(fmt, kp)};
+    cuuint32_t box[4] = {64, (cuuint32_t)(bb / 64), 1, box_tiles};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    return encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<uint8_t *>(w), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -1054,20 +1077,47 @@ cudaError_t pf_prepare_all() {
 }
 
 // One tcgen05 GEMM launch (one CTA per SM) of weight format `fmt`.
-cudaError_t pf_gemm(int fmt, int epi, const CUtensorMap &map, const PfGemm &p, int sms, cudaStream_t st) {
+cudaError_t pf_gemm(int fmt, int epi, const CUtensorMap &map, const CUtensorMap &wmap, const CUtensorMap &wmap2,
+                    const PfGemm &p, int sms, cudaStream_t st) {
     constexpr int bn = 256;
 #define FC_PF_CASE(F, BN, EPI)                                                                       \
     if (fmt == F && bn == BN && epi == EPI)                                                          \
-        return launch_pdl(pf_gemm_kernel<F, BN, EPI>, dim3(sms), dim3(kPfThreads), PfPlan<BN>::SMEM, st, map, p);
+        return launch_pdl(pf_gemm_kernel<F, BN, EPI>, dim3(sms), dim3(kPfThreads), PfPlan<BN>::SMEM, st, map, \
+                          wmap, wmap2, p);
     FC_PF_ALL(FC_PF_CASE)
 #undef FC_PF_CASE
     return cudaErrorInvalidValue;
 }
 
-// A GEMM of matrix `mm` (group stride w_gstride) over `rows` rows of the A map.
+// The weight tensor map of a matrix family for boxes of box_tiles tiles
+// (cached per session; the weights never move).
+const CUtensorMap *pf_wmap(FcSession *s, const DevMat &mm, int box_tiles) {
+    auto key = std::make_pair((const void *)mm.w, box_tiles);
+    auto it = s->pf_wmaps.find(key);
+    if (it != s->pf_wmaps.end()) return &it->second;
+    CUtensorMap map{};
+    const uint64_t tiles = (uint64_t)std::max(mm.count, 1) * (uint64_t)((mm.O + kTileRows - 1) / kTileRows);
+    if (!make_map_weights(&map, mm.w, mm.fmt, tiles, mm.kp, (uint32_t)box_tiles)) return nullptr;
+    return &(s->pf_wmaps[key] = map);
+}
+
+// Launches the prefill GEMM of matrix `w` (and the up rows `w2` for SwiGLU).
+cudaError_t pf_gemm_w(FcSession *s, int epi, const CUtensorMap &amap, const DevMat &w, const DevMat *w2,
+                      PfGemm p) {
+    // a box never exceeds the tensor (such a copy would not complete)
+    const int tiles = std::max(w.count, 1) * ((w.O + kTileRows - 1) / kTileRows);
+    const int box = std::min(epi == PF_SWIGLU_F16 ? 8 : 16, tiles);
+    p.box_tiles = box;
+    const CUtensorMap *m1 = pf_wmap(s, w, box);
+    const CUtensorMap *m2 = w2 ? pf_wmap(s, *w2, box) : m1;
+    if (!m1 || !m2) return cudaErrorInvalidValue;
+    return pf_gemm(w.fmt, epi, amap, *m1, *m2, p, s->m->sms, s->stream);
+}
+
+// A GEMM of matrix `mm` over `rows` rows of the A map.
 PfGemm pf_plain(FcSession *s, const DevMat &mm, int rows, void *out, int64_t out_ld) {
     PfGemm p{};
-    p.w = mm.w;
+    p.tiles_per_group = (mm.O + kTileRows - 1) / kTileRows;
     p.kp = mm.kp;
     p.N = mm.O;
     p.K = mm.kp;
@@ -1088,7 +1138,7 @@ cudaError_t record_prefill(FcSession *s, int T) {
     cudaStream_t st = s->stream;
     const int D = c.hidden_size, H = c.head_count, L = c.kv_lora_rank, R = c.qk_rope_dim;
     const int NP = c.qk_nope_dim, VD = c.value_dim, QW = NP + R;
-    const int df = c.dense_format, ef = c.expert_format, sms = m->sms;
+    const int sms = m->sms;
     const float scale = 1.0f / sqrtf((float)(NP + R));
     const int *d_pos = s->pf_ids, *ids = s->pf_ids + 1;
     FC_TRY(launch_pdl(embed_kernel, dim3(T), dim3(256), 0, st, m->embed.fmt, (const uint8_t *)m->embed.w, D,
@@ -1102,20 +1152,20 @@ cudaError_t record_prefill(FcSession *s, int T) {
         mark(s, "pf_rmsnorm");
         if (c.q_lora_rank > 0) {
             PfGemm a = pf_plain(s, y.q_a, T, s->pf_qa, c.q_lora_rank);
-            FC_TRY(pf_gemm(df, PF_STORE_F32, s->pf_map_x, a, sms, st));
+            FC_TRY(pf_gemm_w(s, PF_STORE_F32, s->pf_map_x, y.q_a, nullptr, a));
             FC_TRY(launch_pdl(pf_rmsnorm_kernel, dim3(T), dim3(256), 0, st, (const float *)s->pf_qa, c.q_lora_rank,
                               (const float *)y.q_a_norm.p, c.rms_norm_epsilon, s->pf_qa16, c.q_lora_rank,
                               (float *)nullptr));
             PfGemm b = pf_plain(s, y.q_b, T, s->pf_q16, H * QW);
-            FC_TRY(pf_gemm(df, PF_STORE_F16, s->pf_map_qa, b, sms, st));
+            FC_TRY(pf_gemm_w(s, PF_STORE_F16, s->pf_map_qa, y.q_b, nullptr, b));
         } else {
             PfGemm a = pf_plain(s, y.q_proj, T, s->pf_q16, H * QW);
-            FC_TRY(pf_gemm(df, PF_STORE_F16, s->pf_map_x, a, sms, st));
+            FC_TRY(pf_gemm_w(s, PF_STORE_F16, s->pf_map_x, y.q_proj, nullptr, a));
         }
         mark(s, "pf_gemm_q");
         {
             PfGemm a = pf_plain(s, y.kv_a, T, s->pf_ckv, L + R);
-            FC_TRY(pf_gemm(df, PF_STORE_F32, s->pf_map_x, a, sms, st));
+            FC_TRY(pf_gemm_w(s, PF_STORE_F32, s->pf_map_x, y.kv_a, nullptr, a));
             mark(s, "pf_gemm_kv_a");
         }
         FC_TRY(launch_pdl(pf_prep_kernel, dim3(T, 1 + (H * (R / 2) + 255) / 256), dim3(256), 0, st,
@@ -1127,7 +1177,7 @@ cudaError_t record_prefill(FcSession *s, int T) {
             // = cache_latent[k] . kv_b[h*(nope+v) + j]  (W_UK rows, then W_UV)
             PfGemm a = pf_plain(s, y.kv_b, s->position + T, s->pf_kvd, (int64_t)H * (NP + VD));
             a.a_y0 = l * s->opt.context_size;
-            FC_TRY(pf_gemm(df, PF_STORE_F16, s->pf_cmap, a, sms, st));
+            FC_TRY(pf_gemm_w(s, PF_STORE_F16, s->pf_cmap, y.kv_b, nullptr, a));
             mark(s, "pf_gemm_kv_b");
         }
         {
@@ -1144,7 +1194,7 @@ cudaError_t record_prefill(FcSession *s, int T) {
         }
         {
             PfGemm a = pf_plain(s, y.o_proj, T, s->pf_resid, D);
-            FC_TRY(pf_gemm(df, PF_ADD_F32, s->pf_map_o, a, sms, st));
+            FC_TRY(pf_gemm_w(s, PF_ADD_F32, s->pf_map_o, y.o_proj, nullptr, a));
             mark(s, "pf_gemm_o_proj");
         }
         FC_TRY(launch_pdl(pf_rmsnorm_kernel, dim3(T), dim3(256), 0, st, (const float *)s->pf_resid, D,
@@ -1153,11 +1203,10 @@ cudaError_t record_prefill(FcSession *s, int T) {
         if (y.dense) {
             const int I = c.dense_intermediate_size;
             PfGemm a = pf_plain(s, y.d_gate, T, s->pf_h16, I);
-            a.w2 = y.d_up.w;
-            FC_TRY(pf_gemm(df, PF_SWIGLU_F16, s->pf_map_x, a, sms, st));
+            FC_TRY(pf_gemm_w(s, PF_SWIGLU_F16, s->pf_map_x, y.d_gate, &y.d_up, a));
             mark(s, "pf_gemm_dense_gate_up");
             PfGemm b = pf_plain(s, y.d_down, T, s->pf_resid, D);
-            FC_TRY(pf_gemm(df, PF_ADD_F32, s->pf_map_hd, b, sms, st));
+            FC_TRY(pf_gemm_w(s, PF_ADD_F32, s->pf_map_hd, y.d_down, nullptr, b));
             mark(s, "pf_gemm_dense_down");
             continue;
         }
@@ -1191,28 +1240,24 @@ cudaError_t record_prefill(FcSession *s, int T) {
         mark(s, "pf_route_group");
         {
             PfGemm a = pf_plain(s, y.e_gate, 0, s->pf_hg, I);
-            a.w2 = y.e_up.w;
-            a.w_gstride = (int64_t)y.e_gate.w_bytes;
             a.mt_count = s->pf_mt_count;
             a.mt_table = s->pf_mt_table;
             a.limit = c.swiglu_limit;
-            FC_TRY(pf_gemm(ef, PF_SWIGLU_F16, s->pf_map_xg, a, sms, st));
+            FC_TRY(pf_gemm_w(s, PF_SWIGLU_F16, s->pf_map_xg, y.e_gate, &y.e_up, a));
             mark(s, "pf_gemm_moe_gate_up");
             PfGemm b = pf_plain(s, y.e_down, 0, s->pf_yd, D);
-            b.w_gstride = (int64_t)y.e_down.w_bytes;
             b.mt_count = s->pf_mt_count;
             b.mt_table = s->pf_mt_table;
-            FC_TRY(pf_gemm(ef, PF_STORE_F32, s->pf_map_hg, b, sms, st));
+            FC_TRY(pf_gemm_w(s, PF_STORE_F32, s->pf_map_hg, y.e_down, nullptr, b));
             mark(s, "pf_gemm_moe_down");
         }
         if (y.s_gate.count) {
             const int W = I * c.shared_expert_count;
             PfGemm a = pf_plain(s, y.s_gate, T, s->pf_h16, W);
-            a.w2 = y.s_up.w;
             a.limit = c.swiglu_limit;
-            FC_TRY(pf_gemm(df, PF_SWIGLU_F16, s->pf_map_x, a, sms, st));
+            FC_TRY(pf_gemm_w(s, PF_SWIGLU_F16, s->pf_map_x, y.s_gate, &y.s_up, a));
             PfGemm b = pf_plain(s, y.s_down, T, s->pf_sh, D);
-            FC_TRY(pf_gemm(df, PF_STORE_F32, s->pf_map_hs, b, sms, st));
+            FC_TRY(pf_gemm_w(s, PF_STORE_F32, s->pf_map_hs, y.s_down, nullptr, b));
             mark(s, "pf_gemm_shared");
         }
         FC_TRY(launch_pdl(pf_combine_kernel, dim3(T), dim3(256), 0, st, s->pf_resid, (const float *)s->pf_yd,
@@ -1227,7 +1272,7 @@ cudaError_t record_prefill(FcSession *s, int T) {
     GemvSeg g = seg_of(m->lm_head, s->xq_norm, EPI_STORE);
     g.y = s->logits;
     g.ldy = c.vocab_size;
-    FC_TRY(gemv1(df, g, 1, 0.0f, s->d_err, m->sms, st));
+    FC_TRY(gemv1(c.dense_format, g, 1, 0.0f, s->d_err, m->sms, st));
     mark(s, "pf_lm_head");
     return cudaGetLastError();
 }
@@ -2087,7 +2132,7 @@ int matmul_gemm(int format, float *y, const float *x, const DevMat &mm, const st
         const size_t n = (size_t)S * K;
         to_f16_kernel<<<(unsigned)((n + 255) / 256), 256>>>(dx, n, dx16);
         PfGemm p{};
-        p.w = dw;
+        p.tiles_per_group = (O + kTileRows - 1) / kTileRows;
         p.kp = mm.kp;
         p.N = O;
         p.K = mm.kp;
@@ -2099,7 +2144,11 @@ int matmul_gemm(int format, float *y, const float *x, const DevMat &mm, const st
         int dev = 0, sms = 148;
         cudaGetDevice(&dev);
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        e = pf_gemm(format, PF_STORE_F32, map, p, sms, 0);
+        CUtensorMap wmap{};
+        p.box_tiles = std::min(16, p.tiles_per_group);
+        if (!make_map_weights(&wmap, dw, format, (uint64_t)p.tiles_per_group, mm.kp, (uint32_t)p.box_tiles))
+            e = cudaErrorInvalidValue;
+        else e = pf_gemm(format, PF_STORE_F32, map, wmap, wmap, p, sms, 0);
         if (e == cudaSuccess) e = cudaDeviceSynchronize();
         if (e == cudaSuccess) e = cudaMemcpy(y, dy, (size_t)S * O * 4, cudaMemcpyDeviceToHost);
         if (e == cudaSuccess) e = cudaMemcpy(&herr, derr, 4, cudaMemcpyDeviceToHost);
