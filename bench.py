@@ -52,6 +52,8 @@ def parse():
                     help="configs[2] leg: prompt length of the prefill (0 = skip the leg)")
     ap.add_argument("--prefill-decode", type=int, default=512, help="configs[2] leg: greedy decodes after it")
     ap.add_argument("--prefill-reps", type=int, default=5, help="configs[2] leg: timed prefills")
+    ap.add_argument("--prefill-layers", type=int, default=None,
+                    help="configs[2] leg with fewer layers (a small case of the same kernels, for profilers)")
     ap.add_argument("--prefill-only", action="store_true",
                     help="run only the configs[2] prefill / decode leg and print its JSON")
     ap.add_argument("--layers", type=int, default=None,
@@ -341,6 +343,8 @@ def prefill_leg(args, d):
     from floyd_b200.configs import CONFIGS, prefill_flops
     name = "c3_moonlight_q4"
     cfg = dict(CONFIGS[name])
+    if args.prefill_layers:
+        cfg["layer_count"] = args.prefill_layers
     T, ndec = args.prefill_tokens, args.prefill_decode
     model = floyd_b200.Model(cfg, device=d.local, seed=0)
     sess = floyd_b200.Session(model, T + ndec + 8, T)
@@ -388,7 +392,7 @@ def prefill_leg(args, d):
                 "avg_launch_us": per_ms * 1e3,
                 "measured": "CUDA events between launches on the session stream, one eager profiled prefill"}
     out = {
-        "workload": name, "tokens": T, "reps": args.prefill_reps,
+        "workload": name, "tokens": T, "reps": args.prefill_reps, "layers": cfg["layer_count"],
         "prefill_ms": ms, "prefill_tok_s": T / (ms / 1e3),
         "prefill_e2e_tok_s": T / float(np.median(wall)),
         "prefill_tflops": (fl["linear"] + fl["attention"]) / (ms / 1e3) / 1e12,
