@@ -20,27 +20,50 @@ constexpr int kMaxRows = 8;       // rows per forward pass
 constexpr int kHeadChunk = 2048;  // vocab entries per partial block
 
 // Host -> device per-launch parameters (one H2D copy at the head of a graph).
+// The rows of a pass form `groups` sequence groups of group_rows consecutive
+// rows (one group for an ordinary session); row r sits at position
+// rowpos[r] of sequence rowseq[r], and each group is accepted on its own.
 struct Staging {
     int pos;
     int rows;
-    int k;          // drafts (verify) or -1 (plain forward)
+    int k;          // drafts per group (verify) or -1 (plain forward)
     int mode;       // FcAcceptMode
     float temperature;
     int pad;
     unsigned long long seed;
-    unsigned long long counter;
+    unsigned long long counter;   // Philox counter of group 0
     int ids[kMaxRows];
+    int rowpos[kMaxRows];
+    int rowseq[kMaxRows];
+    int group_rows;
+    int groups;
+    unsigned long long gcounter[kMaxRows];  // Philox counter of each group
 };
 
 // Device -> host results (one D2H copy at the tail of a graph).
 struct Result {
-    int commit;
+    int commit;       // group 0 (the session's sequence)
     int next_token;
     int error;      // error bits raised by kernels of this pass
     int pad;
     int row_tops[kMaxRows];
     int drafts[kMaxRows];   // MTP drafter proposals (verify with k > 0)
+    int g_commit[kMaxRows];
+    int g_next[kMaxRows];
 };
+
+// Latent-cache paging: sequence `seq`'s position p lives at row
+// pt[seq * pps + p / 64] * 64 + p % 64 of a layer's region (64-row pages, so
+// a 64- or 32-key block never straddles two pages).  Ordinary sessions map
+// every page to itself.
+constexpr int kPageRows = 64;
+struct PageMap {
+    const int *pt;
+    int pps;        // pages per sequence
+};
+__device__ __forceinline__ int kv_row(const PageMap &pm, int seq, int p) {
+    return pm.pt[seq * pm.pps + (p >> 6)] * kPageRows + (p & (kPageRows - 1));
+}
 
 __device__ __forceinline__ float accept_uniform(unsigned long long seed, unsigned long long counter,
                                                 int row) {
@@ -86,7 +109,10 @@ __global__ void head_partial_kernel(const float *logits, int V, const Staging *s
     int begin = chunk * kHeadChunk, end = min(V, begin + kHeadChunk);
     bool sample = st->mode == FC_ACCEPT_SAMPLE && st->k >= 0;
     float temp = sample ? st->temperature : 1.0f;
-    int excluded = (sample && row < st->k) ? st->ids[row + 1] : -1;
+    // row index and Philox counter within the row's sequence group
+    const int grp = row / st->group_rows, local = row - grp * st->group_rows;
+    const unsigned long long counter = st->gcounter[grp];
+    int excluded = (sample && local < st->k) ? st->ids[row + 1] : -1;
     float bv = -INFINITY; int bi = 0x7fffffff;
     float zm = -INFINITY;
     float gv = -INFINITY; int gi = 0x7fffffff;
@@ -98,7 +124,7 @@ __global__ void head_partial_kernel(const float *logits, int V, const Staging *s
             float z = x / temp;
             zm = fmaxf(zm, z);
             if (v != excluded) {
-                float t = z + gumbel(st->seed, st->counter, row, v);
+                float t = z + gumbel(st->seed, counter, local, v);
                 if (better(t, v, gv, gi)) { gv = t; gi = v; }
             }
         }
@@ -196,17 +222,21 @@ __global__ void __launch_bounds__(256) accept_kernel(const float *logits, int V,
         }
     }
     __syncthreads();
-    if (threadIdx.x != 0) return;
-    for (int r = 0; r < rows; ++r) res->row_tops[r] = tops[r];
+    if (threadIdx.x >= st->groups) return;
+    // thread g applies the acceptance rule to sequence group g
+    const int g = threadIdx.x, gr = st->group_rows, r0 = g * gr;
+    if (g == 0)
+        for (int r = 0; r < rows; ++r) res->row_tops[r] = tops[r];
     const int k = st->k;
-    int commit = rows, next = tops[rows - 1];
+    const int *ids = st->ids + r0;
+    int commit = gr, next = tops[r0 + gr - 1];
     if (sample) {
         commit = k + 1;
-        next = picks[k];
+        next = picks[r0 + k];
         for (int i = 1; i <= k; ++i) {
-            const int r = i - 1, x = st->ids[i];
+            const int r = r0 + i - 1, x = ids[i];
             float p = expf(logits[(size_t)r * V + x] / st->temperature - zmax_row[r]) / den_row[r];
-            float u = accept_uniform(st->seed, st->counter, r);
+            float u = accept_uniform(st->seed, st->gcounter[g], i - 1);
             if (!(u < p)) {
                 commit = i;
                 next = picks[r];
@@ -216,15 +246,19 @@ __global__ void __launch_bounds__(256) accept_kernel(const float *logits, int V,
     } else if (k >= 0) {
         commit = 1;
         for (int i = 1; i <= k; ++i) {
-            if (tops[i - 1] != st->ids[i]) break;
+            if (tops[r0 + i - 1] != ids[i]) break;
             commit++;
         }
-        next = tops[commit - 1];
+        next = tops[r0 + commit - 1];
     }
-    res->commit = commit;
-    res->next_token = next;
-    res->error = *err;
-    *err = 0;
+    res->g_commit[g] = commit;
+    res->g_next[g] = next;
+    if (g == 0) {
+        res->commit = commit;
+        res->next_token = next;
+        res->error = *err;
+        *err = 0;
+    }
 }
 
 // ---- MTP drafter glue --------------------------------------------------
@@ -241,6 +275,11 @@ __global__ void mtp_prep_kernel(int i, const Staging *main_st, const Result *res
         mst->rows = 1;
         mst->k = -1;
         mst->mode = FC_ACCEPT_GREEDY;
+        mst->rowpos[0] = mst->pos;
+        mst->rowseq[0] = 0;
+        mst->group_rows = 1;
+        mst->groups = 1;
+        mst->gcounter[0] = 0;
         int t = i == 0 ? res->next_token : res->drafts[i - 1];
         mst->ids[0] = t < 0 ? 0 : t;
     }

@@ -20,6 +20,7 @@
 #pragma once
 
 #include "common.cuh"
+#include "head.cuh"
 
 namespace fc {
 
@@ -141,12 +142,13 @@ __device__ __forceinline__ void rope_pair(float first, float second, int p, int 
 // blocks y >= 1 rotate a slice of the heads' query rope pairs.
 __device__ __forceinline__ void mla_prep_block(int bx, int by, const float *ckv, const float *q,
                                                const float *norm_w, int L, int R, int H, int nope, float eps,
-                                               float theta, const int *d_pos, __half *cache, __half *qcat) {
+                                               float theta, const Staging *st, PageMap pm, __half *cache,
+                                               __half *qcat) {
     pdl_wait();
     pdl_release();
     __shared__ float scratch[32];
     const int s = bx;
-    const int position = *d_pos + s;
+    const int position = st->rowpos[s];
     const int half = R / 2;
     if (by == 0) {
         const float *src = ckv + (size_t)s * (L + R);
@@ -154,7 +156,7 @@ __device__ __forceinline__ void mla_prep_block(int bx, int by, const float *ckv,
         for (int i = threadIdx.x; i < L; i += blockDim.x) ss += src[i] * src[i];
         ss = block_sum(ss, scratch);
         float scale = 1.0f / sqrtf(ss / (float)L + eps);
-        __half *dst = cache + (size_t)position * (L + R);
+        __half *dst = cache + (size_t)kv_row(pm, st->rowseq[s], position) * (L + R);
         for (int i = threadIdx.x; i < L; i += blockDim.x)
             dst[i] = __float2half_rn(src[i] * scale * norm_w[i]);
         for (int p = threadIdx.x; p < half; p += blockDim.x) {
@@ -254,11 +256,11 @@ __device__ __forceinline__ void mla_absorb_block(int bx, int by, int fmt, const 
 // kv_a outputs, so neither waits for the other.
 __global__ void __launch_bounds__(256)
 mla_prep_absorb_kernel(const float *ckv, const float *q, const float *norm_w, int L, int R, int H, int nope,
-                       float eps, float theta, const int *d_pos, __half *cache, __half *qcat, int S, int prep_y,
-                       int fmt, const uint8_t *w, int kp, int vdim) {
+                       float eps, float theta, const Staging *st, PageMap pm, __half *cache, __half *qcat, int S,
+                       int prep_y, int fmt, const uint8_t *w, int kp, int vdim) {
     const int b = blockIdx.x, n_prep = S * prep_y;
     if (b < n_prep) {
-        mla_prep_block(b / prep_y, b % prep_y, ckv, q, norm_w, L, R, H, nope, eps, theta, d_pos, cache, qcat);
+        mla_prep_block(b / prep_y, b % prep_y, ckv, q, norm_w, L, R, H, nope, eps, theta, st, pm, cache, qcat);
     } else {
         const int a = b - n_prep, cols = L / kAbsorbCols;
         mla_absorb_block(a / cols, a % cols, fmt, w, kp, q, S, H, nope, vdim, R, L, qcat);
@@ -316,7 +318,7 @@ struct AttnSmem {
 template <int L, int R>
 __global__ void __launch_bounds__(kAttnThreads, 1)
 mla_attention_kernel(const __half *cache, const __half *qcat, int S, int H, int chunks_per_split,
-                     const int *d_pos, float softmax_scale, float *part_o, float *part_m,
+                     const Staging *st, PageMap pm, float softmax_scale, float *part_o, float *part_m,
                      float *part_l) {
     pdl_wait();
     pdl_release();
@@ -339,8 +341,9 @@ mla_attention_kernel(const __half *cache, const __half *qcat, int S, int H, int 
     const int g = lane >> 2, j = lane & 3;
     const int nq = S * H;
     const int q0 = blockIdx.x * kAttnQ;
-    const int pos = *d_pos;
-    const int total_keys = pos + S;  // keys 0 .. pos+S-1 exist
+    // the tile's rows belong to one sequence; keys up to its last row's position
+    const int seq = st->rowseq[q0 / H];
+    const int total_keys = st->rowpos[(min(q0 + kAttnQ, nq) - 1) / H] + 1;
     const int chunk0 = blockIdx.y * chunks_per_split;
     int chunk1 = chunk0 + chunks_per_split;
     const int last_chunk = (total_keys + kAttnKeys - 1) / kAttnKeys;
@@ -359,6 +362,7 @@ mla_attention_kernel(const __half *cache, const __half *qcat, int S, int H, int 
     auto load_chunk = [&](int chunk, int buf) {
         __half *dst = Ks + buf * kAttnKeys * ST;
         int base = chunk * kAttnKeys;
+        const __half *src = cache + (size_t)kv_row(pm, seq, base) * DW;  // one 64-row page
         // 16-byte pieces i = tid + n * threads of the [keys][DW/8] tile;
         // (row, column) advance incrementally instead of by division
         constexpr int kCols = DW / 8;
@@ -367,8 +371,7 @@ mla_attention_kernel(const __half *cache, const __half *qcat, int S, int H, int 
 #pragma unroll 4
         for (int i = tid; i < kAttnKeys * kCols; i += kAttnThreads) {
             bool ok = base + r < total_keys;
-            cp_async16(dst + r * ST + c8 * 8,
-                       cache + (size_t)(ok ? base + r : 0) * DW + c8 * 8, ok);
+            cp_async16(dst + r * ST + c8 * 8, src + (size_t)(ok ? r : 0) * DW + c8 * 8, ok);
             r += kStepR;
             c8 += kStepC;
             if (c8 >= kCols) { c8 -= kCols; ++r; }
@@ -390,7 +393,7 @@ mla_attention_kernel(const __half *cache, const __half *qcat, int S, int H, int 
 #pragma unroll
     for (int h2 = 0; h2 < 2; ++h2) {
         int q = q0 + 16 * mt + g + 8 * h2;
-        row_limit[h2] = q < nq ? pos + q / H : -1;  // key <= limit is visible
+        row_limit[h2] = q < nq ? st->rowpos[q / H] : -1;  // key <= limit is visible
     }
 
     for (int chunk = chunk0; chunk < chunk1; ++chunk) {

@@ -28,6 +28,7 @@
 #include <cuda.h>
 
 #include "common.cuh"
+#include "head.cuh"
 
 namespace fc {
 
@@ -188,7 +189,7 @@ struct TcAttnPlan {
 template <int L>
 __global__ void __launch_bounds__(kTcThreads, 1)
 mla_attention_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kvmap,
-                        int kv_row0, int S, int H, int keys_per_split, const int *d_pos,
+                        int kv_row0, int S, int H, int keys_per_split, const Staging *st, PageMap pm,
                         float softmax_scale, float *part_o, float *part_m, float *part_l, int *err) {
     using P = TcAttnPlan<L>;
     extern __shared__ uint8_t tc_smem_raw[];
@@ -231,8 +232,10 @@ mla_attention_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_c
     pdl_release();
     if (tid == 0) TC_MARK(1);
 
-    // keys up to the last query row of this tile (causal: key <= pos + row)
-    const int pos = *d_pos, nq = S * H, total = pos + min(q0 + kTcRows, nq) / H + ((min(q0 + kTcRows, nq) % H) != 0);
+    // the tile's rows belong to one sequence; keys up to its last row's
+    // position (causal: key <= that row's position)
+    const int nq = S * H, seq = st->rowseq[q0 / H];
+    const int total = st->rowpos[(min(q0 + kTcRows, nq) - 1) / H] + 1;
     const int k0 = split * keys_per_split;
     const int k1 = min(k0 + keys_per_split, total);
     const int nblk = k1 > k0 ? (k1 - k0 + kTcKeys - 1) / kTcKeys : 0;
@@ -244,13 +247,14 @@ mla_attention_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_c
             mbar_expect_tx(q_full, P::Q_BYTES);
             for (int kb = 0; kb < P::NKB; ++kb) tma_load_2d(Qs + kb * kTcRows * 128, &qmap, kb * 64, q0, q_full);
             for (int j = 0; j < nblk; ++j) {
-                const int st = j & 1;
-                if (j >= 2) mbar_wait_timed(&kv_empty[st], (uint32_t)(((j - 2) >> 1) & 1), err, 1);
+                const int stg = j & 1;
+                if (j >= 2) mbar_wait_timed(&kv_empty[stg], (uint32_t)(((j - 2) >> 1) & 1), err, 1);
                 TC_MARK(136 + j);
-                mbar_expect_tx(&kv_full[st], P::K_BYTES);
-                uint8_t *dst = Ks + st * P::K_BYTES;
+                mbar_expect_tx(&kv_full[stg], P::K_BYTES);
+                uint8_t *dst = Ks + stg * P::K_BYTES;
                 for (int kb = 0; kb < P::NKB; ++kb)
-                    tma_load_2d(dst + kb * kTcKeys * 128, &kvmap, kb * 64, kv_row0 + k0 + j * kTcKeys, &kv_full[st]);
+                    tma_load_2d(dst + kb * kTcKeys * 128, &kvmap, kb * 64, kv_row0 + kv_row(pm, seq, k0 + j * kTcKeys),
+                                &kv_full[stg]);
             }
         }
     } else if (warp == 1) {
@@ -262,8 +266,8 @@ mla_attention_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_c
             mbar_wait_timed(q_full, 0, err, 0);
             TC_MARK(2);
             auto issue_scores = [&](int j) {
-                const int st = j & 1;
-                const uint32_t kst = ka + st * P::K_BYTES;
+                const int stg = j & 1;
+                const uint32_t kst = ka + stg * P::K_BYTES;
                 for (int kb = 0; kb < P::NKB; ++kb)
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk) {
@@ -271,9 +275,9 @@ mla_attention_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_c
                         // the k-th 16-column step starts 32 B further into the row
                         uint64_t a = smem_desc(qa + kb * kTcRows * 128 + kk * 32, 16, 1024, kSmemLayoutSw128);
                         uint64_t b = smem_desc(kst + kb * kTcKeys * 128 + kk * 32, 16, 1024, kSmemLayoutSw128);
-                        tc_mma_f16(tS + st * kTcKeys, a, b, idS, (kb | kk) != 0);
+                        tc_mma_f16(tS + stg * kTcKeys, a, b, idS, (kb | kk) != 0);
                     }
-                tc_commit(&s_full[st]);
+                tc_commit(&s_full[stg]);
             };
             // scores of block k can go once its keys have landed and the
             // softmax has read the score buffer's previous block (k - 2)
@@ -325,20 +329,20 @@ mla_attention_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_c
         const int row = tid - 128;                      // == 32 * (warp & 3) + lane
         const uint32_t lane_off = (uint32_t)(32 * (warp & 3)) << 16;
         const int q = q0 + row;
-        const int limit = q < nq ? pos + q / H : -1;    // key <= limit is visible
+        const int limit = q < nq ? st->rowpos[q / H] : -1;  // key <= limit is visible
         const float scale2 = softmax_scale * 1.4426950408889634f;  // log2(e)
         float m_run = -INFINITY, l_run = 0.0f;                      // log2 domain
         for (int j = 0; j < nblk; ++j) {
-            const int st = j & 1;
-            mbar_wait_timed(&s_full[st], (uint32_t)((j >> 1) & 1), err, 5);
+            const int stg = j & 1;
+            mbar_wait_timed(&s_full[stg], (uint32_t)((j >> 1) & 1), err, 5);
             if (row == 0) TC_MARK(72 + j);
             __syncwarp();  // tcgen05.ld is warp-collective
             tc_fence_after();
             float sv[32];
-            tmem_ld32(tS + st * kTcKeys + lane_off, sv);
+            tmem_ld32(tS + stg * kTcKeys + lane_off, sv);
             tmem_wait_ld();
             tc_fence_before();
-            mbar_arrive_cta(&s_free[st]);
+            mbar_arrive_cta(&s_free[stg]);
             // scores in the log2 domain: s2 = score * scale * log2(e)
             const int nvis = min(max(limit - (k0 + j * kTcKeys) + 1, 0), kTcKeys);
             float mb = -INFINITY;

@@ -117,6 +117,15 @@ struct FcSession {
     int rows_max = 0;        // rows per pass (<= kMaxRows)
     int position = 0;
     int last_rows = 0;
+    // latent-cache paging (head.cuh PageMap): page table [sequences][pps] on
+    // the device; an ordinary session maps each page to itself
+    int *page_table = nullptr;
+    PageMap pmap{};
+    int layer_rows = 0;      // cache rows per layer
+    int n_seq = 1;           // sequences (batch sessions)
+    int group_rows = 0;      // rows per sequence in a batch pass (1 + drafts)
+    int shared_rows = 0;     // leading positions every sequence shares (batch sessions)
+    std::vector<int> seq_pos;  // position of each sequence (batch sessions)
     int max_slots = 0;
     int splits = 0, chunks_per_split = 1;
     bool attn_tc = true;     // tcgen05 attention (else the mma.sync kernel)
@@ -583,7 +592,7 @@ void mark(FcSession *s, const char *name) {
 // Enqueues layer l (target layers 0 .. layer_count - 1, the MTP layer at
 // layer_count) for S rows at positions *d_pos + s, updating s->resid.
 // `ids` are the rows' token ids (hash routing).
-cudaError_t record_layer(FcSession *s, int S, int l, const int *d_pos, const int *ids) {
+cudaError_t record_layer(FcSession *s, int S, int l, const Staging *dst) {
     FcModel *m = s->m;
     const FcModelConfig &c = m->c;
     cudaStream_t st = s->stream;
@@ -597,7 +606,7 @@ cudaError_t record_layer(FcSession *s, int S, int l, const int *d_pos, const int
     (void)kpO;
     (void)ef;
     DevLayer &y = m->layers[l];
-    __half *cache = s->cache + (size_t)l * s->opt.context_size * (L + R);
+    __half *cache = s->cache + (size_t)l * s->layer_rows * (L + R);
     FC_TRY(launch_pdl(rmsnorm_kernel, dim3(S), dim3(norm_threads(D)), 0, st, s->resid, D, y.attn_norm.p, D, c.rms_norm_epsilon,
                                       s->xq_norm, kpD, nullptr, 0));
     mark(s, "rmsnorm");
@@ -637,20 +646,20 @@ cudaError_t record_layer(FcSession *s, int S, int l, const int *d_pos, const int
         const int blocks = S * prep_y + H * (L / kAbsorbCols);
         FC_TRY(launch_pdl(mla_prep_absorb_kernel, dim3(blocks), dim3(256), 0, st, (const float *)s->ckv,
                           (const float *)s->q, (const float *)y.kv_a_norm.p, L, R, H, NP, c.rms_norm_epsilon,
-                          c.rope_theta, d_pos, cache, s->qcat, S, prep_y, df, (const uint8_t *)y.kv_b.w,
+                          c.rope_theta, dst, s->pmap, cache, s->qcat, S, prep_y, df, (const uint8_t *)y.kv_b.w,
                           y.kv_b.kp, VD));
         mark(s, "mla_prep_absorb");
     }
     if (s->attn_tc) {
         dim3 grid((S * H + kTcRows - 1) / kTcRows, 2, s->splits);
-        const int kv_row0 = l * s->opt.context_size, kps = s->chunks_per_split * kAttnKeys;
+        const int kv_row0 = l * s->layer_rows, kps = s->chunks_per_split * kAttnKeys;
         if (L == 512)
             FC_TRY(launch_pdl(mla_attention_tc_kernel<512>, grid, dim3(kTcThreads), TcAttnPlan<512>::SMEM, st,
-                              s->qmap, s->kvmap, kv_row0, S, H, kps, d_pos, scale, s->part_o, s->part_m,
+                              s->qmap, s->kvmap, kv_row0, S, H, kps, dst, s->pmap, scale, s->part_o, s->part_m,
                               s->part_l, s->d_err));
         else
             FC_TRY(launch_pdl(mla_attention_tc_kernel<256>, grid, dim3(kTcThreads), TcAttnPlan<256>::SMEM, st,
-                              s->qmap, s->kvmap, kv_row0, S, H, kps, d_pos, scale, s->part_o, s->part_m,
+                              s->qmap, s->kvmap, kv_row0, S, H, kps, dst, s->pmap, scale, s->part_o, s->part_m,
                               s->part_l, s->d_err));
         mark(s, "mla_attention");
     } else {
@@ -658,11 +667,11 @@ cudaError_t record_layer(FcSession *s, int S, int l, const int *d_pos, const int
         if (L == 512)
             FC_TRY(launch_pdl(mla_attention_kernel<512, 64>, grid, dim3(kAttnThreads), s->attn_smem,
                               st, (const __half *)cache, (const __half *)s->qcat, S, H,
-                              s->chunks_per_split, d_pos, scale, s->part_o, s->part_m, s->part_l));
+                              s->chunks_per_split, dst, s->pmap, scale, s->part_o, s->part_m, s->part_l));
         else
             FC_TRY(launch_pdl(mla_attention_kernel<256, 64>, grid, dim3(kAttnThreads), s->attn_smem,
                               st, (const __half *)cache, (const __half *)s->qcat, S, H,
-                              s->chunks_per_split, d_pos, scale, s->part_o, s->part_m, s->part_l));
+                              s->chunks_per_split, dst, s->pmap, scale, s->part_o, s->part_m, s->part_l));
         mark(s, "mla_attention");
     }
     {
@@ -720,7 +729,7 @@ cudaError_t record_layer(FcSession *s, int S, int l, const int *d_pos, const int
         rp.routed_scale = c.routed_scale;
         rp.bias = y.bias.p;
         rp.hash = y.hash;
-        rp.ids = ids;
+        rp.ids = dst->ids;
         rp.expert_lo = m->expert_lo;
         rp.expert_hi = m->expert_hi;
         rp.route_ids = s->route_ids + (size_t)l * mb * K;
@@ -834,7 +843,6 @@ cudaError_t record_forward(FcSession *s, int S, int drafts) {
     const FcModelConfig &c = m->c;
     cudaStream_t st = s->stream;
     const int D = c.hidden_size, kpD = kpad(D);
-    const int *d_pos = &s->d_stage->pos;
     const int df = c.dense_format;
 
     FC_TRY(cudaMemcpyAsync(s->d_stage, s->h_stage, sizeof(Staging), cudaMemcpyHostToDevice, st));
@@ -842,7 +850,7 @@ cudaError_t record_forward(FcSession *s, int S, int drafts) {
                                     s->resid));
     FC_TRY(cudaGetLastError());
     mark(s, "embed");
-    for (int l = 0; l < c.layer_count; ++l) FC_TRY(record_layer(s, S, l, d_pos, s->d_stage->ids));
+    for (int l = 0; l < c.layer_count; ++l) FC_TRY(record_layer(s, S, l, s->d_stage));
     FC_TRY(launch_pdl(rmsnorm_kernel, dim3(S), dim3(norm_threads(D)), 0, st, s->resid, D, m->final_norm.p, D, c.rms_norm_epsilon,
                                       s->xq_norm, kpD, nullptr, 0));
     mark(s, "rmsnorm");
@@ -895,7 +903,7 @@ cudaError_t record_mtp_step(FcSession *s, int i) {
         FC_TRY(gemv1(df, g, 1, 0.0f, s->d_err, m->sms, st));
     }
     mark(s, "mtp_input");
-    FC_TRY(record_layer(s, 1, lm, &s->d_mtp->pos, s->d_mtp->ids));
+    FC_TRY(record_layer(s, 1, lm, s->d_mtp));
     FC_TRY(cudaMemcpyAsync(s->mtp_h, s->resid, (size_t)D * 4, cudaMemcpyDeviceToDevice, st));
     FC_TRY(launch_pdl(rmsnorm_kernel, dim3(1), dim3(norm_threads(D)), 0, st, (const float *)s->resid, D,
                       (const float *)y.head_norm.p, D, c.rms_norm_epsilon, s->xq_norm, kpD, (float *)nullptr, 0));
@@ -1005,7 +1013,14 @@ int run_pass(FcSession *s, const int *ids, int rows, int k, const FcAcceptConfig
     st->temperature = accept ? accept->temperature : 1.0f;
     st->seed = accept ? accept->seed : 0;
     st->counter = accept ? accept->counter : 0;
-    for (int i = 0; i < rows; ++i) st->ids[i] = ids[i];
+    for (int i = 0; i < rows; ++i) {
+        st->ids[i] = ids[i];
+        st->rowpos[i] = s->position + i;
+        st->rowseq[i] = 0;
+    }
+    st->group_rows = rows;
+    st->groups = 1;
+    st->gcounter[0] = st->counter;
     // the drafter runs after a verify (k > 0) of a model with an MTP layer
     const int drafts = (s->m->c.mtp_layers > 0 && k > 0) ? k : 0;
     cudaSetDevice(s->m->device);
@@ -1650,7 +1665,17 @@ int fc_session_create(FcSession **out, FcModel *m, const FcOptions *options, cha
     bool ok = cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking) == cudaSuccess;
     ok = ok && cudaEventCreate(&s->ev_begin) == cudaSuccess && cudaEventCreate(&s->ev_end) == cudaSuccess;
     const int NLc = c.layer_count + c.mtp_layers;  // cache layers (target + drafter)
+    s->layer_rows = options->context_size;
     ok = ok && salloc(s, s->cache, (size_t)NLc * options->context_size * (L + R));
+    {
+        const int pps = (options->context_size + kPageRows - 1) / kPageRows;
+        std::vector<int> ident(pps);
+        for (int p = 0; p < pps; ++p) ident[p] = p;
+        ok = ok && salloc(s, s->page_table, (size_t)pps) &&
+             cudaMemcpy(s->page_table, ident.data(), (size_t)pps * sizeof(int), cudaMemcpyHostToDevice) == cudaSuccess;
+        s->pmap.pt = s->page_table;
+        s->pmap.pps = pps;
+    }
     ok = ok && salloc(s, s->resid, (size_t)mb * D) && salloc(s, s->xn, (size_t)mb * D);
     ok = ok && salloc(s, s->xq_norm, (size_t)mb * kpad(D) * 2);
     ok = ok && salloc(s, s->q, (size_t)mb * H * QW);
@@ -1968,7 +1993,7 @@ int fc_session_seed_context(FcSession *s, int positions, uint64_t seed, char *er
     cudaSetDevice(s->m->device);
     int L = c.kv_lora_rank, R = c.qk_rope_dim;
     for (int l = 0; l < c.layer_count && positions > 0; ++l) {
-        __half *cache = s->cache + (size_t)l * s->opt.context_size * (L + R);
+        __half *cache = s->cache + (size_t)l * s->layer_rows * (L + R);
         synth_kv_kernel<<<grid_for((size_t)positions * (L + R)), 256, 0, s->stream>>>(
             cache, positions, L, R, seed, fc_tensor_id(l, FC_T_KV_LATENT, 0),
             fc_tensor_id(l, FC_T_KV_ROPE, 0));
@@ -1990,7 +2015,7 @@ int fc_test_copy_kv(const FcSession *s, int layer, float *latent, float *rope, i
     const FcModelConfig &c = s->m->c;
     int L = c.kv_lora_rank, R = c.qk_rope_dim, P = s->position;
     std::vector<__half> h((size_t)P * (L + R));
-    if (P && cudaMemcpy(h.data(), s->cache + (size_t)layer * s->opt.context_size * (L + R),
+    if (P && cudaMemcpy(h.data(), s->cache + (size_t)layer * s->layer_rows * (L + R),
                         h.size() * 2, cudaMemcpyDeviceToHost) != cudaSuccess)
         return 0;
     for (int p = 0; p < P; ++p) {
