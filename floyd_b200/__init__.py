@@ -16,10 +16,10 @@ import numpy as np
 from . import _lib
 from ._lib import (ACCEPT_GREEDY, ACCEPT_SAMPLE, FMT_F32, FMT_MXFP4, FMT_Q4, FMT_Q8,
                    SCORE_SIGMOID, SCORE_SOFTMAX, SCORE_SQRT_SOFTPLUS, FcAcceptConfig,
-                   FcModelConfig, FcOptions)
+                   FcModelConfig, FcOptions, FcBatchOptions)
 from .configs import CONFIGS, model_fields, scaled, step_bytes
 
-__all__ = ["Model", "Session", "FloydError", "CONFIGS", "blocks_to_logical", "BLOCKS_Q8_0", "BLOCKS_MXFP4", "model_fields", "scaled", "step_bytes",
+__all__ = ["Model", "Session", "BatchSession", "FloydError", "CONFIGS", "blocks_to_logical", "BLOCKS_Q8_0", "BLOCKS_MXFP4", "model_fields", "scaled", "step_bytes",
            "FMT_F32", "FMT_Q8", "FMT_Q4", "FMT_MXFP4", "ACCEPT_GREEDY", "ACCEPT_SAMPLE",
            "SCORE_SOFTMAX", "SCORE_SIGMOID", "SCORE_SQRT_SOFTPLUS", "lib"]
 
@@ -307,3 +307,52 @@ class Session:
             self.close()
         except Exception:
             pass
+class BatchSession(Session):
+    """Several sequences over one paged latent cache (fc_session_create_batch):
+    a shared prefix, private pages per sequence, and one verify of
+    rows_per_sequence rows for every sequence per verify_batch call."""
+
+    def __init__(self, model, context_size, sequences, rows_per_sequence, shared_prefix=0):
+        self._lib = model._lib
+        self.model = model
+        self.vocab = model.config["vocab_size"]
+        self.sequences = sequences
+        self.rows = rows_per_sequence
+        opt = FcBatchOptions(context_size, sequences, rows_per_sequence, shared_prefix)
+        handle = ctypes.c_void_p()
+        err = _err()
+        if not self._lib.fc_session_create_batch(ctypes.byref(handle), model.handle, ctypes.byref(opt), err,
+                                                 len(err)):
+            raise FloydError(err.value.decode())
+        self.handle = handle
+
+    def seed(self, sequence, start, end, seed):
+        err = _err()
+        self._check(self._lib.fc_session_batch_seed(self.handle, sequence, start, end, ctypes.c_uint64(seed),
+                                                    err, len(err)), err)
+
+    def verify_batch(self, ids, accept=None):
+        """ids: [sequences][rows_per_sequence]; accept: None (greedy) or one
+        (mode, temperature, seed, counter) per sequence.  Returns
+        (n_emitted list, next_token list)."""
+        ids = np.ascontiguousarray(ids, dtype=np.int32).reshape(self.sequences, self.rows)
+        acc = None
+        if accept is not None:
+            acc = (FcAcceptConfig * self.sequences)(*[FcAcceptConfig(*a) for a in accept])
+        n = np.zeros(self.sequences, dtype=np.int32)
+        nxt = np.zeros(self.sequences, dtype=np.int32)
+        err = _err()
+        ip = ctypes.POINTER(ctypes.c_int)
+        self._check(self._lib.fc_session_verify_batch(
+            self.handle, ids.ctypes.data_as(ip), self.rows - 1, acc, n.ctypes.data_as(ip), nxt.ctypes.data_as(ip),
+            err, len(err)), err)
+        return n.tolist(), nxt.tolist()
+
+    def position_of(self, sequence):
+        return int(self._lib.fc_session_batch_position(self.handle, sequence))
+
+    def rollback_seq(self, sequence, position):
+        err = _err()
+        self._check(self._lib.fc_session_batch_rollback(self.handle, sequence, int(position), err, len(err)), err)
+
+

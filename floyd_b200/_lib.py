@@ -50,6 +50,11 @@ class FcOptions(ctypes.Structure):
     _fields_ = [("context_size", ctypes.c_int), ("max_batch", ctypes.c_int)]
 
 
+class FcBatchOptions(ctypes.Structure):
+    _fields_ = [("context_size", ctypes.c_int), ("sequences", ctypes.c_int),
+                ("rows_per_sequence", ctypes.c_int), ("shared_prefix", ctypes.c_int)]
+
+
 class FcStats(ctypes.Structure):
     _fields_ = [
         ("command_buffers", ctypes.c_uint64), ("prefill_tokens", ctypes.c_uint64),
@@ -91,6 +96,11 @@ SIGNATURES = {
     "fc_device_name": (_C, [_P]),
     "fc_model_info": (FcModelConfig, [_P]),
     "fc_session_create": (_I, [ctypes.POINTER(_P), _P, ctypes.POINTER(FcOptions), _C, _S]),
+    "fc_session_create_batch": (_I, [ctypes.POINTER(_P), _P, ctypes.POINTER(FcBatchOptions), _C, _S]),
+    "fc_session_batch_seed": (_I, [_P, _I, _I, _I, ctypes.c_uint64, _C, _S]),
+    "fc_session_verify_batch": (_I, [_P, _IP, _I, ctypes.POINTER(FcAcceptConfig), _IP, _IP, _C, _S]),
+    "fc_session_batch_position": (_I, [_P, _I]),
+    "fc_session_batch_rollback": (_I, [_P, _I, _I, _C, _S]),
     "fc_session_destroy": (None, [_P]),
     "fc_session_reset": (None, [_P]),
     "fc_session_position": (_I, [_P]),

@@ -126,6 +126,7 @@ struct FcSession {
     int group_rows = 0;      // rows per sequence in a batch pass (1 + drafts)
     int shared_rows = 0;     // leading positions every sequence shares (batch sessions)
     std::vector<int> seq_pos;  // position of each sequence (batch sessions)
+    bool batch = false;      // created by fc_session_create_batch
     int max_slots = 0;
     int splits = 0, chunks_per_split = 1;
     bool attn_tc = true;     // tcgen05 attention (else the mma.sync kernel)
@@ -1000,6 +1001,8 @@ void collect_profile(FcSession *s) {
 }
 
 // Runs one forward pass of `rows` <= rows_max tokens at the session position.
+int exec_pass(FcSession *s, int rows, int drafts, char *err, size_t n);
+
 int run_pass(FcSession *s, const int *ids, int rows, int k, const FcAcceptConfig *accept,
              char *err, size_t n) {
     if (s->m->world > 1 && !s->ep_connected)
@@ -1023,6 +1026,12 @@ int run_pass(FcSession *s, const int *ids, int rows, int k, const FcAcceptConfig
     st->gcounter[0] = st->counter;
     // the drafter runs after a verify (k > 0) of a model with an MTP layer
     const int drafts = (s->m->c.mtp_layers > 0 && k > 0) ? k : 0;
+    return exec_pass(s, rows, drafts, err, n);
+}
+
+// Runs the pass whose parameters are in h_stage: the captured graph for
+// (rows, drafts), or an eager profiled pass.
+int exec_pass(FcSession *s, int rows, int drafts, char *err, size_t n) {
     cudaSetDevice(s->m->device);
     cudaError_t e;
     if (s->profiling) {
@@ -1322,6 +1331,50 @@ int run_prefill_chunk(FcSession *s, const int *ids, int T, char *err, size_t n) 
     return 1;
 }
 
+// Synthetic latent KV (synth_kv_kernel's values, by logical position) for
+// positions [start, end) of sequence `seq`, written through the page table.
+__global__ void synth_kv_range_kernel(__half *cache, PageMap pm, int seq, int start, int end, int L, int R,
+                                      uint64_t seed, uint32_t tid_latent, uint32_t tid_rope) {
+    const size_t total = (size_t)(end - start) * (L + R);
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const size_t p = (size_t)start + i / (L + R);
+        const int c = (int)(i % (L + R));
+        const float v = c < L ? fc_synth_kv(seed, tid_latent, p * L + c) : fc_synth_kv(seed, tid_rope, p * R + (c - L));
+        cache[(size_t)kv_row(pm, seq, (int)p) * (L + R) + c] = __float2half_rn(v);
+    }
+}
+
+// One device pass of the batch verify: sequences seqs[0 .. ng) with their
+// rows ids[j * group_rows ..] at their own positions; no drafter.
+int run_batch_pass(FcSession *s, const int *seqs, int ng, const int *ids, int k, const FcAcceptConfig *accept,
+                   char *err, size_t n) {
+    if (s->m->world > 1 && !s->ep_connected)
+        return set_error(err, n, "expert-parallel session is not connected (fc_session_ep_connect)");
+    const int gr = s->group_rows, rows = ng * gr;
+    Staging *st = s->h_stage;
+    memset(st, 0, sizeof(*st));
+    const FcAcceptConfig *a0 = accept ? &accept[seqs[0]] : nullptr;
+    st->pos = s->seq_pos[seqs[0]];
+    st->rows = rows;
+    st->k = k;
+    st->mode = a0 ? a0->mode : FC_ACCEPT_GREEDY;
+    st->temperature = a0 ? a0->temperature : 1.0f;
+    st->seed = a0 ? a0->seed : 0;
+    st->group_rows = gr;
+    st->groups = ng;
+    for (int j = 0; j < ng; ++j) {
+        const int q = seqs[j];
+        st->gcounter[j] = accept ? accept[q].counter : 0;
+        for (int i = 0; i < gr; ++i) {
+            st->ids[j * gr + i] = ids[j * gr + i];
+            st->rowpos[j * gr + i] = s->seq_pos[q] + i;
+            st->rowseq[j * gr + i] = q;
+        }
+    }
+    st->counter = st->gcounter[0];
+    return exec_pass(s, rows, 0, err, n);
+}
+
 int check_ids(const FcSession *s, const int *ids, int count, char *err, size_t n) {
     for (int i = 0; i < count; ++i)
         if (ids[i] < 0 || ids[i] >= s->m->c.vocab_size)
@@ -1615,8 +1668,14 @@ FcModelConfig fc_model_info(const FcModel *m) {
     return c;
 }
 
-int fc_session_create(FcSession **out, FcModel *m, const FcOptions *options, char *error,
-                      size_t error_size) {
+}  // extern "C"
+
+namespace {
+
+// Session construction; `batch` (nullable) makes a multi-sequence session
+// whose passes hold whole sequences of batch->rows_per_sequence rows.
+int create_session(FcSession **out, FcModel *m, const FcOptions *options, const FcBatchOptions *batch,
+                   char *error, size_t error_size) {
     if (!out || !m || !options)
         return set_error(error, error_size, "model and session options are required");
     *out = nullptr;
@@ -1629,6 +1688,13 @@ int fc_session_create(FcSession **out, FcModel *m, const FcOptions *options, cha
     s->m = m;
     s->opt = *options;
     s->rows_max = std::min(options->max_batch, kMaxRows);
+    if (batch) {
+        s->batch = true;
+        s->n_seq = batch->sequences;
+        s->group_rows = batch->rows_per_sequence;
+        s->shared_rows = batch->shared_prefix;
+        s->seq_pos.assign(batch->sequences, 0);
+    }
     s->stats.resident_bytes = m->resident;
     const int mb = s->rows_max;
     const int D = c.hidden_size, H = c.head_count, L = c.kv_lora_rank, R = c.qk_rope_dim;
@@ -1648,6 +1714,16 @@ int fc_session_create(FcSession **out, FcModel *m, const FcOptions *options, cha
     s->attn_tc = std::min(mb, 4) * H >= kTcRows;
     if (attn_env && strcmp(attn_env, "mma") == 0) s->attn_tc = false;
     if (attn_env && strcmp(attn_env, "tc") == 0) s->attn_tc = true;
+    if (batch) {
+        // a query tile must hold rows of one sequence only
+        const int q = s->group_rows * H;
+        s->attn_tc = q % kTcRows == 0;
+        if (!s->attn_tc && q % kAttnQ) {
+            delete s;
+            return set_error(error, error_size,
+                             "rows_per_sequence x heads (%d) must be a multiple of %d", q, kAttnQ);
+        }
+    }
     int target;
     if (s->attn_tc) {
         // one wave of (128-query tile, half) CTAs at up to 4 rows; at most
@@ -1665,14 +1741,22 @@ int fc_session_create(FcSession **out, FcModel *m, const FcOptions *options, cha
     bool ok = cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking) == cudaSuccess;
     ok = ok && cudaEventCreate(&s->ev_begin) == cudaSuccess && cudaEventCreate(&s->ev_end) == cudaSuccess;
     const int NLc = c.layer_count + c.mtp_layers;  // cache layers (target + drafter)
-    s->layer_rows = options->context_size;
-    ok = ok && salloc(s, s->cache, (size_t)NLc * options->context_size * (L + R));
     {
+        // page table: an ordinary session maps page p to itself; a batch
+        // session maps every sequence's first shared_rows / 64 pages to the
+        // same (shared) pages and the rest to its own pages
         const int pps = (options->context_size + kPageRows - 1) / kPageRows;
-        std::vector<int> ident(pps);
-        for (int p = 0; p < pps; ++p) ident[p] = p;
-        ok = ok && salloc(s, s->page_table, (size_t)pps) &&
-             cudaMemcpy(s->page_table, ident.data(), (size_t)pps * sizeof(int), cudaMemcpyHostToDevice) == cudaSuccess;
+        const int nseq = s->n_seq, shared = s->shared_rows / kPageRows;
+        std::vector<int> table((size_t)nseq * pps);
+        for (int q = 0; q < nseq; ++q)
+            for (int p = 0; p < pps; ++p)
+                table[(size_t)q * pps + p] = p < shared ? p : shared + q * (pps - shared) + (p - shared);
+        const int pages = batch ? shared + nseq * (pps - shared) : pps;
+        s->layer_rows = batch ? pages * kPageRows : options->context_size;
+        ok = ok && salloc(s, s->cache, (size_t)NLc * s->layer_rows * (L + R));
+        ok = ok && salloc(s, s->page_table, table.size()) &&
+             cudaMemcpy(s->page_table, table.data(), table.size() * sizeof(int), cudaMemcpyHostToDevice) ==
+                 cudaSuccess;
         s->pmap.pt = s->page_table;
         s->pmap.pps = pps;
     }
@@ -1732,7 +1816,7 @@ int fc_session_create(FcSession **out, FcModel *m, const FcOptions *options, cha
     // per pass than a verify holds (single-GPU models with quantized weights)
     auto quant = [](int f) { return f == FC_FMT_Q8 || f == FC_FMT_Q4 || f == FC_FMT_MXFP4; };
     const int NP = c.qk_nope_dim, VD = c.value_dim, DI = c.dense_intermediate_size;
-    const bool pf_ok = options->max_batch > s->rows_max && m->world == 1 && quant(c.dense_format) &&
+    const bool pf_ok = !batch && options->max_batch > s->rows_max && m->world == 1 && quant(c.dense_format) &&
                        (c.expert_count == 0 || quant(c.expert_format)) && L % 64 == 0 && R == 64 &&
                        (NP == 64 || NP == 128) && (VD == 64 || VD == 128) && (size_t)NLc * options->context_size >= (size_t)kPfM && D % 32 == 0 && (H * QW) % 32 == 0 && I % 32 == 0 &&
                        W % 32 == 0 && DI % 32 == 0 && c.q_lora_rank % 32 == 0 && K <= 64 && E <= 1024;
@@ -1775,7 +1859,7 @@ int fc_session_create(FcSession **out, FcModel *m, const FcOptions *options, cha
         ok = ok && pf_prepare_all() == cudaSuccess;
     }
     if (ok && (s->attn_tc || s->pf_rows))
-        ok = make_map_f16(&s->kvmap, s->cache, (uint64_t)(L + R), (uint64_t)NLc * options->context_size, kTcKeys);
+        ok = make_map_f16(&s->kvmap, s->cache, (uint64_t)(L + R), (uint64_t)NLc * s->layer_rows, kTcKeys);
     if (ok) {
         cudaError_t e1 = cudaFuncSetAttribute(mla_attention_kernel<512, 64>,
                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1801,6 +1885,30 @@ int fc_session_create(FcSession **out, FcModel *m, const FcOptions *options, cha
     return 1;
 }
 
+}  // namespace
+
+extern "C" {
+
+int fc_session_create(FcSession **out, FcModel *m, const FcOptions *options, char *error,
+                      size_t error_size) {
+    return create_session(out, m, options, nullptr, error, error_size);
+}
+
+int fc_session_create_batch(FcSession **out, FcModel *m, const FcBatchOptions *options, char *error,
+                            size_t error_size) {
+    if (!out || !m || !options) return set_error(error, error_size, "model and batch options are required");
+    *out = nullptr;
+    const FcBatchOptions &b = *options;
+    if (b.sequences < 1 || b.sequences > 64 || b.rows_per_sequence < 1 || b.rows_per_sequence > kMaxRows ||
+        b.context_size < b.rows_per_sequence || b.shared_prefix < 0 || b.shared_prefix % kPageRows ||
+        b.shared_prefix > b.context_size)
+        return set_error(error, error_size, "invalid batch options");
+    FcOptions o{};
+    o.context_size = b.context_size;
+    o.max_batch = std::min(b.sequences, kMaxRows / b.rows_per_sequence) * b.rows_per_sequence;
+    return create_session(out, m, &o, &b, error, error_size);
+}
+
 void fc_session_destroy(FcSession *s) {
     if (!s) return;
     cudaSetDevice(s->m->device);
@@ -1812,6 +1920,7 @@ void fc_session_reset(FcSession *s) {
     if (!s) return;
     s->position = 0;
     s->last_rows = 0;
+    std::fill(s->seq_pos.begin(), s->seq_pos.end(), 0);
     uint64_t allocs = s->stats.buffer_allocations, resident = s->stats.resident_bytes;
     s->stats = FcStats{};
     s->stats.buffer_allocations = allocs;
@@ -1827,6 +1936,7 @@ FcStats fc_session_stats(const FcSession *s) {
 
 int fc_session_prefill(FcSession *s, const int *ids, int count, float *last_logits, char *error,
                        size_t error_size) {
+    if (s && s->batch) return set_error(error, error_size, "batch sessions run fc_session_verify_batch");
     if (!s || !ids || !last_logits || count <= 0 || count > s->opt.max_batch ||
         count > s->opt.context_size)
         return set_error(error, error_size, "invalid prefill request");
@@ -1840,6 +1950,7 @@ int fc_session_prefill(FcSession *s, const int *ids, int count, float *last_logi
 
 int fc_session_append(FcSession *s, const int *ids, int count, float *last_logits, char *error,
                       size_t error_size) {
+    if (s && s->batch) return set_error(error, error_size, "batch sessions run fc_session_verify_batch");
     if (!s || !ids || !last_logits || count <= 0 || count > s->opt.max_batch || s->position <= 0 ||
         s->position + count > s->opt.context_size)
         return set_error(error, error_size, "invalid append request");
@@ -1851,6 +1962,7 @@ int fc_session_append(FcSession *s, const int *ids, int count, float *last_logit
 }
 
 int fc_session_decode(FcSession *s, int token, float *logits, char *error, size_t error_size) {
+    if (s && s->batch) return set_error(error, error_size, "batch sessions run fc_session_verify_batch");
     if (!s || !logits || s->position < 0 || s->position >= s->opt.context_size)
         return set_error(error, error_size, "invalid decode request");
     double t0 = now_ms();
@@ -1863,6 +1975,7 @@ int fc_session_decode(FcSession *s, int token, float *logits, char *error, size_
 int fc_session_verify(FcSession *s, const int *ids, int k, const FcAcceptConfig *accept,
                       int *emitted, int *n_emitted, int *next_token, float *last_logits,
                       char *error, size_t error_size) {
+    if (s && s->batch) return set_error(error, error_size, "batch sessions run fc_session_verify_batch");
     if (!s || !ids || !emitted || !n_emitted || !next_token || k < 0)
         return set_error(error, error_size, "invalid verify request");
     int rows = k + 1;
@@ -1893,6 +2006,80 @@ int fc_session_verify(FcSession *s, const int *ids, int k, const FcAcceptConfig 
     s->stats.proposed_tokens += (uint64_t)k;
     s->stats.accepted_tokens += (uint64_t)commit;
     s->stats.verify_ms += now_ms() - t0;
+    return 1;
+}
+
+int fc_session_batch_seed(FcSession *s, int sequence, int start, int end, uint64_t seed, char *error,
+                          size_t error_size) {
+    if (!s || !s->batch || sequence < 0 || sequence >= s->n_seq || start < 0 || end < start ||
+        end > s->opt.context_size)
+        return set_error(error, error_size, "invalid batch seed request");
+    const FcModelConfig &c = s->m->c;
+    cudaSetDevice(s->m->device);
+    const int L = c.kv_lora_rank, R = c.qk_rope_dim;
+    for (int l = 0; l < c.layer_count && end > start; ++l)
+        synth_kv_range_kernel<<<grid_for((size_t)(end - start) * (L + R)), 256, 0, s->stream>>>(
+            s->cache + (size_t)l * s->layer_rows * (L + R), s->pmap, sequence, start, end, L, R, seed,
+            fc_tensor_id(l, FC_T_KV_LATENT, 0), fc_tensor_id(l, FC_T_KV_ROPE, 0));
+    cudaError_t e = cudaStreamSynchronize(s->stream);
+    if (e == cudaSuccess) e = cudaGetLastError();
+    if (e != cudaSuccess) return set_error(error, error_size, "seeding failed: %s", cudaGetErrorString(e));
+    s->seq_pos[sequence] = std::max(s->seq_pos[sequence], end);
+    return 1;
+}
+
+int fc_session_verify_batch(FcSession *s, const int *ids, int k, const FcAcceptConfig *accept, int *n_emitted,
+                            int *next_token, char *error, size_t error_size) {
+    if (!s || !s->batch || !ids || !n_emitted || !next_token || k + 1 != s->group_rows)
+        return set_error(error, error_size, "invalid batch verify request (k must be rows_per_sequence - 1)");
+    const int gr = s->group_rows, nseq = s->n_seq;
+    for (int q = 0; q < nseq; ++q) {
+        if (s->seq_pos[q] + gr > s->opt.context_size)
+            return set_error(error, error_size, "sequence %d: verify exceeds the context (%d + %d > %d)", q,
+                             s->seq_pos[q], gr, s->opt.context_size);
+        if (s->seq_pos[q] < 1) return set_error(error, error_size, "sequence %d has no context", q);
+        if (accept) {
+            if (accept[q].mode == FC_ACCEPT_SAMPLE && !(accept[q].temperature > 0.0f))
+                return set_error(error, error_size, "sampling needs a positive temperature");
+            if (accept[q].mode != accept[0].mode || accept[q].temperature != accept[0].temperature ||
+                accept[q].seed != accept[0].seed)
+                return set_error(error, error_size, "sequences of a batch share mode, temperature and seed");
+        }
+    }
+    if (!check_ids(s, ids, nseq * gr, error, error_size)) return 0;
+    double t0 = now_ms();
+    const int per_pass = s->rows_max / gr;
+    int seqs[kMaxRows];
+    for (int q0 = 0; q0 < nseq; q0 += per_pass) {
+        const int ng = std::min(per_pass, nseq - q0);
+        for (int j = 0; j < ng; ++j) seqs[j] = q0 + j;
+        if (!run_batch_pass(s, seqs, ng, ids + (size_t)q0 * gr, k, accept, error, error_size)) return 0;
+        const Result &r = *s->h_res;
+        for (int j = 0; j < ng; ++j) {
+            const int q = q0 + j, commit = r.g_commit[j];
+            if (commit < 1 || commit > gr)
+                return set_error(error, error_size, "sequence %d: verify produced commit %d", q, commit);
+            n_emitted[q] = commit;
+            next_token[q] = r.g_next[j];
+            s->seq_pos[q] += commit;  // rows past the commit are overwritten later
+            s->stats.accepted_tokens += (uint64_t)commit;
+        }
+    }
+    s->stats.verify_calls++;
+    s->stats.proposed_tokens += (uint64_t)k * nseq;
+    s->stats.verify_ms += now_ms() - t0;
+    return 1;
+}
+
+int fc_session_batch_position(const FcSession *s, int sequence) {
+    if (!s || !s->batch || sequence < 0 || sequence >= s->n_seq) return -1;
+    return s->seq_pos[sequence];
+}
+
+int fc_session_batch_rollback(FcSession *s, int sequence, int position, char *error, size_t error_size) {
+    if (!s || !s->batch || sequence < 0 || sequence >= s->n_seq || position < 0)
+        return set_error(error, error_size, "invalid batch rollback");
+    s->seq_pos[sequence] = std::min(s->seq_pos[sequence], position);
     return 1;
 }
 
@@ -1930,6 +2117,7 @@ void fc_session_profile_reset(FcSession *s) {
 }
 
 int fc_session_rollback(FcSession *s, int position, char *error, size_t error_size) {
+    if (s && s->batch) return set_error(error, error_size, "batch sessions run fc_session_verify_batch");
     if (!s || position < 0) return set_error(error, error_size, "invalid rollback request");
     if (position < s->position) s->position = position;
     return 1;
@@ -1987,6 +2175,7 @@ int fc_session_ep_connect(FcSession *s, const void *handles, int world, char *er
 
 int fc_session_seed_context(FcSession *s, int positions, uint64_t seed, char *error,
                             size_t error_size) {
+    if (s && s->batch) return set_error(error, error_size, "batch sessions run fc_session_verify_batch");
     if (!s || positions < 0 || positions > s->opt.context_size)
         return set_error(error, error_size, "invalid seeded context");
     const FcModelConfig &c = s->m->c;

@@ -272,6 +272,46 @@ int fc_session_copy_row_logits(const FcSession *session, float *logits,
 int fc_session_seed_context(FcSession *session, int positions, uint64_t seed,
                             char *error, size_t error_size);
 
+/* ---- batched multi-sequence verify ---------------------------------------
+ * A batch session holds `sequences` sequences over one paged latent cache
+ * (64-row pages).  Their first `shared_prefix` positions (a multiple of 64)
+ * live in pages every sequence maps: the prefix-cache snapshot of
+ * deepseek_v4_prefix_cache.c:139-229, reused instead of copied.  Each
+ * sequence has its own position and private pages for the rest of its
+ * context.  fc_session_verify_batch runs one verify of 1 + k rows for every
+ * sequence, packing floor(8 / (1 + k)) sequences into each device pass so
+ * that they share the weight reads, and accepts and rolls back each sequence
+ * on its own.  Each sequence gets the same result as the same verify in a
+ * one-sequence session.  No reference counterpart: floyd verifies one
+ * sequence at a time. */
+typedef struct {
+    int context_size;        /* positions per sequence                       */
+    int sequences;           /* 1 .. 64                                      */
+    int rows_per_sequence;   /* 1 + drafts of each verify (1 .. 8)           */
+    int shared_prefix;       /* positions shared by all sequences (x64)      */
+} FcBatchOptions;
+
+int fc_session_create_batch(FcSession **out, FcModel *model, const FcBatchOptions *options,
+                            char *error, size_t error_size);
+
+/* Synthetic latent KV (the generator of fc_session_seed_context) for
+ * positions [start, end) of one sequence; positions below shared_prefix are
+ * the shared pages.  The sequence's position becomes end when that is
+ * further.  Benchmark and test hook. */
+int fc_session_batch_seed(FcSession *session, int sequence, int start, int end, uint64_t seed,
+                          char *error, size_t error_size);
+
+/* ids: [sequences][1 + k] (row 0 the last accepted token, then the drafts);
+ * accept: one config per sequence (NULL: greedy).  Outputs per sequence:
+ * n_emitted (1 .. k + 1, the committed prefix of its ids) and next_token. */
+int fc_session_verify_batch(FcSession *session, const int *ids, int k, const FcAcceptConfig *accept,
+                            int *n_emitted, int *next_token, char *error, size_t error_size);
+
+int fc_session_batch_position(const FcSession *session, int sequence);
+/* Truncates one sequence to `position` (clamped to <= its current one). */
+int fc_session_batch_rollback(FcSession *session, int sequence, int position, char *error,
+                              size_t error_size);
+
 /* Draft proposals of the on-device MTP drafter (models with mtp_layers = 1).
  * Every fc_session_verify with k > 0 runs the drafter in the same device
  * graph after acceptance: k sequential greedy steps from the last committed

@@ -622,6 +622,25 @@ int orc_session_seed_context(OrcSession *s, int positions, uint64_t seed) {
     return 1;
 }
 
+/* Synthetic latent KV for positions [start, end) only (the values depend on
+ * the position, as in orc_session_seed_context); the position becomes end
+ * when that is further.  Lets a test build a context whose leading part is
+ * shared with other sequences and whose tail is its own. */
+int orc_session_seed_range(OrcSession *s, int start, int end, uint64_t seed) {
+    const FcModelConfig *c = &s->m->c;
+    if (start < 0 || end < start || end > s->ctx) return 0;
+    int L = c->kv_lora_rank, R = c->qk_rope_dim;
+    for (int l = 0; l < c->layer_count; ++l) {
+        uint32_t tl = fc_tensor_id(l, FC_T_KV_LATENT, 0), tr = fc_tensor_id(l, FC_T_KV_ROPE, 0);
+        float *lat = s->latent + (size_t)l * s->ctx * L;
+        float *rop = s->rope + (size_t)l * s->ctx * R;
+        for (size_t e = (size_t)start * L; e < (size_t)end * L; ++e) lat[e] = fc_synth_kv(seed, tl, e);
+        for (size_t e = (size_t)start * R; e < (size_t)end * R; ++e) rop[e] = fc_synth_kv(seed, tr, e);
+    }
+    if (end > s->position) s->position = end;
+    return 1;
+}
+
 static float round_kv(const OrcSession *s, float v) {
     return s->kv_fp16 ? orc_fp16_to_f32(orc_f32_to_fp16(v)) : v;
 }

@@ -114,6 +114,7 @@ void orc_session_free(OrcSession *session);
 int orc_session_position(const OrcSession *session);
 void orc_session_set_position(OrcSession *session, int position);
 int orc_session_seed_context(OrcSession *session, int positions, uint64_t seed);
+int orc_session_seed_range(OrcSession *session, int start, int end, uint64_t seed);
 
 /* Runs `rows` tokens at the current position and advances it.
  * logits [rows][V] (nullable), layer_out [layers][rows][D] (nullable),

@@ -56,6 +56,7 @@ def lib():
             "orc_session_position": (I, [P]),
             "orc_session_set_position": (None, [P, I]),
             "orc_session_seed_context": (I, [P, I, ctypes.c_uint64]),
+            "orc_session_seed_range": (I, [P, I, I, ctypes.c_uint64]),
             "orc_session_forward": (I, [P, IP, I, FP, FP, IP]),
             "orc_session_copy_kv": (I, [P, I, FP, FP, I]),
             "orc_session_verify": (I, [P, IP, I, ctypes.POINTER(FcAcceptConfig), IP, IP, IP, FP, IP]),
@@ -159,6 +160,11 @@ class OracleSession:
 
     def seed_context(self, positions, seed):
         if not lib().orc_session_seed_context(self.handle, positions, ctypes.c_uint64(seed)):
+            raise RuntimeError("oracle seed failed")
+
+    def seed_range(self, start, end, seed):
+        """Synthetic KV for positions [start, end) (position -> max(position, end))."""
+        if not lib().orc_session_seed_range(self.handle, start, end, ctypes.c_uint64(seed)):
             raise RuntimeError("oracle seed failed")
 
     def forward(self, ids, want_layers=False, want_routes=False):
