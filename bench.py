@@ -52,6 +52,9 @@ def parse():
                     help="configs[2] leg: prompt length of the prefill (0 = skip the leg)")
     ap.add_argument("--prefill-decode", type=int, default=512, help="configs[2] leg: greedy decodes after it")
     ap.add_argument("--prefill-reps", type=int, default=5, help="configs[2] leg: timed prefills")
+    ap.add_argument("--batch-steps", type=int, default=10,
+                    help="configs[4] leg: timed batched verify steps per acceptance rate (0 = skip)")
+    ap.add_argument("--batch-warmup", type=int, default=2)
     ap.add_argument("--prefill-layers", type=int, default=None,
                     help="configs[2] leg with fewer layers (a small case of the same kernels, for profilers)")
     ap.add_argument("--prefill-only", action="store_true",
@@ -410,6 +413,79 @@ def prefill_leg(args, d):
     return out
 
 
+def batch_leg(args, d, model, cfg):
+    """configs[4] on the C4 stand-in: 8 sequences verifying 1 + draft rows
+    each in one batch session (floor(8 / rows) sequences per device pass),
+    per-sequence context uniform in [1024, 16384] (seeded), the first 1024
+    positions shared by all sequences (prefix pages), planted acceptance
+    p in {0.5, 0.7, 0.9} against each sequence's own greedy continuation."""
+    import floyd_b200
+    nseq, rows, prefix = 8, args.draft + 1, 1024
+    V = cfg["vocab_size"]
+    ctxs = np.random.default_rng(5).integers(prefix, 16384 + 1, size=nseq).tolist()
+    n_rounds = args.batch_warmup + args.batch_steps
+    gen = rows * n_rounds + 2
+    bs = floyd_b200.BatchSession(model, 16384 + gen + 8, nseq, rows, prefix)
+    if d.world > 1:
+        bs.ep_connect(d.all_gather_bytes(bs.ep_handle()))
+        d.barrier()
+    bs.seed(0, 0, prefix, 7)
+    for q in range(nseq):
+        bs.seed(q, prefix, ctxs[q], 100 + q)
+    # untimed: each sequence's greedy continuation (drafts that do not match
+    # commit one token and return the greedy next one)
+    junk = np.random.default_rng(9)
+    streams = [[1] for _ in range(nseq)]
+    while min(len(st) for st in streams) < gen:
+        ids = [[st[-1]] + junk.integers(0, V, size=rows - 1).tolist() for st in streams]
+        n, nxt = bs.verify_batch(ids)
+        for q in range(nseq):
+            streams[q].extend(ids[q][1:n[q]] + [nxt[q]])
+    results = []
+    for p in (0.5, 0.7, 0.9):
+        for q in range(nseq):
+            bs.rollback_seq(q, ctxs[q])
+        plans = [planted_rounds(streams[q], n_rounds, args.draft, p, V, seed=1234 + q) for q in range(nseq)]
+        offs = [0] * nseq
+        emitted = mismatches = 0
+        wall = 0.0
+        for r in range(n_rounds):
+            if r == args.batch_warmup:
+                d.barrier()
+                g0 = bs.stats()["gpu_ms"]
+            ids = [make_ids(streams[q], offs[q], plans[q][r], V) for q in range(nseq)]
+            t0 = time.perf_counter()
+            n, nxt = bs.verify_batch(ids)
+            dt = time.perf_counter() - t0
+            for q in range(nseq):
+                expect = 1
+                for h in plans[q][r][0]:
+                    if not h:
+                        break
+                    expect += 1
+                if n[q] != expect or nxt[q] != streams[q][offs[q] + n[q]]:
+                    mismatches += 1
+                offs[q] += n[q]
+                if r >= args.batch_warmup:
+                    emitted += n[q]
+            if r >= args.batch_warmup:
+                wall += dt
+        g = d.max(bs.stats()["gpu_ms"] - g0)
+        results.append({"accept_p": p, "value": emitted / (g / 1e3), "unit": "accepted tok/s (all sequences)",
+                        "e2e": emitted / d.max(wall), "ms_per_step": g / args.batch_steps,
+                        "mean_commit_per_sequence": emitted / (args.batch_steps * nseq),
+                        "acceptance_mismatches": int(d.sum(mismatches))})
+    bs.close()
+    return {"workload": "c5_batched_verify", "sequences": nseq, "rows_per_sequence": rows,
+            "sequences_per_pass": 8 // rows, "shared_prefix": prefix, "contexts": ctxs,
+            "steps": args.batch_steps, "warmup": args.batch_warmup, "n_gpus": d.world,
+            "results": results,
+            "exchange_exposed_ms": None,
+            "note": ("one batch step = one verify of every sequence; device time of the graph replays "
+                     "(max over ranks); the expert exchange (N > 1) is fused into the down-projection "
+                     "epilogue and the combine's wait, so it has no separate exposed time")}
+
+
 def run_ours(args, d):
     import floyd_b200
     from floyd_b200.configs import CONFIGS
@@ -589,6 +665,8 @@ def run_ours(args, d):
         except Exception as exc:  # reported, never silently replaced
             out["cpu_baseline"] = {"error": str(exc)}
     sess.close()
+    if args.batch_steps > 0:
+        out["batch_verify"] = batch_leg(args, d, model, cfg)
     model.close()
     return out
 

@@ -63,3 +63,54 @@ def test_two_gpu_expert_parallel_equals_single_gpu(tmp_path):
         got = np.load(tmp_path / f"rank{r}.npz")
         assert np.array_equal(got["rows"], rows), f"rank {r} verify rows"
         assert np.array_equal(got["dec"], dec), f"rank {r} decodes"
+
+
+def _batch_rank_main(rank, world, port, out_dir):
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    import floyd_b200
+    cfg = _cfg()
+    m = floyd_b200.Model(cfg, device=rank, seed=0, rank=rank, world=world)
+    bs = floyd_b200.BatchSession(m, cfg["context"] + 32, 3, 4, 64)
+    handles = [None] * world
+    dist.all_gather_object(handles, bs.ep_handle())
+    bs.ep_connect(handles)
+    dist.barrier()
+    _seed_batch(bs)
+    n, nxt = bs.verify_batch(BATCH_IDS)
+    np.savez(os.path.join(out_dir, f"batch{rank}.npz"), n=np.array(n), nxt=np.array(nxt), rows=bs.row_logits(4))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+BATCH_IDS = [[3, 1000, 77, 2024], [5, 6, 7, 8], [11, 12, 13, 14]]
+
+
+def _seed_batch(bs):
+    bs.seed(0, 0, 64, 7)
+    for q in range(3):
+        bs.seed(q, 64, 150 + 40 * q, 100 + q)
+
+
+def test_two_gpu_batch_verify_equals_single_gpu(tmp_path):
+    """The batched multi-sequence verify over expert parallelism: every
+    rank's commits, next tokens and last-pass rows equal one GPU's."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+    import floyd_b200
+    port = 29600 + os.getpid() % 1000
+    mp.spawn(_batch_rank_main, args=(2, port, str(tmp_path)), nprocs=2, join=True)
+    cfg = _cfg()
+    m = floyd_b200.Model(cfg, device=0, seed=0)
+    bs = floyd_b200.BatchSession(m, cfg["context"] + 32, 3, 4, 64)
+    _seed_batch(bs)
+    n, nxt = bs.verify_batch(BATCH_IDS)
+    rows = bs.row_logits(4)
+    for r in range(2):
+        got = np.load(tmp_path / f"batch{r}.npz")
+        assert got["n"].tolist() == n and got["nxt"].tolist() == nxt, f"rank {r}"
+        assert np.array_equal(got["rows"], rows), f"rank {r} rows"
