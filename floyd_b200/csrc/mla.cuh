@@ -210,31 +210,63 @@ __device__ __forceinline__ void mla_absorb_block(int bx, int by, int fmt, const 
         reinterpret_cast<uint4 *>(raw[t])[v] = __ldg(src + v);
     }
     __syncthreads();
-    const int srb = scale_row_bytes(fmt), el = scale_elem_bytes(fmt);
-    for (int i = threadIdx.x; i < nope * kAbsorbCols; i += blockDim.x) {
-        int n = i / kAbsorbCols, col = i % kAbsorbCols;
-        int r = col0 + col, byte, nib;
-        inner_position(fmt, r, byte, nib);
+    // Record-wise decode: unit (row n, record j) holds columns 16 i + 4 j + b
+    // (i, b < 4) of the 64-column half `sub` of the chunk (common.cuh
+    // layout); every value is the exact fp32 product value x group scale.
+    const int srb = scale_row_bytes(fmt), sub = col0 / 64;
+    for (int u = threadIdx.x; u < nope * 4; u += blockDim.x) {
+        const int n = u >> 2, j = u & 3, g = n % kTileRows;
         const uint8_t *b = raw[n / kTileRows];
-        int g = n % kTileRows;
-        uint8_t v = b[g * 64 + byte];
-        const uint8_t *sp = b + kBlockValueBytes + g * srb + (r / 32) * el;
-        float wv;
+        const uint4 rec = *reinterpret_cast<const uint4 *>(b + g * 64 + 16 * j);
+        const uint8_t *sp = b + kBlockValueBytes + g * srb;
+        float *dst = &wsm[n][4 * j];
         if (fmt == FC_FMT_Q8) {
-            wv = (float)(int8_t)v * __half2float(*reinterpret_cast<const __half *>(sp));
+            const uint32_t words[4] = {rec.x, rec.y, rec.z, rec.w};
+            const float s0 = __half2float(reinterpret_cast<const __half *>(sp)[0]);
+            const float s1 = __half2float(reinterpret_cast<const __half *>(sp)[1]);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int bb = 0; bb < 4; ++bb)
+                    dst[16 * i + bb] = (float)(int8_t)((words[i] >> (8 * bb)) & 0xFFu) * (i < 2 ? s0 : s1);
         } else {
-            uint32_t code = (v >> (4 * nib)) & 15u;
-            if (fmt == FC_FMT_Q4) {
-                wv = (float)((int)code - 8) * __half2float(*reinterpret_cast<const __half *>(sp));
-            } else {
-                // e2m1 magnitude: 0, 0.5, 1, 1.5, 2, 3, 4, 6
-                uint32_t e = (code >> 1) & 3u, mb = code & 1u;
-                float m = e == 0 ? 0.5f * (float)mb : (float)(2u + mb) * (float)(1u << e) * 0.25f;
-                if (code & 8) m = -m;
-                wv = m * e8m0_to_float(*sp);
+            const uint32_t w0 = sub ? rec.z : rec.x, w1 = sub ? rec.w : rec.y;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int grp = 2 * sub + (i >> 1);
+                float scale;
+                if (fmt == FC_FMT_Q4) scale = __half2float(reinterpret_cast<const __half *>(sp)[grp]);
+                else scale = e8m0_to_float(sp[grp]);
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    uint32_t lo, hi;
+                    if (fmt == FC_FMT_Q4) {
+                        const uint32_t word = i < 2 ? w0 : w1, sh = 4 * (2 * (i & 1) + h);
+                        lo = (word >> sh) & 15u;
+                        hi = (word >> (sh + 16)) & 15u;
+                    } else {
+                        const uint32_t byte = ((i < 2 ? w0 : w1) >> (8 * (2 * (i & 1) + h))) & 0xFFu;
+                        lo = byte & 15u;
+                        hi = byte >> 4;
+                    }
+                    const uint32_t codes[2] = {lo, hi};
+#pragma unroll
+                    for (int e = 0; e < 2; ++e) {
+                        const uint32_t code = codes[e];
+                        float v;
+                        if (fmt == FC_FMT_Q4) {
+                            v = (float)((int)code - 8);
+                        } else {
+                            // e2m1 magnitude: 0, 0.5, 1, 1.5, 2, 3, 4, 6
+                            const uint32_t ex = (code >> 1) & 3u, mb = code & 1u;
+                            v = ex == 0 ? 0.5f * (float)mb : (float)(2u + mb) * (float)(1u << ex) * 0.25f;
+                            if (code & 8) v = -v;
+                        }
+                        dst[16 * i + 2 * h + e] = v * scale;
+                    }
+                }
             }
         }
-        wsm[n][col] = wv;
     }
     pdl_wait();
     pdl_release();
