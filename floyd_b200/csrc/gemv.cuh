@@ -135,6 +135,11 @@ struct GemvWork {
     float swiglu_limit;
     int *err;
     int stages;               // ring depth (set by the launcher)
+    // MoE gate/up: the shared expert's items come first and run before the
+    // wait on the predecessor (the router).  Its input is the RMSNorm output
+    // two kernels back, complete by the time this kernel can start (the
+    // router has passed its own wait before releasing its dependents).
+    int shared_first;
 #ifdef FC_GEMV_TRACE
     int trace;
 #endif
@@ -161,6 +166,9 @@ __device__ __forceinline__ bool resolve_item(const GemvWork &wk, int item, GemvI
         const GemvSeg &r = wk.seg[0];
         int rt = r.tiles;
         int routed_items = wk.max_slots * rt;
+        if (wk.shared_first) {  // shared items first, then the routed ones
+            item = item < wk.seg[1].tiles ? routed_items + item : item - wk.seg[1].tiles;
+        }
         if (item < routed_items) {
             int slot = item / rt;
             if (slot >= *wk.n_active) return false;
@@ -398,7 +406,12 @@ __device__ __forceinline__ void gemv_consume(const GemvWork &wk, const uint8_t *
     const bool has_b = brow < wk.S;
     int idx = 0, slot = 0;
     uint32_t phase = 0;  // parity of the ring pass `slot` is in
+    bool waited = !(wk.moe && wk.shared_first);
     for (int item = blockIdx.x; item < wk.total_items; item += gridDim.x) {
+        if (!waited && item >= wk.seg[1].tiles) {
+            pdl_wait();
+            waited = true;
+        }
         GemvItem it;
         if (!resolve_item<FA, FB>(wk, item, it)) continue;
         const bool fa = it.fmt == FA;
@@ -526,7 +539,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
         // activation rows (kSmemB) and the MoE work list (written by the
         // router kernel) need the wait.
         bool waited = false;
-        if (wk.moe) {
+        if (wk.moe && !wk.shared_first) {
             pdl_wait();
             waited = true;
         }
@@ -541,6 +554,10 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
         uint32_t phase = 0;    // parity of the ring pass `slot` is in
         bool reuse = false;    // slot already used once (wait for its release)
         for (int item = blockIdx.x; item < wk.total_items; item += gridDim.x) {
+            if (wk.moe && !waited && item >= wk.seg[1].tiles) {
+                pdl_wait();  // the routed items need the router's work list
+                waited = true;
+            }
             GemvItem it;
             if (!resolve_item<FA, FB>(wk, item, it)) continue;
             const int blk = it.fmt == FA ? block_bytes(FA) : block_bytes(FB);
@@ -571,7 +588,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
                 bulk_g2s(sb, it.t0 + (size_t)c0 * blk, bytes, &full[slot]);
                 if (it.t1) bulk_g2s(sb + kSlotW, it.t1 + (size_t)c0 * blk, bytes, &full[slot]);
                 if (kSmemB) {
-                    if (waited) {
+                    if (waited || wk.moe) {  // MoE: shared-first items read an input that is ready
                         for (int r = 0; r < wk.S; ++r)
                             bulk_g2s(sb + 2 * kSlotW + (size_t)r * kBRow, it.xq + ((size_t)r * it.kp + c0 * ccols) * 2,
                                      (uint32_t)(nch * ccols * 4), &full[slot]);
@@ -599,7 +616,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
 
     // ---------------- consumers ----------------
     if (tid == 0) GEMV_MARK(125);
-    pdl_wait();
+    if (!(wk.moe && wk.shared_first)) pdl_wait();
     if (tid == 0) GEMV_MARK(126);
     if (wk.S <= 4)
         gemv_consume<FA, FB, true>(wk, smem, kSlotW, kSlotBytes, full, empty, red, out);

@@ -762,6 +762,7 @@ cudaError_t record_layer(FcSession *s, int S, int l, const Staging *dst) {
             gu.seg[1].kpy = kpW;
         }
         gu.nseg = 2;
+        gu.shared_first = y.s_gate.count ? 1 : 0;  // the shared expert overlaps the router
         gu.max_slots = s->max_slots;
         gu.expert_base = m->expert_lo;
         gu.n_active = s->n_active;
