@@ -76,6 +76,12 @@ def test_host_entry_points_reject_null_arguments():
     assert lib.fc_model_create(None, None, 0, err, len(err)) == 0
     assert lib.fc_session_create(None, None, None, err, len(err)) == 0
     assert lib.fc_session_position(None) == 0
+    assert lib.fc_session_create_batch(None, None, None, err, len(err)) == 0
+    assert lib.fc_session_batch_seed(None, 0, 0, 1, 0, err, len(err)) == 0
+    assert lib.fc_session_verify_batch(None, None, 3, None, None, None, err, len(err)) == 0
+    assert b"invalid" in err.value
+    assert lib.fc_session_batch_position(None, 0) == -1
+    assert lib.fc_session_batch_rollback(None, 0, 0, err, len(err)) == 0
     assert lib.fc_runtime_argmax(None, 10) == -1
     lib.fc_model_close(None)
     lib.fc_session_destroy(None)
