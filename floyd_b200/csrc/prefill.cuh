@@ -781,22 +781,39 @@ pf_attention_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_const
 // ---------------------------------------------------------------------------
 
 // RMSNorm of row blockIdx.x (moonlight_kernels.metal:23-41) -> fp16 GEMM
-// operand y16[row][0..D) and, optionally, fp32 y32.
+// operand y16[row][0..D) and, optionally, fp32 y32.  float4 loads, the row
+// held in registers (D <= 8192), half4 / float4 stores.
+constexpr int kPfNormVec = 8;  // float4 per thread at most
 __global__ void __launch_bounds__(256) pf_rmsnorm_kernel(const float *x, int D, const float *w, float eps,
                                                          __half *y16, int ld16, float *y32) {
     pdl_wait();
     pdl_release();
     __shared__ float scratch[32];
-    const int s = blockIdx.x;
-    const float *xs = x + (size_t)s * D;
+    const int s = blockIdx.x, n4 = D / 4;
+    const float4 *xs = reinterpret_cast<const float4 *>(x + (size_t)s * D);
+    float4 v[kPfNormVec];
     float ss = 0.0f;
-    for (int i = threadIdx.x; i < D; i += blockDim.x) ss += xs[i] * xs[i];
+#pragma unroll
+    for (int i = 0; i < kPfNormVec; ++i) {
+        const int k4 = threadIdx.x + i * blockDim.x;
+        if (k4 < n4) {
+            v[i] = xs[k4];
+            ss += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
+        }
+    }
     ss = block_sum(ss, scratch);
     const float scale = 1.0f / sqrtf(ss / (float)D + eps);
-    for (int i = threadIdx.x; i < D; i += blockDim.x) {
-        const float o = xs[i] * scale * w[i];
-        y16[(size_t)s * ld16 + i] = __float2half_rn(fminf(fmaxf(o, -65504.0f), 65504.0f));
-        if (y32) y32[(size_t)s * D + i] = o;
+#pragma unroll
+    for (int i = 0; i < kPfNormVec; ++i) {
+        const int k4 = threadIdx.x + i * blockDim.x;
+        if (k4 >= n4) continue;
+        const float4 wv = reinterpret_cast<const float4 *>(w)[k4];
+        float o[4] = {v[i].x * scale * wv.x, v[i].y * scale * wv.y, v[i].z * scale * wv.z, v[i].w * scale * wv.w};
+        __half2 h0 = __floats2half2_rn(fminf(fmaxf(o[0], -65504.0f), 65504.0f), fminf(fmaxf(o[1], -65504.0f), 65504.0f));
+        __half2 h1 = __floats2half2_rn(fminf(fmaxf(o[2], -65504.0f), 65504.0f), fminf(fmaxf(o[3], -65504.0f), 65504.0f));
+        *reinterpret_cast<uint2 *>(y16 + (size_t)s * ld16 + 4 * k4) =
+            make_uint2(*reinterpret_cast<uint32_t *>(&h0), *reinterpret_cast<uint32_t *>(&h1));
+        if (y32) reinterpret_cast<float4 *>(y32 + (size_t)s * D)[k4] = make_float4(o[0], o[1], o[2], o[3]);
     }
 }
 
@@ -978,7 +995,8 @@ __global__ void __launch_bounds__(256) pf_gather_kernel(const int *route_ids, in
 }
 
 // resid[t] += (sum over the row's experts in ascending id of w * y[slot])
-// + shared[t]  (moe_exec.h:97-110 order).
+// + shared[t]  (moe_exec.h:97-110 order); float4 loads and stores, each
+// element's sum in the same order.
 __global__ void __launch_bounds__(256) pf_combine_kernel(float *resid, const float *yd, const float *shared,
                                                          const int *route_ids, const float *route_w,
                                                          const int *slot_of, int K, int D) {
@@ -1002,11 +1020,30 @@ __global__ void __launch_bounds__(256) pf_combine_kernel(float *resid, const flo
             }
     }
     __syncthreads();
-    for (int d = threadIdx.x; d < D; d += blockDim.x) {
-        float y = 0.0f;
-        for (int k = 0; k < K; ++k) y = __fadd_rn(y, __fmul_rn(sw[k], yd[(size_t)sl[k] * D + d]));
-        if (shared) y = __fadd_rn(y, shared[(size_t)t * D + d]);
-        resid[(size_t)t * D + d] = __fadd_rn(resid[(size_t)t * D + d], y);
+    float4 *r4 = reinterpret_cast<float4 *>(resid + (size_t)t * D);
+    for (int d4 = threadIdx.x; d4 < D / 4; d4 += blockDim.x) {
+        float4 y = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        for (int k = 0; k < K; ++k) {
+            const float4 v = __ldcs(reinterpret_cast<const float4 *>(yd + (size_t)sl[k] * D) + d4);
+            const float c = sw[k];
+            y.x = __fadd_rn(y.x, __fmul_rn(c, v.x));
+            y.y = __fadd_rn(y.y, __fmul_rn(c, v.y));
+            y.z = __fadd_rn(y.z, __fmul_rn(c, v.z));
+            y.w = __fadd_rn(y.w, __fmul_rn(c, v.w));
+        }
+        if (shared) {
+            const float4 sh = reinterpret_cast<const float4 *>(shared + (size_t)t * D)[d4];
+            y.x = __fadd_rn(y.x, sh.x);
+            y.y = __fadd_rn(y.y, sh.y);
+            y.z = __fadd_rn(y.z, sh.z);
+            y.w = __fadd_rn(y.w, sh.w);
+        }
+        float4 r = r4[d4];
+        r.x = __fadd_rn(r.x, y.x);
+        r.y = __fadd_rn(r.y, y.y);
+        r.z = __fadd_rn(r.z, y.z);
+        r.w = __fadd_rn(r.w, y.w);
+        r4[d4] = r;
     }
 }
 

@@ -1819,7 +1819,7 @@ int create_session(FcSession **out, FcModel *m, const FcOptions *options, const 
     const int NP = c.qk_nope_dim, VD = c.value_dim, DI = c.dense_intermediate_size;
     const bool pf_ok = !batch && options->max_batch > s->rows_max && m->world == 1 && quant(c.dense_format) &&
                        (c.expert_count == 0 || quant(c.expert_format)) && L % 64 == 0 && R == 64 &&
-                       (NP == 64 || NP == 128) && (VD == 64 || VD == 128) && (size_t)NLc * options->context_size >= (size_t)kPfM && D % 32 == 0 && (H * QW) % 32 == 0 && I % 32 == 0 &&
+                       (NP == 64 || NP == 128) && (VD == 64 || VD == 128) && D <= 4 * kPfNormVec * 256 && c.q_lora_rank <= 4 * kPfNormVec * 256 && (size_t)NLc * options->context_size >= (size_t)kPfM && D % 32 == 0 && (H * QW) % 32 == 0 && I % 32 == 0 &&
                        W % 32 == 0 && DI % 32 == 0 && c.q_lora_rank % 32 == 0 && K <= 64 && E <= 1024;
     if (ok && pf_ok) {
         const int P = options->max_batch, Pp = (P + kPfM - 1) / kPfM * kPfM;
