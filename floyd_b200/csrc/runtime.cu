@@ -2039,6 +2039,9 @@ int fc_session_verify_batch(FcSession *s, const int *ids, int k, const FcAcceptC
             return set_error(error, error_size, "sequence %d: verify exceeds the context (%d + %d > %d)", q,
                              s->seq_pos[q], gr, s->opt.context_size);
         if (s->seq_pos[q] < 1) return set_error(error, error_size, "sequence %d has no context", q);
+        if (s->seq_pos[q] < s->shared_rows)  // its rows would land in pages every sequence reads
+            return set_error(error, error_size, "sequence %d is inside the shared prefix (%d < %d)", q,
+                             s->seq_pos[q], s->shared_rows);
         if (accept) {
             if (accept[q].mode == FC_ACCEPT_SAMPLE && !(accept[q].temperature > 0.0f))
                 return set_error(error, error_size, "sampling needs a positive temperature");

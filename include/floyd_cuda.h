@@ -303,7 +303,9 @@ int fc_session_batch_seed(FcSession *session, int sequence, int start, int end, 
 
 /* ids: [sequences][1 + k] (row 0 the last accepted token, then the drafts);
  * accept: one config per sequence (NULL: greedy).  Outputs per sequence:
- * n_emitted (1 .. k + 1, the committed prefix of its ids) and next_token. */
+ * n_emitted (1 .. k + 1, the committed prefix of its ids) and next_token.
+ * Every sequence must be at a position >= shared_prefix (its rows must not
+ * land in the shared pages). */
 int fc_session_verify_batch(FcSession *session, const int *ids, int k, const FcAcceptConfig *accept,
                             int *n_emitted, int *next_token, char *error, size_t error_size);
 

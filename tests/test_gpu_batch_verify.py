@@ -139,3 +139,9 @@ def test_batch_refuses_invalid_shapes():
         bs.decode(1)                                          # single-sequence calls are refused
     with pytest.raises(floyd_b200.FloydError):
         bs.verify_batch([[1, 2, 3, 4], [5, 6, 7, 8]])          # sequences without context
+    bs.seed(0, 0, 32, 7)
+    bs.seed(1, 0, 200, 8)
+    with pytest.raises(floyd_b200.FloydError):
+        bs.verify_batch([[1, 2, 3, 4], [5, 6, 7, 8]])          # sequence 0 would write into the shared pages
+    bs.seed(0, 32, 100, 9)
+    bs.verify_batch([[1, 2, 3, 4], [5, 6, 7, 8]])
