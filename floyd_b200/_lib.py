@@ -126,6 +126,7 @@ SIGNATURES = {
     "fc_session_profile_reset": (None, [_P]),
     "fc_session_set_layer_trace": (_I, [_P, _I]),
     "fc_test_kv_length": (_I, [_P, _I]),
+    "fc_test_batch_page_table": (_I, [_I, _I, _I, _IP, _I]),
     "fc_test_copy_kv": (_I, [_P, _I, _FP, _FP, _I]),
     "fc_test_copy_routes": (_I, [_P, _I, _IP, _I]),
     "fc_test_copy_layer_outputs": (_I, [_P, _FP, _I]),

@@ -1673,6 +1673,17 @@ FcModelConfig fc_model_info(const FcModel *m) {
 
 namespace {
 
+// Page table [sequences][pages per sequence] of 64-row pages: the first
+// shared_rows / 64 pages of every sequence are the same physical pages, the
+// rest are each sequence's own.  Returns the number of physical pages.
+int build_page_table(int context_size, int sequences, int shared_rows, int *table) {
+    const int pps = (context_size + kPageRows - 1) / kPageRows, shared = shared_rows / kPageRows;
+    for (int q = 0; q < sequences; ++q)
+        for (int p = 0; p < pps; ++p)
+            table[(size_t)q * pps + p] = p < shared ? p : shared + q * (pps - shared) + (p - shared);
+    return shared + sequences * (pps - shared);
+}
+
 // Session construction; `batch` (nullable) makes a multi-sequence session
 // whose passes hold whole sequences of batch->rows_per_sequence rows.
 int create_session(FcSession **out, FcModel *m, const FcOptions *options, const FcBatchOptions *batch,
@@ -1747,12 +1758,8 @@ int create_session(FcSession **out, FcModel *m, const FcOptions *options, const 
         // session maps every sequence's first shared_rows / 64 pages to the
         // same (shared) pages and the rest to its own pages
         const int pps = (options->context_size + kPageRows - 1) / kPageRows;
-        const int nseq = s->n_seq, shared = s->shared_rows / kPageRows;
-        std::vector<int> table((size_t)nseq * pps);
-        for (int q = 0; q < nseq; ++q)
-            for (int p = 0; p < pps; ++p)
-                table[(size_t)q * pps + p] = p < shared ? p : shared + q * (pps - shared) + (p - shared);
-        const int pages = batch ? shared + nseq * (pps - shared) : pps;
+        std::vector<int> table((size_t)s->n_seq * pps);
+        const int pages = build_page_table(options->context_size, s->n_seq, s->shared_rows, table.data());
         s->layer_rows = batch ? pages * kPageRows : options->context_size;
         ok = ok && salloc(s, s->cache, (size_t)NLc * s->layer_rows * (L + R));
         ok = ok && salloc(s, s->page_table, table.size()) &&
@@ -2196,6 +2203,15 @@ int fc_session_seed_context(FcSession *s, int positions, uint64_t seed, char *er
     if (e != cudaSuccess) return set_error(error, error_size, "seeding failed: %s", cudaGetErrorString(e));
     s->position = positions;
     return 1;
+}
+
+int fc_test_batch_page_table(int context_size, int sequences, int shared_prefix, int *table, int capacity) {
+    if (context_size <= 0 || sequences < 1 || shared_prefix < 0 || shared_prefix % kPageRows ||
+        shared_prefix > context_size)
+        return -1;
+    const int pps = (context_size + kPageRows - 1) / kPageRows;
+    if (!table || capacity < sequences * pps) return -1;
+    return build_page_table(context_size, sequences, shared_prefix, table);
 }
 
 int fc_test_kv_length(const FcSession *s, int layer) {

@@ -361,6 +361,11 @@ void fc_session_profile_reset(FcSession *session);
 /* ---- test hooks (moonlight_metal.h:69-96) -------------------------------- */
 
 int fc_test_kv_length(const FcSession *session, int layer);      /* :85 */
+/* The page table a batch session builds (host only, no GPU): fills
+ * table[sequence][page] and returns the physical page count, -1 on invalid
+ * options or a short buffer. */
+int fc_test_batch_page_table(int context_size, int sequences, int shared_prefix, int *table,
+                             int capacity);
 /* latent [capacity][kv_lora_rank], rope [capacity][qk_rope_dim] as fp32. */
 int fc_test_copy_kv(const FcSession *session, int layer, float *latent,
                     float *rope, int capacity);                   /* :86-87 */

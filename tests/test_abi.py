@@ -85,3 +85,32 @@ def test_host_entry_points_reject_null_arguments():
     assert lib.fc_runtime_argmax(None, 10) == -1
     lib.fc_model_close(None)
     lib.fc_session_destroy(None)
+
+
+def test_batch_page_table_layout():
+    """Host-side page table of batch sessions: the shared prefix pages are the
+    same physical pages for every sequence, the other pages are private and
+    disjoint, and every entry is a valid physical page."""
+    import numpy as np
+    import floyd_b200
+    lib = floyd_b200.lib()
+    ctx, nseq, shared = 16448, 8, 1024
+    pps = (ctx + 63) // 64
+    table = np.full(nseq * pps, -1, dtype=np.int32)
+    ip = ctypes.POINTER(ctypes.c_int)
+    pages = lib.fc_test_batch_page_table(ctx, nseq, shared, table.ctypes.data_as(ip), table.size)
+    sp = shared // 64
+    assert pages == sp + nseq * (pps - sp)
+    t = table.reshape(nseq, pps)
+    assert (t >= 0).all() and (t < pages).all()
+    assert (t[:, :sp] == np.arange(sp)).all()                       # one shared copy
+    private = t[:, sp:].ravel()
+    assert len(np.unique(private)) == private.size                   # disjoint tails
+    assert not np.intersect1d(private, np.arange(sp)).size
+    # an ordinary session's table is the identity
+    one = np.zeros(pps, dtype=np.int32)
+    assert lib.fc_test_batch_page_table(ctx, 1, 0, one.ctypes.data_as(ip), one.size) == pps
+    assert (one == np.arange(pps)).all()
+    # invalid requests
+    assert lib.fc_test_batch_page_table(ctx, nseq, 100, table.ctypes.data_as(ip), table.size) == -1
+    assert lib.fc_test_batch_page_table(ctx, nseq, shared, table.ctypes.data_as(ip), 10) == -1
