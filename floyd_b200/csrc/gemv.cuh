@@ -140,10 +140,6 @@ struct GemvWork {
     // two kernels back, complete by the time this kernel can start (the
     // router has passed its own wait before releasing its dependents).
     int shared_first;
-    // MoE down: the work list comes from the router two kernels back (already
-    // complete), so the producer resolves items and streams weights before
-    // the wait; only the activation rows (the gate/up output) wait.
-    int early_items;
 #ifdef FC_GEMV_TRACE
     int trace;
 #endif
@@ -543,7 +539,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
         // activation rows (kSmemB) and the MoE work list (written by the
         // router kernel) need the wait.
         bool waited = false;
-        if (wk.moe && !wk.shared_first && !wk.early_items) {
+        if (wk.moe && !wk.shared_first) {
             pdl_wait();
             waited = true;
         }
@@ -558,7 +554,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
         uint32_t phase = 0;    // parity of the ring pass `slot` is in
         bool reuse = false;    // slot already used once (wait for its release)
         for (int item = blockIdx.x; item < wk.total_items; item += gridDim.x) {
-            if (wk.moe && wk.shared_first && !waited && item >= wk.seg[1].tiles) {
+            if (wk.moe && !waited && item >= wk.seg[1].tiles) {
                 pdl_wait();  // the routed items need the router's work list
                 waited = true;
             }
@@ -592,7 +588,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
                 bulk_g2s(sb, it.t0 + (size_t)c0 * blk, bytes, &full[slot]);
                 if (it.t1) bulk_g2s(sb + kSlotW, it.t1 + (size_t)c0 * blk, bytes, &full[slot]);
                 if (kSmemB) {
-                    if (waited || (wk.moe && wk.shared_first)) {  // shared-first items read a ready input
+                    if (waited || wk.moe) {  // MoE: shared-first items read an input that is ready
                         for (int r = 0; r < wk.S; ++r)
                             bulk_g2s(sb + 2 * kSlotW + (size_t)r * kBRow, it.xq + ((size_t)r * it.kp + c0 * ccols) * 2,
                                      (uint32_t)(nch * ccols * 4), &full[slot]);

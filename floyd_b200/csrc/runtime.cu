@@ -800,7 +800,6 @@ cudaError_t record_layer(FcSession *s, int S, int l, const Staging *dst) {
             dn.seg[1].ldy = D;
         }
         dn.nseg = 2;
-        dn.early_items = 1;  // weights stream while the gate/up kernel drains
         dn.max_slots = s->max_slots;
         dn.expert_base = m->expert_lo;
         dn.n_active = s->n_active;
