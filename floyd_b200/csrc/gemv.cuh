@@ -137,8 +137,10 @@ struct GemvWork {
     int stages;               // ring depth (set by the launcher)
     // MoE gate/up: the shared expert's items come first and run before the
     // wait on the predecessor (the router).  Its input is the RMSNorm output
-    // two kernels back, complete by the time this kernel can start (the
-    // router has passed its own wait before releasing its dependents).
+    // two kernels back, complete by the time this kernel can start: the
+    // router releases its dependents only after its own wait.  (This kernel
+    // releases its dependents at its start, so its successor may not assume
+    // the same of the router.)
     int shared_first;
 #ifdef FC_GEMV_TRACE
     int trace;
