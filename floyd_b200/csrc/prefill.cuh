@@ -379,6 +379,27 @@ pf_gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__
                 const uint8_t *raw = sQ + q_slot * kPfRawBytes;
                 uint8_t *dst = sD + d_slot * P::D_BYTES;
                 const int sub = ks % KPR;
+                if (vmask == (1u << UPT) - 1u) {
+                    // every unit valid (all but a matrix's last n-tile): loads,
+                    // decodes and stores of the units as independent chains
+                    if (sub == 0) {
+#pragma unroll
+                        for (int r = 0; r < UPT; ++r) {
+                            recs[r] = *reinterpret_cast<const uint4 *>(raw + u_rec[r]);
+                            if (FMT == FC_FMT_Q4) scs[r] = *reinterpret_cast<const uint2 *>(raw + u_scl[r]);
+                            else scs[r] = make_uint2(*reinterpret_cast<const uint32_t *>(raw + u_scl[r]), 0u);
+                        }
+                    }
+                    uint32_t o[UPT][8];
+#pragma unroll
+                    for (int r = 0; r < UPT; ++r) pf_dequant_rec<FMT>(recs[r], scs[r], sub, o[r]);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+#pragma unroll
+                        for (int r = 0; r < UPT; ++r)
+                            *reinterpret_cast<uint2 *>(dst + (u_dst[r] ^ (uint32_t)(i << 5))) =
+                                make_uint2(o[r][2 * i], o[r][2 * i + 1]);
+                } else
 #pragma unroll
                 for (int r = 0; r < UPT; ++r) {
                     if (!((vmask >> r) & 1u)) continue;
