@@ -230,54 +230,184 @@ def kernel_bytes(cfg, name, rows, context, n_active):
     return None
 
 
+def _dequant(O, fmt, values, scale_bytes, rows, cols):
+    """fp32 [rows][cols] from the oracle's logical tensor bytes."""
+    if fmt == 1:
+        v = values.view(np.int8).reshape(rows, cols).astype(np.float32)
+        sc = scale_bytes.view(np.float16).astype(np.float32).reshape(rows, cols // 32)
+    else:
+        b = values.reshape(rows, cols // 2)
+        codes = np.empty((rows, cols), dtype=np.uint8)
+        codes[:, 0::2] = b & 15
+        codes[:, 1::2] = b >> 4
+        if fmt == 2:
+            v = codes.astype(np.float32) - 8.0
+            sc = scale_bytes.view(np.float16).astype(np.float32).reshape(rows, cols // 32)
+        else:
+            table = np.array([O.lib().orc_e2m1_to_f32(c) for c in range(16)], dtype=np.float32)
+            v = table[codes]
+            sc = np.array([O.lib().orc_e8m0_to_f32(e) for e in range(256)],
+                          dtype=np.float32)[scale_bytes].reshape(rows, cols // 32)
+    return (v.reshape(rows, cols // 32, 32) * sc[:, :, None]).reshape(rows, cols)
+
+
+class CpuSample:
+    """The CPU implementation of one verify step, timed on this host on a
+    bounded sample and extrapolated to the full step:
+      - attention: the oracle's C restatement of absorbed MLA
+        (moonlight_kernels.metal:132-375) on one layer at the full context;
+      - MoE: the reference's own moe_f32_forward (moe_exec.h:65-114, built from
+        the reference headers into oracle/_ref/libref_harness.so) on fp32
+        weights dequantized from the same synthetic experts (the reference
+        path runs on pre-dequantized weights); where that library was not
+        built, the oracle's MoE (kind "port");
+      - lm-head: the oracle's q8 GEMV on a vocab slice.
+    step_s = layers x (attention + MoE) + head x vocab / slice."""
+
+    def __init__(self, cfg, rows):
+        import ctypes
+        from oracle import oracle as O
+        from floyd_b200.configs import scaled
+        self.O, self.cfg, self.rows = O, cfg, rows
+        self.cores = os.cpu_count() or 1
+        os.environ.setdefault("OMP_NUM_THREADS", str(self.cores))
+        K = cfg["experts_per_token"]
+        # the per-token work depends on top-k, not on the expert count
+        self.E = min(cfg["expert_count"], 2 * K)
+        self.vslice = 8192
+        ctx = cfg["context"]
+        sl = scaled(cfg, layer_count=1, first_dense_layer_count=0, hash_layer_count=0,
+                    expert_count=self.E, vocab_size=self.vslice, mtp_layers=0)
+        self.m = O.OracleModel(sl, 0)
+        self.s = O.OracleSession(self.m, ctx + rows + 1, kv_fp16=True)
+        self.s.seed_context(ctx, 7)
+        self.ctx = ctx
+        rng = np.random.default_rng(0)
+        D, I = cfg["hidden_size"], cfg["moe_intermediate_size"]
+        self.x = rng.standard_normal((rows, D)).astype(np.float32)
+        self.ref = None
+        harness = os.path.join(ROOT, "oracle", "_ref", "libref_harness.so")
+        if os.path.exists(harness):
+            L = ctypes.CDLL(harness)
+            FP = ctypes.POINTER(ctypes.c_float)
+            L.ref_moe_forward.argtypes = [ctypes.c_int] * 6 + [
+                ctypes.c_float, ctypes.c_float, FP, FP, ctypes.c_void_p, ctypes.c_int, FP,
+                ctypes.c_int, FP, FP, ctypes.POINTER(ctypes.c_int), ctypes.c_int, FP]
+            ef, df = cfg["expert_format"], cfg["dense_format"]
+
+            def mat(name, fmt, r, c):
+                vb = r * c if fmt == 1 else r * c // 2
+                sb = r * (c // 32) * (1 if fmt == 3 else 2)
+                return _dequant(O, fmt, self.m.get_tensor(name, vb), self.m.get_tensor(name, sb, True), r, c)
+
+            pre = "model.layers.0.mlp."
+            ew = np.empty((self.E, 3, I * D), dtype=np.float32)
+            for e in range(self.E):  # w1 = gate, w2 = down, w3 = up
+                ew[e, 0] = mat(f"{pre}experts.{e}.gate_proj.weight", ef, I, D).ravel()
+                ew[e, 1] = mat(f"{pre}experts.{e}.down_proj.weight", ef, D, I).ravel()
+                ew[e, 2] = mat(f"{pre}experts.{e}.up_proj.weight", ef, I, D).ravel()
+            nsh = cfg["shared_expert_count"]
+            sw = np.empty((max(nsh, 1), 3, I * D), dtype=np.float32)
+            if nsh:
+                g = mat(pre + "shared_experts.gate_proj.weight", df, nsh * I, D)
+                dn = mat(pre + "shared_experts.down_proj.weight", df, D, nsh * I)
+                u = mat(pre + "shared_experts.up_proj.weight", df, nsh * I, D)
+                for j in range(nsh):
+                    sw[j, 0] = g[j * I:(j + 1) * I].ravel()
+                    sw[j, 1] = np.ascontiguousarray(dn[:, j * I:(j + 1) * I]).ravel()
+                    sw[j, 2] = u[j * I:(j + 1) * I].ravel()
+            router = self.m.get_tensor(pre + "gate.weight", self.E * D * 4).view(np.float32).copy()
+            bias = (self.m.get_tensor(pre + "gate.e_score_correction_bias", self.E * 4).view(np.float32).copy()
+                    if cfg["has_selection_bias"] else None)
+            self.ref = (L, FP, ew, nsh, sw, router, bias)
+        vals = rng.integers(-127, 128, size=(self.vslice, D), dtype=np.int8)
+        self.head = (vals, np.full((self.vslice, D // 32), 1e-3, dtype=np.float32))
+
+    def step(self):
+        """One sample; returns the extrapolated step time in seconds."""
+        O, cfg, rows = self.O, self.cfg, self.rows
+        D, I = cfg["hidden_size"], cfg["moe_intermediate_size"]
+        self.s.set_position(self.ctx)
+        O.part_times()
+        self.s.forward(list(range(1, rows + 1)))
+        t_attn, t_ffn = O.part_times()
+        if self.ref is not None:
+            L, FP, ew, nsh, sw, router, bias = self.ref
+            out = np.zeros((rows, D), dtype=np.float32)
+            t0 = time.perf_counter()
+            ok = L.ref_moe_forward(D, I, self.E, cfg["experts_per_token"], cfg["score_fn"],
+                                   cfg["normalize_topk"], cfg["routed_scale"], cfg["swiglu_limit"],
+                                   router.ctypes.data_as(FP),
+                                   bias.ctypes.data_as(FP) if bias is not None else None, None,
+                                   cfg["vocab_size"], ew.ctypes.data_as(FP), nsh, sw.ctypes.data_as(FP),
+                                   self.x.ctypes.data_as(FP), None, rows, out.ctypes.data_as(FP))
+            t_moe = time.perf_counter() - t0
+            if not ok:
+                raise RuntimeError("reference moe_f32_forward failed")
+        else:
+            t_moe = t_ffn
+        t0 = time.perf_counter()
+        O.gemv(1, self.head[0], self.head[1], self.x)
+        t_head = time.perf_counter() - t0
+        self.last = (t_attn, t_moe, t_head)
+        return cfg["layer_count"] * (t_attn + t_moe) + t_head * cfg["vocab_size"] / self.vslice
+
+    def describe(self, commit, t_step):
+        t_attn, t_moe, t_head = self.last
+        cfg = self.cfg
+        return {"value": commit / t_step, "unit": "tok/s", "cores": self.cores,
+                "kind": "reference" if self.ref is not None else "port",
+                "sample": (f"{cfg['_name']}: 1 layer at ctx {self.ctx}, {self.rows} rows - attention by the "
+                           f"oracle's MLA restatement ({t_attn * 1e3:.1f} ms, OpenMP {self.cores} threads), "
+                           + (f"MoE by the reference's moe_f32_forward on dequantized fp32 experts "
+                              f"({self.E} of them, top-{cfg['experts_per_token']}; {t_moe * 1e3:.1f} ms, "
+                              f"1 thread as the reference runs it)" if self.ref is not None else
+                              f"MoE by the oracle port ({t_moe * 1e3:.1f} ms)")
+                           + f", {self.vslice}-row q8 lm-head slice ({t_head * 1e3:.1f} ms); extrapolated to "
+                           f"{cfg['layer_count']} layers and vocab {cfg['vocab_size']}: step "
+                           f"{t_step * 1e3:.1f} ms x mean commit {commit:.3f}"),
+                "step_ms": t_step * 1e3}
+
+    def close(self):
+        self.s.close()
+        self.m.close()
+
+
 def cpu_baseline(cfg, rows, mean_commit, budget_s=20.0):
-    """The oracle port timed on this host on a bounded sample: one MoE layer of
-    the config (experts cut to the ones a 4-row verify can touch; the per-token
-    work is unchanged) plus a vocab slice of the lm-head, extrapolated to the
-    full step."""
-    from oracle import oracle as O
-    from floyd_b200.configs import scaled
-    cores = os.cpu_count() or 1
-    os.environ.setdefault("OMP_NUM_THREADS", str(cores))
-    E = min(cfg["expert_count"], rows * cfg["experts_per_token"])
-    vslice = 8192
-    ctx = cfg["context"]
-    sl = scaled(cfg, layer_count=1, first_dense_layer_count=0, hash_layer_count=0,
-                expert_count=E, vocab_size=vslice)
-    m = O.OracleModel(sl, 0)
-    s = O.OracleSession(m, ctx + rows + 1, kv_fp16=True)
-    s.seed_context(ctx, 7)
+    """CpuSample timed for up to `budget_s` (at most 5 samples, median)."""
+    cs = CpuSample(cfg, rows)
     times = []
     t_end = time.time() + budget_s
     while time.time() < t_end and len(times) < 5:
-        s.set_position(ctx)
-        t0 = time.perf_counter()
-        s.forward(list(range(1, rows + 1)))
-        times.append(time.perf_counter() - t0)
-    t_slice = float(np.median(times))
-    # the vocab-slice head on its own
-    rng = np.random.default_rng(0)
-    vals = rng.integers(-127, 128, size=(vslice, cfg["hidden_size"]), dtype=np.int8)
-    sc = np.full((vslice, cfg["hidden_size"] // 32), 1e-3, dtype=np.float32)
-    x = rng.standard_normal((rows, cfg["hidden_size"])).astype(np.float32)
-    t0 = time.perf_counter()
-    O.gemv(1, vals, sc, x)
-    t_head = time.perf_counter() - t0
-    t_layer = max(t_slice - t_head, 1e-9)
-    t_step = cfg["layer_count"] * t_layer + t_head * cfg["vocab_size"] / vslice
-    m.close()
-    return {"value": mean_commit / t_step, "unit": "tok/s", "cores": cores, "kind": "port",
-            "sample": (f"oracle (C, OpenMP {cores} threads) on 1 MoE layer of {cfg['_name']} "
-                       f"({E} experts, ctx {ctx}, {rows} rows) + {vslice}-row lm-head slice, "
-                       f"extrapolated to {cfg['layer_count']} layers / vocab {cfg['vocab_size']}; "
-                       f"step {t_step * 1e3:.1f} ms x measured mean commit {mean_commit:.3f}"),
-            "step_ms": t_step * 1e3}
+        times.append(cs.step())
+    t = float(np.median(times))
+    out = cs.describe(mean_commit, t)
+    cs.close()
+    return out
+
+
+def planted_commit(args, vocab):
+    """Mean commit of the timed rounds: a planted round commits 1 + its
+    leading hits (the drafts that equal the target's greedy token), which
+    the GPU arm checks round by round (acceptance_mismatches), so both arms
+    count the same commits."""
+    plans = planted_rounds(None, args.warmup + args.steps, args.draft, args.accept_p, vocab, seed=1234)
+    tot = 0
+    for hits, _ in plans[args.warmup:]:
+        c = 1
+        for h in hits:
+            if not h:
+                break
+            c += 1
+        tot += c
+    return tot / args.steps
 
 
 def run_reference(args, d):
-    """--impl reference: the CPU implementation of the path (the oracle port;
-    the reference's verify path exists only in Metal and in the absent ds4
-    engine) timed on this host, one bounded sample per step."""
+    """--impl reference: the CPU implementation of the path timed on this
+    host's cores (CpuSample: the reference's moe_exec.h for the MoE, the
+    oracle's restatement for MLA; the reference's verify path itself exists
+    only in Metal and in the absent ds4 engine), one bounded sample per step."""
     if d.rank != 0:
         return None
     from floyd_b200.configs import CONFIGS
@@ -285,24 +415,24 @@ def run_reference(args, d):
     cfg["_name"] = args.config
     rows = args.draft + 1
     p = args.accept_p
-    expected = sum(p ** i for i in range(rows))
+    commit = planted_commit(args, cfg["vocab_size"])
+    cs = CpuSample(cfg, rows)
     for _ in range(args.warmup):
-        cpu_baseline(cfg, rows, expected, budget_s=2.0)
-    vals = []
+        cs.step()
     t0 = time.time()
-    for _ in range(args.steps):
-        vals.append(cpu_baseline(cfg, rows, expected, budget_s=2.0))
+    steps = [cs.step() for _ in range(args.steps)]
     wall = time.time() - t0
-    v = float(np.mean([x["value"] for x in vals]))
-    base = vals[-1]
-    base["value"] = v
-    base["sample"] += f"; expected commit 1+p+p^2+p^3 at p={p}"
+    t_step = float(np.mean(steps))
+    base = cs.describe(commit, t_step)
+    cs.close()
+    v = base["value"]
+    base["sample"] += f"; commit of the same planted rounds the GPU arm runs (p={p}, seed 1234)"
     return {"metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": float(np.mean([x["step_ms"] for x in vals])),
+            "warmup": args.warmup, "ms_per_step": t_step * 1e3,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8/fp4 x fp32",
             "data": "synthetic", "impl": "reference",
             "config": {"workload": args.config, "draft": args.draft, "accept_p": p,
-                       "context": cfg["context"]},
+                       "context": cfg["context"], "rows_per_verify": rows},
             "cpu_baseline": base,
             "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "wall_s": wall}
@@ -649,8 +779,10 @@ def run_ours(args, d):
         "acceptance_mismatches": int(d.sum(mismatches)),
         "sampling": samp,
         "roofline": roof,
-        "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 72, "d2h_bytes_per_step": 48,
-                "note": "fc_session_verify wall time with host id / result buffers"},
+        "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": floyd_b200.io_bytes()[0],
+                "d2h_bytes_per_step": floyd_b200.io_bytes()[1],
+                "note": ("fc_session_verify wall time with host id / result buffers; the bytes are "
+                         "the parameter and result records each verify copies (fc_io_bytes)")},
         "gpu_launches": None,
         "kernels": {k: {"ms": v[0], "launches": v[1]} for k, v in prof.items()},
         "clocks": clk,

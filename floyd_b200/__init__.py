@@ -49,6 +49,14 @@ def blocks_to_logical(block_type, blocks, rows, cols):
     return values, scales
 
 
+def io_bytes():
+    """(h2d, d2h) bytes of the parameter and result records every forward
+    pass copies (fc_io_bytes)."""
+    h, d = ctypes.c_size_t(), ctypes.c_size_t()
+    lib().fc_io_bytes(ctypes.byref(h), ctypes.byref(d))
+    return int(h.value), int(d.value)
+
+
 def lib():
     return _lib.load()
 

@@ -2142,6 +2142,11 @@ int fc_session_copy_row_logits(const FcSession *s, float *logits, int capacity_r
 
 int fc_session_last_kernel_count(const FcSession *s) { return s ? s->last_kernels : 0; }
 
+void fc_io_bytes(size_t *h2d, size_t *d2h) {
+    if (h2d) *h2d = sizeof(Staging);
+    if (d2h) *d2h = sizeof(Result);
+}
+
 int fc_session_drafts(const FcSession *s, int *drafts, int capacity) {
     if (!s || !drafts) return 0;
     int n = std::min(s->last_drafts, capacity);
@@ -2517,8 +2522,12 @@ __global__ void noalloc_pack_scales(int fmt, int O, int K, int kp, const uint8_t
 extern "C" int fc_matmul_noalloc(int format, float *y, const float *x, const void *values,
                                  const void *scales, int O, int K, int S, char *error,
                                  size_t error_size) {
-    if (!y || !x || !values || !scales || O <= 0 || K <= 0 || K % 32 || S < 1 || S > kMaxRows)
+    if (!y || !x || !values || !scales || O <= 0 || K <= 0 || K % 32 || S < 1)
         return set_error(error, error_size, "invalid matmul shape");
+    if (S > kMaxRows)
+        return set_error(error, error_size,
+                         "S=%d exceeds the %d-row limit of the no-allocation path "
+                         "(fc_matmul takes wider inputs)", S, kMaxRows);
     if (format != FC_FMT_Q8 && format != FC_FMT_Q4 && format != FC_FMT_MXFP4)
         return set_error(error, error_size, "unsupported format %d", format);
     const int kp = kpad(K);

@@ -327,6 +327,12 @@ int fc_session_drafts(const FcSession *session, int *drafts, int capacity);
  * graph; 0 for eager profiled passes).  No reference counterpart. */
 int fc_session_last_kernel_count(const FcSession *session);
 
+/* Bytes of the two host<->device copies every forward pass makes: the
+ * per-pass parameter record copied to the device at the head of the pass
+ * and the result record copied back at its tail (logits copies the caller
+ * asks for come on top).  No reference counterpart. */
+void fc_io_bytes(size_t *h2d, size_t *d2h);
+
 /* Expert parallelism across the GPUs of one box (no reference counterpart:
  * floyd has no communication backend; the contract follows the expert
  * partitioning of moe_exec.h:97-110 with one exchange per MoE layer).

@@ -33,13 +33,18 @@ int fc_matmul(int format, float *y, const float *x, const void *values,
  * cudaMalloc at all - code running under a caching allocator that owns all
  * free device memory, an embedding host whose memory policy forbids driver
  * allocations, or a path that must not fail on out-of-memory.  Same arguments
- * and result as fc_matmul (no counterpart in the reference).  Its working
- * memory is one fixed device array of about 14 MiB that every GPU loading
- * this library keeps until exit, so it accepts only: weight image (tile-major
- * values + scales) <= 6 MiB, packed values <= 6 MiB, S*K*4 <= 256 KiB,
- * S*O*4 <= 512 KiB; larger shapes are rejected with an error.  The first call
- * on a device looks up the array's device address and should come before
- * any stream capture on that device.  All calls share the array: calls that
+ * and result as fc_matmul for S <= 8 rows, the GEMV path (no counterpart in
+ * the reference; wider inputs are rejected, fc_matmul takes them).  Its
+ * working memory is one fixed device array of about 14 MiB that every GPU
+ * loading this library keeps until exit, so it accepts only: weight image
+ * (tile-major values + scales) <= 6 MiB, packed values <= 6 MiB,
+ * S*K*4 <= 256 KiB, S*O*4 <= 512 KiB; larger shapes are rejected with an
+ * error.  The array becomes resident when the library's device code is
+ * loaded on a device, which under CUDA's lazy module loading may be this
+ * entry point's first call: make that first call (or any other call of this
+ * library on that device) before the host's allocator claims the free device
+ * memory, and before any stream capture on that device, since it also looks
+ * up the array's device address.  All calls share the array: calls that
  * overlap on the GPU (from several host threads) race and must not. */
 int fc_matmul_noalloc(int format, float *y, const float *x, const void *values,
                       const void *scales, int O, int K, int S, char *error,

@@ -14,6 +14,7 @@
 #include "floyd_oracle.h"
 
 #include <math.h>
+#include <omp.h>
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
@@ -283,6 +284,12 @@ typedef struct {
     float *scales;    /* [O][K/32]                                         */
     uint16_t *scale_bits; /* fp16 bits or e8m0 byte per group              */
     float *f32;       /* [O][K] for F32                                    */
+    int pending;      /* 1: not generated yet (routed experts are generated
+                         on first use, so full-width configs with hundreds of
+                         experts need host memory only for the ones a test
+                         touches)                                           */
+    uint64_t seed;
+    uint32_t tid;
 } Mat;
 
 typedef struct {
@@ -371,6 +378,20 @@ static void mat_gen(Mat *m, int fmt, int O, int K, uint64_t seed, uint32_t tid) 
     }
 }
 
+/* Deferred generation: the same values mat_gen would make, produced when
+ * the matrix is first read or written. */
+static void mat_defer(Mat *m, int fmt, int O, int K, uint64_t seed, uint32_t tid) {
+    memset(m, 0, sizeof(*m));
+    m->fmt = fmt; m->O = O; m->K = K; m->seed = seed; m->tid = tid; m->pending = 1;
+}
+
+static void mat_ensure(Mat *m) {
+    if (m->pending) {
+        m->pending = 0;
+        mat_gen(m, m->fmt, m->O, m->K, m->seed, m->tid);
+    }
+}
+
 static void mat_free(Mat *m) {
     free(m->values); free(m->scales); free(m->scale_bits); free(m->f32);
     memset(m, 0, sizeof(*m));
@@ -447,9 +468,9 @@ OrcModel *orc_model_create(const FcModelConfig *config, uint64_t seed) {
         y->up = (Mat *)calloc((size_t)E, sizeof(Mat));
         y->down = (Mat *)calloc((size_t)E, sizeof(Mat));
         for (int e = 0; e < E; ++e) {
-            mat_gen(&y->gate[e], ef, I, D, seed, fc_tensor_id(l, FC_T_EXP_GATE, e + 1));
-            mat_gen(&y->up[e], ef, I, D, seed, fc_tensor_id(l, FC_T_EXP_UP, e + 1));
-            mat_gen(&y->down[e], ef, D, I, seed, fc_tensor_id(l, FC_T_EXP_DOWN, e + 1));
+            mat_defer(&y->gate[e], ef, I, D, seed, fc_tensor_id(l, FC_T_EXP_GATE, e + 1));
+            mat_defer(&y->up[e], ef, I, D, seed, fc_tensor_id(l, FC_T_EXP_UP, e + 1));
+            mat_defer(&y->down[e], ef, D, I, seed, fc_tensor_id(l, FC_T_EXP_DOWN, e + 1));
         }
         if (c->shared_expert_count > 0) {
             int W = I * c->shared_expert_count;
@@ -519,9 +540,10 @@ static int lookup(OrcModel *m, const char *name, Mat **mat, float **vec, size_t 
     if (!strcmp(rest, "mlp.shared_experts.down_proj.weight")) { *mat = &y->sh_down; return 1; }
     char proj[64];
     if (sscanf(rest, "mlp.experts.%d.%63s", &e, proj) == 2 && e >= 0 && e < c->expert_count) {
-        if (!strcmp(proj, "gate_proj.weight")) { *mat = &y->gate[e]; return 1; }
-        if (!strcmp(proj, "up_proj.weight")) { *mat = &y->up[e]; return 1; }
-        if (!strcmp(proj, "down_proj.weight")) { *mat = &y->down[e]; return 1; }
+        if (!strcmp(proj, "gate_proj.weight")) *mat = &y->gate[e];
+        if (!strcmp(proj, "up_proj.weight")) *mat = &y->up[e];
+        if (!strcmp(proj, "down_proj.weight")) *mat = &y->down[e];
+        if (*mat) { mat_ensure(*mat); return 1; }
     }
     return 0;
 }
@@ -651,6 +673,7 @@ static float silu(float x) { return x / (1.0f + expf(-x)); }
  * coefficient * down(swiglu(gate x, up x)) into out. */
 static void add_expert(const Mat *gate, const Mat *up, const Mat *down, const float *x,
                        float coefficient, float limit, float *out, float *tmp) {
+    mat_ensure((Mat *)gate); mat_ensure((Mat *)up); mat_ensure((Mat *)down);
     int I = gate->O, D = down->O;
     float *g = tmp, *u = tmp + I, *h = tmp + 2 * I, *p = tmp + 3 * I;
     mat_apply(gate, x, 1, g);
@@ -741,6 +764,17 @@ int orc_moe_forward_f32(int hidden, int intermediate, int n_experts, int top_k, 
     return ok;
 }
 
+/* Wall time spent in the attention blocks and in the FFN / MoE blocks of
+ * run_layers since the last orc_part_times call (bench.py's CPU baseline
+ * splits a layer with it). */
+static double g_t_attn, g_t_ffn;
+
+void orc_part_times(double *attn_s, double *ffn_s) {
+    if (attn_s) *attn_s = g_t_attn;
+    if (ffn_s) *ffn_s = g_t_ffn;
+    g_t_attn = g_t_ffn = 0.0;
+}
+
 /* Layers [l0, l1) over the residual rows x at positions pos .. pos+rows-1
  * (the MTP layer is layer_count; its cache follows the target's). */
 static int run_layers(OrcSession *s, float *x, int rows, int pos, const int *ids, int l0, int l1,
@@ -772,6 +806,7 @@ static int run_layers(OrcSession *s, float *x, int rows, int pos, const int *ids
         float *lat = s->latent + (size_t)l * s->ctx * L;
         float *rop = s->rope + (size_t)l * s->ctx * R;
         /* attention block, moonlight_metal.m:287-440 */
+        double t_a0 = omp_get_wtime();
         orc_rmsnorm(x, ly->attn_norm, rows, D, c->rms_norm_epsilon, xn);
         if (c->q_lora_rank > 0) {
             mat_apply(&ly->q_a, xn, rows, qa);
@@ -853,6 +888,8 @@ static int run_layers(OrcSession *s, float *x, int rows, int pos, const int *ids
         for (size_t i = 0; i < (size_t)rows * D; ++i) x[i] += ao[i];
 
         /* FFN block */
+        double t_f0 = omp_get_wtime();
+        g_t_attn += t_f0 - t_a0;
         orc_rmsnorm(x, ly->ffn_norm, rows, D, c->rms_norm_epsilon, xn);
         for (int r = 0; r < rows; ++r) {
             const float *xr = xn + (int64_t)r * D;
@@ -871,6 +908,7 @@ static int run_layers(OrcSession *s, float *x, int rows, int pos, const int *ids
             }
             for (int d = 0; d < D; ++d) x[(int64_t)r * D + d] += y[d];
         }
+        g_t_ffn += omp_get_wtime() - t_f0;
         if (layer_out) memcpy(layer_out + (size_t)l * rows * D, x, (size_t)rows * D * sizeof(float));
     }
     free(xn); free(q); free(qa); free(ckv); free(attn); free(tmp); free(y); free(ao);

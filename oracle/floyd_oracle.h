@@ -136,6 +136,10 @@ int orc_session_verify(OrcSession *session, const int *ids, int k,
                        int *n_emitted, int *next_token, float *row_logits,
                        int *row_tops);
 
+/* Wall seconds spent in the attention and in the FFN / MoE blocks of the
+ * forwards since the previous call; resets both. */
+void orc_part_times(double *attn_s, double *ffn_s);
+
 #ifdef __cplusplus
 }
 #endif

@@ -61,6 +61,7 @@ def lib():
             "orc_session_copy_kv": (I, [P, I, FP, FP, I]),
             "orc_session_verify": (I, [P, IP, I, ctypes.POINTER(FcAcceptConfig), IP, IP, IP, FP, IP]),
             "orc_session_drafts": (I, [P, IP, I]),
+            "orc_part_times": (None, [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double)]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -114,6 +115,13 @@ def route(logits, bias, top_k, score_fn, normalize, scale, fixed=None):
     n = lib().orc_route(_fp(logits), bp, E, top_k, score_fn, normalize, scale,
                         _ip(fx) if fx is not None else None, _ip(idx), _fp(w))
     return n, idx, w
+
+
+def part_times():
+    """(attention s, ffn s) spent by oracle forwards since the last call."""
+    a, f = ctypes.c_double(), ctypes.c_double()
+    lib().orc_part_times(ctypes.byref(a), ctypes.byref(f))
+    return a.value, f.value
 
 
 class OracleModel:

@@ -62,3 +62,13 @@ def test_noalloc_rejects_shapes_beyond_its_workspace(fc):
     x = np.zeros((1, K), dtype=np.float32)
     ok, _, e = call(lib.fc_matmul_noalloc, 1, values, bits, x, O, K)
     assert not ok and b"exceeds" in e
+
+
+def test_noalloc_rejects_more_than_eight_rows(fc):
+    lib = fc.lib()
+    O, K, S = 64, 64, 9
+    values = np.zeros((O, K), dtype=np.uint8)
+    bits = np.zeros((O, K // 32), dtype=np.uint16)
+    x = np.zeros((S, K), dtype=np.float32)
+    ok, _, e = call(lib.fc_matmul_noalloc, 1, values, bits, x, O, K)
+    assert not ok and b"8-row limit" in e
