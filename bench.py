@@ -55,6 +55,8 @@ def parse():
     ap.add_argument("--batch-steps", type=int, default=10,
                     help="configs[4] leg: timed batched verify steps per acceptance rate (0 = skip)")
     ap.add_argument("--batch-warmup", type=int, default=2)
+    ap.add_argument("--decode-steps", type=int, default=200,
+                    help="configs[1] leg: timed greedy decodes of the Moonlight q8 model (0 = skip)")
     ap.add_argument("--prefill-layers", type=int, default=None,
                     help="configs[2] leg with fewer layers (a small case of the same kernels, for profilers)")
     ap.add_argument("--prefill-only", action="store_true",
@@ -543,6 +545,55 @@ def prefill_leg(args, d):
     return out
 
 
+def decode_leg(args, d):
+    """the Moonlight-shaped q8 model (27 layers, vocab 163840),
+    plain greedy decode (draft 0, batch 1) at a seeded latent context of
+    4096 positions.  Device time of the graph replays per token, the same
+    through fc_session_decode with host logits (e2e), and the step's
+    algorithmic bytes (every weight the token reads once, the fp16 latent
+    cache, the fp32 router) over the measured HBM peak."""
+    import floyd_b200
+    from floyd_b200.configs import CONFIGS
+    name = "c2_moonlight_q8"
+    cfg = dict(CONFIGS[name])
+    ctx, n = cfg["context"], args.decode_steps
+    model = floyd_b200.Model(cfg, device=d.local, seed=0)
+    sess = floyd_b200.Session(model, ctx + n + 16, 1)
+    sess.seed_context(ctx, 7)
+    tok = 1
+    for _ in range(max(args.warmup, 3)):
+        tok = int(np.argmax(sess.decode(tok)))
+    sess.rollback(ctx)
+    tok = 1
+    s0 = sess.stats()
+    wall = 0.0
+    for _ in range(n):
+        t0 = time.perf_counter()
+        logits = sess.decode(tok)
+        wall += time.perf_counter() - t0
+        tok = int(np.argmax(logits))
+    gpu = sess.stats()["gpu_ms"] - s0["gpu_ms"]
+    kernels = sess.last_kernel_count()
+    # active experts per MoE layer of a one-row decode: exactly top-k
+    b = floyd_b200.step_bytes(cfg, 1, ctx + n // 2, cfg["experts_per_token"])
+    peak, peak_kind = measured_peaks()
+    us = gpu / n * 1e3
+    h2d, d2h = floyd_b200.io_bytes()
+    out = {"workload": name, "context": ctx, "steps": n, "layers": cfg["layer_count"],
+           "tok_s": n / (gpu / 1e3), "us_per_token": us,
+           "e2e": {"value": n / wall, "unit": "tok/s", "h2d_bytes_per_step": h2d,
+                   "d2h_bytes_per_step": d2h + cfg["vocab_size"] * 4,
+                   "note": "fc_session_decode wall time, logits copied to a host array each token"},
+           "step_hbm": {"algorithmic_bytes": b, "achieved_gbs": b / (us / 1e6) / 1e9,
+                        "frac": b / (us / 1e6) / 1e9 / peak, "peak": peak, "peak_kind": peak_kind},
+           "kernels_per_token": kernels,
+           "data": "synthetic (seeded q8 weights, latent KV prefix of 4096 positions)",
+           "timing": "CUDA events around each graph replay on the session stream, summed"}
+    sess.close()
+    model.close()
+    return out
+
+
 def batch_leg(args, d, model, cfg):
     """configs[4] on the C4 stand-in: 8 sequences verifying 1 + draft rows
     each in one batch session (floor(8 / rows) sequences per device pass),
@@ -633,6 +684,9 @@ def run_ours(args, d):
     prefill = None
     if args.prefill_tokens > 0 and d.world == 1:
         prefill = prefill_leg(args, d)
+    decode = None
+    if args.decode_steps > 0 and d.world == 1:
+        decode = decode_leg(args, d)
 
     t_setup = time.time()
     # N > 1: the routed experts are split across the N GPUs (contiguous id
@@ -787,6 +841,7 @@ def run_ours(args, d):
         "kernels": {k: {"ms": v[0], "launches": v[1]} for k, v in prof.items()},
         "clocks": clk,
         "prefill": prefill,
+        "decode": decode,
         "setup_s": setup_s,
         "device": model.device_name(),
     }

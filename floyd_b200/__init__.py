@@ -57,6 +57,24 @@ def io_bytes():
     return int(h.value), int(d.value)
 
 
+def accept_trials(logits, ids, mode=ACCEPT_SAMPLE, temperature=1.0, seed=0, counter=0, trials=1):
+    """The device acceptance kernels on given logits [rows][vocab] for
+    `trials` consecutive Philox counters (fc_test_accept); returns
+    (commits, next_tokens) arrays."""
+    logits = np.ascontiguousarray(logits, dtype=np.float32)
+    rows, vocab = logits.shape
+    ids = np.ascontiguousarray(ids, dtype=np.int32)
+    commits = np.zeros(trials, dtype=np.int32)
+    nxt = np.zeros(trials, dtype=np.int32)
+    acc = _lib.FcAcceptConfig(mode, temperature, seed, counter)
+    e = _err()
+    if not lib().fc_test_accept(logits.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), rows, vocab,
+                                _i32(ids)[1], ctypes.byref(acc), trials, _i32(commits)[1],
+                                _i32(nxt)[1], e, len(e)):
+        raise FloydError(e.value.decode())
+    return commits, nxt
+
+
 def lib():
     return _lib.load()
 

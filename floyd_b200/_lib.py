@@ -129,6 +129,7 @@ SIGNATURES = {
     "fc_test_kv_length": (_I, [_P, _I]),
     "fc_test_batch_page_table": (_I, [_I, _I, _I, _IP, _I]),
     "fc_test_copy_kv": (_I, [_P, _I, _FP, _FP, _I]),
+    "fc_test_accept": (_I, [_FP, _I, _I, _IP, ctypes.POINTER(FcAcceptConfig), _I, _IP, _IP, _C, _S]),
     "fc_test_copy_routes": (_I, [_P, _I, _IP, _I]),
     "fc_test_copy_layer_outputs": (_I, [_P, _FP, _I]),
     "fc_runtime_init": (_I, [ctypes.POINTER(FcRuntime), _P, _I, _I]),

@@ -2450,6 +2450,62 @@ extern "C" int fc_matmul(int format, float *y, const float *x, const void *value
 }
 
 // ===========================================================================
+// fc_test_accept: the acceptance kernels of the verify graph on caller-given
+// logits, for `trials` consecutive Philox counters (test hook).
+// ===========================================================================
+extern "C" int fc_test_accept(const float *logits, int rows, int vocab, const int *ids,
+                              const FcAcceptConfig *accept, int trials, int *commits,
+                              int *next_tokens, char *error, size_t error_size) {
+    if (!logits || !ids || !accept || !commits || !next_tokens || rows < 1 || rows > kMaxRows ||
+        vocab < 1 || trials < 1)
+        return set_error(error, error_size, "invalid acceptance test arguments");
+    if (accept->mode == FC_ACCEPT_SAMPLE && !(accept->temperature > 0.0f))
+        return set_error(error, error_size, "sampling needs a temperature > 0");
+    const int chunks = (vocab + kHeadChunk - 1) / kHeadChunk;
+    const size_t part = (size_t)rows * chunks;
+    float *d_logits = nullptr, *d_f = nullptr;
+    int *d_i = nullptr, *d_err = nullptr;
+    Staging *d_st = nullptr;
+    Result *d_res = nullptr;
+    cudaError_t e = cudaMalloc(&d_logits, (size_t)rows * vocab * 4);
+    if (e == cudaSuccess) e = cudaMalloc(&d_f, part * 4 * 4);
+    if (e == cudaSuccess) e = cudaMalloc(&d_i, part * 2 * 4);
+    if (e == cudaSuccess) e = cudaMalloc(&d_err, 4);
+    if (e == cudaSuccess) e = cudaMalloc(&d_st, sizeof(Staging));
+    if (e == cudaSuccess) e = cudaMalloc(&d_res, sizeof(Result));
+    if (e == cudaSuccess) e = cudaMemcpy(d_logits, logits, (size_t)rows * vocab * 4, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemset(d_err, 0, 4);
+    HeadPartials hp{};
+    hp.amax = d_f; hp.zmax = d_f + part; hp.zsum = d_f + 2 * part; hp.gval = d_f + 3 * part;
+    hp.aidx = d_i; hp.gidx = d_i + part;
+    Staging h{};
+    h.rows = rows;
+    h.k = rows - 1;
+    h.mode = accept->mode;
+    h.temperature = accept->mode == FC_ACCEPT_SAMPLE ? accept->temperature : 1.0f;
+    h.seed = accept->seed;
+    h.group_rows = rows;
+    h.groups = 1;
+    for (int r = 0; r < rows; ++r) h.ids[r] = ids[r];
+    Result res{};
+    for (int t = 0; t < trials && e == cudaSuccess; ++t) {
+        h.counter = accept->counter + (unsigned long long)t;
+        h.gcounter[0] = h.counter;
+        e = cudaMemcpy(d_st, &h, sizeof(Staging), cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) break;
+        head_partial_kernel<<<dim3(chunks, rows), 256>>>(d_logits, vocab, d_st, hp, chunks);
+        accept_kernel<<<1, 256>>>(d_logits, vocab, d_st, hp, chunks, d_res, d_err);
+        e = cudaGetLastError();
+        if (e == cudaSuccess) e = cudaMemcpy(&res, d_res, sizeof(Result), cudaMemcpyDeviceToHost);
+        commits[t] = res.commit;
+        next_tokens[t] = res.next_token;
+    }
+    cudaFree(d_logits); cudaFree(d_f); cudaFree(d_i); cudaFree(d_err); cudaFree(d_st); cudaFree(d_res);
+    if (e != cudaSuccess) return set_error(error, error_size, "acceptance test failed: %s", cudaGetErrorString(e));
+    return 1;
+}
+
+// ===========================================================================
 // fc_matmul_noalloc: fc_matmul for callers that must not allocate device
 // memory.  Its working memory is one fixed file-scope device array.
 // ===========================================================================

@@ -367,6 +367,16 @@ void fc_session_profile_reset(FcSession *session);
 /* ---- test hooks (moonlight_metal.h:69-96) -------------------------------- */
 
 int fc_test_kv_length(const FcSession *session, int layer);      /* :85 */
+/* The acceptance kernels of the verify graph (row argmax, softmax
+ * partials, Gumbel picks, the acceptance rule of fc_session_verify) run on
+ * caller-given logits [rows][vocab] with ids[0..rows-1] (ids[0] the target's
+ * token, ids[1..] the drafts, k = rows - 1), once for each of `trials`
+ * Philox counters accept->counter, accept->counter + 1, ...; writes each
+ * trial's commit and next token.  For distribution tests of the sampling
+ * rule, which has no counterpart in the reference. */
+int fc_test_accept(const float *logits, int rows, int vocab, const int *ids,
+                   const FcAcceptConfig *accept, int trials, int *commits,
+                   int *next_tokens, char *error, size_t error_size);
 /* The page table a batch session builds (host only, no GPU): fills
  * table[sequence][page] and returns the physical page count, -1 on invalid
  * options or a short buffer. */
