@@ -31,7 +31,7 @@ class FcModelConfig(ctypes.Structure):
         ("swiglu_limit", ctypes.c_float), ("rms_norm_epsilon", ctypes.c_float),
         ("rope_theta", ctypes.c_float), ("dense_format", ctypes.c_int),
         ("expert_format", ctypes.c_int), ("mtp_layers", ctypes.c_int),
-        ("resident_bytes", ctypes.c_uint64),
+        ("embed_f32", ctypes.c_int), ("resident_bytes", ctypes.c_uint64),
     ]
 
     @classmethod
@@ -75,7 +75,8 @@ class FcAcceptConfig(ctypes.Structure):
 class FcRuntime(ctypes.Structure):
     _fields_ = [("session", ctypes.c_void_p), ("logits", ctypes.POINTER(ctypes.c_float)),
                 ("vocab_size", ctypes.c_int), ("max_context", ctypes.c_int),
-                ("last_count", ctypes.c_int), ("last_start_position", ctypes.c_int)]
+                ("last_count", ctypes.c_int), ("last_start_position", ctypes.c_int),
+                ("dspark_ready", ctypes.c_int)]
 
 
 _P = ctypes.c_void_p
@@ -127,6 +128,20 @@ SIGNATURES = {
     "fc_session_profile_reset": (None, [_P]),
     "fc_session_set_layer_trace": (_I, [_P, _I]),
     "fc_test_kv_length": (_I, [_P, _I]),
+    "fc_test_embed": (_I, [_P, _IP, _I, _FP]),
+    "fc_test_rmsnorm": (_I, [_P, _FP, ctypes.c_char_p, _I, _I, _FP]),
+    "fc_test_matmul": (_I, [_P, ctypes.c_char_p, _FP, _I, _I, _I, _FP]),
+    "fc_test_attention": (_I, [_P, _I, _FP, _I, _I, _FP]),
+    "fc_test_moe": (_I, [_P, _I, _FP, _I, _IP, _FP, _FP, _FP, _FP, _FP]),
+    "fc_test_dense_mlp": (_I, [_P, _I, _FP, _I, _FP]),
+    "fc_test_prefill_layers": (_I, [_P, _IP, _I, _FP, _FP, _C, _S]),
+    "fc_model_open": (_I, [ctypes.POINTER(_P), ctypes.c_char_p, _I, _C, _S]),
+    "fm_init": (_I, []),
+    "fm_device_name": (ctypes.c_char_p, []),
+    "fm_matmul_q8": (None, [_FP, _FP, _P, _FP, _I, _I, _I, _I]),
+    "fm_matmul_q4": (None, [_FP, _FP, _P, _FP, _I, _I, _I, _I]),
+    "fm_matmul_deepseek_v4_fp8": (_I, [_FP, _FP, _P, _P, _I, _I, _I, _I]),
+    "fm_matmul_deepseek_v4_fp4": (_I, [_FP, _FP, _P, _P, _I, _I, _I]),
     "fc_test_batch_page_table": (_I, [_I, _I, _I, _IP, _I]),
     "fc_test_copy_kv": (_I, [_P, _I, _FP, _FP, _I]),
     "fc_test_accept": (_I, [_FP, _I, _I, _IP, ctypes.POINTER(FcAcceptConfig), _I, _IP, _IP, _C, _S]),
@@ -137,6 +152,8 @@ SIGNATURES = {
     "fc_runtime_argmax": (_I, [_FP, _I]),
     "fc_runtime_verify_token": (_I, [_FP, _I, ctypes.c_int64, _IP]),
     "fc_runtime_reset": (None, [ctypes.POINTER(FcRuntime)]),
+    "fc_runtime_dspark_prefill": (_I, [ctypes.POINTER(FcRuntime)]),
+    "fc_runtime_dspark_propose": (_I, [ctypes.POINTER(FcRuntime), _I, ctypes.POINTER(ctypes.c_int64), _FP]),
     "fc_runtime_free": (None, [ctypes.POINTER(FcRuntime)]),
     # include/floyd_kernels.h
     "fc_matmul": (_I, [_I, _FP, _FP, _P, _P, _I, _I, _I, _C, _S]),

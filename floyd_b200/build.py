@@ -14,7 +14,7 @@ ROOT = os.path.dirname(HERE)
 LIB = os.path.join(HERE, "libfloyd_cuda.so")
 SOURCES = [os.path.join(HERE, "csrc", "runtime.cu")]
 DEPS = SOURCES + [os.path.join(HERE, "csrc", f) for f in os.listdir(os.path.join(HERE, "csrc"))] + [
-    os.path.join(ROOT, "include", "floyd_cuda.h"), os.path.join(ROOT, "include", "floyd_synth.h")]
+    os.path.join(ROOT, "include", f) for f in os.listdir(os.path.join(ROOT, "include"))]
 
 
 def nvcc():

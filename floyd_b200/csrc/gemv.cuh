@@ -703,4 +703,74 @@ inline cudaError_t launch_gemv_batch(int fmt, GemvBatch &b, int sms, cudaStream_
     return launch_gemv_work(fmt, fmt, wk, sms, stream);
 }
 
+// ---------------------------------------------------------------------------
+// fp32-weight GEMV (an unquantized embedding-sized matrix, e.g. the fp32
+// lm-head of floyd's Moonlight container; moonlight_matmul_f32 in
+// moonlight_kernels.metal): y[s][o] = sum_k x[s][k] * w[o][k], w row-major
+// [O][K].  HBM-bound: one warp per output row streams the row with 16-byte
+// loads (the same rows for every activation row, so each weight byte is read
+// once per launch), the activations (decoded from the xq hi / lo halves) sit
+// in shared memory.  Each lane sums its columns in ascending k and the warp
+// reduces in a fixed butterfly, so a row's result does not depend on S.
+// ---------------------------------------------------------------------------
+constexpr int kF32GemvThreads = 256;
+constexpr int kF32MaxRows = 8;  // activation rows per launch
+
+__global__ void __launch_bounds__(kF32GemvThreads) f32_gemv_kernel(const float *w, int O, int K,
+                                                                    const __half *xq, int kp, int S,
+                                                                    float *y, int ldy) {
+    extern __shared__ float xs[];  // [S][K]
+    pdl_wait();
+    pdl_release();
+    for (int i = threadIdx.x; i < S * K; i += blockDim.x) {
+        const int s = i / K, k = i - s * K;
+        const __half *rec = xq + ((size_t)s * kp + (k & ~3)) * 2;
+        xs[i] = __half2float(rec[k & 3]) + __half2float(rec[4 + (k & 3)]);
+    }
+    __syncthreads();
+    const int lane = threadIdx.x & 31, warps = blockDim.x >> 5;
+    for (int o = blockIdx.x * warps + (threadIdx.x >> 5); o < O; o += gridDim.x * warps) {
+        const float4 *row = reinterpret_cast<const float4 *>(w + (size_t)o * K);
+        float acc[kF32MaxRows];
+#pragma unroll
+        for (int s = 0; s < kF32MaxRows; ++s) acc[s] = 0.0f;
+        for (int k4 = lane; k4 < K / 4; k4 += 32) {
+            const float4 v = __ldcs(row + k4);
+#pragma unroll
+            for (int s = 0; s < kF32MaxRows; ++s) {
+                if (s >= S) break;
+                const float4 x = *reinterpret_cast<const float4 *>(xs + (size_t)s * K + 4 * k4);
+                acc[s] = fmaf(v.x, x.x, acc[s]);
+                acc[s] = fmaf(v.y, x.y, acc[s]);
+                acc[s] = fmaf(v.z, x.z, acc[s]);
+                acc[s] = fmaf(v.w, x.w, acc[s]);
+            }
+        }
+#pragma unroll
+        for (int s = 0; s < kF32MaxRows; ++s) {
+            if (s >= S) break;
+            float v = acc[s];
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+            if (lane == 0) y[(size_t)s * ldy + o] = v;
+        }
+    }
+}
+
+inline cudaError_t launch_f32_gemv(const float *w, int O, int K, const __half *xq, int kp, int S,
+                                   float *y, int ldy, int sms, cudaStream_t stream) {
+    const size_t smem = (size_t)S * K * 4;
+    static bool attr_set = false;
+    if (!attr_set) {
+        cudaError_t e = cudaFuncSetAttribute(f32_gemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             200 * 1024);
+        if (e != cudaSuccess) return e;
+        attr_set = true;
+    }
+    const int warps = kF32GemvThreads / 32;
+    const int grid = std::min((O + warps - 1) / warps, sms * 4);
+    return launch_pdl(f32_gemv_kernel, dim3(grid), dim3(kF32GemvThreads), smem, stream, w, O, K, xq,
+                      kp, S, y, ldy);
+}
+
 }  // namespace fc

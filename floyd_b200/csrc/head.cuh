@@ -50,6 +50,7 @@ struct Result {
     int drafts[kMaxRows];   // MTP drafter proposals (verify with k > 0)
     int g_commit[kMaxRows];
     int g_next[kMaxRows];
+    float draft_conf[kMaxRows];  // the drafter's top-1 logit of each proposal
 };
 
 // Latent-cache paging: sequence `seq`'s position p lives at row
@@ -288,6 +289,31 @@ __global__ void mtp_prep_kernel(int i, const Staging *main_st, const Result *res
             mtp_h[d] = resid[(size_t)(commit - 1) * D + d];
 }
 
+// Final hidden rows (pre-norm residual) of a forward, stored by position
+// for the drafter's prefill (models with an MTP layer): hist[rowpos[r]] =
+// resid[r].
+__global__ void hist_store_kernel(const float *resid, const Staging *st, float *hist, int D) {
+    pdl_wait();
+    pdl_release();
+    const int r = blockIdx.y;
+    if (r >= st->rows) return;
+    float *dst = hist + (size_t)st->rowpos[r] * D;
+    for (int d = blockIdx.x * blockDim.x + threadIdx.x; d < D; d += gridDim.x * blockDim.x)
+        dst[d] = resid[(size_t)r * D + d];
+}
+
+// The same for T prefill rows at positions pos0 .. pos0 + T - 1, pos0 read
+// from the device (the prefill parameter record's first word).
+__global__ void hist_store_rows_kernel(const float *rows, const int *pos0, int T, float *hist, int D) {
+    pdl_wait();
+    pdl_release();
+    const int t = blockIdx.y;
+    if (t >= T) return;
+    float *dst = hist + ((size_t)*pos0 + t) * D;
+    for (int d = blockIdx.x * blockDim.x + threadIdx.x; d < D; d += gridDim.x * blockDim.x)
+        dst[d] = rows[(size_t)t * D + d];
+}
+
 // Greedy pick of the drafter's row (same order as the target's argmax:
 // NaN never wins, lower index on ties); writes proposal i.
 __global__ void __launch_bounds__(32) mtp_pick_kernel(HeadPartials hp, int chunks, Result *res,
@@ -308,6 +334,7 @@ __global__ void __launch_bounds__(32) mtp_pick_kernel(HeadPartials hp, int chunk
     if (lane == 0) {
         const int t = bi == 0x7fffffff ? 0 : bi;
         res->drafts[i] = t;
+        res->draft_conf[i] = bv;
         mst->ids[0] = t;
     }
 }

@@ -28,6 +28,7 @@ namespace fc {
 // Embedding gather (moonlight_kernels.metal:10-21) of a quantized table.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ float dequant_element(int fmt, const uint8_t *w, int kp, int row, int k) {
+    if (fmt == FC_FMT_F32) return reinterpret_cast<const float *>(w)[(size_t)row * kp + k];
     int nib;
     uint8_t byte = w[value_offset(fmt, kp, row, k, &nib)];
     const uint8_t *sp = w + scale_offset(fmt, kp, row, k >> 5);

@@ -24,7 +24,9 @@
 #include <vector>
 
 #include "../../include/floyd_kernels.h"
+#include "../../include/floyd_fm.h"
 #include "common.cuh"
+#include "container.h"
 #include "gemv.cuh"
 #include "head.cuh"
 #include "mla.cuh"
@@ -150,7 +152,13 @@ struct FcSession {
     Staging *d_mtp = nullptr;        // MTP drafter step parameters (device)
     float *mtp_h = nullptr;          // drafter hidden state [D]
     float *mtp_logits = nullptr;     // drafter logits [V] (the target's stay readable)
-    __half *mtp_xq = nullptr;        // [enorm(embed) | hnorm(h)] as xq, kpad(2D)
+    __half *mtp_xq = nullptr;        // [enorm(embed) | hnorm(h)] as xq, [rows_max][kpad(2D)]
+    float *hist = nullptr;           // final hidden row of every position [context][D] (MTP models)
+    std::vector<int> tok_hist;       // token id of every position (MTP models)
+    // routes of every row of the last fc_test_prefill_layers call
+    // [layers][rows][top-k]; cleared by the next forward
+    std::vector<int> route_trace;
+    int route_trace_rows = 0;
     int last_drafts = 0;             // proposals made by the last pass
     int *n_global = nullptr, *n_before = nullptr;  // global active experts / first global slot here
     int g_slots = 0;                 // global slots (active experts of all ranks) at most
@@ -277,8 +285,9 @@ int build_model(FcModel *m, char *err, size_t n) {
     const FcModelConfig &c = m->c;
     int D = c.hidden_size, H = c.head_count, L = c.kv_lora_rank, R = c.qk_rope_dim;
     int df = c.dense_format, ef = c.expert_format;
-    plan_mat(m->embed, df, c.vocab_size, D, 1, fc_tensor_id(-1, FC_T_EMBED, 0), 0);
-    plan_mat(m->lm_head, df, c.vocab_size, D, 1, fc_tensor_id(-1, FC_T_LM_HEAD, 0), 0);
+    const int hf = c.embed_f32 ? FC_FMT_F32 : df;
+    plan_mat(m->embed, hf, c.vocab_size, D, 1, fc_tensor_id(-1, FC_T_EMBED, 0), 0);
+    plan_mat(m->lm_head, hf, c.vocab_size, D, 1, fc_tensor_id(-1, FC_T_LM_HEAD, 0), 0);
     plan_vec(m->final_norm, D, fc_tensor_id(-1, FC_T_FINAL_NORM, 0), 1);
     m->layers.resize(c.layer_count + c.mtp_layers);
     int nl = m->expert_hi - m->expert_lo;
@@ -409,7 +418,11 @@ int grid_for(size_t n) { return (int)std::min<size_t>((n + 255) / 256, 148 * 16)
 
 cudaError_t fill_mat(const DevMat &mm, uint64_t seed, cudaStream_t st) {
     if (!mm.count) return cudaSuccess;
-    if (mm.fmt == FC_FMT_F32) return cudaSuccess;
+    if (mm.fmt == FC_FMT_F32) {
+        size_t n = (size_t)mm.O * mm.K * mm.count;
+        synth_f32_kernel<<<grid_for(n), 256, 0, st>>>(reinterpret_cast<float *>(mm.w), n, 0, seed, mm.tid);
+        return cudaGetLastError();
+    }
     size_t nb = (size_t)mm.O * mm.K / (mm.fmt == FC_FMT_Q8 ? 8 : 32) * mm.count;
     synth_values_kernel<<<grid_for(nb), 256, 0, st>>>(mm.fmt, mm.w, mm.O, mm.K, mm.kp, mm.count,
                                                       seed, mm.tid, mm.slot0);
@@ -536,6 +549,19 @@ cudaError_t gemv1(int fmt, GemvSeg a, int S, float limit, int *err, int sms, cud
     return launch_gemv_batch(fmt, b, sms, st);
 }
 
+// The lm-head over S rows of xq activations: the quantized GEMV, or the fp32
+// GEMV when the model keeps its lm-head unquantized.
+cudaError_t head_gemv(const FcModel *m, const __half *xq, int S, float *y, int *err, cudaStream_t st) {
+    const DevMat &h = m->lm_head;
+    if (h.fmt == FC_FMT_F32)
+        return launch_f32_gemv(reinterpret_cast<const float *>(h.w), h.O, h.K, xq, kpad(h.K), S, y, h.O,
+                               m->sms, st);
+    GemvSeg g = seg_of(h, xq, EPI_STORE);
+    g.y = y;
+    g.ldy = h.O;
+    return gemv1(h.fmt, g, S, 0.0f, err, m->sms, st);
+}
+
 // 2-D fp16 tensor map [rows][inner] with a {64, box_rows} box and the
 // 128-byte swizzle the tcgen05 descriptors expect.
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
@@ -593,7 +619,11 @@ void mark(FcSession *s, const char *name) {
 // Enqueues layer l (target layers 0 .. layer_count - 1, the MTP layer at
 // layer_count) for S rows at positions *d_pos + s, updating s->resid.
 // `ids` are the rows' token ids (hash routing).
-cudaError_t record_layer(FcSession *s, int S, int l, const Staging *dst) {
+// The attention block of layer l over S rows whose normalized input is
+// already in xq_norm: q / kv_a projections, KV append, absorbed attention,
+// W_UV, and o_proj through epilogue `o_epi` into `o_y` (EPI_ADD into the
+// residual in a forward; EPI_STORE for the attention test hook).
+cudaError_t record_attention(FcSession *s, int S, int l, const Staging *dst, int o_epi, float *o_y) {
     FcModel *m = s->m;
     const FcModelConfig &c = m->c;
     cudaStream_t st = s->stream;
@@ -608,9 +638,7 @@ cudaError_t record_layer(FcSession *s, int S, int l, const Staging *dst) {
     (void)ef;
     DevLayer &y = m->layers[l];
     __half *cache = s->cache + (size_t)l * s->layer_rows * (L + R);
-    FC_TRY(launch_pdl(rmsnorm_kernel, dim3(S), dim3(norm_threads(D)), 0, st, s->resid, D, y.attn_norm.p, D, c.rms_norm_epsilon,
-                                      s->xq_norm, kpD, nullptr, 0));
-    mark(s, "rmsnorm");
+    (void)kpD;
     {
         GemvBatch b{};
         b.S = S;
@@ -699,15 +727,29 @@ cudaError_t record_layer(FcSession *s, int S, int l, const Staging *dst) {
         mark(s, "gemv_w_uv");
     }
     {
-        GemvSeg g = seg_of(y.o_proj, s->o_xq, EPI_ADD);
-        g.y = s->resid;
+        GemvSeg g = seg_of(y.o_proj, s->o_xq, o_epi);
+        g.y = o_y;
         g.ldy = D;
         FC_TRY(gemv1(df, g, S, 0.0f, s->d_err, m->sms, st));
         mark(s, "gemv_o_proj");
     }
-    FC_TRY(launch_pdl(rmsnorm_kernel, dim3(S), dim3(norm_threads(D)), 0, st, s->resid, D, y.ffn_norm.p, D, c.rms_norm_epsilon,
-                                      s->xq_norm, kpD, s->xn, D));
-    mark(s, "rmsnorm");
+    return cudaSuccess;
+}
+
+// The FFN block of layer l over S rows whose normalized input is in xq_norm
+// (xq) and xn (fp32, the router's input): the dense MLP, or router + routed
+// and shared experts + combine, added into `out` (the residual in a
+// forward).  `routed_only`: the combine leaves out the shared expert (the
+// MoE test hook reads the shared output from sh_part).
+cudaError_t record_ffn(FcSession *s, int S, int l, const Staging *dst, float *out, int dense_epi,
+                       bool routed_only) {
+    FcModel *m = s->m;
+    const FcModelConfig &c = m->c;
+    cudaStream_t st = s->stream;
+    const int D = c.hidden_size;
+    const int mb = s->rows_max;
+    const int df = c.dense_format, ef = c.expert_format;
+    DevLayer &y = m->layers[l];
     if (y.dense) {
         int kpI = kpad(c.dense_intermediate_size);
         GemvSeg g = seg_of(y.d_gate, s->xq_norm, EPI_SWIGLU_XQ);
@@ -716,8 +758,8 @@ cudaError_t record_layer(FcSession *s, int S, int l, const Staging *dst) {
         g.kpy = kpI;
         FC_TRY(gemv1(df, g, S, 0.0f, s->d_err, m->sms, st));
         mark(s, "gemv_dense_gate_up");
-        GemvSeg d = seg_of(y.d_down, s->hd_xq, EPI_ADD);
-        d.y = s->resid;
+        GemvSeg d = seg_of(y.d_down, s->hd_xq, dense_epi);
+        d.y = out;
         d.ldy = D;
         FC_TRY(gemv1(df, d, S, 0.0f, s->d_err, m->sms, st));
         mark(s, "gemv_dense_down");
@@ -824,11 +866,30 @@ cudaError_t record_layer(FcSession *s, int S, int l, const Staging *dst) {
             mark(s, "ep_signal");
         }
         FC_TRY(launch_pdl(moe_combine_kernel, dim3(S * ((D + kMoeCombineThreads - 1) / kMoeCombineThreads)),
-                          dim3(kMoeCombineThreads), 0, st, s->resid, ep ? (const float *)s->ep_xbuf : s->moe_part,
-                          y.s_down.count ? (const float *)s->sh_part : nullptr, (const float *)s->coef,
-                          (const int *)s->n_global, S, D, mb, link, parity_stride, s->d_err));
+                          dim3(kMoeCombineThreads), 0, st, out, ep ? (const float *)s->ep_xbuf : s->moe_part,
+                          (y.s_down.count && !routed_only) ? (const float *)s->sh_part : nullptr,
+                          (const float *)s->coef, (const int *)s->n_global, S, D, mb, link, parity_stride,
+                          s->d_err));
         mark(s, "moe_combine");
     }
+    return cudaSuccess;
+}
+
+cudaError_t record_layer(FcSession *s, int S, int l, const Staging *dst) {
+    FcModel *m = s->m;
+    const FcModelConfig &c = m->c;
+    cudaStream_t st = s->stream;
+    const int D = c.hidden_size, kpD = kpad(D);
+    const int mb = s->rows_max;
+    DevLayer &y = m->layers[l];
+    FC_TRY(launch_pdl(rmsnorm_kernel, dim3(S), dim3(norm_threads(D)), 0, st, s->resid, D, y.attn_norm.p, D, c.rms_norm_epsilon,
+                                      s->xq_norm, kpD, nullptr, 0));
+    mark(s, "rmsnorm");
+    FC_TRY(record_attention(s, S, l, dst, EPI_ADD, s->resid));
+    FC_TRY(launch_pdl(rmsnorm_kernel, dim3(S), dim3(norm_threads(D)), 0, st, s->resid, D, y.ffn_norm.p, D, c.rms_norm_epsilon,
+                                      s->xq_norm, kpD, s->xn, D));
+    mark(s, "rmsnorm");
+    FC_TRY(record_ffn(s, S, l, dst, s->resid, EPI_ADD, false));
     if (s->trace && l < c.layer_count) {
         FC_TRY(cudaMemcpyAsync(s->layer_out + (size_t)l * mb * D, s->resid, (size_t)S * D * 4,
                                cudaMemcpyDeviceToDevice, st));
@@ -845,7 +906,6 @@ cudaError_t record_forward(FcSession *s, int S, int drafts) {
     const FcModelConfig &c = m->c;
     cudaStream_t st = s->stream;
     const int D = c.hidden_size, kpD = kpad(D);
-    const int df = c.dense_format;
 
     FC_TRY(cudaMemcpyAsync(s->d_stage, s->h_stage, sizeof(Staging), cudaMemcpyHostToDevice, st));
     FC_TRY(launch_pdl(embed_kernel, dim3(S), dim3(256), 0, st, m->embed.fmt, m->embed.w, D, m->embed.kp, s->d_stage->ids,
@@ -853,16 +913,16 @@ cudaError_t record_forward(FcSession *s, int S, int drafts) {
     FC_TRY(cudaGetLastError());
     mark(s, "embed");
     for (int l = 0; l < c.layer_count; ++l) FC_TRY(record_layer(s, S, l, s->d_stage));
+    if (s->hist) {
+        FC_TRY(launch_pdl(hist_store_kernel, dim3((D + 255) / 256, S), dim3(256), 0, st, (const float *)s->resid,
+                          (const Staging *)s->d_stage, s->hist, D));
+        mark(s, "hist_store");
+    }
     FC_TRY(launch_pdl(rmsnorm_kernel, dim3(S), dim3(norm_threads(D)), 0, st, s->resid, D, m->final_norm.p, D, c.rms_norm_epsilon,
                                       s->xq_norm, kpD, nullptr, 0));
     mark(s, "rmsnorm");
-    {
-        GemvSeg g = seg_of(m->lm_head, s->xq_norm, EPI_STORE);
-        g.y = s->logits;
-        g.ldy = c.vocab_size;
-        FC_TRY(gemv1(df, g, S, 0.0f, s->d_err, m->sms, st));
-        mark(s, "gemv_lm_head");
-    }
+    FC_TRY(head_gemv(m, s->xq_norm, S, s->logits, s->d_err, st));
+    mark(s, "gemv_lm_head");
     {
         dim3 grid(s->head_chunks, S);
         FC_TRY(launch_pdl(head_partial_kernel, dim3(grid), dim3(256), 0, st, s->logits, c.vocab_size, s->d_stage, s->hp,
@@ -909,12 +969,7 @@ cudaError_t record_mtp_step(FcSession *s, int i) {
     FC_TRY(cudaMemcpyAsync(s->mtp_h, s->resid, (size_t)D * 4, cudaMemcpyDeviceToDevice, st));
     FC_TRY(launch_pdl(rmsnorm_kernel, dim3(1), dim3(norm_threads(D)), 0, st, (const float *)s->resid, D,
                       (const float *)y.head_norm.p, D, c.rms_norm_epsilon, s->xq_norm, kpD, (float *)nullptr, 0));
-    {
-        GemvSeg g = seg_of(m->lm_head, s->xq_norm, EPI_STORE);
-        g.y = s->mtp_logits;
-        g.ldy = c.vocab_size;
-        FC_TRY(gemv1(df, g, 1, 0.0f, s->d_err, m->sms, st));
-    }
+    FC_TRY(head_gemv(m, s->xq_norm, 1, s->mtp_logits, s->d_err, st));
     FC_TRY(launch_pdl(head_partial_kernel, dim3(s->head_chunks, 1), dim3(256), 0, st, (const float *)s->mtp_logits,
                       c.vocab_size, (const Staging *)s->d_mtp, s->hp, s->head_chunks));
     FC_TRY(launch_pdl(mtp_pick_kernel, dim3(1), dim3(32), 0, st, s->hp, s->head_chunks, s->d_res, s->d_mtp, i));
@@ -1021,6 +1076,7 @@ int run_pass(FcSession *s, const int *ids, int rows, int k, const FcAcceptConfig
         st->ids[i] = ids[i];
         st->rowpos[i] = s->position + i;
         st->rowseq[i] = 0;
+        if (!s->tok_hist.empty()) s->tok_hist[s->position + i] = ids[i];
     }
     st->group_rows = rows;
     st->groups = 1;
@@ -1034,6 +1090,7 @@ int run_pass(FcSession *s, const int *ids, int rows, int k, const FcAcceptConfig
 // (rows, drafts), or an eager profiled pass.
 int exec_pass(FcSession *s, int rows, int drafts, char *err, size_t n) {
     cudaSetDevice(s->m->device);
+    s->route_trace_rows = 0;
     cudaError_t e;
     if (s->profiling) {
         // eager pass with an event after every kernel (MOONLIGHT_PROFILE-style
@@ -1290,14 +1347,16 @@ cudaError_t record_prefill(FcSession *s, int T) {
                           (const int *)s->pf_route_ids, (const float *)s->pf_route_w, (const int *)s->pf_slot_of, K, D));
         mark(s, "pf_moe_combine");
     }
+    if (s->hist) {
+        FC_TRY(launch_pdl(hist_store_rows_kernel, dim3((D + 255) / 256, T), dim3(256), 0, st,
+                          (const float *)s->pf_resid, (const int *)s->pf_ids, T, s->hist, D));
+        mark(s, "hist_store");
+    }
     // final norm + lm-head of the last row (a one-row GEMV)
     const int kpD = kpad(D);
     FC_TRY(launch_pdl(rmsnorm_kernel, dim3(1), dim3(norm_threads(D)), 0, st, (const float *)(s->pf_resid + (size_t)(T - 1) * D),
                       D, (const float *)m->final_norm.p, D, c.rms_norm_epsilon, s->xq_norm, kpD, (float *)nullptr, 0));
-    GemvSeg g = seg_of(m->lm_head, s->xq_norm, EPI_STORE);
-    g.y = s->logits;
-    g.ldy = c.vocab_size;
-    FC_TRY(gemv1(c.dense_format, g, 1, 0.0f, s->d_err, m->sms, st));
+    FC_TRY(head_gemv(m, s->xq_norm, 1, s->logits, s->d_err, st));
     mark(s, "pf_lm_head");
     return cudaGetLastError();
 }
@@ -1307,6 +1366,7 @@ int run_prefill_chunk(FcSession *s, const int *ids, int T, char *err, size_t n) 
     cudaSetDevice(s->m->device);
     s->pf_h_ids[0] = s->position;
     memcpy(s->pf_h_ids + 1, ids, (size_t)T * sizeof(int));
+    if (!s->tok_hist.empty()) memcpy(&s->tok_hist[s->position], ids, (size_t)T * sizeof(int));
     cudaError_t e = cudaMemcpyAsync(s->pf_ids, s->pf_h_ids, (size_t)(T + 1) * sizeof(int), cudaMemcpyHostToDevice,
                                     s->stream);
     if (e == cudaSuccess) e = cudaMemsetAsync(s->d_err, 0, sizeof(int), s->stream);
@@ -1647,6 +1707,164 @@ int fc_model_set_tensor_rowscale(FcModel *m, const char *name, const void *value
                                error_size);
 }
 
+// floyd's Moonlight model directory (moonlight_model.c:41-110): config.json
+// and *.safetensors shards written by tools/convert_moonlight.py.
+int fc_model_open(FcModel **out, const char *path, int device, char *error, size_t error_size) {
+    using namespace fc_container;
+    if (!out) return set_error(error, error_size, "model output is required");
+    *out = nullptr;
+    if (!path || !path[0]) return set_error(error, error_size, "model path is required");
+    const std::string dir(path);
+    std::string text, err;
+    if (!read_file(dir + "/config.json", text))
+        return set_error(error, error_size, "cannot open %s/config.json", path);
+    Json cfg;
+    JsonParser jp(text.data(), text.data() + text.size());
+    if (!jp.parse(cfg) || cfg.kind != Json::Obj)
+        return set_error(error, error_size, "invalid JSON in %s/config.json", path);
+    auto num = [&](const char *k, double fallback) {
+        const Json *v = cfg.get(k);
+        return v && v->kind == Json::Num ? v->num : fallback;
+    };
+    auto flag = [&](const char *k, int fallback) {
+        const Json *v = cfg.get(k);
+        return v && v->kind == Json::Bool ? (int)v->b : fallback;
+    };
+    Index idx;
+    if (!idx.open_dir(dir, err)) return set_error(error, error_size, "%s", err.c_str());
+    if (idx.tensors.empty()) return set_error(error, error_size, "no safetensors found in %s", path);
+
+    FcModelConfig c{};
+    c.hidden_size = (int)num("hidden_size", 0);
+    c.layer_count = (int)num("num_hidden_layers", 0);
+    c.vocab_size = (int)num("vocab_size", 0);
+    c.head_count = (int)num("num_attention_heads", 0);
+    c.q_lora_rank = (int)num("q_lora_rank", 0);  // null (Moonlight) reads as 0
+    c.kv_lora_rank = (int)num("kv_lora_rank", 0);
+    c.qk_nope_dim = (int)num("qk_nope_head_dim", 0);
+    c.qk_rope_dim = (int)num("qk_rope_head_dim", 0);
+    c.value_dim = (int)num("v_head_dim", 0);
+    c.expert_count = (int)num("n_routed_experts", 0);
+    c.experts_per_token = (int)num("num_experts_per_tok", 0);
+    c.moe_intermediate_size = (int)num("moe_intermediate_size", 0);
+    c.shared_expert_count = (int)num("n_shared_experts", 0);
+    c.first_dense_layer_count = (int)num("first_k_dense_replace", 0);
+    c.dense_intermediate_size = (int)num("intermediate_size", 0);
+    c.normalize_topk = flag("norm_topk_prob", 1);
+    c.routed_scale = (float)num("routed_scaling_factor", 1.0);
+    c.rms_norm_epsilon = (float)num("rms_norm_eps", 1e-5);
+    c.rope_theta = (float)num("rope_theta", 10000.0);
+    if (c.rope_theta == 10000.0f) {
+        const Json *rp = cfg.get("rope_parameters");
+        const Json *t = rp ? rp->get("rope_theta") : nullptr;
+        if (t && t->kind == Json::Num) c.rope_theta = (float)t->num;
+    }
+    // Moonlight routes with sigmoid scores and a selection bias (noaux_tc);
+    // the Metal runtime has only that router (moonlight_kernels.metal:469-512)
+    c.score_fn = FC_SCORE_SIGMOID;
+    if (const Json *sf = cfg.get("scoring_func"))
+        if (sf->kind == Json::Str) {
+            if (sf->str == "softmax") c.score_fn = FC_SCORE_SOFTMAX;
+            else if (sf->str == "sqrtsoftplus") c.score_fn = FC_SCORE_SQRT_SOFTPLUS;
+            else if (sf->str != "sigmoid")
+                return set_error(error, error_size, "unsupported scoring_func %s", sf->str.c_str());
+        }
+    c.swiglu_limit = (float)num("swiglu_limit", 0.0);
+    c.mtp_layers = 0;
+    if (c.hidden_size <= 0 || c.layer_count <= 0 || c.head_count <= 0 || c.vocab_size <= 0 ||
+        c.kv_lora_rank <= 0 || c.qk_rope_dim <= 0 ||
+        (c.first_dense_layer_count < c.layer_count && (c.expert_count <= 0 || c.experts_per_token <= 0)))
+        return set_error(error, error_size, "unsupported Moonlight config in %s/config.json", path);
+
+    // storage formats from the tensors themselves (convert_moonlight.py:56-75):
+    // U8 + ".qs" is int8 when it has O*I bytes, int4 when O*ceil(I/2)
+    auto row_format = [&](const std::string &name, int I, int *fmt) {
+        const Tensor *t = idx.find(name), *qs = idx.find(name + ".qs");
+        if (!t || !qs || t->dtype != DT_U8 || qs->dtype != DT_F32 || qs->numel() <= 0) return false;
+        const uint64_t O = (uint64_t)qs->numel();
+        if (t->bytes == O * (uint64_t)I) *fmt = FC_FMT_Q8;
+        else if (t->bytes == O * (uint64_t)((I + 1) / 2)) *fmt = FC_FMT_Q4;
+        else return false;
+        return true;
+    };
+    if (!row_format("model.layers.0.self_attn.kv_a_proj_with_mqa.weight", c.hidden_size, &c.dense_format))
+        return set_error(error, error_size, "layer 0 kv_a_proj_with_mqa is not an int8 / int4 container matrix");
+    c.expert_format = c.dense_format;
+    if (c.first_dense_layer_count < c.layer_count) {
+        const std::string e0 = "model.layers." + std::to_string(c.first_dense_layer_count) +
+                               ".mlp.experts.0.gate_proj.weight";
+        if (!row_format(e0, c.hidden_size, &c.expert_format))
+            return set_error(error, error_size, "%s is not an int8 / int4 container matrix", e0.c_str());
+        c.has_selection_bias = idx.find("model.layers." + std::to_string(c.first_dense_layer_count) +
+                                        ".mlp.gate.e_score_correction_bias") != nullptr;
+    }
+    const Tensor *emb = idx.find("model.embed_tokens.weight");
+    if (!emb) return set_error(error, error_size, "model.embed_tokens.weight is missing");
+    if (emb->dtype == DT_F32 || emb->dtype == DT_BF16 || emb->dtype == DT_F16) {
+        c.embed_f32 = 1;
+    } else {
+        int f = 0;
+        if (!row_format("model.embed_tokens.weight", c.hidden_size, &f) || f != c.dense_format)
+            return set_error(error, error_size, "the embedding must be F32 or in the attention format");
+    }
+
+    FcModel *m = nullptr;
+    if (!fc_model_create(&m, &c, device, error, error_size)) return 0;
+    std::map<std::string, bool> pending;
+    for (auto &kv : m->names) pending[kv.first] = true;
+    std::vector<uint8_t> raw;
+    std::vector<float> f32;
+    for (auto &kv : idx.tensors) {
+        const std::string &name = kv.first;
+        const Tensor &t = kv.second;
+        if (name.size() > 3 && name.compare(name.size() - 3, 3, ".qs") == 0) continue;
+        auto it = m->names.find(name);
+        if (it == m->names.end()) continue;  // e.g. rotary_emb.inv_freq: not used
+        const Tensor *qs = idx.find(name + ".qs");
+        int ok = 1;
+        if (qs) {
+            if (t.dtype != DT_U8 || !idx.read_f32(*qs, f32)) {
+                ok = set_error(error, error_size, "cannot read %s / %s.qs", name.c_str(), name.c_str());
+            } else {
+                raw.resize(t.bytes);
+                const int rows = (int)f32.size();
+                const TensorRef &r = it->second;
+                if (!r.mat) {
+                    ok = set_error(error, error_size, "%s is a vector in this model", name.c_str());
+                } else if (!idx.read(t, raw.data())) {
+                    ok = set_error(error, error_size, "cannot read %s", name.c_str());
+                } else {
+                    // int4 rows of an odd width are padded to a whole byte on
+                    // disk; the widths here are multiples of 32, so the packed
+                    // rows are contiguous
+                    ok = fc_model_set_tensor_rowscale(m, name.c_str(), raw.data(), raw.size(), f32.data(), rows,
+                                                      error, error_size);
+                }
+            }
+        } else {
+            if (!idx.read_f32(t, f32))
+                ok = set_error(error, error_size, "%s: unsupported dtype for an unquantized tensor", name.c_str());
+            else
+                ok = fc_model_set_tensor(m, name.c_str(), f32.data(), f32.size() * 4, error, error_size);
+        }
+        if (!ok) {
+            fc_model_close(m);
+            return 0;
+        }
+        pending.erase(name);
+    }
+    for (auto &kv : pending) {
+        const TensorRef &r = m->names[kv.first];
+        if (r.ints) continue;  // hash-routing tables (not in Moonlight)
+        std::string missing = kv.first;
+        fc_model_close(m);
+        return set_error(error, error_size, "tensor %s is missing from %s", missing.c_str(), path);
+    }
+    cudaDeviceSynchronize();
+    *out = m;
+    return 1;
+}
+
 int fc_model_get_tensor(const FcModel *m, const char *name, void *data, size_t bytes, char *error,
                         size_t error_size) {
     return tensor_io(m, name, data, bytes, false, error, error_size);
@@ -1788,7 +2006,11 @@ int create_session(FcSession **out, FcModel *m, const FcOptions *options, const 
     if (c.mtp_layers) {
         ok = ok && salloc(s, s->d_mtp, 1) && salloc(s, s->mtp_h, (size_t)D);
         ok = ok && salloc(s, s->mtp_logits, (size_t)V);
-        ok = ok && salloc(s, s->mtp_xq, (size_t)kpad(2 * D) * 2);
+        ok = ok && salloc(s, s->mtp_xq, (size_t)mb * kpad(2 * D) * 2);
+        if (!batch) {
+            ok = ok && salloc(s, s->hist, (size_t)s->opt.context_size * D);
+            s->tok_hist.assign((size_t)s->opt.context_size, 0);
+        }
     }
     ok = ok && salloc(s, s->n_active, 1) && salloc(s, s->active, (size_t)s->max_slots + 1);
     s->g_slots = std::min(E, mb * K);
@@ -2242,10 +2464,17 @@ int fc_test_copy_kv(const FcSession *s, int layer, float *latent, float *rope, i
 }
 
 int fc_test_copy_routes(const FcSession *s, int layer, int *route_ids, int capacity) {
-    if (!s || !route_ids || capacity < s->last_rows) return 0;
+    if (!s || !route_ids) return 0;
     const FcModelConfig &c = s->m->c;
     if (layer < c.first_dense_layer_count || layer >= c.layer_count) return 0;
     int K = c.experts_per_token;
+    if (s->route_trace_rows) {  // all rows of the last fc_test_prefill_layers
+        if (capacity < s->route_trace_rows) return 0;
+        memcpy(route_ids, s->route_trace.data() + (size_t)layer * s->route_trace_rows * K,
+               (size_t)s->route_trace_rows * K * 4);
+        return 1;
+    }
+    if (capacity < s->last_rows) return 0;
     return cudaMemcpy(route_ids, s->route_ids + (size_t)layer * s->rows_max * K,
                       (size_t)s->last_rows * K * 4, cudaMemcpyDeviceToHost) == cudaSuccess;
 }
@@ -2263,6 +2492,13 @@ int fc_test_copy_layer_outputs(const FcSession *s, float *outputs, int capacity_
 }
 
 // ---- spec-runtime shim (deepseek_v4_runtime.h:72-256) ----
+}  // extern "C"
+namespace {
+cudaError_t mtp_history_rows(FcSession *s, int p0, int r);
+int mtp_finish(FcSession *s);
+}  // namespace
+extern "C" {
+
 int fc_runtime_init(FcRuntime *rt, FcModel *m, int max_context, int max_batch) {
     if (!rt || !m || max_context <= 0) return 0;
     memset(rt, 0, sizeof(*rt));
@@ -2297,6 +2533,16 @@ int fc_runtime_forward(FcRuntime *rt, const int *ids, int n, const float **logit
     }
     rt->last_start_position = start;
     rt->last_count = n;
+    // a prefilled drafter follows the target: its cache gains the pairs
+    // (hidden row q - 1, token q) of the new positions (the reference
+    // appends its DSpark main KV the same way, deepseek_v4_runtime.h:171-176)
+    if (rt->dspark_ready && start > 0) {
+        FcSession *s = rt->session;
+        for (int q0 = start; q0 < start + n; q0 += s->rows_max) {
+            const int r = std::min(s->rows_max, start + n - q0);
+            if (mtp_history_rows(s, q0 - 1, r) != cudaSuccess || !mtp_finish(s)) return 0;
+        }
+    }
     if (logits) *logits = rt->logits;
     return 1;
 }
@@ -2320,6 +2566,7 @@ void fc_runtime_reset(FcRuntime *rt) {
     fc_session_reset(rt->session);
     rt->last_count = 0;
     rt->last_start_position = 0;
+    rt->dspark_ready = 0;
 }
 
 void fc_runtime_free(FcRuntime *rt) {
@@ -2327,6 +2574,122 @@ void fc_runtime_free(FcRuntime *rt) {
     if (rt->session) fc_session_destroy(rt->session);
     free(rt->logits);
     memset(rt, 0, sizeof(*rt));
+}
+
+}  // extern "C"
+
+namespace {
+
+// The MTP drafter layer over `r` (<= rows_max) consecutive positions
+// p0 + 1 .. p0 + r of the session's own history: row i takes the final
+// hidden row of position p0 + i and the token at position p0 + 1 + i, the
+// pairing the drafter's steps use during a verify (record_mtp_step), and
+// writes the drafter's latent KV at position p0 + 1 + i.  Eager, on the
+// session stream.
+cudaError_t mtp_history_rows(FcSession *s, int p0, int r) {
+    FcModel *m = s->m;
+    const FcModelConfig &c = m->c;
+    cudaStream_t st = s->stream;
+    const int D = c.hidden_size, kp2 = kpad(2 * D), lm = c.layer_count;
+    DevLayer &y = m->layers[lm];
+    Staging *h = s->h_stage;
+    memset(h, 0, sizeof(*h));
+    h->pos = p0 + 1;
+    h->rows = r;
+    h->k = -1;
+    h->temperature = 1.0f;
+    for (int i = 0; i < r; ++i) {
+        h->ids[i] = s->tok_hist[p0 + 1 + i];
+        h->rowpos[i] = p0 + 1 + i;
+    }
+    h->group_rows = r;
+    h->groups = 1;
+    FC_TRY(cudaMemcpyAsync(s->d_mtp, h, sizeof(Staging), cudaMemcpyHostToDevice, st));
+    FC_TRY(launch_pdl(embed_kernel, dim3(r), dim3(256), 0, st, m->embed.fmt, (const uint8_t *)m->embed.w, D,
+                      m->embed.kp, (const int *)s->d_mtp->ids, s->resid));
+    FC_TRY(cudaMemsetAsync(s->mtp_xq, 0, (size_t)r * kp2 * 4, st));
+    FC_TRY(launch_pdl(rmsnorm_kernel, dim3(r), dim3(norm_threads(D)), 0, st, (const float *)s->resid, D,
+                      (const float *)y.enorm.p, D, c.rms_norm_epsilon, s->mtp_xq, kp2, (float *)nullptr, 0));
+    FC_TRY(launch_pdl(rmsnorm_kernel, dim3(r), dim3(norm_threads(D)), 0, st, (const float *)(s->hist + (size_t)p0 * D),
+                      D, (const float *)y.hnorm.p, D, c.rms_norm_epsilon, s->mtp_xq + (size_t)D * 2, kp2,
+                      (float *)nullptr, 0));
+    GemvSeg g = seg_of(y.eh_proj, s->mtp_xq, EPI_STORE);
+    g.y = s->resid;
+    g.ldy = D;
+    FC_TRY(gemv1(c.dense_format, g, r, 0.0f, s->d_err, m->sms, st));
+    return record_layer(s, r, lm, s->d_mtp);
+}
+
+int mtp_finish(FcSession *s) {
+    cudaError_t e = cudaStreamSynchronize(s->stream);
+    int flag = 0;
+    if (e == cudaSuccess) e = cudaMemcpy(&flag, s->d_err, 4, cudaMemcpyDeviceToHost);
+    if (flag) {
+        cudaMemset(s->d_err, 0, 4);
+        cudaMemset(s->route_arrivals, 0, sizeof(int));
+    }
+    return e == cudaSuccess && !flag;
+}
+
+}  // namespace
+
+extern "C" {
+
+int fc_runtime_dspark_prefill(FcRuntime *rt) {
+    if (!rt || !rt->session || rt->dspark_ready || rt->last_count <= 0 || rt->last_start_position != 0)
+        return 0;
+    FcSession *s = rt->session;
+    if (s->m->c.mtp_layers != 1 || !s->hist || s->m->world != 1) return 0;
+    cudaSetDevice(s->m->device);
+    const int pairs = rt->last_count - 1;
+    for (int p0 = 0; p0 < pairs; p0 += s->rows_max) {
+        const int r = std::min(s->rows_max, pairs - p0);
+        if (mtp_history_rows(s, p0, r) != cudaSuccess || !mtp_finish(s)) return 0;
+    }
+    s->stats.command_buffers++;
+    rt->dspark_ready = 1;
+    return 1;
+}
+
+int fc_runtime_dspark_propose(FcRuntime *rt, int input_id, int64_t output_ids[6], float confidence[5]) {
+    enum { kDraft = 5 };
+    if (!rt || !rt->session || !rt->dspark_ready || rt->last_count <= 0 || input_id < 0) return 0;
+    FcSession *s = rt->session;
+    FcModel *m = s->m;
+    if (input_id >= m->c.vocab_size) return 0;
+    const int p = rt->last_start_position + rt->last_count - 1;  // the current row
+    if (p + kDraft >= s->opt.context_size) return 0;
+    cudaSetDevice(m->device);
+    const int D = m->c.hidden_size;
+    cudaStream_t st = s->stream;
+    // the drafter's inputs as if a verify had just committed the current row:
+    // main position p with commit 1, next token input_id, hidden row p
+    Staging *h = s->h_stage;
+    memset(h, 0, sizeof(*h));
+    h->pos = p;
+    h->rows = 1;
+    h->k = -1;
+    h->group_rows = 1;
+    h->groups = 1;
+    Result *res = s->h_res;
+    memset(res, 0, sizeof(*res));
+    res->commit = 1;
+    res->next_token = input_id;
+    cudaError_t e = cudaMemcpyAsync(s->d_stage, h, sizeof(Staging), cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(s->d_res, res, sizeof(Result), cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(s->resid, s->hist + (size_t)p * D, (size_t)D * 4, cudaMemcpyDeviceToDevice, st);
+    for (int i = 0; i < kDraft && e == cudaSuccess; ++i) e = record_mtp_step(s, i);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(res, s->d_res, sizeof(Result), cudaMemcpyDeviceToHost, st);
+    if (e != cudaSuccess || !mtp_finish(s)) return 0;
+    s->stats.command_buffers++;
+    if (output_ids) {
+        output_ids[0] = input_id;
+        for (int i = 0; i < kDraft; ++i) output_ids[i + 1] = res->drafts[i];
+    }
+    if (confidence)
+        for (int i = 0; i < kDraft; ++i) confidence[i] = res->draft_conf[i];
+    return 1;
 }
 
 }  // extern "C"
@@ -2666,3 +3029,6 @@ extern "C" int fc_debug_gemv_trace(int items, unsigned long long *out, int n) {
     return cudaMemcpyFromSymbol(out, g_gemv_trace, sizeof(unsigned long long) * (n < 512 ? n : 512)) == cudaSuccess;
 }
 #endif
+
+#include "hooks.cuh"
+#include "fm.cuh"

@@ -99,6 +99,11 @@ typedef struct {
     int mtp_layers;              /* 0, or 1: a DeepSeek-V3-style MTP drafter
                                     layer (enorm / hnorm / eh_proj, one MoE
                                     layer, shared_head.norm, shared lm-head) */
+    int embed_f32;               /* 1: embedding and lm-head stored as fp32
+                                    [vocab][hidden] (floyd's Moonlight
+                                    container keeps them unquantized,
+                                    tools/convert_moonlight.py:12-17); 0: in
+                                    dense_format                         */
     uint64_t resident_bytes;     /* filled by fc_model_info              */
 } FcModelConfig;
 
@@ -155,6 +160,21 @@ int fc_model_create(FcModel **out, const FcModelConfig *config, int device,
  * router and lm-head weights are replicated.  E must divide by world. */
 int fc_model_create_ep(FcModel **out, const FcModelConfig *config, int device,
                        int rank, int world, char *error, size_t error_size);
+
+/* Opens floyd's Moonlight model directory, the counterpart of
+ * moonlight_model_open (moonlight_metal.h:46-47, moonlight_model.c:41-110):
+ * config.json (hidden_size, num_hidden_layers, ..., rope_theta or
+ * rope_parameters.rope_theta, scoring_func with sigmoid as the default) and
+ * every *.safetensors shard written by tools/convert_moonlight.py.  Int8 /
+ * int4 matrices come as U8 values plus `name`.qs fp32 row scales (each row's
+ * scale is rounded to fp16 for its group scales, as in
+ * fc_model_set_tensor_rowscale); the embedding and lm-head stay fp32
+ * (embed_f32 = 1); router weights, norms and selection biases are fp32.
+ * Fails, naming the tensor, when one the model needs is missing; tensors the
+ * model does not use (rotary_emb.inv_freq) are ignored.  Weights are
+ * uploaded once and stay resident on CUDA device `device`. */
+int fc_model_open(FcModel **out, const char *path, int device, char *error,
+                  size_t error_size);
 
 /* Fills every weight with the seeded synthetic generator of floyd_synth.h
  * (integer-only Philox mapping, identical to the CPU oracle's). */
@@ -366,6 +386,45 @@ void fc_session_profile_reset(FcSession *session);
 
 /* ---- test hooks (moonlight_metal.h:69-96) -------------------------------- */
 
+/* Single-primitive hooks, each the counterpart of the moonlight_test_* call
+ * named beside it and returning 1 on success, 0 on failure.  Each runs the
+ * same device code the forward runs, on up to options.max_batch rows, and
+ * counts one submission in FcStats.command_buffers (one per hook call, the
+ * MoE hook included: routing and experts run without a host round trip).
+ *   embed:      output[count][hidden] = embedding rows of ids       (:73-74)
+ *   rmsnorm:    output = RMSNorm(input) with the named norm vector  (:75-77)
+ *   matmul:     output[rows][output_width] = input . W^T of the named
+ *               matrix (quantized or fp32)                          (:78-80)
+ *   attention:  the attention block of `layer` (q / kv_a, KV append, MLA,
+ *               o_proj) on normalized input rows at positions position ..
+ *               position + rows - 1; position must equal the session's
+ *               position (the layer's KV length), which then advances
+ *               by rows                                             (:81-83)
+ *   moe:        the MoE block of `layer` on normalized rows: route ids and
+ *               weights [rows][top-k] in selection order, the raw router
+ *               logits [rows][experts], routed sum, shared experts' output
+ *               and their sum [rows][hidden] (any output may be NULL
+ *               except `output`)                                    (:88-92)
+ *   dense_mlp:  the dense MLP of a first-k-dense layer              (:93-94)
+ *   prefill_layers: prefill of `count` tokens into an empty session with
+ *               the hidden state after every layer [layers][count][hidden]
+ *               and the last row's logits                           (:67-70) */
+int fc_test_embed(FcSession *session, const int *ids, int count, float *output);
+int fc_test_rmsnorm(FcSession *session, const float *input, const char *weight_name,
+                    int rows, int width, float *output);
+int fc_test_matmul(FcSession *session, const char *weight_name, const float *input,
+                   int rows, int input_width, int output_width, float *output);
+int fc_test_attention(FcSession *session, int layer, const float *input, int rows,
+                      int position, float *output);
+int fc_test_moe(FcSession *session, int layer, const float *input, int rows,
+                int *route_ids, float *route_weights, float *router_scores,
+                float *routed_output, float *shared_output, float *output);
+int fc_test_dense_mlp(FcSession *session, int layer, const float *input, int rows,
+                      float *output);
+int fc_test_prefill_layers(FcSession *session, const int *ids, int count,
+                           float *layer_outputs, float *last_logits,
+                           char *error, size_t error_size);
+
 int fc_test_kv_length(const FcSession *session, int layer);      /* :85 */
 /* The acceptance kernels of the verify graph (row argmax, softmax
  * partials, Gumbel picks, the acceptance rule of fc_session_verify) run on
@@ -406,6 +465,7 @@ typedef struct {
     int max_context;
     int last_count;
     int last_start_position;
+    int dspark_ready;    /* fc_runtime_dspark_prefill has run          */
 } FcRuntime;
 
 int fc_runtime_init(FcRuntime *runtime, FcModel *model, int max_context,
@@ -416,6 +476,20 @@ int fc_runtime_argmax(const float *logits, int vocab_size);        /* :231-237 *
 int fc_runtime_verify_token(const float *logits, int vocab_size,
                             int64_t proposal, int *accepted);      /* :239-244 */
 void fc_runtime_reset(FcRuntime *runtime);                         /* :99-128  */
+/* The drafter of a model with an MTP layer (mtp_layers = 1), the stand-in
+ * for ds4's DSpark block (deepseek_v4_runtime.h:180-223).
+ * dspark_prefill: after a forward that started at position 0, runs the
+ * drafter layer over the prompt (hidden row of position p with the token at
+ * p + 1, for every p) so that its latent cache covers the prompt; once per
+ * runtime until fc_runtime_reset.
+ * dspark_propose: from the last forward's last row and the next token
+ * `input_id`, five greedy drafter steps; output_ids[0] = input_id,
+ * output_ids[1..5] = the proposals, confidence[i] = the drafter's top-1
+ * logit of proposal i (the stand-in drafter has no learned confidence head,
+ * deepseek_v4_forward.h:1935-1944).  Both return 1 on success. */
+int fc_runtime_dspark_prefill(FcRuntime *runtime);
+int fc_runtime_dspark_propose(FcRuntime *runtime, int input_id, int64_t output_ids[6],
+                              float confidence[5]);
 void fc_runtime_free(FcRuntime *runtime);                          /* :246-256 */
 
 #ifdef __cplusplus

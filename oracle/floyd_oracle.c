@@ -320,6 +320,8 @@ struct OrcSession {
     float *latent; /* [layers (+ MTP)][ctx][L] */
     float *rope;   /* [layers (+ MTP)][ctx][R] */
     float *last_x; /* final pre-norm hidden rows of the last forward */
+    float *hist;   /* final pre-norm hidden row of every position [ctx][D] */
+    int *tok;      /* token id of every position [ctx]                      */
     int last_rows;
     int drafts[64], n_drafts;  /* MTP proposals of the last verify */
 };
@@ -416,8 +418,9 @@ OrcModel *orc_model_create(const FcModelConfig *config, uint64_t seed) {
     int D = c->hidden_size, H = c->head_count, L = c->kv_lora_rank, R = c->qk_rope_dim;
     int qw = H * (c->qk_nope_dim + R);
     int df = c->dense_format, ef = c->expert_format;
-    mat_gen(&m->embed, df, c->vocab_size, D, seed, fc_tensor_id(-1, FC_T_EMBED, 0));
-    mat_gen(&m->lm_head, df, c->vocab_size, D, seed, fc_tensor_id(-1, FC_T_LM_HEAD, 0));
+    int hf = c->embed_f32 ? FC_FMT_F32 : df;  /* fp32 embedding / lm-head */
+    mat_gen(&m->embed, hf, c->vocab_size, D, seed, fc_tensor_id(-1, FC_T_EMBED, 0));
+    mat_gen(&m->lm_head, hf, c->vocab_size, D, seed, fc_tensor_id(-1, FC_T_LM_HEAD, 0));
     m->final_norm = norm_gen(D, seed, fc_tensor_id(-1, FC_T_FINAL_NORM, 0));
     m->layers = (Layer *)calloc((size_t)(c->layer_count + c->mtp_layers), sizeof(Layer));
     for (int l = 0; l < c->layer_count + c->mtp_layers; ++l) {
@@ -614,13 +617,15 @@ OrcSession *orc_session_create(OrcModel *m, int context_size, int kv_fp16) {
     size_t rows = (size_t)(m->c.layer_count + m->c.mtp_layers) * context_size;
     s->latent = alloc_f(rows * m->c.kv_lora_rank);
     s->rope = alloc_f(rows * m->c.qk_rope_dim);
+    s->hist = alloc_f((size_t)context_size * m->c.hidden_size);
+    s->tok = (int *)calloc((size_t)context_size, sizeof(int));
     if (!s->latent || !s->rope) { orc_session_free(s); return NULL; }
     return s;
 }
 
 void orc_session_free(OrcSession *s) {
     if (!s) return;
-    free(s->latent); free(s->rope); free(s->last_x); free(s);
+    free(s->latent); free(s->rope); free(s->last_x); free(s->hist); free(s->tok); free(s);
 }
 
 int orc_session_position(const OrcSession *s) { return s ? s->position : 0; }
@@ -953,6 +958,8 @@ int orc_session_forward(OrcSession *s, const int *ids, int rows, float *logits,
     s->last_x = alloc_f((size_t)rows * D);
     memcpy(s->last_x, x, (size_t)rows * D * sizeof(float));
     s->last_rows = rows;
+    memcpy(s->hist + (size_t)pos * D, x, (size_t)rows * D * sizeof(float));
+    memcpy(s->tok + pos, ids, (size_t)rows * sizeof(int));
     if (logits) {
         orc_rmsnorm(x, m->final_norm, rows, D, c->rms_norm_epsilon, xn);
         mat_apply(&m->lm_head, xn, rows, logits);
@@ -968,7 +975,8 @@ int orc_session_forward(OrcSession *s, const int *ids, int rows, float *logits,
  * token, then the previous proposal) and hidden h (h_0 = the target's last
  * committed row): x = eh_proj([enorm(embed(t_i)) | hnorm(h)]), the MTP
  * layer, h = x, proposal = argmax(lm_head(shared_head.norm(x))). */
-static int mtp_drafts(OrcSession *s, const float *h0, int start, int first_token, int k, int *out) {
+static int mtp_drafts(OrcSession *s, const float *h0, int start, int first_token, int k, int *out,
+                      float *conf) {
     OrcModel *m = s->m;
     const FcModelConfig *c = &m->c;
     int D = c->hidden_size, V = c->vocab_size, lm = c->layer_count;
@@ -989,6 +997,7 @@ static int mtp_drafts(OrcSession *s, const float *h0, int start, int first_token
         mat_apply(&m->lm_head, xn, 1, lg);
         token = orc_argmax(lg, V);
         out[i] = token;
+        if (conf) conf[i] = lg[token];
     }
     free(h); free(e); free(cat); free(x); free(xn); free(lg);
     return ok;
@@ -1040,9 +1049,43 @@ int orc_session_verify(OrcSession *s, const int *ids, int k, const FcAcceptConfi
     if (s->m->c.mtp_layers > 0 && k > 0) {
         int D = s->m->c.hidden_size;
         if (mtp_drafts(s, s->last_x + (size_t)(commit - 1) * D, start + commit, next < 0 ? 0 : next, k,
-                       s->drafts))
+                       s->drafts, NULL))
             s->n_drafts = k;
     }
     if (!row_logits) free(logits);
     return 1;
 }
+
+/* The drafter layer over positions p0 + 1 .. p0 + r of the session's own
+ * history: row i takes the final hidden row of position p0 + i and the
+ * token at p0 + 1 + i (the pairing of mtp_drafts) and writes the drafter's
+ * latent KV at p0 + 1 + i.  The counterpart of the reference runtime's
+ * DSpark prefill / append (deepseek_v4_runtime.h:130-198) for the MTP
+ * stand-in. */
+int orc_dspark_rows(OrcSession *s, int p0, int r) {
+    OrcModel *m = s->m;
+    const FcModelConfig *c = &m->c;
+    int D = c->hidden_size, lm = c->layer_count;
+    if (c->mtp_layers != 1 || p0 < 0 || p0 + r >= s->ctx) return 0;
+    const Layer *y = &m->layers[lm];
+    float *e = alloc_f((size_t)D), *cat = alloc_f((size_t)2 * D), *x = alloc_f((size_t)D);
+    int ok = 1;
+    for (int i = 0; i < r && ok; ++i) {
+        int q = p0 + 1 + i, token = s->tok[q];
+        embed_rows(m, &token, 1, e);
+        orc_rmsnorm(e, y->enorm, 1, D, c->rms_norm_epsilon, cat);
+        orc_rmsnorm(s->hist + (size_t)(q - 1) * D, y->hnorm, 1, D, c->rms_norm_epsilon, cat + D);
+        mat_apply(&y->eh_proj, cat, 1, x);
+        ok = run_layers(s, x, 1, q, &token, lm, lm + 1, NULL, NULL);
+    }
+    free(e); free(cat); free(x);
+    return ok;
+}
+
+/* Five greedy drafter steps from the hidden row of position p and the next
+ * token: out[0..4] proposals, conf[0..4] their top-1 logits. */
+int orc_dspark_propose(OrcSession *s, int p, int input_id, int *out, float *conf) {
+    if (p < 0 || p + 5 >= s->ctx) return 0;
+    return mtp_drafts(s, s->hist + (size_t)p * s->m->c.hidden_size, p + 1, input_id, 5, out, conf);
+}
+

@@ -136,6 +136,13 @@ int orc_session_verify(OrcSession *session, const int *ids, int k,
                        int *n_emitted, int *next_token, float *row_logits,
                        int *row_tops);
 
+/* The MTP drafter over the session's history: orc_dspark_rows writes the
+ * drafter's latent KV at positions p0 + 1 .. p0 + r from (hidden row q - 1,
+ * token q); orc_dspark_propose makes five greedy proposals from the hidden
+ * row of position p and the next token. */
+int orc_dspark_rows(OrcSession *s, int p0, int r);
+int orc_dspark_propose(OrcSession *s, int p, int input_id, int *out, float *conf);
+
 /* Wall seconds spent in the attention and in the FFN / MoE blocks of the
  * forwards since the previous call; resets both. */
 void orc_part_times(double *attn_s, double *ffn_s);

@@ -61,6 +61,8 @@ def lib():
             "orc_session_copy_kv": (I, [P, I, FP, FP, I]),
             "orc_session_verify": (I, [P, IP, I, ctypes.POINTER(FcAcceptConfig), IP, IP, IP, FP, IP]),
             "orc_session_drafts": (I, [P, IP, I]),
+            "orc_dspark_rows": (I, [P, I, I]),
+            "orc_dspark_propose": (I, [P, I, I, IP, FP]),
             "orc_part_times": (None, [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double)]),
         }
         for name, (res, args) in sig.items():
@@ -220,6 +222,17 @@ class OracleSession:
         rope = np.zeros((max(P, 1), c["qk_rope_dim"]), dtype=np.float32)
         lib().orc_session_copy_kv(self.handle, layer, _fp(lat), _fp(rope), max(P, 1))
         return lat[:P], rope[:P]
+
+    def dspark_rows(self, p0, r):
+        if not lib().orc_dspark_rows(self.handle, p0, r):
+            raise RuntimeError("oracle dspark rows failed")
+
+    def dspark_propose(self, p, input_id):
+        out = np.zeros(5, dtype=np.int32)
+        conf = np.zeros(5, dtype=np.float32)
+        if not lib().orc_dspark_propose(self.handle, p, input_id, _ip(out), _fp(conf)):
+            raise RuntimeError("oracle dspark propose failed")
+        return out.tolist(), conf
 
     def position(self):
         return lib().orc_session_position(self.handle)

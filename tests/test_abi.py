@@ -18,7 +18,7 @@ def declared_functions():
         text = open(os.path.join(ROOT, "include", h)).read()
         text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
         text = re.sub(r"//[^\n]*", "", text)
-        for m in re.finditer(r"\b(fc_[a-z0-9_]+)\s*\(", text):
+        for m in re.finditer(r"\b((?:fc|fm)_[a-z0-9_]+)\s*\(", text):
             names.add(m.group(1))
     # static inline helpers of floyd_synth.h are not exported
     return {n for n in names if not n.startswith("fc_synth") and n not in
