@@ -234,6 +234,54 @@ __device__ __forceinline__ void gemv_chunk(const uint8_t *blk0, const uint8_t *b
     const int lane = threadIdx.x & 31;
     const int g = lane >> 2, j = lane & 3;
     const uint8_t *blks[2] = {blk0, blk1};
+    if constexpr (FMT == FC_FMT_MXFP4) {
+        // group by group: each group's 8 codes per row are decoded right
+        // before its two MMAs, so few registers are live at a time (the
+        // same arithmetic, in the same order, as the general path below)
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+            const uint8_t *blk = blks[t];
+            if (!blk) continue;
+            uint4 a_raw[2];
+            uint32_t s4[2];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int r = g + 8 * h;
+                a_raw[h] = *reinterpret_cast<const uint4 *>(blk + r * 64 + 16 * j);
+                s4[h] = *reinterpret_cast<const uint32_t *>(blk + kBlockValueBytes + r * scale_row_bytes(FMT));
+            }
+#pragma unroll
+            for (int q = 0; q < kGroups; ++q) {
+                const uint32_t w0 = q == 0 ? a_raw[0].x : q == 1 ? a_raw[0].y : q == 2 ? a_raw[0].z : a_raw[0].w;
+                const uint32_t w1 = q == 0 ? a_raw[1].x : q == 1 ? a_raw[1].y : q == 2 ? a_raw[1].z : a_raw[1].w;
+                uint32_t r0[4], r1[4];
+                dequant_e2m1_word(w0, r0);
+                dequant_e2m1_word(w1, r1);
+                float sc0[4], sc1[4];
+                e8m0x4_to_float(s4[0], sc0);
+                e8m0x4_to_float(s4[1], sc1);
+                float tmp[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                float tml[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+                for (int ii = 0; ii < 2; ++ii) {
+                    const int i = 2 * q + ii;
+                    uint32_t a[4] = {r0[2 * ii], r1[2 * ii], r0[2 * ii + 1], r1[2 * ii + 1]};
+                    mma_f16(tmp, a, b_raw[i].x, b_raw[i].y, tmp);
+                    if (!PACK) mma_f16(tml, a, b_raw[i].z, b_raw[i].w, tml);
+                }
+                acc[t][0] = fmaf(sc0[q], tmp[0], acc[t][0]);
+                acc[t][1] = fmaf(sc0[q], tmp[1], acc[t][1]);
+                acc[t][2] = fmaf(sc1[q], tmp[2], acc[t][2]);
+                acc[t][3] = fmaf(sc1[q], tmp[3], acc[t][3]);
+                if (!PACK) {
+                    accl[t][0] = fmaf(sc0[q], tml[0], accl[t][0]);
+                    accl[t][1] = fmaf(sc0[q], tml[1], accl[t][1]);
+                    accl[t][2] = fmaf(sc1[q], tml[2], accl[t][2]);
+                    accl[t][3] = fmaf(sc1[q], tml[3], accl[t][3]);
+                }
+            }
+        }
+    } else {
 #pragma unroll
     for (int t = 0; t < 2; ++t) {
         const uint8_t *blk = blks[t];
@@ -310,6 +358,7 @@ __device__ __forceinline__ void gemv_chunk(const uint8_t *blk0, const uint8_t *b
                 accl[t][3] = fmaf(scale[1][q], tml[3], accl[t][3]);
             }
         }
+    }
     }
 }
 
