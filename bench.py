@@ -634,6 +634,7 @@ def batch_leg(args, d, model, cfg):
             if r == args.batch_warmup:
                 d.barrier()
                 g0 = bs.stats()["gpu_ms"]
+                bs.exchange_wait_ms()  # resets the exchange-wait timer
             ids = [make_ids(streams[q], offs[q], plans[q][r], V) for q in range(nseq)]
             t0 = time.perf_counter()
             n, nxt = bs.verify_batch(ids)
@@ -652,8 +653,10 @@ def batch_leg(args, d, model, cfg):
             if r >= args.batch_warmup:
                 wall += dt
         g = d.max(bs.stats()["gpu_ms"] - g0)
+        xw = d.max(bs.exchange_wait_ms()) / args.batch_steps if d.world > 1 else 0.0
         results.append({"accept_p": p, "value": emitted / (g / 1e3), "unit": "accepted tok/s (all sequences)",
                         "e2e": emitted / d.max(wall), "ms_per_step": g / args.batch_steps,
+                        "exchange_exposed_ms_per_step": xw,
                         "mean_commit_per_sequence": emitted / (args.batch_steps * nseq),
                         "acceptance_mismatches": int(d.sum(mismatches))})
     bs.close()
@@ -661,10 +664,13 @@ def batch_leg(args, d, model, cfg):
             "sequences_per_pass": 8 // rows, "shared_prefix": prefix, "contexts": ctxs,
             "steps": args.batch_steps, "warmup": args.batch_warmup, "n_gpus": d.world,
             "results": results,
-            "exchange_exposed_ms": None,
+            "exchange_exposed_ms": (float(np.mean([r["exchange_exposed_ms_per_step"] for r in results]))
+                                    if d.world > 1 else None),
             "note": ("one batch step = one verify of every sequence; device time of the graph replays "
                      "(max over ranks); the expert exchange (N > 1) is fused into the down-projection "
-                     "epilogue and the combine's wait, so it has no separate exposed time")}
+                     "epilogue (NVLink stores) and the combine's flag wait; exchange_exposed_ms is the "
+                     "device time the combines spent waiting for peers per batch step (globaltimer, "
+                     "max over ranks)")}
 
 
 def run_ours(args, d):
@@ -724,6 +730,7 @@ def run_ours(args, d):
         if r == args.warmup:
             d.barrier()
             st0 = sess.stats()
+            sess.exchange_wait_ms()  # resets the exchange-wait timer
             clocks.start()
         ids = make_ids(stream, o, plans[r], V)
         t0 = time.perf_counter()
@@ -746,6 +753,7 @@ def run_ours(args, d):
             wall_timed += dt
     clk = clocks.stop()
     st1 = sess.stats()
+    xwait = d.max(sess.exchange_wait_ms()) / args.steps if ep else None
     gpu_ms = st1["gpu_ms"] - st0["gpu_ms"]
     d.barrier()
     gpu_ms_max = d.max(gpu_ms)
@@ -830,6 +838,7 @@ def run_ours(args, d):
         "step_hbm": {"algorithmic_bytes": step_bytes, "achieved_gbs": step_bytes / (step_ms / 1e3) / 1e9,
                      "frac": step_bytes / (step_ms / 1e3) / 1e9 / peak, "peak": peak},
         "mean_commit": total_emitted / args.steps,
+        "exchange_exposed_ms_per_step": xwait,
         "acceptance_mismatches": int(d.sum(mismatches)),
         "sampling": samp,
         "roofline": roof,

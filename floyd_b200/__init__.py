@@ -230,6 +230,11 @@ class Session:
         err = _err()
         self._check(self._lib.fc_session_rollback(self.handle, int(position), err, len(err)), err)
 
+    def exchange_wait_ms(self):
+        """Device time the expert-exchange combines spent waiting for the
+        peers since the previous call (fc_session_exchange_wait_ms)."""
+        return float(self._lib.fc_session_exchange_wait_ms(self.handle))
+
     def last_kernel_count(self):
         """Kernels launched by the last forward pass (graph kernel nodes)."""
         return int(self._lib.fc_session_last_kernel_count(self.handle))

@@ -120,6 +120,7 @@ SIGNATURES = {
     "fc_model_set_tensor_rowscale": (_I, [_P, ctypes.c_char_p, ctypes.c_void_p, _S,
                                           ctypes.POINTER(ctypes.c_float), _I, _C, _S]),
     "fc_session_last_kernel_count": (_I, [_P]),
+    "fc_session_exchange_wait_ms": (ctypes.c_double, [_P]),
     "fc_io_bytes": (None, [ctypes.POINTER(ctypes.c_size_t), ctypes.POINTER(ctypes.c_size_t)]),
     "fc_session_ep_connect": (_I, [_P, ctypes.c_char_p, _I, _C, _S]),
     "fc_session_set_profiling": (_I, [_P, _I]),

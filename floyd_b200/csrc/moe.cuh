@@ -345,6 +345,7 @@ struct EpLink {
     int *epoch;                      // local counter, +1 per MoE layer (both sides in lockstep)
     int *flags;                      // [world] epochs published by the peers into this GPU
     int *peer_flags[kMaxRanks];      // the peers' flag arrays (index rank = this rank)
+    unsigned long long *wait_ns;     // nullable: block 0 adds the time it spent waiting for the peers
 };
 
 __device__ __forceinline__ int ld_acquire_sys(const int *p) {
@@ -387,7 +388,8 @@ moe_combine_kernel(float *resid, const float *routed, const float *shared, const
     if (link.world > 1) {
         if (threadIdx.x == 0) {
             const int e = *link.epoch;
-            uint64_t t0 = 0;
+            uint64_t t0 = 0, w0;
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(w0));
             for (int r = 0; r < link.world; ++r) {
                 if (r == link.rank) continue;
                 for (uint32_t it = 0; ld_acquire_sys(link.flags + r) < e; ++it) {
@@ -403,6 +405,11 @@ moe_combine_kernel(float *resid, const float *routed, const float *shared, const
                 }
             }
             count = e;  // reused below for the parity
+            if (link.wait_ns && blockIdx.x == 0) {  // the exchange time this rank was exposed to
+                uint64_t w1;
+                asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(w1));
+                atomicAdd(link.wait_ns, (unsigned long long)(w1 - w0));
+            }
         }
         __syncthreads();
         routed += (count & 1) * parity_stride;

@@ -168,6 +168,7 @@ struct FcSession {
     void *ep_region = nullptr;
     float *ep_xbuf = nullptr;
     int *ep_flags = nullptr, *ep_epoch = nullptr;
+    unsigned long long *ep_wait_ns = nullptr;  // time the combines spent waiting for peers
     void *ep_peer_region[kMaxRanks] = {};
     bool ep_connected = false;
     Staging *d_stage = nullptr, *h_stage = nullptr;
@@ -858,6 +859,7 @@ cudaError_t record_ffn(FcSession *s, int S, int l, const Staging *dst, float *ou
         if (ep) {
             link.epoch = s->ep_epoch;
             link.flags = s->ep_flags;
+            link.wait_ns = s->ep_wait_ns;
             for (int r = 0; r < m->world; ++r)
                 if (r != m->rank)
                     link.peer_flags[r] = reinterpret_cast<int *>(
@@ -2029,6 +2031,7 @@ int create_session(FcSession **out, FcModel *m, const FcOptions *options, const 
             s->ep_flags = reinterpret_cast<int *>(reinterpret_cast<uint8_t *>(s->ep_region) + xb);
         }
         ok = ok && salloc(s, s->ep_epoch, 1);
+        ok = ok && salloc(s, s->ep_wait_ns, 1);
     }
     ok = ok && salloc(s, s->sh_part, (size_t)mb * D);
     ok = ok && salloc(s, s->logits, (size_t)mb * V);
@@ -2363,6 +2366,16 @@ int fc_session_copy_row_logits(const FcSession *s, float *logits, int capacity_r
 }
 
 int fc_session_last_kernel_count(const FcSession *s) { return s ? s->last_kernels : 0; }
+
+double fc_session_exchange_wait_ms(FcSession *s) {
+    if (!s || !s->ep_wait_ns) return 0.0;
+    unsigned long long ns = 0;
+    cudaSetDevice(s->m->device);
+    cudaStreamSynchronize(s->stream);
+    cudaMemcpy(&ns, s->ep_wait_ns, sizeof ns, cudaMemcpyDeviceToHost);
+    cudaMemset(s->ep_wait_ns, 0, sizeof ns);
+    return (double)ns * 1e-6;
+}
 
 void fc_io_bytes(size_t *h2d, size_t *d2h) {
     if (h2d) *h2d = sizeof(Staging);

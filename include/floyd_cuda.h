@@ -369,6 +369,11 @@ void fc_io_bytes(size_t *h2d, size_t *d2h);
  * exactly as on one GPU.  Forward calls fail until the session is
  * connected. */
 #define FC_EP_HANDLE_BYTES 64
+/* Milliseconds the MoE combines of this rank spent waiting for the peers'
+ * expert outputs (the exposed part of the exchange: one timer per MoE layer,
+ * on the device) since the previous call; resets the counter.  0 for a
+ * single-GPU session. */
+double fc_session_exchange_wait_ms(FcSession *session);
 int fc_session_ep_handle(FcSession *session, void *handle, size_t handle_size,
                          char *error, size_t error_size);
 int fc_session_ep_connect(FcSession *session, const void *handles, int world,
