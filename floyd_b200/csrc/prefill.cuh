@@ -33,6 +33,10 @@ namespace fc {
 constexpr int kPfThreads = 448;
 constexpr int kPfWarpProducer = 4, kPfWarpMma = 5, kPfWarpDq0 = 6, kPfDqThreads = 256;
 constexpr int kPfM = 128, kPfK = 64;
+// m-tiles per work item: each dequantized weight tile feeds the MMAs of two
+// 128-row m-tiles, so the dequant work per MMA is half of one m-tile's
+constexpr int kPfMP = 2, kPfMI = kPfM * kPfMP;
+constexpr int kPfBN = 128;  // weight rows (MMA N) per n-tile
 constexpr int kPfSA = 4, kPfSD = 3, kPfSQ = 2;
 constexpr int kPfRawBytes = 16 * 1152;
 
@@ -56,18 +60,18 @@ struct PfGemm {
 
 template <int BN>
 struct PfPlan {
-    static constexpr int A_BYTES = kPfM * 128;
+    static constexpr int A_BYTES = kPfMP * kPfM * 128;  // both m-tiles of a k-step
     static constexpr int D_BYTES = BN * 128;
     static constexpr int OFF_D = kPfSA * A_BYTES;
     static constexpr int OFF_Q = OFF_D + kPfSD * D_BYTES;
     static constexpr int OFF_BAR = OFF_Q + kPfSQ * kPfRawBytes;
     static constexpr size_t SMEM = (size_t)OFF_BAR + 256 + 1024;  // + base alignment
-    static constexpr uint32_t TMEM_COLS = 2 * BN;
+    static constexpr uint32_t TMEM_COLS = 2 * kPfMP * BN;  // (double buffer) x (m-tile)
     static_assert(SMEM <= 232448, "shared memory plan");
 };
 
 struct PfTile {
-    int g, a_x, a_y, out_row0, nvalid;
+    int g, a_x, a_y, out_row0, nvalid;  // nvalid: rows of the item (m-tile mp has nvalid - 128 mp)
 };
 
 __device__ __forceinline__ PfTile pf_tile(const PfGemm &p, int mi, int mpg) {
@@ -78,14 +82,14 @@ __device__ __forceinline__ PfTile pf_tile(const PfGemm &p, int mi, int mpg) {
         t.a_x = e.x * p.a_gx;
         t.a_y = e.y;
         t.out_row0 = e.y;
-        t.nvalid = min(kPfM, e.z - e.y);
+        t.nvalid = min(kPfMI, e.z - e.y);
     } else {
         t.g = mi / mpg;
-        const int m0 = (mi % mpg) * kPfM;
+        const int m0 = (mi % mpg) * kPfMI;
         t.a_x = t.g * p.a_gx;
         t.a_y = p.a_y0 + t.g * p.a_gy + m0;
         t.out_row0 = m0;
-        t.nvalid = min(kPfM, p.rows - m0);
+        t.nvalid = min(kPfMI, p.rows - m0);
     }
     return t;
 }
@@ -261,7 +265,7 @@ pf_gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__
     pdl_wait();
     pdl_release();
 
-    const int mpg = (p.rows + kPfM - 1) / kPfM;
+    const int mpg = (p.rows + kPfMI - 1) / kPfMI;
     const int n_mt = p.mt_table ? *p.mt_count : p.groups * mpg;
     const int n_nt = (p.N + BNO - 1) / BNO;
     const int items = n_mt * n_nt;
@@ -294,7 +298,10 @@ pf_gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__
                     }
                     if (a_fill >= kPfSA && !pf_wait(&a_empty[a_slot], a_ph ^ 1, p.err, abort, 1)) break;
                     mbar_expect_tx(&a_full[a_slot], P::A_BYTES);
+                    // both m-tiles (rows past the tensor arrive as zeros)
                     tma_load_2d(sA + a_slot * P::A_BYTES, &amap, t.a_x + ks * kPfK, t.a_y, &a_full[a_slot]);
+                    tma_load_2d(sA + a_slot * P::A_BYTES + kPfM * 128, &amap, t.a_x + ks * kPfK, t.a_y + kPfM,
+                                &a_full[a_slot]);
                     ++a_fill;
                     if (++a_slot == kPfSA) { a_slot = 0; a_ph ^= 1; }
                 }
@@ -320,16 +327,20 @@ pf_gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__
                 const int b = t & 1;
                 if (t >= 2) pf_wait(&acc_empty[b], ((t >> 1) - 1) & 1, p.err, abort, 2);
                 tc_fence_after();
-                const uint32_t tacc = tmem + b * BN;
+                const uint32_t tacc = tmem + b * kPfMP * BN;
                 for (int ks = 0; ks < nk; ++ks) {
                     pf_wait(&a_full[a_slot], a_ph, p.err, abort, 3);
                     pf_wait(&d_full[d_slot], d_ph, p.err, abort, 4);
                     tc_fence_after();
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk) {
-                        const uint64_t ad = smem_desc(a0 + a_slot * P::A_BYTES + kk * 32, 16, 1024, kSmemLayoutSw128);
                         const uint64_t bd = smem_desc(d0 + d_slot * P::D_BYTES + kk * 32, 16, 1024, kSmemLayoutSw128);
-                        tc_mma_f16(tacc, ad, bd, idesc, (ks | kk) != 0);
+#pragma unroll
+                        for (int mp = 0; mp < kPfMP; ++mp) {
+                            const uint64_t ad = smem_desc(a0 + a_slot * P::A_BYTES + mp * kPfM * 128 + kk * 32, 16,
+                                                          1024, kSmemLayoutSw128);
+                            tc_mma_f16(tacc + mp * BN, ad, bd, idesc, (ks | kk) != 0);
+                        }
                     }
                     tc_commit(&a_empty[a_slot]);
                     tc_commit(&d_empty[d_slot]);
@@ -438,9 +449,11 @@ pf_gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__
             pf_wait(&acc_full[b], (t >> 1) & 1, p.err, abort, 7);
             __syncwarp();
             tc_fence_after();
-            const uint32_t tacc = tmem + b * BN + lane_off;
-            const bool ok = row < tl.nvalid;
-            const int64_t orow = (int64_t)(tl.out_row0 + row) * p.out_ld + (int64_t)tl.g * p.out_gstride;
+#pragma unroll 1
+            for (int mp = 0; mp < kPfMP; ++mp) {
+            const uint32_t tacc = tmem + (b * kPfMP + mp) * BN + lane_off;
+            const bool ok = mp * kPfM + row < tl.nvalid;
+            const int64_t orow = (int64_t)(tl.out_row0 + mp * kPfM + row) * p.out_ld + (int64_t)tl.g * p.out_gstride;
             if (EPI == PF_SWIGLU_F16) {
                 __half *out = reinterpret_cast<__half *>(p.out) + orow;
 #pragma unroll 1
@@ -508,6 +521,7 @@ pf_gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__
                     }
                 }
             }
+            }  // m-tile
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cta(&acc_empty[b]);
@@ -972,7 +986,7 @@ __global__ void __launch_bounds__(1024) pf_group_kernel(int *counts, int E, int 
     const int e = threadIdx.x;
     const int c = e < E ? counts[e] : 0;
     off[e + 1] = c;
-    tiles[e + 1] = (c + kPfM - 1) / kPfM;
+    tiles[e + 1] = (c + kPfMI - 1) / kPfMI;
     if (e == 0) off[0] = tiles[0] = 0;
     __syncthreads();
     for (int o = 1; o < 1024; o <<= 1) {
@@ -991,7 +1005,7 @@ __global__ void __launch_bounds__(1024) pf_group_kernel(int *counts, int E, int 
         cursor[e] = off[e];
         counts[e] = 0;
         for (int i = 0; i < tiles[e + 1] - tiles[e]; ++i)
-            mt_table[tiles[e] + i] = make_int4(e, off[e] + i * kPfM, off[e] + c, 0);
+            mt_table[tiles[e] + i] = make_int4(e, off[e] + i * kPfMI, off[e] + c, 0);
     }
     if (e == 0) *mt_count = tiles[E];
 }

@@ -1135,7 +1135,7 @@ int exec_pass(FcSession *s, int rows, int drafts, char *err, size_t n) {
 // prefill chunks on the tensor cores
 // ---------------------------------------------------------------------------
 #define FC_PF_VARIANTS(X, F) \
-    X(F, 256, PF_STORE_F32) X(F, 256, PF_STORE_F16) X(F, 256, PF_ADD_F32) X(F, 256, PF_SWIGLU_F16)
+    X(F, kPfBN, PF_STORE_F32) X(F, kPfBN, PF_STORE_F16) X(F, kPfBN, PF_ADD_F32) X(F, kPfBN, PF_SWIGLU_F16)
 #define FC_PF_ALL(X) FC_PF_VARIANTS(X, FC_FMT_Q8) FC_PF_VARIANTS(X, FC_FMT_Q4) FC_PF_VARIANTS(X, FC_FMT_MXFP4)
 
 cudaError_t pf_prepare_all() {
@@ -1163,7 +1163,7 @@ cudaError_t pf_prepare_all() {
 // One tcgen05 GEMM launch (one CTA per SM) of weight format `fmt`.
 cudaError_t pf_gemm(int fmt, int epi, const CUtensorMap &map, const CUtensorMap &wmap, const CUtensorMap &wmap2,
                     const PfGemm &p, int sms, cudaStream_t st) {
-    constexpr int bn = 256;
+    constexpr int bn = kPfBN;
 #define FC_PF_CASE(F, BN, EPI)                                                                       \
     if (fmt == F && bn == BN && epi == EPI)                                                          \
         return launch_pdl(pf_gemm_kernel<F, BN, EPI>, dim3(sms), dim3(kPfThreads), PfPlan<BN>::SMEM, st, map, \
@@ -1190,7 +1190,7 @@ cudaError_t pf_gemm_w(FcSession *s, int epi, const CUtensorMap &amap, const DevM
                       PfGemm p) {
     // a box never exceeds the tensor (such a copy would not complete)
     const int tiles = std::max(w.count, 1) * ((w.O + kTileRows - 1) / kTileRows);
-    const int box = std::min(epi == PF_SWIGLU_F16 ? 8 : 16, tiles);
+    const int box = std::min(epi == PF_SWIGLU_F16 ? kPfBN / 32 : kPfBN / 16, tiles);
     p.box_tiles = box;
     const CUtensorMap *m1 = pf_wmap(s, w, box);
     const CUtensorMap *m2 = w2 ? pf_wmap(s, *w2, box) : m1;
