@@ -657,13 +657,18 @@ __device__ __forceinline__ void combine_row(const float *part_o, const float *pa
 
 __global__ void __launch_bounds__(kCombineThreads)
 mla_combine_kernel(const float *part_o, const float *part_m, const float *part_l, int splits, int S,
-                   int H, int L, __half *ctx_xq, size_t head_stride) {
+                   int H, int L, int ml_cols, __half *ctx_xq, size_t head_stride) {
     pdl_wait();
     pdl_release();
     __shared__ float wts[kMaxSplits];
     __shared__ float red[kCombineThreads / 32];
     const int q = blockIdx.x, nq = S * H;
     const int l = blockIdx.y * kCombineThreads + threadIdx.x;
+    // every ml_cols output columns (a multiple of the block width) have their
+    // own max / sum partials [group][split][q]
+    const size_t grp = (size_t)(blockIdx.y * kCombineThreads / ml_cols) * splits * nq;
+    part_m += grp;
+    part_l += grp;
     float v;
     if (splits <= 16) combine_row<16>(part_o, part_m, part_l, splits, nq, q, L, l, wts, red, v);
     else if (splits <= 32) combine_row<32>(part_o, part_m, part_l, splits, nq, q, L, l, wts, red, v);

@@ -5,22 +5,29 @@
 // the math): for every query q = s * H + h of the batch and every key of one
 // split, scores = qcat[q] . cache[key] (latent + rope, width L + 64), scaled,
 // masked to key <= pos + s, online softmax, and O = P . cache[key][0:L].
-// Writes the unnormalized split partials part_o [split][q][L], part_m,
-// part_l [split][q] that mla_combine_kernel folds in split order.
+// Writes the unnormalized split partials part_o [split][q][L] and, per half
+// of the output columns, part_m / part_l [half][split][q] that
+// mla_combine_kernel folds in split order.
 //
 // One CTA = (128-query tile, half of the L output columns, key split):
 //   warp 0      TMA producer: the query tile once, then 32-key blocks of the
-//               latent cache into a two-stage ring (128-byte swizzle);
+//               latent cache into a two-stage ring (128-byte swizzle).  Each
+//               stage has two parts with their own barriers: the 64-column
+//               slices this half's P . V reads (V slices) and the others.
+//               The other slices are refilled as soon as the block's score
+//               MMAs are done, the V slices once its P . V is done;
 //   warp 1      MMA issuer: S = Q . K^T into one of two 32-column TMEM score
-//               buffers (M=128, N=32, K=L+64), then O += P . V into the
-//               L/2-column TMEM accumulator (M=128, N=L/2, K=32, V read
-//               MN-major straight from the key block);
+//               buffers (M=128, N=32, K=L+64; the V slices last, so the
+//               V-slice load of a block overlaps its first score MMAs), then
+//               O += P . V into the L/2-column TMEM accumulator (M=128,
+//               N=L/2, K=32, V read MN-major straight from the key block);
 //   warp 2      TMEM allocation;
 //   warps 4-7   softmax: thread = query row = TMEM lane; reads its 32 scores,
 //               masks, updates max / sum, rescales its O row in TMEM when the
 //               max rises, writes its P row (fp16) to shared memory.
-// The two halves of a query tile compute the same scores; each keeps its own
-// 256 (or 128) output columns, so O fits the 512 TMEM columns.
+// The two halves of a query tile compute the same scores (summed in each
+// half's slice order, so each half keeps its own max and sum); each keeps its
+// own 256 (or 128) output columns, so O fits the 512 TMEM columns.
 // Each output row depends only on its own query and the split's keys, so a
 // verify row and a decode of the same token give the same bits.
 #pragma once
@@ -171,6 +178,8 @@ struct TcAttnPlan {
     static constexpr int DW = L + 64;            // score width (latent + rope)
     static constexpr int NKB = DW / 64;          // 64-column (128-byte) slices
     static constexpr int HALF = L / 2;           // output columns per CTA
+    static constexpr int VS = HALF / 64;         // V slices of a half
+    static constexpr int NV = NKB - VS;          // slices only the scores read
     static constexpr int Q_BYTES = NKB * kTcRows * 128;
     static constexpr int K_BYTES = NKB * kTcKeys * 128;
     static constexpr int P_BYTES = kTcRows * kTcKeys * 2;
@@ -198,17 +207,21 @@ mla_attention_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_c
     uint8_t *Ks = sm + P::OFF_K;
     uint8_t *Ps = sm + P::OFF_P;
     uint64_t *bars = reinterpret_cast<uint64_t *>(sm + P::OFF_BAR);
-    uint64_t *q_full = bars + 0, *kv_full = bars + 1, *kv_empty = bars + 3, *s_full = bars + 5,
-             *s_free = bars + 7, *p_full = bars + 9, *pv_done = bars + 10;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 12);
+    // kv_*_a: the stage's non-V slices, kv_*_b: its V slices
+    uint64_t *q_full = bars + 0, *kv_full_a = bars + 1, *kv_full_b = bars + 3, *kv_empty_a = bars + 5,
+             *kv_empty_b = bars + 7, *s_full = bars + 9, *s_free = bars + 11, *p_full = bars + 13,
+             *pv_done = bars + 14;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 15);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int q0 = blockIdx.x * kTcRows, half = blockIdx.y, split = blockIdx.z;
     if (tid == 0) {
         mbar_init(q_full, 1);
         for (int i = 0; i < 2; ++i) {
-            mbar_init(&kv_full[i], 1);
-            mbar_init(&kv_empty[i], 1);
+            mbar_init(&kv_full_a[i], 1);
+            mbar_init(&kv_full_b[i], 1);
+            mbar_init(&kv_empty_a[i], 1);
+            mbar_init(&kv_empty_b[i], 1);
             mbar_init(&s_full[i], 1);
             mbar_init(&s_free[i], 128);
         }
@@ -240,6 +253,8 @@ mla_attention_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_c
     const int k1 = min(k0 + keys_per_split, total);
     const int nblk = k1 > k0 ? (k1 - k0 + kTcKeys - 1) / kTcKeys : 0;
     const uint32_t tO = tmem, tS = tmem + P::HALF;
+    // i-th slice in this half's order: the non-V slices ascending, then the V slices
+    auto slice = [&](int i) { return i < P::NV ? (i < half * P::VS ? i : i + P::VS) : half * P::VS + (i - P::NV); };
 
     if (warp == 0) {
         // ---------------- TMA producer ----------------
@@ -248,13 +263,22 @@ mla_attention_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_c
             for (int kb = 0; kb < P::NKB; ++kb) tma_load_2d(Qs + kb * kTcRows * 128, &qmap, kb * 64, q0, q_full);
             for (int j = 0; j < nblk; ++j) {
                 const int stg = j & 1;
-                if (j >= 2) mbar_wait_timed(&kv_empty[stg], (uint32_t)(((j - 2) >> 1) & 1), err, 1);
-                TC_MARK(136 + j);
-                mbar_expect_tx(&kv_full[stg], P::K_BYTES);
+                const uint32_t ph = (uint32_t)(((j - 2) >> 1) & 1);
+                const int krow = kv_row0 + kv_row(pm, seq, k0 + j * kTcKeys);
                 uint8_t *dst = Ks + stg * P::K_BYTES;
-                for (int kb = 0; kb < P::NKB; ++kb)
-                    tma_load_2d(dst + kb * kTcKeys * 128, &kvmap, kb * 64, kv_row0 + kv_row(pm, seq, k0 + j * kTcKeys),
-                                &kv_full[stg]);
+                if (j >= 2) mbar_wait_timed(&kv_empty_a[stg], ph, err, 1);
+                TC_MARK(136 + j);
+                mbar_expect_tx(&kv_full_a[stg], P::NV * kTcKeys * 128);
+                for (int i = 0; i < P::NV; ++i) {
+                    const int kb = slice(i);
+                    tma_load_2d(dst + kb * kTcKeys * 128, &kvmap, kb * 64, krow, &kv_full_a[stg]);
+                }
+                if (j >= 2) mbar_wait_timed(&kv_empty_b[stg], ph, err, 1);
+                mbar_expect_tx(&kv_full_b[stg], P::VS * kTcKeys * 128);
+                for (int i = P::NV; i < P::NKB; ++i) {
+                    const int kb = slice(i);
+                    tma_load_2d(dst + kb * kTcKeys * 128, &kvmap, kb * 64, krow, &kv_full_b[stg]);
+                }
             }
         }
     } else if (warp == 1) {
@@ -265,40 +289,53 @@ mla_attention_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_c
             const uint32_t qa = smem_u32(Qs), ka = smem_u32(Ks), pa = smem_u32(Ps);
             mbar_wait_timed(q_full, 0, err, 0);
             TC_MARK(2);
-            auto issue_scores = [&](int j) {
-                const int stg = j & 1;
-                const uint32_t kst = ka + stg * P::K_BYTES;
-                for (int kb = 0; kb < P::NKB; ++kb)
+            // score MMAs of slices [i0, i1) (in this half's order) of block k
+            auto issue_scores = [&](int k, int i0, int i1) {
+                const uint32_t kst = ka + (k & 1) * P::K_BYTES;
+                for (int i = i0; i < i1; ++i) {
+                    const int kb = slice(i);
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk) {
                         // K-major, 128-byte swizzle: rows 128 B apart, 8-row groups 1024 B apart;
                         // the k-th 16-column step starts 32 B further into the row
                         uint64_t a = smem_desc(qa + kb * kTcRows * 128 + kk * 32, 16, 1024, kSmemLayoutSw128);
                         uint64_t b = smem_desc(kst + kb * kTcKeys * 128 + kk * 32, 16, 1024, kSmemLayoutSw128);
-                        tc_mma_f16(tS + stg * kTcKeys, a, b, idS, (kb | kk) != 0);
+                        tc_mma_f16(tS + (k & 1) * kTcKeys, a, b, idS, (i | kk) != 0);
                     }
-                tc_commit(&s_full[stg]);
+                }
             };
-            // scores of block k can go once its keys have landed and the
-            // softmax has read the score buffer's previous block (k - 2)
-            auto scores_ready = [&](int k) {
-                return mbar_try_wait(&kv_full[k & 1], (uint32_t)((k >> 1) & 1)) &&
-                       (k < 2 || mbar_try_wait(&s_free[k & 1], (uint32_t)(((k - 2) >> 1) & 1)));
-            };
-            int next = 0;  // next score block to issue
+            int next = 0;           // next score block to issue
+            bool next_nv = false;   // its non-V slices are issued
             for (int j = 0; j < nblk; ++j) {
                 // Issue P . V of block j as soon as its P is written; until
                 // then issue the scores of block j (needed for that) and of
-                // block j + 1 whenever their inputs are ready.
+                // block j + 1 whenever their inputs are ready: the non-V
+                // slices once they have landed and the softmax has read the
+                // score buffer's previous block (k - 2), the V slices once
+                // they have landed.
                 uint64_t t0 = 0;
                 for (uint32_t it = 0;; ++it) {
-                    if (next <= j + 1 && next < nblk && scores_ready(next)) {
-                        tc_fence_after();
-                        TC_MARK(8 + next);
-                        issue_scores(next);
-                        ++next;
-                    }
                     if (next > j && mbar_try_wait(p_full, (uint32_t)(j & 1))) break;
+                    if (next <= j + 1 && next < nblk) {
+                        const int stg = next & 1;
+                        const uint32_t ph = (uint32_t)((next >> 1) & 1);
+                        if (!next_nv && mbar_try_wait(&kv_full_a[stg], ph) &&
+                            (next < 2 || mbar_try_wait(&s_free[stg], (uint32_t)(((next - 2) >> 1) & 1)))) {
+                            tc_fence_after();
+                            TC_MARK(8 + next);
+                            issue_scores(next, 0, P::NV);
+                            tc_commit(&kv_empty_a[stg]);
+                            next_nv = true;
+                        }
+                        if (next_nv && mbar_try_wait(&kv_full_b[stg], ph)) {
+                            tc_fence_after();
+                            issue_scores(next, P::NV, P::NKB);
+                            tc_commit(&s_full[stg]);
+                            ++next;
+                            next_nv = false;
+                            continue;
+                        }
+                    }
                     if ((it & 255u) == 0) {
                         uint64_t t = global_ns();
                         if (t0 == 0) t0 = t;
@@ -320,7 +357,7 @@ mla_attention_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_c
                     uint64_t b = smem_desc(vst + kk * 2048, kTcKeys * 128, 1024, kSmemLayoutSw128);
                     tc_mma_f16(tO, a, b, idO, (j | kk) != 0);
                 }
-                tc_commit(&kv_empty[j & 1]);
+                tc_commit(&kv_empty_b[j & 1]);
                 tc_commit(pv_done);
             }
         }
@@ -426,10 +463,11 @@ mla_attention_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_c
             }
         }
         if (row == 0) TC_MARK(200);
-        if (q < nq && half == 0) {
+        if (q < nq) {
             // back to the natural-log domain of the split combine
-            part_m[(size_t)split * nq + q] = m_run == -INFINITY ? -INFINITY : m_run * 0.6931471805599453f;
-            part_l[(size_t)split * nq + q] = l_run;
+            const size_t at = ((size_t)half * gridDim.z + split) * nq + q;
+            part_m[at] = m_run == -INFINITY ? -INFINITY : m_run * 0.6931471805599453f;
+            part_l[at] = l_run;
         }
     }
     tc_fence_before();
@@ -442,3 +480,4 @@ mla_attention_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_c
 }
 
 }  // namespace fc
+

@@ -709,7 +709,7 @@ cudaError_t record_attention(FcSession *s, int S, int l, const Staging *dst, int
         FC_TRY(launch_pdl(mla_combine_kernel, dim3(S * H, (L + kCombineThreads - 1) / kCombineThreads),
                           dim3(kCombineThreads), 0, st, (const float *)s->part_o,
                           (const float *)s->part_m, (const float *)s->part_l, s->splits, S, H, L,
-                          s->ctx_xq, head_stride));
+                          s->attn_tc ? L / 2 : L, s->ctx_xq, head_stride));
         mark(s, "mla_combine");
         // W_UV: rows nope .. nope+v of each head's kv_b block (decode_value, :345-375)
         // nope and value_dim are multiples of 16, so each head's W_UV
@@ -1998,8 +1998,8 @@ int create_session(FcSession **out, FcModel *m, const FcOptions *options, const 
     const int q_rows = (mb * H + kTcRows - 1) / kTcRows * kTcRows;
     ok = ok && salloc(s, s->qcat, (size_t)q_rows * (L + R));
     ok = ok && salloc(s, s->part_o, (size_t)s->splits * mb * H * L);
-    ok = ok && salloc(s, s->part_m, (size_t)s->splits * mb * H);
-    ok = ok && salloc(s, s->part_l, (size_t)s->splits * mb * H);
+    ok = ok && salloc(s, s->part_m, (size_t)2 * s->splits * mb * H);  // [half][split][row] (tcgen05 attention)
+    ok = ok && salloc(s, s->part_l, (size_t)2 * s->splits * mb * H);
     ok = ok && salloc(s, s->ctx_xq, (size_t)H * mb * kpad(L) * 2);
     ok = ok && salloc(s, s->o_xq, (size_t)mb * kpad(H * c.value_dim) * 2);
     ok = ok && salloc(s, s->router_logits, (size_t)2 * mb * E);  // scores, then choices
