@@ -16,8 +16,9 @@
 //               slices this half's P . V reads (V slices) and the others.
 //               The other slices are refilled as soon as the block's score
 //               MMAs are done, the V slices once its P . V is done;
-//   warp 1      MMA issuer: S = Q . K^T into one of two 32-column TMEM score
-//               buffers (M=128, N=32, K=L+64; the V slices last, so the
+//   warp 1      MMA issuer: S = Q . K^T into one of two TMEM score buffers
+//               of 4 partial 32-column accumulators that consecutive MMAs
+//               rotate over (M=128, N=32, K=L+64; the V slices last, so the
 //               V-slice load of a block overlaps its first score MMAs), then
 //               O += P . V into the L/2-column TMEM accumulator (M=128,
 //               N=L/2, K=32, V read MN-major straight from the key block);
@@ -171,6 +172,11 @@ __device__ unsigned long long g_tc_trace[256];
 constexpr int kTcThreads = 256;
 constexpr int kTcRows = 128;  // queries per tile (MMA M)
 constexpr int kTcKeys = 32;   // keys per block (score MMA N)
+// Partial score accumulators per block: consecutive score MMAs go to
+// different TMEM tiles, so they do not wait on each other's accumulation
+// (an N=32 MMA chained on one accumulator runs at ~1/6 of the tensor rate);
+// the softmax adds the partials.
+constexpr int kTcSAcc = 4;  // the softmax sums exactly four
 constexpr float kRescaleLog2 = 11.0f;  // lazy softmax rescale threshold (log2)
 
 template <int L>
@@ -187,8 +193,10 @@ struct TcAttnPlan {
     static constexpr int OFF_P = OFF_K + 2 * K_BYTES;
     static constexpr int OFF_BAR = OFF_P + P_BYTES;
     static constexpr size_t SMEM = (size_t)OFF_BAR + 128 + 1024;  // + 1 KB for base alignment
+    static constexpr int S_COLS = kTcSAcc * kTcKeys;            // one score buffer (partials)
     static constexpr uint32_t TMEM_COLS = 512;                   // O (HALF) + two score buffers
-    static_assert(HALF + 2 * kTcKeys <= (int)TMEM_COLS, "TMEM plan");
+    static_assert(HALF + 2 * S_COLS <= (int)TMEM_COLS, "TMEM plan");
+    static_assert(NKB >= kTcSAcc, "every partial accumulator gets a slice");
     static_assert(SMEM <= 232448, "shared memory plan");
 };
 
@@ -261,23 +269,33 @@ mla_attention_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_c
         if (lane == 0 && nblk > 0) {
             mbar_expect_tx(q_full, P::Q_BYTES);
             for (int kb = 0; kb < P::NKB; ++kb) tma_load_2d(Qs + kb * kTcRows * 128, &qmap, kb * 64, q0, q_full);
-            for (int j = 0; j < nblk; ++j) {
-                const int stg = j & 1;
-                const uint32_t ph = (uint32_t)(((j - 2) >> 1) & 1);
-                const int krow = kv_row0 + kv_row(pm, seq, k0 + j * kTcKeys);
-                uint8_t *dst = Ks + stg * P::K_BYTES;
-                if (j >= 2) mbar_wait_timed(&kv_empty_a[stg], ph, err, 1);
-                TC_MARK(136 + j);
-                mbar_expect_tx(&kv_full_a[stg], P::NV * kTcKeys * 128);
-                for (int i = 0; i < P::NV; ++i) {
-                    const int kb = slice(i);
-                    tma_load_2d(dst + kb * kTcKeys * 128, &kvmap, kb * 64, krow, &kv_full_a[stg]);
+            // the non-V slices run one block ahead of the V slices: those of
+            // block j are refilled once block j - 2's scores are done, before
+            // the V slices of block j - 1 (which wait for block j - 3's P . V)
+            for (int j = 0; j <= nblk; ++j) {
+                if (j < nblk) {
+                    const int stg = j & 1;
+                    if (j >= 2) mbar_wait_timed(&kv_empty_a[stg], (uint32_t)(((j - 2) >> 1) & 1), err, 1);
+                    TC_MARK(136 + j);
+                    const int krow = kv_row0 + kv_row(pm, seq, k0 + j * kTcKeys);
+                    uint8_t *dst = Ks + stg * P::K_BYTES;
+                    mbar_expect_tx(&kv_full_a[stg], P::NV * kTcKeys * 128);
+                    for (int i = 0; i < P::NV; ++i) {
+                        const int kb = slice(i);
+                        tma_load_2d(dst + kb * kTcKeys * 128, &kvmap, kb * 64, krow, &kv_full_a[stg]);
+                    }
                 }
-                if (j >= 2) mbar_wait_timed(&kv_empty_b[stg], ph, err, 1);
-                mbar_expect_tx(&kv_full_b[stg], P::VS * kTcKeys * 128);
-                for (int i = P::NV; i < P::NKB; ++i) {
-                    const int kb = slice(i);
-                    tma_load_2d(dst + kb * kTcKeys * 128, &kvmap, kb * 64, krow, &kv_full_b[stg]);
+                if (j >= 1) {
+                    const int k = j - 1, stg = k & 1;
+                    if (k >= 2) mbar_wait_timed(&kv_empty_b[stg], (uint32_t)(((k - 2) >> 1) & 1), err, 1);
+                    TC_MARK(168 + k);
+                    const int krow = kv_row0 + kv_row(pm, seq, k0 + k * kTcKeys);
+                    uint8_t *dst = Ks + stg * P::K_BYTES;
+                    mbar_expect_tx(&kv_full_b[stg], P::VS * kTcKeys * 128);
+                    for (int i = P::NV; i < P::NKB; ++i) {
+                        const int kb = slice(i);
+                        tma_load_2d(dst + kb * kTcKeys * 128, &kvmap, kb * 64, krow, &kv_full_b[stg]);
+                    }
                 }
             }
         }
@@ -289,18 +307,33 @@ mla_attention_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_c
             const uint32_t qa = smem_u32(Qs), ka = smem_u32(Ks), pa = smem_u32(Ps);
             mbar_wait_timed(q_full, 0, err, 0);
             TC_MARK(2);
-            // score MMAs of slices [i0, i1) (in this half's order) of block k
+            // score MMAs of slices [i0, i1) (in this half's order) of block k.
+            // K-major, 128-byte swizzle: rows 128 B apart, 8-row groups 1024 B
+            // apart; the k-th 16-column step starts 32 B further into the row.
+            // The descriptors are built once; a step adds its byte offset / 16
+            // to the start-address field (every operand lies below 256 KB).
+            const uint64_t qdesc = smem_desc(qa, 16, 1024, kSmemLayoutSw128);
+            const uint64_t kdesc = smem_desc(ka, 16, 1024, kSmemLayoutSw128);
             auto issue_scores = [&](int k, int i0, int i1) {
-                const uint32_t kst = ka + (k & 1) * P::K_BYTES;
-                for (int i = i0; i < i1; ++i) {
+                const uint64_t kd = kdesc + (uint64_t)(((k & 1) * P::K_BYTES) >> 4);
+                const uint32_t ts = tS + (k & 1) * P::S_COLS;
+#pragma unroll
+                for (int i = 0; i < P::NKB; ++i) {
+                    if (i < i0 || i >= i1) continue;
                     const int kb = slice(i);
+                    const uint64_t ad = qdesc + (uint64_t)(kb * (kTcRows * 128 / 16));
+                    const uint64_t bd = kd + (uint64_t)(kb * (kTcKeys * 128 / 16));
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk) {
-                        // K-major, 128-byte swizzle: rows 128 B apart, 8-row groups 1024 B apart;
-                        // the k-th 16-column step starts 32 B further into the row
-                        uint64_t a = smem_desc(qa + kb * kTcRows * 128 + kk * 32, 16, 1024, kSmemLayoutSw128);
-                        uint64_t b = smem_desc(kst + kb * kTcKeys * 128 + kk * 32, 16, 1024, kSmemLayoutSw128);
-                        tc_mma_f16(tS + (k & 1) * kTcKeys, a, b, idS, (i | kk) != 0);
+#ifndef FC_TC_NOS
+                        // slice position i accumulates into partial i % kTcSAcc
+#ifdef FC_TC_N64
+                        tc_mma_f16(ts, ad + 2 * kk, bd + 2 * kk, idesc_f16(kTcRows, 64, false), i > 0 || kk != 0);
+#else
+                        tc_mma_f16(ts + (i % kTcSAcc) * kTcKeys, ad + 2 * kk, bd + 2 * kk, idS,
+                                   i >= kTcSAcc || kk != 0);
+#endif
+#endif
                     }
                 }
             };
@@ -329,6 +362,7 @@ mla_attention_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_c
                         }
                         if (next_nv && mbar_try_wait(&kv_full_b[stg], ph)) {
                             tc_fence_after();
+                            TC_MARK(24 + next);
                             issue_scores(next, P::NV, P::NKB);
                             tc_commit(&s_full[stg]);
                             ++next;
@@ -355,7 +389,9 @@ mla_attention_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_c
                     // V: MN-major, 128-byte swizzle: 64 columns per 128-byte key row, next 64 columns
                     // in the next slice (4 KB), next 8 keys 1024 B further
                     uint64_t b = smem_desc(vst + kk * 2048, kTcKeys * 128, 1024, kSmemLayoutSw128);
+#ifndef FC_TC_NOPV
                     tc_mma_f16(tO, a, b, idO, (j | kk) != 0);
+#endif
                 }
                 tc_commit(&kv_empty_b[j & 1]);
                 tc_commit(pv_done);
@@ -376,8 +412,18 @@ mla_attention_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_c
             __syncwarp();  // tcgen05.ld is warp-collective
             tc_fence_after();
             float sv[32];
-            tmem_ld32(tS + stg * kTcKeys + lane_off, sv);
-            tmem_wait_ld();
+            {
+                // (p0 + p1) + (p2 + p3) of the partial accumulators
+                float t1[32], t2[32], t3[32];
+                const uint32_t ts = tS + stg * P::S_COLS + lane_off;
+                tmem_ld32(ts, sv);
+                tmem_ld32(ts + kTcKeys, t1);
+                tmem_ld32(ts + 2 * kTcKeys, t2);
+                tmem_ld32(ts + 3 * kTcKeys, t3);
+                tmem_wait_ld();
+#pragma unroll
+                for (int c = 0; c < 32; ++c) sv[c] = (sv[c] + t1[c]) + (t2[c] + t3[c]);
+            }
             tc_fence_before();
             mbar_arrive_cta(&s_free[stg]);
             // scores in the log2 domain: s2 = score * scale * log2(e)
