@@ -16,9 +16,8 @@
 //               slices this half's P . V reads (V slices) and the others.
 //               The other slices are refilled as soon as the block's score
 //               MMAs are done, the V slices once its P . V is done;
-//   warp 1      MMA issuer: S = Q . K^T into one of two TMEM score buffers
-//               of 4 partial 32-column accumulators that consecutive MMAs
-//               rotate over (M=128, N=32, K=L+64; the V slices last, so the
+//   warp 1      MMA issuer: S = Q . K^T into one of two 32-column TMEM score
+//               buffers (M=128, N=32, K=L+64; the V slices last, so the
 //               V-slice load of a block overlaps its first score MMAs), then
 //               O += P . V into the L/2-column TMEM accumulator (M=128,
 //               N=L/2, K=32, V read MN-major straight from the key block);
@@ -172,11 +171,6 @@ __device__ unsigned long long g_tc_trace[256];
 constexpr int kTcThreads = 256;
 constexpr int kTcRows = 128;  // queries per tile (MMA M)
 constexpr int kTcKeys = 32;   // keys per block (score MMA N)
-// Partial score accumulators per block: consecutive score MMAs go to
-// different TMEM tiles, so they do not wait on each other's accumulation
-// (an N=32 MMA chained on one accumulator runs at ~1/6 of the tensor rate);
-// the softmax adds the partials.
-constexpr int kTcSAcc = 4;  // the softmax sums exactly four
 constexpr float kRescaleLog2 = 11.0f;  // lazy softmax rescale threshold (log2)
 
 template <int L>
@@ -193,10 +187,9 @@ struct TcAttnPlan {
     static constexpr int OFF_P = OFF_K + 2 * K_BYTES;
     static constexpr int OFF_BAR = OFF_P + P_BYTES;
     static constexpr size_t SMEM = (size_t)OFF_BAR + 128 + 1024;  // + 1 KB for base alignment
-    static constexpr int S_COLS = kTcSAcc * kTcKeys;            // one score buffer (partials)
+    static constexpr int S_COLS = kTcKeys;                      // one score buffer
     static constexpr uint32_t TMEM_COLS = 512;                   // O (HALF) + two score buffers
     static_assert(HALF + 2 * S_COLS <= (int)TMEM_COLS, "TMEM plan");
-    static_assert(NKB >= kTcSAcc, "every partial accumulator gets a slice");
     static_assert(SMEM <= 232448, "shared memory plan");
 };
 
@@ -325,15 +318,7 @@ mla_attention_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_c
                     const uint64_t bd = kd + (uint64_t)(kb * (kTcKeys * 128 / 16));
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk) {
-#ifndef FC_TC_NOS
-                        // slice position i accumulates into partial i % kTcSAcc
-#ifdef FC_TC_N64
-                        tc_mma_f16(ts, ad + 2 * kk, bd + 2 * kk, idesc_f16(kTcRows, 64, false), i > 0 || kk != 0);
-#else
-                        tc_mma_f16(ts + (i % kTcSAcc) * kTcKeys, ad + 2 * kk, bd + 2 * kk, idS,
-                                   i >= kTcSAcc || kk != 0);
-#endif
-#endif
+                        tc_mma_f16(ts, ad + 2 * kk, bd + 2 * kk, idS, i > 0 || kk != 0);
                     }
                 }
             };
@@ -389,9 +374,7 @@ mla_attention_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_c
                     // V: MN-major, 128-byte swizzle: 64 columns per 128-byte key row, next 64 columns
                     // in the next slice (4 KB), next 8 keys 1024 B further
                     uint64_t b = smem_desc(vst + kk * 2048, kTcKeys * 128, 1024, kSmemLayoutSw128);
-#ifndef FC_TC_NOPV
                     tc_mma_f16(tO, a, b, idO, (j | kk) != 0);
-#endif
                 }
                 tc_commit(&kv_empty_b[j & 1]);
                 tc_commit(pv_done);
@@ -412,18 +395,8 @@ mla_attention_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_c
             __syncwarp();  // tcgen05.ld is warp-collective
             tc_fence_after();
             float sv[32];
-            {
-                // (p0 + p1) + (p2 + p3) of the partial accumulators
-                float t1[32], t2[32], t3[32];
-                const uint32_t ts = tS + stg * P::S_COLS + lane_off;
-                tmem_ld32(ts, sv);
-                tmem_ld32(ts + kTcKeys, t1);
-                tmem_ld32(ts + 2 * kTcKeys, t2);
-                tmem_ld32(ts + 3 * kTcKeys, t3);
-                tmem_wait_ld();
-#pragma unroll
-                for (int c = 0; c < 32; ++c) sv[c] = (sv[c] + t1[c]) + (t2[c] + t3[c]);
-            }
+            tmem_ld32(tS + stg * P::S_COLS + lane_off, sv);
+            tmem_wait_ld();
             tc_fence_before();
             mbar_arrive_cta(&s_free[stg]);
             // scores in the log2 domain: s2 = score * scale * log2(e)

@@ -112,6 +112,8 @@ struct FcModel {
     uint64_t resident = 0;
 };
 
+constexpr int kMaxLanes = 4;  // concurrent passes of a batch step
+
 struct FcSession {
     FcModel *m = nullptr;
     FcOptions opt{};
@@ -198,6 +200,13 @@ struct FcSession {
     CUtensorMap pf_map_x{}, pf_map_q{}, pf_map_qa{}, pf_map_o{}, pf_map_hd{}, pf_map_hs{}, pf_map_xg{},
         pf_map_hg{}, pf_map_kvd{}, pf_cmap{}, pf_cmap64{};
     std::vector<std::string> prof_marks;
+    // batch sessions: child sessions ("lanes") with their own workspace,
+    // stream and graphs over this session's latent cache and page table; the
+    // passes of one batch step run on them concurrently (single GPU)
+    std::vector<FcSession *> lanes;
+    bool lane = false;                 // a lane (does not own the cache)
+    const FcSession *last_lane = nullptr;  // the lane of the last pass (its logits)
+    cudaEvent_t ev_lane = nullptr;     // end of this lane's pass
     std::vector<std::pair<std::string, std::pair<double, uint64_t>>> prof;
 };
 
@@ -519,6 +528,8 @@ void free_session_buffers(FcSession *s) {
     s->stream = nullptr;
     if (s->ev_begin) cudaEventDestroy(s->ev_begin);
     if (s->ev_end) cudaEventDestroy(s->ev_end);
+    if (s->ev_lane) cudaEventDestroy(s->ev_lane);
+    s->ev_begin = s->ev_end = s->ev_lane = nullptr;
     for (cudaEvent_t ev : s->prof_events) cudaEventDestroy(ev);
     s->prof_events.clear();
 }
@@ -1088,6 +1099,33 @@ int run_pass(FcSession *s, const int *ids, int rows, int k, const FcAcceptConfig
     return exec_pass(s, rows, drafts, err, n);
 }
 
+// Launches the captured graph of the pass staged in h_stage on the
+// session's stream, without waiting for it.
+int launch_pass(FcSession *s, int rows, int drafts, char *err, size_t n) {
+    cudaGraphExec_t g = get_graph(s, rows, drafts, err, n);
+    if (!g) return 0;
+    s->last_kernels = s->graph_kernels[(rows * 2 + (s->trace ? 1 : 0)) * 16 + drafts];
+    cudaError_t e = cudaGraphLaunch(g, s->stream);
+    if (e != cudaSuccess) return set_error(err, n, "CUDA forward failed: %s", cudaGetErrorString(e));
+    s->stats.graph_replays++;
+    return 1;
+}
+
+// After a launched pass has completed: its kernels' error word.
+int finish_pass(FcSession *s, int rows, int drafts, char *err, size_t n) {
+    if (s->h_res->error) {
+        // a kernel that gave up may have left the router counter mid-count
+        cudaMemsetAsync(s->route_arrivals, 0, sizeof(int), s->stream);
+        cudaStreamSynchronize(s->stream);
+        return set_error(err, n, "a kernel wait gave up (error bits 0x%x); results are invalid",
+                         s->h_res->error);
+    }
+    s->stats.command_buffers++;
+    s->last_rows = rows;
+    s->last_drafts = drafts;
+    return 1;
+}
+
 // Runs the pass whose parameters are in h_stage: the captured graph for
 // (rows, drafts), or an eager profiled pass.
 int exec_pass(FcSession *s, int rows, int drafts, char *err, size_t n) {
@@ -1407,17 +1445,16 @@ __global__ void synth_kv_range_kernel(__half *cache, PageMap pm, int seq, int st
     }
 }
 
-// One device pass of the batch verify: sequences seqs[0 .. ng) with their
-// rows ids[j * group_rows ..] at their own positions; no drafter.
-int run_batch_pass(FcSession *s, const int *seqs, int ng, const int *ids, int k, const FcAcceptConfig *accept,
-                   char *err, size_t n) {
-    if (s->m->world > 1 && !s->ep_connected)
-        return set_error(err, n, "expert-parallel session is not connected (fc_session_ep_connect)");
+// Stages one device pass of the batch verify in s->h_stage: sequences
+// seqs[0 .. ng) at positions seq_pos[...] with their rows
+// ids[j * group_rows ..]; no drafter.
+void stage_batch_pass(FcSession *s, const std::vector<int> &seq_pos, const int *seqs, int ng, const int *ids,
+                      int k, const FcAcceptConfig *accept) {
     const int gr = s->group_rows, rows = ng * gr;
     Staging *st = s->h_stage;
     memset(st, 0, sizeof(*st));
     const FcAcceptConfig *a0 = accept ? &accept[seqs[0]] : nullptr;
-    st->pos = s->seq_pos[seqs[0]];
+    st->pos = seq_pos[seqs[0]];
     st->rows = rows;
     st->k = k;
     st->mode = a0 ? a0->mode : FC_ACCEPT_GREEDY;
@@ -1430,12 +1467,20 @@ int run_batch_pass(FcSession *s, const int *seqs, int ng, const int *ids, int k,
         st->gcounter[j] = accept ? accept[q].counter : 0;
         for (int i = 0; i < gr; ++i) {
             st->ids[j * gr + i] = ids[j * gr + i];
-            st->rowpos[j * gr + i] = s->seq_pos[q] + i;
+            st->rowpos[j * gr + i] = seq_pos[q] + i;
             st->rowseq[j * gr + i] = q;
         }
     }
     st->counter = st->gcounter[0];
-    return exec_pass(s, rows, 0, err, n);
+}
+
+// One device pass of the batch verify (see stage_batch_pass), run to completion.
+int run_batch_pass(FcSession *s, const int *seqs, int ng, const int *ids, int k, const FcAcceptConfig *accept,
+                   char *err, size_t n) {
+    if (s->m->world > 1 && !s->ep_connected)
+        return set_error(err, n, "expert-parallel session is not connected (fc_session_ep_connect)");
+    stage_batch_pass(s, s->seq_pos, seqs, ng, ids, k, accept);
+    return exec_pass(s, ng * s->group_rows, 0, err, n);
 }
 
 int check_ids(const FcSession *s, const int *ids, int count, char *err, size_t n) {
@@ -1907,7 +1952,7 @@ int build_page_table(int context_size, int sequences, int shared_rows, int *tabl
 // Session construction; `batch` (nullable) makes a multi-sequence session
 // whose passes hold whole sequences of batch->rows_per_sequence rows.
 int create_session(FcSession **out, FcModel *m, const FcOptions *options, const FcBatchOptions *batch,
-                   char *error, size_t error_size) {
+                   char *error, size_t error_size, FcSession *share = nullptr) {
     if (!out || !m || !options)
         return set_error(error, error_size, "model and session options are required");
     *out = nullptr;
@@ -1972,6 +2017,7 @@ int create_session(FcSession **out, FcModel *m, const FcOptions *options, const 
     s->attn_smem = AttnSmem::total(L + R);
     bool ok = cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking) == cudaSuccess;
     ok = ok && cudaEventCreate(&s->ev_begin) == cudaSuccess && cudaEventCreate(&s->ev_end) == cudaSuccess;
+    ok = ok && cudaEventCreateWithFlags(&s->ev_lane, cudaEventDisableTiming) == cudaSuccess;
     const int NLc = c.layer_count + c.mtp_layers;  // cache layers (target + drafter)
     {
         // page table: an ordinary session maps page p to itself; a batch
@@ -1981,10 +2027,16 @@ int create_session(FcSession **out, FcModel *m, const FcOptions *options, const 
         std::vector<int> table((size_t)s->n_seq * pps);
         const int pages = build_page_table(options->context_size, s->n_seq, s->shared_rows, table.data());
         s->layer_rows = batch ? pages * kPageRows : options->context_size;
-        ok = ok && salloc(s, s->cache, (size_t)NLc * s->layer_rows * (L + R));
-        ok = ok && salloc(s, s->page_table, table.size()) &&
-             cudaMemcpy(s->page_table, table.data(), table.size() * sizeof(int), cudaMemcpyHostToDevice) ==
-                 cudaSuccess;
+        if (share) {  // a lane: the parent's cache and page table
+            s->lane = true;
+            s->cache = share->cache;
+            s->page_table = share->page_table;
+        } else {
+            ok = ok && salloc(s, s->cache, (size_t)NLc * s->layer_rows * (L + R));
+            ok = ok && salloc(s, s->page_table, table.size()) &&
+                 cudaMemcpy(s->page_table, table.data(), table.size() * sizeof(int), cudaMemcpyHostToDevice) ==
+                     cudaSuccess;
+        }
         s->pmap.pt = s->page_table;
         s->pmap.pps = pps;
     }
@@ -2139,12 +2191,34 @@ int fc_session_create_batch(FcSession **out, FcModel *m, const FcBatchOptions *o
     FcOptions o{};
     o.context_size = b.context_size;
     o.max_batch = std::min(b.sequences, kMaxRows / b.rows_per_sequence) * b.rows_per_sequence;
-    return create_session(out, m, &o, &b, error, error_size);
+    if (!create_session(out, m, &o, &b, error, error_size)) return 0;
+    // one lane per pass of a batch step (at most kMaxLanes) on a single
+    // GPU; FLOYD_BATCH_LANES=n caps it (1: the passes run one at a time)
+    FcSession *s = *out;
+    const int per_pass = o.max_batch / b.rows_per_sequence;
+    int nl = std::min((b.sequences + per_pass - 1) / per_pass, kMaxLanes);
+    if (const char *env = getenv("FLOYD_BATCH_LANES")) nl = std::max(1, std::min(nl, atoi(env)));
+    if (m->world > 1) nl = 1;  // the expert exchange buffers belong to one session
+    for (int i = 1; i < nl; ++i) {
+        FcSession *c = nullptr;
+        if (!create_session(&c, m, &o, &b, error, error_size, s)) {
+            fc_session_destroy(s);
+            *out = nullptr;
+            return 0;
+        }
+        s->lanes.push_back(c);
+    }
+    return 1;
 }
 
 void fc_session_destroy(FcSession *s) {
     if (!s) return;
     cudaSetDevice(s->m->device);
+    for (FcSession *c : s->lanes) {
+        free_session_buffers(c);
+        delete c;
+    }
+    s->lanes.clear();
     free_session_buffers(s);
     delete s;
 }
@@ -2285,20 +2359,70 @@ int fc_session_verify_batch(FcSession *s, const int *ids, int k, const FcAcceptC
     if (!check_ids(s, ids, nseq * gr, error, error_size)) return 0;
     double t0 = now_ms();
     const int per_pass = s->rows_max / gr;
-    int seqs[kMaxRows];
-    for (int q0 = 0; q0 < nseq; q0 += per_pass) {
-        const int ng = std::min(per_pass, nseq - q0);
-        for (int j = 0; j < ng; ++j) seqs[j] = q0 + j;
-        if (!run_batch_pass(s, seqs, ng, ids + (size_t)q0 * gr, k, accept, error, error_size)) return 0;
-        const Result &r = *s->h_res;
-        for (int j = 0; j < ng; ++j) {
-            const int q = q0 + j, commit = r.g_commit[j];
-            if (commit < 1 || commit > gr)
-                return set_error(error, error_size, "sequence %d: verify produced commit %d", q, commit);
-            n_emitted[q] = commit;
-            next_token[q] = r.g_next[j];
-            s->seq_pos[q] += commit;  // rows past the commit are overwritten later
-            s->stats.accepted_tokens += (uint64_t)commit;
+    // passes run in waves of one pass per lane (the session itself is lane
+    // 0); eager profiled and traced passes run one at a time
+    const int nl = (s->profiling || s->trace) ? 1 : 1 + (int)s->lanes.size();
+    auto lane = [&](int w) { return w == 0 ? s : s->lanes[w - 1]; };
+    int seqs[kMaxLanes][kMaxRows], ngs[kMaxLanes];
+    for (int q0 = 0; q0 < nseq; q0 += per_pass * nl) {
+        int nw = 0;
+        for (; nw < nl && q0 + nw * per_pass < nseq; ++nw) {
+            const int qa = q0 + nw * per_pass;
+            ngs[nw] = std::min(per_pass, nseq - qa);
+            for (int j = 0; j < ngs[nw]; ++j) seqs[nw][j] = qa + j;
+        }
+        s->last_lane = nullptr;
+        if (nw == 1) {
+            if (!run_batch_pass(s, seqs[0], ngs[0], ids + (size_t)q0 * gr, k, accept, error, error_size)) return 0;
+        } else {
+            // every pass of the wave is staged and its graph recorded before
+            // any is launched; the lanes start after an event on the
+            // session's stream and the session's stream waits for all of
+            // them, so the events around the wave time all its passes
+            for (int w = 0; w < nw; ++w) {
+                FcSession *L = lane(w);
+                stage_batch_pass(L, s->seq_pos, seqs[w], ngs[w], ids + (size_t)(q0 + w * per_pass) * gr, k, accept);
+                if (!get_graph(L, ngs[w] * gr, 0, error, error_size)) return 0;
+            }
+            cudaSetDevice(s->m->device);
+            cudaEventRecord(s->ev_begin, s->stream);
+            for (int w = 0; w < nw; ++w) {
+                FcSession *L = lane(w);
+                if (w > 0) cudaStreamWaitEvent(L->stream, s->ev_begin, 0);
+                if (!launch_pass(L, ngs[w] * gr, 0, error, error_size)) {
+                    cudaDeviceSynchronize();
+                    return 0;
+                }
+                if (w > 0) {
+                    cudaEventRecord(L->ev_lane, L->stream);
+                    cudaStreamWaitEvent(s->stream, L->ev_lane, 0);
+                }
+            }
+            cudaEventRecord(s->ev_end, s->stream);
+            cudaError_t e = cudaStreamSynchronize(s->stream);
+            if (e != cudaSuccess) return set_error(error, error_size, "CUDA forward failed: %s", cudaGetErrorString(e));
+            float ms = 0.0f;
+            cudaEventElapsedTime(&ms, s->ev_begin, s->ev_end);
+            s->stats.gpu_ms += ms;
+            int kernels = 0;
+            for (int w = 0; w < nw; ++w) {
+                if (!finish_pass(lane(w), ngs[w] * gr, 0, error, error_size)) return 0;
+                kernels += lane(w)->last_kernels;
+            }
+            s->last_lane = lane(nw - 1);
+            s->last_kernels = kernels;  // every pass of the wave
+        }
+        for (int w = 0; w < nw; ++w) {
+            const Result &r = *lane(w)->h_res;
+            for (int j = 0; j < ngs[w]; ++j) {
+                const int q = seqs[w][j], commit = r.g_commit[j];
+                if (commit < 1 || commit > gr)
+                    return set_error(error, error_size, "sequence %d: verify produced commit %d", q, commit);
+                n_emitted[q] = commit;
+                next_token[q] = r.g_next[j];
+                s->seq_pos[q] += commit;  // rows past the commit are overwritten later
+                s->stats.accepted_tokens += (uint64_t)commit;
+            }
         }
     }
     s->stats.verify_calls++;
@@ -2360,6 +2484,7 @@ int fc_session_rollback(FcSession *s, int position, char *error, size_t error_si
 }
 
 int fc_session_copy_row_logits(const FcSession *s, float *logits, int capacity_rows) {
+    if (s && s->last_lane) s = s->last_lane;  // a batch step's last pass ran on a lane
     if (!s || !logits || capacity_rows < s->last_rows || s->last_rows <= 0) return 0;
     return cudaMemcpy(logits, s->logits, (size_t)s->last_rows * s->m->c.vocab_size * 4,
                       cudaMemcpyDeviceToHost) == cudaSuccess;

@@ -280,8 +280,9 @@ int fc_session_verify(FcSession *session, const int *ids, int k,
 int fc_session_rollback(FcSession *session, int position,
                         char *error, size_t error_size);
 
-/* Copies the logits of every row of the last forward ([rows][vocab]); the
- * Metal backend keeps only the last row (moonlight_metal.m:708-725). */
+/* Copies the logits of every row of the last forward ([rows][vocab]; for a
+ * batch session, the last pass of the last verify); the Metal backend keeps
+ * only the last row (moonlight_metal.m:708-725). */
 int fc_session_copy_row_logits(const FcSession *session, float *logits,
                                int capacity_rows);
 
@@ -301,7 +302,10 @@ int fc_session_seed_context(FcSession *session, int positions, uint64_t seed,
  * context.  fc_session_verify_batch runs one verify of 1 + k rows for every
  * sequence, packing floor(8 / (1 + k)) sequences into each device pass so
  * that they share the weight reads, and accepts and rolls back each sequence
- * on its own.  Each sequence gets the same result as the same verify in a
+ * on its own.  On one GPU the passes of a verify run concurrently, up to 4
+ * at a time, each on its own stream and workspace over the shared cache
+ * (environment FLOYD_BATCH_LANES=n caps that at n; 1 runs them one at a
+ * time).  Each sequence gets the same result as the same verify in a
  * one-sequence session.  No reference counterpart: floyd verifies one
  * sequence at a time. */
 typedef struct {
@@ -344,7 +348,8 @@ int fc_session_batch_rollback(FcSession *session, int sequence, int position, ch
 int fc_session_drafts(const FcSession *session, int *drafts, int capacity);
 
 /* Kernels launched by the last forward pass (kernel nodes of its CUDA
- * graph; 0 for eager profiled passes).  No reference counterpart. */
+ * graph; 0 for eager profiled passes; for a batch session, every pass of
+ * the last wave of concurrent passes).  No reference counterpart. */
 int fc_session_last_kernel_count(const FcSession *session);
 
 /* Bytes of the two host<->device copies every forward pass makes: the

@@ -145,3 +145,28 @@ def test_batch_refuses_invalid_shapes():
         bs.verify_batch([[1, 2, 3, 4], [5, 6, 7, 8]])          # sequence 0 would write into the shared pages
     bs.seed(0, 32, 100, 9)
     bs.verify_batch([[1, 2, 3, 4], [5, 6, 7, 8]])
+
+
+def test_concurrent_passes_equal_sequential_passes(monkeypatch):
+    """The passes of a batch step run concurrently on lanes (own stream and
+    workspace over the shared cache); the results and the last pass's logits
+    equal those of the same steps run one pass at a time, bit for bit."""
+    import floyd_b200
+    name, cfg = CASES[2]
+    gm, _ = pair(cfg, name)
+    rows, n = 4, 3
+    out = []
+    for lanes in ("1", "4"):
+        monkeypatch.setenv("FLOYD_BATCH_LANES", lanes)
+        bs = floyd_b200.BatchSession(gm, CTX, n, rows, PREFIX)
+        _seed_batch(bs, n)
+        steps = []
+        for step in range(3):
+            ids = [_ids(cfg, 10 * step + q, rows) for q in range(n)]
+            got_n, got_next = bs.verify_batch(ids)
+            steps.append((list(got_n), list(got_next), [bs.position_of(q) for q in range(n)],
+                          bs.row_logits(rows).copy()))
+        out.append(steps)
+    for a, b in zip(*out):
+        assert a[:3] == b[:3]
+        assert np.array_equal(a[3], b[3])
