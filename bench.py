@@ -55,6 +55,9 @@ def parse():
     ap.add_argument("--batch-steps", type=int, default=10,
                     help="configs[4] leg: timed batched verify steps per acceptance rate (0 = skip)")
     ap.add_argument("--batch-warmup", type=int, default=2)
+    ap.add_argument("--batch-sharding", default="sequences", choices=["sequences", "experts"],
+                    help="configs[4] leg at N > 1: each rank a full model with its own 8 sequences "
+                         "(weak scaling, no data-path collective), or one batch over the expert-split model")
     ap.add_argument("--decode-steps", type=int, default=200,
                     help="configs[1] leg: timed greedy decodes of the Moonlight q8 model (0 = skip)")
     ap.add_argument("--prefill-layers", type=int, default=None,
@@ -594,20 +597,26 @@ def decode_leg(args, d):
     return out
 
 
-def batch_leg(args, d, model, cfg):
+def batch_leg(args, d, model, cfg, replica=False):
     """configs[4] on the C4 stand-in: 8 sequences verifying 1 + draft rows
     each in one batch session (floor(8 / rows) sequences per device pass),
     per-sequence context uniform in [1024, 16384] (seeded), the first 1024
     positions shared by all sequences (prefix pages), planted acceptance
-    p in {0.5, 0.7, 0.9} against each sequence's own greedy continuation."""
+    p in {0.5, 0.7, 0.9} against each sequence's own greedy continuation.
+    replica (N > 1, sequence sharding): `model` is this rank's full copy and
+    the rank verifies its own 8 sequences (contexts seeded by rank); the
+    reported throughput is all ranks' accepted tokens over the slowest
+    rank's device time."""
     import floyd_b200
     nseq, rows, prefix = 8, args.draft + 1, 1024
     V = cfg["vocab_size"]
-    ctxs = np.random.default_rng(5).integers(prefix, 16384 + 1, size=nseq).tolist()
+    ctx_seed = 5 + (1000 * d.rank if replica else 0)
+    ctxs = np.random.default_rng(ctx_seed).integers(prefix, 16384 + 1, size=nseq).tolist()
     n_rounds = args.batch_warmup + args.batch_steps
     gen = rows * n_rounds + 2
     bs = floyd_b200.BatchSession(model, 16384 + gen + 8, nseq, rows, prefix)
-    if d.world > 1:
+    ep = d.world > 1 and not replica
+    if ep:
         bs.ep_connect(d.all_gather_bytes(bs.ep_handle()))
         d.barrier()
     bs.seed(0, 0, prefix, 7)
@@ -653,19 +662,24 @@ def batch_leg(args, d, model, cfg):
             if r >= args.batch_warmup:
                 wall += dt
         g = d.max(bs.stats()["gpu_ms"] - g0)
-        xw = d.max(bs.exchange_wait_ms()) / args.batch_steps if d.world > 1 else 0.0
-        results.append({"accept_p": p, "value": emitted / (g / 1e3), "unit": "accepted tok/s (all sequences)",
-                        "e2e": emitted / d.max(wall), "ms_per_step": g / args.batch_steps,
+        xw = d.max(bs.exchange_wait_ms()) / args.batch_steps if ep else 0.0
+        total = d.sum(emitted) if replica else emitted  # replicas: every rank's sequences
+        nall = nseq * (d.world if replica else 1)
+        results.append({"accept_p": p, "value": total / (g / 1e3), "unit": "accepted tok/s (all sequences)",
+                        "e2e": total / d.max(wall), "ms_per_step": g / args.batch_steps,
                         "exchange_exposed_ms_per_step": xw,
-                        "mean_commit_per_sequence": emitted / (args.batch_steps * nseq),
+                        "mean_commit_per_sequence": total / (args.batch_steps * nall),
                         "acceptance_mismatches": int(d.sum(mismatches))})
     bs.close()
-    return {"workload": "c5_batched_verify", "sequences": nseq, "rows_per_sequence": rows,
+    shard = ("sequences: a full model and 8 sequences per rank, no data-path collective (weak scaling)"
+             if replica else ("experts: one batch over the expert-split model" if d.world > 1 else None))
+    return {"workload": "c5_batched_verify", "sequences": nseq * (d.world if replica else 1),
+            "sequences_per_rank": nseq if replica else None, "sharding": shard, "rows_per_sequence": rows,
             "sequences_per_pass": 8 // rows, "shared_prefix": prefix, "contexts": ctxs,
             "steps": args.batch_steps, "warmup": args.batch_warmup, "n_gpus": d.world,
             "results": results,
             "exchange_exposed_ms": (float(np.mean([r["exchange_exposed_ms_per_step"] for r in results]))
-                                    if d.world > 1 else None),
+                                    if ep else None),
             "note": ("one batch step = one verify of every sequence; device time of the graph replays "
                      "(max over ranks); the expert exchange (N > 1) is fused into the down-projection "
                      "epilogue (NVLink stores) and the combine's flag wait; exchange_exposed_ms is the "
@@ -862,7 +876,16 @@ def run_ours(args, d):
             out["cpu_baseline"] = {"error": str(exc)}
     sess.close()
     if args.batch_steps > 0:
-        out["batch_verify"] = batch_leg(args, d, model, cfg)
+        if d.world > 1 and args.batch_sharding == "sequences":
+            # sequence sharding: the expert-split model gives way to a full
+            # copy on every rank (the C4 stand-in fits one B200)
+            model.close()
+            d.barrier()
+            rmodel = floyd_b200.Model(cfg, device=d.local, seed=0)
+            out["batch_verify"] = batch_leg(args, d, rmodel, cfg, replica=True)
+            rmodel.close()
+        else:
+            out["batch_verify"] = batch_leg(args, d, model, cfg)
     model.close()
     return out
 
