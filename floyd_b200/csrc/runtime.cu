@@ -133,6 +133,10 @@ struct FcSession {
     bool batch = false;      // created by fc_session_create_batch
     int max_slots = 0;
     int splits = 0, chunks_per_split = 1;
+    // split plan of the drafter (MTP) layers: they always run one row per
+    // pass against their own cache, so with the tcgen05 kernel they take
+    // enough splits to fill the SMs with one query tile
+    int mtp_splits = 0, mtp_chunks_per_split = 1;
     bool attn_tc = true;     // tcgen05 attention (else the mma.sync kernel)
     CUtensorMap qmap{}, kvmap{};  // TMA maps of qcat and of the latent cache
     int head_chunks = 0;
@@ -691,9 +695,12 @@ cudaError_t record_attention(FcSession *s, int S, int l, const Staging *dst, int
                           y.kv_b.kp, VD));
         mark(s, "mla_prep_absorb");
     }
+    const bool mtp_layer = l >= c.layer_count;
+    const int nsplit = mtp_layer ? s->mtp_splits : s->splits;
     if (s->attn_tc) {
-        dim3 grid((S * H + kTcRows - 1) / kTcRows, 2, s->splits);
-        const int kv_row0 = l * s->layer_rows, kps = s->chunks_per_split * kAttnKeys;
+        dim3 grid((S * H + kTcRows - 1) / kTcRows, 2, nsplit);
+        const int kv_row0 = l * s->layer_rows,
+                  kps = (mtp_layer ? s->mtp_chunks_per_split : s->chunks_per_split) * kAttnKeys;
         if (L == 512)
             FC_TRY(launch_pdl(mla_attention_tc_kernel<512>, grid, dim3(kTcThreads), TcAttnPlan<512>::SMEM, st,
                               s->qmap, s->kvmap, kv_row0, S, H, kps, dst, s->pmap, scale, s->part_o, s->part_m,
@@ -719,7 +726,7 @@ cudaError_t record_attention(FcSession *s, int S, int l, const Staging *dst, int
         size_t head_stride = (size_t)mb * kpL * 2;
         FC_TRY(launch_pdl(mla_combine_kernel, dim3(S * H, (L + kCombineThreads - 1) / kCombineThreads),
                           dim3(kCombineThreads), 0, st, (const float *)s->part_o,
-                          (const float *)s->part_m, (const float *)s->part_l, s->splits, S, H, L,
+                          (const float *)s->part_m, (const float *)s->part_l, nsplit, S, H, L,
                           s->attn_tc ? L / 2 : L, s->ctx_xq, head_stride));
         mark(s, "mla_combine");
         // W_UV: rows nope .. nope+v of each head's kv_b block (decode_value, :345-375)
@@ -2013,6 +2020,15 @@ int create_session(FcSession **out, FcModel *m, const FcOptions *options, const 
     }
     s->chunks_per_split = (max_chunks + target - 1) / target;
     s->splits = (max_chunks + s->chunks_per_split - 1) / s->chunks_per_split;
+    s->mtp_chunks_per_split = s->chunks_per_split;
+    s->mtp_splits = s->splits;
+    if (s->attn_tc) {
+        const int qt1 = (H + kTcRows - 1) / kTcRows;  // one row's query tiles
+        const int t1 = std::max(1, std::min(64, 148 / (2 * qt1)));
+        s->mtp_chunks_per_split = (max_chunks + t1 - 1) / t1;
+        s->mtp_splits = (max_chunks + s->mtp_chunks_per_split - 1) / s->mtp_chunks_per_split;
+    }
+    const int part_splits = std::max(s->splits, s->mtp_splits);  // split partial buffers hold either plan
     s->head_chunks = (V + kHeadChunk - 1) / kHeadChunk;
     s->attn_smem = AttnSmem::total(L + R);
     bool ok = cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking) == cudaSuccess;
@@ -2049,9 +2065,9 @@ int create_session(FcSession **out, FcModel *m, const FcOptions *options, const 
     // rows padded to whole 128-query tiles (the TMA box of the query tile)
     const int q_rows = (mb * H + kTcRows - 1) / kTcRows * kTcRows;
     ok = ok && salloc(s, s->qcat, (size_t)q_rows * (L + R));
-    ok = ok && salloc(s, s->part_o, (size_t)s->splits * mb * H * L);
-    ok = ok && salloc(s, s->part_m, (size_t)2 * s->splits * mb * H);  // [half][split][row] (tcgen05 attention)
-    ok = ok && salloc(s, s->part_l, (size_t)2 * s->splits * mb * H);
+    ok = ok && salloc(s, s->part_o, (size_t)part_splits * mb * H * L);
+    ok = ok && salloc(s, s->part_m, (size_t)2 * part_splits * mb * H);  // [half][split][row] (tcgen05 attention)
+    ok = ok && salloc(s, s->part_l, (size_t)2 * part_splits * mb * H);
     ok = ok && salloc(s, s->ctx_xq, (size_t)H * mb * kpad(L) * 2);
     ok = ok && salloc(s, s->o_xq, (size_t)mb * kpad(H * c.value_dim) * 2);
     ok = ok && salloc(s, s->router_logits, (size_t)2 * mb * E);  // scores, then choices
