@@ -910,13 +910,27 @@ __global__ void __launch_bounds__(256) pf_router_logits_kernel(const float *W, c
     const int kb = sp * ksplit, ke = min(D, kb + ksplit);
     const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
     float acc[4][4] = {};
+    // the next k-tile is loaded into registers while this one is multiplied
+    constexpr int kPer = kPfRtTile * kPfRtK / 256;  // elements per thread per tile
+    float xr[kPer], wr[kPer];
+    auto load = [&](int k0) {
+#pragma unroll
+        for (int j = 0; j < kPer; ++j) {
+            const int i = threadIdx.x + j * 256, r = i / kPfRtK, k = i % kPfRtK;
+            xr[j] = t0 + r < T ? x[(size_t)(t0 + r) * D + k0 + k] : 0.0f;
+            wr[j] = e0 + r < E ? W[(size_t)(e0 + r) * D + k0 + k] : 0.0f;
+        }
+    };
+    if (kb < ke) load(kb);
     for (int k0 = kb; k0 < ke; k0 += kPfRtK) {
-        for (int i = threadIdx.x; i < kPfRtTile * kPfRtK; i += 256) {
-            const int r = i / kPfRtK, k = i % kPfRtK;
-            xs[k][r] = t0 + r < T ? x[(size_t)(t0 + r) * D + k0 + k] : 0.0f;
-            ws[k][r] = e0 + r < E ? W[(size_t)(e0 + r) * D + k0 + k] : 0.0f;
+#pragma unroll
+        for (int j = 0; j < kPer; ++j) {
+            const int i = threadIdx.x + j * 256, r = i / kPfRtK, k = i % kPfRtK;
+            xs[k][r] = xr[j];
+            ws[k][r] = wr[j];
         }
         __syncthreads();
+        if (k0 + kPfRtK < ke) load(k0 + kPfRtK);
 #pragma unroll 8
         for (int k = 0; k < kPfRtK; ++k) {
             const float4 xv = *reinterpret_cast<const float4 *>(&xs[k][ty * 4]);
