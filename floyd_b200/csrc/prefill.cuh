@@ -557,7 +557,7 @@ pf_gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__
 //               rescale as in mla_attention_tc_kernel), P to shared memory;
 //               at the end O / l as fp16 into o16[t][h * value_dim ..].
 // ---------------------------------------------------------------------------
-constexpr int kFaRows = 128, kFaKeys = 64, kFaStages = 3, kFaThreads = 256;
+constexpr int kFaRows = 128, kFaKeys = 128, kFaStages = 2, kFaThreads = 256;
 
 template <int NQS, int NVS>  // 64-column slices of q.k (nope + rope) and of v
 struct FaPlan {
@@ -565,13 +565,14 @@ struct FaPlan {
     static constexpr int K_BYTES = NQS * kFaKeys * 128;
     static constexpr int V_BYTES = NVS * kFaKeys * 128;
     static constexpr int STAGE = K_BYTES + V_BYTES;
-    static constexpr int P_BYTES = kFaRows * kFaKeys * 2;
     static constexpr int OFF_KV = Q_BYTES;
-    static constexpr int OFF_P = OFF_KV + kFaStages * STAGE;
-    static constexpr int OFF_BAR = OFF_P + P_BYTES;
+    static constexpr int OFF_BAR = OFF_KV + kFaStages * STAGE;
     static constexpr size_t SMEM = (size_t)OFF_BAR + 256 + 1024;
     static constexpr int DV = NVS * 64;
-    static constexpr uint32_t TMEM_COLS = DV + 2 * kFaKeys <= 256 ? 256 : 512;
+    // TMEM: O (DV columns), two score buffers, P (fp16 pairs: kFaKeys / 2)
+    static constexpr uint32_t T_P = DV + 2 * kFaKeys;
+    static constexpr uint32_t TMEM_COLS = T_P + kFaKeys / 2 <= 256 ? 256 : 512;
+    static_assert(T_P + kFaKeys / 2 <= 512, "TMEM plan");
     static_assert(SMEM <= 232448, "shared memory plan");
 };
 
@@ -588,7 +589,7 @@ pf_attention_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_const
     constexpr int NP = (NQS - 1) * 64, DV = P::DV;
     extern __shared__ uint8_t fa_smem_raw[];
     uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(fa_smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t *Qs = sm, *KVs = sm + P::OFF_KV, *Ps = sm + P::OFF_P;
+    uint8_t *Qs = sm, *KVs = sm + P::OFF_KV;
     uint64_t *bars = reinterpret_cast<uint64_t *>(sm + P::OFF_BAR);
     uint64_t *q_full = bars, *kv_full = bars + 1, *kv_empty = kv_full + kFaStages, *s_full = kv_empty + kFaStages,
              *s_free = s_full + 2, *p_full = s_free + 2, *pv_done = p_full + 1;
@@ -630,7 +631,7 @@ pf_attention_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_const
     const int pos = *d_pos;
     const int nkeys = pos + min(t0 + kFaRows, T);   // keys visible to the tile's last row
     const int nblk = (nkeys + kFaKeys - 1) / kFaKeys;
-    const uint32_t tO = tmem, tS = tmem + DV;
+    const uint32_t tO = tmem, tS = tmem + DV, tP = tmem + P::T_P;
 
     if (warp == 0) {
         if (lane == 0) {
@@ -658,7 +659,7 @@ pf_attention_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_const
         if (lane == 0) {
             constexpr uint32_t idS = idesc_f16(kFaRows, kFaKeys, false);
             constexpr uint32_t idO = idesc_f16(kFaRows, DV, true);
-            const uint32_t qa = smem_u32(Qs), kva = smem_u32(KVs), pa = smem_u32(Ps);
+            const uint32_t qa = smem_u32(Qs), kva = smem_u32(KVs);
             mbar_wait_timed(q_full, 0, err, 0);
             auto issue_scores = [&](int j) {
                 const uint32_t kst = kva + (j % kFaStages) * P::STAGE;
@@ -698,11 +699,10 @@ pf_attention_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_const
                 const uint32_t vst = kva + (j % kFaStages) * P::STAGE + P::K_BYTES;
 #pragma unroll
                 for (int kk = 0; kk < kFaKeys / 16; ++kk) {
-                    // P: K-major core matrices, K-adjacent 128 B apart, 8-row groups kFaKeys * 16 B apart
-                    uint64_t a = smem_desc(pa + kk * 256, 128, kFaKeys * 16, kSmemLayoutNone);
+                    // P from TMEM (one query row per lane, 16 keys = 8 columns per step);
                     // V: MN-major 128-byte swizzle, 64-column slices kFaKeys * 128 B apart
                     uint64_t b = smem_desc(vst + kk * 2048, kFaKeys * 128, 1024, kSmemLayoutSw128);
-                    tc_mma_f16(tO, a, b, idO, (j | kk) != 0);
+                    tc_mma_f16_ta(tO, tP + kk * 8, b, idO, (j | kk) != 0);
                 }
                 tc_commit(&kv_empty[j % kFaStages]);
                 tc_commit(pv_done);
@@ -720,34 +720,32 @@ pf_attention_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_const
             mbar_wait_timed(&s_full[st], (uint32_t)((j >> 1) & 1), err, 5);
             __syncwarp();
             tc_fence_after();
-            float sv[kFaKeys];
-            tmem_ld32(tS + st * kFaKeys + lane_off, *reinterpret_cast<float(*)[32]>(sv));
-            tmem_ld32(tS + st * kFaKeys + 32 + lane_off, *reinterpret_cast<float(*)[32]>(sv + 32));
-            tmem_wait_ld();
-            tc_fence_before();
-            mbar_arrive_cta(&s_free[st]);
+            // pass 1: the block max; a block with every key visible (all but
+            // the diagonal one) skips the mask; scaling after the max is
+            // exact (scale2 > 0)
             const int nvis = min(max(limit - j * kFaKeys + 1, 0), kFaKeys);
+            const uint32_t ts = tS + st * kFaKeys + lane_off;
+            const bool full = nvis == kFaKeys;
             float mb = -INFINITY;
+#pragma unroll 1
+            for (int c0 = 0; c0 < kFaKeys; c0 += 32) {
+                float sv[32];
+                tmem_ld32(ts + c0, sv);
+                tmem_wait_ld();
+                if (full) {
 #pragma unroll
-            for (int c = 0; c < kFaKeys; ++c) {
-                float v = c < nvis ? sv[c] * scale2 : -INFINITY;
-                sv[c] = v;
-                mb = fmaxf(mb, v);
+                    for (int c = 0; c < 32; ++c) mb = fmaxf(mb, sv[c]);
+                } else {
+#pragma unroll
+                    for (int c = 0; c < 32; ++c) mb = fmaxf(mb, c0 + c < nvis ? sv[c] : -INFINITY);
+                }
             }
+            mb = mb == -INFINITY ? mb : mb * scale2;
             const float m_new = (m_run == -INFINITY || mb > m_run + kRescaleLog2) ? mb : m_run;
             const float alpha = m_new == m_run ? 1.0f : exp2f(m_run - m_new);
             const float msub = m_new == -INFINITY ? 0.0f : m_new;
-            float ps = 0.0f;
-            uint32_t packed[kFaKeys / 2];
-#pragma unroll
-            for (int c = 0; c < kFaKeys; c += 2) {
-                float p0 = exp2f(sv[c] - msub);
-                float p1 = exp2f(sv[c + 1] - msub);
-                ps += p0;
-                ps += p1;
-                __half2 hp = __floats2half2_rn(p0, p1);
-                packed[c / 2] = *reinterpret_cast<uint32_t *>(&hp);
-            }
+            // the previous block's P . V must be done before P is rewritten
+            // and before O is rescaled
             if (j > 0) {
                 mbar_wait_timed(pv_done, (uint32_t)((j - 1) & 1), err, 6);
                 __syncwarp();
@@ -765,13 +763,40 @@ pf_attention_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_const
                 }
                 tmem_wait_st();
             }
-            uint8_t *prow = Ps + (row >> 3) * (kFaKeys * 16) + (row & 7) * 16;
+            // pass 2: P = 2^(s - m) as fp16 pairs into TMEM, 32 keys at a time
+            float ps = 0.0f;
+#pragma unroll 1
+            for (int c0 = 0; c0 < kFaKeys; c0 += 32) {
+                float sv[32];
+                tmem_ld32(ts + c0, sv);
+                tmem_wait_ld();
+                uint32_t packed[16];
+                if (full) {
 #pragma unroll
-            for (int c = 0; c < kFaKeys / 8; ++c)
-                *reinterpret_cast<uint4 *>(prow + c * 128) =
-                    make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2], packed[4 * c + 3]);
-            fence_async_smem();
+                    for (int c = 0; c < 32; c += 2) {
+                        float p0 = exp2f(fmaf(sv[c], scale2, -msub));
+                        float p1 = exp2f(fmaf(sv[c + 1], scale2, -msub));
+                        ps += p0;
+                        ps += p1;
+                        __half2 hp = __floats2half2_rn(p0, p1);
+                        packed[c / 2] = *reinterpret_cast<uint32_t *>(&hp);
+                    }
+                } else {
+#pragma unroll
+                    for (int c = 0; c < 32; c += 2) {
+                        float p0 = c0 + c < nvis ? exp2f(fmaf(sv[c], scale2, -msub)) : 0.0f;
+                        float p1 = c0 + c + 1 < nvis ? exp2f(fmaf(sv[c + 1], scale2, -msub)) : 0.0f;
+                        ps += p0;
+                        ps += p1;
+                        __half2 hp = __floats2half2_rn(p0, p1);
+                        packed[c / 2] = *reinterpret_cast<uint32_t *>(&hp);
+                    }
+                }
+                tmem_st16(tP + c0 / 2 + lane_off, packed);
+            }
+            tmem_wait_st();
             tc_fence_before();
+            mbar_arrive_cta(&s_free[st]);
             mbar_arrive_cta(p_full);
             l_run = l_run * alpha + ps;
             m_run = m_new;
