@@ -90,7 +90,7 @@ int fc_test_embed(FcSession *s, const int *ids, int count, float *output) {
     if (!d_ids || !d_x) return 0;
     cudaError_t e = cudaMemcpyAsync(d_ids, ids, (size_t)count * 4, cudaMemcpyHostToDevice, s->stream);
     if (e == cudaSuccess)
-        e = launch_pdl(embed_kernel, dim3(count), dim3(256), 0, s->stream, m->embed.fmt,
+        e = launch_pdl(embed_kernel, embed_grid(count, D), dim3(kEmbedThreads), 0, s->stream, m->embed.fmt,
                        (const uint8_t *)m->embed.w, D, m->embed.kp, (const int *)d_ids, d_x);
     if (e == cudaSuccess)
         e = cudaMemcpyAsync(output, d_x, (size_t)count * D * 4, cudaMemcpyDeviceToHost, s->stream);

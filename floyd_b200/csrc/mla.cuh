@@ -42,14 +42,16 @@ __device__ __forceinline__ float dequant_element(int fmt, const uint8_t *w, int 
     return v * e8m0_to_float(*sp);
 }
 
+// grid (rows, ceil(D / 256)), 256 threads: one element per thread, so the
+// scattered weight and scale loads of a row are all in flight at once.
+constexpr int kEmbedThreads = 256;
 __global__ void embed_kernel(int fmt, const uint8_t *w, int D, int kp, const int *ids, float *x) {
     pdl_wait();
     pdl_release();
-    int s = blockIdx.x;
-    int row = ids[s];
-    for (int k = threadIdx.x; k < D; k += blockDim.x)
-        x[(size_t)s * D + k] = dequant_element(fmt, w, kp, row, k);
+    const int s = blockIdx.x, k = blockIdx.y * kEmbedThreads + threadIdx.x;
+    if (k < D) x[(size_t)s * D + k] = dequant_element(fmt, w, kp, ids[s], k);
 }
+inline dim3 embed_grid(int rows, int D) { return dim3(rows, (D + kEmbedThreads - 1) / kEmbedThreads); }
 
 // ---------------------------------------------------------------------------
 // RMSNorm (moonlight_kernels.metal:23-41): y = x / sqrt(mean(x^2) + eps) * w.

@@ -928,7 +928,7 @@ cudaError_t record_forward(FcSession *s, int S, int drafts) {
     const int D = c.hidden_size, kpD = kpad(D);
 
     FC_TRY(cudaMemcpyAsync(s->d_stage, s->h_stage, sizeof(Staging), cudaMemcpyHostToDevice, st));
-    FC_TRY(launch_pdl(embed_kernel, dim3(S), dim3(256), 0, st, m->embed.fmt, m->embed.w, D, m->embed.kp, s->d_stage->ids,
+    FC_TRY(launch_pdl(embed_kernel, embed_grid(S, D), dim3(kEmbedThreads), 0, st, m->embed.fmt, m->embed.w, D, m->embed.kp, s->d_stage->ids,
                                     s->resid));
     FC_TRY(cudaGetLastError());
     mark(s, "embed");
@@ -971,7 +971,7 @@ cudaError_t record_mtp_step(FcSession *s, int i) {
     FC_TRY(launch_pdl(mtp_prep_kernel, dim3((D + 255) / 256), dim3(256), 0, st, i, (const Staging *)s->d_stage,
                       (const Result *)s->d_res, s->d_mtp, (const float *)s->resid, s->mtp_h, D));
     mark(s, "mtp_prep");
-    FC_TRY(launch_pdl(embed_kernel, dim3(1), dim3(256), 0, st, m->embed.fmt, m->embed.w, D, m->embed.kp,
+    FC_TRY(launch_pdl(embed_kernel, embed_grid(1, D), dim3(kEmbedThreads), 0, st, m->embed.fmt, m->embed.w, D, m->embed.kp,
                       (const int *)s->d_mtp->ids, s->resid));
     FC_TRY(launch_pdl(rmsnorm_kernel, dim3(1), dim3(norm_threads(D)), 0, st, (const float *)s->resid, D,
                       (const float *)y.enorm.p, D, c.rms_norm_epsilon, s->mtp_xq, kp2, (float *)nullptr, 0));
@@ -1270,7 +1270,7 @@ cudaError_t record_prefill(FcSession *s, int T) {
     const int sms = m->sms;
     const float scale = 1.0f / sqrtf((float)(NP + R));
     const int *d_pos = s->pf_ids, *ids = s->pf_ids + 1;
-    FC_TRY(launch_pdl(embed_kernel, dim3(T), dim3(256), 0, st, m->embed.fmt, (const uint8_t *)m->embed.w, D,
+    FC_TRY(launch_pdl(embed_kernel, embed_grid(T, D), dim3(kEmbedThreads), 0, st, m->embed.fmt, (const uint8_t *)m->embed.w, D,
                       m->embed.kp, ids, s->pf_resid));
     mark(s, "pf_embed");
     for (int l = 0; l < c.layer_count; ++l) {
@@ -2759,7 +2759,7 @@ cudaError_t mtp_history_rows(FcSession *s, int p0, int r) {
     h->group_rows = r;
     h->groups = 1;
     FC_TRY(cudaMemcpyAsync(s->d_mtp, h, sizeof(Staging), cudaMemcpyHostToDevice, st));
-    FC_TRY(launch_pdl(embed_kernel, dim3(r), dim3(256), 0, st, m->embed.fmt, (const uint8_t *)m->embed.w, D,
+    FC_TRY(launch_pdl(embed_kernel, embed_grid(r, D), dim3(kEmbedThreads), 0, st, m->embed.fmt, (const uint8_t *)m->embed.w, D,
                       m->embed.kp, (const int *)s->d_mtp->ids, s->resid));
     FC_TRY(cudaMemsetAsync(s->mtp_xq, 0, (size_t)r * kp2 * 4, st));
     FC_TRY(launch_pdl(rmsnorm_kernel, dim3(r), dim3(norm_threads(D)), 0, st, (const float *)s->resid, D,
