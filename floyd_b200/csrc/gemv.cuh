@@ -107,8 +107,8 @@ struct GemvSeg {
     int64_t xq_stride;      // halves between members' inputs
     int out_stride;         // output columns between members
     int tiles;              // work items per member (set by the launcher)
-    int npeer;              // EPI_STORE copies into peer GPUs' buffers (expert parallel)
-    float *peer_y[7];       // same offsets as y, in each peer's receive buffer
+    int npeer;              // EPI_STORE / EPI_STORE_XQ copies into peer GPUs' buffers
+    float *peer_y[7];       // same offsets as y (or yq, as __half *) in each peer's buffer
 };
 
 constexpr int kMaxSegs = 6;
@@ -142,10 +142,47 @@ struct GemvWork {
     // releases its dependents at its start, so its successor may not assume
     // the same of the router.)
     int shared_first;
+    // cross-GPU hand-off (head-parallel attention), all nullable:
+    // publish - the last CTA to finish (done counter, zero between launches)
+    //   stores epoch + 1 into every peer's flag slot `rank` after the CTAs'
+    //   peer stores are fenced;
+    // wait - the producer waits (bounded, error bit 2) until every peer has
+    //   published this GPU's current epoch before copying activation rows
+    int *pub_done, *pub_epoch;
+    int *pub_flags[8];        // each peer's flag array, by peer rank (slot = this rank)
+    const int *wait_flags, *wait_epoch;
+    unsigned long long *wait_ns;
+    int peer_world, peer_rank;
 #ifdef FC_GEMV_TRACE
     int trace;
 #endif
 };
+
+__device__ __forceinline__ void gemv_peer_wait(const GemvWork &wk) {
+    if (!wk.wait_flags) return;
+    const int e = *wk.wait_epoch;
+    uint64_t t0 = 0, w0, w1;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(w0));
+    for (int r = 0; r < wk.peer_world; ++r) {
+        if (r == wk.peer_rank) continue;
+        for (uint32_t it = 0;; ++it) {
+            int v;
+            asm volatile("ld.acquire.sys.global.s32 %0, [%1];\n" : "=r"(v) : "l"(wk.wait_flags + r) : "memory");
+            if (v >= e) break;
+            if ((it & 255u) == 0) {
+                uint64_t t;
+                asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+                if (t0 == 0) t0 = t;
+                else if (t - t0 > 1000000000ull) {
+                    atomicOr(wk.err, 2);
+                    break;
+                }
+            }
+        }
+    }
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(w1));
+    if (wk.wait_ns && blockIdx.x == 0) atomicAdd(wk.wait_ns, (unsigned long long)(w1 - w0));
+}
 
 // A resolved work item.
 struct GemvItem {
@@ -418,6 +455,10 @@ __device__ __forceinline__ void gemv_epilogue(const GemvSeg &sg, const GemvItem 
         sg.y[it.out_shift + (size_t)s * sg.ldy + col] += v;
     } else {
         store_xq(sg.yq + it.out_shift, sg.kpy, s, sg.col_off + col, v);
+        // xq copies into peer GPUs' buffers (head-parallel attention: each
+        // rank's W_UV heads into every rank's o_proj input); NVLink stores
+        for (int p = 0; p < sg.npeer; ++p)
+            store_xq(reinterpret_cast<__half *>(sg.peer_y[p]) + it.out_shift, sg.kpy, s, sg.col_off + col, v);
     }
 }
 
@@ -556,6 +597,18 @@ __device__ __forceinline__ void gemv_consume(const GemvWork &wk, const uint8_t *
         consumer_sync();
         if (tid == 0) __threadfence_system();
     }
+    if (wk.pub_done && tid == 0) {
+        // the last CTA publishes the next epoch to every peer
+        if (atomicAdd(wk.pub_done, 1) == (int)gridDim.x - 1) {
+            *wk.pub_done = 0;
+            __threadfence_system();
+            const int e = *wk.pub_epoch + 1;
+            *wk.pub_epoch = e;
+            for (int r = 0; r < wk.peer_world; ++r)
+                if (r != wk.peer_rank)
+                    asm volatile("st.release.sys.global.s32 [%0], %1;\n" ::"l"(wk.pub_flags[r] + wk.peer_rank), "r"(e) : "memory");
+        }
+    }
 }
 
 template <int FA, int FB>
@@ -620,6 +673,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
                     // the ring is full: wait for the predecessor, then send
                     // the activation rows of the stages already in flight
                     pdl_wait();
+                    gemv_peer_wait(wk);
                     waited = true;
                     for (int p = 0; p < npend; ++p)
                         for (int r = 0; r < wk.S; ++r)
@@ -656,6 +710,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
         }
         if (kSmemB && !waited) {
             pdl_wait();
+            gemv_peer_wait(wk);
             for (int p = 0; p < npend; ++p)
                 for (int r = 0; r < wk.S; ++r)
                     bulk_g2s(smem + (size_t)pend[p].slot * kSlotBytes + 2 * kSlotW + (size_t)r * kBRow,
@@ -740,6 +795,7 @@ struct GemvBatch {
     int S;
     float swiglu_limit;
     int *err;
+    const GemvWork *sync;  // nullable: the cross-GPU hand-off fields (pub_*, wait_*, peer_*)
 };
 
 inline cudaError_t launch_gemv_batch(int fmt, GemvBatch &b, int sms, cudaStream_t stream) {
@@ -749,6 +805,16 @@ inline cudaError_t launch_gemv_batch(int fmt, GemvBatch &b, int sms, cudaStream_
     wk.S = b.S;
     wk.swiglu_limit = b.swiglu_limit;
     wk.err = b.err;
+    if (b.sync) {
+        wk.pub_done = b.sync->pub_done;
+        wk.pub_epoch = b.sync->pub_epoch;
+        for (int r = 0; r < 8; ++r) wk.pub_flags[r] = b.sync->pub_flags[r];
+        wk.wait_flags = b.sync->wait_flags;
+        wk.wait_epoch = b.sync->wait_epoch;
+        wk.wait_ns = b.sync->wait_ns;
+        wk.peer_world = b.sync->peer_world;
+        wk.peer_rank = b.sync->peer_rank;
+    }
     return launch_gemv_work(fmt, fmt, wk, sms, stream);
 }
 

@@ -175,6 +175,15 @@ struct FcSession {
     float *ep_xbuf = nullptr;
     int *ep_flags = nullptr, *ep_epoch = nullptr;
     unsigned long long *ep_wait_ns = nullptr;  // time the combines spent waiting for peers
+    // head-parallel attention (expert-parallel single-sequence sessions):
+    // this rank runs heads [head0, head0 + heads) of the MLA block; the W_UV
+    // outputs of every rank meet in each rank's o_proj input, two buffers
+    // (layer parity) in the receive region after the expert exchange
+    bool head_shard = false;
+    int head0 = 0, heads = 0;
+    size_t ep_attn_off = 0, ep_oxq_bytes = 0;  // byte offsets in the region: flags, then [2] o_proj inputs
+    int *ep_aepoch = nullptr;
+    int *ep_adone = nullptr;     // W_UV CTAs finished (zero between launches)
     void *ep_peer_region[kMaxRanks] = {};
     bool ep_connected = false;
     Staging *d_stage = nullptr, *h_stage = nullptr;
@@ -555,8 +564,10 @@ GemvSeg seg_of(const DevMat &mm, const __half *xq, int epi) {
         if (e_ != cudaSuccess) return e_;            \
     } while (0)
 
-cudaError_t gemv1(int fmt, GemvSeg a, int S, float limit, int *err, int sms, cudaStream_t st) {
+cudaError_t gemv1(int fmt, GemvSeg a, int S, float limit, int *err, int sms, cudaStream_t st,
+                  const GemvWork *sync = nullptr) {
     GemvBatch b{};
+    b.sync = sync;
     b.seg[0] = a;
     b.nseg = 1;
     b.S = S;
@@ -654,6 +665,11 @@ cudaError_t record_attention(FcSession *s, int S, int l, const Staging *dst, int
     (void)ef;
     DevLayer &y = m->layers[l];
     __half *cache = s->cache + (size_t)l * s->layer_rows * (L + R);
+    // head-parallel sessions run heads [h0, h0 + Hl) from q_b to W_UV
+    const int Hl = s->head_shard ? s->heads : H, h0 = s->head0;
+    const uint8_t *kv_b_w = y.kv_b.w + (size_t)(h0 * (NP + VD) / kTileRows) * tile_bytes(df, y.kv_b.kp);
+    const __half *o_in = s->o_xq;  // o_proj input
+    GemvWork o_sync{};             // o_proj's wait for the peers' heads (head-parallel)
     (void)kpD;
     {
         GemvBatch b{};
@@ -681,33 +697,35 @@ cudaError_t record_attention(FcSession *s, int S, int l, const Staging *dst, int
                                           nullptr, 0));
         mark(s, "rmsnorm");
         GemvSeg g = seg_of(y.q_b, s->qa_xq, EPI_STORE);
+        g.w += (size_t)(h0 * QW / kTileRows) * tile_bytes(df, y.q_b.kp);
+        g.O = Hl * QW;
         g.y = s->q;
-        g.ldy = H * QW;
+        g.ldy = Hl * QW;
         FC_TRY(gemv1(df, g, S, 0.0f, s->d_err, m->sms, st));
         mark(s, "gemv_q_b");
     }
     {
-        const int prep_y = 1 + (H * (R / 2) + 255) / 256;
-        const int blocks = S * prep_y + H * (L / kAbsorbCols);
+        const int prep_y = 1 + (Hl * (R / 2) + 255) / 256;
+        const int blocks = S * prep_y + Hl * (L / kAbsorbCols);
         FC_TRY(launch_pdl(mla_prep_absorb_kernel, dim3(blocks), dim3(256), 0, st, (const float *)s->ckv,
-                          (const float *)s->q, (const float *)y.kv_a_norm.p, L, R, H, NP, c.rms_norm_epsilon,
-                          c.rope_theta, dst, s->pmap, cache, s->qcat, S, prep_y, df, (const uint8_t *)y.kv_b.w,
+                          (const float *)s->q, (const float *)y.kv_a_norm.p, L, R, Hl, NP, c.rms_norm_epsilon,
+                          c.rope_theta, dst, s->pmap, cache, s->qcat, S, prep_y, df, kv_b_w,
                           y.kv_b.kp, VD));
         mark(s, "mla_prep_absorb");
     }
     const bool mtp_layer = l >= c.layer_count;
     const int nsplit = mtp_layer ? s->mtp_splits : s->splits;
     if (s->attn_tc) {
-        dim3 grid((S * H + kTcRows - 1) / kTcRows, 2, nsplit);
+        dim3 grid((S * Hl + kTcRows - 1) / kTcRows, 2, nsplit);
         const int kv_row0 = l * s->layer_rows,
                   kps = (mtp_layer ? s->mtp_chunks_per_split : s->chunks_per_split) * kAttnKeys;
         if (L == 512)
             FC_TRY(launch_pdl(mla_attention_tc_kernel<512>, grid, dim3(kTcThreads), TcAttnPlan<512>::SMEM, st,
-                              s->qmap, s->kvmap, kv_row0, S, H, kps, dst, s->pmap, scale, s->part_o, s->part_m,
+                              s->qmap, s->kvmap, kv_row0, S, Hl, kps, dst, s->pmap, scale, s->part_o, s->part_m,
                               s->part_l, s->d_err));
         else
             FC_TRY(launch_pdl(mla_attention_tc_kernel<256>, grid, dim3(kTcThreads), TcAttnPlan<256>::SMEM, st,
-                              s->qmap, s->kvmap, kv_row0, S, H, kps, dst, s->pmap, scale, s->part_o, s->part_m,
+                              s->qmap, s->kvmap, kv_row0, S, Hl, kps, dst, s->pmap, scale, s->part_o, s->part_m,
                               s->part_l, s->d_err));
         mark(s, "mla_attention");
     } else {
@@ -724,9 +742,9 @@ cudaError_t record_attention(FcSession *s, int S, int l, const Staging *dst, int
     }
     {
         size_t head_stride = (size_t)mb * kpL * 2;
-        FC_TRY(launch_pdl(mla_combine_kernel, dim3(S * H, (L + kCombineThreads - 1) / kCombineThreads),
+        FC_TRY(launch_pdl(mla_combine_kernel, dim3(S * Hl, (L + kCombineThreads - 1) / kCombineThreads),
                           dim3(kCombineThreads), 0, st, (const float *)s->part_o,
-                          (const float *)s->part_m, (const float *)s->part_l, nsplit, S, H, L,
+                          (const float *)s->part_m, (const float *)s->part_l, nsplit, S, Hl, L,
                           s->attn_tc ? L / 2 : L, s->ctx_xq, head_stride));
         mark(s, "mla_combine");
         // W_UV: rows nope .. nope+v of each head's kv_b block (decode_value, :345-375)
@@ -734,22 +752,55 @@ cudaError_t record_attention(FcSession *s, int S, int l, const Staging *dst, int
         // block starts on a tile boundary of kv_b
         GemvSeg g = seg_of(y.kv_b, s->ctx_xq, EPI_STORE_XQ);
         size_t tb = tile_bytes(df, y.kv_b.kp);
-        g.w = y.kv_b.w + (size_t)(NP / kTileRows) * tb;
-        g.O = VD;
-        g.count = H;
         g.w_stride = (int64_t)((NP + VD) / kTileRows) * (int64_t)tb;
+        g.w = kv_b_w + (size_t)(NP / kTileRows) * tb;
+        g.O = VD;
+        g.count = Hl;
         g.xq_stride = (int64_t)head_stride;
         g.yq = s->o_xq;
         g.kpy = kpO;
+        g.col_off = h0 * VD;
         g.out_stride = VD;
-        FC_TRY(gemv1(df, g, S, 0.0f, s->d_err, m->sms, st));
+        if (s->head_shard) {
+            // this rank's heads into its own o_proj input and every peer's
+            // (buffer = layer parity), then the epoch is published and the
+            // peers' heads awaited (bounded) before o_proj
+            const size_t off = s->ep_attn_off + 256 + (size_t)(l & 1) * s->ep_oxq_bytes;
+            g.yq = reinterpret_cast<__half *>(reinterpret_cast<uint8_t *>(s->ep_region) + off);
+            for (int r = 0, k = 0; r < m->world; ++r)
+                if (r != m->rank)
+                    g.peer_y[k++] = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(s->ep_peer_region[r]) + off);
+            g.npeer = m->world - 1;
+        }
+        // head-parallel: the W_UV launch's last CTA publishes the epoch to
+        // the peers, o_proj's producer waits for theirs (bounded)
+        GemvWork hand{};
+        if (s->head_shard) {
+            hand.pub_done = s->ep_adone;
+            hand.pub_epoch = s->ep_aepoch;
+            for (int r = 0; r < m->world; ++r)
+                if (r != m->rank)
+                    hand.pub_flags[r] =
+                        reinterpret_cast<int *>(reinterpret_cast<uint8_t *>(s->ep_peer_region[r]) + s->ep_attn_off);
+            hand.wait_flags = reinterpret_cast<const int *>(reinterpret_cast<uint8_t *>(s->ep_region) + s->ep_attn_off);
+            hand.wait_epoch = s->ep_aepoch;
+            hand.wait_ns = s->ep_wait_ns;
+            hand.peer_world = m->world;
+            hand.peer_rank = m->rank;
+        }
+        GemvWork pub = hand, wait = hand;
+        pub.wait_flags = nullptr;
+        wait.pub_done = nullptr;
+        FC_TRY(gemv1(df, g, S, 0.0f, s->d_err, m->sms, st, s->head_shard ? &pub : nullptr));
         mark(s, "gemv_w_uv");
+        o_in = g.yq;
+        o_sync = s->head_shard ? wait : GemvWork{};
     }
     {
-        GemvSeg g = seg_of(y.o_proj, s->o_xq, o_epi);
+        GemvSeg g = seg_of(y.o_proj, o_in, o_epi);
         g.y = o_y;
         g.ldy = D;
-        FC_TRY(gemv1(df, g, S, 0.0f, s->d_err, m->sms, st));
+        FC_TRY(gemv1(df, g, S, 0.0f, s->d_err, m->sms, st, s->head_shard ? &o_sync : nullptr));
         mark(s, "gemv_o_proj");
     }
     return cudaSuccess;
@@ -2092,13 +2143,31 @@ int create_session(FcSession **out, FcModel *m, const FcOptions *options, const 
     ok = ok && salloc(s, s->moe_part, (size_t)s->g_slots * mb * D);
     if (ok && m->world > 1) {
         const size_t xb = (size_t)2 * s->g_slots * mb * D * sizeof(float);
-        ok = cudaMalloc(&s->ep_region, xb + kMaxRanks * sizeof(int)) == cudaSuccess;
+        // head-parallel attention: single-sequence sessions of models with
+        // q-lora whose heads split evenly and whose last target layer and
+        // drafter layers are MoE (the expert exchange between two attention
+        // exchanges of the same buffer parity orders them);
+        // opt-in with FLOYD_HEAD_SHARD=1 (measured slower than replicated
+        // heads at 2 GPUs: the W_UV hand-off costs more than the halved MLA work)
+        bool hs = !batch && c.q_lora_rank > 0 && c.head_count % m->world == 0 && s->attn_tc &&
+                  (c.qk_nope_dim + c.qk_rope_dim) % kTileRows == 0 && (c.qk_nope_dim + c.value_dim) % kTileRows == 0;
+        for (int l = c.layer_count - 1; hs && l < (int)m->layers.size(); ++l) hs = !m->layers[l].dense;
+        const char *hs_env = getenv("FLOYD_HEAD_SHARD");
+        hs = hs && hs_env && strcmp(hs_env, "1") == 0;
+        s->head_shard = hs;
+        s->heads = hs ? c.head_count / m->world : c.head_count;
+        s->head0 = hs ? m->rank * s->heads : 0;
+        s->ep_attn_off = xb + 256;
+        s->ep_oxq_bytes = hs ? align256((size_t)mb * kpad(H * c.value_dim) * 2 * sizeof(__half)) : 0;
+        const size_t region = s->ep_attn_off + 256 + 2 * s->ep_oxq_bytes;
+        ok = cudaMalloc(&s->ep_region, region) == cudaSuccess;
         if (ok) {
-            cudaMemset(s->ep_region, 0, xb + kMaxRanks * sizeof(int));
+            cudaMemset(s->ep_region, 0, region);
             s->ep_xbuf = reinterpret_cast<float *>(s->ep_region);
             s->ep_flags = reinterpret_cast<int *>(reinterpret_cast<uint8_t *>(s->ep_region) + xb);
         }
         ok = ok && salloc(s, s->ep_epoch, 1);
+        ok = ok && salloc(s, s->ep_aepoch, 1) && salloc(s, s->ep_adone, 1);
         ok = ok && salloc(s, s->ep_wait_ns, 1);
     }
     ok = ok && salloc(s, s->sh_part, (size_t)mb * D);

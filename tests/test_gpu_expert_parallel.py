@@ -44,10 +44,15 @@ def _rank_main(rank, world, port, out_dir):
     dist.destroy_process_group()
 
 
-def test_two_gpu_expert_parallel_equals_single_gpu(tmp_path):
+@pytest.mark.parametrize("head_shard", ["0", "1"])
+def test_two_gpu_expert_parallel_equals_single_gpu(tmp_path, monkeypatch, head_shard):
+    """head_shard "1": each rank also runs half the attention heads and
+    hands its W_UV outputs to the peer (FLOYD_HEAD_SHARD=1); the results
+    stay bit-identical to one GPU either way."""
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
+    monkeypatch.setenv("FLOYD_HEAD_SHARD", head_shard)
     import torch.multiprocessing as mp
     import floyd_b200
     port = 29500 + os.getpid() % 1000
